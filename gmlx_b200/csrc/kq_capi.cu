@@ -1,0 +1,383 @@
+// kq_capi.cu -- the extern "C" entry points declared in include/kq_cuda.h.
+//
+// Host-side validation (codec, block-multiple K, alignment, dtypes, workspace
+// size) happens before any launch and reports a KQ_ERR_* code plus a
+// thread-local message; nothing throws across the ABI.  Mirrors the loud
+// failures of the reference's module swap (unknown codec -> error,
+// gmlx/modules.py:1561-1574; geometry rules gmlx/modules.py:502-509).
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/kq_cuda.h"
+#include "kq_internal.cuh"
+
+namespace kq {
+
+int num_sms() {
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!cache[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = v > 0 ? v : 148;
+    }
+    return cache[dev];
+}
+
+}  // namespace kq
+
+using namespace kq;
+
+namespace {
+
+thread_local char g_msg[512];
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_status(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return KQ_OK;
+    return fail(KQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool codec_ok(int c) { return c == KQ_Q4_K || c == KQ_Q6_K || c == KQ_IQ2_XXS; }
+bool act_dtype_ok(int d) { return d == KQ_F16 || d == KQ_BF16; }
+bool out_dtype_ok(int d) { return d == KQ_F32 || d == KQ_F16 || d == KQ_BF16; }
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+int check_weights(int codec, const void *w, int64_t k, int64_t row_stride, const char *what) {
+    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q4_k=12, q6_k=14, iq2_xxs=16)", what, codec);
+    if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a positive multiple of %d", what, (long long)k, QK);
+    const int64_t rb = k / QK * block_bytes(codec);
+    if (row_stride < rb) return fail(KQ_ERR_SHAPE, "%s: row stride %lld < row bytes %lld", what, (long long)row_stride, (long long)rb);
+    const int64_t need = codec == KQ_Q4_K ? 16 : 2;
+    if (((uintptr_t)w | (uintptr_t)row_stride) % need)
+        return fail(KQ_ERR_ALIGN, "%s: weight base/row stride must be %lld-byte aligned for codec %d", what, (long long)need, codec);
+    return KQ_OK;
+}
+
+int check_x(const void *x, int dtype, int64_t row_stride, const char *what) {
+    if (!act_dtype_ok(dtype)) return fail(KQ_ERR_DTYPE, "%s: activations must be f16 or bf16 (got dtype %d)", what, dtype);
+    if ((uintptr_t)x % 16 || row_stride % 8)
+        return fail(KQ_ERR_ALIGN, "%s: activation base must be 16-byte aligned and row stride a multiple of 8", what);
+    return KQ_OK;
+}
+
+// Workspace layout: [0,256) header (err int, n_groups int); then the group
+// tables, the per-slot f32 outputs, the split-K counters and partials.
+struct WsPlan {
+    size_t groups_off = 256, ys_off = 0, cnt_off = 0, part_off = 0, total = 256;
+    int max_groups = 0;
+};
+
+int moe_max_groups(int64_t slots, int64_t e, int gsize) {
+    return (int)(slots / gsize + (slots < e ? slots : e) + 1);
+}
+
+WsPlan plan(size_t group_ints, size_t ys_bytes, size_t cnt_bytes, size_t part_bytes) {
+    WsPlan p;
+    p.ys_off = align256(p.groups_off + group_ints * sizeof(int));
+    p.cnt_off = align256(p.ys_off + ys_bytes);
+    p.part_off = align256(p.cnt_off + cnt_bytes);
+    p.total = align256(p.part_off + part_bytes);
+    return p;
+}
+
+GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t xs, const void *w,
+                    const void *w2, int64_t n, int64_t ws_, void *y, int y_dtype, int64_t ys, int act) {
+    GemvArgs a{};
+    a.codec = codec;
+    a.w = (const uint8_t *)w;
+    a.w_row_stride = ws_;
+    a.w2 = (const uint8_t *)w2;
+    a.w2_row_stride = ws_;
+    a.N = (int)n;
+    a.K = (int)k;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.x_row_stride = xs;
+    a.dense_m = (int)m;
+    a.max_groups = (int)((m + 31) / 32);
+    a.y = y;
+    a.y_dtype = y_dtype;
+    a.y_row_stride = ys;
+    a.act = act;
+    a.max_tokens = (int)(m < 32 ? m : 32);
+    a.splits = gemv_choose_splits(codec, (int)n, (int)k, a.max_groups, a.max_tokens, act != ACT_NONE, num_sms());
+    return a;
+}
+
+size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
+    GemvArgs a = dense_args(codec, nullptr, KQ_BF16, m, k, k, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
+    size_t pb, cb;
+    gemv_scratch_need(a, &pb, &cb);
+    return plan(0, 0, cb, pb).total;
+}
+
+int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t xs, const void *w, const void *w2,
+              int64_t n, int64_t wstride, int act, void *y, int y_dtype, int64_t ys, void *ws, size_t ws_bytes,
+              void *stream, const char *what) {
+    int rc;
+    if ((rc = check_weights(codec, w, k, wstride, what))) return rc;
+    if (w2 && (rc = check_weights(codec, w2, k, wstride, what))) return rc;
+    if ((rc = check_x(x, x_dtype, xs, what))) return rc;
+    if (!out_dtype_ok(y_dtype)) return fail(KQ_ERR_DTYPE, "%s: bad output dtype %d", what, y_dtype);
+    if (m < 0 || n <= 0 || xs < k || ys < n) return fail(KQ_ERR_SHAPE, "%s: bad sizes m=%lld n=%lld", what, (long long)m, (long long)n);
+    if (m == 0) return KQ_OK;
+    if (n > 0x7fffffff || k > 0x7fffffff) return fail(KQ_ERR_SHAPE, "%s: n/k too large", what);
+    GemvArgs a = dense_args(codec, x, x_dtype, m, k, xs, w, w2, n, wstride, y, y_dtype, ys, act);
+    size_t pb, cb;
+    gemv_scratch_need(a, &pb, &cb);
+    const WsPlan p = plan(0, 0, cb, pb);
+    if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
+        return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
+    a.err = (int *)ws;
+    a.counters = (int *)((char *)ws + p.cnt_off);
+    a.partial = (float *)((char *)ws + p.part_off);
+    return cuda_status(launch_gemv(a, (cudaStream_t)stream), what);
+}
+
+// Routed (MoE) GEMV over expert stacks.  mode: 0 glu (x row = slot/k),
+// 1 per-slot rows (x row = slot), 2 explicit x_index.
+int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, int64_t slots, int kslot,
+               int64_t tokens, const int32_t *idx, const int32_t *xidx, int mode, const void *w, const void *w2,
+               int64_t e, int64_t n, int64_t wrs, int64_t wes, int act, void *y, int y_dtype, int64_t yrs,
+               const float *scores, void *ws, size_t ws_bytes, void *stream, const char *what) {
+    int rc;
+    if ((rc = check_weights(codec, w, kin, wrs, what))) return rc;
+    if (w2 && (rc = check_weights(codec, w2, kin, wrs, what))) return rc;
+    if ((rc = check_x(x, x_dtype, xs, what))) return rc;
+    if (!out_dtype_ok(y_dtype)) return fail(KQ_ERR_DTYPE, "%s: bad output dtype %d", what, y_dtype);
+    if (e <= 0 || e > 1024) return fail(KQ_ERR_SHAPE, "%s: expert count %lld outside 1..1024", what, (long long)e);
+    if (wes < n * wrs) return fail(KQ_ERR_SHAPE, "%s: expert stride smaller than one expert", what);
+    if (slots == 0) return KQ_OK;
+    if (slots < 0 || slots > (1 << 20)) return fail(KQ_ERR_SHAPE, "%s: slot count %lld out of range", what, (long long)slots);
+    const int64_t per_expert = mode == 2 ? slots : tokens;  // distinct experts per token bound group sizes
+    const int maxtok = (int)(per_expert < 32 ? per_expert : 32);
+    const int gsize = (maxtok + 7) / 8 * 8 < 32 ? (maxtok + 7) / 8 * 8 : 32;
+    const int maxg = moe_max_groups(slots, e, gsize);
+    GemvArgs a{};
+    a.codec = codec;
+    a.w = (const uint8_t *)w;
+    a.w_row_stride = wrs;
+    a.w_expert_stride = wes;
+    a.w2 = (const uint8_t *)w2;
+    a.w2_row_stride = wrs;
+    a.w2_expert_stride = wes;
+    a.N = (int)n;
+    a.K = (int)kin;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.x_row_stride = xs;
+    a.dense_m = 0;
+    a.max_groups = maxg;
+    a.act = act;
+    a.max_tokens = gsize;
+    a.splits = gemv_choose_splits(codec, (int)n, (int)kin, maxg, gsize, act != ACT_NONE, num_sms());
+    size_t pb, cb;
+    gemv_scratch_need(a, &pb, &cb);
+    const size_t ys_bytes = scores ? (size_t)slots * n * sizeof(float) : 0;
+    const WsPlan p = plan((size_t)maxg * 66, ys_bytes, cb, pb);
+    if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
+        return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
+    char *base = (char *)ws;
+    int *err = (int *)base, *ng = (int *)(base + 4);
+    int *gexp = (int *)(base + p.groups_off), *gcnt = gexp + maxg, *gx = gcnt + maxg, *go = gx + (size_t)maxg * 32;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t ce = launch_moe_groups(idx, (int)slots, kslot, (int)e, mode == 1, xidx, gsize, ng, gexp, gcnt, gx, go,
+                                       maxg, err, st);
+    if (ce != cudaSuccess) return cuda_status(ce, what);
+    a.n_groups = ng;
+    a.grp_expert = gexp;
+    a.grp_count = gcnt;
+    a.grp_xrow = gx;
+    a.grp_orow = go;
+    a.err = err;
+    a.counters = (int *)(base + p.cnt_off);
+    a.partial = (float *)(base + p.part_off);
+    if (scores) {
+        a.y = base + p.ys_off;
+        a.y_dtype = KQ_F32;
+        a.y_row_stride = n;
+    } else {
+        a.y = y;
+        a.y_dtype = y_dtype;
+        a.y_row_stride = yrs;
+    }
+    if ((ce = launch_gemv(a, st)) != cudaSuccess) return cuda_status(ce, what);
+    if (scores)
+        if ((ce = launch_moe_mix((const float *)(base + p.ys_off), scores, (int)tokens, kslot, (int)n, y, y_dtype, st)) !=
+            cudaSuccess)
+            return cuda_status(ce, what);
+    return KQ_OK;
+}
+
+size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_t n, int64_t kin, int act,
+                 bool mix) {
+    const int maxtok = (int)(per_expert < 32 ? (per_expert > 0 ? per_expert : 1) : 32);
+    const int gsize = (maxtok + 7) / 8 * 8 < 32 ? (maxtok + 7) / 8 * 8 : 32;
+    const int maxg = moe_max_groups(slots, e, gsize);
+    GemvArgs a{};
+    a.codec = codec;
+    a.N = (int)n;
+    a.K = (int)kin;
+    a.max_groups = maxg;
+    a.act = act;
+    a.splits = gemv_choose_splits(codec, (int)n, (int)kin, maxg, gsize, act != ACT_NONE, num_sms());
+    size_t pb, cb;
+    gemv_scratch_need(a, &pb, &cb);
+    return plan((size_t)maxg * 66, mix ? (size_t)slots * n * sizeof(float) : 0, cb, pb).total;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kq_version(void) { return 100; }
+
+const char *kq_last_error(void) { return g_msg; }
+
+int kq_codecs(int *out, int cap) {
+    static const int ids[3] = {KQ_Q4_K, KQ_Q6_K, KQ_IQ2_XXS};
+    for (int i = 0; i < 3 && i < cap; i++) out[i] = ids[i];
+    return 3;
+}
+
+int kq_codec_has_matmul(int codec) { return codec_ok(codec) ? 1 : 0; }
+
+int kq_block_bytes(int codec) { return codec_ok(codec) ? block_bytes(codec) : -1; }
+
+int kq_dequantize(int codec, const void *w, int64_t rows, int64_t k, int64_t w_row_stride, void *out, int out_dtype,
+                  void *stream) {
+    g_msg[0] = 0;
+    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "dequantize: unsupported codec %d", codec);
+    if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "dequantize: K=%lld is not a positive multiple of 256", (long long)k);
+    if (rows < 0) return fail(KQ_ERR_SHAPE, "dequantize: rows < 0");
+    if (!out_dtype_ok(out_dtype)) return fail(KQ_ERR_DTYPE, "dequantize: bad output dtype %d", out_dtype);
+    if ((uintptr_t)out % 16) return fail(KQ_ERR_ALIGN, "dequantize: output must be 16-byte aligned");
+    if (w_row_stride < k / QK * block_bytes(codec)) return fail(KQ_ERR_SHAPE, "dequantize: row stride too small");
+    return cuda_status(launch_dequantize(codec, (const uint8_t *)w, rows, k, w_row_stride, out, out_dtype,
+                                         (cudaStream_t)stream),
+                       "dequantize");
+}
+
+size_t kq_quantized_matmul_workspace_size(int codec, int64_t m, int64_t n, int64_t k) {
+    if (!codec_ok(codec) || k <= 0 || k % QK || n <= 0 || m <= 0) return 256;
+    return dense_ws(codec, m, n, k, ACT_NONE);
+}
+
+int kq_quantized_matmul(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
+                        const void *w, int64_t n, int64_t w_row_stride, void *y, int y_dtype, int64_t y_row_stride,
+                        void *workspace, size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    return run_dense(codec, x, x_dtype, m, k, x_row_stride, w, nullptr, n, w_row_stride, ACT_NONE, y, y_dtype,
+                     y_row_stride, workspace, workspace_bytes, stream, "quantized_matmul");
+}
+
+size_t kq_quantized_glu_workspace_size(int codec, int64_t m, int64_t n, int64_t k) {
+    if (!codec_ok(codec) || k <= 0 || k % QK || n <= 0 || m <= 0) return 256;
+    return dense_ws(codec, m, n, k, ACT_SILU);
+}
+
+int kq_quantized_glu(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
+                     const void *gate_w, const void *up_w, int64_t n, int64_t w_row_stride, int act, void *y,
+                     int y_dtype, int64_t y_row_stride, void *workspace, size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    if (act < KQ_ACT_SILU || act > KQ_ACT_GELU_TANH) return fail(KQ_ERR_SHAPE, "quantized_glu: bad activation %d", act);
+    return run_dense(codec, x, x_dtype, m, k, x_row_stride, gate_w, up_w, n, w_row_stride, act, y, y_dtype,
+                     y_row_stride, workspace, workspace_bytes, stream, "quantized_glu");
+}
+
+int kq_moe_router_topk(const float *logits, int64_t t, int64_t e, int k, int norm_topk_prob, int32_t *idx,
+                       float *scores, void *stream) {
+    g_msg[0] = 0;
+    if (e <= 0 || e > 1024) return fail(KQ_ERR_SHAPE, "moe_router_topk: expert count %lld outside 1..1024", (long long)e);
+    if (k <= 0 || k > 16 || k > e) return fail(KQ_ERR_SHAPE, "moe_router_topk: k=%d outside 1..min(16, E)", k);
+    if (t < 0) return fail(KQ_ERR_SHAPE, "moe_router_topk: t < 0");
+    return cuda_status(launch_router_topk(logits, (int)t, (int)e, k, norm_topk_prob, idx, scores, nullptr,
+                                          (cudaStream_t)stream),
+                       "moe_router_topk");
+}
+
+size_t kq_moe_workspace_size(int codec, int64_t slots, int64_t e, int64_t n, int64_t k_in) {
+    if (!codec_ok(codec) || k_in <= 0 || k_in % QK || n <= 0 || e <= 0) return 256;
+    if (slots <= 0) slots = 1;
+    // the largest plan over every group size the calls can pick
+    size_t best = 256;
+    const int64_t pe[5] = {1, 9, 17, 25, 32};
+    for (int i = 0; i < 5; i++)
+        for (int act = 0; act < 2; act++) {
+            const size_t s = routed_ws(codec, slots, pe[i], e, n, k_in, act ? ACT_SILU : ACT_NONE, true);
+            best = s > best ? s : best;
+        }
+    return best;
+}
+
+int kq_moe_glu_gather(int codec, const void *x, int x_dtype, int64_t t, int64_t d, const int32_t *idx, int k,
+                      const void *gate_w, const void *up_w, int64_t e, int64_t f, int64_t w_row_stride,
+                      int64_t w_expert_stride, int act, void *h, int h_dtype, void *workspace,
+                      size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    if (act < KQ_ACT_SILU || act > KQ_ACT_GELU_TANH) return fail(KQ_ERR_SHAPE, "moe_glu_gather: bad activation %d", act);
+    if (k <= 0) return fail(KQ_ERR_SHAPE, "moe_glu_gather: k <= 0");
+    return run_routed(codec, x, x_dtype, d, d, t * k, k, t, idx, nullptr, 0, gate_w, up_w, e, f, w_row_stride,
+                      w_expert_stride, act, h, h_dtype, f, nullptr, workspace, workspace_bytes, stream,
+                      "moe_glu_gather");
+}
+
+int kq_gather_qmv(int codec, const void *h, int h_dtype, int64_t t, int k, int64_t f, const int32_t *idx,
+                  const void *w, int64_t e, int64_t n, int64_t w_row_stride, int64_t w_expert_stride, void *y,
+                  int y_dtype, void *workspace, size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    if (k <= 0) return fail(KQ_ERR_SHAPE, "gather_qmv: k <= 0");
+    return run_routed(codec, h, h_dtype, f, f, t * k, k, t, idx, nullptr, 1, w, nullptr, e, n, w_row_stride,
+                      w_expert_stride, ACT_NONE, y, y_dtype, n, nullptr, workspace, workspace_bytes, stream,
+                      "gather_qmv");
+}
+
+int kq_gather_qmv_mix(int codec, const void *h, int h_dtype, int64_t t, int k, int64_t f, const int32_t *idx,
+                      const float *scores, const void *w, int64_t e, int64_t n, int64_t w_row_stride,
+                      int64_t w_expert_stride, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                      void *stream) {
+    g_msg[0] = 0;
+    if (k <= 0) return fail(KQ_ERR_SHAPE, "gather_qmv_mix: k <= 0");
+    if (!scores) return fail(KQ_ERR_SHAPE, "gather_qmv_mix: scores required");
+    return run_routed(codec, h, h_dtype, f, f, t * k, k, t, idx, nullptr, 1, w, nullptr, e, n, w_row_stride,
+                      w_expert_stride, ACT_NONE, y, y_dtype, n, scores, workspace, workspace_bytes, stream,
+                      "gather_qmv_mix");
+}
+
+int kq_gather_qmm(int codec, const void *x, int x_dtype, int64_t k, int64_t x_row_stride, int64_t rows,
+                  const int32_t *x_index, const int32_t *expert_index, const void *w, int64_t e, int64_t n,
+                  int64_t w_row_stride, int64_t w_expert_stride, void *y, int y_dtype, void *workspace,
+                  size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    return run_routed(codec, x, x_dtype, x_row_stride, k, rows, 1, rows, expert_index, x_index, x_index ? 2 : 1, w,
+                      nullptr, e, n, w_row_stride, w_expert_stride, ACT_NONE, y, y_dtype, n, nullptr, workspace,
+                      workspace_bytes, stream, "gather_qmm");
+}
+
+int kq_workspace_error(void *workspace, int clear, void *stream) {
+    if (!workspace) return 0;
+    int v = 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return -1;
+    if (clear && v) {
+        int z = 0;
+        cudaMemcpyAsync(workspace, &z, sizeof(int), cudaMemcpyHostToDevice, st);
+        cudaStreamSynchronize(st);
+    }
+    return v;
+}
+
+}  // extern "C"

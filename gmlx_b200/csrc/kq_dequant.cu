@@ -1,0 +1,111 @@
+// kq_dequant.cu -- block dequantization (the kq.dequantize op).
+//
+// Replaces mlx-kquant's dequantize as called from gmlx/modules.py:1461,
+// gmlx/loader.py:3046-3048 and gmlx/dsv32_patches.py:229.  f32 output is
+// bit-identical to gguf-py's dequantize (see kq_formats.cuh for why any
+// evaluation order gives the same bits); f16/bf16 outputs are the f32 value
+// rounded to nearest even.
+//
+// Memory-bound: each warp owns one super-block, each lane 8 consecutive
+// weights (one 32-byte f32 store or one 16-byte f16/bf16 store).
+#include "kq_internal.cuh"
+
+namespace kq {
+
+template <int C>
+__device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
+    if constexpr (C == Q4_K) {
+        const int j = lane >> 2, i0 = 8 * (lane & 3), c = j >> 1, h = j & 1;
+        const float d = half_bits_to_float(ld_u16(b));
+        const float dmin = half_bits_to_float(ld_u16(b + 2));
+        const uint32_t s0 = ld_u32_unaligned(b + 4), s1 = ld_u32_unaligned(b + 8), s2 = ld_u32_unaligned(b + 12);
+        uint32_t sc03, sc47, m03, m47;
+        q4k_unpack_scales(s0, s1, s2, sc03, sc47, m03, m47);
+        const uint32_t scw = j < 4 ? sc03 : sc47, mw = j < 4 ? m03 : m47;
+        const float dl = d * byte_f(scw, j & 3), ml = dmin * byte_f(mw, j & 3);
+        const uint8_t *q = b + 16 + 32 * c + i0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = dl * (float)((q[i] >> (4 * h)) & 15) - ml;
+    } else if constexpr (C == Q6_K) {
+        const int i0 = 8 * lane, hf = i0 >> 7, s = (i0 & 127) >> 5, lo = i0 & 31;
+        const float d = half_bits_to_float(ld_u16(b + 208));
+        const float dl = d * (float)(int8_t)b[192 + (i0 >> 4)];
+        const uint8_t *ql = b + 64 * hf + 32 * (s & 1) + lo, *qh = b + 128 + 32 * hf + lo;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int q = (((ql[i] >> (4 * (s >> 1))) & 15) | (((qh[i] >> (2 * s)) & 3) << 4)) - 32;
+            o[i] = dl * (float)q;
+        }
+    } else {
+        const int g = lane >> 2, s = lane & 3;
+        const float d = half_bits_to_float(ld_u16(b));
+        const uint32_t a0 = ld_u32_unaligned(b + 2 + 8 * g), a1 = ld_u32_unaligned(b + 6 + 8 * g);
+        const float db = d * (0.5f + (float)(a1 >> 28)) * 0.25f;
+        const uint32_t sg = ksigns((a1 >> (7 * s)) & 127u);
+        const uint64_t e = c_iq2xxs_grid[(a0 >> (8 * s)) & 255u];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float gv = (float)((e >> (8 * i)) & 255u);
+            o[i] = db * gv * (((sg >> i) & 1u) ? -1.0f : 1.0f);
+        }
+    }
+}
+
+template <int C, int OUT>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict__ w, int64_t rows, int64_t nb,
+                                                      int64_t row_stride, void *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t blk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (blk >= rows * nb) return;
+    const int64_t r = blk / nb, b = blk - r * nb;
+    float o[8];
+    deq8<C>(w + r * row_stride + b * Fmt<C>::bpb, lane, o);
+    const int64_t e0 = r * nb * QK + b * QK + 8 * lane;
+    if constexpr (OUT == F32) {
+        float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + e0);
+        p[0] = make_float4(o[0], o[1], o[2], o[3]);
+        p[1] = make_float4(o[4], o[5], o[6], o[7]);
+    } else if constexpr (OUT == BF16) {
+        uint4 v;
+        uint32_t *u = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+            u[i] = *reinterpret_cast<uint32_t *>(&h);
+        }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(out) + e0) = v;
+    } else {
+        uint4 v;
+        uint32_t *u = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            __half2 h = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
+            u[i] = *reinterpret_cast<uint32_t *>(&h);
+        }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<__half *>(out) + e0) = v;
+    }
+}
+
+template <int C>
+static cudaError_t launch_deq(const uint8_t *w, int64_t rows, int64_t nb, int64_t stride, void *out, int dtype,
+                              cudaStream_t st) {
+    const int64_t nblk = rows * nb;
+    const unsigned grid = (unsigned)((nblk + 7) / 8);
+    if (dtype == F32) dequant_kernel<C, F32><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);
+    else if (dtype == BF16) dequant_kernel<C, BF16><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);
+    else dequant_kernel<C, F16><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t k, int64_t row_stride, void *out,
+                              int dtype, cudaStream_t st) {
+    const int64_t nb = k / QK;
+    if (rows * nb == 0) return cudaSuccess;
+    switch (codec) {
+    case Q4_K: return launch_deq<Q4_K>(w, rows, nb, row_stride, out, dtype, st);
+    case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st);
+    default: return launch_deq<IQ2_XXS>(w, rows, nb, row_stride, out, dtype, st);
+    }
+}
+
+}  // namespace kq

@@ -1,0 +1,79 @@
+// kq_formats.cuh -- GGUF K-quant / IQ-quant super-block formats on sm_100a.
+//
+// Block layouts (256 weights per super-block), as decoded by gguf-py 0.19.0
+// gguf/quants.py, the restatement of ggml's formats that gmlx depends on
+// (gmlx pyproject.toml:62; the kernels gmlx calls live in the external
+// mlx-kquant, gmlx/modules.py:35-40):
+//
+//   Q4_K  144 B  d f16 | dmin f16 | 12 B packed 6-bit (sc, m) x 8 | 128 B nibbles
+//                w = (d*sc_j)*q - (dmin*m_j)              quants.py:475-522
+//   Q6_K  210 B  128 B ql | 64 B qh | 16 x int8 sc | d f16
+//                w = (d*sc_j)*(q - 32)                    quants.py:552-572
+//   IQ2_XXS 66 B d f16 | 8 x (u32 grid indices, u32 signs+scale)
+//                w = d*(0.5+ls)*0.25 * grid * sign        quants.py:766-829
+//
+// Exactness: every product above is exact in f32 (fp16 d has 11 significant
+// bits; d*sc <= 17 bits, d*sc*q <= 21 bits; Q6_K d*sc*(q-32) <= 24 bits;
+// IQ2_XXS d*(0.5+ls)*0.25*grid <= 22 bits), so a dequantized weight is
+// bit-identical to gguf-py whether or not the compiler contracts to FMA: only
+// the final Q4_K subtraction rounds, once, in either form.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "_gen/kq_tables.h"
+
+namespace kq {
+
+enum Codec : int { Q4_K = 12, Q6_K = 14, IQ2_XXS = 16 };
+enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
+
+constexpr int QK = 256;
+
+template <int C> struct Fmt;
+template <> struct Fmt<Q4_K> { static constexpr int bpb = 144; static constexpr int sub = 32; };
+template <> struct Fmt<Q6_K> { static constexpr int bpb = 210; static constexpr int sub = 16; };
+template <> struct Fmt<IQ2_XXS> { static constexpr int bpb = 66; static constexpr int sub = 32; };
+
+__host__ __device__ inline int block_bytes(int codec) {
+    return codec == Q4_K ? 144 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66 : -1;
+}
+
+// 256-entry IQ2_XXS grid, byte i of entry e = |w_i| in {8, 25, 43}.
+static __device__ __constant__ uint64_t c_iq2xxs_grid[256] = KQ_IQ2XXS_GRID_INIT;
+
+// ggml's 7-bit -> 8-bit sign expansion: bit 7 restores even parity.
+__device__ __forceinline__ uint32_t ksigns(uint32_t i7) {
+    return i7 | ((__popc(i7) & 1u) << 7);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
+    return __half2float(__ushort_as_half((unsigned short)h16));
+}
+
+__device__ __forceinline__ uint16_t ld_u16(const uint8_t *p) {
+    return (uint16_t)p[0] | ((uint16_t)p[1] << 8);
+}
+__device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// Q4_K 12-byte scale/min unpack (gguf-py Q4_K.get_scale_min, quants.py:479-501)
+// done four lanes at a time on 32-bit words: s0 = bytes 0-3, s1 = 4-7, s2 = 8-11.
+__device__ __forceinline__ void q4k_unpack_scales(uint32_t s0, uint32_t s1, uint32_t s2,
+                                                  uint32_t &sc03, uint32_t &sc47,
+                                                  uint32_t &m03, uint32_t &m47) {
+    sc03 = s0 & 0x3f3f3f3fu;
+    m03 = s1 & 0x3f3f3f3fu;
+    sc47 = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);
+    m47 = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);
+}
+
+__device__ __forceinline__ float byte_f(uint32_t w, int i) { return (float)((w >> (8 * i)) & 0xffu); }
+
+// Bounded spin limits for every device-side wait (mbarrier and flags).  A
+// wait that runs out sets the kernel's error word and abandons the unit.
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+}  // namespace kq

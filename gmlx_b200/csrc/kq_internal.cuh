@@ -1,0 +1,65 @@
+// kq_internal.cuh -- launchers shared between the kernel files and the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kq_formats.cuh"
+
+namespace kq {
+
+// Activation functions of the fused gate/up epilogue (gmlx/modules.py:522-525
+// lists silu and gelu for the kq fused MoE ops).
+enum Act : int { ACT_NONE = 0, ACT_SILU = 1, ACT_GELU = 2, ACT_GELU_TANH = 3 };
+
+cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t k, int64_t row_stride, void *out,
+                              int dtype, cudaStream_t st);
+
+// Decode-shaped GEMV over groups of <= 32 activation rows sharing one weight
+// matrix (dense decode: one group per 32 rows; MoE decode: one group per
+// routed expert).  See kq_gemv.cu.
+struct GemvArgs {
+    int codec;
+    const uint8_t *w;  // weights [E][N] rows of nb blocks
+    int64_t w_row_stride, w_expert_stride;
+    const uint8_t *w2;  // up weights for the fused GLU (same codec / shape)
+    int64_t w2_row_stride, w2_expert_stride;
+    int N, K;
+    const void *x;  // activations, row i at x + i*x_row_stride elements
+    int x_dtype;    // F16 or BF16
+    int64_t x_row_stride;
+    // Groups.  dense_m > 0: implicit groups of rows [32g, 32g+32) of x/y.
+    // Otherwise the routed tables (device): *n_groups, expert, count, xrow/orow[32 per group].
+    int dense_m;
+    int max_groups;
+    const int *n_groups;
+    const int *grp_expert, *grp_count, *grp_xrow, *grp_orow;
+    void *y;
+    int y_dtype;
+    int64_t y_row_stride;
+    int act;     // ACT_NONE: plain; otherwise fused GLU y = act(x.Wg) * (x.Wu)
+    int splits;  // K splits (>1 needs partial + counters scratch)
+    float *partial;
+    int *counters;
+    int *err;
+    int max_tokens;  // upper bound of rows in any group (<= 32)
+};
+cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st);
+// Scratch the GEMV needs for `a` (bytes of f32 partials, ints of counters).
+void gemv_scratch_need(const GemvArgs &a, size_t *partial_bytes, size_t *counter_bytes);
+int gemv_choose_splits(int codec, int N, int K, int max_groups, int max_tokens, bool glu, int num_sms);
+
+// MoE slot grouping: idx[S] (S = T*k slots) -> per-expert groups of <= gsize
+// slots (ascending slot order inside a group, groups ordered by expert id).
+// Activation row of slot s: xidx[s] if given, else s (xrow_is_slot) or s/k.
+cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int E, int xrow_is_slot, const int32_t *xidx,
+                              int gsize, int *n_groups, int *grp_expert, int *grp_count, int *grp_xrow,
+                              int *grp_orow, int max_groups, int *err, cudaStream_t st);
+// y[t][n] = sum_j scores[t][j] * ys[t*k+j][n]  (fixed j order).
+cudaError_t launch_moe_mix(const float *ys, const float *scores, int T, int k, int N, void *y, int y_dtype,
+                           cudaStream_t st);
+cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int norm, int32_t *idx, float *scores,
+                               int *err, cudaStream_t st);
+
+int num_sms();
+
+}  // namespace kq

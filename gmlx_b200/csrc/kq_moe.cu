@@ -1,0 +1,169 @@
+// kq_moe.cu -- MoE routing support kernels.
+//
+//  * router_topk: softmax -> top-k -> optional renormalisation in one launch,
+//    the kq.moe_router_topk op (gmlx/modules.py:751-752) and the stock
+//    Qwen3-MoE selection it replaces (gmlx/moe_experts.py:226-240:
+//    softmax(precise) -> argpartition top-k -> take -> scores/sum).  Output
+//    order is descending probability, ties to the lower expert id.
+//  * moe_groups: bucket the T*k routed slots by expert into groups of <= 32
+//    slots so the GEMV streams every touched expert's weights exactly once.
+//  * moe_mix: y[t] = sum_j scores[t,j] * ys[t,j] in a fixed j order (the
+//    gather_qmv_mix_ns_kq combine, gmlx/modules.py:589-594, in f32).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "kq_internal.cuh"
+
+namespace kq {
+namespace {
+
+constexpr int RT_MAXE = 1024, RT_MAXK = 16;
+
+__global__ void router_kernel(const float *__restrict__ logits, int T, int E, int k, int norm, int32_t *__restrict__ idx,
+                              float *__restrict__ scores) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const float *l = logits + (int64_t)warp * E;
+    constexpr int PER = RT_MAXE / 32;
+    float p[PER];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int e = lane + 32 * i;
+        p[i] = e < E ? l[e] : -INFINITY;
+        mx = fmaxf(mx, p[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int e = lane + 32 * i;
+        p[i] = e < E ? expf(p[i] - mx) : 0.f;
+        s += p[i];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float inv = 1.0f / s;
+#pragma unroll
+    for (int i = 0; i < PER; i++) p[i] = (lane + 32 * i) < E ? p[i] * inv : -1.0f;
+    float sel[RT_MAXK];
+    int seli[RT_MAXK];
+    float tot = 0.f;
+    for (int c = 0; c < k; c++) {
+        float bv = -2.0f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int e = lane + 32 * i;
+            if (p[i] > bv || (p[i] == bv && e < bi)) { bv = p[i]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        sel[c] = bv;
+        seli[c] = bi;
+        tot += bv;
+#pragma unroll
+        for (int i = 0; i < PER; i++)
+            if (lane + 32 * i == bi) p[i] = -1.0f;
+    }
+    if (lane == 0) {
+        for (int c = 0; c < k; c++) {
+            idx[(int64_t)warp * k + c] = seli[c];
+            scores[(int64_t)warp * k + c] = norm ? sel[c] / tot : sel[c];
+        }
+    }
+}
+
+__global__ void groups_kernel(const int32_t *__restrict__ idx, int S, int k, int E, int xrow_is_slot,
+                              const int32_t *__restrict__ xidx, int gsize, int *__restrict__ n_groups, int *__restrict__ grp_expert, int *__restrict__ grp_count,
+                              int *__restrict__ grp_xrow, int *__restrict__ grp_orow, int max_groups,
+                              int *__restrict__ err) {
+    __shared__ int s_first[RT_MAXE + 1];
+    __shared__ int s_bad;
+    if (threadIdx.x == 0) s_bad = 0;
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int c = 0;
+        for (int s = 0; s < S; s++) {
+            const int v = idx[s];
+            c += v == e;
+            if (e == 0 && (v < 0 || v >= E)) s_bad = 1;
+        }
+        s_first[e + 1] = (c + gsize - 1) / gsize;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        s_first[0] = 0;
+        for (int e = 0; e < E; e++) s_first[e + 1] += s_first[e];
+        *n_groups = s_bad ? 0 : min(s_first[E], max_groups);
+        if (s_bad) atomicCAS(err, 0, 3);
+        else if (s_first[E] > max_groups) atomicCAS(err, 0, 4);
+    }
+    __syncthreads();
+    if (s_bad) return;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int gi = s_first[e], n = 0;
+        for (int s = 0; s < S; s++) {
+            if (idx[s] != e) continue;
+            if (gi >= max_groups) break;
+            grp_xrow[gi * 32 + n] = xidx ? xidx[s] : xrow_is_slot ? s : s / k;
+            grp_orow[gi * 32 + n] = s;
+            if (++n == gsize) {
+                grp_expert[gi] = e;
+                grp_count[gi] = gsize;
+                gi++;
+                n = 0;
+            }
+        }
+        if (n && gi < max_groups) {
+            grp_expert[gi] = e;
+            grp_count[gi] = n;
+        }
+    }
+}
+
+__global__ void mix_kernel(const float *__restrict__ ys, const float *__restrict__ scores, int T, int k, int N,
+                           void *__restrict__ y, int y_dtype) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)T * N) return;
+    const int t = (int)(i / N), n = (int)(i - (int64_t)t * N);
+    float v = 0.f;
+    for (int j = 0; j < k; j++) v = fmaf(scores[t * k + j], ys[((int64_t)t * k + j) * N + n], v);
+    if (y_dtype == F32) reinterpret_cast<float *>(y)[i] = v;
+    else if (y_dtype == BF16) reinterpret_cast<__nv_bfloat16 *>(y)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<__half *>(y)[i] = __float2half_rn(v);
+}
+
+}  // namespace
+
+cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int norm, int32_t *idx, float *scores,
+                               int *err, cudaStream_t st) {
+    (void)err;
+    if (T <= 0) return cudaSuccess;
+    const int threads = 256, per = threads / 32;
+    router_kernel<<<(T + per - 1) / per, threads, 0, st>>>(logits, T, E, k, norm, idx, scores);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int E, int xrow_is_slot, const int32_t *xidx,
+                              int gsize, int *n_groups, int *grp_expert, int *grp_count, int *grp_xrow,
+                              int *grp_orow, int max_groups, int *err, cudaStream_t st) {
+    groups_kernel<<<1, 1024, 0, st>>>(idx, S, k, E, xrow_is_slot, xidx, gsize, n_groups, grp_expert, grp_count,
+                                      grp_xrow, grp_orow, max_groups, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_mix(const float *ys, const float *scores, int T, int k, int N, void *y, int y_dtype,
+                           cudaStream_t st) {
+    const int64_t n = (int64_t)T * N;
+    if (n == 0) return cudaSuccess;
+    mix_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ys, scores, T, k, N, y, y_dtype);
+    return cudaGetLastError();
+}
+
+}  // namespace kq

@@ -1,0 +1,366 @@
+"""The ``mlx_kquant`` op surface that gmlx calls, on B200.
+
+gmlx reaches its quantized kernels as ``import mlx_kquant as kq``
+(gmlx/modules.py:35-40).  This module offers the same names, argument meaning
+and error behaviour over torch CUDA tensors, each backed by one entry point of
+``libkq_cuda.so`` (``include/kq_cuda.h``):
+
+=========================  =============================================
+kq op                      gmlx call sites
+=========================  =============================================
+``dequantize``             modules.py:1461, loader.py:3046-3048
+``quantized_matmul``       KQuantLinear (modules.py:1535-1539),
+                           occupancy_fuse.py:284-287, 412-418, 434-437
+``gather_qmm``             KQuantSwitchLinear (modules.py:1548-1552),
+                           sorted prefill path modules.py:1308-1309
+``moe_glu_gather_kq``      modules.py:585-588, 980-983
+``gather_qmv_kq``          modules.py:596-598
+``gather_qmv_mix_ns_kq``   modules.py:591-593, 989-991
+``moe_router_topk``        modules.py:446-447, 751-752
+``codecs`` /               preflight.py:625-632, _FusedMoeCaps
+``codec_has_matmul``       (modules.py:155-234)
+=========================  =============================================
+
+Weights are uint8 wire-byte tensors ``[N, K/256*bpb]`` (or ``[E, N, ...]``),
+never repacked; ``scales`` is the reference's ``(1,)`` placeholder and is
+ignored.  Outputs are fresh tensors in the activation dtype.  Unknown codecs
+raise ``NotImplementedError``; bad shapes ``ValueError``.  All work is enqueued
+on the current torch CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes as _ct
+
+import torch
+
+from . import _lib
+from .synth import BLOCK_BYTES, CODECS, QK, codec_id
+
+__all__ = [
+    "codecs", "codec_has_matmul", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
+    "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
+]
+
+_DT = {torch.float32: _lib.KQ_F32, torch.float16: _lib.KQ_F16, torch.bfloat16: _lib.KQ_BF16}
+_TORCH_DT = {v: k for k, v in _DT.items()}
+
+
+def codecs() -> list[str]:
+    """Codec names with kernels here (the loader whitelists against this)."""
+    L = _lib.load()
+    buf = (_ct.c_int * 8)()
+    n = L.kq_codecs(buf, 8)
+    names = {v: k for k, v in CODECS.items()}
+    return [names[buf[i]] for i in range(min(n, 8))]
+
+
+def codec_has_matmul(codec) -> bool:
+    try:
+        c = codec_id(codec)
+    except ValueError:
+        return False
+    return bool(_lib.load().kq_codec_has_matmul(c))
+
+
+def block_bytes(codec) -> int:
+    return BLOCK_BYTES[codec_id(codec)]
+
+
+def _cid(codec) -> int:
+    try:
+        c = codec_id(codec)
+    except ValueError as e:
+        raise NotImplementedError(f"[gmlx_b200.kq] unsupported codec {codec!r}") from e
+    if c not in BLOCK_BYTES:
+        raise NotImplementedError(f"[gmlx_b200.kq] unsupported codec {codec!r}")
+    return c
+
+
+def _stream(dev: torch.device):
+    return _ct.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _p(t: torch.Tensor | None):
+    return _ct.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("[gmlx_b200.kq] tensors must be CUDA tensors (there is no CPU implementation)")
+
+
+def _wire_k(w: torch.Tensor, c: int) -> int:
+    bpb = BLOCK_BYTES[c]
+    if w.dtype != torch.uint8:
+        raise ValueError(f"wire weights must be uint8, got {w.dtype}")
+    if w.shape[-1] % bpb:
+        raise ValueError(f"wire row of {w.shape[-1]} bytes is not a whole number of {bpb}-byte blocks")
+    return w.shape[-1] // bpb * QK
+
+
+def _rows2d(w: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """View w [..., R, bytes] with unit byte stride; return (w, row stride bytes)."""
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    if w.dim() >= 2 and w.shape[-2] > 1:
+        return w, w.stride(-2)
+    return w, w.shape[-1]
+
+
+# --------------------------------------------------------------------------
+# per-(device, stream) workspaces, zero-filled once and kept zero by the library
+
+_WS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(dev).cuda_stream)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _WS[key] = ws
+    return ws
+
+
+def workspace_error(device=None, clear: bool = True) -> int:
+    """Device-side error word of the current stream's workspace (syncs)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _WS.get(key)
+    if ws is None:
+        return 0
+    return _lib.load().kq_workspace_error(_p(ws), int(clear), _stream(dev))
+
+
+# --------------------------------------------------------------------------
+# ops
+
+
+def dequantize(w: torch.Tensor, scales=None, codec=None, dtype: torch.dtype = torch.float32,
+               biases=None) -> torch.Tensor:
+    """``kq.dequantize``: wire ``[..., nb*bpb]`` -> ``[..., nb*256]`` in ``dtype``."""
+    c = _cid(codec)
+    _need_cuda(w)
+    if dtype not in _DT:
+        raise ValueError(f"unsupported dequantize dtype {dtype}")
+    k = _wire_k(w, c)
+    w = w.contiguous()
+    rows = w.numel() // w.shape[-1] if w.numel() else 0
+    out = torch.empty(*w.shape[:-1], k, dtype=dtype, device=w.device)
+    if rows == 0:
+        return out
+    L = _lib.load()
+    _lib.check(L.kq_dequantize(c, _p(w), rows, k, w.shape[-1], _p(out), _DT[dtype], _stream(w.device)), "dequantize")
+    return out
+
+
+def _act_2d(x: torch.Tensor, k: int) -> torch.Tensor:
+    if x.shape[-1] != k:
+        raise ValueError(f"activation K={x.shape[-1]} does not match weight K={k}")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"activations must be bf16 or fp16, got {x.dtype}")
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    return x2
+
+
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, transpose: bool = True,
+                     out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``kq.quantized_matmul(x, w, scales, codec, transpose=True)``: ``x @ dequant(w).T``."""
+    if not transpose:
+        raise NotImplementedError("kq.quantized_matmul: only transpose=True (wire rows are outputs)")
+    c = _cid(codec)
+    _need_cuda(x, w)
+    k = _wire_k(w, c)
+    w, wstride = _rows2d(w)
+    n = w.shape[-2] if w.dim() >= 2 else 1
+    x2 = _act_2d(x, k)
+    m = x2.shape[0]
+    od = out_dtype or x.dtype
+    y = torch.empty(m, n, dtype=od, device=x.device)
+    if m:
+        L = _lib.load()
+        ws = _workspace(x.device, L.kq_quantized_matmul_workspace_size(c, m, n, k))
+        _lib.check(L.kq_quantized_matmul(c, _p(x2), _DT[x2.dtype], m, k, x2.stride(0), _p(w), n, wstride, _p(y),
+                                         _DT[od], n, _p(ws), ws.numel(), _stream(x.device)), "quantized_matmul")
+    return y.reshape(*x.shape[:-1], n)
+
+
+def quantized_glu(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, codec=None, act: str = "silu",
+                  out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Fused ``act(x @ Wg.T) * (x @ Wu.T)`` for a dense gate/up pair (one launch)."""
+    c = _cid(codec)
+    _need_cuda(x, gate_w, up_w)
+    k = _wire_k(gate_w, c)
+    if gate_w.shape != up_w.shape:
+        raise ValueError("gate and up wire tensors must have the same shape")
+    gate_w, ws_ = _rows2d(gate_w)
+    up_w, ws2 = _rows2d(up_w)
+    if ws_ != ws2:
+        up_w = up_w.contiguous()
+        gate_w = gate_w.contiguous()
+        ws_ = gate_w.shape[-1]
+    n = gate_w.shape[-2]
+    x2 = _act_2d(x, k)
+    m = x2.shape[0]
+    od = out_dtype or x.dtype
+    y = torch.empty(m, n, dtype=od, device=x.device)
+    if m:
+        L = _lib.load()
+        ws = _workspace(x.device, L.kq_quantized_glu_workspace_size(c, m, n, k))
+        _lib.check(L.kq_quantized_glu(c, _p(x2), _DT[x2.dtype], m, k, x2.stride(0), _p(gate_w), _p(up_w), n, ws_,
+                                      _lib.ACTS[act], _p(y), _DT[od], n, _p(ws), ws.numel(), _stream(x.device)),
+                   "quantized_glu")
+    return y.reshape(*x.shape[:-1], n)
+
+
+def _stack(w: torch.Tensor) -> tuple[torch.Tensor, int, int]:
+    """Expert stack [E, N, bytes] (unit byte stride) -> (w, row stride, expert stride)."""
+    if w.dim() != 3:
+        raise ValueError(f"expert stack must be [E, N, bytes], got shape {tuple(w.shape)}")
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    return w, w.stride(1), w.stride(0)
+
+
+def moe_router_topk(logits: torch.Tensor, k: int, norm_topk_prob: bool = True, shared_gate=None,
+                    per_expert_scale=None):
+    """``kq.moe_router_topk``: softmax -> top-k -> optional renorm (f32)."""
+    if shared_gate is not None or per_expert_scale is not None:
+        raise NotImplementedError("moe_router_topk: shared_gate / per_expert_scale are not supported")
+    _need_cuda(logits)
+    lg = logits.reshape(-1, logits.shape[-1]).float().contiguous()
+    t, e = lg.shape
+    idx = torch.empty(t, k, dtype=torch.int32, device=lg.device)
+    sc = torch.empty(t, k, dtype=torch.float32, device=lg.device)
+    if t:
+        _lib.check(_lib.load().kq_moe_router_topk(_p(lg), t, e, k, int(bool(norm_topk_prob)), _p(idx), _p(sc),
+                                                  _stream(lg.device)), "moe_router_topk")
+    shape = (*logits.shape[:-1], k)
+    return idx.reshape(shape), sc.reshape(shape)
+
+
+def _idx2d(idx: torch.Tensor, t: int) -> torch.Tensor:
+    i = idx.reshape(t, -1)
+    if i.dtype != torch.int32:
+        i = i.to(torch.int32)
+    return i.contiguous()
+
+
+def moe_glu_gather_kq(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, codec, idx: torch.Tensor,
+                      act: str = "silu", out_dtype: torch.dtype | None = None, **kw) -> torch.Tensor:
+    """``kq.moe_glu_gather_kq(x[T,D], Wg, Wu, codec, idx[T,k], act)`` -> ``h[T,k,F]`` (f32 epilogue)."""
+    if kw:
+        raise NotImplementedError(f"moe_glu_gather_kq: unsupported arguments {sorted(kw)}")
+    c = _cid(codec)
+    _need_cuda(x, gate_w, up_w, idx)
+    d = _wire_k(gate_w, c)
+    gate_w, wrs, wes = _stack(gate_w)
+    up_w, wrs2, wes2 = _stack(up_w)
+    if (wrs, wes) != (wrs2, wes2) or gate_w.shape != up_w.shape:
+        raise ValueError("gate and up stacks must share shape and layout")
+    e, f = gate_w.shape[0], gate_w.shape[1]
+    x2 = _act_2d(x, d)
+    t = x2.shape[0]
+    i2 = _idx2d(idx, t)
+    k = i2.shape[1]
+    od = out_dtype or x.dtype
+    h = torch.empty(t, k, f, dtype=od, device=x.device)
+    if t:
+        L = _lib.load()
+        ws = _workspace(x.device, L.kq_moe_workspace_size(c, t * k, e, f, d))
+        _lib.check(L.kq_moe_glu_gather(c, _p(x2), _DT[x2.dtype], t, d, _p(i2), k, _p(gate_w), _p(up_w), e, f, wrs,
+                                       wes, _lib.ACTS[act], _p(h), _DT[od], _p(ws), ws.numel(), _stream(x.device)),
+                   "moe_glu_gather_kq")
+    return h
+
+
+def gather_qmv_kq(h: torch.Tensor, w: torch.Tensor, codec, idx: torch.Tensor, bias=None,
+                  out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``kq.gather_qmv_kq(h[T,k,F], W, codec, idx[T,k])`` -> ``y[T,k,N]``."""
+    c = _cid(codec)
+    _need_cuda(h, w, idx)
+    f = _wire_k(w, c)
+    w, wrs, wes = _stack(w)
+    e, n = w.shape[0], w.shape[1]
+    t = h.shape[0]
+    i2 = _idx2d(idx, t)
+    k = i2.shape[1]
+    h2 = _act_2d(h.reshape(t * k, f), f)
+    od = out_dtype or h.dtype
+    y = torch.empty(t, k, n, dtype=od, device=h.device)
+    if t:
+        L = _lib.load()
+        ws = _workspace(h.device, L.kq_moe_workspace_size(c, t * k, e, n, f))
+        _lib.check(L.kq_gather_qmv(c, _p(h2), _DT[h2.dtype], t, k, f, _p(i2), _p(w), e, n, wrs, wes, _p(y), _DT[od],
+                                   _p(ws), ws.numel(), _stream(h.device)), "gather_qmv_kq")
+    if bias is not None:
+        y = y + bias[idx.long()].to(y.dtype)
+    return y
+
+
+def gather_qmv_mix_ns_kq(h: torch.Tensor, w: torch.Tensor, codec, idx: torch.Tensor, scores: torch.Tensor,
+                         out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``kq.gather_qmv_mix_ns_kq``: ``y[t] = sum_j scores[t,j] * (h[t,j] @ W[idx[t,j]].T)`` (f32)."""
+    c = _cid(codec)
+    _need_cuda(h, w, idx, scores)
+    f = _wire_k(w, c)
+    w, wrs, wes = _stack(w)
+    e, n = w.shape[0], w.shape[1]
+    t = h.shape[0]
+    i2 = _idx2d(idx, t)
+    k = i2.shape[1]
+    h2 = _act_2d(h.reshape(t * k, f), f)
+    s2 = scores.reshape(t, k).float().contiguous()
+    od = out_dtype or h.dtype
+    y = torch.empty(t, n, dtype=od, device=h.device)
+    if t:
+        L = _lib.load()
+        ws = _workspace(h.device, L.kq_moe_workspace_size(c, t * k, e, n, f))
+        _lib.check(L.kq_gather_qmv_mix(c, _p(h2), _DT[h2.dtype], t, k, f, _p(i2), _p(s2), _p(w), e, n, wrs, wes,
+                                       _p(y), _DT[od], _p(ws), ws.numel(), _stream(h.device)), "gather_qmv_mix_ns_kq")
+    return y
+
+
+def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, lhs_indices=None, rhs_indices=None,
+               transpose: bool = True, sorted_indices: bool = False,
+               out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``kq.gather_qmm`` (mlx ``gather_qmm`` semantics over wire stacks):
+    ``out[b] = x[lhs[b]] @ dequant(w[rhs[b]]).T`` with ``b`` over the broadcast of
+    the index shapes (``x``'s batch dims stand in for ``lhs`` when it is None)."""
+    if not transpose:
+        raise NotImplementedError("kq.gather_qmm: only transpose=True")
+    c = _cid(codec)
+    _need_cuda(x, w)
+    kin = _wire_k(w, c)
+    w, wrs, wes = _stack(w)
+    e, n = w.shape[0], w.shape[1]
+    if x.shape[-1] != kin:
+        raise ValueError(f"activation K={x.shape[-1]} does not match weight K={kin}")
+    m = x.shape[-2]
+    xb_shape = x.shape[:-2]
+    xb = torch.arange(int(torch.tensor(xb_shape).prod().item()) if len(xb_shape) else 1, device=x.device)
+    xb = xb.reshape(xb_shape) if len(xb_shape) else xb.reshape(())
+    if lhs_indices is not None:
+        xb = xb.reshape(-1)[lhs_indices.long()]
+    rhs = torch.zeros((), dtype=torch.long, device=x.device) if rhs_indices is None else rhs_indices.long()
+    xb, rhs = torch.broadcast_tensors(xb, rhs)
+    bshape = xb.shape
+    xb, rhs = xb.reshape(-1), rhs.reshape(-1)
+    ar = torch.arange(m, device=x.device)
+    xrow = (xb[:, None] * m + ar[None, :]).reshape(-1).to(torch.int32).contiguous()
+    expert = rhs[:, None].expand(-1, m).reshape(-1).to(torch.int32).contiguous()
+    rows = xrow.numel()
+    x2 = _act_2d(x.reshape(-1, kin), kin)
+    od = out_dtype or x.dtype
+    y = torch.empty(rows, n, dtype=od, device=x.device)
+    if rows:
+        L = _lib.load()
+        ws = _workspace(x.device, L.kq_moe_workspace_size(c, rows, e, n, kin))
+        _lib.check(L.kq_gather_qmm(c, _p(x2), _DT[x2.dtype], kin, x2.stride(0), rows, _p(xrow), _p(expert), _p(w),
+                                   e, n, wrs, wes, _p(y), _DT[od], _p(ws), ws.numel(), _stream(x.device)),
+                   "gather_qmm")
+    return y.reshape(*bshape, m, n)

@@ -1,0 +1,116 @@
+"""Seeded synthetic K-quant / IQ-quant weights and activations.
+
+There are no GGUF files or datasets on the benchmark hosts, so every weight is
+a stack of random super-blocks drawn the way the benchmark configurations
+prescribe:
+
+* Q4_K (144 B): uniform random bytes, then the two fp16 scales ``d`` and
+  ``dmin`` overwritten with fp16(U[1e-4, 2e-3]).  (Raw random fp16 bytes would
+  hold NaN/Inf.)
+* Q6_K (210 B): random ``ql``/``qh``, the 16 int8 sub-block scales uniform in
+  [-64, 63], ``d`` (the last two bytes) fp16(U[1e-4, 2e-3]).
+* IQ2_XXS (66 B): random ``qs`` words (grid indices, sign indices and 4-bit
+  sub-scales all uniform), ``d`` fp16(U[1e-4, 2e-3]).
+
+Activations are bf16 N(0, 1); router logits are f32 N(0, 1).  All draws use
+``numpy.random.default_rng(seed)``.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+Q4_K, Q6_K, IQ2_XXS = 12, 14, 16
+CODECS = {"q4_k": Q4_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
+CODEC_NAMES = {v: k for k, v in CODECS.items()}
+BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, IQ2_XXS: 66}
+QK = 256
+D_LO, D_HI = 1e-4, 2e-3
+
+
+def codec_id(codec) -> int:
+    if isinstance(codec, str):
+        try:
+            return CODECS[codec.lower()]
+        except KeyError:
+            raise ValueError(f"unknown K-quant codec {codec!r}") from None
+    return int(codec)
+
+
+def row_bytes(codec, k: int) -> int:
+    c = codec_id(codec)
+    if k % QK:
+        raise ValueError(f"K={k} is not a whole number of {QK}-weight blocks")
+    return k // QK * BLOCK_BYTES[c]
+
+
+def _fp16_bytes(rng, n: int) -> np.ndarray:
+    v = rng.uniform(D_LO, D_HI, size=n).astype(np.float16)
+    return v.view(np.uint8).reshape(n, 2)
+
+
+def random_blocks(codec, n_blocks: int, seed: int = 0) -> np.ndarray:
+    """``[n_blocks, bpb]`` uint8 of seeded random super-blocks."""
+    c = codec_id(codec)
+    rng = np.random.default_rng(seed)
+    bpb = BLOCK_BYTES[c]
+    b = rng.integers(0, 256, size=(n_blocks, bpb), dtype=np.uint8)
+    if c == Q4_K:
+        b[:, 0:2] = _fp16_bytes(rng, n_blocks)
+        b[:, 2:4] = _fp16_bytes(rng, n_blocks)
+    elif c == Q6_K:
+        b[:, 192:208] = rng.integers(-64, 64, size=(n_blocks, 16), dtype=np.int8).view(np.uint8)
+        b[:, 208:210] = _fp16_bytes(rng, n_blocks)
+    elif c == IQ2_XXS:
+        b[:, 0:2] = _fp16_bytes(rng, n_blocks)
+    else:
+        raise ValueError(codec)
+    return b
+
+
+def random_weight(codec, n: int, k: int, seed: int = 0, experts: int | None = None) -> np.ndarray:
+    """Wire bytes ``[n, k/256*bpb]`` (or ``[experts, n, ...]``)."""
+    c = codec_id(codec)
+    nb = k // QK
+    e = 1 if experts is None else experts
+    b = random_blocks(c, e * n * nb, seed)
+    shape = (n, nb * BLOCK_BYTES[c]) if experts is None else (e, n, nb * BLOCK_BYTES[c])
+    return b.reshape(shape)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def random_activations(m: int, k: int, seed: int = 0) -> np.ndarray:
+    """bf16 N(0,1) activations as uint16 bits ``[m, k]``."""
+    rng = np.random.default_rng(seed)
+    return f32_to_bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+
+
+def random_logits(t: int, e: int, seed: int = 0) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return rng.standard_normal((t, e), dtype=np.float32)
+
+
+# Llama-3-8B decoder layer, Q4_K_M-style (benchmark configuration 2/3):
+# (name, codec, out N, in K) in projection order; weight seed = position.
+LLAMA3_8B_LAYER = (
+    ("q_proj", "q4_k", 4096, 4096),
+    ("k_proj", "q4_k", 1024, 4096),
+    ("v_proj", "q4_k", 1024, 4096),
+    ("o_proj", "q4_k", 4096, 4096),
+    ("gate_proj", "q4_k", 14336, 4096),
+    ("up_proj", "q4_k", 14336, 4096),
+    ("down_proj", "q6_k", 4096, 14336),
+)
+
+# MoE expert layers (benchmark configurations 4 and 5)
+QWEN3_30B_A3B_MOE = dict(experts=128, top_k=8, hidden=2048, ffn=768,
+                         gate_codec="q4_k", up_codec="q4_k", down_codec="q6_k")
+DEEPSEEK_V3_IQ2_MOE = dict(experts=256, top_k=8, hidden=7168, ffn=2048,
+                           gate_codec="iq2_xxs", up_codec="iq2_xxs", down_codec="iq2_xxs")
+
+
+def layer_weight_bytes(layer=LLAMA3_8B_LAYER) -> int:
+    return sum(n * row_bytes(c, k) for _, c, n, k in layer)

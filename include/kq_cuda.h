@@ -1,0 +1,163 @@
+/*
+ * kq_cuda.h -- C ABI of libkq_cuda.so, the B200 (sm_100a) fused
+ * dequantize-and-multiply library for GGUF K-quant / IQ-quant weights.
+ *
+ * It replaces the kernel library that gmlx reaches as ``import mlx_kquant as
+ * kq`` (gmlx/modules.py:35-40; pinned mlx-kquant>=0.3.13,<0.4 at
+ * pyproject.toml:33).  Each entry point below names the kq op and the gmlx
+ * call site(s) it serves.  Conventions:
+ *
+ *  - All pointers are device pointers unless stated; sizes are element counts
+ *    unless the name ends in _bytes / _stride (bytes for weights, elements for
+ *    activations).  Weight rows are raw GGUF wire bytes, never repacked.
+ *  - Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *    default stream) and returns KQ_OK or a KQ_ERR_* code; a human-readable
+ *    message for the calling thread is available from kq_last_error().
+ *    Nothing crosses the ABI as an exception.
+ *  - Calls that take a `workspace` need kq_*_workspace_size() bytes of device
+ *    memory, 256-byte aligned and zero-filled before its first use.  The
+ *    library leaves it zeroed after every successful call (self-resetting
+ *    split-K counters), so one workspace can be reused by consecutive calls
+ *    on one stream; calls that overlap in time must use different workspaces.
+ *    The first int of a workspace is a sticky device error word set by a
+ *    kernel whose bounded wait ran out (read it with kq_workspace_error).
+ *  - Codec ids are ggml's: Q4_K = 12, Q6_K = 14, IQ2_XXS = 16.
+ *    Activation / output dtypes: KQ_F32 = 0, KQ_F16 = 1, KQ_BF16 = 2.
+ */
+#ifndef KQ_CUDA_H
+#define KQ_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KQ_Q4_K 12
+#define KQ_Q6_K 14
+#define KQ_IQ2_XXS 16
+
+#define KQ_F32 0
+#define KQ_F16 1
+#define KQ_BF16 2
+
+#define KQ_ACT_NONE 0
+#define KQ_ACT_SILU 1
+#define KQ_ACT_GELU 2
+#define KQ_ACT_GELU_TANH 3
+
+#define KQ_OK 0
+#define KQ_ERR_CODEC 1     /* unknown / unsupported codec */
+#define KQ_ERR_SHAPE 2     /* K not a whole number of blocks, bad sizes */
+#define KQ_ERR_ALIGN 3     /* pointer or stride alignment */
+#define KQ_ERR_DTYPE 4     /* unsupported activation / output dtype */
+#define KQ_ERR_CUDA 5      /* CUDA runtime error (launch, attribute) */
+#define KQ_ERR_WORKSPACE 6 /* workspace missing or too small */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int kq_version(void);
+
+/* Message describing the last failed call on this thread ("" if none). */
+const char *kq_last_error(void);
+
+/* Codec capability query; replaces kq.codecs() (checked against the loader's
+ * whitelist at gmlx/preflight.py:625-632, tests/test_preflight.py:99).
+ * Writes up to `cap` codec ids to `out`, returns how many codecs exist. */
+int kq_codecs(int *out, int cap);
+
+/* 1 when `codec` has matmul / gather kernels here (gmlx probes this through
+ * _FusedMoeCaps, gmlx/modules.py:155-234), else 0. */
+int kq_codec_has_matmul(int codec);
+
+/* Bytes per 256-weight super-block of `codec` (gguf GGML_QUANT_SIZES, used by
+ * gmlx/modules.py:250-255 _kq_wire_k), or -1. */
+int kq_block_bytes(int codec);
+
+/* kq.dequantize(w, scales, codec, dtype): rows x k weights, row r at
+ * w + r*w_row_stride bytes -> out[rows][k] (dense, out_dtype).  f32 output is
+ * bit-identical to ggml/gguf-py block dequantization.
+ * Call sites: gmlx/modules.py:1461, gmlx/loader.py:3046-3048,
+ * gmlx/dsv32_patches.py:229. */
+int kq_dequantize(int codec, const void *w, int64_t rows, int64_t k, int64_t w_row_stride, void *out, int out_dtype,
+                  void *stream);
+
+/* kq.quantized_matmul(x, w, scales, codec, transpose=True):
+ *   y[m][n] = sum_k x[m][k] * dequant(W)[n][k]   (f32 accumulate)
+ * x: [m][k] f16/bf16, row stride x_row_stride elements (multiple of 8);
+ * w: [n] rows of k/256 blocks, row stride w_row_stride bytes;
+ * y: [m][n] f32/f16/bf16 with row stride y_row_stride elements.
+ * Decode-sized m uses the streaming GEMV kernels; prefill-sized m the
+ * tensor-core (tcgen05) GEMM.
+ * Call sites: KQuantLinear (gmlx/modules.py:1535-1539), gmlx/occupancy_fuse.py:
+ * 284-287, 412-418, 434-437, gmlx/mtp_load.py:298. */
+int kq_quantized_matmul(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
+                        const void *w, int64_t n, int64_t w_row_stride, void *y, int y_dtype, int64_t y_row_stride,
+                        void *workspace, size_t workspace_bytes, void *stream);
+size_t kq_quantized_matmul_workspace_size(int codec, int64_t m, int64_t n, int64_t k);
+
+/* Fused gate/up projection with activation, one launch:
+ *   y[m][n] = act(x[m] . Wg[n]) * (x[m] . Wu[n])
+ * The dense analogue of moe_glu_gather_kq for a row-concatenated gate/up pair
+ * (gmlx/occupancy_fuse.py:412-418 splits a fused gate+up matmul, then applies
+ * the activation in Python). */
+int kq_quantized_glu(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
+                     const void *gate_w, const void *up_w, int64_t n, int64_t w_row_stride, int act, void *y,
+                     int y_dtype, int64_t y_row_stride, void *workspace, size_t workspace_bytes, void *stream);
+size_t kq_quantized_glu_workspace_size(int codec, int64_t m, int64_t n, int64_t k);
+
+/* kq.moe_router_topk(logits, k, norm_topk_prob): softmax over E (f32),
+ * top-k (descending; ties -> lower id), optional renormalisation.
+ * logits [t][e] f32, e <= 1024, k <= 16 -> idx [t][k] int32, scores [t][k] f32.
+ * Call sites: gmlx/modules.py:446-447, 751-752; semantics of the stock
+ * forward gmlx/moe_experts.py:226-240. */
+int kq_moe_router_topk(const float *logits, int64_t t, int64_t e, int k, int norm_topk_prob, int32_t *idx,
+                       float *scores, void *stream);
+
+/* kq.moe_glu_gather_kq(x, gate_w, up_w, codec, idx, act):
+ *   h[t][j][f] = act(x[t] . Wg[idx[t][j]][f]) * (x[t] . Wu[idx[t][j]][f])
+ * x [t][d] f16/bf16; idx [t][k] int32 device; gate/up stacks [e][f] rows of
+ * d/256 blocks (row / expert strides in bytes, shared by both stacks);
+ * h [t][k][f] in h_dtype.  Each routed expert's weights stream once.
+ * Call sites: gmlx/modules.py:585-588, 980-983. */
+int kq_moe_glu_gather(int codec, const void *x, int x_dtype, int64_t t, int64_t d, const int32_t *idx, int k,
+                      const void *gate_w, const void *up_w, int64_t e, int64_t f, int64_t w_row_stride,
+                      int64_t w_expert_stride, int act, void *h, int h_dtype, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/* kq.gather_qmv_kq(h, w, codec, idx):  y[t][j][n] = h[t][j] . W[idx[t][j]][n]
+ * h [t][k][f] f16/bf16 -> y [t][k][n].  Call site: gmlx/modules.py:596-598. */
+int kq_gather_qmv(int codec, const void *h, int h_dtype, int64_t t, int k, int64_t f, const int32_t *idx,
+                  const void *w, int64_t e, int64_t n, int64_t w_row_stride, int64_t w_expert_stride, void *y,
+                  int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
+
+/* kq.gather_qmv_mix_ns_kq(h, w, codec, idx, scores):
+ *   y[t][n] = sum_j scores[t][j] * (h[t][j] . W[idx[t][j]][n])   (f32, fixed j order)
+ * scores [t][k] f32.  Call sites: gmlx/modules.py:591-593, 989-991. */
+int kq_gather_qmv_mix(int codec, const void *h, int h_dtype, int64_t t, int k, int64_t f, const int32_t *idx,
+                      const float *scores, const void *w, int64_t e, int64_t n, int64_t w_row_stride,
+                      int64_t w_expert_stride, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                      void *stream);
+
+/* kq.gather_qmm(x, w, scales, rhs_indices=...) flattened to rows:
+ *   y[r][n] = x[x_index[r]] . W[expert_index[r]][n]   for r < rows
+ * (KQuantSwitchLinear, gmlx/modules.py:1548-1552; the sorted-indices prefill
+ * variant at gmlx/modules.py:1308-1309).  x_index may be NULL (row r). */
+int kq_gather_qmm(int codec, const void *x, int x_dtype, int64_t k, int64_t x_row_stride, int64_t rows,
+                  const int32_t *x_index, const int32_t *expert_index, const void *w, int64_t e, int64_t n,
+                  int64_t w_row_stride, int64_t w_expert_stride, void *y, int y_dtype, void *workspace,
+                  size_t workspace_bytes, void *stream);
+
+/* Workspace bytes for the MoE calls above with `slots` = t*k routed rows
+ * (or `rows` for kq_gather_qmm), over stacks of e experts, n outputs, k_in
+ * inputs. */
+size_t kq_moe_workspace_size(int codec, int64_t slots, int64_t e, int64_t n, int64_t k_in);
+
+/* Reads (and with clear != 0 resets) the workspace's device error word;
+ * synchronises `stream`.  Returns the word (0 = no device-side error). */
+int kq_workspace_error(void *workspace, int clear, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KQ_CUDA_H */

@@ -1,0 +1,233 @@
+/*
+ * kq_oracle.c -- CPU restatement of the GGUF K-quant / IQ-quant block formats
+ * on the fused dequantize-and-multiply path.  TEST INFRASTRUCTURE ONLY: this
+ * file is the checker the CUDA kernels are compared against, and the timed
+ * CPU baseline.  The product library (libkq_cuda.so) never links or calls it.
+ *
+ * The reference (gmlx) reaches these formats through the external mlx-kquant
+ * library (gmlx/modules.py:35-40, pinned at pyproject.toml:33), whose source is
+ * not available.  The published block semantics it implements are those of
+ * ggml; the runnable restatement in this environment is gguf-py 0.19.0
+ * (gguf/quants.py), a declared gmlx dependency (pyproject.toml:62).  Each
+ * decoder below cites the gguf-py function it follows; the Python tests pin
+ * this file bit-for-bit against gguf-py on seeded blocks and edge cases.
+ *
+ * Arithmetic order matches gguf-py exactly (all f32):
+ *   Q4_K   (quants.py:504-522): dl = d*sc, ml = dmin*m, w = dl*q - ml
+ *   Q6_K   (quants.py:554-572): dl = d*sc, w = dl*(q-32)
+ *   IQ2_XXS(quants.py:802-829): db = d*(0.5+ls)*0.25, w = db*grid*sign
+ * Every product above is exact in f32 (see the kernels' header), so results
+ * are independent of FMA contraction; the file is still built with
+ * -ffp-contract=off to keep the statement literal.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#include "kq_tables.h"
+
+#define QK 256
+enum { KQO_Q4_K = 12, KQO_Q6_K = 14, KQO_IQ2_XXS = 16 };
+
+static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
+
+/* IEEE binary16 -> f32, exact (gguf-py: view(np.float16).astype(np.float32)). */
+static float kqo_half(uint16_t h) {
+    uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 0x1f, m = h & 0x3ff, u;
+    if (e == 0) {
+        if (m == 0) { u = s; }
+        else { /* subnormal: renormalise */
+            e = 113;
+            while (!(m & 0x400)) { m <<= 1; e--; }
+            u = s | (e << 23) | ((m & 0x3ff) << 13);
+        }
+    } else if (e == 31) {
+        u = s | 0x7f800000u | (m << 13);
+    } else {
+        u = s | ((e + 112) << 23) | (m << 13);
+    }
+    float f; memcpy(&f, &u, 4); return f;
+}
+
+static float kqo_bf16(uint16_t b) { uint32_t u = (uint32_t)b << 16; float f; memcpy(&f, &u, 4); return f; }
+
+int kqo_block_bytes(int codec) {
+    switch (codec) { case KQO_Q4_K: return 144; case KQO_Q6_K: return 210; case KQO_IQ2_XXS: return 66; }
+    return -1;
+}
+
+/* gguf-py Q4_K.get_scale_min (quants.py:479-501): 12 packed bytes -> 8 x (sc, m). */
+static void q4k_scale_min(const uint8_t *s, uint8_t sc[8], uint8_t mn[8]) {
+    for (int j = 0; j < 4; j++) {
+        sc[j] = s[j] & 0x3f;
+        mn[j] = s[j + 4] & 0x3f;
+        sc[j + 4] = (s[j + 8] & 0x0f) | ((s[j] >> 2) & 0x30);
+        mn[j + 4] = (s[j + 8] >> 4) | ((s[j + 4] >> 2) & 0x30);
+    }
+}
+
+/* gguf-py Q4_K.dequantize_blocks (quants.py:504-522). */
+static void deq_q4k(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    float dmin = kqo_half((uint16_t)(b[2] | b[3] << 8));
+    uint8_t sc[8], mn[8];
+    q4k_scale_min(b + 4, sc, mn);
+    const uint8_t *q = b + 16;
+    for (int c = 0; c < 4; c++) {          /* 32-byte chunk c -> sub-blocks 2c, 2c+1 */
+        for (int h = 0; h < 2; h++) {      /* low nibble, then high nibble */
+            int j = 2 * c + h;
+            float dl = d * (float)sc[j], ml = dmin * (float)mn[j];
+            for (int l = 0; l < 32; l++) {
+                float qv = (float)((q[32 * c + l] >> (4 * h)) & 0x0f);
+                o[32 * j + l] = dl * qv - ml;
+            }
+        }
+    }
+}
+
+/* gguf-py Q6_K.dequantize_blocks (quants.py:554-572). */
+static void deq_q6k(const uint8_t *b, float *o) {
+    const uint8_t *ql = b, *qh = b + 128;
+    const int8_t *sc = (const int8_t *)(b + 192);
+    float d = kqo_half((uint16_t)(b[208] | b[209] << 8));
+    for (int hf = 0; hf < 2; hf++) {       /* two 128-weight halves */
+        for (int s = 0; s < 4; s++) {      /* 32-weight group s of the half */
+            for (int l = 0; l < 32; l++) {
+                int i = 128 * hf + 32 * s + l;
+                int lo = (ql[64 * hf + 32 * (s & 1) + l] >> (4 * (s >> 1))) & 0x0f;
+                int hi = (qh[32 * hf + l] >> (2 * s)) & 0x03;
+                int q = (lo | (hi << 4)) - 32;
+                float dl = d * (float)sc[i / 16];
+                o[i] = dl * (float)q;
+            }
+        }
+    }
+}
+
+/* ggml's ksigns table: 7-bit index plus an even-parity top bit
+ * (gguf-py IQ2_XXS.ksigns, quants.py:767-776, is this table written out). */
+static uint8_t kqo_ksigns(unsigned i) {
+    unsigned p = i ^ (i >> 4); p ^= p >> 2; p ^= p >> 1;
+    return (uint8_t)(i | ((p & 1) << 7));
+}
+
+/* gguf-py IQ2_XXS.dequantize_blocks (quants.py:802-829). */
+static void deq_iq2xxs(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    for (int g = 0; g < 8; g++) {
+        uint32_t a0, a1;
+        memcpy(&a0, b + 2 + 8 * g, 4);
+        memcpy(&a1, b + 6 + 8 * g, 4);
+        float db = d * (0.5f + (float)(a1 >> 28)) * 0.25f;
+        for (int s = 0; s < 4; s++) {
+            uint8_t sg = kqo_ksigns((a1 >> (7 * s)) & 0x7f);
+            uint64_t e = kqo_grid[(a0 >> (8 * s)) & 0xff];
+            for (int i = 0; i < 8; i++) {
+                float gv = (float)((e >> (8 * i)) & 0xff);
+                float sv = ((sg >> i) & 1) ? -1.0f : 1.0f;
+                o[32 * g + 8 * s + i] = db * gv * sv;
+            }
+        }
+    }
+}
+
+static int deq_block(int codec, const uint8_t *b, float *o) {
+    switch (codec) {
+    case KQO_Q4_K: deq_q4k(b, o); return 0;
+    case KQO_Q6_K: deq_q6k(b, o); return 0;
+    case KQO_IQ2_XXS: deq_iq2xxs(b, o); return 0;
+    }
+    return -1;
+}
+
+/* Dequantize rows x k weights; row r starts at w + r*row_stride bytes. */
+int kqo_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t k, int64_t row_stride,
+                   float *out, int threads) {
+    int bpb = kqo_block_bytes(codec);
+    if (bpb < 0 || k % QK) return -1;
+    int64_t nb = k / QK;
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel for schedule(static)
+#endif
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t b = 0; b < nb; b++)
+            deq_block(codec, w + r * row_stride + b * bpb, out + r * k + b * QK);
+    return 0;
+}
+
+/* Reference matmul y[m][n] = sum_k x[m][k] * dequant(W)[n][k], f32 accumulate
+ * in index order, x given as bf16 bits (x_bf16 != 0) or f32.  Dequantizes one
+ * row at a time (the reference's CPU dequantize-then-matmul arm). */
+int kqo_matmul(int codec, const void *x, int x_bf16, int64_t m, int64_t k,
+               const uint8_t *w, int64_t n, int64_t row_stride, float *y, int threads) {
+    int bpb = kqo_block_bytes(codec);
+    if (bpb < 0 || k % QK) return -1;
+    int64_t nb = k / QK;
+    float *xf = (float *)malloc(sizeof(float) * (size_t)(m * k));
+    if (!xf) return -2;
+    for (int64_t i = 0; i < m * k; i++)
+        xf[i] = x_bf16 ? kqo_bf16(((const uint16_t *)x)[i]) : ((const float *)x)[i];
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel
+#endif
+    {
+        float *wr = (float *)malloc(sizeof(float) * (size_t)k);
+#ifdef _OPENMP
+#pragma omp for schedule(static)
+#endif
+        for (int64_t r = 0; r < n; r++) {
+            for (int64_t b = 0; b < nb; b++) deq_block(codec, w + r * row_stride + b * bpb, wr + b * QK);
+            for (int64_t i = 0; i < m; i++) {
+                /* eight interleaved f32 partial sums (vectorisable without
+                 * reassociation flags), combined pairwise at the end */
+                const float *xr = xf + i * k;
+                float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int64_t j = 0; j < k; j += 8)
+                    for (int u = 0; u < 8; u++) acc[u] += xr[j + u] * wr[j + u];
+                y[i * n + r] = ((acc[0] + acc[4]) + (acc[2] + acc[6])) + ((acc[1] + acc[5]) + (acc[3] + acc[7]));
+            }
+        }
+        free(wr);
+    }
+    free(xf);
+    return 0;
+}
+
+/* MoE router (gmlx/moe_experts.py:226-240): softmax over E logits (f32,
+ * max-subtracted), top-k by probability (ties -> lower expert id), optional
+ * renormalisation of the k scores.  Output order: descending probability. */
+int kqo_router_topk(const float *logits, int64_t t, int64_t e, int k, int norm,
+                    int32_t *idx, float *scores) {
+    if (k <= 0 || k > e) return -1;
+    float *p = (float *)malloc(sizeof(float) * (size_t)e);
+    for (int64_t r = 0; r < t; r++) {
+        const float *l = logits + r * e;
+        float mx = -INFINITY, s = 0.f;
+        for (int64_t j = 0; j < e; j++) mx = l[j] > mx ? l[j] : mx;
+        for (int64_t j = 0; j < e; j++) { p[j] = expf(l[j] - mx); s += p[j]; }
+        for (int64_t j = 0; j < e; j++) p[j] = p[j] / s;
+        float tot = 0.f;
+        for (int c = 0; c < k; c++) {
+            int64_t best = -1;
+            for (int64_t j = 0; j < e; j++) {
+                int taken = 0;
+                for (int q = 0; q < c; q++) taken |= idx[r * k + q] == (int32_t)j;
+                if (taken) continue;
+                if (best < 0 || p[j] > p[best]) best = j;
+            }
+            idx[r * k + c] = (int32_t)best;
+            scores[r * k + c] = p[best];
+            tot += p[best];
+        }
+        if (norm)
+            for (int c = 0; c < k; c++) scores[r * k + c] /= tot;
+    }
+    free(p);
+    return 0;
+}

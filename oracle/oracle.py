@@ -1,0 +1,198 @@
+"""CPU oracle for the K-quant / IQ-quant fused dequantize-and-multiply path.
+
+TEST INFRASTRUCTURE ONLY.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+CPU-baseline legs of ``bench.py`` import this module; the product package
+(``gmlx_b200``) never does.
+
+Two restatements of the reference's block arithmetic live here:
+
+* ``libkq_oracle.so`` (``kq_oracle.c``, OpenMP) -- dequantize, dequantize-then-
+  matmul and the MoE router; it is the fast checker and the timed CPU baseline.
+* ``np_dequantize`` -- a pure-numpy statement of the same three decoders used
+  to cross-check the C file on small inputs.
+
+Both follow gguf-py 0.19.0 ``gguf/quants.py`` (Q4_K ``:475-522``, Q6_K
+``:552-572``, IQ2_XXS ``:766-829``), the ggml-format restatement that gmlx
+itself depends on (gmlx ``pyproject.toml:62``); the external mlx-kquant
+kernels that gmlx calls (gmlx ``modules.py:35-40``) are not available.  The
+tests pin both against gguf-py and against committed golden vectors.
+
+MoE helpers restate gmlx's routing forward (``gmlx/moe_experts.py:226-240``)
+and the fused decode ops' semantics (``gmlx/modules.py:514-605``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
+
+Q4_K, Q6_K, IQ2_XXS = 12, 14, 16
+CODEC_IDS = {"q4_k": Q4_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
+BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, IQ2_XXS: 66}
+QK = 256
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile ``libkq_oracle.so`` with the committed Makefile."""
+    if force or not os.path.exists(LIB_PATH):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        i64, vp, i32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
+        L.kqo_dequantize.argtypes = [i32, vp, i64, i64, i64, vp, i32]
+        L.kqo_matmul.argtypes = [i32, vp, i32, i64, i64, vp, i64, i64, vp, i32]
+        L.kqo_router_topk.argtypes = [vp, i64, i64, i32, i32, vp, vp]
+        for f in (L.kqo_dequantize, L.kqo_matmul, L.kqo_router_topk):
+            f.restype = i32
+        _lib = L
+    return _lib
+
+
+def codec_id(codec) -> int:
+    return CODEC_IDS[codec.lower()] if isinstance(codec, str) else int(codec)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def dequantize(w: np.ndarray, codec, threads: int = 0) -> np.ndarray:
+    """Wire bytes ``[rows, nb*bpb]`` (uint8, C-contiguous) -> f32 ``[rows, nb*256]``."""
+    c = codec_id(codec)
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    rows, nbytes = w.reshape(-1, w.shape[-1]).shape
+    assert nbytes % BLOCK_BYTES[c] == 0
+    k = nbytes // BLOCK_BYTES[c] * QK
+    out = np.empty((rows, k), np.float32)
+    rc = lib().kqo_dequantize(c, _ptr(w), rows, k, nbytes, _ptr(out), threads)
+    assert rc == 0, rc
+    return out.reshape(*w.shape[:-1], k)
+
+
+def matmul(x_bf16_bits: np.ndarray, w: np.ndarray, codec, threads: int = 0) -> np.ndarray:
+    """``y = x @ dequant(w).T`` in f32; x given as uint16 bf16 bits ``[M, K]``."""
+    c = codec_id(codec)
+    x = np.ascontiguousarray(x_bf16_bits, dtype=np.uint16)
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    m, k = x.shape
+    n, nbytes = w.shape
+    assert nbytes // BLOCK_BYTES[c] * QK == k
+    y = np.empty((m, n), np.float32)
+    rc = lib().kqo_matmul(c, _ptr(x), 1, m, k, _ptr(w), n, nbytes, _ptr(y), threads)
+    assert rc == 0, rc
+    return y
+
+
+def router_topk(logits: np.ndarray, k: int, norm_topk_prob: bool = True):
+    """softmax -> top-k -> optional renorm; returns (idx int32 [T,k], scores f32 [T,k])."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    t, e = lg.shape
+    idx = np.empty((t, k), np.int32)
+    sc = np.empty((t, k), np.float32)
+    rc = lib().kqo_router_topk(_ptr(lg), t, e, k, int(norm_topk_prob), _ptr(idx), _ptr(sc))
+    assert rc == 0, rc
+    return idx, sc
+
+
+# --------------------------------------------------------------------------
+# bf16 helpers (round-to-nearest-even, as torch and the kernels round)
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return r.astype(np.uint16)
+
+
+# --------------------------------------------------------------------------
+# pure-numpy restatement (small inputs)
+
+def _half(b2: np.ndarray) -> np.ndarray:
+    return b2.copy().view(np.float16).astype(np.float32)
+
+
+def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
+    """numpy statement of the three decoders (follows gguf/quants.py)."""
+    c = codec_id(codec)
+    bpb = BLOCK_BYTES[c]
+    blocks = np.ascontiguousarray(w, np.uint8).reshape(-1, bpb)
+    n = blocks.shape[0]
+    if c == Q4_K:  # quants.py:504-522
+        d = _half(blocks[:, 0:2]).reshape(n, 1)
+        dmin = _half(blocks[:, 2:4]).reshape(n, 1)
+        s = blocks[:, 4:16].astype(np.uint8)
+        sc = np.concatenate([s[:, 0:4] & 63, (s[:, 8:12] & 15) | ((s[:, 0:4] >> 2) & 48)], 1)
+        mn = np.concatenate([s[:, 4:8] & 63, (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 2) & 48)], 1)
+        q = blocks[:, 16:].reshape(n, 4, 1, 32) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
+        q = (q & 15).reshape(n, 8, 32).astype(np.float32)
+        dl = (d * sc.astype(np.float32)).reshape(n, 8, 1)
+        ml = (dmin * mn.astype(np.float32)).reshape(n, 8, 1)
+        out = dl * q - ml
+    elif c == Q6_K:  # quants.py:554-572
+        ql, qh = blocks[:, :128], blocks[:, 128:192]
+        sc = blocks[:, 192:208].view(np.int8).astype(np.float32)
+        d = _half(blocks[:, 208:210]).reshape(n, 1)
+        dl = (d * sc).reshape(n, 16, 1)
+        lo = (ql.reshape(n, 2, 1, 64) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)) & 15
+        hi = (qh.reshape(n, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
+        q = (lo.reshape(n, 8, 32) | (hi.reshape(n, 8, 32) << 4)).astype(np.int8) - np.int8(32)
+        out = dl * q.reshape(n, 16, 16).astype(np.float32)
+    elif c == IQ2_XXS:  # quants.py:802-829
+        from_grid = iq2xxs_grid()
+        d = _half(blocks[:, 0:2]).reshape(n, 1)
+        qs = blocks[:, 2:].copy().view(np.uint32).reshape(n, 8, 2)
+        db = (d * (np.float32(0.5) + (qs[..., 1] >> 28).astype(np.float32)) * np.float32(0.25))
+        db = db.reshape(n, 8, 1, 1)
+        sidx = (qs[..., 1].reshape(n, 8, 1) >> np.array([0, 7, 14, 21], np.uint32)) & 127
+        ks = ksigns_table()[sidx].reshape(n, 8, 4, 1)
+        sgn = np.where((ks >> np.arange(8, dtype=np.uint8)) & 1, np.float32(-1), np.float32(1))
+        gidx = qs[..., 0].copy().view(np.uint8).reshape(n, 8, 4)
+        g = from_grid[gidx].astype(np.float32)
+        out = db * g * sgn
+    else:
+        raise ValueError(codec)
+    return out.reshape(*np.asarray(w).shape[:-1], -1).astype(np.float32)
+
+
+def ksigns_table() -> np.ndarray:
+    """ggml ksigns: 7-bit index with an even-parity bit 7."""
+    i = np.arange(128, dtype=np.uint8)
+    p = np.zeros(128, np.uint8)
+    for b in range(7):
+        p ^= (i >> b) & 1
+    return (i | (p << 7)).astype(np.uint8)
+
+
+_GRID = None
+
+
+def iq2xxs_grid() -> np.ndarray:
+    """``[256, 8]`` uint8 magnitudes, parsed from the generated kernel header."""
+    global _GRID
+    if _GRID is None:
+        hdr = os.path.join(HERE, "..", "gmlx_b200", "csrc", "_gen", "kq_tables.h")
+        if not os.path.exists(hdr):
+            build(force=True)
+        vals = [int(t.strip().rstrip(",").rstrip("ull").rstrip("u"), 16)
+                for t in open(hdr).read().split("{", 1)[1].split("}")[0].replace("\\", "").split()
+                if t.startswith("0x")]
+        assert len(vals) == 256
+        _GRID = np.array([[(v >> (8 * i)) & 0xFF for i in range(8)] for v in vals], np.uint8)
+    return _GRID
