@@ -112,7 +112,6 @@ GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k,
     a.y_row_stride = ys;
     a.act = act;
     a.max_tokens = (int)(m < 32 ? m : 32);
-    a.splits = gemv_choose_splits(codec, (int)n, (int)k, a.max_groups, a.max_tokens, act != ACT_NONE, num_sms());
     return a;
 }
 
@@ -182,7 +181,6 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     a.max_groups = maxg;
     a.act = act;
     a.max_tokens = gsize;
-    a.splits = gemv_choose_splits(codec, (int)n, (int)kin, maxg, gsize, act != ACT_NONE, num_sms());
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
     const size_t ys_bytes = scores ? (size_t)slots * n * sizeof(float) : 0;
@@ -232,7 +230,7 @@ size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_
     a.K = (int)kin;
     a.max_groups = maxg;
     a.act = act;
-    a.splits = gemv_choose_splits(codec, (int)n, (int)kin, maxg, gsize, act != ACT_NONE, num_sms());
+    a.max_tokens = gsize;
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
     return plan((size_t)maxg * 66, mix ? (size_t)slots * n * sizeof(float) : 0, cb, pb).total;

@@ -36,17 +36,15 @@ struct GemvArgs {
     void *y;
     int y_dtype;
     int64_t y_row_stride;
-    int act;     // ACT_NONE: plain; otherwise fused GLU y = act(x.Wg) * (x.Wu)
-    int splits;  // K splits (>1 needs partial + counters scratch)
-    float *partial;
-    int *counters;
+    int act;         // ACT_NONE: plain; otherwise fused GLU y = act(x.Wg) * (x.Wu)
+    float *partial;  // stream-K partial tiles: 2 x grid x 1024 floats
+    int *counters;   // one per (group, tile), zero on entry, left zero
     int *err;
     int max_tokens;  // upper bound of rows in any group (<= 32)
 };
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st);
-// Scratch the GEMV needs for `a` (bytes of f32 partials, ints of counters).
+// Scratch the GEMV needs for `a` (bytes of f32 partials, bytes of counters).
 void gemv_scratch_need(const GemvArgs &a, size_t *partial_bytes, size_t *counter_bytes);
-int gemv_choose_splits(int codec, int N, int K, int max_groups, int max_tokens, bool glu, int num_sms);
 
 // MoE slot grouping: idx[S] (S = T*k slots) -> per-expert groups of <= gsize
 // slots (ascending slot order inside a group, groups ordered by expert id).
