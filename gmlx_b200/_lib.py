@@ -42,6 +42,7 @@ SIGNATURES = {
                              _sz, _vp]),
     "kq_moe_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64]),
     "kq_workspace_error": (_i32, [_vp, _i32, _vp]),
+    "kq_quantized_matmul_noalloc": (_i32, [_i32, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _vp]),
 }
 
 _lib = None

@@ -238,6 +238,8 @@ size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_
 
 }  // namespace
 
+void kq::set_last_error(const char *msg) { snprintf(g_msg, sizeof(g_msg), "%s", msg); }
+
 extern "C" {
 
 int kq_version(void) { return 100; }

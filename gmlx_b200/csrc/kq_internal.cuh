@@ -59,5 +59,7 @@ cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int nor
                                int *err, cudaStream_t st);
 
 int num_sms();
+// Sets the calling thread's kq_last_error() message.
+void set_last_error(const char *msg);
 
 }  // namespace kq

@@ -153,6 +153,24 @@ int kq_gather_qmm(int codec, const void *x, int x_dtype, int64_t k, int64_t x_ro
  * inputs. */
 size_t kq_moe_workspace_size(int codec, int64_t slots, int64_t e, int64_t n, int64_t k_in);
 
+/* Size of the fixed scratch array behind kq_quantized_matmul_noalloc. */
+#define KQ_NOALLOC_SCRATCH_BYTES (4 << 20)
+
+/* kq_quantized_matmul for callers that cannot allocate device memory (a host
+ * framework whose allocator owns the GPU, a plugin that may not allocate after
+ * start-up, a latency-critical path where an allocation could block or fail).
+ * No counterpart in the reference: it is an addition of this library.  Same
+ * arguments and result as kq_quantized_matmul minus the workspace: the split-K
+ * scratch comes from one library-owned device array of KQ_NOALLOC_SCRATCH_BYTES
+ * per GPU (held until exit).  It allocates nothing.  The first call on a
+ * device looks up that array's device address (make it before any stream
+ * capture); each call clears the scratch it uses on `stream`; calls whose GPU
+ * work overlaps race on the shared array.  Shapes needing more scratch than
+ * the array holds return KQ_ERR_WORKSPACE. */
+int kq_quantized_matmul_noalloc(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
+                                const void *w, int64_t n, int64_t w_row_stride, void *y, int y_dtype,
+                                int64_t y_row_stride, void *stream);
+
 /* Reads (and with clear != 0 resets) the workspace's device error word;
  * synchronises `stream`.  Returns the word (0 = no device-side error). */
 int kq_workspace_error(void *workspace, int clear, void *stream);
