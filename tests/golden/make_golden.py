@@ -1,0 +1,125 @@
+"""Generate the committed golden vectors for the three block formats.
+
+Source of truth: gguf-py 0.19.0 (``gguf.quants.dequantize``), the restatement
+of ggml's block formats that gmlx depends on (gmlx pyproject.toml:62).  The
+reference's own kernels (external mlx-kquant) ship no numeric tests; these
+vectors pin the oracle and the CUDA kernels instead.  Run from the repo root:
+
+    python tests/golden/make_golden.py
+
+Each codec gets (a) seeded random blocks per the benchmark statistics and
+(b) known-answer / edge blocks:
+  Q4_K   all-zero quants (w = -dmin*m), scale/min = 0 and 63 on every
+         sub-block, one-hot sub-block scales;
+  Q6_K   int8 scales at -128, -64, 0, 63, 127; quants all 0 / all 63;
+  IQ2_XXS every grid index and every 7-bit sign index, ls = 0 and 15.
+Matmul references are x @ dequant(W).T in float64 for bf16 x (N(0,1)) plus
+one-hot x rows, which must reproduce single dequantized columns exactly.
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from gguf.constants import GGMLQuantizationType as T  # noqa: E402
+from gguf.quants import dequantize  # noqa: E402
+
+from gmlx_b200 import synth  # noqa: E402
+
+QT = {"q4_k": T.Q4_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}
+
+
+def fp16(v):
+    return np.array([v], np.float16).view(np.uint8)
+
+
+def edge_blocks(codec):
+    rng = np.random.default_rng(123)
+    blocks = []
+    if codec == "q4_k":
+        for sc_val, m_val in [(0, 0), (63, 63), (63, 0), (0, 63), (17, 42)]:
+            b = np.zeros(144, np.uint8)
+            b[0:2], b[2:4] = fp16(1e-3), fp16(5e-4)
+            # pack sc/m = (sc_val, m_val) into all 8 sub-blocks (quants.py:479-501 layout)
+            for j in range(4):
+                b[4 + j] = (sc_val & 63) | ((sc_val >> 4) << 6)
+                b[8 + j] = (m_val & 63) | ((m_val >> 4) << 6)
+                b[12 + j] = (sc_val & 15) | ((m_val & 15) << 4)
+            b[16:] = 0 if (sc_val, m_val) == (0, 0) else rng.integers(0, 256, 128, dtype=np.uint8)
+            blocks.append(b)
+        for one in range(8):  # one-hot sub-block scale, zero min
+            b = np.zeros(144, np.uint8)
+            b[0:2], b[2:4] = fp16(1e-3), fp16(1e-3)
+            if one < 4:
+                b[4 + one] = 1
+            else:
+                b[12 + one - 4] = 1
+            b[16:] = rng.integers(0, 256, 128, dtype=np.uint8)
+            blocks.append(b)
+    elif codec == "q6_k":
+        for scv, qfill in [(-128, None), (-64, 0), (0, None), (63, 255), (127, None)]:
+            b = rng.integers(0, 256, 210, dtype=np.uint8)
+            if qfill is not None:
+                b[:192] = qfill
+            b[192:208] = np.array([scv] * 16, np.int8).view(np.uint8)
+            b[208:210] = fp16(2e-3)
+            blocks.append(b)
+    else:
+        # every grid index (4 per 8-byte group, 8 groups per block -> 8 blocks)
+        # with sign indices sweeping 0..127 and ls alternating 0 / 15
+        gi = np.arange(256, dtype=np.uint32)
+        si = np.arange(128, dtype=np.uint32)
+        k = 0
+        for blk in range(8):
+            b = np.zeros(66, np.uint8)
+            b[0:2] = fp16(1.5e-3)
+            for g in range(8):
+                a0 = 0
+                a1 = 0
+                for s in range(4):
+                    a0 |= int(gi[(k + s) % 256]) << (8 * s)
+                    a1 |= int(si[(k + s) % 128]) << (7 * s)
+                a1 |= (15 if (g + blk) % 2 else 0) << 28
+                k += 4
+                b[2 + 8 * g:6 + 8 * g] = np.array([a0], np.uint32).view(np.uint8)
+                b[6 + 8 * g:10 + 8 * g] = np.array([a1], np.uint32).view(np.uint8)
+            blocks.append(b)
+    return np.stack(blocks)
+
+
+def main():
+    out = {}
+    for codec in QT:
+        k = 1024
+        rand = synth.random_weight(codec, 12, k, seed=2024)
+        edge = edge_blocks(codec)
+        nb = k // 256
+        pad = (-len(edge)) % nb
+        if pad:
+            edge = np.concatenate([edge, synth.random_blocks(codec, pad, seed=7)])
+        edge = edge.reshape(-1, nb * edge.shape[1])
+        w = np.concatenate([rand, edge], 0)
+        deq = dequantize(w, QT[codec]).astype(np.float32)
+        x = synth.random_activations(3, k, seed=99)
+        xf = (x.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        onehot = np.zeros((2, k), np.float32)
+        onehot[0, 5] = 1.0
+        onehot[1, k - 1] = -2.0
+        xo = synth.f32_to_bf16_bits(onehot)
+        xall = np.concatenate([x, xo], 0)
+        xallf = (xall.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        y = xallf @ deq.astype(np.float64).T
+        out[f"{codec}_w"] = w
+        out[f"{codec}_deq"] = deq
+        out[f"{codec}_x"] = xall
+        out[f"{codec}_y"] = y
+        del xf
+    np.savez_compressed(os.path.join(HERE, "golden_blocks.npz"), **out)
+    print("wrote", os.path.join(HERE, "golden_blocks.npz"))
+
+
+if __name__ == "__main__":
+    main()

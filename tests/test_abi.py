@@ -1,0 +1,57 @@
+"""CPU tests of the C ABI: the library loads and exports every symbol that
+include/kq_cuda.h declares; host-side validation answers without a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from gmlx_b200 import _lib
+
+HDR = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "kq_cuda.h")
+
+
+def declared():
+    src = open(HDR).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(kq_\w+)\s*\(", src, re.M)))
+
+
+def test_header_symbols_exported():
+    L = _lib.load()
+    names = declared()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+
+
+def test_codecs_and_block_bytes():
+    L = _lib.load()
+    buf = (ctypes.c_int * 8)()
+    assert L.kq_codecs(buf, 8) == 3
+    assert list(buf[:3]) == [12, 14, 16]
+    assert [L.kq_block_bytes(c) for c in (12, 14, 16, 2)] == [144, 210, 66, -1]
+    assert L.kq_codec_has_matmul(12) == 1 and L.kq_codec_has_matmul(8) == 0
+    assert L.kq_version() >= 100
+
+
+def test_validation_without_gpu():
+    L = _lib.load()
+    # unknown codec -> KQ_ERR_CODEC, message names the op (validated before any launch)
+    rc = L.kq_dequantize(3, None, 1, 256, 144, None, 0, None)
+    assert rc == _lib.KQ_ERR_CODEC
+    assert b"dequantize" in L.kq_last_error()
+    rc = L.kq_dequantize(12, None, 1, 300, 144, None, 0, None)
+    assert rc == _lib.KQ_ERR_SHAPE
+    rc = L.kq_moe_router_topk(None, 1, 2048, 8, 1, None, None, None)
+    assert rc == _lib.KQ_ERR_SHAPE
+
+
+def test_python_ops_fail_loudly_without_cuda():
+    import torch
+    from gmlx_b200 import kq
+    w = torch.zeros(4, 144, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="CUDA"):
+        kq.dequantize(w, None, "q4_k")
+    with pytest.raises(NotImplementedError):
+        kq.dequantize(w, None, "q5_0")

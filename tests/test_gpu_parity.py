@@ -171,3 +171,39 @@ def test_gather_qmm(cuda, codec):
                       out_dtype=torch.float32)
     assert tuple(y.shape) == (t, k, 1, n)
     assert rel_err(y.cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("codec", CODECS)
+def test_golden_vectors_on_gpu(cuda, codec):
+    """Kernels against the committed gguf-py golden vectors (edge blocks included)."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz"))
+    w, deq, x, yref = g[f"{codec}_w"], g[f"{codec}_deq"], g[f"{codec}_x"], g[f"{codec}_y"]
+    wd = torch.from_numpy(w).to(cuda)
+    out = kq.dequantize(wd, None, codec).cpu().numpy()
+    assert np.array_equal(out.view(np.uint32), deq.view(np.uint32))
+    y = kq.quantized_matmul(to_dev_x(x, cuda), wd, None, codec, out_dtype=torch.float32).cpu().numpy()
+    assert rel_err(y, yref) <= TOL
+
+
+def test_nn_modules_fused_and_stock_paths_agree(cuda):
+    from gmlx_b200 import nn as knn
+    e, d, f, k, t = 8, 512, 256, 2, 3
+    m = knn.KQuantSwitchGLU(d, f, e, "q4_k", "q6_k", device=cuda)
+    m.gate_proj.weight.copy_(torch.from_numpy(synth.random_weight("q4_k", f, d, seed=1, experts=e)))
+    m.up_proj.weight.copy_(torch.from_numpy(synth.random_weight("q4_k", f, d, seed=2, experts=e)))
+    m.down_proj.weight.copy_(torch.from_numpy(synth.random_weight("q6_k", d, f, seed=3, experts=e)))
+    x = torch.randn(t, d, device=cuda).to(torch.bfloat16)
+    idx, sc = kq.moe_router_topk(torch.randn(t, e, device=cuda), k, True)
+    y_fused = m(x, idx, sc).float()
+    # stock path (forced by a 64-slot index tensor) on the same routing
+    xs = x.repeat(32, 1)
+    ids = idx.repeat(32, 1)
+    y_stock = m(xs, ids, sc.repeat(32, 1))[:t].float()
+    assert rel_err(y_fused.cpu().numpy(), y_stock.cpu().numpy()) <= TOL
+    lin = knn.KQuantLinear(d, 128, True, "iq2_xxs", device=cuda)
+    lin.weight.copy_(torch.from_numpy(synth.random_weight("iq2_xxs", 128, d, seed=4)))
+    lin.bias.fill_(0.5)
+    xb = synth.random_activations(2, d, seed=5)
+    ref = O.matmul(xb, lin.weight.cpu().numpy(), "iq2_xxs") + 0.5
+    assert rel_err(lin(to_dev_x(xb, cuda)).float().cpu().numpy(), ref) <= TOL

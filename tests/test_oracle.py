@@ -1,0 +1,117 @@
+"""CPU tests: the oracle (C and numpy restatements) pinned to gguf-py and to
+the committed golden vectors, plus known-answer cases.  No GPU needed."""
+import os
+
+import numpy as np
+import pytest
+
+from gmlx_b200 import synth
+from oracle import oracle as O
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
+CODECS = ["q4_k", "q6_k", "iq2_xxs"]
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLD)
+
+
+def bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("codec", CODECS)
+def test_oracle_matches_golden_dequant(gold, codec):
+    w, deq = gold[f"{codec}_w"], gold[f"{codec}_deq"]
+    assert np.array_equal(bits(O.dequantize(w, codec)), bits(deq))
+    assert np.array_equal(bits(O.np_dequantize(w, codec)), bits(deq))
+
+
+@pytest.mark.parametrize("codec", CODECS)
+def test_oracle_matmul_matches_golden(gold, codec):
+    y = O.matmul(gold[f"{codec}_x"], gold[f"{codec}_w"], codec)
+    ref = gold[f"{codec}_y"]
+    assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+    # one-hot rows reproduce dequantized columns exactly (x = 1.0 and -2.0)
+    deq = gold[f"{codec}_deq"]
+    assert np.array_equal(y[3], deq[:, 5])          # value-exact (+0 == -0)
+    assert np.array_equal(y[4], -2.0 * deq[:, -1])
+
+
+@pytest.mark.parametrize("codec", CODECS)
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_oracle_matches_gguf_py_random(codec, seed):
+    gq = pytest.importorskip("gguf.quants")
+    from gguf.constants import GGMLQuantizationType as T
+    qt = {"q4_k": T.Q4_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}[codec]
+    w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
+    assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
+
+
+def test_raw_random_bytes_match_where_finite():
+    # fully random bytes (fp16 scales may be NaN/Inf/subnormal): bit patterns of
+    # every finite result agree with gguf-py
+    gq = pytest.importorskip("gguf.quants")
+    from gguf.constants import GGMLQuantizationType as T
+    rng = np.random.default_rng(5)
+    for codec, qt, bpb in [("q4_k", T.Q4_K, 144), ("q6_k", T.Q6_K, 210), ("iq2_xxs", T.IQ2_XXS, 66)]:
+        w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
+        a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
+        fin = np.isfinite(b)
+        assert np.array_equal(bits(a)[fin], bits(b)[fin])
+        assert np.array_equal(np.isnan(a), np.isnan(b))
+
+
+def test_known_answer_q4k_zero_quants():
+    # all-zero quants: w = -dmin * m for every weight of sub-block j
+    b = np.zeros((1, 144), np.uint8)
+    b[0, 0:2] = np.array([1e-3], np.float16).view(np.uint8)
+    b[0, 2:4] = np.array([2.5e-4], np.float16).view(np.uint8)
+    b[0, 8:12] = [1, 2, 3, 4]   # m0..m3
+    b[0, 12:16] = [5 << 4, 6 << 4, 7 << 4, 8 << 4]  # m4..m7 (low bits), sc4..7 = 0
+    w = O.dequantize(b, "q4_k")[0]
+    dmin = np.float32(np.float16(2.5e-4))
+    for j, m in enumerate([1, 2, 3, 4, 5, 6, 7, 8]):
+        assert np.all(w[32 * j:32 * j + 32] == -(dmin * np.float32(m)))
+
+
+def test_ksigns_parity_rule():
+    gq = pytest.importorskip("gguf.quants")
+    assert np.array_equal(O.ksigns_table(), np.frombuffer(gq.IQ2_XXS.ksigns, np.uint8))
+
+
+def test_iq2xxs_grid_matches_gguf():
+    gq = pytest.importorskip("gguf.quants")
+    gq.IQ2_XXS.init_grid()
+    assert np.array_equal(O.iq2xxs_grid().astype(np.float32), np.asarray(gq.IQ2_XXS.grid).reshape(256, 8))
+
+
+def test_router_topk_semantics():
+    lg = synth.random_logits(16, 64, seed=3)
+    idx, sc = O.router_topk(lg, 8, True)
+    p = np.exp(lg - lg.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    ref_idx = np.argsort(-p, axis=1, kind="stable")[:, :8]
+    assert np.array_equal(idx, ref_idx)
+    top = np.take_along_axis(p, ref_idx, 1)
+    assert np.allclose(sc, top / top.sum(1, keepdims=True), rtol=1e-5)
+    idx2, sc2 = O.router_topk(lg, 8, False)
+    assert np.allclose(sc2, top, rtol=1e-5)
+
+
+def test_synthetic_block_statistics():
+    for codec in CODECS:
+        w = synth.random_blocks(codec, 4096, seed=1)
+        if codec == "q4_k":
+            d = w[:, 0:2].copy().view(np.float16).astype(np.float32)
+            dm = w[:, 2:4].copy().view(np.float16).astype(np.float32)
+            assert d.min() >= 9e-5 and d.max() <= 2.01e-3 and dm.min() >= 9e-5
+        elif codec == "q6_k":
+            sc = w[:, 192:208].view(np.int8)
+            assert sc.min() == -64 and sc.max() == 63
+            d = w[:, 208:210].copy().view(np.float16).astype(np.float32)
+            assert d.min() >= 9e-5 and d.max() <= 2.01e-3
+        else:
+            d = w[:, 0:2].copy().view(np.float16).astype(np.float32)
+            assert d.min() >= 9e-5 and d.max() <= 2.01e-3
