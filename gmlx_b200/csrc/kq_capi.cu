@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "../../include/kq_cuda.h"
@@ -112,6 +113,8 @@ GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k,
     a.y_row_stride = ys;
     a.act = act;
     a.max_tokens = (int)(m < 32 ? m : 32);
+    const char *dbg = getenv("KQ_GEMV_DEBUG");
+    a.debug = dbg ? atoi(dbg) : 0;
     return a;
 }
 

@@ -15,9 +15,10 @@
 //    row's raw super-blocks (144/210/66 B, never repacked) into a shared-memory
 //    ring with 1-D bulk async copies (cp.async.bulk, mbarrier completion, L2
 //    evict-first).  Copies start at the 16-byte granule holding the first
-//    byte, so unaligned Q6_K/IQ2_XXS rows stream the same way as Q4_K.  For
-//    <= 8 activation rows the matching activation slice rides in the same
-//    stage, so the MMA B operands come from shared memory too.
+//    byte, so unaligned Q6_K/IQ2_XXS rows stream the same way as Q4_K.  Each
+//    row copy is >= ~1 KB (smaller bulk copies are request-rate bound).  For
+//    one activation row its matching slice rides in the same stage, so the
+//    MMA B operands come from shared memory too.
 //  * Consumer warp = 16 rows x one super-block per stage.  Packed bits become
 //    mma.sync m16n8k16 A fragments directly: quant values turn into exact
 //    small-integer bf16 (or f16) by OR-ing them into the mantissa of a magic
@@ -40,41 +41,57 @@ namespace kq {
 namespace {
 
 constexpr int CW = 8;             // consumer warps: 2 row halves x 4 block columns
-constexpr int KB = 4;             // super-blocks per row per stage (one per block column)
+constexpr int NCOL = 4;           // block columns (consumer warps per row half)
 constexpr int NTHREADS = 32 * (CW + 1);
 constexpr int TROWS = 32;         // weight rows per tile
 constexpr int RED_TS = 36;        // token stride (floats) of the reduction buffer
-constexpr int XSTR = KB * QK * 2 + 64;  // staged activation row stride (bytes), bank-spread
 
 // NS: ring stages; TABW: floats of the per-warp scale table.  Tables are laid
 // out [sub-block][g][..] so lane (g, t) reads the values of both its rows
 // (g and g+8) with one 16- or 8-byte load, conflict-free.
+// BPW: super-blocks each consumer warp decodes per stage, so one row's copy
+// per stage is KB = 4*BPW blocks (>= ~1 KB: smaller bulk copies are
+// request-rate bound on the TMA engine).
 template <int C> struct GCfg;
-template <> struct GCfg<Q4_K> { static constexpr int NS = 2, TABW = 8 * 8 * 4; };     // (dsc, -mt) x 2 rows
-template <> struct GCfg<Q6_K> { static constexpr int NS = 2, TABW = 16 * 8 * 2; };    // dsc x 2 rows
-template <> struct GCfg<IQ2_XXS> { static constexpr int NS = 3, TABW = 8 * 8 * 2; };  // db x 2 rows
+template <> struct GCfg<Q4_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // (dsc, -mt) x 2 rows
+template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1; };    // dsc x 2 rows
+template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 2; };  // db x 2 rows
+template <int C> constexpr int KB_OF = NCOL * GCfg<C>::BPW;
+template <int C> constexpr int XSTR_OF = KB_OF<C> * QK * 2 + 64;  // staged activation row stride (bytes)
+constexpr int SMEM_BUDGET = 112 * 1024;  // per CTA: two CTAs per SM
+constexpr int S_MAX = 2048;              // Q4_K one-row sub-block sums table: K <= 65536
 
-__host__ __device__ constexpr int spitch_of(int bpb) {
+template <int C> __host__ __device__ constexpr int spitch_of() {
     // one row of a stage: KB blocks + 16 B slack for the granule offset;
     // pitch == 32 (mod 128) spreads 8 rows x 32 B over all banks.
-    return ((((KB * bpb + 16 + 15) / 16 * 16) - 32 + 127) / 128) * 128 + 32;
+    return ((((KB_OF<C> * Fmt<C>::bpb + 16 + 15) / 16 * 16) - 32 + 127) / 128) * 128 + 32;
 }
 
-template <int C, int NT> struct GLayout {
-    static constexpr bool XS = NT == 1;  // activation slice staged with the weights
+// XR: activation rows staged per stage with the weights (0 = read from global)
+template <int C, int NT, int XR> struct GLayout {
+    static constexpr bool XS = XR > 0;
     static constexpr int bpb = Fmt<C>::bpb;
-    static constexpr int SP = spitch_of(bpb);
-    static constexpr int NS = GCfg<C>::NS;
+    static constexpr int KB = KB_OF<C>;
+    static constexpr int XSTR = XSTR_OF<C>;
+    static constexpr int SP = spitch_of<C>();
     static constexpr int WBYTES = TROWS * SP;
-    static constexpr int STAGE = WBYTES + (XS ? 8 * XSTR : 0);
+    static constexpr int STAGE = WBYTES + XR * XSTR;
+    static constexpr int TABS = CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;
+    static constexpr bool SX = false;  // Q4_K one-row sums table (off: its per-launch prologue costs more than it saves)
+    static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
+    static constexpr int REDB = NCOL * 8 * NT * RED_TS * 4;  // one reduction buffer (two, alternating)
+    static constexpr int FIXED = 512 + (C == IQ2_XXS ? 4096 : 0) + TABS + SBYTES + 2 * REDB;
+    static constexpr int NS_FIT = (SMEM_BUDGET - FIXED) / STAGE;
+    static constexpr int NS = NS_FIT > 8 ? 8 : (NS_FIT < 2 ? 2 : NS_FIT);  // ring depth (<= 8: rowoff table)
     static constexpr int OFF_BAR = 0;                              // 2*NS mbarriers
     static constexpr int OFF_ROWOFF = 128;                         // NS x 32 bytes
     static constexpr int OFF_MISC = OFF_ROWOFF + 32 * 8;           // flags
     static constexpr int OFF_GRID = 512;                           // IQ2 grid: 256 x 16 B
     static constexpr int OFF_RING = OFF_GRID + (C == IQ2_XXS ? 4096 : 0);
     static constexpr int OFF_SCALE = OFF_RING + NS * STAGE;        // CW x TABW floats
-    static constexpr int OFF_RED = OFF_SCALE + CW * GCfg<C>::TABW * 4;
-    static constexpr int BYTES = OFF_RED + KB * 8 * NT * RED_TS * 4;
+    static constexpr int OFF_S = OFF_SCALE + TABS;
+    static constexpr int OFF_RED = OFF_S + SBYTES;
+    static constexpr int BYTES = OFF_RED + 2 * REDB;
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -201,23 +218,34 @@ __device__ __forceinline__ int64_t cta_of(int64_t i, int64_t I, int64_t P) { ret
 template <int C, int NT, bool F16, bool XS>
 struct Block;
 
+// Each run() decodes NB consecutive super-blocks (block columns col0 ..
+// col0+NB-1 of the stage) for the warp's 16 rows; the NB blocks are
+// independent work interleaved for instruction-level parallelism.  xr[nt]
+// points at block col0's first activation element; block bb is at +bb*256.
+
 // Q4_K --------------------------------------------------------------------
 template <int NT, bool F16, bool XS>
 struct Block<Q4_K, NT, F16, XS> {
-    static __device__ __forceinline__ void run(const uint8_t *sb, const uint8_t *roff, int col, int mt, float *stab,
-                                               const uint16_t *const xr[NT], float acc[NT][4], const uint4 *) {
+    // Sx (one activation row): sub-block sums of x for block col0 from a shared
+    // table; otherwise they come from an extra MMA with an all-ones A operand.
+    template <int NB>
+    static __device__ __forceinline__ void run(const uint8_t *sb, const uint8_t *roff, int col0, int mt, float *stab,
+                                               const uint16_t *const xr[NT], float acc[NT][4], const uint4 *,
+                                               const float *Sx = nullptr) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-        constexpr int bpb = 144, SP = spitch_of(bpb);
+        constexpr int bpb = 144, SP = spitch_of<Q4_K>();
+        constexpr int TW = GCfg<Q4_K>::TABW;
         // header: lane -> (row lane&15, sub-blocks 4*(lane>>4) .. +3): (d*sc, -(128*d*sc + dmin*m))
-        {
+#pragma unroll
+        for (int bb = 0; bb < NB; bb++) {
             const int rr = lane & 15, r = 16 * mt + rr, hh = lane >> 4;
-            const uint8_t *h = sb + r * SP + roff[r] + col * bpb;
+            const uint8_t *h = sb + r * SP + roff[r] + (col0 + bb) * bpb;
             const uint4 hv = *reinterpret_cast<const uint4 *>(h);
             const float d = half_bits_to_float(hv.x & 0xffffu), dmin = half_bits_to_float(hv.x >> 16);
             uint32_t sc03, sc47, m03, m47;
             q4k_unpack_scales(hv.y, hv.z, hv.w, sc03, sc47, m03, m47);
             const uint32_t sw = hh ? sc47 : sc03, mw = hh ? m47 : m03;
-            float *o = stab + (rr & 7) * 4 + (rr >> 3) * 2;
+            float *o = stab + bb * TW + (rr & 7) * 4 + (rr >> 3) * 2;
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const float ds = d * bytef(sw, j);
@@ -227,57 +255,60 @@ struct Block<Q4_K, NT, F16, XS> {
         }
         __syncwarp();
         const int ra = 16 * mt + g, rb = ra + 8;
-        const uint8_t *pa = sb + ra * SP + roff[ra] + col * bpb + 16 + 8 * t;
-        const uint8_t *pb = sb + rb * SP + roff[rb] + col * bpb + 16 + 8 * t;
+        const uint8_t *pa = sb + ra * SP + roff[ra] + col0 * bpb + 16 + 8 * t;
+        const uint8_t *pb = sb + rb * SP + roff[rb] + col0 * bpb + 16 + 8 * t;
         const uint32_t ONES[4] = {ones2<F16>(), ones2<F16>(), ones2<F16>(), ones2<F16>()};
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-            // B fragments: sub 2c (low nibbles) at 64c, sub 2c+1 (high) at 64c+32;
-            // thread t holds logical weights 8t..8t+7 of each sub-block
-            uint32_t B[2][NT][2][2];
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                const uint4 xl = ldx16<XS>(xr[nt] + 64 * c + 8 * t);
-                const uint4 xh = ldx16<XS>(xr[nt] + 64 * c + 32 + 8 * t);
-                B[0][nt][0][0] = prmt(xl.x, xl.y, 0x5410);
-                B[0][nt][0][1] = prmt(xl.x, xl.y, 0x7632);
-                B[0][nt][1][0] = prmt(xl.z, xl.w, 0x5410);
-                B[0][nt][1][1] = prmt(xl.z, xl.w, 0x7632);
-                B[1][nt][0][0] = prmt(xh.x, xh.y, 0x5410);
-                B[1][nt][0][1] = prmt(xh.x, xh.y, 0x7632);
-                B[1][nt][1][0] = prmt(xh.z, xh.w, 0x5410);
-                B[1][nt][1][1] = prmt(xh.z, xh.w, 0x7632);
-            }
-            const uint2 wa = *reinterpret_cast<const uint2 *>(pa + 32 * c);
-            const uint2 wb = *reinterpret_cast<const uint2 *>(pb + 32 * c);
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                float T[NT][4], S[NT][4];
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-                    for (int q = 0; q < 4; q++) T[nt][q] = S[nt][q] = 0.f;
-#pragma unroll
-                for (int s = 0; s < 2; s++) {
-                    const uint32_t xa = s ? wa.y : wa.x, xb = s ? wb.y : wb.x;
-                    uint32_t A[4];
-                    A[0] = lop_and_or(xa >> (4 * h), 0x000f000fu, magic2<F16>());
-                    A[1] = lop_and_or(xb >> (4 * h), 0x000f000fu, magic2<F16>());
-                    A[2] = lop_and_or(xa >> (8 + 4 * h), 0x000f000fu, magic2<F16>());
-                    A[3] = lop_and_or(xb >> (8 + 4 * h), 0x000f000fu, magic2<F16>());
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        mma16816<F16>(T[nt], A, B[h][nt][s][0], B[h][nt][s][1], T[nt]);
-                        mma16816<F16>(S[nt], ONES, B[h][nt][s][0], B[h][nt][s][1], S[nt]);
-                    }
-                }
-                const float4 sc = *reinterpret_cast<const float4 *>(stab + (2 * c + h) * 32 + g * 4);  // rows g, g+8
+            for (int bb = 0; bb < NB; bb++) {
+                // B fragments: sub 2c (low nibbles) at 64c, sub 2c+1 (high) at 64c+32;
+                // thread t holds logical weights 8t..8t+7 of each sub-block
+                uint32_t B[2][NT][2][2];
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
-                    ffma2(acc[nt][0], acc[nt][1], sc.x, sc.x, T[nt][0], T[nt][1]);
-                    ffma2(acc[nt][0], acc[nt][1], sc.y, sc.y, S[nt][0], S[nt][1]);
-                    ffma2(acc[nt][2], acc[nt][3], sc.z, sc.z, T[nt][2], T[nt][3]);
-                    ffma2(acc[nt][2], acc[nt][3], sc.w, sc.w, S[nt][2], S[nt][3]);
+                    const uint4 xl = ldx16<XS>(xr[nt] + bb * QK + 64 * c + 8 * t);
+                    const uint4 xh = ldx16<XS>(xr[nt] + bb * QK + 64 * c + 32 + 8 * t);
+                    B[0][nt][0][0] = prmt(xl.x, xl.y, 0x5410);
+                    B[0][nt][0][1] = prmt(xl.x, xl.y, 0x7632);
+                    B[0][nt][1][0] = prmt(xl.z, xl.w, 0x5410);
+                    B[0][nt][1][1] = prmt(xl.z, xl.w, 0x7632);
+                    B[1][nt][0][0] = prmt(xh.x, xh.y, 0x5410);
+                    B[1][nt][0][1] = prmt(xh.x, xh.y, 0x7632);
+                    B[1][nt][1][0] = prmt(xh.z, xh.w, 0x5410);
+                    B[1][nt][1][1] = prmt(xh.z, xh.w, 0x7632);
+                }
+                const uint2 wa = *reinterpret_cast<const uint2 *>(pa + bb * bpb + 32 * c);
+                const uint2 wb = *reinterpret_cast<const uint2 *>(pb + bb * bpb + 32 * c);
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    float T[NT][4], S[NT][4];
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                        for (int q = 0; q < 4; q++) T[nt][q] = S[nt][q] = 0.f;
+#pragma unroll
+                    for (int s = 0; s < 2; s++) {
+                        const uint32_t xa = s ? wa.y : wa.x, xb = s ? wb.y : wb.x;
+                        uint32_t A[4];
+                        A[0] = lop_and_or(xa >> (4 * h), 0x000f000fu, magic2<F16>());
+                        A[1] = lop_and_or(xb >> (4 * h), 0x000f000fu, magic2<F16>());
+                        A[2] = lop_and_or(xa >> (8 + 4 * h), 0x000f000fu, magic2<F16>());
+                        A[3] = lop_and_or(xb >> (8 + 4 * h), 0x000f000fu, magic2<F16>());
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) {
+                            mma16816<F16>(T[nt], A, B[h][nt][s][0], B[h][nt][s][1], T[nt]);
+                            mma16816<F16>(S[nt], ONES, B[h][nt][s][0], B[h][nt][s][1], S[nt]);
+                        }
+                    }
+                    const float4 sc = *reinterpret_cast<const float4 *>(stab + bb * TW + (2 * c + h) * 32 + g * 4);
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        ffma2(acc[nt][0], acc[nt][1], sc.x, sc.x, T[nt][0], T[nt][1]);
+                        ffma2(acc[nt][0], acc[nt][1], sc.y, sc.y, S[nt][0], S[nt][1]);
+                        ffma2(acc[nt][2], acc[nt][3], sc.z, sc.z, T[nt][2], T[nt][3]);
+                        ffma2(acc[nt][2], acc[nt][3], sc.w, sc.w, S[nt][2], S[nt][3]);
+                    }
                 }
             }
         }
@@ -290,16 +321,20 @@ struct Block<Q6_K, NT, F16, XS> {
     static __device__ __forceinline__ uint32_t qh_shift(uint32_t q, int s) {
         return s == 0 ? (q << 4) : s == 1 ? (q << 2) : s == 2 ? q : (q >> 2);
     }
-    static __device__ __forceinline__ void run(const uint8_t *sb, const uint8_t *roff, int col, int mt, float *stab,
-                                               const uint16_t *const xr[NT], float acc[NT][4], const uint4 *) {
+    template <int NB>
+    static __device__ __forceinline__ void run(const uint8_t *sb, const uint8_t *roff, int col0, int mt, float *stab,
+                                               const uint16_t *const xr[NT], float acc[NT][4], const uint4 *,
+                                               const float * = nullptr) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-        constexpr int bpb = 210, SP = spitch_of(bpb);
-        {
+        constexpr int bpb = 210, SP = spitch_of<Q6_K>();
+        constexpr int TW = GCfg<Q6_K>::TABW;
+#pragma unroll
+        for (int bb = 0; bb < NB; bb++) {
             // header: lane -> (row lane&15, scales 8*(lane>>4) .. +7): d * sc
             const int rr = lane & 15, r = 16 * mt + rr, hh = lane >> 4;
-            const uint8_t *h = sb + r * SP + roff[r] + col * bpb;
+            const uint8_t *h = sb + r * SP + roff[r] + (col0 + bb) * bpb;
             const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(h + 208));
-            float *o = stab + (rr & 7) * 2 + (rr >> 3);
+            float *o = stab + bb * TW + (rr & 7) * 2 + (rr >> 3);
 #pragma unroll
             for (int q = 0; q < 2; q++) {
                 const uint32_t w = lds_u32_a2(h + 192 + 8 * hh + 4 * q) ^ 0x80808080u;  // int8 -> biased byte
@@ -309,45 +344,48 @@ struct Block<Q6_K, NT, F16, XS> {
         }
         __syncwarp();
         const int ra = 16 * mt + g, rb = ra + 8;
-        const uint8_t *pa = sb + ra * SP + roff[ra] + col * bpb;
-        const uint8_t *pb = sb + rb * SP + roff[rb] + col * bpb;
 #pragma unroll
         for (int hf = 0; hf < 2; hf++) {
 #pragma unroll
             for (int lh = 0; lh < 2; lh++) {
-                // logical weights 128hf + 32s + 16lh + 4t + {0..3}, s = 0..3
-                uint32_t B[NT][4][2];
 #pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-                    for (int s = 0; s < 4; s++) {
-                        const uint2 xv = ldx8<XS>(xr[nt] + 128 * hf + 32 * s + 16 * lh + 4 * t);
-                        B[nt][s][0] = prmt(xv.x, xv.y, 0x5410);
-                        B[nt][s][1] = prmt(xv.x, xv.y, 0x7632);
-                    }
-                }
-                const int lo = 64 * hf + 16 * lh + 4 * t, ho = 128 + 32 * hf + 16 * lh + 4 * t;
-                const uint32_t qla[2] = {lds_u32_a2(pa + lo), lds_u32_a2(pa + lo + 32)};
-                const uint32_t qlb[2] = {lds_u32_a2(pb + lo), lds_u32_a2(pb + lo + 32)};
-                const uint32_t qha = lds_u32_a2(pa + ho), qhb = lds_u32_a2(pb + ho);
-#pragma unroll
-                for (int s = 0; s < 4; s++) {
-                    const int ns = 4 * (s >> 1);
-                    const uint32_t la = qla[s & 1] >> ns, lb = qlb[s & 1] >> ns;
-                    const uint32_t ha = qh_shift(qha, s), hb = qh_shift(qhb, s);
-                    uint32_t A[4];
-                    A[0] = sub2<F16>(lop_and_or(ha, 0x00300030u, lop_and_or(la, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
-                    A[1] = sub2<F16>(lop_and_or(hb, 0x00300030u, lop_and_or(lb, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
-                    A[2] = sub2<F16>(lop_and_or(ha >> 8, 0x00300030u, lop_and_or(la >> 8, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
-                    A[3] = sub2<F16>(lop_and_or(hb >> 8, 0x00300030u, lop_and_or(lb >> 8, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
-                    const int j = 8 * hf + 2 * s + lh;
-                    const float2 sc = *reinterpret_cast<const float2 *>(stab + j * 16 + g * 2);
+                for (int bb = 0; bb < NB; bb++) {
+                    const uint8_t *pa = sb + ra * SP + roff[ra] + (col0 + bb) * bpb;
+                    const uint8_t *pb = sb + rb * SP + roff[rb] + (col0 + bb) * bpb;
+                    // logical weights 128hf + 32s + 16lh + 4t + {0..3}, s = 0..3
+                    uint32_t B[NT][4][2];
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++) {
-                        float T[4] = {0.f, 0.f, 0.f, 0.f};
-                        mma16816<F16>(T, A, B[nt][s][0], B[nt][s][1], T);
-                        ffma2(acc[nt][0], acc[nt][1], sc.x, sc.x, T[0], T[1]);
-                        ffma2(acc[nt][2], acc[nt][3], sc.y, sc.y, T[2], T[3]);
+#pragma unroll
+                        for (int s = 0; s < 4; s++) {
+                            const uint2 xv = ldx8<XS>(xr[nt] + bb * QK + 128 * hf + 32 * s + 16 * lh + 4 * t);
+                            B[nt][s][0] = prmt(xv.x, xv.y, 0x5410);
+                            B[nt][s][1] = prmt(xv.x, xv.y, 0x7632);
+                        }
+                    }
+                    const int lo = 64 * hf + 16 * lh + 4 * t, ho = 128 + 32 * hf + 16 * lh + 4 * t;
+                    const uint32_t qla[2] = {lds_u32_a2(pa + lo), lds_u32_a2(pa + lo + 32)};
+                    const uint32_t qlb[2] = {lds_u32_a2(pb + lo), lds_u32_a2(pb + lo + 32)};
+                    const uint32_t qha = lds_u32_a2(pa + ho), qhb = lds_u32_a2(pb + ho);
+#pragma unroll
+                    for (int s = 0; s < 4; s++) {
+                        const int ns = 4 * (s >> 1);
+                        const uint32_t la = qla[s & 1] >> ns, lb = qlb[s & 1] >> ns;
+                        const uint32_t ha = qh_shift(qha, s), hb = qh_shift(qhb, s);
+                        uint32_t A[4];
+                        A[0] = sub2<F16>(lop_and_or(ha, 0x00300030u, lop_and_or(la, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
+                        A[1] = sub2<F16>(lop_and_or(hb, 0x00300030u, lop_and_or(lb, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
+                        A[2] = sub2<F16>(lop_and_or(ha >> 8, 0x00300030u, lop_and_or(la >> 8, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
+                        A[3] = sub2<F16>(lop_and_or(hb >> 8, 0x00300030u, lop_and_or(lb >> 8, 0x000f000fu, magic2<F16>())), magic_f<F16>() + 32.f);
+                        const int j = 8 * hf + 2 * s + lh;
+                        const float2 sc = *reinterpret_cast<const float2 *>(stab + bb * TW + j * 16 + g * 2);
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) {
+                            float T[4] = {0.f, 0.f, 0.f, 0.f};
+                            mma16816<F16>(T, A, B[nt][s][0], B[nt][s][1], T);
+                            ffma2(acc[nt][0], acc[nt][1], sc.x, sc.x, T[0], T[1]);
+                            ffma2(acc[nt][2], acc[nt][3], sc.y, sc.y, T[2], T[3]);
+                        }
                     }
                 }
             }
@@ -358,17 +396,20 @@ struct Block<Q6_K, NT, F16, XS> {
 // IQ2_XXS -----------------------------------------------------------------
 template <int NT, bool F16, bool XS>
 struct Block<IQ2_XXS, NT, F16, XS> {
-    static __device__ __forceinline__ void run(const uint8_t *sb, const uint8_t *roff, int col, int mt, float *stab,
+    template <int NB>
+    static __device__ __forceinline__ void run(const uint8_t *sb, const uint8_t *roff, int col0, int mt, float *stab,
                                                const uint16_t *const xr[NT], float acc[NT][4],
-                                               const uint4 *gridtab) {
+                                               const uint4 *gridtab, const float * = nullptr) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-        constexpr int bpb = 66, SP = spitch_of(bpb);
-        {
+        constexpr int bpb = 66, SP = spitch_of<IQ2_XXS>();
+        constexpr int TW = GCfg<IQ2_XXS>::TABW;
+#pragma unroll
+        for (int bb = 0; bb < NB; bb++) {
             // header: lane -> (row lane&15, sub-blocks 4*(lane>>4) .. +3): d*(0.5+ls)*0.25
             const int rr = lane & 15, r = 16 * mt + rr, hh = lane >> 4;
-            const uint8_t *h = sb + r * SP + roff[r] + col * bpb;
+            const uint8_t *h = sb + r * SP + roff[r] + (col0 + bb) * bpb;
             const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(h));
-            float *o = stab + (rr & 7) * 2 + (rr >> 3);
+            float *o = stab + bb * TW + (rr & 7) * 2 + (rr >> 3);
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 const uint32_t a1 = lds_u32_a2(h + 6 + 8 * (4 * hh + q));
@@ -377,48 +418,51 @@ struct Block<IQ2_XXS, NT, F16, XS> {
         }
         __syncwarp();
         const int ra = 16 * mt + g, rb = ra + 8;
-        const uint8_t *pa = sb + ra * SP + roff[ra] + col * bpb + 2;
-        const uint8_t *pb = sb + rb * SP + roff[rb] + col * bpb + 2;
 #pragma unroll 2
         for (int sbk = 0; sbk < 8; sbk++) {
-            uint32_t B[NT][4];
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                const uint4 xv = ldx16<XS>(xr[nt] + 32 * sbk + 8 * t);
-                B[nt][0] = xv.x;
-                B[nt][1] = xv.y;
-                B[nt][2] = xv.z;
-                B[nt][3] = xv.w;
-            }
-            uint32_t Av[2][4];  // [row a/b][4 bf16 pairs of this thread's 8 weights]
+            for (int bb = 0; bb < NB; bb++) {
+                const uint8_t *pa = sb + ra * SP + roff[ra] + (col0 + bb) * bpb + 2;
+                const uint8_t *pb = sb + rb * SP + roff[rb] + (col0 + bb) * bpb + 2;
+                uint32_t B[NT][4];
 #pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                const uint8_t *p = (rr ? pb : pa) + 8 * sbk;
-                const uint32_t a0 = lds_u32_a2(p), a1 = lds_u32_a2(p + 4);
-                const uint32_t gi = (a0 >> (8 * t)) & 255u;
-                const uint32_t sg = ksigns((a1 >> (7 * t)) & 127u);
-                const uint4 G = gridtab[gi];
-                // byte i of plo/phi carries the sign of weight i (lo) / 4+i (hi) in bit 7
-                const uint32_t plo = (sg & 15u) * 0x10204080u, phi = (sg >> 4) * 0x10204080u;
-                Av[rr][0] = lop_xor_and(G.x, prmt(plo, 0, 0x9484), 0x80008000u);
-                Av[rr][1] = lop_xor_and(G.y, prmt(plo, 0, 0xB4A4), 0x80008000u);
-                Av[rr][2] = lop_xor_and(G.z, prmt(phi, 0, 0x9484), 0x80008000u);
-                Av[rr][3] = lop_xor_and(G.w, prmt(phi, 0, 0xB4A4), 0x80008000u);
-            }
-            float T[NT][4];
+                for (int nt = 0; nt < NT; nt++) {
+                    const uint4 xv = ldx16<XS>(xr[nt] + bb * QK + 32 * sbk + 8 * t);
+                    B[nt][0] = xv.x;
+                    B[nt][1] = xv.y;
+                    B[nt][2] = xv.z;
+                    B[nt][3] = xv.w;
+                }
+                uint32_t Av[2][4];  // [row a/b][4 bf16 pairs of this thread's 8 weights]
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) T[nt][0] = T[nt][1] = T[nt][2] = T[nt][3] = 0.f;
+                for (int rr = 0; rr < 2; rr++) {
+                    const uint8_t *p = (rr ? pb : pa) + 8 * sbk;
+                    const uint32_t a0 = lds_u32_a2(p), a1 = lds_u32_a2(p + 4);
+                    const uint32_t gi = (a0 >> (8 * t)) & 255u;
+                    const uint32_t sg = ksigns((a1 >> (7 * t)) & 127u);
+                    const uint4 G = gridtab[gi];
+                    // byte i of plo/phi carries the sign of weight i (lo) / 4+i (hi) in bit 7
+                    const uint32_t plo = (sg & 15u) * 0x10204080u, phi = (sg >> 4) * 0x10204080u;
+                    Av[rr][0] = lop_xor_and(G.x, prmt(plo, 0, 0x9484), 0x80008000u);
+                    Av[rr][1] = lop_xor_and(G.y, prmt(plo, 0, 0xB4A4), 0x80008000u);
+                    Av[rr][2] = lop_xor_and(G.z, prmt(phi, 0, 0x9484), 0x80008000u);
+                    Av[rr][3] = lop_xor_and(G.w, prmt(phi, 0, 0xB4A4), 0x80008000u);
+                }
+                float T[NT][4];
 #pragma unroll
-            for (int s = 0; s < 2; s++) {
-                const uint32_t A[4] = {Av[0][2 * s], Av[1][2 * s], Av[0][2 * s + 1], Av[1][2 * s + 1]};
+                for (int nt = 0; nt < NT; nt++) T[nt][0] = T[nt][1] = T[nt][2] = T[nt][3] = 0.f;
 #pragma unroll
-                for (int nt = 0; nt < NT; nt++) mma16816<F16>(T[nt], A, B[nt][2 * s], B[nt][2 * s + 1], T[nt]);
-            }
-            const float2 sc = *reinterpret_cast<const float2 *>(stab + sbk * 16 + g * 2);
+                for (int s = 0; s < 2; s++) {
+                    const uint32_t A[4] = {Av[0][2 * s], Av[1][2 * s], Av[0][2 * s + 1], Av[1][2 * s + 1]};
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                ffma2(acc[nt][0], acc[nt][1], sc.x, sc.x, T[nt][0], T[nt][1]);
-                ffma2(acc[nt][2], acc[nt][3], sc.y, sc.y, T[nt][2], T[nt][3]);
+                    for (int nt = 0; nt < NT; nt++) mma16816<F16>(T[nt], A, B[nt][2 * s], B[nt][2 * s + 1], T[nt]);
+                }
+                const float2 sc = *reinterpret_cast<const float2 *>(stab + bb * TW + sbk * 16 + g * 2);
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    ffma2(acc[nt][0], acc[nt][1], sc.x, sc.x, T[nt][0], T[nt][1]);
+                    ffma2(acc[nt][2], acc[nt][3], sc.y, sc.y, T[nt][2], T[nt][3]);
+                }
             }
         }
     }
@@ -426,11 +470,11 @@ struct Block<IQ2_XXS, NT, F16, XS> {
 
 // -------------------------------------------------------------------------
 
-template <int C, int NT, bool F16, bool GLU>
+template <int C, int NT, bool F16, bool GLU, int XR>
 __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
-    using L = GLayout<C, NT>;
+    using L = GLayout<C, NT, XR>;
     constexpr bool XS = L::XS;
-    constexpr int bpb = Fmt<C>::bpb, NS = L::NS;
+    constexpr int bpb = Fmt<C>::bpb, NS = L::NS, KB = L::KB, XSTR = L::XSTR, BPW = GCfg<C>::BPW;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
     uint64_t *empty = full + NS;
@@ -439,7 +483,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     int *s_last = reinterpret_cast<int *>(smem + L::OFF_MISC + 4);
     uint4 *gridtab = reinterpret_cast<uint4 *>(smem + L::OFF_GRID);
     uint8_t *ring = smem + L::OFF_RING;
-    float *red = reinterpret_cast<float *>(smem + L::OFF_RED);
+    float *red0 = reinterpret_cast<float *>(smem + L::OFF_RED);
+    float *Ssm = reinterpret_cast<float *>(smem + L::OFF_S);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = a.K / QK;
@@ -508,7 +553,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             const int bs = st * KB, nbk = min(KB, nb - bs);
             const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
             const uint32_t off = (uint32_t)(src & 15);
-            const uint32_t bytes = valid ? ((off + nbk * bpb + 15) & ~15u) : 0u;
+            const uint32_t bytes = (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
             const uint32_t xbytes = (XS && lane < T.m) ? (uint32_t)nbk * QK * 2 : 0u;
             rowoff[slot * 32 + lane] = (uint8_t)off;
             uint32_t total = bytes + xbytes;
@@ -528,10 +573,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
 
     // ---------------- consumer warps: warp -> (16-row half mt, block column col) ----------------
     const int mt = warp & 1, col = warp >> 1;
-    float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * GCfg<C>::TABW;
+    float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * GCfg<C>::TABW * BPW;
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
     uint32_t it = 0;
     int64_t i = lo;
+    int rp = 0, s_group = -1;
     while (i < hi) {
         const int64_t gt = i / nst;
         const int st0 = (int)(i - gt * nst);
@@ -539,6 +585,34 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         const int64_t end = min(hi, tile_hi);
         Tile T;
         tile_of(a, gt, tiles, T);
+        float *red = red0 + rp * (L::REDB / 4);
+        rp ^= 1;
+        if constexpr (L::SX) {
+            if (T.g != s_group) {  // sub-block sums of this group's one activation row
+                s_group = T.g;
+                named_bar_sync(1, CW * 32);
+                const uint16_t *xs = reinterpret_cast<const uint16_t *>(a.x) + (int64_t)xrow_of(a, T, 0) * a.x_row_stride;
+                for (int q = ctid; q < nb * 8; q += CW * 32) {
+                    float sacc = 0.f;
+#pragma unroll
+                    for (int v = 0; v < 4; v++) {
+                        const uint4 u = __ldg(reinterpret_cast<const uint4 *>(xs + 32 * q + 8 * v));
+                        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            if constexpr (F16) {
+                                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w4[e]));
+                                sacc += f.x + f.y;
+                            } else {
+                                sacc += __uint_as_float(w4[e] << 16) + __uint_as_float(w4[e] & 0xffff0000u);
+                            }
+                        }
+                    }
+                    Ssm[q] = sacc;
+                }
+                named_bar_sync(1, CW * 32);
+            }
+        }
         float acc[NT][4];
         const uint16_t *xg[NT];  // global activation rows (non-staged path)
 #pragma unroll
@@ -553,15 +627,26 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         for (int st = st0; i < end; st++, i++, it++) {
             const int slot = it % NS;
             wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2);
-            const int b = st * KB + col;
-            if (b < nb && !*s_abort) {
+            const int col0 = col * BPW, b = st * KB + col0;
+            if (b < nb && !*s_abort && !(a.debug & 1)) {
                 const uint8_t *stg = ring + slot * L::STAGE;
                 const uint16_t *xr[NT];
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++)
-                    xr[nt] = XS ? reinterpret_cast<const uint16_t *>(stg + L::WBYTES + xtok * XSTR) + col * QK
+                    xr[nt] = XS ? reinterpret_cast<const uint16_t *>(stg + L::WBYTES + xtok * XSTR) + col0 * QK
                                 : xg[nt] + (int64_t)b * QK;
-                Block<C, NT, F16, XS>::run(stg, rowoff + slot * 32, col, mt, stab, xr, acc, gridtab);
+                if (b + BPW <= nb) {
+                    Block<C, NT, F16, XS>::template run<BPW>(stg, rowoff + slot * 32, col0, mt, stab, xr, acc, gridtab,
+                                                             Ssm + b * 8);
+                } else {  // ragged last stage of a row: one block at a time
+                    for (int bb = 0; b + bb < nb; bb++) {
+                        const uint16_t *xb[NT];
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) xb[nt] = xr[nt] + bb * QK;
+                        Block<C, NT, F16, XS>::template run<1>(stg, rowoff + slot * 32, col0 + bb, mt, stab, xb, acc,
+                                                               gridtab, Ssm + (b + bb) * 8);
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -590,7 +675,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 if (n >= a.N) continue;
                 float v = 0.f, v2 = 0.f;
 #pragma unroll
-                for (int w = 0; w < KB; w++) {
+                for (int w = 0; w < NCOL; w++) {
                     v += red[w * 8 * NT * RED_TS + tok * RED_TS + row];
                     if (GLU) v2 += red[w * 8 * NT * RED_TS + tok * RED_TS + row + 16];
                 }
@@ -605,7 +690,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 const int row = q & 31, tok = q >> 5;
                 float v = 0.f;
 #pragma unroll
-                for (int w = 0; w < KB; w++) v += red[w * 8 * NT * RED_TS + tok * RED_TS + row];
+                for (int w = 0; w < NCOL; w++) v += red[w * 8 * NT * RED_TS + tok * RED_TS + row];
                 __stcg(part + tok * 32 + row, v);
             }
             __threadfence();
@@ -635,65 +720,63 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 if (ctid == 0) a.counters[gt] = 0;
             }
         }
-        named_bar_sync(1, CW * 32);
+        // no trailing barrier: the next tile reduces into the other buffer, and
+        // the tile after that passes this tile's reads at its own barrier
     }
 }
 
-template <int C, int NT, bool F16, bool GLU>
+template <int C, int NT, bool F16, bool GLU, int XR>
 cudaError_t configure() {
     static bool done = false;  // per instantiation; the attribute set is idempotent
     if (done) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<C, NT, F16, GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GLayout<C, NT>::BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<C, NT, F16, GLU, XR>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, GLayout<C, NT, XR>::BYTES);
     if (e == cudaSuccess) done = true;
     return e;
 }
 
-template <int C, int NT, bool F16, bool GLU>
+template <int C, int NT, bool F16, bool GLU, int XR>
 int grid_for(const GemvArgs &a) {
-    using L = GLayout<C, NT>;
-    configure<C, NT, F16, GLU>();
+    using L = GLayout<C, NT, XR>;
+    configure<C, NT, F16, GLU, XR>();
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<C, NT, F16, GLU>, NTHREADS, L::BYTES);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<C, NT, F16, GLU, XR>, NTHREADS, L::BYTES);
     if (per_sm < 1) per_sm = 1;
     const int rows_out = GLU ? 16 : 32;
     const long tiles = (a.N + rows_out - 1) / rows_out;
     const long groups = a.dense_m > 0 ? (a.dense_m + 31) / 32 : a.max_groups;
-    const long nst = (a.K / QK + KB - 1) / KB;
+    const long nst = (a.K / QK + L::KB - 1) / L::KB;
     const long iters = groups * tiles * nst;
     const long cap = (long)num_sms() * per_sm;
     return (int)(iters < cap ? iters : cap);
 }
 
-template <int C, int NT, bool F16, bool GLU>
-cudaError_t launch_t(const GemvArgs &a, cudaStream_t st) {
-    using L = GLayout<C, NT>;
-    cudaError_t e = configure<C, NT, F16, GLU>();
+template <int C, int NT, bool F16, bool GLU, int XR>
+cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
+    using L = GLayout<C, NT, XR>;
+    cudaError_t e = configure<C, NT, F16, GLU, XR>();
     if (e != cudaSuccess) return e;
-    const int grid = grid_for<C, NT, F16, GLU>(a);
+    const int grid = grid_for<C, NT, F16, GLU, XR>(a);
+    if (grid_out) {  // grid size query only: sizes the stream-K partial scratch
+        *grid_out = grid;
+        return cudaSuccess;
+    }
     if (grid <= 0) return cudaSuccess;
-    gemv_kernel<C, NT, F16, GLU><<<grid, NTHREADS, L::BYTES, st>>>(a);
+    gemv_kernel<C, NT, F16, GLU, XR><<<grid, NTHREADS, L::BYTES, st>>>(a);
     return cudaGetLastError();
 }
 
 template <int C, bool F16, bool GLU>
 cudaError_t launch_nt(const GemvArgs &a, cudaStream_t st, int *grid_out) {
-    const int nt = (a.max_tokens + 7) / 8;
-    if (grid_out) {
-        // grid size query only (no launch): sizes the stream-K partial scratch
-        switch (nt) {
-        case 1: *grid_out = grid_for<C, 1, F16, GLU>(a); break;
-        case 2: *grid_out = grid_for<C, 2, F16, GLU>(a); break;
-        case 3: *grid_out = grid_for<C, 3, F16, GLU>(a); break;
-        default: *grid_out = grid_for<C, 4, F16, GLU>(a); break;
-        }
-        return cudaSuccess;
-    }
-    switch (nt) {
-    case 1: return launch_t<C, 1, F16, GLU>(a, st);
-    case 2: return launch_t<C, 2, F16, GLU>(a, st);
-    case 3: return launch_t<C, 3, F16, GLU>(a, st);
-    default: return launch_t<C, 4, F16, GLU>(a, st);
+    // one activation row: its slice is staged in the ring with the weights;
+    // more rows: MMA B fragments read from global / L1
+    switch ((a.max_tokens + 7) / 8) {
+    case 1:
+        return (a.max_tokens == 1 && a.K <= 32 * S_MAX) ? launch_t<C, 1, F16, GLU, 1>(a, st, grid_out)
+                                 : launch_t<C, 1, F16, GLU, 0>(a, st, grid_out);
+    case 2: return launch_t<C, 2, F16, GLU, 0>(a, st, grid_out);
+    case 3: return launch_t<C, 3, F16, GLU, 0>(a, st, grid_out);
+    default: return launch_t<C, 4, F16, GLU, 0>(a, st, grid_out);
     }
 }
 
