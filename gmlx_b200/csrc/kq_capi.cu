@@ -73,10 +73,13 @@ int check_x(const void *x, int dtype, int64_t row_stride, const char *what) {
     return KQ_OK;
 }
 
-// Workspace layout: [0,256) header (err int, n_groups int); then the group
-// tables, the per-slot f32 outputs, the split-K counters and partials.
+// Workspace layout: [0,256) header (err int, n_groups int); [256, 256+CNT)
+// the stream-K tile counters -- a fixed region that only the GEMV touches and
+// always leaves zero, so every call can rely on it whatever ran before; then
+// the group tables, the per-slot f32 outputs / GEMM scratch, the partials.
+constexpr size_t CNT_RESERVE = 128 * 1024;  // 32768 tiles
 struct WsPlan {
-    size_t groups_off = 256, ys_off = 0, cnt_off = 0, part_off = 0, total = 256;
+    size_t cnt_off = 256, groups_off = 256 + CNT_RESERVE, ys_off = 0, part_off = 0, total = 256;
     int max_groups = 0;
 };
 
@@ -86,9 +89,9 @@ int moe_max_groups(int64_t slots, int64_t e, int gsize) {
 
 WsPlan plan(size_t group_ints, size_t ys_bytes, size_t cnt_bytes, size_t part_bytes) {
     WsPlan p;
+    (void)cnt_bytes;  // checked against CNT_RESERVE by the callers
     p.ys_off = align256(p.groups_off + group_ints * sizeof(int));
-    p.cnt_off = align256(p.ys_off + ys_bytes);
-    p.part_off = align256(p.cnt_off + cnt_bytes);
+    p.part_off = align256(p.ys_off + ys_bytes);
     p.total = align256(p.part_off + part_bytes);
     return p;
 }
@@ -118,7 +121,10 @@ GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k,
     return a;
 }
 
+bool use_gemm(int64_t m, int act) { return act == ACT_NONE && m >= GEMM_MIN_M; }
+
 size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
+    if (use_gemm(m, act)) return plan(0, gemm_scratch_bytes(codec, n, k), 0, 0).total;
     GemvArgs a = dense_args(codec, nullptr, KQ_BF16, m, k, k, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
@@ -136,10 +142,31 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
     if (m < 0 || n <= 0 || xs < k || ys < n) return fail(KQ_ERR_SHAPE, "%s: bad sizes m=%lld n=%lld", what, (long long)m, (long long)n);
     if (m == 0) return KQ_OK;
     if (n > 0x7fffffff || k > 0x7fffffff) return fail(KQ_ERR_SHAPE, "%s: n/k too large", what);
+    if (use_gemm(m, act) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
+        const WsPlan p = plan(0, gemm_scratch_bytes(codec, n, k), 0, 0);
+        if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
+            return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
+        GemmArgs g{};
+        g.codec = codec;
+        g.M = (int)m;
+        g.N = (int)n;
+        g.K = (int)k;
+        g.x = x;
+        g.x_dtype = x_dtype;
+        g.x_row_stride = xs;
+        g.w = (const uint8_t *)w;
+        g.w_row_stride = wstride;
+        g.y = y;
+        g.y_dtype = y_dtype;
+        g.y_row_stride = ys;
+        g.err = (int *)ws;
+        return cuda_status(launch_gemm(g, (char *)ws + p.ys_off, (cudaStream_t)stream), what);
+    }
     GemvArgs a = dense_args(codec, x, x_dtype, m, k, xs, w, w2, n, wstride, y, y_dtype, ys, act);
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
     const WsPlan p = plan(0, 0, cb, pb);
+    if (cb > CNT_RESERVE) return fail(KQ_ERR_SHAPE, "%s: too many output tiles (%zu counter bytes)", what, cb);
     if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
         return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
     a.err = (int *)ws;
@@ -188,6 +215,7 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     gemv_scratch_need(a, &pb, &cb);
     const size_t ys_bytes = scores ? (size_t)slots * n * sizeof(float) : 0;
     const WsPlan p = plan((size_t)maxg * 66, ys_bytes, cb, pb);
+    if (cb > CNT_RESERVE) return fail(KQ_ERR_SHAPE, "%s: too many output tiles (%zu counter bytes)", what, cb);
     if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
         return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
     char *base = (char *)ws;

@@ -1,0 +1,369 @@
+// kq_gemm_sm100.cu -- prefill-shaped fused dequantize x GEMM on the 5th-gen
+// tensor cores (tcgen05, TMEM accumulators).  Replaces mlx-kquant's M-banded
+// qmm route of quantized_matmul (KQuantLinear, gmlx/modules.py:1535-1539;
+// "M-banded qmm tiles" CHANGELOG.md:599-600) for large M.
+//
+//   y[M_tok, N_w] = x[M_tok, K] . dequant(W[N_w, K])^T
+//
+// Tile: 128 activation rows (MMA M) x 256 weight rows (MMA N) x K, K staged
+// 64 at a time (one 128-byte swizzle atom of bf16/f16).  Warp roles (320 thr):
+//   warp 0      TMA producer: activation tile (and, for dense B, the B tile)
+//               into a 4-stage ring, SWIZZLE_128B, no cluster multicast;
+//   warp 1      allocates 256 TMEM columns; one elected lane issues
+//               tcgen05.mma (kind::f16, f32 accumulate) and tcgen05.commit;
+//   warps 2-9   Q4_K: each thread owns one weight row, reads its raw 144-byte
+//               blocks (16-byte header once per block, 32 bytes per stage) and
+//               writes the dequantized bf16/f16 row of the stage straight into
+//               the UMMA K-major SWIZZLE_128B layout; then the epilogue
+//               (tcgen05.ld 32x32b, convert, 16-byte stores).
+// Weights are rounded to the activation type before the MMA (the tolerance of
+// the matmul outputs covers it; the exact dequantization is kq_dequantize).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "kq_internal.cuh"
+#include "kq_ptx.cuh"
+
+namespace kq {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, NSTAGE = 4;
+constexpr int GT = 320;  // threads
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+constexpr int OFF_A = 0, OFF_B = NSTAGE * A_BYTES, OFF_BAR = OFF_B + NSTAGE * B_BYTES;
+constexpr int SMEM = OFF_BAR + 256 + 1024;  // + 1 KB for base alignment
+
+enum BMode : int { B_Q4K = 0, B_TMA = 1 };
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool wait_b(uint64_t *bar, uint32_t par, volatile int *abort, int *err, int code) {
+    if (mbar_try_wait(bar, par)) return true;
+    const uint64_t t0 = gtimer();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_try_wait(bar, par)) return true;
+        if ((i & 255) == 0) {
+            if (*abort) return false;
+            if (gtimer() - t0 > 2000000000ull) {
+                *abort = 1;
+                atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFF) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+template <bool F16> __device__ __forceinline__ uint32_t idesc() {
+    const uint32_t fmt = F16 ? 0u : 1u;
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(da), "l"(db), "r"(id), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t r[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+        "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <bool F16> __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (F16) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+}
+
+// (q pair as magic-offset 16-bit floats) -> d*q - m, one rounding (packed FMA)
+template <bool F16> __device__ __forceinline__ uint32_t q4_pair(uint32_t nib2, uint32_t dsc2, uint32_t ndm2) {
+    uint32_t r;
+    if constexpr (F16) {
+        __half2 q = __hsub2(*reinterpret_cast<__half2 *>(&nib2), __float2half2_rn(1024.f));
+        __half2 o = __hfma2(q, *reinterpret_cast<__half2 *>(&dsc2), *reinterpret_cast<__half2 *>(&ndm2));
+        r = *reinterpret_cast<uint32_t *>(&o);
+    } else {
+        __nv_bfloat162 q = __hsub2(*reinterpret_cast<__nv_bfloat162 *>(&nib2), __float2bfloat162_rn(128.f));
+        __nv_bfloat162 o =
+            __hfma2(q, *reinterpret_cast<__nv_bfloat162 *>(&dsc2), *reinterpret_cast<__nv_bfloat162 *>(&ndm2));
+        r = *reinterpret_cast<uint32_t *>(&o);
+    }
+    return r;
+}
+
+template <bool F16, int BMODE>
+__global__ void __launch_bounds__(GT, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+    uint64_t *fullB = fullA + NSTAGE;
+    uint64_t *empty = fullB + NSTAGE;
+    uint64_t *accbar = empty + NSTAGE;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accbar + 1);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int nk = a.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NSTAGE; i++) {
+            mbar_init(&fullA[i], 1);
+            mbar_init(&fullB[i], 8);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(accbar, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t tx = A_BYTES + (BMODE == B_TMA ? B_BYTES : 0);
+            for (int s = 0; s < nk; s++) {
+                const int slot = s % NSTAGE;
+                wait_b(&empty[slot], ((s / NSTAGE) & 1) ^ 1, s_abort, a.err, 11);
+                mbar_arrive_expect_tx(&fullA[slot], tx);
+                if (*s_abort) continue;
+                tma_load_2d(smem + OFF_A + slot * A_BYTES, &tmA, s * BK, m0, &fullA[slot]);
+                if (BMODE == B_TMA) tma_load_2d(smem + OFF_B + slot * B_BYTES, &tmB, s * BK, n0, &fullA[slot]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t id = idesc<F16>();
+            for (int s = 0; s < nk; s++) {
+                const int slot = s % NSTAGE, par = (s / NSTAGE) & 1;
+                wait_b(&fullA[slot], par, s_abort, a.err, 12);
+                if (BMODE == B_Q4K) wait_b(&fullB[slot], par, s_abort, a.err, 13);
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + OFF_A + slot * A_BYTES);
+                const uint32_t sb = smem_u32(smem + OFF_B + slot * B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++)
+                    if (!*s_abort) umma(tmem, umma_desc(sa + kk * 32), umma_desc(sb + kk * 32), id, (s | kk) ? 1u : 0u);
+                umma_commit(&empty[slot]);
+            }
+            umma_commit(accbar);
+        }
+    } else {
+        const int i = threadIdx.x - 64;  // 0..255: weight row of the tile
+        if constexpr (BMODE == B_Q4K) {
+            const int n = n0 + i;
+            const bool valid = n < a.N;
+            const uint8_t *row = a.w + (int64_t)(valid ? n : 0) * a.w_row_stride;
+            uint32_t dsc2[8], ndm2[8];
+            for (int s = 0; s < nk; s++) {
+                const int slot = s % NSTAGE, b = s >> 2, q = s & 3;
+                if (q == 0) {  // new super-block: 8 x (d*sc, -dmin*m) as packed 16-bit pairs
+                    const uint4 hv = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b * 144));
+                    const float d = half_bits_to_float(hv.x & 0xffffu), dmin = half_bits_to_float(hv.x >> 16);
+                    uint32_t sc03, sc47, m03, m47;
+                    q4k_unpack_scales(hv.y, hv.z, hv.w, sc03, sc47, m03, m47);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float ds = d * (float)((((j < 4) ? sc03 : sc47) >> (8 * (j & 3))) & 63u);
+                        const float dm = dmin * (float)((((j < 4) ? m03 : m47) >> (8 * (j & 3))) & 63u);
+                        dsc2[j] = pack2<F16>(ds, ds);
+                        ndm2[j] = pack2<F16>(-dm, -dm);
+                    }
+                }
+                const uint4 c0 = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b * 144 + 16 + 32 * q));
+                const uint4 c1 = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b * 144 + 32 + 32 * q));
+                const uint32_t wds[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                wait_b(&empty[slot], ((s / NSTAGE) & 1) ^ 1, s_abort, a.err, 14);
+                uint8_t *dst = smem + OFF_B + slot * B_BYTES + (i >> 3) * 1024 + (i & 7) * 128;
+                const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {  // 16-byte chunk c = k 8c..8c+7 of the stage
+                    const int h = c >> 2, j = 2 * q + h;
+                    const uint32_t w0 = wds[2 * (c & 3)] >> (4 * h), w1 = wds[2 * (c & 3) + 1] >> (4 * h);
+                    uint4 o;
+                    o.x = q4_pair<F16>(lop_and_or(prmt(w0, 0, 0x4140), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    o.y = q4_pair<F16>(lop_and_or(prmt(w0, 0, 0x4342), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    o.z = q4_pair<F16>(lop_and_or(prmt(w1, 0, 0x4140), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    o.w = q4_pair<F16>(lop_and_or(prmt(w1, 0, 0x4342), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    if (!valid) o = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4 *>(dst + ((c ^ (i & 7)) << 4)) = o;
+                }
+                fence_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&fullB[slot]);
+            }
+        }
+        // ---- epilogue: TMEM lane quarter = warp % 4; two warps per quarter split the columns
+        wait_b(accbar, 0, s_abort, a.err, 15);
+        tc_fence_after();
+        const int quarter = warp & 3, chalf = (warp - 2) >> 2;
+        const int tok = m0 + quarter * 32 + lane;
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 2; cc += 32) {
+            const int col = chalf * (BN / 2) + cc;
+            uint32_t r[32];
+            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col, r);
+            if (tok >= a.M || *s_abort) continue;
+            const int nb = n0 + col;
+            if (a.y_dtype == F32) {
+                float *yp = reinterpret_cast<float *>(a.y) + (int64_t)tok * a.y_row_stride + nb;
+                if (nb + 32 <= a.N && ((uintptr_t)yp & 15) == 0) {
+#pragma unroll
+                    for (int v = 0; v < 8; v++)
+                        reinterpret_cast<float4 *>(yp)[v] =
+                            make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                        __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                } else {
+                    for (int v = 0; v < 32 && nb + v < a.N; v++) yp[v] = __uint_as_float(r[v]);
+                }
+            } else {
+                const bool of16 = a.y_dtype == F16;
+                uint16_t *yp = reinterpret_cast<uint16_t *>(a.y) + (int64_t)tok * a.y_row_stride + nb;
+                uint32_t pk[16];
+#pragma unroll
+                for (int v = 0; v < 16; v++) {
+                    const float f0 = __uint_as_float(r[2 * v]), f1 = __uint_as_float(r[2 * v + 1]);
+                    pk[v] = of16 ? pack2<true>(f0, f1) : pack2<false>(f0, f1);
+                }
+                if (nb + 32 <= a.N && ((uintptr_t)yp & 15) == 0) {
+#pragma unroll
+                    for (int v = 0; v < 4; v++)
+                        reinterpret_cast<uint4 *>(yp)[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                } else {
+                    for (int v = 0; v < 32 && nb + v < a.N; v++) yp[v] = (uint16_t)(pk[v >> 1] >> (16 * (v & 1)));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host: tensor maps through the driver entry point (no -lcuda link needed)
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+bool make_map(CUtensorMap *m, const void *base, bool f16, int64_t rows, int64_t cols, int64_t row_stride_elems,
+              int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_stride_elems * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
+              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool F16, int BMODE>
+cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st) {
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, a.x, F16, a.M, a.K, a.x_row_stride, BM)) return cudaErrorInvalidValue;
+    if (BMODE == B_TMA) {
+        if (!make_map(&tb, bdense, F16, a.N, a.K, a.K, BN)) return cudaErrorInvalidValue;
+    } else {
+        tb = ta;
+    }
+    dim3 grid((a.M + BM - 1) / BM, (a.N + BN - 1) / BN);
+    gemm_kernel<F16, BMODE><<<grid, GT, SMEM, st>>>(ta, tb, a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride) {
+    (void)codec;
+    (void)n;
+    return m >= 1 && k % BK == 0 && (x_row_stride * 2) % 16 == 0 && (x_dtype == F16 || x_dtype == BF16) &&
+           encode_fn() != nullptr;
+}
+
+size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k) {
+    return codec == Q4_K ? 0 : (size_t)n * k * 2;  // dequantized copy for the B-by-TMA path
+}
+
+cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st) {
+    const bool f16 = a.x_dtype == F16;
+    if (a.codec == Q4_K) return f16 ? launch_gemm_t<true, B_Q4K>(a, nullptr, st) : launch_gemm_t<false, B_Q4K>(a, nullptr, st);
+    // other codecs: dequantize once into scratch (activation dtype), then B by TMA
+    cudaError_t e = launch_dequantize(a.codec, a.w, a.N, a.K, a.w_row_stride, scratch, a.x_dtype, st);
+    if (e != cudaSuccess) return e;
+    return f16 ? launch_gemm_t<true, B_TMA>(a, scratch, st) : launch_gemm_t<false, B_TMA>(a, scratch, st);
+}
+
+}  // namespace kq

@@ -47,6 +47,25 @@ cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st);
 // Scratch the GEMV needs for `a` (bytes of f32 partials, bytes of counters).
 void gemv_scratch_need(const GemvArgs &a, size_t *partial_bytes, size_t *counter_bytes);
 
+// Prefill-shaped GEMM on tcgen05 (see kq_gemm_sm100.cu).
+struct GemmArgs {
+    int codec;
+    int M, N, K;
+    const void *x;
+    int x_dtype;
+    int64_t x_row_stride;  // elements
+    const uint8_t *w;
+    int64_t w_row_stride;  // bytes
+    void *y;
+    int y_dtype;
+    int64_t y_row_stride;  // elements
+    int *err;
+};
+bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride);
+size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k);
+cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st);
+constexpr int GEMM_MIN_M = 33;  // activation rows from which the tensor-core GEMM takes over
+
 // MoE slot grouping: idx[S] (S = T*k slots) -> per-expert groups of <= gsize
 // slots (ascending slot order inside a group, groups ordered by expert id).
 // Activation row of slot s: xidx[s] if given, else s (xrow_is_slot) or s/k.

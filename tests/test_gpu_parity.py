@@ -207,3 +207,17 @@ def test_nn_modules_fused_and_stock_paths_agree(cuda):
     xb = synth.random_activations(2, d, seed=5)
     ref = O.matmul(xb, lin.weight.cpu().numpy(), "iq2_xxs") + 0.5
     assert rel_err(lin(to_dev_x(xb, cuda)).float().cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("codec", CODECS)
+@pytest.mark.parametrize("m,n,k", [(64, 256, 512), (200, 320, 1024), (1000, 512, 2048)])
+def test_prefill_gemm_tcgen05(cuda, codec, m, n, k):
+    """Prefill-sized M runs the tcgen05 GEMM (weights rounded to bf16 before the MMA)."""
+    w = synth.random_weight(codec, n, k, seed=31)
+    x = synth.random_activations(m, k, seed=32)
+    ref = O.matmul(x, w, codec)
+    y = kq.quantized_matmul(to_dev_x(x, cuda), torch.from_numpy(w).to(cuda), None, codec, out_dtype=torch.float32)
+    assert rel_err(y.cpu().numpy(), ref) <= TOL
+    y16 = kq.quantized_matmul(to_dev_x(x, cuda, torch.float16), torch.from_numpy(w).to(cuda), None, codec)
+    assert y16.dtype == torch.float16
+    assert rel_err(y16.float().cpu().numpy(), ref) <= TOL

@@ -63,9 +63,9 @@ def test_noalloc_matches_workspace_entry(cuda, codec, n, k, m):
 def test_noalloc_rejects_oversized_shape(cuda):
     L = _lib.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    # 256 groups of 32 rows x 2048 tiles of counters exceed the fixed array;
-    # the size check comes before any pointer is used
-    rc = L.kq_quantized_matmul_noalloc(12, None, KQ_BF16, 8192, 256, 256, None, 65536, 144, None, KQ_BF16, 65536,
+    # a Q6_K prefill of 65536 x 256 needs a 32 MiB dequantized-weight scratch,
+    # beyond the fixed array; the size check comes before any pointer is used
+    rc = L.kq_quantized_matmul_noalloc(14, None, KQ_BF16, 8192, 256, 256, None, 65536, 210, None, KQ_BF16, 65536,
                                        stream)
     assert rc == _lib.KQ_ERR_WORKSPACE
     assert b"scratch" in L.kq_last_error()
