@@ -29,11 +29,19 @@
 namespace kq {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, NSTAGE = 4;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int GT = 320;  // threads
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
-constexpr int OFF_A = 0, OFF_B = NSTAGE * A_BYTES, OFF_BAR = OFF_B + NSTAGE * B_BYTES;
-constexpr int SMEM = OFF_BAR + 256 + 1024;  // + 1 KB for base alignment
+
+// MT activation-row tiles of 128 per CTA (MT accumulators of 256 TMEM columns
+// each): with MT = 2 every dequantized weight tile feeds twice the MMA work.
+template <int MT> struct GL {
+    static constexpr int NSTAGE = MT == 1 ? 4 : 3;
+    static constexpr int STAGE_A = MT * A_BYTES;
+    static constexpr int OFF_A = 0, OFF_B = NSTAGE * STAGE_A, OFF_BAR = OFF_B + NSTAGE * B_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + 1 KB for base alignment
+    static constexpr int TMEM_COLS = MT * BN;
+};
 
 enum BMode : int { B_Q4K = 0, B_TMA = 1 };
 
@@ -132,9 +140,11 @@ template <bool F16> __device__ __forceinline__ uint32_t q4_pair(uint32_t nib2, u
     return r;
 }
 
-template <bool F16, int BMODE>
+template <bool F16, int BMODE, int MT>
 __global__ void __launch_bounds__(GT, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+    using L = GL<MT>;
+    constexpr int NSTAGE = L::NSTAGE, OFF_A = L::OFF_A, OFF_B = L::OFF_B, OFF_BAR = L::OFF_BAR;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
@@ -145,7 +155,7 @@ __global__ void __launch_bounds__(GT, 1)
     volatile int *s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int m0 = blockIdx.x * BM * MT, n0 = blockIdx.y * BN;
     const int nk = a.K / BK;
 
     if (threadIdx.x == 0) {
@@ -160,7 +170,7 @@ __global__ void __launch_bounds__(GT, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(BN));
+                     "r"(L::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -170,13 +180,15 @@ __global__ void __launch_bounds__(GT, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t tx = A_BYTES + (BMODE == B_TMA ? B_BYTES : 0);
+            const uint32_t tx = MT * A_BYTES + (BMODE == B_TMA ? B_BYTES : 0);
             for (int s = 0; s < nk; s++) {
                 const int slot = s % NSTAGE;
                 wait_b(&empty[slot], ((s / NSTAGE) & 1) ^ 1, s_abort, a.err, 11);
                 mbar_arrive_expect_tx(&fullA[slot], tx);
                 if (*s_abort) continue;
-                tma_load_2d(smem + OFF_A + slot * A_BYTES, &tmA, s * BK, m0, &fullA[slot]);
+#pragma unroll
+                for (int t = 0; t < MT; t++)
+                    tma_load_2d(smem + OFF_A + slot * L::STAGE_A + t * A_BYTES, &tmA, s * BK, m0 + t * BM, &fullA[slot]);
                 if (BMODE == B_TMA) tma_load_2d(smem + OFF_B + slot * B_BYTES, &tmB, s * BK, n0, &fullA[slot]);
             }
         }
@@ -188,11 +200,15 @@ __global__ void __launch_bounds__(GT, 1)
                 wait_b(&fullA[slot], par, s_abort, a.err, 12);
                 if (BMODE == B_Q4K) wait_b(&fullB[slot], par, s_abort, a.err, 13);
                 tc_fence_after();
-                const uint32_t sa = smem_u32(smem + OFF_A + slot * A_BYTES);
+                const uint32_t sa = smem_u32(smem + OFF_A + slot * L::STAGE_A);
                 const uint32_t sb = smem_u32(smem + OFF_B + slot * B_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++)
-                    if (!*s_abort) umma(tmem, umma_desc(sa + kk * 32), umma_desc(sb + kk * 32), id, (s | kk) ? 1u : 0u);
+                for (int t = 0; t < MT; t++)
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; kk++)
+                        if (!*s_abort)
+                            umma(tmem + t * BN, umma_desc(sa + t * A_BYTES + kk * 32), umma_desc(sb + kk * 32), id,
+                                 (s | kk) ? 1u : 0u);
                 umma_commit(&empty[slot]);
             }
             umma_commit(accbar);
@@ -204,10 +220,21 @@ __global__ void __launch_bounds__(GT, 1)
             const bool valid = n < a.N;
             const uint8_t *row = a.w + (int64_t)(valid ? n : 0) * a.w_row_stride;
             uint32_t dsc2[8], ndm2[8];
+            // loads run one stage ahead of the decode (header of the next block, next chunk)
+            uint4 nh = __ldg(reinterpret_cast<const uint4 *>(row));
+            uint4 n0c = __ldg(reinterpret_cast<const uint4 *>(row + 16));
+            uint4 n1c = __ldg(reinterpret_cast<const uint4 *>(row + 32));
             for (int s = 0; s < nk; s++) {
                 const int slot = s % NSTAGE, b = s >> 2, q = s & 3;
+                const uint4 hcur = nh, c0 = n0c, c1 = n1c;
+                if (s + 1 < nk) {
+                    const int b1 = (s + 1) >> 2, q1 = (s + 1) & 3;
+                    if (q1 == 0) nh = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b1 * 144));
+                    n0c = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b1 * 144 + 16 + 32 * q1));
+                    n1c = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b1 * 144 + 32 + 32 * q1));
+                }
                 if (q == 0) {  // new super-block: 8 x (d*sc, -dmin*m) as packed 16-bit pairs
-                    const uint4 hv = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b * 144));
+                    const uint4 hv = hcur;
                     const float d = half_bits_to_float(hv.x & 0xffffu), dmin = half_bits_to_float(hv.x >> 16);
                     uint32_t sc03, sc47, m03, m47;
                     q4k_unpack_scales(hv.y, hv.z, hv.w, sc03, sc47, m03, m47);
@@ -219,8 +246,6 @@ __global__ void __launch_bounds__(GT, 1)
                         ndm2[j] = pack2<F16>(-dm, -dm);
                     }
                 }
-                const uint4 c0 = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b * 144 + 16 + 32 * q));
-                const uint4 c1 = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b * 144 + 32 + 32 * q));
                 const uint32_t wds[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
                 wait_b(&empty[slot], ((s / NSTAGE) & 1) ^ 1, s_abort, a.err, 14);
                 uint8_t *dst = smem + OFF_B + slot * B_BYTES + (i >> 3) * 1024 + (i & 7) * 128;
@@ -246,12 +271,13 @@ __global__ void __launch_bounds__(GT, 1)
         wait_b(accbar, 0, s_abort, a.err, 15);
         tc_fence_after();
         const int quarter = warp & 3, chalf = (warp - 2) >> 2;
-        const int tok = m0 + quarter * 32 + lane;
 #pragma unroll 1
-        for (int cc = 0; cc < BN / 2; cc += 32) {
+        for (int q32 = 0; q32 < MT * (BN / 2); q32 += 32) {
+            const int t = q32 / (BN / 2), cc = q32 % (BN / 2);
+            const int tok = m0 + t * BM + quarter * 32 + lane;
             const int col = chalf * (BN / 2) + cc;
             uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col, r);
+            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * BN + col), r);
             if (tok >= a.M || *s_abort) continue;
             const int nb = n0 + col;
             if (a.y_dtype == F32) {
@@ -288,7 +314,7 @@ __global__ void __launch_bounds__(GT, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS));
     }
 }
 
@@ -324,11 +350,12 @@ bool make_map(CUtensorMap *m, const void *base, bool f16, int64_t rows, int64_t 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool F16, int BMODE>
+template <bool F16, int BMODE, int MT>
 cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        cudaError_t e =
+            cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, GL<MT>::SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
@@ -339,9 +366,17 @@ cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st
     } else {
         tb = ta;
     }
-    dim3 grid((a.M + BM - 1) / BM, (a.N + BN - 1) / BN);
-    gemm_kernel<F16, BMODE><<<grid, GT, SMEM, st>>>(ta, tb, a);
+    dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + BN - 1) / BN);
+    gemm_kernel<F16, BMODE, MT><<<grid, GT, GL<MT>::SMEM, st>>>(ta, tb, a);
     return cudaGetLastError();
+}
+
+template <bool F16, int BMODE>
+cudaError_t launch_gemm_mt(const GemmArgs &a, const void *bdense, cudaStream_t st) {
+    // two activation-row tiles per CTA once there are enough CTAs to fill the GPU
+    const long ctas2 = (long)((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
+    if (ctas2 >= num_sms()) return launch_gemm_t<F16, BMODE, 2>(a, bdense, st);
+    return launch_gemm_t<F16, BMODE, 1>(a, bdense, st);
 }
 
 }  // namespace
@@ -359,11 +394,11 @@ size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k) {
 
 cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st) {
     const bool f16 = a.x_dtype == F16;
-    if (a.codec == Q4_K) return f16 ? launch_gemm_t<true, B_Q4K>(a, nullptr, st) : launch_gemm_t<false, B_Q4K>(a, nullptr, st);
+    if (a.codec == Q4_K) return f16 ? launch_gemm_mt<true, B_Q4K>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K>(a, nullptr, st);
     // other codecs: dequantize once into scratch (activation dtype), then B by TMA
     cudaError_t e = launch_dequantize(a.codec, a.w, a.N, a.K, a.w_row_stride, scratch, a.x_dtype, st);
     if (e != cudaSuccess) return e;
-    return f16 ? launch_gemm_t<true, B_TMA>(a, scratch, st) : launch_gemm_t<false, B_TMA>(a, scratch, st);
+    return f16 ? launch_gemm_mt<true, B_TMA>(a, scratch, st) : launch_gemm_mt<false, B_TMA>(a, scratch, st);
 }
 
 }  // namespace kq
