@@ -107,33 +107,41 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(mhz)}
 
 
-def build_layers(dev, n_layers, seed0=100):
+def build_layers(dev, n_layers, world=1, rank=0, seed0=100):
+    """n_layers distinct Llama-3-8B layers; with world > 1 this rank's tensor-
+    parallel shards (q/k/v/gate/up by output rows, o/down by K blocks)."""
     import torch
 
+    from gmlx_b200 import parallel as par
     from gmlx_b200 import synth
     layers = []
     for li in range(n_layers):
         s = seed0 + 10 * li
-        q = synth.random_weight("q4_k", 4096, 4096, seed=s)
-        k = synth.random_weight("q4_k", 1024, 4096, seed=s + 1)
-        v = synth.random_weight("q4_k", 1024, 4096, seed=s + 2)
-        layer = {
-            "qkv": torch.from_numpy(np.concatenate([q, k, v], 0)).to(dev),
-            "o": torch.from_numpy(synth.random_weight("q4_k", 4096, 4096, seed=s + 3)).to(dev),
-            "gate": torch.from_numpy(synth.random_weight("q4_k", 14336, 4096, seed=s + 4)).to(dev),
-            "up": torch.from_numpy(synth.random_weight("q4_k", 14336, 4096, seed=s + 5)).to(dev),
-            "down": torch.from_numpy(synth.random_weight("q6_k", 4096, 14336, seed=s + 6)).to(dev),
+        full = {
+            "q": synth.random_weight("q4_k", 4096, 4096, seed=s),
+            "k": synth.random_weight("q4_k", 1024, 4096, seed=s + 1),
+            "v": synth.random_weight("q4_k", 1024, 4096, seed=s + 2),
+            "o": synth.random_weight("q4_k", 4096, 4096, seed=s + 3),
+            "gate": synth.random_weight("q4_k", 14336, 4096, seed=s + 4),
+            "up": synth.random_weight("q4_k", 14336, 4096, seed=s + 5),
+            "down": synth.random_weight("q6_k", 4096, 14336, seed=s + 6),
         }
-        layers.append(layer)
+        sh = par.shard_llama_layer(full, world, rank)
+        layers.append({k: torch.from_numpy(v).to(dev) for k, v in sh.items()})
     return layers
 
 
-def layer_step(kq, L, x):
-    """One decoder-layer pass of the seven quantized projections (4 launches)."""
+def layer_step(kq, L, x, a=None, dist=None):
+    """One decoder-layer pass of the seven quantized projections (4 launches;
+    under tensor parallelism + 2 all-reduces of the row-parallel outputs).
+    `a` stands in for this rank's slice of the attention output."""
     qkv = kq.quantized_matmul(x, L["qkv"], None, "q4_k")
-    o = kq.quantized_matmul(x, L["o"], None, "q4_k")
+    o = kq.quantized_matmul(x if a is None else a, L["o"], None, "q4_k")
     h = kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
     y = kq.quantized_matmul(h, L["down"], None, "q6_k")
+    if dist is not None:
+        dist.all_reduce(o)
+        dist.all_reduce(y)
     return qkv, o, y
 
 
@@ -169,6 +177,56 @@ def time_graph(torch, fn, steps, warmup, stream, min_warm_s=0.0):
         b.record(stream)
     torch.cuda.synchronize()
     return a.elapsed_time(b) / 1e3  # seconds for `steps` replays
+
+
+MOE_CONFIGS = (
+    # (name, experts, top_k, hidden, ffn, gate/up codec, down codec, token counts)
+    ("qwen3-30b-a3b-like", 128, 8, 2048, 768, "q4_k", "q6_k", (1, 64)),
+    ("deepseek-v3-like-iq2", 256, 8, 7168, 2048, "iq2_xxs", "iq2_xxs", (1, 8, 64)),
+)
+
+
+def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
+    """Expert-parallel routed expert layer (configs 4 and 5): experts split by
+    id range over ranks, all ranks route the same tokens, partial outputs are
+    all-reduced.  Reported per token count: layer ms (max over ranks) and GB/s
+    of the expert bytes the routing touched (unique experts x expert bytes)."""
+    from gmlx_b200 import synth
+    out = {}
+    for name, E, K, D, F, cgu, cd, ts in MOE_CONFIGS:
+        el = E // world
+        base = rank * el
+        wg = torch.from_numpy(synth.random_weight(cgu, F, D, seed=11, experts=E)[base:base + el]).to(dev)
+        wu = torch.from_numpy(synth.random_weight(cgu, F, D, seed=12, experts=E)[base:base + el]).to(dev)
+        wd = torch.from_numpy(synth.random_weight(cd, D, F, seed=13, experts=E)[base:base + el]).to(dev)
+        router_w = torch.randn(E, D, device=dev, generator=torch.Generator(device=dev).manual_seed(5)) / D ** 0.5
+        ebytes = (wg[0].numel() + wu[0].numel() + wd[0].numel())
+        cell = {}
+        for t in ts:
+            x = torch.randn(t, D, device=dev, generator=torch.Generator(device=dev).manual_seed(t)).to(torch.bfloat16)
+            logits = x.float() @ router_w.t()
+
+            def layer():
+                idx, sc = kq.moe_router_topk(logits, K, True)
+                y = kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, cgu, cd, base, E, out_dtype=torch.float32)
+                if world > 1:
+                    dist.all_reduce(y)
+                return idx
+            idx = layer()
+            uniq = int(torch.unique(idx).numel())
+            reps = 20
+            secs = time_graph(torch, layer, reps, 3, stream) / reps
+            tt = torch.tensor([secs], device=dev, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            secs = float(tt.item())
+            gbs = uniq * ebytes / secs / 1e9
+            cell[f"t{t}"] = {"ms": secs * 1e3, "unique_experts": uniq, "GB/s": gbs,
+                             "frac_hbm_per_gpu": gbs / world / hbm_peak}
+        out[name] = cell
+        del wg, wu, wd
+        torch.cuda.empty_cache()
+    return out
 
 
 def cpu_baseline_run(seconds=12.0, threads=None):
@@ -225,6 +283,7 @@ def main():
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-moe", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -247,16 +306,19 @@ def main():
     _lib.load()
     hbm_peak, tc_peak, peak_kind = _peaks()
 
-    layers = build_layers(dev, N_LAYERS, seed0=100 + 1000 * rank)
+    layers = build_layers(dev, N_LAYERS, world, rank)
     stream = torch.cuda.Stream(dev)
+    dd = dist if world > 1 else None
+    ka = 4096 // world  # this rank's slice of the attention output (o_proj K)
 
     def measure(m, steps, warmup, min_warm_s=0.0):
         g = torch.Generator(device="cpu").manual_seed(0)
         xs = [torch.randn(m, 4096, generator=g).to(torch.bfloat16).to(dev) for _ in range(N_LAYERS)]
+        att = [x[:, :ka].contiguous() for x in xs]
 
         def one_pass():
             for li, L in enumerate(layers):
-                layer_step(kq, L, xs[li])
+                layer_step(kq, L, xs[li], att[li], dd)
         reps = max(1, steps // N_LAYERS)
         secs = time_graph(torch, one_pass, reps, max(1, warmup // N_LAYERS), stream, min_warm_s)
         return secs / (reps * N_LAYERS)
@@ -272,7 +334,7 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     t_step = float(tt.item())
     nbytes = step_bytes(args.m)
-    value = nbytes * world / t_step / 1e9
+    value = nbytes / t_step / 1e9  # the whole layer's bytes (strong scaling: the layer is split over ranks)
 
     # dominant kernel: the fused gate/up GLU GEMV (66 MB of the 138 MB step),
     # timed alone on its launch stream with CUDA events over many launches
@@ -283,7 +345,7 @@ def main():
             kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
     reps = 6
     glu_t = time_graph(torch, glu_pass, reps, 2, stream) / (reps * N_LAYERS)
-    glu_bytes = 2 * 14336 * 2304 + args.m * 4096 * 2 + args.m * 14336 * 2
+    glu_bytes = 2 * (14336 // world) * 2304 + args.m * 4096 * 2 + args.m * (14336 // world) * 2
     achieved = glu_bytes / glu_t / 1e9
 
     # e2e through the public op API: pinned host input -> device, layer, output -> host
@@ -293,14 +355,14 @@ def main():
     torch.cuda.synchronize()
     for i in range(args.warmup):
         dx = hx.to(dev, non_blocking=True)
-        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx)
+        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka], dd)
         hy.copy_(y, non_blocking=True)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for i in range(e2e_steps):
         dx = hx.to(dev, non_blocking=True)
-        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx)
+        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka].contiguous(), dd)
         hy.copy_(y, non_blocking=True)
     b.record()
     torch.cuda.synchronize()
@@ -337,22 +399,26 @@ def main():
                                 "frac_tensor": flops_per_tok * m / t / 1e12 / tc_peak}
         del gu
 
+    moe = {} if args.no_moe else run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak)
+
     if rank == 0:
         cpu = None if args.no_cpu or world > 1 else cpu_baseline_run()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "llama3-8b Q4_K_M decoder layer decode GEMV (q/k/v/o/gate/up Q4_K, down Q6_K)",
                        "m": args.m, "layers_cycled": N_LAYERS, "weight_bytes_per_step": LAYER_WEIGHT_BYTES,
                        "l2": "inputs larger than L2 (8 distinct layers, 1.10 GB, cycled)",
-                       "parallelism": f"replicas{world}" if world > 1 else "single"},
+                       "parallelism": f"tp{world} (column-parallel qkv/gate/up, row-parallel o/down, "
+                                      "NCCL all-reduce)" if world > 1 else "single"},
             "frac_hbm": value / world / hbm_peak,
+            "moe": moe,
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K, GLU> (gate+up 14336x4096)",
                          "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None},
             "cpu_baseline": cpu,
-            "e2e": {"value": nbytes * world / e2e_t / 1e9, "unit": UNIT,
+            "e2e": {"value": nbytes / e2e_t / 1e9, "unit": UNIT,
                     "h2d_bytes_per_step": int(hx.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2)},
             "gpu_launches": 4 * args.steps,
             "clocks": clk.summary(),

@@ -42,6 +42,9 @@ SIGNATURES = {
                              _sz, _vp]),
     "kq_moe_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64]),
     "kq_workspace_error": (_i32, [_vp, _i32, _vp]),
+    "kq_moe_expert_layer_local": (_i32, [_i32, _i32, _vp, _i32, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _vp,
+                                         _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _i32, _vp, _sz, _vp]),
+    "kq_moe_expert_layer_workspace_size": (_sz, [_i32, _i32, _i64, _i32, _i64, _i64, _i64, _i32]),
     "kq_quantized_matmul_noalloc": (_i32, [_i32, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _vp]),
 }
 

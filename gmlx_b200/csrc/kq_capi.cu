@@ -77,7 +77,7 @@ int check_x(const void *x, int dtype, int64_t row_stride, const char *what) {
 // the stream-K tile counters -- a fixed region that only the GEMV touches and
 // always leaves zero, so every call can rely on it whatever ran before; then
 // the group tables, the per-slot f32 outputs / GEMM scratch, the partials.
-constexpr size_t CNT_RESERVE = 128 * 1024;  // 32768 tiles
+constexpr size_t CNT_RESERVE = 1024 * 1024;  // 262144 (group, tile) counters
 struct WsPlan {
     size_t cnt_off = 256, groups_off = 256 + CNT_RESERVE, ys_off = 0, part_off = 0, total = 256;
     int max_groups = 0;
@@ -180,7 +180,9 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
 int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, int64_t slots, int kslot,
                int64_t tokens, const int32_t *idx, const int32_t *xidx, int mode, const void *w, const void *w2,
                int64_t e, int64_t n, int64_t wrs, int64_t wes, int act, void *y, int y_dtype, int64_t yrs,
-               const float *scores, void *ws, size_t ws_bytes, void *stream, const char *what) {
+               const float *scores, void *ws, size_t ws_bytes, void *stream, const char *what, int64_t ebase = 0,
+               int64_t etotal = -1) {
+    if (etotal < 0) etotal = e;
     int rc;
     if ((rc = check_weights(codec, w, kin, wrs, what))) return rc;
     if (w2 && (rc = check_weights(codec, w2, kin, wrs, what))) return rc;
@@ -190,9 +192,10 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     if (wes < n * wrs) return fail(KQ_ERR_SHAPE, "%s: expert stride smaller than one expert", what);
     if (slots == 0) return KQ_OK;
     if (slots < 0 || slots > (1 << 20)) return fail(KQ_ERR_SHAPE, "%s: slot count %lld out of range", what, (long long)slots);
+    // groups of <= 8 slots: one MMA n-tile; an expert with more routed rows
+    // streams its weights once per 8 rows (decode routes few rows per expert)
     const int64_t per_expert = mode == 2 ? slots : tokens;  // distinct experts per token bound group sizes
-    const int maxtok = (int)(per_expert < 32 ? per_expert : 32);
-    const int gsize = (maxtok + 7) / 8 * 8 < 32 ? (maxtok + 7) / 8 * 8 : 32;
+    const int gsize = (int)(per_expert < 8 ? per_expert : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;
@@ -222,7 +225,8 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     int *err = (int *)base, *ng = (int *)(base + 4);
     int *gexp = (int *)(base + p.groups_off), *gcnt = gexp + maxg, *gx = gcnt + maxg, *go = gx + (size_t)maxg * 32;
     cudaStream_t st = (cudaStream_t)stream;
-    cudaError_t ce = launch_moe_groups(idx, (int)slots, kslot, (int)e, mode == 1, xidx, gsize, ng, gexp, gcnt, gx, go,
+    cudaError_t ce = launch_moe_groups(idx, (int)slots, kslot, (int)ebase, (int)e, (int)etotal, mode == 1, xidx, gsize,
+                                       ng, gexp, gcnt, gx, go,
                                        maxg, err, st);
     if (ce != cudaSuccess) return cuda_status(ce, what);
     a.n_groups = ng;
@@ -244,7 +248,8 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     }
     if ((ce = launch_gemv(a, st)) != cudaSuccess) return cuda_status(ce, what);
     if (scores)
-        if ((ce = launch_moe_mix((const float *)(base + p.ys_off), scores, (int)tokens, kslot, (int)n, y, y_dtype, st)) !=
+        if ((ce = launch_moe_mix((const float *)(base + p.ys_off), scores, idx, (int)ebase, (int)e, (int)tokens, kslot,
+                                 (int)n, y, y_dtype, st)) !=
             cudaSuccess)
             return cuda_status(ce, what);
     return KQ_OK;
@@ -252,8 +257,7 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
 
 size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_t n, int64_t kin, int act,
                  bool mix) {
-    const int maxtok = (int)(per_expert < 32 ? (per_expert > 0 ? per_expert : 1) : 32);
-    const int gsize = (maxtok + 7) / 8 * 8 < 32 ? (maxtok + 7) / 8 * 8 : 32;
+    const int gsize = (int)(per_expert < 8 ? (per_expert > 0 ? per_expert : 1) : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;
@@ -344,8 +348,8 @@ size_t kq_moe_workspace_size(int codec, int64_t slots, int64_t e, int64_t n, int
     if (slots <= 0) slots = 1;
     // the largest plan over every group size the calls can pick
     size_t best = 256;
-    const int64_t pe[5] = {1, 9, 17, 25, 32};
-    for (int i = 0; i < 5; i++)
+    const int64_t pe[8] = {1, 2, 3, 4, 5, 6, 7, 8};
+    for (int i = 0; i < 8; i++)
         for (int act = 0; act < 2; act++) {
             const size_t s = routed_ws(codec, slots, pe[i], e, n, k_in, act ? ACT_SILU : ACT_NONE, true);
             best = s > best ? s : best;
@@ -395,6 +399,47 @@ int kq_gather_qmm(int codec, const void *x, int x_dtype, int64_t k, int64_t x_ro
     return run_routed(codec, x, x_dtype, x_row_stride, k, rows, 1, rows, expert_index, x_index, x_index ? 2 : 1, w,
                       nullptr, e, n, w_row_stride, w_expert_stride, ACT_NONE, y, y_dtype, n, nullptr, workspace,
                       workspace_bytes, stream, "gather_qmm");
+}
+
+size_t kq_moe_expert_layer_workspace_size(int codec_gu, int codec_d, int64_t t, int k, int64_t e_local, int64_t d,
+                                          int64_t f, int h_dtype) {
+    if (!codec_ok(codec_gu) || !codec_ok(codec_d) || t <= 0 || k <= 0 || e_local <= 0 || d % QK || f % QK) return 256;
+    const int64_t slots = t * k;
+    const size_t a = routed_ws(codec_gu, slots, t, e_local, f, d, ACT_SILU, false);
+    const size_t b = routed_ws(codec_d, slots, t, e_local, d, f, ACT_NONE, true);
+    const size_t esz = h_dtype == KQ_F32 ? 4 : 2;
+    return align256(a > b ? a : b) + align256((size_t)slots * f * esz);
+}
+
+int kq_moe_expert_layer_local(int codec_gu, int codec_d, const void *x, int x_dtype, int64_t t, int64_t d,
+                              const int32_t *idx, int k, const float *scores, const void *gate_w, const void *up_w,
+                              int64_t gu_row_stride, int64_t gu_expert_stride, const void *down_w,
+                              int64_t d_row_stride, int64_t d_expert_stride, int64_t e_local, int64_t f,
+                              int64_t expert_base, int64_t e_total, int act, void *y, int y_dtype, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    if (act < KQ_ACT_SILU || act > KQ_ACT_GELU_TANH) return fail(KQ_ERR_SHAPE, "moe_expert_layer_local: bad activation %d", act);
+    if (k <= 0 || t < 0) return fail(KQ_ERR_SHAPE, "moe_expert_layer_local: bad t/k");
+    if (expert_base < 0 || e_local <= 0 || expert_base + e_local > e_total)
+        return fail(KQ_ERR_SHAPE, "moe_expert_layer_local: local experts [%lld, %lld) outside %lld", (long long)expert_base,
+                    (long long)(expert_base + e_local), (long long)e_total);
+    if (t == 0) return KQ_OK;
+    const int64_t slots = t * k;
+    const size_t a = routed_ws(codec_gu, slots, t, e_local, f, d, ACT_SILU, false);
+    const size_t b = routed_ws(codec_d, slots, t, e_local, d, f, ACT_NONE, true);
+    const size_t routed = align256(a > b ? a : b);
+    const size_t need = routed + align256((size_t)slots * f * 2);
+    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255))
+        return fail(KQ_ERR_WORKSPACE, "moe_expert_layer_local: workspace of %zu bytes required, got %zu", need,
+                    workspace_bytes);
+    void *h = (char *)workspace + routed;
+    int rc = run_routed(codec_gu, x, x_dtype, d, d, slots, k, t, idx, nullptr, 0, gate_w, up_w, e_local, f,
+                        gu_row_stride, gu_expert_stride, act, h, x_dtype, f, nullptr, workspace, routed, stream,
+                        "moe_expert_layer_local", expert_base, e_total);
+    if (rc) return rc;
+    return run_routed(codec_d, h, x_dtype, f, f, slots, k, t, idx, nullptr, 1, down_w, nullptr, e_local, d, d_row_stride,
+                      d_expert_stride, ACT_NONE, y, y_dtype, d, scores, workspace, routed, stream,
+                      "moe_expert_layer_local", expert_base, e_total);
 }
 
 int kq_workspace_error(void *workspace, int clear, void *stream) {

@@ -66,15 +66,16 @@ size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k);
 cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st);
 constexpr int GEMM_MIN_M = 33;  // activation rows from which the tensor-core GEMM takes over
 
-// MoE slot grouping: idx[S] (S = T*k slots) -> per-expert groups of <= gsize
-// slots (ascending slot order inside a group, groups ordered by expert id).
-// Activation row of slot s: xidx[s] if given, else s (xrow_is_slot) or s/k.
-cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int E, int xrow_is_slot, const int32_t *xidx,
-                              int gsize, int *n_groups, int *grp_expert, int *grp_count, int *grp_xrow,
-                              int *grp_orow, int max_groups, int *err, cudaStream_t st);
-// y[t][n] = sum_j scores[t][j] * ys[t*k+j][n]  (fixed j order).
-cudaError_t launch_moe_mix(const float *ys, const float *scores, int T, int k, int N, void *y, int y_dtype,
-                           cudaStream_t st);
+// MoE slot grouping: idx[S] (S = T*k slots) -> groups of <= gsize slots per
+// local expert (experts [ebase, ebase+ecount); ascending slot order inside a
+// group, groups ordered by expert).  Activation row of slot s: xidx[s] if
+// given, else s (xrow_is_slot) or s/k.  Group expert ids are local.
+cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int ebase, int ecount, int etotal, int xrow_is_slot,
+                              const int32_t *xidx, int gsize, int *n_groups, int *grp_expert, int *grp_count,
+                              int *grp_xrow, int *grp_orow, int max_groups, int *err, cudaStream_t st);
+// y[t][n] = sum over local slots j of scores[t][j] * ys[t*k+j][n]  (fixed j order).
+cudaError_t launch_moe_mix(const float *ys, const float *scores, const int32_t *idx, int ebase, int ecount, int T,
+                           int k, int N, void *y, int y_dtype, cudaStream_t st);
 cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int norm, int32_t *idx, float *scores,
                                int *err, cudaStream_t st);
 

@@ -79,37 +79,41 @@ __global__ void router_kernel(const float *__restrict__ logits, int T, int E, in
     }
 }
 
-__global__ void groups_kernel(const int32_t *__restrict__ idx, int S, int k, int E, int xrow_is_slot,
-                              const int32_t *__restrict__ xidx, int gsize, int *__restrict__ n_groups, int *__restrict__ grp_expert, int *__restrict__ grp_count,
+// Groups over the local expert range [ebase, ebase + ecount): slots routed
+// elsewhere are skipped (expert-parallel ranks); ids outside [0, etotal) are
+// an error.
+__global__ void groups_kernel(const int32_t *__restrict__ idx, int S, int k, int ebase, int ecount, int etotal,
+                              int xrow_is_slot, const int32_t *__restrict__ xidx, int gsize,
+                              int *__restrict__ n_groups, int *__restrict__ grp_expert, int *__restrict__ grp_count,
                               int *__restrict__ grp_xrow, int *__restrict__ grp_orow, int max_groups,
                               int *__restrict__ err) {
     __shared__ int s_first[RT_MAXE + 1];
     __shared__ int s_bad;
     if (threadIdx.x == 0) s_bad = 0;
     __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    for (int s = threadIdx.x; s < S; s += blockDim.x) {
+        const int v = idx[s];
+        if (v < 0 || v >= etotal) s_bad = 1;
+    }
+    for (int e = threadIdx.x; e < ecount; e += blockDim.x) {
         int c = 0;
-        for (int s = 0; s < S; s++) {
-            const int v = idx[s];
-            c += v == e;
-            if (e == 0 && (v < 0 || v >= E)) s_bad = 1;
-        }
+        for (int s = 0; s < S; s++) c += idx[s] == ebase + e;
         s_first[e + 1] = (c + gsize - 1) / gsize;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         s_first[0] = 0;
-        for (int e = 0; e < E; e++) s_first[e + 1] += s_first[e];
-        *n_groups = s_bad ? 0 : min(s_first[E], max_groups);
+        for (int e = 0; e < ecount; e++) s_first[e + 1] += s_first[e];
+        *n_groups = s_bad ? 0 : min(s_first[ecount], max_groups);
         if (s_bad) atomicCAS(err, 0, 3);
-        else if (s_first[E] > max_groups) atomicCAS(err, 0, 4);
+        else if (s_first[ecount] > max_groups) atomicCAS(err, 0, 4);
     }
     __syncthreads();
     if (s_bad) return;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    for (int e = threadIdx.x; e < ecount; e += blockDim.x) {
         int gi = s_first[e], n = 0;
         for (int s = 0; s < S; s++) {
-            if (idx[s] != e) continue;
+            if (idx[s] != ebase + e) continue;
             if (gi >= max_groups) break;
             grp_xrow[gi * 32 + n] = xidx ? xidx[s] : xrow_is_slot ? s : s / k;
             grp_orow[gi * 32 + n] = s;
@@ -127,13 +131,17 @@ __global__ void groups_kernel(const int32_t *__restrict__ idx, int S, int k, int
     }
 }
 
-__global__ void mix_kernel(const float *__restrict__ ys, const float *__restrict__ scores, int T, int k, int N,
+__global__ void mix_kernel(const float *__restrict__ ys, const float *__restrict__ scores,
+                           const int32_t *__restrict__ idx, int ebase, int ecount, int T, int k, int N,
                            void *__restrict__ y, int y_dtype) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * N) return;
     const int t = (int)(i / N), n = (int)(i - (int64_t)t * N);
     float v = 0.f;
-    for (int j = 0; j < k; j++) v = fmaf(scores[t * k + j], ys[((int64_t)t * k + j) * N + n], v);
+    for (int j = 0; j < k; j++) {
+        const int e = idx[t * k + j] - ebase;
+        if (e >= 0 && e < ecount) v = fmaf(scores[t * k + j], ys[((int64_t)t * k + j) * N + n], v);
+    }
     if (y_dtype == F32) reinterpret_cast<float *>(y)[i] = v;
     else if (y_dtype == BF16) reinterpret_cast<__nv_bfloat16 *>(y)[i] = __float2bfloat16_rn(v);
     else reinterpret_cast<__half *>(y)[i] = __float2half_rn(v);
@@ -150,19 +158,19 @@ cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int nor
     return cudaGetLastError();
 }
 
-cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int E, int xrow_is_slot, const int32_t *xidx,
-                              int gsize, int *n_groups, int *grp_expert, int *grp_count, int *grp_xrow,
-                              int *grp_orow, int max_groups, int *err, cudaStream_t st) {
-    groups_kernel<<<1, 1024, 0, st>>>(idx, S, k, E, xrow_is_slot, xidx, gsize, n_groups, grp_expert, grp_count,
-                                      grp_xrow, grp_orow, max_groups, err);
+cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int ebase, int ecount, int etotal, int xrow_is_slot,
+                              const int32_t *xidx, int gsize, int *n_groups, int *grp_expert, int *grp_count,
+                              int *grp_xrow, int *grp_orow, int max_groups, int *err, cudaStream_t st) {
+    groups_kernel<<<1, 1024, 0, st>>>(idx, S, k, ebase, ecount, etotal, xrow_is_slot, xidx, gsize, n_groups,
+                                      grp_expert, grp_count, grp_xrow, grp_orow, max_groups, err);
     return cudaGetLastError();
 }
 
-cudaError_t launch_moe_mix(const float *ys, const float *scores, int T, int k, int N, void *y, int y_dtype,
-                           cudaStream_t st) {
+cudaError_t launch_moe_mix(const float *ys, const float *scores, const int32_t *idx, int ebase, int ecount, int T,
+                           int k, int N, void *y, int y_dtype, cudaStream_t st) {
     const int64_t n = (int64_t)T * N;
     if (n == 0) return cudaSuccess;
-    mix_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ys, scores, T, k, N, y, y_dtype);
+    mix_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ys, scores, idx, ebase, ecount, T, k, N, y, y_dtype);
     return cudaGetLastError();
 }
 

@@ -39,6 +39,7 @@ from .synth import BLOCK_BYTES, CODECS, QK, codec_id
 __all__ = [
     "codecs", "codec_has_matmul", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
     "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
+    "moe_expert_layer_local",
 ]
 
 _DT = {torch.float32: _lib.KQ_F32, torch.float16: _lib.KQ_F16, torch.bfloat16: _lib.KQ_BF16}
@@ -364,3 +365,39 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, lhs_in
                                    e, n, wrs, wes, _p(y), _DT[od], _p(ws), ws.numel(), _stream(x.device)),
                    "gather_qmm")
     return y.reshape(*bshape, m, n)
+
+
+def moe_expert_layer_local(x: torch.Tensor, idx: torch.Tensor, scores: torch.Tensor, gate_w: torch.Tensor,
+                           up_w: torch.Tensor, down_w: torch.Tensor, codec_gu, codec_d, expert_base: int = 0,
+                           n_experts_total: int | None = None, act: str = "silu",
+                           out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """One expert-parallel rank's share of the routed expert layer (decode):
+    ``sum_j scores[t,j] * down(act(gate(x)) * up(x))`` over the slots routed to
+    the local experts ``[expert_base, expert_base + gate_w.shape[0])``; summed
+    over ranks it is the full layer (gmlx/moe_experts.py:250-266)."""
+    cg, cd = _cid(codec_gu), _cid(codec_d)
+    _need_cuda(x, idx, scores, gate_w, up_w, down_w)
+    d = _wire_k(gate_w, cg)
+    f = _wire_k(down_w, cd)
+    gate_w, grs, ges = _stack(gate_w)
+    up_w, urs, ues = _stack(up_w)
+    down_w, drs, des = _stack(down_w)
+    if (grs, ges) != (urs, ues) or gate_w.shape != up_w.shape:
+        raise ValueError("gate and up stacks must share shape and layout")
+    e_local = gate_w.shape[0]
+    e_total = n_experts_total if n_experts_total is not None else expert_base + e_local
+    x2 = _act_2d(x, d)
+    t = x2.shape[0]
+    i2 = _idx2d(idx, t)
+    k = i2.shape[1]
+    s2 = scores.reshape(t, k).float().contiguous()
+    od = out_dtype or x.dtype
+    y = torch.empty(t, down_w.shape[1], dtype=od, device=x.device)
+    if t:
+        L = _lib.load()
+        ws = _workspace(x.device, L.kq_moe_expert_layer_workspace_size(cg, cd, t, k, e_local, d, f, _DT[x2.dtype]))
+        _lib.check(L.kq_moe_expert_layer_local(cg, cd, _p(x2), _DT[x2.dtype], t, d, _p(i2), k, _p(s2), _p(gate_w),
+                                               _p(up_w), grs, ges, _p(down_w), drs, des, e_local, f, expert_base,
+                                               e_total, _lib.ACTS[act], _p(y), _DT[od], _p(ws), ws.numel(),
+                                               _stream(x.device)), "moe_expert_layer_local")
+    return y

@@ -1,0 +1,128 @@
+"""Tensor- and expert-parallel layers over the kq ops (one process per GPU,
+torch.distributed for the collectives: NCCL on B200s, gloo in CPU tests).
+
+Dense decoder layer: column-parallel q/k/v and gate/up
+(split the output rows -- wire rows are independent, so any row split is exact,
+gmlx/occupancy_fuse.py:32-34), row-parallel o and down (split K at whole
+256-weight-block granularity, i.e. a byte range of every wire row), one
+all-reduce of the partial sums after each row-parallel projection.  This is the
+shard_linear layout gmlx uses for hy_v3 (gmlx/hy_v3_model.py:396-443) with the
+all_sum of gmlx/hy_v3_model.py:259.
+
+MoE expert layer (e2): experts split by contiguous expert-id range; every rank
+routes the same tokens, runs the routed slots whose expert it owns, and the
+per-rank partial outputs are summed -- the sharding_group all_sum of
+gmlx/moe_experts.py:250-266.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .synth import BLOCK_BYTES, QK, codec_id
+
+
+def block_split(n_blocks: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous whole-block range [b0, b1) of rank `rank`."""
+    if n_blocks % world:
+        raise ValueError(f"{n_blocks} blocks do not split evenly over {world} ranks")
+    per = n_blocks // world
+    return rank * per, (rank + 1) * per
+
+
+def row_split(n_rows: int, world: int, rank: int) -> tuple[int, int]:
+    if n_rows % world:
+        raise ValueError(f"{n_rows} rows do not split evenly over {world} ranks")
+    per = n_rows // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_rows(w, world: int, rank: int):
+    """Column-parallel shard: this rank's output rows of a wire tensor [N, bytes]."""
+    r0, r1 = row_split(w.shape[0], world, rank)
+    return w[r0:r1]
+
+
+def shard_k(w, codec, world: int, rank: int):
+    """Row-parallel shard: this rank's whole-block K range of every wire row."""
+    bpb = BLOCK_BYTES[codec_id(codec)]
+    nb = w.shape[-1] // bpb
+    b0, b1 = block_split(nb, world, rank)
+    return w[..., b0 * bpb:b1 * bpb]
+
+
+def shard_llama_layer(full: dict, world: int, rank: int) -> dict:
+    """Shard a Llama-style layer dict (numpy or torch wire tensors):
+    q/k/v/gate/up by rows, o/down by K blocks.  Returns contiguous shards with a
+    fused q|k|v tensor."""
+    cat = np.concatenate if isinstance(full["q"], np.ndarray) else torch.cat
+
+    def c(t):
+        return np.ascontiguousarray(t) if isinstance(t, np.ndarray) else t.contiguous()
+    return {
+        "qkv": c(cat([shard_rows(full[n], world, rank) for n in ("q", "k", "v")], 0)),
+        "o": c(shard_k(full["o"], "q4_k", world, rank)),
+        "gate": c(shard_rows(full["gate"], world, rank)),
+        "up": c(shard_rows(full["up"], world, rank)),
+        "down": c(shard_k(full["down"], "q6_k", world, rank)),
+    }
+
+
+class TPDecoderMLP:
+    """The seven projections of one decoder layer on this rank's shards.
+
+    forward(x, attn_local) -> (qkv_local, o_full, y_full): qkv for this rank's
+    heads; o-proj of this rank's slice of the attention output, summed over
+    ranks; gate/up/SiLU on this rank's FFN slice and the down projection summed
+    over ranks.  (Attention itself is outside the quantized-matmul path.)"""
+
+    def __init__(self, shards: dict, group=None, codecs=("q4_k", "q6_k")):
+        self.s = shards
+        self.group = group
+        self.cg, self.cd = codecs
+
+    def forward(self, x, attn_local):
+        from . import kq
+        qkv = kq.quantized_matmul(x, self.s["qkv"], None, self.cg)
+        o = kq.quantized_matmul(attn_local, self.s["o"], None, self.cg, out_dtype=torch.float32)
+        h = kq.quantized_glu(x, self.s["gate"], self.s["up"], self.cg, act="silu")
+        y = kq.quantized_matmul(h, self.s["down"], None, self.cd, out_dtype=torch.float32)
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            dist.all_reduce(o, group=self.group)
+            dist.all_reduce(y, group=self.group)
+        return qkv, o, y
+
+
+def expert_range(n_experts: int, world: int, rank: int) -> tuple[int, int]:
+    return row_split(n_experts, world, rank)
+
+
+def ep_moe_forward(x, logits, top_k, gate_w, up_w, down_w, codec_gu, codec_d, expert_base, group=None,
+                   norm_topk_prob=True):
+    """Expert-parallel MoE layer (decode): route all tokens, run the slots whose
+    expert lies in [expert_base, expert_base + local experts), sum over ranks."""
+    from . import kq
+    idx, scores = kq.moe_router_topk(logits, top_k, norm_topk_prob)
+    y = kq.moe_expert_layer_local(x, idx, scores, gate_w, up_w, down_w, codec_gu, codec_d, expert_base)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(y, group=group)
+    return y
+
+
+def ep_partial_reference(x_f32: np.ndarray, idx: np.ndarray, scores: np.ndarray, expert_out, expert_base: int,
+                         n_local: int) -> np.ndarray:
+    """Host statement of one rank's share of the expert layer (tests): sum over
+    the routed slots whose expert is local of score * expert_out(e, x)."""
+    t, k = idx.shape
+    y = np.zeros((t, x_f32.shape[1]), np.float64)
+    for ti in range(t):
+        for j in range(k):
+            e = int(idx[ti, j])
+            if expert_base <= e < expert_base + n_local:
+                y[ti] += float(scores[ti, j]) * expert_out(e, x_f32[ti])
+    return y
+
+
+__all__ = ["block_split", "row_split", "shard_rows", "shard_k", "shard_llama_layer", "TPDecoderMLP",
+           "expert_range", "ep_moe_forward", "ep_partial_reference", "QK"]

@@ -153,6 +153,24 @@ int kq_gather_qmm(int codec, const void *x, int x_dtype, int64_t k, int64_t x_ro
  * inputs. */
 size_t kq_moe_workspace_size(int codec, int64_t slots, int64_t e, int64_t n, int64_t k_in);
 
+/* One expert-parallel rank's share of a routed MoE expert layer (decode), in
+ * one call: y[t] = sum over the slots j whose expert lies in this rank's
+ * range [expert_base, expert_base + e_local) of
+ *     scores[t][j] * down_e( act(gate_e(x[t])) * up_e(x[t]) ),
+ * with e = idx[t][j] - expert_base indexing the local stacks.  Summing y over
+ * the ranks (all-reduce) gives the full layer: the reference shards SwitchGLU
+ * experts this way and all_sums the result (gmlx/moe_experts.py:250-266;
+ * fused decode ops gmlx/modules.py:585-594).  idx holds global expert ids in
+ * [0, e_total).  y is [t][d] in y_dtype. */
+int kq_moe_expert_layer_local(int codec_gu, int codec_d, const void *x, int x_dtype, int64_t t, int64_t d,
+                              const int32_t *idx, int k, const float *scores, const void *gate_w, const void *up_w,
+                              int64_t gu_row_stride, int64_t gu_expert_stride, const void *down_w,
+                              int64_t d_row_stride, int64_t d_expert_stride, int64_t e_local, int64_t f,
+                              int64_t expert_base, int64_t e_total, int act, void *y, int y_dtype, void *workspace,
+                              size_t workspace_bytes, void *stream);
+size_t kq_moe_expert_layer_workspace_size(int codec_gu, int codec_d, int64_t t, int k, int64_t e_local, int64_t d,
+                                          int64_t f, int h_dtype);
+
 /* Size of the fixed scratch array behind kq_quantized_matmul_noalloc. */
 #define KQ_NOALLOC_SCRATCH_BYTES (4 << 20)
 

@@ -221,3 +221,51 @@ def test_prefill_gemm_tcgen05(cuda, codec, m, n, k):
     y16 = kq.quantized_matmul(to_dev_x(x, cuda, torch.float16), torch.from_numpy(w).to(cuda), None, codec)
     assert y16.dtype == torch.float16
     assert rel_err(y16.float().cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs")])
+def test_expert_parallel_partials_sum_to_full_layer(cuda, codec_gu, codec_d):
+    """Two expert-parallel 'ranks' (expert ranges) on one GPU: their partial
+    layers sum to the full routed layer, which matches the oracle."""
+    e, d, f, k, t = 16, 512, 256, 4, 3
+    wg, wu, wd, x, lg = _moe_case(codec_gu, codec_d, e, d, f, t, k, seed=80)
+    xd = to_dev_x(x, cuda)
+    idx, sc = kq.moe_router_topk(torch.from_numpy(lg).to(cuda), k, True)
+    tw = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    full = kq.moe_expert_layer_local(xd, idx, sc, tw(wg), tw(wu), tw(wd), codec_gu, codec_d, 0, e,
+                                     out_dtype=torch.float32)
+    parts = []
+    for r in range(2):
+        sl = slice(8 * r, 8 * r + 8)
+        parts.append(kq.moe_expert_layer_local(xd, idx, sc, tw(wg[sl]), tw(wu[sl]), tw(wd[sl]), codec_gu, codec_d,
+                                               8 * r, e, out_dtype=torch.float32))
+    assert rel_err((parts[0] + parts[1]).cpu().numpy(), full.cpu().numpy()) <= 1e-5
+    # oracle: f32 dequant-then-matmul per slot (h rounded to bf16 as the kernel does)
+    ii, ss = idx.cpu().numpy(), sc.cpu().numpy()
+    ref = np.zeros((t, d))
+    for ti in range(t):
+        for j in range(k):
+            ex = ii[ti, j]
+            g = O.matmul(x[ti:ti + 1], wg[ex], codec_gu)[0].astype(np.float64)
+            u = O.matmul(x[ti:ti + 1], wu[ex], codec_gu)[0].astype(np.float64)
+            hb = synth.f32_to_bf16_bits((g / (1 + np.exp(-g)) * u).astype(np.float32))[None]
+            ref[ti] += ss[ti, j] * O.matmul(hb, wd[ex], codec_d)[0]
+    assert rel_err(full.cpu().numpy(), ref) <= TOL
+
+
+def test_tensor_parallel_shards_sum_to_full(cuda):
+    """Row-parallel K shards (whole blocks, unaligned Q6_K byte offsets) of o and
+    down summed over 4 'ranks' equal the unsharded projection."""
+    from gmlx_b200 import parallel as par
+    for codec, n, k in [("q4_k", 256, 2048), ("q6_k", 256, 4096)]:
+        w = synth.random_weight(codec, n, k, seed=90)
+        x = synth.random_activations(2, k, seed=91)
+        full = kq.quantized_matmul(to_dev_x(x, cuda), torch.from_numpy(w).to(cuda), None, codec,
+                                   out_dtype=torch.float32)
+        acc = torch.zeros_like(full)
+        for r in range(4):
+            ws = par.shard_k(torch.from_numpy(w), codec, 4, r).contiguous().to(cuda)
+            kk = k // 4
+            acc += kq.quantized_matmul(to_dev_x(x[:, r * kk:(r + 1) * kk], cuda), ws, None, codec,
+                                       out_dtype=torch.float32)
+        assert rel_err(acc.cpu().numpy(), full.cpu().numpy()) <= 1e-4
