@@ -61,19 +61,22 @@ template <int C> constexpr int XSTR_OF = KB_OF<C> * QK * 2 + 64;  // staged acti
 constexpr int SMEM_BUDGET = 112 * 1024;  // per CTA: two CTAs per SM
 constexpr int S_MAX = 2048;              // Q4_K one-row sub-block sums table: K <= 65536
 
-template <int C> __host__ __device__ constexpr int spitch_of() {
+template <int C, bool DPL = false> __host__ __device__ constexpr int spitch_of() {
     // one row of a stage: KB blocks + 16 B slack for the granule offset;
-    // pitch == 32 (mod 128) spreads 8 rows x 32 B over all banks.
-    return ((((KB_OF<C> * Fmt<C>::bpb + 16 + 15) / 16 * 16) - 32 + 127) / 128) * 128 + 32;
+    // pitch == 32 (mod 128) spreads 8 rows x 32 B over all banks (MMA path);
+    // pitch == 16 (mod 128) spreads 8 lanes x 16 B of 8 rows (lane-per-row path).
+    return ((((KB_OF<C> * Fmt<C>::bpb + 16 + 15) / 16 * 16) - (DPL ? 16 : 32) + 127) / 128) * 128 + (DPL ? 16 : 32);
 }
 
 // XR: activation rows staged per stage with the weights (0 = read from global)
 template <int C, int NT, int XR> struct GLayout {
     static constexpr bool XS = XR > 0;
+    // lane-per-row integer dot-product path (one activation row, Q4_K)
+    static constexpr bool DP = XR == 1 && C == Q4_K;
     static constexpr int bpb = Fmt<C>::bpb;
     static constexpr int KB = KB_OF<C>;
     static constexpr int XSTR = XSTR_OF<C>;
-    static constexpr int SP = spitch_of<C>();
+    static constexpr int SP = spitch_of<C, DP>();
     static constexpr int WBYTES = TROWS * SP;
     static constexpr int STAGE = WBYTES + XR * XSTR;
     static constexpr int TABS = CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;
@@ -469,6 +472,100 @@ struct Block<IQ2_XXS, NT, F16, XS> {
 };
 
 // -------------------------------------------------------------------------
+// Lane-per-row Q4_K path for one activation row.  Each consumer warp owns one
+// super-block column of the stage; lane r owns tile row r.  The warp first
+// quantizes its 256 activation values to int16 with one f32 scale per 32
+// (relative error ~2^-16), then every lane dots its row's nibbles (as bytes)
+// against them with dp2a into int32, one sum per 32-weight sub-block, and
+// applies the block scales once per sub-block:
+//     acc += (d sc_j dx_j) * sum_j(q x_q) - (dmin m_j) * (dx_j * sum_j x_q).
+template <bool F16>
+__device__ __forceinline__ float dp_q4k_block(const uint8_t *row, const uint16_t *xs, uint32_t *xq, float *xsc) {
+    const int lane = threadIdx.x & 31, j = lane >> 2;
+    // -- quantize x[8*lane .. 8*lane+7] (sub-block j)
+    {
+        const uint4 v = *reinterpret_cast<const uint4 *>(xs + 8 * lane);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            if constexpr (F16) {
+                const float2 h = __half22float2(*reinterpret_cast<const __half2 *>(&w4[e]));
+                f[2 * e] = h.x;
+                f[2 * e + 1] = h.y;
+            } else {
+                f[2 * e] = __uint_as_float(w4[e] << 16);
+                f[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
+            }
+        }
+        float am = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) am = fmaxf(am, fabsf(f[e]));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        const float dx = am * (1.0f / 32767.0f), inv = am > 0.f ? 32767.0f / am : 0.f;
+        int qs = 0;
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int q0 = __float2int_rn(f[2 * e] * inv), q1 = __float2int_rn(f[2 * e + 1] * inv);
+            qs += q0 + q1;
+            pk[e] = (uint32_t)(q0 & 0xffff) | ((uint32_t)q1 << 16);
+        }
+        qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+        qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+        *reinterpret_cast<uint4 *>(xq + 4 * lane) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        if ((lane & 3) == 0) {
+            xsc[j] = dx;
+            xsc[8 + j] = dx * (float)qs;
+        }
+    }
+    __syncwarp();
+    // -- this lane's row
+    const uint4 hv = *reinterpret_cast<const uint4 *>(row);
+    const float d = half_bits_to_float(hv.x & 0xffffu), dmin = half_bits_to_float(hv.x >> 16);
+    uint32_t sc03, sc47, m03, m47;
+    q4k_unpack_scales(hv.y, hv.z, hv.w, sc03, sc47, m03, m47);
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint4 wa = *reinterpret_cast<const uint4 *>(row + 16 + 32 * c);
+        const uint4 wb = *reinterpret_cast<const uint4 *>(row + 32 + 32 * c);
+        const uint32_t w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        int sl = 0, sh = 0;
+#pragma unroll
+        for (int h4 = 0; h4 < 2; h4++) {
+            // x values of sub 2c (k = 64c + 16*h4 .. +15) and sub 2c+1 (+32)
+            const uint4 xl0 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 8 * h4);
+            const uint4 xl1 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 8 * h4 + 4);
+            const uint4 xh0 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 16 + 8 * h4);
+            const uint4 xh1 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 16 + 8 * h4 + 4);
+            const uint32_t xl[8] = {xl0.x, xl0.y, xl0.z, xl0.w, xl1.x, xl1.y, xl1.z, xl1.w};
+            const uint32_t xh[8] = {xh0.x, xh0.y, xh0.z, xh0.w, xh1.x, xh1.y, xh1.z, xh1.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t w = w8[4 * h4 + i];
+                const int lo = (int)(w & 0x0f0f0f0fu), hi = (int)((w >> 4) & 0x0f0f0f0fu);
+                sl = __dp2a_lo((int)xl[2 * i], lo, sl);
+                sl = __dp2a_hi((int)xl[2 * i + 1], lo, sl);
+                sh = __dp2a_lo((int)xh[2 * i], hi, sh);
+                sh = __dp2a_hi((int)xh[2 * i + 1], hi, sh);
+            }
+        }
+        const int j0 = 2 * c, j1 = 2 * c + 1;
+        const uint32_t scw = j0 < 4 ? sc03 : sc47, mw = j0 < 4 ? m03 : m47;
+        const float sc0 = (float)((scw >> (8 * (j0 & 3))) & 63u), sc1 = (float)((scw >> (8 * (j1 & 3))) & 63u);
+        const float m0 = (float)((mw >> (8 * (j0 & 3))) & 63u), m1 = (float)((mw >> (8 * (j1 & 3))) & 63u);
+        acc = fmaf(d * sc0 * xsc[j0], (float)sl, acc);
+        acc = fmaf(d * sc1 * xsc[j1], (float)sh, acc);
+        acc = fmaf(-dmin * m0, xsc[8 + j0], acc);
+        acc = fmaf(-dmin * m1, xsc[8 + j1], acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
+// -------------------------------------------------------------------------
 
 template <int C, int NT, bool F16, bool GLU, int XR>
 __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
@@ -572,7 +669,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     }
 
     // ---------------- consumer warps: warp -> (16-row half mt, block column col) ----------------
-    const int mt = warp & 1, col = warp >> 1;
+    // (lane-per-row path: warp -> block column, lane -> row)
+    constexpr bool DP = L::DP;
+    constexpr int RCOLS = DP ? KB : NCOL;                    // partial sums per row to reduce
+    constexpr int RCS = DP ? RED_TS : 8 * NT * RED_TS;       // their stride in the reduction buffer
+    const int mt = DP ? 0 : (warp & 1), col = DP ? warp : (warp >> 1);
     float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * GCfg<C>::TABW * BPW;
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
     uint32_t it = 0;
@@ -627,8 +728,15 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         for (int st = st0; i < end; st++, i++, it++) {
             const int slot = it % NS;
             wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2);
-            const int col0 = col * BPW, b = st * KB + col0;
-            if (b < nb && !*s_abort && !(a.debug & 1)) {
+            const int col0 = DP ? col : col * BPW, b = st * KB + col0;
+            if constexpr (DP) {
+                if (b < nb && !*s_abort && !(a.debug & 1)) {
+                    const uint8_t *stg = ring + slot * L::STAGE;
+                    const uint16_t *xs = reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK;
+                    acc[0][0] += dp_q4k_block<F16>(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, xs,
+                                                   reinterpret_cast<uint32_t *>(stab), stab + 128);
+                }
+            } else if (b < nb && !*s_abort && !(a.debug & 1)) {
                 const uint8_t *stg = ring + slot * L::STAGE;
                 const uint16_t *xr[NT];
 #pragma unroll
@@ -652,8 +760,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
 
-        // ---- reduce the 4 block columns: red[col][tok][row]
-        {
+        // ---- reduce the block columns: red[col][tok][row]
+        if constexpr (DP) {
+            red[col * RCS + lane] = acc[0][0];
+        } else {
             const int g = lane >> 2, t = lane & 3;
             float *r = red + col * 8 * NT * RED_TS;
 #pragma unroll
@@ -675,9 +785,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 if (n >= a.N) continue;
                 float v = 0.f, v2 = 0.f;
 #pragma unroll
-                for (int w = 0; w < NCOL; w++) {
-                    v += red[w * 8 * NT * RED_TS + tok * RED_TS + row];
-                    if (GLU) v2 += red[w * 8 * NT * RED_TS + tok * RED_TS + row + 16];
+                for (int w = 0; w < RCOLS; w++) {
+                    v += red[w * RCS + tok * RED_TS + row];
+                    if (GLU) v2 += red[w * RCS + tok * RED_TS + row + 16];
                 }
                 if (GLU) v = apply_act(a.act, v) * v2;
                 store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, tok) * a.y_row_stride + n, v);
@@ -690,7 +800,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 const int row = q & 31, tok = q >> 5;
                 float v = 0.f;
 #pragma unroll
-                for (int w = 0; w < NCOL; w++) v += red[w * 8 * NT * RED_TS + tok * RED_TS + row];
+                for (int w = 0; w < RCOLS; w++) v += red[w * RCS + tok * RED_TS + row];
                 __stcg(part + tok * 32 + row, v);
             }
             __threadfence();
