@@ -33,6 +33,7 @@
 //    act(gate)*up is formed in the epilogue without a second pass.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <stdlib.h>
 
 #include "kq_internal.cuh"
 #include "kq_ptx.cuh"
@@ -79,11 +80,13 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int SP = spitch_of<C, DP>();
     static constexpr int WBYTES = TROWS * SP;
     static constexpr int STAGE = WBYTES + XR * XSTR;
-    static constexpr int TABS = CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;
+    // scale tables (MMA path) or per-warp quantized activations (lane-per-row path)
+    static constexpr int TABS = DP ? CW * 640 : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;
+    static constexpr int DPB = DP ? 3 * KB * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 = 3)
     static constexpr bool SX = false;  // Q4_K one-row sums table (off: its per-launch prologue costs more than it saves)
     static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
     static constexpr int REDB = NCOL * 8 * NT * RED_TS * 4;  // one reduction buffer (two, alternating)
-    static constexpr int FIXED = 512 + (C == IQ2_XXS ? 4096 : 0) + TABS + SBYTES + 2 * REDB;
+    static constexpr int FIXED = 512 + (C == IQ2_XXS ? 4096 : 0) + TABS + SBYTES + 2 * REDB + DPB;
     static constexpr int NS_FIT = (SMEM_BUDGET - FIXED) / STAGE;
     static constexpr int NS = NS_FIT > 8 ? 8 : (NS_FIT < 2 ? 2 : NS_FIT);  // ring depth (<= 8: rowoff table)
     static constexpr int OFF_BAR = 0;                              // 2*NS mbarriers
@@ -94,7 +97,9 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int OFF_SCALE = OFF_RING + NS * STAGE;        // CW x TABW floats
     static constexpr int OFF_S = OFF_SCALE + TABS;
     static constexpr int OFF_RED = OFF_S + SBYTES;
-    static constexpr int BYTES = OFF_RED + 2 * REDB;
+    static constexpr int OFF_DPB = OFF_RED + 2 * REDB;
+    static constexpr int BYTES = OFF_DPB + DPB;
+    static_assert(!DP || NS == 2, "lane-per-row path sizes its partial buffers for NS = 2");
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -599,6 +604,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             mbar_init(&empty[i], CW);
         }
         *s_abort = 0;
+        for (int b = 0; b <= NS; b++) reinterpret_cast<int *>(smem + L::OFF_MISC + 16)[b] = 0;
         fence_mbar_init();
     }
     if constexpr (C == IQ2_XXS) {
@@ -651,7 +657,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
             const uint32_t off = (uint32_t)(src & 15);
             const uint32_t bytes = (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
-            const uint32_t xbytes = (XS && lane < T.m) ? (uint32_t)nbk * QK * 2 : 0u;
+            const uint32_t xbytes = (XS && lane < T.m && !(a.debug & 8)) ? (uint32_t)nbk * QK * 2 : 0u;
             rowoff[slot * 32 + lane] = (uint8_t)off;
             uint32_t total = bytes + xbytes;
 #pragma unroll
@@ -660,7 +666,16 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             __syncwarp();
             if (!*s_abort) {
                 uint8_t *stg = ring + slot * L::STAGE;
-                if (bytes) bulk_g2s(stg + lane * L::SP, (const void *)(src - off), bytes, &full[slot], pol);
+                if (bytes) {
+                    if (a.debug & 4)
+                        asm volatile(
+                            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                                smem_u32(stg + lane * L::SP)),
+                            "l"((const void *)(src - off)), "r"(bytes), "r"(smem_u32(&full[slot]))
+                            : "memory");
+                    else
+                        bulk_g2s(stg + lane * L::SP, (const void *)(src - off), bytes, &full[slot], pol);
+                }
                 if (xbytes)
                     bulk_g2s(stg + L::WBYTES + lane * XSTR, xsrc + (int64_t)bs * QK * 2, xbytes, &full[slot], pol_x);
             }
@@ -678,7 +693,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
     uint32_t it = 0;
     int64_t i = lo;
-    int rp = 0, s_group = -1;
+    int rp = 0, s_group = -1, tix = 0;
+    int *dcnt = const_cast<int *>(reinterpret_cast<volatile int *>(smem + L::OFF_MISC + 16));  // NS+1 tile counters
     while (i < hi) {
         const int64_t gt = i / nst;
         const int st0 = (int)(i - gt * nst);
@@ -760,6 +776,43 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
 
+        if (a.debug & 32) continue;  // development: skip the epilogue
+        const bool whole = tile_lo >= lo && tile_hi <= hi;
+        if constexpr (DP) {
+            if (whole) {
+                // barrier-free: each warp posts its 32 row partials; the last of
+                // the KB warps to arrive sums them in column order and stores.
+                // Buffers rotate over NS+1 tiles, which the ring keeps apart.
+                const int bi = tix % (NS + 1);
+                float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (KB * 32);
+                rb[col * 32 + lane] = acc[0][0];
+                __syncwarp();
+                int old = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    old = atomicAdd(dcnt + bi, 1);
+                }
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == KB - 1) {
+                    __threadfence_block();
+                    const int row = GLU ? (lane & 15) : lane;
+                    const int n = T.tile * rows_out + row;
+                    float v = 0.f, v2 = 0.f;
+#pragma unroll
+                    for (int w = 0; w < KB; w++) {
+                        v += rb[w * 32 + row];
+                        if (GLU) v2 += rb[w * 32 + row + 16];
+                    }
+                    if (GLU) v = apply_act(a.act, v) * v2;
+                    if (n < a.N && (!GLU || lane < 16)) store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
+                    __syncwarp();
+                    if (lane == 0) dcnt[bi] = 0;
+                }
+                tix++;
+                continue;
+            }
+            tix++;
+        }
         // ---- reduce the block columns: red[col][tok][row]
         if constexpr (DP) {
             red[col * RCS + lane] = acc[0][0];
@@ -777,7 +830,6 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         }
         named_bar_sync(1, CW * 32);
         const int m = T.m;
-        const bool whole = tile_lo >= lo && tile_hi <= hi;
         if (whole) {
             for (int q = ctid; q < rows_out * m; q += CW * 32) {
                 const int row = q % rows_out, tok = q / rows_out;
@@ -803,16 +855,19 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 for (int w = 0; w < RCOLS; w++) v += red[w * RCS + tok * RED_TS + row];
                 __stcg(part + tok * 32 + row, v);
             }
-            __threadfence();
+            // publish: CTA barrier, then one thread orders the CTA's partial
+            // stores before its counter increment (gpu-scope fence)
             named_bar_sync(1, CW * 32);
             const int64_t c0 = cta_of(tile_lo, I, P), c1 = cta_of(tile_hi - 1, I, P);
             if (ctid == 0) {
+                __threadfence();
                 const int old = atomicAdd(a.counters + gt, 1);
-                *s_last = (old == (int)(c1 - c0));
+                const int last = (old == (int)(c1 - c0));
+                if (last) __threadfence();  // acquire the other contributors' partials
+                *s_last = last;
             }
             named_bar_sync(1, CW * 32);
             if (*s_last) {
-                __threadfence();
                 for (int q = ctid; q < rows_out * m; q += CW * 32) {
                     const int row = q % rows_out, tok = q / rows_out;
                     const int n = T.tile * rows_out + row;
@@ -857,7 +912,8 @@ int grid_for(const GemvArgs &a) {
     const long groups = a.dense_m > 0 ? (a.dense_m + 31) / 32 : a.max_groups;
     const long nst = (a.K / QK + L::KB - 1) / L::KB;
     const long iters = groups * tiles * nst;
-    const long cap = (long)num_sms() * per_sm;
+    long cap = (long)num_sms() * per_sm;
+    if (const char *g = getenv("KQ_GEMV_GRID")) cap = atol(g);  // development override
     return (int)(iters < cap ? iters : cap);
 }
 
