@@ -73,7 +73,7 @@ template <int C, bool DPL = false> __host__ __device__ constexpr int spitch_of()
 template <int C, int NT, int XR> struct GLayout {
     static constexpr bool XS = XR > 0;
     // lane-per-row integer dot-product path (one activation row, Q4_K)
-    static constexpr bool DP = XR == 1 && C == Q4_K;
+    static constexpr bool DP = XR == 1 && (C == Q4_K || C == Q6_K);
     static constexpr int bpb = Fmt<C>::bpb;
     static constexpr int KB = KB_OF<C>;
     static constexpr int XSTR = XSTR_OF<C>;
@@ -82,7 +82,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int STAGE = WBYTES + XR * XSTR;
     // scale tables (MMA path) or per-warp quantized activations (lane-per-row path)
     static constexpr int TABS = DP ? CW * 640 : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;
-    static constexpr int DPB = DP ? 3 * KB * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 = 3)
+    static constexpr int DPB = DP ? 4 * KB * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 <= 4)
     static constexpr bool SX = false;  // Q4_K one-row sums table (off: its per-launch prologue costs more than it saves)
     static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
     static constexpr int REDB = NCOL * 8 * NT * RED_TS * 4;  // one reduction buffer (two, alternating)
@@ -99,7 +99,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int OFF_RED = OFF_S + SBYTES;
     static constexpr int OFF_DPB = OFF_RED + 2 * REDB;
     static constexpr int BYTES = OFF_DPB + DPB;
-    static_assert(!DP || NS == 2, "lane-per-row path sizes its partial buffers for NS = 2");
+    static_assert(!DP || NS <= 3, "lane-per-row path sizes its partial buffers for NS <= 3");
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -484,10 +484,11 @@ struct Block<IQ2_XXS, NT, F16, XS> {
 // against them with dp2a into int32, one sum per 32-weight sub-block, and
 // applies the block scales once per sub-block:
 //     acc += (d sc_j dx_j) * sum_j(q x_q) - (dmin m_j) * (dx_j * sum_j x_q).
+// Quantize the warp's 256 activations: xq = int16 values, one f32 scale per
+// 32 (xsc[0..7]), dx*sum per 32 (xsc[8..15]) and per 16 (xsc[16..31]).
 template <bool F16>
-__device__ __forceinline__ float dp_q4k_block(const uint8_t *row, const uint16_t *xs, uint32_t *xq, float *xsc) {
+__device__ __forceinline__ void dp_quantize(const uint16_t *xs, uint32_t *xq, float *xsc) {
     const int lane = threadIdx.x & 31, j = lane >> 2;
-    // -- quantize x[8*lane .. 8*lane+7] (sub-block j)
     {
         const uint4 v = *reinterpret_cast<const uint4 *>(xs + 8 * lane);
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
@@ -517,15 +518,21 @@ __device__ __forceinline__ float dp_q4k_block(const uint8_t *row, const uint16_t
             qs += q0 + q1;
             pk[e] = (uint32_t)(q0 & 0xffff) | ((uint32_t)q1 << 16);
         }
-        qs += __shfl_xor_sync(0xffffffffu, qs, 1);
-        qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+        const int q16 = qs + __shfl_xor_sync(0xffffffffu, qs, 1);
+        const int q32 = q16 + __shfl_xor_sync(0xffffffffu, q16, 2);
         *reinterpret_cast<uint4 *>(xq + 4 * lane) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         if ((lane & 3) == 0) {
             xsc[j] = dx;
-            xsc[8 + j] = dx * (float)qs;
+            xsc[8 + j] = dx * (float)q32;
         }
+        if ((lane & 1) == 0) xsc[16 + (lane >> 1)] = dx * (float)q16;
     }
     __syncwarp();
+}
+
+template <bool F16>
+__device__ __forceinline__ float dp_q4k_block(const uint8_t *row, const uint16_t *xs, uint32_t *xq, float *xsc) {
+    dp_quantize<F16>(xs, xq, xsc);
     // -- this lane's row
     const uint4 hv = *reinterpret_cast<const uint4 *>(row);
     const float d = half_bits_to_float(hv.x & 0xffffu), dmin = half_bits_to_float(hv.x >> 16);
@@ -565,6 +572,57 @@ __device__ __forceinline__ float dp_q4k_block(const uint8_t *row, const uint16_t
         acc = fmaf(d * sc1 * xsc[j1], (float)sh, acc);
         acc = fmaf(-dmin * m0, xsc[8 + j0], acc);
         acc = fmaf(-dmin * m1, xsc[8 + j1], acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
+// Lane-per-row Q6_K: lanes 0-15 / 16-31 of a warp take the two 128-weight
+// halves of rows row0..row0+15 of one block.  q6 = ql nibble | qh pair << 4 is
+// dotted unsigned with dp2a; the -32 offset is applied as -32 * sum(x) per
+// 16-weight sub-block.  Rows are only 2-byte aligned (210-byte blocks), so
+// words are assembled from aligned loads with funnel shifts.
+__device__ __forceinline__ uint32_t lds_w2(const uint32_t *base, int i, uint32_t sh) {
+    return __funnelshift_r(base[i], base[i + 1], sh);
+}
+
+template <bool F16>
+__device__ __forceinline__ float dp_q6k_half(const uint8_t *blk, int hf, const uint16_t *xs, uint32_t *xq, float *xsc) {
+    dp_quantize<F16>(xs, xq, xsc);
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    uint32_t ql[16], qh[8];
+#pragma unroll
+    for (int i = 0; i < 16; i++) ql[i] = lds_w2(aw, 16 * hf + i, sh);       // bytes 64hf .. 64hf+63
+#pragma unroll
+    for (int i = 0; i < 8; i++) qh[i] = lds_w2(aw, 32 + 8 * hf + i, sh);    // bytes 128+32hf ..
+    const uint32_t scw0 = lds_w2(aw, 48 + 2 * hf, sh), scw1 = lds_w2(aw, 49 + 2 * hf, sh);  // int8 scales 8hf..8hf+7
+    const float d = half_bits_to_float(lds_w2(aw, 52, sh) & 0xffffu);       // bytes 208-209
+    float acc = 0.f;
+#pragma unroll
+    for (int s4 = 0; s4 < 4; s4++) {
+        const int ns = 4 * (s4 >> 1);
+        int sm[2] = {0, 0};  // the two 16-weight sub-blocks of this 32-weight group
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t lw = ql[8 * (s4 & 1) + i] >> ns;
+            const uint32_t hw = s4 == 0 ? (qh[i] << 4) : s4 == 1 ? (qh[i] << 2) : s4 == 2 ? qh[i] : (qh[i] >> 2);
+            const int q6 = (int)lop_and_or(hw, 0x30303030u, lw & 0x0f0f0f0fu);
+            // weights 128hf + 32 s4 + 4i .. +3  <-> x words (64 s4 + 8i)/2 of the block-half
+            const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 64 * hf + 16 * s4 + 2 * i);
+            int &acc_i = sm[i >> 2];
+            acc_i = __dp2a_lo((int)xv.x, q6, acc_i);
+            acc_i = __dp2a_hi((int)xv.y, q6, acc_i);
+        }
+        const int g32 = 4 * hf + s4;  // x quantization group of these 32 weights
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int j = 2 * s4 + u;  // sub-block within the half (scale 8hf + j)
+            const uint32_t scw = j < 4 ? scw0 : scw1;
+            const float sc = (float)(int)(int8_t)((scw >> (8 * (j & 3))) & 255u);
+            acc = fmaf(d * sc, fmaf(xsc[g32], (float)sm[u], -32.f * xsc[16 + 2 * g32 + u]), acc);
+        }
     }
     __syncwarp();  // xq is rewritten for the next block
     return acc;
@@ -688,7 +746,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     constexpr bool DP = L::DP;
     constexpr int RCOLS = DP ? KB : NCOL;                    // partial sums per row to reduce
     constexpr int RCS = DP ? RED_TS : 8 * NT * RED_TS;       // their stride in the reduction buffer
-    const int mt = DP ? 0 : (warp & 1), col = DP ? warp : (warp >> 1);
+    // Q4_K lane-per-row: warp = block column, lane = row.  Q6_K: warp =
+    // (block column warp&3, 16-row half warp>>2), half-warp = block half.
+    const int mt = (DP && C == Q4_K) ? 0 : (warp & 1), col = (DP && C == Q4_K) ? warp : (DP ? (warp & 3) : (warp >> 1));
     float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * GCfg<C>::TABW * BPW;
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
     uint32_t it = 0;
@@ -749,8 +809,14 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 if (b < nb && !*s_abort && !(a.debug & 1)) {
                     const uint8_t *stg = ring + slot * L::STAGE;
                     const uint16_t *xs = reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK;
-                    acc[0][0] += dp_q4k_block<F16>(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, xs,
-                                                   reinterpret_cast<uint32_t *>(stab), stab + 128);
+                    if constexpr (C == Q4_K) {
+                        acc[0][0] += dp_q4k_block<F16>(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, xs,
+                                                       reinterpret_cast<uint32_t *>(stab), stab + 128);
+                    } else {
+                        const int r = 16 * (warp >> 2) + (lane & 15);
+                        acc[0][0] += dp_q6k_half<F16>(stg + r * L::SP + rowoff[slot * 32 + r] + col * bpb, lane >> 4,
+                                                      xs, reinterpret_cast<uint32_t *>(stab), stab + 128);
+                    }
                 }
             } else if (b < nb && !*s_abort && !(a.debug & 1)) {
                 const uint8_t *stg = ring + slot * L::STAGE;
@@ -785,7 +851,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 // Buffers rotate over NS+1 tiles, which the ring keeps apart.
                 const int bi = tix % (NS + 1);
                 float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (KB * 32);
-                rb[col * 32 + lane] = acc[0][0];
+                if constexpr (C == Q4_K) {
+                    rb[col * 32 + lane] = acc[0][0];
+                } else {
+                    const float v = acc[0][0] + __shfl_xor_sync(0xffffffffu, acc[0][0], 16);  // both block halves
+                    if (lane < 16) rb[col * 32 + 16 * (warp >> 2) + lane] = v;
+                }
                 __syncwarp();
                 int old = 0;
                 if (lane == 0) {
@@ -793,7 +864,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                     old = atomicAdd(dcnt + bi, 1);
                 }
                 old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == KB - 1) {
+                if (old == CW - 1) {
                     __threadfence_block();
                     const int row = GLU ? (lane & 15) : lane;
                     const int n = T.tile * rows_out + row;
@@ -814,8 +885,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             tix++;
         }
         // ---- reduce the block columns: red[col][tok][row]
-        if constexpr (DP) {
+        if constexpr (DP && C == Q4_K) {
             red[col * RCS + lane] = acc[0][0];
+        } else if constexpr (DP) {
+            const float v = acc[0][0] + __shfl_xor_sync(0xffffffffu, acc[0][0], 16);
+            if (lane < 16) red[col * RCS + 16 * (warp >> 2) + lane] = v;
         } else {
             const int g = lane >> 2, t = lane & 3;
             float *r = red + col * 8 * NT * RED_TS;
