@@ -684,6 +684,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         }
     }
     __syncthreads();
+    // programmatic dependent launch: let the next kernel on the stream start
+    // its prologue now; weights are read-only, so only activation reads and
+    // global writes below wait for the previous kernel (griddepcontrol.wait)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (lo >= hi) return;
 
     if (warp == CW) {
@@ -695,6 +699,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         const uint8_t *base = nullptr;
         bool valid = false;
         const uint8_t *xsrc = nullptr;
+        bool dep_done = false;
         for (int64_t i = lo; i < hi; i++, it++) {
             const int64_t gt = i / nst;
             const int st = (int)(i - gt * nst);
@@ -734,6 +739,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                     else
                         bulk_g2s(stg + lane * L::SP, (const void *)(src - off), bytes, &full[slot], pol);
                 }
+                if (!dep_done) {  // the first weight copies are in flight; activations may be the
+                    asm volatile("griddepcontrol.wait;" ::: "memory");  // previous kernel's output
+                    dep_done = true;
+                }
                 if (xbytes)
                     bulk_g2s(stg + L::WBYTES + lane * XSTR, xsrc + (int64_t)bs * QK * 2, xbytes, &full[slot], pol_x);
             }
@@ -751,6 +760,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     const int mt = (DP && C == Q4_K) ? 0 : (warp & 1), col = (DP && C == Q4_K) ? warp : (DP ? (warp & 3) : (warp >> 1));
     float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * GCfg<C>::TABW * BPW;
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
+    if (!XS) asm volatile("griddepcontrol.wait;" ::: "memory");  // MMA B operands read global activations
     uint32_t it = 0;
     int64_t i = lo;
     int rp = 0, s_group = -1, tix = 0;
@@ -843,6 +853,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         }
 
         if (a.debug & 32) continue;  // development: skip the epilogue
+        if (XS) asm volatile("griddepcontrol.wait;" ::: "memory");  // before the first global write
         const bool whole = tile_lo >= lo && tile_hi <= hi;
         if constexpr (DP) {
             if (whole) {
@@ -1002,8 +1013,17 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
         return cudaSuccess;
     }
     if (grid <= 0) return cudaSuccess;
-    gemv_kernel<C, NT, F16, GLU, XR><<<grid, NTHREADS, L::BYTES, st>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = L::BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<C, NT, F16, GLU, XR>, a);
 }
 
 template <int C, bool F16, bool GLU>

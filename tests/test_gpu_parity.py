@@ -187,26 +187,40 @@ def test_golden_vectors_on_gpu(cuda, codec):
 
 
 def test_nn_modules_fused_and_stock_paths_agree(cuda):
+    """KQuantSwitchGLU's fused decode path and its stock gather path both match
+    the oracle (each output is bf16, so each is checked against f64 separately)."""
     from gmlx_b200 import nn as knn
     e, d, f, k, t = 8, 512, 256, 2, 3
+    wg = synth.random_weight("q4_k", f, d, seed=1, experts=e)
+    wu = synth.random_weight("q4_k", f, d, seed=2, experts=e)
+    wd = synth.random_weight("q6_k", d, f, seed=3, experts=e)
     m = knn.KQuantSwitchGLU(d, f, e, "q4_k", "q6_k", device=cuda)
-    m.gate_proj.weight.copy_(torch.from_numpy(synth.random_weight("q4_k", f, d, seed=1, experts=e)))
-    m.up_proj.weight.copy_(torch.from_numpy(synth.random_weight("q4_k", f, d, seed=2, experts=e)))
-    m.down_proj.weight.copy_(torch.from_numpy(synth.random_weight("q6_k", d, f, seed=3, experts=e)))
-    x = torch.randn(t, d, device=cuda).to(torch.bfloat16)
-    idx, sc = kq.moe_router_topk(torch.randn(t, e, device=cuda), k, True)
-    y_fused = m(x, idx, sc).float()
-    # stock path (forced by a 64-slot index tensor) on the same routing
-    xs = x.repeat(32, 1)
-    ids = idx.repeat(32, 1)
-    y_stock = m(xs, ids, sc.repeat(32, 1))[:t].float()
-    assert rel_err(y_fused.cpu().numpy(), y_stock.cpu().numpy()) <= TOL
+    m.gate_proj.weight.copy_(torch.from_numpy(wg))
+    m.up_proj.weight.copy_(torch.from_numpy(wu))
+    m.down_proj.weight.copy_(torch.from_numpy(wd))
+    xb = synth.random_activations(t, d, seed=4)
+    x = to_dev_x(xb, cuda)
+    idx, sc = kq.moe_router_topk(torch.from_numpy(synth.random_logits(t, e, seed=5)).to(cuda), k, True)
+    y_fused = m(x, idx, sc).float().cpu().numpy()
+    y_stock = m(x.repeat(32, 1), idx.repeat(32, 1), sc.repeat(32, 1))[:t].float().cpu().numpy()  # >= 64 slots
+    ii, ss = idx.cpu().numpy(), sc.cpu().numpy()
+    ref = np.zeros((t, d))
+    for ti in range(t):
+        for j in range(k):
+            ex = ii[ti, j]
+            g = O.matmul(xb[ti:ti + 1], wg[ex], "q4_k")[0].astype(np.float64)
+            u = O.matmul(xb[ti:ti + 1], wu[ex], "q4_k")[0].astype(np.float64)
+            hb = synth.f32_to_bf16_bits((g / (1 + np.exp(-g)) * u).astype(np.float32))[None]
+            ref[ti] += ss[ti, j] * O.matmul(hb, wd[ex], "q6_k")[0]
+    assert rel_err(y_fused, ref) <= TOL
+    assert rel_err(y_stock, ref) <= TOL
     lin = knn.KQuantLinear(d, 128, True, "iq2_xxs", device=cuda)
     lin.weight.copy_(torch.from_numpy(synth.random_weight("iq2_xxs", 128, d, seed=4)))
     lin.bias.fill_(0.5)
-    xb = synth.random_activations(2, d, seed=5)
-    ref = O.matmul(xb, lin.weight.cpu().numpy(), "iq2_xxs") + 0.5
-    assert rel_err(lin(to_dev_x(xb, cuda)).float().cpu().numpy(), ref) <= TOL
+    xl = synth.random_activations(2, d, seed=5)
+    refl = O.matmul(xl, lin.weight.cpu().numpy(), "iq2_xxs") + 0.5
+    assert rel_err(lin(to_dev_x(xl, cuda)).float().cpu().numpy(), refl) <= TOL
+
 
 
 @pytest.mark.parametrize("codec", CODECS)
