@@ -181,7 +181,7 @@ def time_graph(torch, fn, steps, warmup, stream, min_warm_s=0.0):
 
 MOE_CONFIGS = (
     # (name, experts, top_k, hidden, ffn, gate/up codec, down codec, token counts)
-    ("qwen3-30b-a3b-like", 128, 8, 2048, 768, "q4_k", "q6_k", (1, 64)),
+    ("qwen3-30b-a3b-like", 128, 8, 2048, 768, "q4_k", "q6_k", (1, 64, 4096)),
     ("deepseek-v3-like-iq2", 256, 8, 7168, 2048, "iq2_xxs", "iq2_xxs", (1, 8, 64)),
 )
 
@@ -222,7 +222,8 @@ def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
             secs = float(tt.item())
             gbs = uniq * ebytes / secs / 1e9
             cell[f"t{t}"] = {"ms": secs * 1e3, "unique_experts": uniq, "GB/s": gbs,
-                             "frac_hbm_per_gpu": gbs / world / hbm_peak}
+                             "frac_hbm_per_gpu": gbs / world / hbm_peak,
+                             "TFLOP/s": 2.0 * t * K * 3 * D * F / secs / 1e12}
         out[name] = cell
         del wg, wu, wd
         torch.cuda.empty_cache()
@@ -384,20 +385,21 @@ def main():
     prefill = {}
     if not args.no_sweep:
         L0 = layers[0]
-        gu = torch.cat([L0["gate"], L0["up"]], 0)
-        mats = [(L0["qkv"], "q4_k", 4096), (L0["o"], "q4_k", 4096), (gu, "q4_k", 4096), (L0["down"], "q6_k", 14336)]
+        mats = [(L0["qkv"], "q4_k", 4096), (L0["o"], "q4_k", 4096), (L0["gate"], "q4_k", 4096),
+                (L0["up"], "q4_k", 4096), (L0["down"], "q6_k", 14336)]
         flops_per_tok = sum(2 * w.shape[0] * k for w, _, k in mats)
         for m in (512, 2048, 8192):
             xs = {k: torch.randn(m, k, device=dev).to(torch.bfloat16) for k in (4096, 14336)}
 
-            def pf():
-                for w, c, k in mats:
-                    kq.quantized_matmul(xs[k], w, None, c)
+            def pf():  # gate/up/SiLU*up fused in one tcgen05 GEMM (two accumulators per tile)
+                kq.quantized_matmul(xs[4096], L0["qkv"], None, "q4_k")
+                kq.quantized_matmul(xs[4096], L0["o"], None, "q4_k")
+                kq.quantized_glu(xs[4096], L0["gate"], L0["up"], "q4_k", act="silu")
+                kq.quantized_matmul(xs[14336], L0["down"], None, "q6_k")
             reps = 3 if m == 8192 else 6
             t = time_graph(torch, pf, reps, 1, stream) / reps
             prefill[f"m{m}"] = {"ms": t * 1e3, "TFLOP/s": flops_per_tok * m / t / 1e12,
                                 "frac_tensor": flops_per_tok * m / t / 1e12 / tc_peak}
-        del gu
 
     moe = {} if args.no_moe else run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak)
 

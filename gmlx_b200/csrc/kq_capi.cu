@@ -6,6 +6,7 @@
 // failures of the reference's module swap (unknown codec -> error,
 // gmlx/modules.py:1561-1574; geometry rules gmlx/modules.py:502-509).
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -121,10 +122,10 @@ GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k,
     return a;
 }
 
-bool use_gemm(int64_t m, int act) { return act == ACT_NONE && m >= GEMM_MIN_M; }
+bool use_gemm(int64_t m) { return m >= GEMM_MIN_M; }
 
 size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
-    if (use_gemm(m, act)) return plan(0, gemm_scratch_bytes(codec, n, k), 0, 0).total;
+    if (use_gemm(m)) return plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0).total;
     GemvArgs a = dense_args(codec, nullptr, KQ_BF16, m, k, k, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
@@ -142,8 +143,8 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
     if (m < 0 || n <= 0 || xs < k || ys < n) return fail(KQ_ERR_SHAPE, "%s: bad sizes m=%lld n=%lld", what, (long long)m, (long long)n);
     if (m == 0) return KQ_OK;
     if (n > 0x7fffffff || k > 0x7fffffff) return fail(KQ_ERR_SHAPE, "%s: n/k too large", what);
-    if (use_gemm(m, act) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
-        const WsPlan p = plan(0, gemm_scratch_bytes(codec, n, k), 0, 0);
+    if (use_gemm(m) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
+        const WsPlan p = plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0);
         if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
             return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
         GemmArgs g{};
@@ -156,6 +157,8 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
         g.x_row_stride = xs;
         g.w = (const uint8_t *)w;
         g.w_row_stride = wstride;
+        g.w2 = (const uint8_t *)w2;
+        g.act = w2 ? act : ACT_NONE;
         g.y = y;
         g.y_dtype = y_dtype;
         g.y_row_stride = ys;
@@ -175,6 +178,126 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
     return cuda_status(launch_gemv(a, (cudaStream_t)stream), what);
 }
 
+// Grouped tensor-core path for routed calls with many rows per expert (MoE
+// prefill): sort the slots by local expert, gather their activation rows
+// contiguously, run one tcgen05 GEMM over a device table of (expert, 128-row
+// tile) -- every expert's weights stream once per 256 output columns instead of
+// once per 8 rows -- and scatter the outputs back to slot order.
+constexpr size_t GROUPED_B_CHUNK = (size_t)1 << 30;  // dequantized-expert scratch per launch (non-Q4_K codecs)
+
+bool use_grouped(int codec, int64_t slots, int64_t etotal, int64_t n, int64_t kin, int act, bool glu, int x_dtype,
+                 int64_t xs) {
+    if (act != ACT_NONE && !glu) return false;
+    if (n % 4 || n > 0x7fffffff || kin > 0x7fffffff) return false;
+    if (slots < (int64_t)GEMM_MIN_M * etotal) return false;  // fewer than ~33 rows per expert: GEMV
+    return gemm_supported(codec, slots, n, kin, x_dtype, xs);
+}
+
+struct GroupedPlan {
+    size_t perm_off, scr_off, misc_off, tiles_off, xs_off, g_off, b_off, total;
+    int max_tiles, chunk_e, mt;
+};
+
+GroupedPlan grouped_plan(int codec, int64_t slots, int64_t e, int64_t etotal, int64_t n, int64_t kin, bool glu,
+                         bool f32_out) {
+    GroupedPlan g;
+    // 256-row tiles (two accumulators per CTA) once experts average >= 192 rows
+    g.mt = slots >= 192 * etotal ? 2 : 1;
+    g.max_tiles = (int)(slots / (128 * g.mt) + (slots < e ? slots : e) + 1);
+    const size_t per_e = (size_t)n * kin * 2 * (glu ? 2 : 1);
+    g.chunk_e = codec == KQ_Q4_K ? (int)e : (int)std::max<int64_t>(1, std::min<int64_t>(e, GROUPED_B_CHUNK / per_e));
+    size_t o = 256 + CNT_RESERVE;
+    g.perm_off = o;
+    o = align256(o + (size_t)slots * sizeof(int));
+    g.scr_off = o;
+    o = align256(o + (size_t)(slots + e) * sizeof(int));
+    g.misc_off = o;
+    o = align256(o + 2 * sizeof(int));
+    g.tiles_off = o;
+    o = align256(o + (size_t)g.max_tiles * 3 * sizeof(int));
+    g.xs_off = o;
+    o = align256(o + (size_t)slots * kin * 2);
+    g.g_off = o;
+    if (f32_out) o = align256(o + (size_t)slots * n * sizeof(float));
+    g.b_off = o;
+    if (codec != KQ_Q4_K) o = align256(o + (size_t)g.chunk_e * per_e);
+    g.total = o;
+    return g;
+}
+
+int run_grouped(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, int64_t slots, int kslot,
+                int64_t tokens, const int32_t *idx, const int32_t *xidx, int mode, const void *w, const void *w2,
+                int64_t e, int64_t n, int64_t wrs, int64_t wes, int act, void *y, int y_dtype, int64_t yrs,
+                const float *scores, void *ws, size_t ws_bytes, void *stream, const char *what, int64_t ebase,
+                int64_t etotal) {
+    const bool glu = w2 != nullptr;
+    const GroupedPlan p = grouped_plan(codec, slots, e, etotal, n, kin, glu, scores != nullptr);
+    if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
+        return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
+    char *base = (char *)ws;
+    int *err = (int *)base;
+    int *cnt = (int *)(base + 256);  // zero on entry, left zero (counter region)
+    int *perm = (int *)(base + p.perm_off), *scr = (int *)(base + p.scr_off);
+    int *count = (int *)(base + p.misc_off), *ntiles = count + 1;
+    int *te = (int *)(base + p.tiles_off), *tr0 = te + p.max_tiles, *tre = tr0 + p.max_tiles;
+    void *xsorted = base + p.xs_off;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t ce = launch_moe_sort(idx, (int)slots, kslot, (int)ebase, (int)e, (int)etotal, mode == 1, xidx, x, xs,
+                                     (int)kin, xsorted, 128 * p.mt, cnt, scr, perm, count, ntiles, te, tr0, tre,
+                                     p.max_tiles, err, st);
+    if (ce != cudaSuccess) return cuda_status(ce, what);
+    GemmArgs g{};
+    g.codec = codec;
+    g.M = (int)slots;
+    g.N = (int)n;
+    g.K = (int)kin;
+    g.x = xsorted;
+    g.x_dtype = x_dtype;
+    g.x_row_stride = kin;
+    g.w_row_stride = wrs;
+    g.w_expert_stride = wes;
+    g.n_per_expert = (int)n;
+    g.err = err;
+    g.n_tiles = ntiles;
+    g.tile_e = te;
+    g.tile_row0 = tr0;
+    g.tile_rowend = tre;
+    g.out_row = perm;
+    g.act = glu ? act : ACT_NONE;
+    g.y = scores ? (void *)(base + p.g_off) : y;
+    g.y_dtype = scores ? KQ_F32 : y_dtype;
+    g.y_row_stride = scores ? n : yrs;
+    for (int64_t c0 = 0; c0 < e; c0 += p.chunk_e) {
+        const int64_t c1 = std::min<int64_t>(e, c0 + p.chunk_e);
+        g.ex_lo = (int)c0;
+        g.ex_hi = (int)c1;
+        void *bd = nullptr;
+        if (codec == KQ_Q4_K) {
+            g.w = (const uint8_t *)w;
+            g.w2 = (const uint8_t *)w2;
+        } else {
+            bd = base + p.b_off;
+            for (int half = 0; half < (glu ? 2 : 1); half++) {
+                const uint8_t *wp = (const uint8_t *)(half ? w2 : w);
+                char *dst = (char *)bd + (size_t)half * (c1 - c0) * n * kin * 2;
+                if (wes == n * wrs) {  // contiguous expert stack: one launch for the chunk
+                    ce = launch_dequantize(codec, wp + c0 * wes, (c1 - c0) * n, kin, wrs, dst, x_dtype, st);
+                } else {
+                    for (int64_t ex = c0; ex < c1 && ce == cudaSuccess; ex++)
+                        ce = launch_dequantize(codec, wp + ex * wes, n, kin, wrs, dst + (ex - c0) * n * kin * 2, x_dtype,
+                                               st);
+                }
+                if (ce != cudaSuccess) return cuda_status(ce, what);
+            }
+        }
+        if ((ce = launch_gemm_grouped(g, p.mt, p.max_tiles, bd, st)) != cudaSuccess) return cuda_status(ce, what);
+    }
+    if (scores)
+        ce = launch_moe_mix((const float *)(base + p.g_off), scores, idx, (int)ebase, (int)e, (int)tokens, kslot, (int)n,
+                            y, y_dtype, st);
+    return cuda_status(ce, what);
+}
+
 // Routed (MoE) GEMV over expert stacks.  mode: 0 glu (x row = slot/k),
 // 1 per-slot rows (x row = slot), 2 explicit x_index.
 int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, int64_t slots, int kslot,
@@ -192,6 +315,9 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     if (wes < n * wrs) return fail(KQ_ERR_SHAPE, "%s: expert stride smaller than one expert", what);
     if (slots == 0) return KQ_OK;
     if (slots < 0 || slots > (1 << 20)) return fail(KQ_ERR_SHAPE, "%s: slot count %lld out of range", what, (long long)slots);
+    if (use_grouped(codec, slots, etotal, n, kin, act, w2 != nullptr, x_dtype, xs))
+        return run_grouped(codec, x, x_dtype, xs, kin, slots, kslot, tokens, idx, xidx, mode, w, w2, e, n, wrs, wes, act,
+                           y, y_dtype, yrs, scores, ws, ws_bytes, stream, what, ebase, etotal);
     // groups of <= 8 slots: one MMA n-tile; an expert with more routed rows
     // streams its weights once per 8 rows (decode routes few rows per expert)
     const int64_t per_expert = mode == 2 ? slots : tokens;  // distinct experts per token bound group sizes
@@ -268,7 +394,14 @@ size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_
     a.max_tokens = gsize;
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
-    return plan((size_t)maxg * 66, mix ? (size_t)slots * n * sizeof(float) : 0, cb, pb).total;
+    size_t t = plan((size_t)maxg * 66, mix ? (size_t)slots * n * sizeof(float) : 0, cb, pb).total;
+    // the grouped GEMM path may be taken once slots >= GEMM_MIN_M * total experts >= GEMM_MIN_M * e
+    if (slots >= (int64_t)GEMM_MIN_M * e && n % 4 == 0 && kin % 64 == 0) {
+        const size_t gt = std::max(grouped_plan(codec, slots, e, e, n, kin, act != ACT_NONE, mix).total,
+                                   grouped_plan(codec, slots, e, slots, n, kin, act != ACT_NONE, mix).total);
+        t = gt > t ? gt : t;
+    }
+    return t;
 }
 
 }  // namespace

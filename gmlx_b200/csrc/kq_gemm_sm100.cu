@@ -140,7 +140,10 @@ template <bool F16> __device__ __forceinline__ uint32_t q4_pair(uint32_t nib2, u
     return r;
 }
 
-template <bool F16, int BMODE, int MT>
+// GLU: the 256-row weight tile is 128 gate rows over 128 up rows of the same
+// output columns; accumulator columns [0,128) hold x.Wg, [128,256) x.Wu and the
+// epilogue writes act(g) * u for 128 output columns.
+template <bool F16, int BMODE, int MT, bool GLU>
 __global__ void __launch_bounds__(GT, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
     using L = GL<MT>;
@@ -155,8 +158,17 @@ __global__ void __launch_bounds__(GT, 1)
     volatile int *s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM * MT, n0 = blockIdx.y * BN;
+    constexpr int NOUT = GLU ? BN / 2 : BN;  // output columns per CTA
+    const int n0 = blockIdx.y * NOUT;
     const int nk = a.K / BK;
+    int m0 = blockIdx.x * BM * MT, mend = a.M, ex = 0;
+    if (a.n_tiles) {  // grouped: this CTA's (expert, row range) from the device tile table
+        if ((int)blockIdx.x >= *a.n_tiles) return;
+        ex = a.tile_e[blockIdx.x];
+        if (ex < a.ex_lo || ex >= a.ex_hi) return;
+        m0 = a.tile_row0[blockIdx.x];
+        mend = a.tile_rowend[blockIdx.x];
+    }
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSTAGE; i++) {
@@ -189,7 +201,13 @@ __global__ void __launch_bounds__(GT, 1)
 #pragma unroll
                 for (int t = 0; t < MT; t++)
                     tma_load_2d(smem + OFF_A + slot * L::STAGE_A + t * A_BYTES, &tmA, s * BK, m0 + t * BM, &fullA[slot]);
-                if (BMODE == B_TMA) tma_load_2d(smem + OFF_B + slot * B_BYTES, &tmB, s * BK, n0, &fullA[slot]);
+                if (BMODE == B_TMA) {
+                    const int rb = (ex - a.ex_lo) * a.n_per_expert + n0;
+                    tma_load_2d(smem + OFF_B + slot * B_BYTES, &tmB, s * BK, rb, &fullA[slot]);
+                    if (GLU)  // up rows: second half of the dequantized scratch
+                        tma_load_2d(smem + OFF_B + slot * B_BYTES + B_BYTES / 2, &tmB, s * BK,
+                                    rb + (a.ex_hi - a.ex_lo) * a.n_per_expert, &fullA[slot]);
+                }
             }
         }
     } else if (warp == 1) {
@@ -216,9 +234,10 @@ __global__ void __launch_bounds__(GT, 1)
     } else {
         const int i = threadIdx.x - 64;  // 0..255: weight row of the tile
         if constexpr (BMODE == B_Q4K) {
-            const int n = n0 + i;
+            const int n = n0 + (GLU ? (i & 127) : i);
             const bool valid = n < a.N;
-            const uint8_t *row = a.w + (int64_t)(valid ? n : 0) * a.w_row_stride;
+            const uint8_t *wb = (GLU && i >= 128) ? a.w2 : a.w;
+            const uint8_t *row = wb + (int64_t)ex * a.w_expert_stride + (int64_t)(valid ? n : 0) * a.w_row_stride;
             uint32_t dsc2[8], ndm2[8];
             // loads run one stage ahead of the decode (header of the next block, next chunk)
             uint4 nh = __ldg(reinterpret_cast<const uint4 *>(row));
@@ -272,16 +291,24 @@ __global__ void __launch_bounds__(GT, 1)
         tc_fence_after();
         const int quarter = warp & 3, chalf = (warp - 2) >> 2;
 #pragma unroll 1
-        for (int q32 = 0; q32 < MT * (BN / 2); q32 += 32) {
-            const int t = q32 / (BN / 2), cc = q32 % (BN / 2);
+        for (int q32 = 0; q32 < MT * (NOUT / 2); q32 += 32) {
+            const int t = q32 / (NOUT / 2), cc = q32 % (NOUT / 2);
             const int tok = m0 + t * BM + quarter * 32 + lane;
-            const int col = chalf * (BN / 2) + cc;
+            const int col = chalf * (NOUT / 2) + cc;
             uint32_t r[32];
             tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * BN + col), r);
-            if (tok >= a.M || *s_abort) continue;
+            if constexpr (GLU) {
+                uint32_t u[32];
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * BN + BN / 2 + col), u);
+#pragma unroll
+                for (int v = 0; v < 32; v++)
+                    r[v] = __float_as_uint(apply_act(a.act, __uint_as_float(r[v])) * __uint_as_float(u[v]));
+            }
+            if (tok >= mend || *s_abort) continue;
+            const int64_t orow = a.out_row ? (int64_t)a.out_row[tok] : (int64_t)tok;
             const int nb = n0 + col;
             if (a.y_dtype == F32) {
-                float *yp = reinterpret_cast<float *>(a.y) + (int64_t)tok * a.y_row_stride + nb;
+                float *yp = reinterpret_cast<float *>(a.y) + orow * a.y_row_stride + nb;
                 if (nb + 32 <= a.N && ((uintptr_t)yp & 15) == 0) {
 #pragma unroll
                     for (int v = 0; v < 8; v++)
@@ -293,7 +320,7 @@ __global__ void __launch_bounds__(GT, 1)
                 }
             } else {
                 const bool of16 = a.y_dtype == F16;
-                uint16_t *yp = reinterpret_cast<uint16_t *>(a.y) + (int64_t)tok * a.y_row_stride + nb;
+                uint16_t *yp = reinterpret_cast<uint16_t *>(a.y) + orow * a.y_row_stride + nb;
                 uint32_t pk[16];
 #pragma unroll
                 for (int v = 0; v < 16; v++) {
@@ -350,36 +377,179 @@ bool make_map(CUtensorMap *m, const void *base, bool f16, int64_t rows, int64_t 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool F16, int BMODE, int MT>
+template <bool F16, int BMODE, int MT, bool GLU = false>
 cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e =
-            cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, GL<MT>::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT, GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             GL<MT>::SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
     CUtensorMap ta, tb;
     if (!make_map(&ta, a.x, F16, a.M, a.K, a.x_row_stride, BM)) return cudaErrorInvalidValue;
     if (BMODE == B_TMA) {
-        if (!make_map(&tb, bdense, F16, a.N, a.K, a.K, BN)) return cudaErrorInvalidValue;
+        if (!make_map(&tb, bdense, F16, (int64_t)a.N * (GLU ? 2 : 1), a.K, a.K, GLU ? BN / 2 : BN))
+            return cudaErrorInvalidValue;
     } else {
         tb = ta;
     }
-    dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + BN - 1) / BN);
-    gemm_kernel<F16, BMODE, MT><<<grid, GT, GL<MT>::SMEM, st>>>(ta, tb, a);
+    constexpr int NOUT = GLU ? BN / 2 : BN;
+    dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + NOUT - 1) / NOUT);
+    gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT>::SMEM, st>>>(ta, tb, a);
     return cudaGetLastError();
 }
 
-template <bool F16, int BMODE>
+template <bool F16, int BMODE, bool GLU = false>
 cudaError_t launch_gemm_mt(const GemmArgs &a, const void *bdense, cudaStream_t st) {
     // two activation-row tiles per CTA once there are enough CTAs to fill the GPU
-    const long ctas2 = (long)((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
-    if (ctas2 >= num_sms()) return launch_gemm_t<F16, BMODE, 2>(a, bdense, st);
-    return launch_gemm_t<F16, BMODE, 1>(a, bdense, st);
+    constexpr int NOUT = GLU ? BN / 2 : BN;
+    const long ctas2 = (long)((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + NOUT - 1) / NOUT);
+    if (ctas2 >= num_sms()) return launch_gemm_t<F16, BMODE, 2, GLU>(a, bdense, st);
+    return launch_gemm_t<F16, BMODE, 1, GLU>(a, bdense, st);
+}
+
+template <bool F16, int BMODE, int MT, bool GLU>
+cudaError_t launch_grouped_t(const GemmArgs &a, int max_tiles, const void *bdense, cudaStream_t st) {
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT, GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             GL<MT>::SMEM);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, a.x, F16, a.M, a.K, a.x_row_stride, BM)) return cudaErrorInvalidValue;
+    if (BMODE == B_TMA) {
+        const int64_t brows = (int64_t)(a.ex_hi - a.ex_lo) * a.n_per_expert * (GLU ? 2 : 1);
+        if (!make_map(&tb, bdense, F16, brows, a.K, a.K, GLU ? BN / 2 : BN)) return cudaErrorInvalidValue;
+    } else {
+        tb = ta;
+    }
+    if (max_tiles <= 0) return cudaSuccess;
+    const int nout = GLU ? BN / 2 : BN;
+    dim3 grid(max_tiles, (a.N + nout - 1) / nout);
+    gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT>::SMEM, st>>>(ta, tb, a);
+    return cudaGetLastError();
+}
+
+template <bool F16, int BMODE, bool GLU>
+cudaError_t launch_grouped_mt(const GemmArgs &a, int mt, int max_tiles, const void *bdense, cudaStream_t st) {
+    return mt == 2 ? launch_grouped_t<F16, BMODE, 2, GLU>(a, max_tiles, bdense, st)
+                   : launch_grouped_t<F16, BMODE, 1, GLU>(a, max_tiles, bdense, st);
+}
+
+template <bool F16, int BMODE>
+cudaError_t launch_grouped_glu(const GemmArgs &a, int mt, int max_tiles, const void *bdense, cudaStream_t st) {
+    return a.w2 || (BMODE == B_TMA && a.act != ACT_NONE) ? launch_grouped_mt<F16, BMODE, true>(a, mt, max_tiles, bdense, st)
+                                                           : launch_grouped_mt<F16, BMODE, false>(a, mt, max_tiles, bdense, st);
+}
+
+// ---- MoE routing helpers for the grouped path (three parallel passes)
+
+// pass 1: rank of every local slot within its expert (order within an expert
+// is arbitrary; each output row depends only on its own slot)
+__global__ void rank_kernel(const int32_t *__restrict__ idx, int S, int ebase, int ecount, int etotal,
+                            int *__restrict__ cnt, int *__restrict__ rank, int *err) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    const int g = idx[s];
+    if (g < 0 || g >= etotal) atomicCAS(err, 0, 3);  // expert id out of range (as the GEMV grouping)
+    const int e = g - ebase;
+    rank[s] = (e >= 0 && e < ecount) ? atomicAdd(&cnt[e], 1) : -1;
+}
+
+// pass 2 (one CTA): expert offsets and the (expert, row tile) table; resets
+// the counts so the counter region is left zero
+__global__ void table_kernel(int ecount, int tile_rows, int *__restrict__ cnt, int *__restrict__ off,
+                             int *__restrict__ total, int *__restrict__ n_tiles, int *__restrict__ tile_e,
+                             int *__restrict__ tile_row0, int *__restrict__ tile_rowend, int max_tiles, int *err) {
+    __shared__ int s_wsum[2][32];
+    const int e = threadIdx.x, lane = e & 31, w = e >> 5;
+    const int c = e < ecount ? cnt[e] : 0;
+    if (e < ecount) cnt[e] = 0;
+    const int nt = (c + tile_rows - 1) / tile_rows;
+    // block-wide inclusive scans of rows and tiles
+    int rc = c, rt = nt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, rc, o), b = __shfl_up_sync(0xffffffffu, rt, o);
+        if (lane >= o) rc += a, rt += b;
+    }
+    if (lane == 31) s_wsum[0][w] = rc, s_wsum[1][w] = rt;
+    __syncthreads();
+    if (w == 0) {
+        int a = s_wsum[0][lane], b = s_wsum[1][lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+            if (lane >= o) a += x, b += y;
+        }
+        s_wsum[0][lane] = a, s_wsum[1][lane] = b;
+    }
+    __syncthreads();
+    const int r0 = rc - c + (w ? s_wsum[0][w - 1] : 0), t0 = rt - nt + (w ? s_wsum[1][w - 1] : 0);
+    if (e < ecount) {
+        off[e] = r0;
+        for (int j = 0; j < nt; j++)
+            if (t0 + j < max_tiles) {
+                tile_e[t0 + j] = e;
+                tile_row0[t0 + j] = r0 + j * tile_rows;
+                tile_rowend[t0 + j] = r0 + c;
+            }
+    }
+    if (e == blockDim.x - 1) {
+        const int all_t = t0 + nt;
+        if (all_t > max_tiles) atomicCAS(err, 0, 6);
+        *n_tiles = all_t < max_tiles ? all_t : max_tiles;
+        *total = r0 + c;
+    }
+}
+
+// pass 3: slot -> sorted row; copy the slot's activation row there
+__global__ void scatter_rows_kernel(const int32_t *__restrict__ idx, const int *__restrict__ rank,
+                                    const int *__restrict__ off, int ebase, int k, int xrow_is_slot,
+                                    const int32_t *__restrict__ xidx, const uint16_t *__restrict__ x, int64_t xs_stride,
+                                    int K, int *__restrict__ perm, uint16_t *__restrict__ out) {
+    const int s = blockIdx.x;
+    const int r = rank[s];
+    if (r < 0) return;
+    const int p = off[idx[s] - ebase] + r;
+    if (threadIdx.x == 0) perm[p] = s;
+    const int xr = xidx ? xidx[s] : xrow_is_slot ? s : s / k;
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + (int64_t)xr * xs_stride);
+    uint4 *dst = reinterpret_cast<uint4 *>(out + (int64_t)p * K);
+    for (int i = threadIdx.x; i < K / 8; i += blockDim.x) dst[i] = src[i];
 }
 
 }  // namespace
+
+cudaError_t launch_gemm_grouped(const GemmArgs &a, int mt, int max_tiles, const void *b_dense, cudaStream_t st) {
+    const bool f16 = a.x_dtype == F16;
+    if (!b_dense)
+        return f16 ? launch_grouped_glu<true, B_Q4K>(a, mt, max_tiles, nullptr, st)
+                   : launch_grouped_glu<false, B_Q4K>(a, mt, max_tiles, nullptr, st);
+    return f16 ? launch_grouped_glu<true, B_TMA>(a, mt, max_tiles, b_dense, st)
+               : launch_grouped_glu<false, B_TMA>(a, mt, max_tiles, b_dense, st);
+}
+
+cudaError_t launch_moe_sort(const int32_t *idx, int S, int k, int ebase, int ecount, int etotal, int xrow_is_slot,
+                            const int32_t *xidx, const void *x, int64_t x_row_stride, int K, void *xs, int tile_rows,
+                            int *cnt, int *scratch, int *perm, int *counts, int *n_tiles, int *tile_e, int *tile_row0,
+                            int *tile_rowend, int max_tiles, int *err, cudaStream_t st) {
+    if (ecount > 1024) return cudaErrorInvalidValue;
+    int *rank = scratch, *off = scratch + S;
+    rank_kernel<<<(S + 255) / 256, 256, 0, st>>>(idx, S, ebase, ecount, etotal, cnt, rank, err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    table_kernel<<<1, 1024, 0, st>>>(ecount, tile_rows, cnt, off, counts, n_tiles, tile_e, tile_row0, tile_rowend,
+                                     max_tiles, err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    scatter_rows_kernel<<<S, 128, 0, st>>>(idx, rank, off, ebase, k, xrow_is_slot, xidx,
+                                           reinterpret_cast<const uint16_t *>(x), x_row_stride, K, perm,
+                                           reinterpret_cast<uint16_t *>(xs));
+    return cudaGetLastError();
+}
 
 bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride) {
     (void)codec;
@@ -388,12 +558,27 @@ bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int
            encode_fn() != nullptr;
 }
 
-size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k) {
-    return codec == Q4_K ? 0 : (size_t)n * k * 2;  // dequantized copy for the B-by-TMA path
+size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k, bool glu) {
+    return codec == Q4_K ? 0 : (size_t)n * k * 2 * (glu ? 2 : 1);  // dequantized copy for the B-by-TMA path
 }
 
-cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st) {
-    const bool f16 = a.x_dtype == F16;
+cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
+    const bool f16 = a0.x_dtype == F16;
+    if (a0.act != ACT_NONE) {  // fused GLU: gate rows then up rows of the dequantized copy
+        GemmArgs a = a0;
+        a.ex_lo = 0;
+        a.ex_hi = 1;
+        a.n_per_expert = a.N;
+        if (a.codec == Q4_K)
+            return f16 ? launch_gemm_mt<true, B_Q4K, true>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K, true>(a, nullptr, st);
+        cudaError_t e = launch_dequantize(a.codec, a.w, a.N, a.K, a.w_row_stride, scratch, a.x_dtype, st);
+        if (e == cudaSuccess)
+            e = launch_dequantize(a.codec, a.w2, a.N, a.K, a.w_row_stride, (char *)scratch + (size_t)a.N * a.K * 2,
+                                  a.x_dtype, st);
+        if (e != cudaSuccess) return e;
+        return f16 ? launch_gemm_mt<true, B_TMA, true>(a, scratch, st) : launch_gemm_mt<false, B_TMA, true>(a, scratch, st);
+    }
+    const GemmArgs &a = a0;
     if (a.codec == Q4_K) return f16 ? launch_gemm_mt<true, B_Q4K>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K>(a, nullptr, st);
     // other codecs: dequantize once into scratch (activation dtype), then B by TMA
     cudaError_t e = launch_dequantize(a.codec, a.w, a.N, a.K, a.w_row_stride, scratch, a.x_dtype, st);

@@ -155,19 +155,6 @@ __device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, 
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
-__device__ __forceinline__ void store_out(void *y, int dtype, int64_t i, float v) {
-    if (dtype == F32) reinterpret_cast<float *>(y)[i] = v;
-    else if (dtype == BF16) reinterpret_cast<__nv_bfloat16 *>(y)[i] = __float2bfloat16_rn(v);
-    else reinterpret_cast<__half *>(y)[i] = __float2half_rn(v);
-}
-
-__device__ __forceinline__ float apply_act(int act, float g) {
-    if (act == ACT_SILU) return g / (1.0f + expf(-g));
-    if (act == ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
-    const float c = 0.7978845608028654f;  // tanh approximation
-    return 0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g)));
-}
-
 // Activation fragment loads: from the staged slice (shared) or from global.
 template <bool XS> __device__ __forceinline__ uint4 ldx16(const uint16_t *p) {
     if constexpr (XS) {

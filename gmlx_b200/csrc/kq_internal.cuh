@@ -11,6 +11,19 @@ namespace kq {
 // lists silu and gelu for the kq fused MoE ops).
 enum Act : int { ACT_NONE = 0, ACT_SILU = 1, ACT_GELU = 2, ACT_GELU_TANH = 3 };
 
+__device__ __forceinline__ void store_out(void *y, int dtype, int64_t i, float v) {
+    if (dtype == F32) reinterpret_cast<float *>(y)[i] = v;
+    else if (dtype == BF16) reinterpret_cast<__nv_bfloat16 *>(y)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<__half *>(y)[i] = __float2half_rn(v);
+}
+
+__device__ __forceinline__ float apply_act(int act, float g) {
+    if (act == ACT_SILU) return g / (1.0f + expf(-g));
+    if (act == ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+    const float c = 0.7978845608028654f;  // tanh approximation
+    return 0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g)));
+}
+
 cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t k, int64_t row_stride, void *out,
                               int dtype, cudaStream_t st);
 
@@ -60,11 +73,37 @@ struct GemmArgs {
     int y_dtype;
     int64_t y_row_stride;  // elements
     int *err;
+    // grouped (MoE) mode: blockIdx.x indexes a device table of row tiles
+    // (expert, first row, end row) over expert-sorted activation rows; output
+    // row r goes to y row out_row[r]
+    const int *n_tiles;  // device count; null = dense mode
+    const int *tile_e, *tile_row0, *tile_rowend;
+    const int *out_row;
+    int64_t w_expert_stride;  // bytes (Q4_K fused mode)
+    int n_per_expert;         // rows of B per expert (dense B-by-TMA map is [E*N, K])
+    int ex_lo, ex_hi;         // grouped: only tiles of experts [ex_lo, ex_hi) run; B row base (e-ex_lo)*N
+    // fused GLU (act != ACT_NONE): y = act(x.Wg) * (x.Wu); w2 = up weights (Q4_K
+    // fused), or for dense B the up rows follow the gate rows of the scratch
+    const uint8_t *w2;
+    int act;
 };
 bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride);
-size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k);
+size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k, bool glu);
 cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st);
 constexpr int GEMM_MIN_M = 33;  // activation rows from which the tensor-core GEMM takes over
+// Grouped GEMM over expert-sorted rows (see kq_gemm_sm100.cu); the caller
+// prepared the table of (128*mt)-row tiles with launch_moe_sort.  b_dense:
+// dequantized experts [ex_lo, ex_hi) as [(ex_hi-ex_lo)*N, K] in the activation
+// type (GLU: gate rows, then up rows) when the codec has no fused path, else null.
+cudaError_t launch_gemm_grouped(const GemmArgs &a, int mt, int max_tiles, const void *b_dense, cudaStream_t st);
+// Counting sort of routed slots by local expert + (expert, tile_rows-row tile)
+// table for the grouped GEMM + gathered activation rows.  perm[p] = slot at
+// sorted row p.  cnt: ecount ints that are zero on entry and left zero;
+// scratch: S + ecount ints.
+cudaError_t launch_moe_sort(const int32_t *idx, int S, int k, int ebase, int ecount, int etotal, int xrow_is_slot,
+                            const int32_t *xidx, const void *x, int64_t x_row_stride, int K, void *xs, int tile_rows,
+                            int *cnt, int *scratch, int *perm, int *counts, int *n_tiles, int *tile_e, int *tile_row0,
+                            int *tile_rowend, int max_tiles, int *err, cudaStream_t st);
 
 // MoE slot grouping: idx[S] (S = T*k slots) -> groups of <= gsize slots per
 // local expert (experts [ebase, ebase+ecount); ascending slot order inside a

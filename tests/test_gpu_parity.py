@@ -237,6 +237,27 @@ def test_prefill_gemm_tcgen05(cuda, codec, m, n, k):
     assert rel_err(y16.float().cpu().numpy(), ref) <= TOL
 
 
+@pytest.mark.parametrize("codec", CODECS)
+@pytest.mark.parametrize("act", ["silu", "gelu"])
+def test_prefill_glu_tcgen05(cuda, codec, act):
+    """Prefill-sized fused GLU: one tcgen05 GEMM with gate and up accumulators
+    side by side (128 output columns per tile; N=320 leaves a ragged tile)."""
+    from math import erf
+    n, k, m = 320, 1024, 200
+    wg = synth.random_weight(codec, n, k, seed=24)
+    wu = synth.random_weight(codec, n, k, seed=25)
+    x = synth.random_activations(m, k, seed=26)
+    g = O.matmul(x, wg, codec).astype(np.float64)
+    u = O.matmul(x, wu, codec).astype(np.float64)
+    if act == "silu":
+        ref = g / (1 + np.exp(-g)) * u
+    else:
+        ref = 0.5 * g * (1 + np.vectorize(erf)(g / np.sqrt(2))) * u
+    y = kq.quantized_glu(to_dev_x(x, cuda), torch.from_numpy(wg).to(cuda), torch.from_numpy(wu).to(cuda), codec,
+                         act=act, out_dtype=torch.float32)
+    assert rel_err(y.cpu().numpy(), ref) <= TOL
+
+
 @pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs")])
 def test_expert_parallel_partials_sum_to_full_layer(cuda, codec_gu, codec_d):
     """Two expert-parallel 'ranks' (expert ranges) on one GPU: their partial
@@ -283,3 +304,68 @@ def test_tensor_parallel_shards_sum_to_full(cuda):
             acc += kq.quantized_matmul(to_dev_x(x[:, r * kk:(r + 1) * kk], cuda), ws, None, codec,
                                        out_dtype=torch.float32)
         assert rel_err(acc.cpu().numpy(), full.cpu().numpy()) <= 1e-4
+
+
+def _skewed_ids(rng, shape, e):
+    """Expert ids with a skewed load: expert 0 gets several 128-row tiles, the
+    last expert none (the grouped path's empty and ragged groups)."""
+    p = np.array([0.55, 0.25] + [0.2 / (e - 3)] * (e - 3) + [0.0])
+    return rng.choice(e, size=shape, p=p).astype(np.int32)
+
+
+@pytest.mark.parametrize("codec", CODECS)
+def test_grouped_gather_qmm(cuda, codec):
+    """Many routed rows per expert (>= 33 on average) take the grouped tcgen05
+    GEMM: rows sorted by expert, one launch over (expert, 128-row tile), outputs
+    scattered back.  N=320 leaves a ragged 256-column tile."""
+    e, n, kin, rows = 4, 320, 512, 400
+    w = synth.random_weight(codec, n, kin, seed=70, experts=e)
+    x = synth.random_activations(rows, kin, seed=71)
+    rng = np.random.default_rng(72)
+    idx = _skewed_ids(rng, (rows,), e)
+    ref = np.zeros((rows, n))
+    for ex in range(e):
+        sel = np.nonzero(idx == ex)[0]
+        if len(sel):
+            ref[sel] = O.matmul(np.ascontiguousarray(x[sel]), w[ex], codec)
+    xd = to_dev_x(x, cuda).reshape(rows, 1, 1, kin)
+    y = kq.gather_qmm(xd, torch.from_numpy(w).to(cuda), None, codec,
+                      rhs_indices=torch.from_numpy(idx.reshape(rows, 1)).to(cuda), out_dtype=torch.float32)
+    assert rel_err(y.reshape(rows, n).cpu().numpy(), ref) <= TOL
+    assert kq.workspace_error() == 0
+
+
+@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs")])
+def test_grouped_moe_layer_prefill(cuda, codec_gu, codec_d):
+    """MoE prefill (T*k >= 33 * experts) through the grouped GEMM: gate/up GEMMs,
+    SiLU*up, down GEMM and the score mix; the full layer matches the oracle and
+    two expert-parallel halves sum to it."""
+    e, d, f, k, t = 8, 512, 256, 2, 200
+    wg, wu, wd, x, _ = _moe_case(codec_gu, codec_d, e, d, f, t, k, seed=110)
+    rng = np.random.default_rng(111)
+    idx = np.stack([_skewed_ids(rng, (t,), e), rng.integers(0, e, size=t).astype(np.int32)], 1)
+    sc = rng.random((t, k)).astype(np.float32)
+    tw = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    xd = to_dev_x(x, cuda)
+    full = kq.moe_expert_layer_local(xd, tw(idx), tw(sc), tw(wg), tw(wu), tw(wd), codec_gu, codec_d, 0, e,
+                                     out_dtype=torch.float32)
+    parts = sum(kq.moe_expert_layer_local(xd, tw(idx), tw(sc), tw(wg[4 * r:4 * r + 4]), tw(wu[4 * r:4 * r + 4]),
+                                          tw(wd[4 * r:4 * r + 4]), codec_gu, codec_d, 4 * r, e,
+                                          out_dtype=torch.float32) for r in range(2))
+    assert rel_err(parts.cpu().numpy(), full.cpu().numpy()) <= 1e-5
+    ref = np.zeros((t, d))
+    for j in range(k):
+        for ex in range(e):
+            sel = np.nonzero(idx[:, j] == ex)[0]
+            if not len(sel):
+                continue
+            xs = np.ascontiguousarray(x[sel])
+            g = O.matmul(xs, wg[ex], codec_gu).astype(np.float64)
+            u = O.matmul(xs, wu[ex], codec_gu).astype(np.float64)
+            hb = synth.f32_to_bf16_bits((g / (1 + np.exp(-g)) * u).astype(np.float32))
+            ref[sel] += sc[sel, j, None] * O.matmul(hb, wd[ex], codec_d)
+    assert rel_err(full.cpu().numpy(), ref) <= TOL
+    # the GLU op alone on the same routing
+    h = kq.moe_glu_gather_kq(xd, tw(wg), tw(wu), codec_gu, tw(idx))
+    assert tuple(h.shape) == (t, k, f)
+    assert kq.workspace_error() == 0
