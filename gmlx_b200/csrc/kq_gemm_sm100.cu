@@ -52,13 +52,14 @@ __device__ __forceinline__ uint64_t gtimer() {
 }
 
 __device__ __forceinline__ bool wait_b(uint64_t *bar, uint32_t par, volatile int *abort, int *err, int code) {
-    if (mbar_try_wait(bar, par)) return true;
-    const uint64_t t0 = gtimer();
+    uint64_t t0 = 0;  // timer read every 1024 polls only (a %globaltimer read is slow)
     for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, par)) return true;
-        if ((i & 255) == 0) {
+        if ((i & 1023) == 0) {
             if (*abort) return false;
-            if (gtimer() - t0 > 2000000000ull) {
+            const uint64_t now = gtimer();
+            if (t0 == 0) t0 = now;
+            if (now - t0 > 2000000000ull) {
                 *abort = 1;
                 atomicCAS(err, 0, code);
                 return false;

@@ -92,7 +92,8 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int OFF_BAR = 0;                              // 2*NS mbarriers
     static constexpr int OFF_ROWOFF = 128;                         // NS x 32 bytes
     static constexpr int OFF_MISC = OFF_ROWOFF + 32 * 8;           // flags
-    static constexpr int OFF_GRID = 512;                           // IQ2 grid: 256 x 16 B
+    static constexpr int OFF_UNIT = 512;                           // dynamic mode: tile id per ring slot
+    static constexpr int OFF_GRID = 640;                           // IQ2 grid: 256 x 16 B
     static constexpr int OFF_RING = OFF_GRID + (C == IQ2_XXS ? 4096 : 0);
     static constexpr int OFF_SCALE = OFF_RING + NS * STAGE;        // CW x TABW floats
     static constexpr int OFF_S = OFF_SCALE + TABS;
@@ -111,14 +112,17 @@ __device__ __forceinline__ uint64_t globaltimer() {
 // Bounded mbarrier wait shared by all warps of the CTA: gives up after ~2 s or
 // as soon as another warp gave up, records the error once and returns false.
 __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, volatile int *abort, int *err,
-                                             int code) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer();
+                                             int code, bool spin = false) {
+    // the timer is read only every 1024 polls: a %globaltimer read is slow
+    // enough to delay the wake-up of a wait that would otherwise end at once
+    uint64_t t0 = 0;
     for (uint32_t i = 1;; i++) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 0) {
+        if (spin ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023) == 0) {
             if (*abort) return false;
-            if (globaltimer() - t0 > 2000000000ull) {
+            const uint64_t now = globaltimer();
+            if (t0 == 0) t0 = now;
+            if (now - t0 > 2000000000ull) {
                 *abort = 1;
                 atomicCAS(err, 0, code);
                 return false;
@@ -182,8 +186,9 @@ struct Tile {
 };
 
 __device__ __forceinline__ void tile_of(const GemvArgs &a, int64_t gt, int tiles, Tile &T) {
-    T.g = (int)(gt / tiles);
-    T.tile = (int)(gt - (int64_t)T.g * tiles);
+    const int g32 = (int)gt;  // tile index fits 32 bits (checked on the host); 64-bit division is slow
+    T.g = g32 / tiles;
+    T.tile = g32 - T.g * tiles;
     if (a.dense_m > 0) {
         T.m = min(32, a.dense_m - 32 * T.g);
         T.e = 0;
@@ -517,19 +522,27 @@ __device__ __forceinline__ void dp_quantize(const uint16_t *xs, uint32_t *xq, fl
     __syncwarp();
 }
 
-template <bool F16>
-__device__ __forceinline__ float dp_q4k_block(const uint8_t *row, const uint16_t *xs, uint32_t *xq, float *xsc) {
-    dp_quantize<F16>(xs, xq, xsc);
-    // -- this lane's row
-    const uint4 hv = *reinterpret_cast<const uint4 *>(row);
-    const float d = half_bits_to_float(hv.x & 0xffffu), dmin = half_bits_to_float(hv.x >> 16);
+// Lane-per-row Q4_K in two steps: dp_q4k_load pulls the lane's 144-byte block
+// (and the warp's quantized activations) out of the ring, so the stage can be
+// released to the producer before dp_q4k_dot does the arithmetic.
+struct Q4Regs {
+    uint4 h, w[8];
+};
+
+__device__ __forceinline__ void dp_q4k_load(const uint8_t *row, Q4Regs &r) {
+    r.h = *reinterpret_cast<const uint4 *>(row);
+#pragma unroll
+    for (int i = 0; i < 8; i++) r.w[i] = *reinterpret_cast<const uint4 *>(row + 16 + 16 * i);
+}
+
+__device__ __forceinline__ float dp_q4k_dot(const Q4Regs &r, const uint32_t *xq, const float *xsc) {
+    const float d = half_bits_to_float(r.h.x & 0xffffu), dmin = half_bits_to_float(r.h.x >> 16);
     uint32_t sc03, sc47, m03, m47;
-    q4k_unpack_scales(hv.y, hv.z, hv.w, sc03, sc47, m03, m47);
+    q4k_unpack_scales(r.h.y, r.h.z, r.h.w, sc03, sc47, m03, m47);
     float acc = 0.f;
 #pragma unroll
     for (int c = 0; c < 4; c++) {
-        const uint4 wa = *reinterpret_cast<const uint4 *>(row + 16 + 32 * c);
-        const uint4 wb = *reinterpret_cast<const uint4 *>(row + 32 + 32 * c);
+        const uint4 wa = r.w[2 * c], wb = r.w[2 * c + 1];
         const uint32_t w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
         int sl = 0, sh = 0;
 #pragma unroll
@@ -573,19 +586,25 @@ __device__ __forceinline__ uint32_t lds_w2(const uint32_t *base, int i, uint32_t
     return __funnelshift_r(base[i], base[i + 1], sh);
 }
 
-template <bool F16>
-__device__ __forceinline__ float dp_q6k_half(const uint8_t *blk, int hf, const uint16_t *xs, uint32_t *xq, float *xsc) {
-    dp_quantize<F16>(xs, xq, xsc);
+struct Q6Regs {
+    uint32_t ql[16], qh[8], scw0, scw1;
+    float d;
+};
+
+__device__ __forceinline__ void dp_q6k_load(const uint8_t *blk, int hf, Q6Regs &r) {
     const uintptr_t ab = (uintptr_t)blk;
     const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
     const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
-    uint32_t ql[16], qh[8];
 #pragma unroll
-    for (int i = 0; i < 16; i++) ql[i] = lds_w2(aw, 16 * hf + i, sh);       // bytes 64hf .. 64hf+63
+    for (int i = 0; i < 16; i++) r.ql[i] = lds_w2(aw, 16 * hf + i, sh);     // bytes 64hf .. 64hf+63
 #pragma unroll
-    for (int i = 0; i < 8; i++) qh[i] = lds_w2(aw, 32 + 8 * hf + i, sh);    // bytes 128+32hf ..
-    const uint32_t scw0 = lds_w2(aw, 48 + 2 * hf, sh), scw1 = lds_w2(aw, 49 + 2 * hf, sh);  // int8 scales 8hf..8hf+7
-    const float d = half_bits_to_float(lds_w2(aw, 52, sh) & 0xffffu);       // bytes 208-209
+    for (int i = 0; i < 8; i++) r.qh[i] = lds_w2(aw, 32 + 8 * hf + i, sh);  // bytes 128+32hf ..
+    r.scw0 = lds_w2(aw, 48 + 2 * hf, sh);                                   // int8 scales 8hf..8hf+7
+    r.scw1 = lds_w2(aw, 49 + 2 * hf, sh);
+    r.d = half_bits_to_float(lds_w2(aw, 52, sh) & 0xffffu);                 // bytes 208-209
+}
+
+__device__ __forceinline__ float dp_q6k_dot(const Q6Regs &r, int hf, const uint32_t *xq, const float *xsc) {
     float acc = 0.f;
 #pragma unroll
     for (int s4 = 0; s4 < 4; s4++) {
@@ -593,8 +612,8 @@ __device__ __forceinline__ float dp_q6k_half(const uint8_t *blk, int hf, const u
         int sm[2] = {0, 0};  // the two 16-weight sub-blocks of this 32-weight group
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const uint32_t lw = ql[8 * (s4 & 1) + i] >> ns;
-            const uint32_t hw = s4 == 0 ? (qh[i] << 4) : s4 == 1 ? (qh[i] << 2) : s4 == 2 ? qh[i] : (qh[i] >> 2);
+            const uint32_t lw = r.ql[8 * (s4 & 1) + i] >> ns;
+            const uint32_t hw = s4 == 0 ? (r.qh[i] << 4) : s4 == 1 ? (r.qh[i] << 2) : s4 == 2 ? r.qh[i] : (r.qh[i] >> 2);
             const int q6 = (int)lop_and_or(hw, 0x30303030u, lw & 0x0f0f0f0fu);
             // weights 128hf + 32 s4 + 4i .. +3  <-> x words (64 s4 + 8i)/2 of the block-half
             const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 64 * hf + 16 * s4 + 2 * i);
@@ -606,9 +625,9 @@ __device__ __forceinline__ float dp_q6k_half(const uint8_t *blk, int hf, const u
 #pragma unroll
         for (int u = 0; u < 2; u++) {
             const int j = 2 * s4 + u;  // sub-block within the half (scale 8hf + j)
-            const uint32_t scw = j < 4 ? scw0 : scw1;
+            const uint32_t scw = j < 4 ? r.scw0 : r.scw1;
             const float sc = (float)(int)(int8_t)((scw >> (8 * (j & 3))) & 255u);
-            acc = fmaf(d * sc, fmaf(xsc[g32], (float)sm[u], -32.f * xsc[16 + 2 * g32 + u]), acc);
+            acc = fmaf(r.d * sc, fmaf(xsc[g32], (float)sm[u], -32.f * xsc[16 + 2 * g32 + u]), acc);
         }
     }
     __syncwarp();  // xq is rewritten for the next block
@@ -628,11 +647,14 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     uint8_t *rowoff = smem + L::OFF_ROWOFF;
     volatile int *s_abort = reinterpret_cast<volatile int *>(smem + L::OFF_MISC);
     int *s_last = reinterpret_cast<int *>(smem + L::OFF_MISC + 4);
+    int *s_unit = reinterpret_cast<int *>(smem + L::OFF_UNIT);
     uint4 *gridtab = reinterpret_cast<uint4 *>(smem + L::OFF_GRID);
     uint8_t *ring = smem + L::OFF_RING;
     float *red0 = reinterpret_cast<float *>(smem + L::OFF_RED);
     float *Ssm = reinterpret_cast<float *>(smem + L::OFF_S);
 
+    const long long c_entry = clock64();  // development timing (debug bit 128)
+    const uint32_t g_entry = (uint32_t)globaltimer();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = a.K / QK;
     const int nst = (nb + KB - 1) / KB;  // stages per tile
@@ -675,11 +697,72 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     // its prologue now; weights are read-only, so only activation reads and
     // global writes below wait for the previous kernel (griddepcontrol.wait)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (lo >= hi) return;
+    if ((lo >= hi && !(L::DP && a.dyn)) || (a.debug & 64)) return;  // 64: development, prologue only
+    unsigned *stamps = reinterpret_cast<unsigned *>(smem + L::OFF_MISC + 64);  // development timing (16 words)
+    if ((a.debug & 128) && threadIdx.x == 0) stamps[0] = (unsigned)(clock64() - c_entry);
 
     if (warp == CW) {
         // ---------------- producer warp: lane r streams tile row r (+ activation row r) ----------------
         const uint64_t pol = policy_evict_first(), pol_x = policy_evict_last();
+        if (L::DP && a.dyn) {
+            // dynamic whole tiles: the first tile of a CTA is its index, later ones
+            // come from a work counter (read only after griddepcontrol.wait, so a
+            // previous kernel has reset it), so CTAs that start late take fewer
+            const int units = n_groups * tiles;
+            uint32_t it = 0;
+            bool dep_done = false;
+            for (int unit = blockIdx.x;;) {
+                const int slot0 = it % NS;
+                if (unit >= units || *s_abort) {  // end marker: an empty stage with a negative tile id
+                    wait_bounded(&empty[slot0], ((it / NS) & 1) ^ 1, s_abort, a.err, 1);
+                    if (lane == 0) {
+                        s_unit[slot0] = -1;
+                        mbar_arrive(&full[slot0]);
+                    }
+                    break;
+                }
+                Tile T;
+                tile_of(a, unit, tiles, T);
+                const int orow = T.tile * rows_out + (GLU ? (lane & 15) : lane);
+                const bool up = GLU && lane >= 16;
+                const bool valid = orow < a.N;
+                const uint8_t *base = up ? a.w2 + (int64_t)T.e * a.w2_expert_stride + (int64_t)orow * a.w2_row_stride
+                                         : a.w + (int64_t)T.e * a.w_expert_stride + (int64_t)orow * a.w_row_stride;
+                const uint8_t *xsrc =
+                    reinterpret_cast<const uint8_t *>(a.x) + (int64_t)xrow_of(a, T, 0) * a.x_row_stride * 2;
+                for (int st = 0; st < nst; st++, it++) {
+                    const int slot = it % NS;
+                    wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1);
+                    const int bs = st * KB, nbk = min(KB, nb - bs);
+                    const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
+                    const uint32_t off = (uint32_t)(src & 15);
+                    const uint32_t bytes = (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
+                    const uint32_t xbytes = (lane == 0 && !(a.debug & 8)) ? (uint32_t)nbk * QK * 2 : 0u;
+                    rowoff[slot * 32 + lane] = (uint8_t)off;
+                    uint32_t total = bytes + xbytes;
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+                    if (lane == 0) {
+                        s_unit[slot] = unit;
+                        mbar_arrive_expect_tx(&full[slot], total);
+                    }
+                    __syncwarp();
+                    if (!*s_abort) {
+                        uint8_t *stg = ring + slot * L::STAGE;
+                        if (bytes) bulk_g2s(stg + lane * L::SP, (const void *)(src - off), bytes, &full[slot], pol);
+                        if (!dep_done) {
+                            asm volatile("griddepcontrol.wait;" ::: "memory");
+                            dep_done = true;
+                        }
+                        if (xbytes) bulk_g2s(stg + L::WBYTES, xsrc + (int64_t)bs * QK * 2, xbytes, &full[slot], pol_x);
+                    }
+                }
+                int nu = 0;
+                if (lane == 0) nu = (int)gridDim.x + atomicAdd(a.counters, 1);
+                unit = __shfl_sync(0xffffffffu, nu, 0);
+            }
+            return;
+        }
         uint32_t it = 0;
         int64_t cur = -1;
         Tile T{};
@@ -687,9 +770,13 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         bool valid = false;
         const uint8_t *xsrc = nullptr;
         bool dep_done = false;
-        for (int64_t i = lo; i < hi; i++, it++) {
-            const int64_t gt = i / nst;
-            const int st = (int)(i - gt * nst);
+        int64_t gt = lo / nst;
+        int st = (int)(lo - gt * nst);
+        for (int64_t i = lo; i < hi; i++, it++, st++) {
+            if (st == nst) {  // next tile (indices advance incrementally: no 64-bit division per stage)
+                st = 0;
+                gt++;
+            }
             if (gt != cur) {
                 cur = gt;
                 tile_of(a, gt, tiles, T);
@@ -702,7 +789,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                     xsrc = reinterpret_cast<const uint8_t *>(a.x) + (int64_t)xrow_of(a, T, lane) * a.x_row_stride * 2;
             }
             const int slot = it % NS;
-            wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1);
+            wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1, (a.debug & 256) != 0);
+            if ((a.debug & 128) && lane == 0 && it < 6) stamps[10 + it] = (unsigned)(clock64() - c_entry);
             const int bs = st * KB, nbk = min(KB, nb - bs);
             const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
             const uint32_t off = (uint32_t)(src & 15);
@@ -714,6 +802,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
             if (lane == 0) mbar_arrive_expect_tx(&full[slot], total);
             __syncwarp();
+            if ((a.debug & 128) && lane == 0 && it < 6) stamps[4 + it] = (unsigned)(clock64() - c_entry);
             if (!*s_abort) {
                 uint8_t *stg = ring + slot * L::STAGE;
                 if (bytes) {
@@ -734,6 +823,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                     bulk_g2s(stg + L::WBYTES + lane * XSTR, xsrc + (int64_t)bs * QK * 2, xbytes, &full[slot], pol_x);
             }
         }
+        if ((a.debug & 128) && lane == 0) stamps[1] = (unsigned)(clock64() - c_entry);
         return;
     }
 
@@ -747,13 +837,113 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     const int mt = (DP && C == Q4_K) ? 0 : (warp & 1), col = (DP && C == Q4_K) ? warp : (DP ? (warp & 3) : (warp >> 1));
     float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * GCfg<C>::TABW * BPW;
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
-    if (!XS) asm volatile("griddepcontrol.wait;" ::: "memory");  // MMA B operands read global activations
+    // Consumers block here until the previous kernel on the stream has finished
+    // (they need its activations anyway).  Polling the ring instead would burn
+    // the issue slots of the previous kernel's CTAs still running on this SM.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     uint32_t it = 0;
     int64_t i = lo;
     int rp = 0, s_group = -1, tix = 0;
     int *dcnt = const_cast<int *>(reinterpret_cast<volatile int *>(smem + L::OFF_MISC + 16));  // NS+1 tile counters
+    // lane-per-row path: one stage of one block column (operands to registers,
+    // release the stage, then the arithmetic)
+    auto dp_stage = [&](int slot, int b, float &acc) {
+        uint32_t *xq = reinterpret_cast<uint32_t *>(stab);
+        float *xsc = stab + 128;
+        const bool run = b < nb && !*s_abort && !(a.debug & 1);
+        const uint8_t *stg = ring + slot * L::STAGE;
+        if constexpr (C == Q4_K) {
+            Q4Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_q4k_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_q4k_dot(r, xq, xsc);
+        } else if constexpr (C == Q6_K) {
+            const int rr = 16 * (warp >> 2) + (lane & 15);
+            Q6Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_q6k_load(stg + rr * L::SP + rowoff[slot * 32 + rr] + col * bpb, lane >> 4, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_q6k_dot(r, lane >> 4, xq, xsc);
+        }
+    };
+    // lane-per-row path, whole tile: barrier-free store.  Each warp posts its 32
+    // row partials; the last of the KB warps to arrive sums them in column order
+    // and stores.  Buffers rotate over NS+1 tiles, which the ring keeps apart.
+    auto dp_store = [&](const Tile &T, float acc, int tix) {
+        const int bi = tix % (NS + 1);
+        float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (KB * 32);
+        if constexpr (C == Q4_K) {
+            rb[col * 32 + lane] = acc;
+        } else {
+            const float v = acc + __shfl_xor_sync(0xffffffffu, acc, 16);  // both block halves
+            if (lane < 16) rb[col * 32 + 16 * (warp >> 2) + lane] = v;
+        }
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            old = atomicAdd(dcnt + bi, 1);
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == CW - 1) {
+            __threadfence_block();
+            const int row = GLU ? (lane & 15) : lane;
+            const int n = T.tile * rows_out + row;
+            float v = 0.f, v2 = 0.f;
+#pragma unroll
+            for (int w = 0; w < KB; w++) {
+                v += rb[w * 32 + row];
+                if (GLU) v2 += rb[w * 32 + row + 16];
+            }
+            if (GLU) v = apply_act(a.act, v) * v2;
+            if (n < a.N && (!GLU || lane < 16))
+                store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
+            __syncwarp();
+            if (lane == 0) dcnt[bi] = 0;
+        }
+    };
+    if constexpr (DP) {
+        if (a.dyn) {
+            // dynamic whole tiles: the producer names each stage's tile in
+            // s_unit[slot]; a negative id ends the work
+            for (;;) {
+                int slot = it % NS;
+                wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2, (a.debug & 256) != 0);
+                const int unit = s_unit[slot];
+                if (unit < 0 || *s_abort) break;
+                Tile T;
+                tile_of(a, unit, tiles, T);
+                float acc = 0.f;
+                for (int st = 0; st < nst; st++, it++) {
+                    slot = it % NS;
+                    if (st) wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2, (a.debug & 256) != 0);
+                    dp_stage(slot, st * KB + col, acc);
+                }
+                if (!(a.debug & 32)) dp_store(T, acc, tix);
+                tix++;
+            }
+            // the last CTA out resets the work counters (zero on entry, left zero)
+            named_bar_sync(1, CW * 32);
+            if (ctid == 0) {
+                __threadfence();
+                if (atomicAdd(a.counters + 1, 1) == (int)gridDim.x - 1) {
+                    a.counters[0] = 0;
+                    a.counters[1] = 0;
+                }
+            }
+            return;
+        }
+    }
+    int64_t gt_next = lo / nst;
     while (i < hi) {
-        const int64_t gt = i / nst;
+        const int64_t gt = gt_next++;
         const int st0 = (int)(i - gt * nst);
         const int64_t tile_lo = gt * nst, tile_hi = tile_lo + nst;
         const int64_t end = min(hi, tile_hi);
@@ -800,21 +990,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         const int xtok = min(lane >> 2, T.m - 1);
         for (int st = st0; i < end; st++, i++, it++) {
             const int slot = it % NS;
-            wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2);
+            wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2, (a.debug & 256) != 0);
+            if ((a.debug & 128) && ctid == 0 && i == lo) stamps[2] = (unsigned)(clock64() - c_entry);
             const int col0 = DP ? col : col * BPW, b = st * KB + col0;
             if constexpr (DP) {
-                if (b < nb && !*s_abort && !(a.debug & 1)) {
-                    const uint8_t *stg = ring + slot * L::STAGE;
-                    const uint16_t *xs = reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK;
-                    if constexpr (C == Q4_K) {
-                        acc[0][0] += dp_q4k_block<F16>(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, xs,
-                                                       reinterpret_cast<uint32_t *>(stab), stab + 128);
-                    } else {
-                        const int r = 16 * (warp >> 2) + (lane & 15);
-                        acc[0][0] += dp_q6k_half<F16>(stg + r * L::SP + rowoff[slot * 32 + r] + col * bpb, lane >> 4,
-                                                      xs, reinterpret_cast<uint32_t *>(stab), stab + 128);
-                    }
-                }
+                dp_stage(slot, b, acc[0][0]);
+                continue;
             } else if (b < nb && !*s_abort && !(a.debug & 1)) {
                 const uint8_t *stg = ring + slot * L::STAGE;
                 const uint16_t *xr[NT];
@@ -840,43 +1021,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         }
 
         if (a.debug & 32) continue;  // development: skip the epilogue
-        if (XS) asm volatile("griddepcontrol.wait;" ::: "memory");  // before the first global write
         const bool whole = tile_lo >= lo && tile_hi <= hi;
         if constexpr (DP) {
             if (whole) {
-                // barrier-free: each warp posts its 32 row partials; the last of
-                // the KB warps to arrive sums them in column order and stores.
-                // Buffers rotate over NS+1 tiles, which the ring keeps apart.
-                const int bi = tix % (NS + 1);
-                float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (KB * 32);
-                if constexpr (C == Q4_K) {
-                    rb[col * 32 + lane] = acc[0][0];
-                } else {
-                    const float v = acc[0][0] + __shfl_xor_sync(0xffffffffu, acc[0][0], 16);  // both block halves
-                    if (lane < 16) rb[col * 32 + 16 * (warp >> 2) + lane] = v;
-                }
-                __syncwarp();
-                int old = 0;
-                if (lane == 0) {
-                    __threadfence_block();
-                    old = atomicAdd(dcnt + bi, 1);
-                }
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == CW - 1) {
-                    __threadfence_block();
-                    const int row = GLU ? (lane & 15) : lane;
-                    const int n = T.tile * rows_out + row;
-                    float v = 0.f, v2 = 0.f;
-#pragma unroll
-                    for (int w = 0; w < KB; w++) {
-                        v += rb[w * 32 + row];
-                        if (GLU) v2 += rb[w * 32 + row + 16];
-                    }
-                    if (GLU) v = apply_act(a.act, v) * v2;
-                    if (n < a.N && (!GLU || lane < 16)) store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
-                    __syncwarp();
-                    if (lane == 0) dcnt[bi] = 0;
-                }
+                dp_store(T, acc[0][0], tix);
                 tix++;
                 continue;
             }
@@ -960,6 +1108,17 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         // no trailing barrier: the next tile reduces into the other buffer, and
         // the tile after that passes this tile's reads at its own barrier
     }
+    if ((a.debug & 128) && ctid == 0) {  // development timing: per-CTA stamps into y (f32 output)
+        unsigned *o = reinterpret_cast<unsigned *>(a.y) + a.y_row_stride + 32 * blockIdx.x;  // row 1 of a 2-row f32 buffer
+        for (int q = 4; q < 16; q++) o[8 + q] = stamps[q];
+        o[0] = g_entry;
+        o[1] = stamps[0];
+        o[2] = stamps[1];
+        o[3] = stamps[2];
+        o[4] = (unsigned)(clock64() - c_entry);
+        o[5] = (unsigned)(hi - lo);
+        o[6] = (unsigned)globaltimer();
+    }
 }
 
 template <int C, int NT, bool F16, bool GLU, int XR>
@@ -972,8 +1131,12 @@ cudaError_t configure() {
     return e;
 }
 
+// Grid size and schedule.  Lane-per-row (one activation row) problems hand out
+// whole tiles dynamically when there are >= 2 per CTA, or give one whole tile
+// to each CTA when the tiles fit the GPU and a tile's stages fit the ring (no
+// split-K fixup).  Otherwise stream-K over (tile, stage) iterations.
 template <int C, int NT, bool F16, bool GLU, int XR>
-int grid_for(const GemvArgs &a) {
+int grid_for(const GemvArgs &a, int *dyn = nullptr) {
     using L = GLayout<C, NT, XR>;
     configure<C, NT, F16, GLU, XR>();
     int per_sm = 0;
@@ -983,9 +1146,18 @@ int grid_for(const GemvArgs &a) {
     const long tiles = (a.N + rows_out - 1) / rows_out;
     const long groups = a.dense_m > 0 ? (a.dense_m + 31) / 32 : a.max_groups;
     const long nst = (a.K / QK + L::KB - 1) / L::KB;
-    const long iters = groups * tiles * nst;
+    const long iters = groups * tiles * nst, units = groups * tiles;
     long cap = (long)num_sms() * per_sm;
     if (const char *g = getenv("KQ_GEMV_GRID")) cap = atol(g);  // development override
+    int d = 0;
+    if (L::DP && !getenv("KQ_GEMV_STATIC")) {
+        if (units >= 2 * cap) d = 1;
+        else if (units <= cap && nst <= L::NS) {
+            d = 1;
+            cap = units;
+        }
+    }
+    if (dyn) *dyn = d;
     return (int)(iters < cap ? iters : cap);
 }
 
@@ -994,12 +1166,18 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     using L = GLayout<C, NT, XR>;
     cudaError_t e = configure<C, NT, F16, GLU, XR>();
     if (e != cudaSuccess) return e;
-    const int grid = grid_for<C, NT, F16, GLU, XR>(a);
+    int dyn = 0;
+    const int grid = grid_for<C, NT, F16, GLU, XR>(a, &dyn);
     if (grid_out) {  // grid size query only: sizes the stream-K partial scratch
         *grid_out = grid;
         return cudaSuccess;
     }
     if (grid <= 0) return cudaSuccess;
+    {
+        const long tiles = (a.N + (GLU ? 16 : 32) - 1) / (GLU ? 16 : 32);
+        const long groups = a.dense_m > 0 ? (a.dense_m + 31) / 32 : a.max_groups;
+        if (groups * tiles > 0x7fffffffL) return cudaErrorInvalidValue;  // tile indices are 32-bit in the kernel
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(NTHREADS);
@@ -1010,7 +1188,9 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<C, NT, F16, GLU, XR>, a);
+    GemvArgs b = a;
+    b.dyn = dyn;
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<C, NT, F16, GLU, XR>, b);
 }
 
 template <int C, bool F16, bool GLU>

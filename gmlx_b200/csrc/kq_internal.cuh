@@ -54,6 +54,7 @@ struct GemvArgs {
     int *counters;   // one per (group, tile), zero on entry, left zero
     int *err;
     int max_tokens;  // upper bound of rows in any group (<= 32)
+    int dyn;         // set by the launcher: lane-per-row tiles handed out dynamically
     int debug;       // development only: 1 = skip decode, 2 = skip weight copies
 };
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st);
