@@ -81,7 +81,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int WBYTES = TROWS * SP;
     static constexpr int STAGE = WBYTES + XR * XSTR;
     // scale tables (MMA path) or per-warp quantized activations (lane-per-row path)
-    static constexpr int TABS = DP ? CW * 640 : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;
+    static constexpr int TABS = DP ? CW * 640 : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;  // per warp: 160 / TABW*BPW floats
     static constexpr int DPB = DP ? 4 * KB * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 <= 4)
     static constexpr bool SX = false;  // Q4_K one-row sums table (off: its per-launch prologue costs more than it saves)
     static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
@@ -708,7 +708,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             // dynamic whole tiles: the first tile of a CTA is its index, later ones
             // come from a work counter (read only after griddepcontrol.wait, so a
             // previous kernel has reset it), so CTAs that start late take fewer
-            const int units = n_groups * tiles;
+            const int S = a.ksplit, chunk = (nst + S - 1) / S;
+            const int units = n_groups * tiles * S;
             uint32_t it = 0;
             bool dep_done = false;
             for (int unit = blockIdx.x;;) {
@@ -722,7 +723,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                     break;
                 }
                 Tile T;
-                tile_of(a, unit, tiles, T);
+                tile_of(a, unit / S, tiles, T);
+                const int s0 = (unit % S) * chunk, s1 = min(nst, s0 + chunk);
                 const int orow = T.tile * rows_out + (GLU ? (lane & 15) : lane);
                 const bool up = GLU && lane >= 16;
                 const bool valid = orow < a.N;
@@ -730,7 +732,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                                          : a.w + (int64_t)T.e * a.w_expert_stride + (int64_t)orow * a.w_row_stride;
                 const uint8_t *xsrc =
                     reinterpret_cast<const uint8_t *>(a.x) + (int64_t)xrow_of(a, T, 0) * a.x_row_stride * 2;
-                for (int st = 0; st < nst; st++, it++) {
+                for (int st = s0; st < s1; st++, it++) {
                     const int slot = it % NS;
                     wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1);
                     const int bs = st * KB, nbk = min(KB, nb - bs);
@@ -835,7 +837,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     // Q4_K lane-per-row: warp = block column, lane = row.  Q6_K: warp =
     // (block column warp&3, 16-row half warp>>2), half-warp = block half.
     const int mt = (DP && C == Q4_K) ? 0 : (warp & 1), col = (DP && C == Q4_K) ? warp : (DP ? (warp & 3) : (warp >> 1));
-    float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * GCfg<C>::TABW * BPW;
+    // per-warp table: scales (MMA path) or quantized activations + their
+    // scales (lane-per-row path: 128 words + 32 floats = 640 bytes, as TABS)
+    float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * (DP ? 160 : GCfg<C>::TABW * BPW);
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
     // Consumers block here until the previous kernel on the stream has finished
     // (they need its activations anyway).  Polling the ring instead would burn
@@ -876,7 +880,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     // lane-per-row path, whole tile: barrier-free store.  Each warp posts its 32
     // row partials; the last of the KB warps to arrive sums them in column order
     // and stores.  Buffers rotate over NS+1 tiles, which the ring keeps apart.
-    auto dp_store = [&](const Tile &T, float acc, int tix) {
+    auto dp_store = [&](const Tile &T, float acc, int tix, int split_tile = -1, int chunk_id = 0) {
         const int bi = tix % (NS + 1);
         float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (KB * 32);
         if constexpr (C == Q4_K) {
@@ -897,13 +901,40 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             const int row = GLU ? (lane & 15) : lane;
             const int n = T.tile * rows_out + row;
             float v = 0.f, v2 = 0.f;
+            if (split_tile < 0) {
 #pragma unroll
-            for (int w = 0; w < KB; w++) {
-                v += rb[w * 32 + row];
-                if (GLU) v2 += rb[w * 32 + row + 16];
+                for (int w = 0; w < KB; w++) {
+                    v += rb[w * 32 + row];
+                    if (GLU) v2 += rb[w * 32 + row + 16];
+                }
+            } else {
+                // K split over ksplit units: post this unit's 32 row sums, the
+                // last unit of the tile adds them in chunk order and stores
+                float u = 0.f;
+#pragma unroll
+                for (int w = 0; w < KB; w++) u += rb[w * 32 + lane];
+                __stcg(a.partial + ((int64_t)split_tile * a.ksplit + chunk_id) * 32 + lane, u);
+                __syncwarp();
+                int prev = 0;
+                if (lane == 0) {
+                    __threadfence();
+                    prev = atomicAdd(a.counters + 2 + split_tile, 1);
+                    if (prev == a.ksplit - 1) __threadfence();
+                }
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == a.ksplit - 1) {
+                    for (int c = 0; c < a.ksplit; c++) {
+                        const float *pp = a.partial + ((int64_t)split_tile * a.ksplit + c) * 32;
+                        v += __ldcg(pp + row);
+                        if (GLU) v2 += __ldcg(pp + row + 16);
+                    }
+                    if (lane == 0) a.counters[2 + split_tile] = 0;
+                } else {
+                    split_tile = -2;  // not the last: nothing to store
+                }
             }
             if (GLU) v = apply_act(a.act, v) * v2;
-            if (n < a.N && (!GLU || lane < 16))
+            if (split_tile != -2 && n < a.N && (!GLU || lane < 16))
                 store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
             __syncwarp();
             if (lane == 0) dcnt[bi] = 0;
@@ -918,15 +949,17 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2, (a.debug & 256) != 0);
                 const int unit = s_unit[slot];
                 if (unit < 0 || *s_abort) break;
+                const int S = a.ksplit, chunk = (nst + S - 1) / S;
+                const int tile = unit / S, s0 = (unit % S) * chunk, s1 = min(nst, s0 + chunk);
                 Tile T;
-                tile_of(a, unit, tiles, T);
+                tile_of(a, tile, tiles, T);
                 float acc = 0.f;
-                for (int st = 0; st < nst; st++, it++) {
+                for (int st = s0; st < s1; st++, it++) {
                     slot = it % NS;
-                    if (st) wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2, (a.debug & 256) != 0);
+                    if (st > s0) wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2, (a.debug & 256) != 0);
                     dp_stage(slot, st * KB + col, acc);
                 }
-                if (!(a.debug & 32)) dp_store(T, acc, tix);
+                if (!(a.debug & 32)) dp_store(T, acc, tix, S > 1 ? tile : -1, unit % S);
                 tix++;
             }
             // the last CTA out resets the work counters (zero on entry, left zero)
@@ -1136,7 +1169,7 @@ cudaError_t configure() {
 // to each CTA when the tiles fit the GPU and a tile's stages fit the ring (no
 // split-K fixup).  Otherwise stream-K over (tile, stage) iterations.
 template <int C, int NT, bool F16, bool GLU, int XR>
-int grid_for(const GemvArgs &a, int *dyn = nullptr) {
+int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
     using L = GLayout<C, NT, XR>;
     configure<C, NT, F16, GLU, XR>();
     int per_sm = 0;
@@ -1149,15 +1182,25 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr) {
     const long iters = groups * tiles * nst, units = groups * tiles;
     long cap = (long)num_sms() * per_sm;
     if (const char *g = getenv("KQ_GEMV_GRID")) cap = atol(g);  // development override
-    int d = 0;
+    int d = 0, S = 1;
     if (L::DP && !getenv("KQ_GEMV_STATIC")) {
-        if (units >= 2 * cap) d = 1;
-        else if (units <= cap && nst <= L::NS) {
+        if (units >= 2 * cap) {
+            d = 1;
+        } else if (units <= cap && nst <= L::NS) {
             d = 1;
             cap = units;
+        } else if (getenv("KQ_GEMV_KSPLIT")) {
+            // split K into chunks so there are >= 2 units per CTA (off by default:
+            // each chunk's partial publish stalls its CTA on a gpu-scope fence,
+            // slower than stream-K's at most two partial tiles per CTA)
+            const long want = (2 * cap + units - 1) / units;
+            const long chunk = (nst + (want < nst ? want : nst) - 1) / (want < nst ? want : nst);
+            S = (int)((nst + chunk - 1) / chunk);
+            d = 1;
         }
     }
     if (dyn) *dyn = d;
+    if (ksplit) *ksplit = S;
     return (int)(iters < cap ? iters : cap);
 }
 
@@ -1166,8 +1209,8 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     using L = GLayout<C, NT, XR>;
     cudaError_t e = configure<C, NT, F16, GLU, XR>();
     if (e != cudaSuccess) return e;
-    int dyn = 0;
-    const int grid = grid_for<C, NT, F16, GLU, XR>(a, &dyn);
+    int dyn = 0, ksplit = 1;
+    const int grid = grid_for<C, NT, F16, GLU, XR>(a, &dyn, &ksplit);
     if (grid_out) {  // grid size query only: sizes the stream-K partial scratch
         *grid_out = grid;
         return cudaSuccess;
@@ -1190,6 +1233,7 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     cfg.numAttrs = 1;
     GemvArgs b = a;
     b.dyn = dyn;
+    b.ksplit = ksplit;
     return cudaLaunchKernelEx(&cfg, gemv_kernel<C, NT, F16, GLU, XR>, b);
 }
 
@@ -1231,7 +1275,7 @@ void gemv_scratch_need(const GemvArgs &a, size_t *partial_bytes, size_t *counter
     const long tiles = (a.N + rows_out - 1) / rows_out;
     const long groups = a.dense_m > 0 ? (a.dense_m + 31) / 32 : a.max_groups;
     *partial_bytes = (size_t)(2 * (long)(grid > 0 ? grid : 1)) * 1024 * sizeof(float);
-    *counter_bytes = (size_t)(groups * tiles) * sizeof(int);
+    *counter_bytes = (size_t)(groups * tiles + 2) * sizeof(int);  // + the dynamic-schedule work counters
 }
 
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st) { return dispatch(a, st, nullptr); }

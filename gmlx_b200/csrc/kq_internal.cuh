@@ -55,6 +55,7 @@ struct GemvArgs {
     int *err;
     int max_tokens;  // upper bound of rows in any group (<= 32)
     int dyn;         // set by the launcher: lane-per-row tiles handed out dynamically
+    int ksplit;      // set by the launcher: K chunks per dynamic unit (1 = whole tiles)
     int debug;       // development only: 1 = skip decode, 2 = skip weight copies
 };
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st);

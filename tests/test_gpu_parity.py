@@ -54,6 +54,34 @@ def test_quantized_matmul(cuda, codec, m, n, k):
     assert rel_err(y.float().cpu().numpy(), ref) <= TOL
 
 
+@pytest.mark.parametrize("codec,n,k", [
+    ("q4_k", 19200, 512),   # >= 2 tiles per CTA: whole tiles handed out dynamically
+    ("q4_k", 4096, 4096),   # one whole tile per CTA (stages fit the ring)
+    ("q4_k", 256, 8192),    # few tiles, long K: K split into dynamic chunks
+    ("q6_k", 512, 14336),   # Q6_K K split (unaligned 210-byte blocks)
+    ("q6_k", 6144, 1024),
+])
+@pytest.mark.parametrize("ksplit", [False, True])
+def test_one_row_schedules(cuda, codec, n, k, ksplit, monkeypatch):
+    """Decode (one activation row) schedules, each called three times in a row:
+    the work counters the dynamic schedule uses must come back to zero.
+    ksplit: dynamic K-chunk units instead of stream-K for few long tiles."""
+    if ksplit:
+        monkeypatch.setenv("KQ_GEMV_KSPLIT", "1")
+    w = synth.random_weight(codec, n, k, seed=9)
+    x = synth.random_activations(1, k, seed=10)
+    ref = O.matmul(x, w, codec)
+    wd, xd = torch.from_numpy(w).to(cuda), to_dev_x(x, cuda)
+    for _ in range(3):
+        y = kq.quantized_matmul(xd, wd, None, codec, out_dtype=torch.float32)
+        assert rel_err(y.cpu().numpy(), ref) <= TOL
+    wu = synth.random_weight(codec, n, k, seed=11)
+    g, u = ref.astype(np.float64), O.matmul(x, wu, codec).astype(np.float64)
+    h = kq.quantized_glu(xd, wd, torch.from_numpy(wu).to(cuda), codec, out_dtype=torch.float32)
+    assert rel_err(h.cpu().numpy(), g / (1 + np.exp(-g)) * u) <= TOL
+    assert kq.workspace_error() == 0
+
+
 @pytest.mark.parametrize("codec", CODECS)
 def test_quantized_matmul_f16_f32out(cuda, codec):
     w = synth.random_weight(codec, 128, 1024, seed=7)
