@@ -73,7 +73,7 @@ template <int C, bool DPL = false> __host__ __device__ constexpr int spitch_of()
 template <int C, int NT, int XR> struct GLayout {
     static constexpr bool XS = XR > 0;
     // lane-per-row integer dot-product path (one activation row, Q4_K)
-    static constexpr bool DP = XR == 1 && (C == Q4_K || C == Q6_K);
+    static constexpr bool DP = XR == 1;  // every codec has a lane-per-row path
     static constexpr int bpb = Fmt<C>::bpb;
     static constexpr int KB = KB_OF<C>;
     static constexpr int XSTR = XSTR_OF<C>;
@@ -634,6 +634,57 @@ __device__ __forceinline__ float dp_q6k_dot(const Q6Regs &r, int hf, const uint3
     return acc;
 }
 
+// Lane-per-row IQ2_XXS: the lane's 66-byte block (2-byte aligned) is read as
+// words with funnel shifts; each group of 8 weights becomes two words of
+// signed int8 (grid magnitude bytes, negated where the sign bit is set:
+// (g ^ 0xff) + 1 per byte, no carries as 1 <= g < 128) dotted against the
+// int16 activations with dp2a.  Per 32-weight sub-block:
+//     acc += d (0.5 + ls) / 4 * dx_j * sum_j(signed grid * x_q).
+struct IQ2Regs {
+    uint32_t q[16];
+    float d;
+};
+
+__device__ __forceinline__ void dp_iq2_load(const uint8_t *blk, IQ2Regs &r) {
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    uint32_t w[17];
+#pragma unroll
+    for (int i = 0; i < 17; i++) w[i] = aw[i];  // up to 2 bytes past the block: the ring row has slack
+    r.d = half_bits_to_float(__funnelshift_r(w[0], w[1], sh) & 0xffffu);
+    // qs word j = block bytes 2+4j .. 5+4j
+#pragma unroll
+    for (int j = 0; j < 16; j++) r.q[j] = sh ? w[j + 1] : __funnelshift_r(w[j], w[j + 1], 16);
+}
+
+__device__ __forceinline__ float dp_iq2_dot(const IQ2Regs &r, const uint32_t *xq, const float *xsc,
+                                           const uint2 *grid) {
+    float acc = 0.f;
+#pragma unroll
+    for (int sb = 0; sb < 8; sb++) {
+        const uint32_t a0 = r.q[2 * sb], a1 = r.q[2 * sb + 1];
+        int sum = 0;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint2 g = grid[(a0 >> (8 * l)) & 255u];
+            // sign bits -> byte flags (bit i at bit 8i) -> 0x00 / 0xff byte masks
+            // (arithmetic: a shared-memory table lookup per lane bank-conflicts)
+            const uint32_t sg = ksigns((a1 >> (7 * l)) & 127u);
+            const uint32_t f0 = ((sg & 15u) * 0x00204081u) & 0x01010101u, f1 = ((sg >> 4) * 0x00204081u) & 0x01010101u;
+            const int s0 = (int)((g.x ^ (f0 * 0xffu)) + f0), s1 = (int)((g.y ^ (f1 * 0xffu)) + f1);
+            const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 16 * sb + 4 * l);
+            sum = __dp2a_lo((int)xv.x, s0, sum);
+            sum = __dp2a_hi((int)xv.y, s0, sum);
+            sum = __dp2a_lo((int)xv.z, s1, sum);
+            sum = __dp2a_hi((int)xv.w, s1, sum);
+        }
+        acc = fmaf(r.d * (0.5f + (float)(a1 >> 28)) * 0.25f * xsc[sb], (float)sum, acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 // -------------------------------------------------------------------------
 
 template <int C, int NT, bool F16, bool GLU, int XR>
@@ -674,7 +725,13 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
         for (int b = 0; b <= NS; b++) reinterpret_cast<int *>(smem + L::OFF_MISC + 16)[b] = 0;
         fence_mbar_init();
     }
-    if constexpr (C == IQ2_XXS) {
+    if constexpr (C == IQ2_XXS && L::DP) {
+        // lane-per-row path: the raw magnitude bytes (256 x 8 B)
+        for (int e = threadIdx.x; e < 256; e += NTHREADS) {
+            const uint64_t v = c_iq2xxs_grid[e];
+            reinterpret_cast<uint2 *>(gridtab)[e] = make_uint2((uint32_t)v, (uint32_t)(v >> 32));
+        }
+    } else if constexpr (C == IQ2_XXS) {
         for (int e = threadIdx.x; e < 256; e += NTHREADS) {
             const uint64_t v = c_iq2xxs_grid[e];
             uint32_t w[4];
@@ -836,7 +893,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     constexpr int RCS = DP ? RED_TS : 8 * NT * RED_TS;       // their stride in the reduction buffer
     // Q4_K lane-per-row: warp = block column, lane = row.  Q6_K: warp =
     // (block column warp&3, 16-row half warp>>2), half-warp = block half.
-    const int mt = (DP && C == Q4_K) ? 0 : (warp & 1), col = (DP && C == Q4_K) ? warp : (DP ? (warp & 3) : (warp >> 1));
+    const int mt = (DP && C != Q6_K) ? 0 : (warp & 1), col = (DP && C != Q6_K) ? warp : (DP ? (warp & 3) : (warp >> 1));
     // per-warp table: scales (MMA path) or quantized activations + their
     // scales (lane-per-row path: 128 words + 32 floats = 640 bytes, as TABS)
     float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * (DP ? 160 : GCfg<C>::TABW * BPW);
@@ -875,6 +932,15 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q6k_dot(r, lane >> 4, xq, xsc);
+        } else {
+            IQ2Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_iq2_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_iq2_dot(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
         }
     };
     // lane-per-row path, whole tile: barrier-free store.  Each warp posts its 32
@@ -883,7 +949,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     auto dp_store = [&](const Tile &T, float acc, int tix, int split_tile = -1, int chunk_id = 0) {
         const int bi = tix % (NS + 1);
         float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (KB * 32);
-        if constexpr (C == Q4_K) {
+        if constexpr (C != Q6_K) {
             rb[col * 32 + lane] = acc;
         } else {
             const float v = acc + __shfl_xor_sync(0xffffffffu, acc, 16);  // both block halves
@@ -1064,7 +1130,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             tix++;
         }
         // ---- reduce the block columns: red[col][tok][row]
-        if constexpr (DP && C == Q4_K) {
+        if constexpr (DP && C != Q6_K) {
             red[col * RCS + lane] = acc[0][0];
         } else if constexpr (DP) {
             const float v = acc[0][0] + __shfl_xor_sync(0xffffffffu, acc[0][0], 16);
