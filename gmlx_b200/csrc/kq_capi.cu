@@ -122,7 +122,16 @@ GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k,
     return a;
 }
 
-bool use_gemm(int64_t m) { return m >= GEMM_MIN_M; }
+int gemm_min_m() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("KQ_GEMM_MIN_M");  // development override of the GEMV/GEMM crossover
+        v = e ? atoi(e) : GEMM_MIN_M;
+    }
+    return v;
+}
+
+bool use_gemm(int64_t m) { return m >= gemm_min_m(); }
 
 size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
     if (use_gemm(m)) return plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0).total;
