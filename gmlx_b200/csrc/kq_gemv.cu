@@ -82,7 +82,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int STAGE = WBYTES + XR * XSTR;
     // scale tables (MMA path) or per-warp quantized activations (lane-per-row path)
     static constexpr int TABS = DP ? CW * 640 : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;  // per warp: 160 / TABW*BPW floats
-    static constexpr int DPB = DP ? 4 * KB * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 <= 4)
+    static constexpr int DPB = DP ? 4 * CW * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 <= 4), one row per warp
     static constexpr bool SX = false;  // Q4_K one-row sums table (off: its per-launch prologue costs more than it saves)
     static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
     static constexpr int REDB = NCOL * 8 * NT * RED_TS * 4;  // one reduction buffer (two, alternating)
@@ -604,6 +604,54 @@ __device__ __forceinline__ void dp_q6k_load(const uint8_t *blk, int hf, Q6Regs &
     r.d = half_bits_to_float(lds_w2(aw, 52, sh) & 0xffffu);                 // bytes 208-209
 }
 
+// Half-block loader for the row-per-lane mapping: 32 lanes read 32 rows at the
+// same column, so when the rows' offsets agree (rows at a 16-byte multiple
+// stride: every contiguous matrix) the half-block is read with 16-byte loads
+// (conflict-free at the ring's row pitch) and realigned with funnel shifts by
+// a warp-uniform amount; otherwise the word-by-word loader.
+template <int Q>
+__device__ __forceinline__ void q6_realign(const uint32_t (&cl)[20], const uint32_t (&ch)[12], uint32_t sh, Q6Regs &r) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) r.ql[i] = __funnelshift_r(cl[Q + i], cl[Q + i + 1], sh);
+#pragma unroll
+    for (int i = 0; i < 8; i++) r.qh[i] = __funnelshift_r(ch[Q + i], ch[Q + i + 1], sh);
+}
+
+__device__ __forceinline__ void dp_q6k_load_rows(const uint8_t *blk, int hf, Q6Regs &r) {
+    const uint32_t o = (uint32_t)(uintptr_t)blk & 15u;
+    const uint32_t o0 = __shfl_sync(0xffffffffu, o, 0);
+    if (!__all_sync(0xffffffffu, o == o0)) {
+        dp_q6k_load(blk, hf, r);
+        return;
+    }
+    const uint4 *bl = reinterpret_cast<const uint4 *>(((uintptr_t)blk + 64 * hf) & ~(uintptr_t)15);
+    const uint4 *bh = reinterpret_cast<const uint4 *>(((uintptr_t)blk + 128 + 32 * hf) & ~(uintptr_t)15);
+    uint32_t cl[20], ch[12];
+#pragma unroll
+    for (int i = 0; i < 5; i++) {
+        const uint4 v = bl[i];
+        cl[4 * i] = v.x, cl[4 * i + 1] = v.y, cl[4 * i + 2] = v.z, cl[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const uint4 v = bh[i];
+        ch[4 * i] = v.x, ch[4 * i + 1] = v.y, ch[4 * i + 2] = v.z, ch[4 * i + 3] = v.w;
+    }
+    const uint32_t sh = (o & 3u) * 8u;
+    switch (o >> 2) {  // warp-uniform
+    case 0: q6_realign<0>(cl, ch, sh, r); break;
+    case 1: q6_realign<1>(cl, ch, sh, r); break;
+    case 2: q6_realign<2>(cl, ch, sh, r); break;
+    default: q6_realign<3>(cl, ch, sh, r); break;
+    }
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t s2 = (uint32_t)(ab & 3) * 8;
+    r.scw0 = lds_w2(aw, 48 + 2 * hf, s2);  // int8 scales 8hf..8hf+7
+    r.scw1 = lds_w2(aw, 49 + 2 * hf, s2);
+    r.d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk + 208));
+}
+
 __device__ __forceinline__ float dp_q6k_dot(const Q6Regs &r, int hf, const uint32_t *xq, const float *xsc) {
     float acc = 0.f;
 #pragma unroll
@@ -698,7 +746,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     uint8_t *rowoff = smem + L::OFF_ROWOFF;
     volatile int *s_abort = reinterpret_cast<volatile int *>(smem + L::OFF_MISC);
     int *s_last = reinterpret_cast<int *>(smem + L::OFF_MISC + 4);
-    int *s_unit = reinterpret_cast<int *>(smem + L::OFF_UNIT);
+    int *s_unit = reinterpret_cast<int *>(smem + L::OFF_UNIT);  // NS <= 8 ints
+    int *s_npub = s_unit + 8, *s_pub = s_unit + 9;               // deferred K-chunk publishes
+    constexpr int MAXPUB = 23;
     uint4 *gridtab = reinterpret_cast<uint4 *>(smem + L::OFF_GRID);
     uint8_t *ring = smem + L::OFF_RING;
     float *red0 = reinterpret_cast<float *>(smem + L::OFF_RED);
@@ -722,6 +772,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             mbar_init(&empty[i], CW);
         }
         *s_abort = 0;
+        *s_npub = 0;
         for (int b = 0; b <= NS; b++) reinterpret_cast<int *>(smem + L::OFF_MISC + 16)[b] = 0;
         fence_mbar_init();
     }
@@ -889,7 +940,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     // ---------------- consumer warps: warp -> (16-row half mt, block column col) ----------------
     // (lane-per-row path: warp -> block column, lane -> row)
     constexpr bool DP = L::DP;
-    constexpr int RCOLS = DP ? KB : NCOL;                    // partial sums per row to reduce
+    constexpr int RCOLS = DP ? CW : NCOL;                    // partial sums per row to reduce
     constexpr int RCS = DP ? RED_TS : 8 * NT * RED_TS;       // their stride in the reduction buffer
     // Q4_K lane-per-row: warp = block column, lane = row.  Q6_K: warp =
     // (block column warp&3, 16-row half warp>>2), half-warp = block half.
@@ -923,15 +974,16 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q4k_dot(r, xq, xsc);
         } else if constexpr (C == Q6_K) {
-            const int rr = 16 * (warp >> 2) + (lane & 15);
+            // lane = row, warp = (block column warp&3, block half warp>>2)
+            const int hf = warp >> 2;
             Q6Regs r;
             if (run) {
                 dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
-                dp_q6k_load(stg + rr * L::SP + rowoff[slot * 32 + rr] + col * bpb, lane >> 4, r);
+                dp_q6k_load_rows(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, hf, r);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q6k_dot(r, lane >> 4, xq, xsc);
+            if (run) acc += dp_q6k_dot(r, hf, xq, xsc);
         } else {
             IQ2Regs r;
             if (run) {
@@ -948,13 +1000,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
     // and stores.  Buffers rotate over NS+1 tiles, which the ring keeps apart.
     auto dp_store = [&](const Tile &T, float acc, int tix, int split_tile = -1, int chunk_id = 0) {
         const int bi = tix % (NS + 1);
-        float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (KB * 32);
-        if constexpr (C != Q6_K) {
-            rb[col * 32 + lane] = acc;
-        } else {
-            const float v = acc + __shfl_xor_sync(0xffffffffu, acc, 16);  // both block halves
-            if (lane < 16) rb[col * 32 + 16 * (warp >> 2) + lane] = v;
-        }
+        float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (CW * 32);
+        rb[warp * 32 + lane] = acc;
         __syncwarp();
         int old = 0;
         if (lane == 0) {
@@ -969,7 +1016,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             float v = 0.f, v2 = 0.f;
             if (split_tile < 0) {
 #pragma unroll
-                for (int w = 0; w < KB; w++) {
+                for (int w = 0; w < CW; w++) {
                     v += rb[w * 32 + row];
                     if (GLU) v2 += rb[w * 32 + row + 16];
                 }
@@ -978,17 +1025,26 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 // last unit of the tile adds them in chunk order and stores
                 float u = 0.f;
 #pragma unroll
-                for (int w = 0; w < KB; w++) u += rb[w * 32 + lane];
+                for (int w = 0; w < CW; w++) u += rb[w * 32 + lane];
                 __stcg(a.partial + ((int64_t)split_tile * a.ksplit + chunk_id) * 32 + lane, u);
                 __syncwarp();
-                int prev = 0;
+                // defer the publish to the CTA's end (one fence for all its
+                // chunks, off the ring's critical path); immediate if the list is full
+                int k = 0;
                 if (lane == 0) {
+                    k = atomicAdd(s_npub, 1);
+                    if (k < MAXPUB) s_pub[k] = split_tile;
+                }
+                k = __shfl_sync(0xffffffffu, k, 0);
+                if (k < MAXPUB) split_tile = -2;
+                int prev = 0;
+                if (split_tile >= 0 && lane == 0) {
                     __threadfence();
                     prev = atomicAdd(a.counters + 2 + split_tile, 1);
                     if (prev == a.ksplit - 1) __threadfence();
                 }
                 prev = __shfl_sync(0xffffffffu, prev, 0);
-                if (prev == a.ksplit - 1) {
+                if (split_tile >= 0 && prev == a.ksplit - 1) {
                     for (int c = 0; c < a.ksplit; c++) {
                         const float *pp = a.partial + ((int64_t)split_tile * a.ksplit + c) * 32;
                         v += __ldcg(pp + row);
@@ -1027,6 +1083,36 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
                 }
                 if (!(a.debug & 32)) dp_store(T, acc, tix, S > 1 ? tile : -1, unit % S);
                 tix++;
+            }
+            // publish the deferred K-chunk partials: each warp fences its own
+            // partial stores, then the chunks' tile counters are bumped; the
+            // last chunk of a tile sums the partials in chunk order and stores
+            __threadfence();
+            named_bar_sync(1, CW * 32);
+            const int npub = min(*s_npub, MAXPUB);
+            for (int q = warp; q < npub; q += CW) {
+                const int t = s_pub[q];
+                int prev = 0;
+                if (lane == 0) {
+                    prev = atomicAdd(a.counters + 2 + t, 1);
+                    if (prev == a.ksplit - 1) __threadfence();
+                }
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev != a.ksplit - 1) continue;
+                Tile T;
+                tile_of(a, t, tiles, T);
+                const int row = GLU ? (lane & 15) : lane;
+                const int n = T.tile * rows_out + row;
+                float v = 0.f, v2 = 0.f;
+                for (int c = 0; c < a.ksplit; c++) {
+                    const float *pp = a.partial + ((int64_t)t * a.ksplit + c) * 32;
+                    v += __ldcg(pp + row);
+                    if (GLU) v2 += __ldcg(pp + row + 16);
+                }
+                if (GLU) v = apply_act(a.act, v) * v2;
+                if (n < a.N && (!GLU || lane < 16))
+                    store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
+                if (lane == 0) a.counters[2 + t] = 0;
             }
             // the last CTA out resets the work counters (zero on entry, left zero)
             named_bar_sync(1, CW * 32);
@@ -1130,11 +1216,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_kernel(const GemvArgs a) {
             tix++;
         }
         // ---- reduce the block columns: red[col][tok][row]
-        if constexpr (DP && C != Q6_K) {
-            red[col * RCS + lane] = acc[0][0];
-        } else if constexpr (DP) {
-            const float v = acc[0][0] + __shfl_xor_sync(0xffffffffu, acc[0][0], 16);
-            if (lane < 16) red[col * RCS + 16 * (warp >> 2) + lane] = v;
+        if constexpr (DP) {
+            red[warp * RCS + lane] = acc[0][0];
         } else {
             const int g = lane >> 2, t = lane & 3;
             float *r = red + col * 8 * NT * RED_TS;

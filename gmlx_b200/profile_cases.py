@@ -1,0 +1,66 @@
+"""Small, fixed invocations of single kq ops for profiler captures.
+
+    python -m gmlx_b200.profile_cases <case> [launches]
+
+Each case builds seeded synthetic weights (the bench's shapes), runs the op
+`launches` times (default 3) on cuda:0 and synchronizes.  Cases:
+  glu_m1        fused gate/up GEMV, Q4_K 14336x4096 (x2), one activation row
+  down_m1       Q6_K 4096x14336 GEMV, one row
+  iq2_m1        IQ2_XXS 2048x7168 GEMV, one row (DeepSeek-like expert)
+  prefill_glu   fused gate/up tcgen05 GEMM, Q4_K 14336x4096 (x2), M=2048
+  prefill_down  Q6_K 4096x14336 GEMM, M=2048
+  moe_prefill   Qwen3-like expert layer, T=512 (grouped GEMM path)
+"""
+import sys
+
+import torch
+
+from . import kq, synth
+
+
+def _w(codec, n, k, seed, experts=None):
+    return torch.from_numpy(synth.random_weight(codec, n, k, seed=seed, experts=experts)).cuda()
+
+
+def _x(m, k):
+    return torch.randn(m, k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(0)).to(torch.bfloat16)
+
+
+def build(case):
+    if case == "glu_m1":
+        g, u, x = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _x(1, 4096)
+        return lambda: kq.quantized_glu(x, g, u, "q4_k", act="silu")
+    if case == "down_m1":
+        w, x = _w("q6_k", 4096, 14336, 3), _x(1, 14336)
+        return lambda: kq.quantized_matmul(x, w, None, "q6_k")
+    if case == "iq2_m1":
+        w, x = _w("iq2_xxs", 2048, 7168, 4), _x(1, 7168)
+        return lambda: kq.quantized_matmul(x, w, None, "iq2_xxs")
+    if case == "prefill_glu":
+        g, u, x = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _x(2048, 4096)
+        return lambda: kq.quantized_glu(x, g, u, "q4_k", act="silu")
+    if case == "prefill_down":
+        w, x = _w("q6_k", 4096, 14336, 3), _x(2048, 14336)
+        return lambda: kq.quantized_matmul(x, w, None, "q6_k")
+    if case == "moe_prefill":
+        e, k, d, f, t = 128, 8, 2048, 768, 512
+        wg, wu, wd = _w("q4_k", f, d, 11, e), _w("q4_k", f, d, 12, e), _w("q6_k", d, f, 13, e)
+        x = _x(t, d)
+        logits = torch.randn(t, e, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+        idx, sc = kq.moe_router_topk(logits, k, True)
+        return lambda: kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, "q4_k", "q6_k", 0, e)
+    raise SystemExit(f"unknown case {case!r}; see the module docstring")
+
+
+def main(argv):
+    if not argv:
+        raise SystemExit(__doc__)
+    fn = build(argv[0])
+    for _ in range(int(argv[1]) if len(argv) > 1 else 3):
+        fn()
+    torch.cuda.synchronize()
+    print("ok", argv[0])
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
