@@ -1379,7 +1379,7 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = getenv("KQ_GEMV_NOPDL") ? 0 : 1;  // development switch
     GemvArgs b = a;
     b.dyn = dyn;
     b.ksplit = ksplit;
