@@ -244,8 +244,10 @@ __global__ void __launch_bounds__(GT, 1)
             uint4 nh = __ldg(reinterpret_cast<const uint4 *>(row));
             uint4 n0c = __ldg(reinterpret_cast<const uint4 *>(row + 16));
             uint4 n1c = __ldg(reinterpret_cast<const uint4 *>(row + 32));
-            for (int s = 0; s < nk; s++) {
-                const int slot = s % NSTAGE, b = s >> 2, q = s & 3;
+            for (int s0 = 0; s0 < nk; s0 += 4)  // nk is a multiple of 4 (K % 256 == 0)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {  // static q: dsc2[] / ndm2[] stay in registers
+                const int s = s0 + q, slot = s % NSTAGE;
                 const uint4 hcur = nh, c0 = n0c, c1 = n1c;
                 if (s + 1 < nk) {
                     const int b1 = (s + 1) >> 2, q1 = (s + 1) & 3;
@@ -316,8 +318,10 @@ __global__ void __launch_bounds__(GT, 1)
                         reinterpret_cast<float4 *>(yp)[v] =
                             make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
                                         __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-                } else {
-                    for (int v = 0; v < 32 && nb + v < a.N; v++) yp[v] = __uint_as_float(r[v]);
+                } else {  // ragged edge (static indices keep r[] in registers)
+#pragma unroll
+                    for (int v = 0; v < 32; v++)
+                        if (nb + v < a.N) yp[v] = __uint_as_float(r[v]);
                 }
             } else {
                 const bool of16 = a.y_dtype == F16;
@@ -332,8 +336,10 @@ __global__ void __launch_bounds__(GT, 1)
 #pragma unroll
                     for (int v = 0; v < 4; v++)
                         reinterpret_cast<uint4 *>(yp)[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-                } else {
-                    for (int v = 0; v < 32 && nb + v < a.N; v++) yp[v] = (uint16_t)(pk[v >> 1] >> (16 * (v & 1)));
+                } else {  // ragged edge (static indices keep pk[] in registers)
+#pragma unroll
+                    for (int v = 0; v < 32; v++)
+                        if (nb + v < a.N) yp[v] = (uint16_t)(pk[v >> 1] >> (16 * (v & 1)));
                 }
             }
         }
