@@ -179,6 +179,8 @@ def time_graph(torch, fn, steps, warmup, stream, min_warm_s=0.0):
     return a.elapsed_time(b) / 1e3  # seconds for `steps` replays
 
 
+GLU_LAUNCH_DRAM_BYTES = 66_643_712  # ncu: fused gate/up GEMV, Q4_K 2 x 14336 x 4096, M = 1
+
 MOE_CONFIGS = (
     # (name, experts, top_k, hidden, ffn, gate/up codec, down codec, token counts)
     ("qwen3-30b-a3b-like", 128, 8, 2048, 768, "q4_k", "q6_k", (1, 64, 4096)),
@@ -418,7 +420,12 @@ def main():
             "moe": moe,
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K, GLU> (gate+up 14336x4096)",
                          "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None},
+                         "frac": achieved / hbm_peak,
+                         # dram__bytes_read.sum + dram__bytes_write.sum of this launch at this
+                         # shape from an ncu capture (66.14 MB read + 0.51 MB written); the
+                         # algorithmic bytes are 66.07 MB
+                         "traffic": GLU_LAUNCH_DRAM_BYTES if (world == 1 and args.m == 1) else None,
+                         "traffic_unit": "bytes per launch"},
             "cpu_baseline": cpu,
             "e2e": {"value": nbytes / e2e_t / 1e9, "unit": UNIT,
                     "h2d_bytes_per_step": int(hx.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2)},
