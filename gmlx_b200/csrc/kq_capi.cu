@@ -460,6 +460,66 @@ int kq_quantized_matmul(int codec, const void *x, int x_dtype, int64_t m, int64_
                      y_row_stride, workspace, workspace_bytes, stream, "quantized_matmul");
 }
 
+size_t kq_allreduce_buffer_bytes(int world, int64_t n) {
+    return (world < 1 || n < 1) ? 0 : ar_buffer_bytes(world, n);
+}
+
+int kq_quantized_matmul_allreduce(int codec, const void *x, int x_dtype, int64_t k, const void *w, int64_t n,
+                                  int64_t w_row_stride, void *y, int y_dtype, int world, int rank,
+                                  void *const *comm_bufs, void *workspace, size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    const char *what = "quantized_matmul_allreduce";
+    int rc;
+    if ((rc = check_weights(codec, w, k, w_row_stride, what))) return rc;
+    if ((rc = check_x(x, x_dtype, k, what))) return rc;
+    if (!out_dtype_ok(y_dtype)) return fail(KQ_ERR_DTYPE, "%s: bad output dtype %d", what, y_dtype);
+    if (n <= 0 || n > 0x7fffffff || k > 0x7fffffff) return fail(KQ_ERR_SHAPE, "%s: bad sizes n=%lld", what, (long long)n);
+    if (world < 1 || world > 64 || rank < 0 || rank >= world || !comm_bufs)
+        return fail(KQ_ERR_SHAPE, "%s: bad world %d / rank %d / buffers", what, world, rank);
+    GemvArgs a = dense_args(codec, x, x_dtype, 1, k, k, w, nullptr, n, w_row_stride, y, y_dtype, n, ACT_NONE);
+    a.ar_bufs = reinterpret_cast<unsigned char *const *>(comm_bufs);
+    a.ar_world = world;
+    a.ar_rank = rank;
+    size_t pb, cb;
+    gemv_scratch_need(a, &pb, &cb);
+    const WsPlan p = plan(0, 0, cb, pb);
+    if (cb > CNT_RESERVE) return fail(KQ_ERR_SHAPE, "%s: too many output tiles (%zu counter bytes)", what, cb);
+    if (!workspace || workspace_bytes < p.total || ((uintptr_t)workspace & 255))
+        return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total,
+                    workspace_bytes);
+    a.err = (int *)workspace;
+    a.counters = (int *)((char *)workspace + p.cnt_off);
+    a.partial = (float *)((char *)workspace + p.part_off);
+    return cuda_status(launch_gemv(a, (cudaStream_t)stream), what);
+}
+
+int kq_comm_alloc(size_t bytes, void **ptr) {
+    g_msg[0] = 0;
+    if (!ptr || !bytes) return fail(KQ_ERR_SHAPE, "comm_alloc: bad arguments");
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    return cuda_status(e, "comm_alloc");
+}
+
+int kq_comm_free(void *ptr) { return cuda_status(cudaFree(ptr), "comm_free"); }
+
+int kq_ipc_handle(const void *ptr, void *handle64) {
+    g_msg[0] = 0;
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(ptr));
+    if (e == cudaSuccess) memcpy(handle64, &h, sizeof(h));
+    return cuda_status(e, "ipc_handle");
+}
+
+int kq_ipc_open(const void *handle64, void **ptr) {
+    g_msg[0] = 0;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "ipc_open");
+}
+
+int kq_ipc_close(void *ptr) { return cuda_status(cudaIpcCloseMemHandle(ptr), "ipc_close"); }
+
 size_t kq_quantized_glu_workspace_size(int codec, int64_t m, int64_t n, int64_t k) {
     if (!codec_ok(codec) || k <= 0 || k % QK || n <= 0 || m <= 0) return 256;
     return dense_ws(codec, m, n, k, ACT_SILU);

@@ -998,6 +998,19 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<NT>) gemv_kernel(const G
             if (run) acc += dp_iq2_dot(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
         }
     };
+    // final value of output n of tile T: to y, or (fused all-reduce) as this
+    // rank's f32 partial into every rank's communication buffer
+    const unsigned ar_epoch = a.ar_world ? *reinterpret_cast<volatile unsigned *>(a.ar_bufs[a.ar_rank]) : 0u;
+    const int ar_par = (int)(ar_epoch & 1u);
+    auto emit = [&](const Tile &T, int n, float v) {
+        if (a.ar_world == 0) {
+            store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
+            return;
+        }
+        const int64_t off = ((int64_t)(ar_par * a.ar_world + a.ar_rank)) * a.N + n;
+        for (int p = 0; p < a.ar_world; p++)
+            reinterpret_cast<float *>(a.ar_bufs[p] + AR_HDR)[off] = v;
+    };
     // lane-per-row path, whole tile: barrier-free store.  Each warp posts its 32
     // row partials; the last of the KB warps to arrive sums them in column order
     // and stores.  Buffers rotate over NS+1 tiles, which the ring keeps apart.
@@ -1059,8 +1072,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<NT>) gemv_kernel(const G
                 }
             }
             if (GLU) v = apply_act(a.act, v) * v2;
-            if (split_tile != -2 && n < a.N && (!GLU || lane < 16))
-                store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
+            if (split_tile != -2 && n < a.N && (!GLU || lane < 16)) emit(T, n, v);
             __syncwarp();
             if (lane == 0) dcnt[bi] = 0;
         }
@@ -1113,17 +1125,55 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<NT>) gemv_kernel(const G
                     if (GLU) v2 += __ldcg(pp + row + 16);
                 }
                 if (GLU) v = apply_act(a.act, v) * v2;
-                if (n < a.N && (!GLU || lane < 16))
-                    store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
+                if (n < a.N && (!GLU || lane < 16)) emit(T, n, v);
                 if (lane == 0) a.counters[2 + t] = 0;
             }
-            // the last CTA out resets the work counters (zero on entry, left zero)
+            // the last CTA out resets the work counters (zero on entry, left zero);
+            // with the fused all-reduce it also raises this rank's flag on every peer
+            if (a.ar_world) __threadfence_system();  // this CTA's partial stores, all peers
             named_bar_sync(1, CW * 32);
             if (ctid == 0) {
                 __threadfence();
                 if (atomicAdd(a.counters + 1, 1) == (int)gridDim.x - 1) {
                     a.counters[0] = 0;
                     a.counters[1] = 0;
+                    if (a.ar_world) {
+                        __threadfence_system();
+                        const unsigned next = ar_epoch + 1u;
+                        for (int p = 0; p < a.ar_world; p++) {
+                            unsigned *f = reinterpret_cast<unsigned *>(a.ar_bufs[p] + 64) + ar_par * a.ar_world + a.ar_rank;
+                            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(next) : "memory");
+                        }
+                        *reinterpret_cast<volatile unsigned *>(a.ar_bufs[a.ar_rank]) = next;  // own epoch
+                    }
+                }
+            }
+            if (a.ar_world) {
+                // wait (bounded) for every rank's flag of this call, then sum this
+                // CTA's slice of the outputs over ranks in rank order
+                if (ctid < a.ar_world) {
+                    const unsigned *f = reinterpret_cast<const unsigned *>(a.ar_bufs[a.ar_rank] + 64) + ar_par * a.ar_world + ctid;
+                    const uint64_t t0 = globaltimer();
+                    for (uint32_t it2 = 0;; it2++) {
+                        unsigned v;
+                        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                        if (v == ar_epoch + 1u) break;
+                        if ((it2 & 255) == 255 && globaltimer() - t0 > 2000000000ull) {
+                            atomicCAS(a.err, 0, 7);  // a peer never signalled
+                            *s_abort = 1;
+                            break;
+                        }
+                    }
+                }
+                named_bar_sync(1, CW * 32);
+                if (*s_abort) return;
+                const float *slots = reinterpret_cast<const float *>(a.ar_bufs[a.ar_rank] + AR_HDR) +
+                                     (int64_t)ar_par * a.ar_world * a.N;
+                const int per = (a.N + gridDim.x - 1) / gridDim.x;
+                for (int n = blockIdx.x * per + ctid; n < min(a.N, (int)(blockIdx.x + 1) * per); n += CW * 32) {
+                    float v = 0.f;
+                    for (int r = 0; r < a.ar_world; r++) v += __ldcv(slots + (int64_t)r * a.N + n);
+                    store_out(a.y, a.y_dtype, n, v);
                 }
             }
             return;
@@ -1341,7 +1391,7 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
         } else if (units <= cap && nst <= L::NS) {
             d = 1;
             cap = units;
-        } else if (getenv("KQ_GEMV_KSPLIT")) {
+        } else if (getenv("KQ_GEMV_KSPLIT") || a.ar_world) {
             // split K into chunks so there are >= 2 units per CTA (off by default:
             // each chunk's partial publish stalls its CTA on a gpu-scope fence,
             // slower than stream-K's at most two partial tiles per CTA)
@@ -1379,10 +1429,18 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     cfg.dynamicSmemBytes = L::BYTES;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (a.ar_world) {
+        // fused all-reduce: every CTA waits for the last one, so all must be
+        // resident at once (cooperative launch; no early start either)
+        if (!L::DP || !dyn) return cudaErrorInvalidValue;
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+    } else {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = getenv("KQ_GEMV_NOPDL") ? 0 : 1;  // development switch
+    cfg.numAttrs = (getenv("KQ_GEMV_NOPDL") && !a.ar_world) ? 0 : 1;  // development switch
     GemvArgs b = a;
     b.dyn = dyn;
     b.ksplit = ksplit;

@@ -54,11 +54,22 @@ struct GemvArgs {
     int *counters;   // one per (group, tile), zero on entry, left zero
     int *err;
     int max_tokens;  // upper bound of rows in any group (<= 32)
+    // fused all-reduce (row-parallel decode, one activation row): every rank
+    // stores its f32 partial rows into each peer's communication buffer, then
+    // sums all ranks' partials into y.  ar_bufs: device array [ar_world] of the
+    // buffers (this rank's own at [ar_rank]); ar_world == 0: plain output.
+    unsigned char *const *ar_bufs;
+    int ar_world, ar_rank;
     int dyn;         // set by the launcher: lane-per-row tiles handed out dynamically
     int ksplit;      // set by the launcher: K chunks per dynamic unit (1 = whole tiles)
     int debug;       // development only: 1 = skip decode, 2 = skip weight copies
 };
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st);
+// Communication buffer of the fused all-reduce: a 4 KB header (word 0: this
+// rank's call epoch; flags at 64 + 4 * (parity * world + rank)) and f32 slots
+// [parity][world][n] from byte 4096.
+constexpr size_t AR_HDR = 4096;
+inline size_t ar_buffer_bytes(int world, int64_t n) { return AR_HDR + (size_t)2 * world * n * sizeof(float); }
 // Scratch the GEMV needs for `a` (bytes of f32 partials, bytes of counters).
 void gemv_scratch_need(const GemvArgs &a, size_t *partial_bytes, size_t *counter_bytes);
 

@@ -39,7 +39,7 @@ from .synth import BLOCK_BYTES, CODECS, QK, codec_id
 __all__ = [
     "codecs", "codec_has_matmul", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
     "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
-    "moe_expert_layer_local",
+    "moe_expert_layer_local", "quantized_matmul_allreduce",
 ]
 
 _DT = {torch.float32: _lib.KQ_F32, torch.float16: _lib.KQ_F16, torch.bfloat16: _lib.KQ_BF16}
@@ -187,6 +187,33 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, 
         ws = _workspace(x.device, L.kq_quantized_matmul_workspace_size(c, m, n, k))
         _lib.check(L.kq_quantized_matmul(c, _p(x2), _DT[x2.dtype], m, k, x2.stride(0), _p(w), n, wstride, _p(y),
                                          _DT[od], n, _p(ws), ws.numel(), _stream(x.device)), "quantized_matmul")
+    return y.reshape(*x.shape[:-1], n)
+
+
+def quantized_matmul_allreduce(x: torch.Tensor, w: torch.Tensor, codec, comm,
+                               out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Row-parallel decode projection with the cross-rank sum fused in: this
+    rank's ``x @ dequant(w_shard).T`` for one activation row, summed over the
+    ranks of ``comm`` (a ``gmlx_b200.parallel.PeerComm``) inside the kernel.
+    Every rank gets the same bits.  Stands for ``quantized_matmul`` on a K
+    shard followed by ``all_sum`` (gmlx/hy_v3_model.py:259)."""
+    c = _cid(codec)
+    _need_cuda(x, w)
+    k = _wire_k(w, c)
+    w, wstride = _rows2d(w)
+    n = w.shape[-2]
+    x2 = _act_2d(x, k)
+    if x2.shape[0] != 1:
+        raise ValueError("quantized_matmul_allreduce: one activation row (decode)")
+    if n > comm.n:
+        raise ValueError(f"quantized_matmul_allreduce: {n} outputs exceed the communication buffer ({comm.n})")
+    od = out_dtype or x.dtype
+    y = torch.empty(1, n, dtype=od, device=x.device)
+    L = _lib.load()
+    ws = _workspace(x.device, L.kq_quantized_matmul_workspace_size(c, 1, n, k))
+    _lib.check(L.kq_quantized_matmul_allreduce(c, _p(x2), _DT[x2.dtype], k, _p(w), n, wstride, _p(y), _DT[od],
+                                               comm.world, comm.rank, _p(comm.table), _p(ws), ws.numel(),
+                                               _stream(x.device)), "quantized_matmul_allreduce")
     return y.reshape(*x.shape[:-1], n)
 
 

@@ -77,21 +77,77 @@ class TPDecoderMLP:
     ranks; gate/up/SiLU on this rank's FFN slice and the down projection summed
     over ranks.  (Attention itself is outside the quantized-matmul path.)"""
 
-    def __init__(self, shards: dict, group=None, codecs=("q4_k", "q6_k")):
+    def __init__(self, shards: dict, group=None, codecs=("q4_k", "q6_k"), comm: "PeerComm | None" = None):
         self.s = shards
         self.group = group
         self.cg, self.cd = codecs
+        self.comm = comm
 
     def forward(self, x, attn_local):
         from . import kq
         qkv = kq.quantized_matmul(x, self.s["qkv"], None, self.cg)
-        o = kq.quantized_matmul(attn_local, self.s["o"], None, self.cg, out_dtype=torch.float32)
         h = kq.quantized_glu(x, self.s["gate"], self.s["up"], self.cg, act="silu")
+        if self.comm is not None and x.reshape(-1, x.shape[-1]).shape[0] == 1:
+            # decode: each row-parallel projection and its cross-rank sum in one kernel
+            o = kq.quantized_matmul_allreduce(attn_local, self.s["o"], self.cg, self.comm, out_dtype=torch.float32)
+            y = kq.quantized_matmul_allreduce(h, self.s["down"], self.cd, self.comm, out_dtype=torch.float32)
+            return qkv, o, y
+        o = kq.quantized_matmul(attn_local, self.s["o"], None, self.cg, out_dtype=torch.float32)
         y = kq.quantized_matmul(h, self.s["down"], None, self.cd, out_dtype=torch.float32)
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             dist.all_reduce(o, group=self.group)
             dist.all_reduce(y, group=self.group)
         return qkv, o, y
+
+
+class PeerComm:
+    """Communication buffers of the fused row-parallel all-reduce
+    (``kq.quantized_matmul_allreduce``): one zero-filled device buffer per rank,
+    each mapped into every rank's process over CUDA IPC, and a device table of
+    the `world` buffer pointers (own at [rank]).  One set serves every
+    projection of up to `n` outputs, as long as all ranks make the same calls
+    in the same order."""
+
+    def __init__(self, n: int, device, group=None):
+        import ctypes
+        from . import _lib
+        L = _lib.load()
+        self.n = int(n)
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self._L = L
+        own = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(L.kq_comm_alloc(L.kq_allreduce_buffer_bytes(self.world, self.n), ctypes.byref(own)),
+                       "comm_alloc")
+            self._own = own.value
+            ptrs, self._opened = [], []
+            if self.world > 1:
+                h = ctypes.create_string_buffer(64)
+                _lib.check(L.kq_ipc_handle(ctypes.c_void_p(self._own), h), "ipc_handle")
+                handles = [None] * self.world
+                dist.all_gather_object(handles, h.raw, group=group)
+                for r in range(self.world):
+                    if r == self.rank:
+                        ptrs.append(self._own)
+                        continue
+                    p = ctypes.c_void_p()
+                    _lib.check(L.kq_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(p)),
+                               "ipc_open")
+                    self._opened.append(p.value)
+                    ptrs.append(p.value)
+            else:
+                ptrs = [self._own]
+            self.table = torch.tensor(ptrs, dtype=torch.int64, device=device)
+
+    def close(self):
+        import ctypes
+        for p in self._opened:
+            self._L.kq_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self._own:
+            self._L.kq_comm_free(ctypes.c_void_p(self._own))
+            self._own = None
 
 
 def expert_range(n_experts: int, world: int, rank: int) -> tuple[int, int]:
@@ -124,5 +180,5 @@ def ep_partial_reference(x_f32: np.ndarray, idx: np.ndarray, scores: np.ndarray,
     return y
 
 
-__all__ = ["block_split", "row_split", "shard_rows", "shard_k", "shard_llama_layer", "TPDecoderMLP",
+__all__ = ["block_split", "row_split", "shard_rows", "shard_k", "shard_llama_layer", "TPDecoderMLP", "PeerComm",
            "expert_range", "ep_moe_forward", "ep_partial_reference", "QK"]

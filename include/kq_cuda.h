@@ -172,6 +172,34 @@ size_t kq_moe_expert_layer_workspace_size(int codec_gu, int codec_d, int64_t t, 
                                           int64_t f, int h_dtype);
 
 /* Size of the fixed scratch array behind kq_quantized_matmul_noalloc. */
+/* ---- Row-parallel decode with the all-reduce fused in (tensor parallelism)
+ *
+ * Replaces the pair "quantized_matmul on this rank's K shard, then sum over
+ * ranks" of a row-parallel (K-split) projection: the all_sum that follows the
+ * sharded projections in gmlx's tensor-parallel layers
+ * (gmlx/hy_v3_model.py:259 after shard_linear, gmlx/hy_v3_model.py:396-443).
+ * One kernel computes this rank's partial y (one activation row), stores it
+ * into every rank's communication buffer over NVLink (peer stores), raises
+ * this rank's flag there, waits for all ranks' flags (bounded, ~2 s: on
+ * expiry the workspace error word becomes 7) and writes the rank-order sum to
+ * y, identical bits on every rank.
+ *
+ * comm_bufs: device array of `world` device pointers, the communication
+ * buffers of all ranks mapped into this process (own buffer at [rank]), each
+ * kq_allreduce_buffer_bytes(world, n) bytes, zero-filled before the first
+ * call (kq_comm_alloc does both).  All ranks must make the same sequence of
+ * calls on a buffer set.  Peer buffers come from kq_ipc_handle / kq_ipc_open
+ * (CUDA IPC; handles are 64 bytes). */
+size_t kq_allreduce_buffer_bytes(int world, int64_t n);
+int kq_quantized_matmul_allreduce(int codec, const void *x, int x_dtype, int64_t k, const void *w, int64_t n,
+                                  int64_t w_row_stride, void *y, int y_dtype, int world, int rank,
+                                  void *const *comm_bufs, void *workspace, size_t workspace_bytes, void *stream);
+int kq_comm_alloc(size_t bytes, void **ptr);
+int kq_comm_free(void *ptr);
+int kq_ipc_handle(const void *ptr, void *handle64);
+int kq_ipc_open(const void *handle64, void **ptr);
+int kq_ipc_close(void *ptr);
+
 #define KQ_NOALLOC_SCRATCH_BYTES (4 << 20)
 
 /* kq_quantized_matmul for callers that cannot allocate device memory (a host

@@ -397,3 +397,22 @@ def test_grouped_moe_layer_prefill(cuda, codec_gu, codec_d):
     h = kq.moe_glu_gather_kq(xd, tw(wg), tw(wu), codec_gu, tw(idx))
     assert tuple(h.shape) == (t, k, f)
     assert kq.workspace_error() == 0
+
+
+@pytest.mark.parametrize("codec,n,k", [("q4_k", 4096, 512), ("q6_k", 4096, 1792), ("q6_k", 1000, 7168)])
+def test_fused_allreduce_single_rank(cuda, codec, n, k):
+    """The fused row-parallel all-reduce with one rank equals the plain GEMV
+    (f32, same kernel arithmetic); repeated calls alternate the buffer parity."""
+    from gmlx_b200 import parallel as par
+    w = torch.from_numpy(synth.random_weight(codec, n, k, seed=120)).to(cuda)
+    comm = par.PeerComm(4096, cuda)
+    try:
+        for i in range(5):
+            x = to_dev_x(synth.random_activations(1, k, seed=121 + i), cuda)
+            ref = kq.quantized_matmul(x, w, None, codec, out_dtype=torch.float32)
+            y = kq.quantized_matmul_allreduce(x, w, codec, comm, out_dtype=torch.float32)
+            assert torch.equal(y, ref)
+        assert kq.workspace_error() == 0
+    finally:
+        torch.cuda.synchronize()
+        comm.close()

@@ -1,0 +1,63 @@
+"""Tensor-parallel decode on 2 GPUs (skipped with fewer): the fused
+row-parallel all-reduce kernel against the unsharded projection, and the same
+bits on every rank.  Ranks are processes (one per GPU, NCCL for the handle
+exchange), rendezvous on 127.0.0.1."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+
+
+def _rank_main(rank, port, out_q):
+    import torch.distributed as dist
+    from gmlx_b200 import kq, parallel as par, synth
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, device_id=dev)
+    try:
+        comm = par.PeerComm(4096, dev)
+        res = {}
+        for codec, n, k in (("q4_k", 4096, 4096), ("q6_k", 4096, 14336)):
+            w = synth.random_weight(codec, n, k, seed=7)
+            x = synth.random_activations(1, k, seed=8)
+            xd = torch.from_numpy(x.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+            full = kq.quantized_matmul(xd, torch.from_numpy(w).to(dev), None, codec, out_dtype=torch.float32)
+            kk = k // WORLD
+            ws = par.shard_k(torch.from_numpy(w), codec, WORLD, rank).contiguous().to(dev)
+            ys = [kq.quantized_matmul_allreduce(xd[:, rank * kk:(rank + 1) * kk].contiguous(), ws, codec, comm,
+                                                out_dtype=torch.float32) for _ in range(3)]
+            torch.cuda.synchronize()
+            res[codec] = (full.cpu().numpy(), [y.cpu().numpy() for y in ys], kq.workspace_error())
+        dist.barrier()
+        comm.close()
+        out_q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_fused_allreduce_two_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 200
+    procs = [ctx.Process(target=_rank_main, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for codec in ("q4_k", "q6_k"):
+        full = got[0][codec][0]
+        for r in range(WORLD):
+            _, ys, err = got[r][codec]
+            assert err == 0
+            for y in ys:
+                assert np.abs(y - full).max() / np.abs(full).max() <= 1e-4
+                assert np.array_equal(y.view(np.uint32), got[0][codec][1][0].view(np.uint32))  # same bits everywhere
