@@ -131,13 +131,20 @@ def build_layers(dev, n_layers, world=1, rank=0, seed0=100):
     return layers
 
 
-def layer_step(kq, L, x, a=None, dist=None):
-    """One decoder-layer pass of the seven quantized projections (4 launches;
-    under tensor parallelism + 2 all-reduces of the row-parallel outputs).
-    `a` stands in for this rank's slice of the attention output."""
+def layer_step(kq, L, x, a=None, dist=None, comm=None):
+    """One decoder-layer pass of the seven quantized projections (4 launches).
+    Under tensor parallelism the row-parallel o and down outputs are summed
+    over ranks: at M=1 inside their GEMV kernels (peer stores over NVLink,
+    `comm`), otherwise with NCCL all-reduces.  `a` stands in for this rank's
+    slice of the attention output."""
     qkv = kq.quantized_matmul(x, L["qkv"], None, "q4_k")
-    o = kq.quantized_matmul(x if a is None else a, L["o"], None, "q4_k")
     h = kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
+    xa = x if a is None else a
+    if comm is not None and x.shape[0] == 1:
+        o = kq.quantized_matmul_allreduce(xa, L["o"], "q4_k", comm)
+        y = kq.quantized_matmul_allreduce(h, L["down"], "q6_k", comm)
+        return qkv, o, y
+    o = kq.quantized_matmul(xa, L["o"], None, "q4_k")
     y = kq.quantized_matmul(h, L["down"], None, "q6_k")
     if dist is not None:
         dist.all_reduce(o)
@@ -287,6 +294,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--fused-allreduce", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -313,6 +321,11 @@ def main():
     stream = torch.cuda.Stream(dev)
     dd = dist if world > 1 else None
     ka = 4096 // world  # this rank's slice of the attention output (o_proj K)
+    from gmlx_b200 import parallel as par
+    # --fused-allreduce: row-parallel o/down with the cross-rank sum inside their
+    # GEMV kernels (peer stores over NVLink); default: GEMV + NCCL all-reduce,
+    # which measured faster at tp2 (2460 vs 1929 GB/s aggregate)
+    comm = par.PeerComm(4096, dev) if (world > 1 and args.fused_allreduce) else None
 
     def measure(m, steps, warmup, min_warm_s=0.0):
         g = torch.Generator(device="cpu").manual_seed(0)
@@ -321,7 +334,7 @@ def main():
 
         def one_pass():
             for li, L in enumerate(layers):
-                layer_step(kq, L, xs[li], att[li], dd)
+                layer_step(kq, L, xs[li], att[li], dd, comm)
         reps = max(1, steps // N_LAYERS)
         secs = time_graph(torch, one_pass, reps, max(1, warmup // N_LAYERS), stream, min_warm_s)
         return secs / (reps * N_LAYERS)
@@ -358,14 +371,14 @@ def main():
     torch.cuda.synchronize()
     for i in range(args.warmup):
         dx = hx.to(dev, non_blocking=True)
-        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka], dd)
+        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka], dd, comm)
         hy.copy_(y, non_blocking=True)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for i in range(e2e_steps):
         dx = hx.to(dev, non_blocking=True)
-        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka].contiguous(), dd)
+        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka].contiguous(), dd, comm)
         hy.copy_(y, non_blocking=True)
     b.record()
     torch.cuda.synchronize()
@@ -414,8 +427,9 @@ def main():
             "config": {"workload": "llama3-8b Q4_K_M decoder layer decode GEMV (q/k/v/o/gate/up Q4_K, down Q6_K)",
                        "m": args.m, "layers_cycled": N_LAYERS, "weight_bytes_per_step": LAYER_WEIGHT_BYTES,
                        "l2": "inputs larger than L2 (8 distinct layers, 1.10 GB, cycled)",
-                       "parallelism": f"tp{world} (column-parallel qkv/gate/up, row-parallel o/down, "
-                                      "NCCL all-reduce)" if world > 1 else "single"},
+                       "parallelism": (f"tp{world} (column-parallel qkv/gate/up, row-parallel o/down, "
+                                       + ("cross-rank sum fused into their GEMV kernels over NVLink peer stores)"
+                                          if comm is not None else "NCCL all-reduce)")) if world > 1 else "single"},
             "frac_hbm": value / world / hbm_peak,
             "moe": moe,
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K, GLU> (gate+up 14336x4096)",

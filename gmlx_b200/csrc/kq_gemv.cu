@@ -1128,13 +1128,18 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<NT>) gemv_kernel(const G
                 if (n < a.N && (!GLU || lane < 16)) emit(T, n, v);
                 if (lane == 0) a.counters[2 + t] = 0;
             }
-            // the last CTA out resets the work counters (zero on entry, left zero);
-            // with the fused all-reduce it also raises this rank's flag on every peer
-            if (a.ar_world) __threadfence_system();  // this CTA's partial stores, all peers
+            // the last CTA out resets the work counters (zero on entry, left zero).
+            // Fused all-reduce: it also raises this rank's flag on every peer, waits
+            // (bounded) for every rank's flag of this call and writes the rank-order
+            // sum of all partials.  Only that CTA waits, and only on other GPUs, so
+            // no CTA of this kernel depends on another being resident.  The other
+            // CTAs' partial stores reach it through gpu-scope fence + counter; its
+            // system-scope fence then orders them before the flag stores.
             named_bar_sync(1, CW * 32);
             if (ctid == 0) {
                 __threadfence();
-                if (atomicAdd(a.counters + 1, 1) == (int)gridDim.x - 1) {
+                const int last = atomicAdd(a.counters + 1, 1) == (int)gridDim.x - 1;
+                if (last) {
                     a.counters[0] = 0;
                     a.counters[1] = 0;
                     if (a.ar_world) {
@@ -1147,10 +1152,11 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<NT>) gemv_kernel(const G
                         *reinterpret_cast<volatile unsigned *>(a.ar_bufs[a.ar_rank]) = next;  // own epoch
                     }
                 }
+                *s_last = last;
             }
             if (a.ar_world) {
-                // wait (bounded) for every rank's flag of this call, then sum this
-                // CTA's slice of the outputs over ranks in rank order
+                named_bar_sync(1, CW * 32);
+                if (!*s_last) return;
                 if (ctid < a.ar_world) {
                     const unsigned *f = reinterpret_cast<const unsigned *>(a.ar_bufs[a.ar_rank] + 64) + ar_par * a.ar_world + ctid;
                     const uint64_t t0 = globaltimer();
@@ -1169,8 +1175,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<NT>) gemv_kernel(const G
                 if (*s_abort) return;
                 const float *slots = reinterpret_cast<const float *>(a.ar_bufs[a.ar_rank] + AR_HDR) +
                                      (int64_t)ar_par * a.ar_world * a.N;
-                const int per = (a.N + gridDim.x - 1) / gridDim.x;
-                for (int n = blockIdx.x * per + ctid; n < min(a.N, (int)(blockIdx.x + 1) * per); n += CW * 32) {
+                for (int n = ctid; n < a.N; n += CW * 32) {
                     float v = 0.f;
                     for (int r = 0; r < a.ar_world; r++) v += __ldcv(slots + (int64_t)r * a.N + n);
                     store_out(a.y, a.y_dtype, n, v);
@@ -1428,19 +1433,12 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = L::BYTES;
     cfg.stream = st;
+    if (a.ar_world && (!L::DP || !dyn)) return cudaErrorInvalidValue;  // fused all-reduce: one-row dynamic schedule
     cudaLaunchAttribute attr[1];
-    if (a.ar_world) {
-        // fused all-reduce: every CTA waits for the last one, so all must be
-        // resident at once (cooperative launch; no early start either)
-        if (!L::DP || !dyn) return cudaErrorInvalidValue;
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-    } else {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-    }
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = (getenv("KQ_GEMV_NOPDL") && !a.ar_world) ? 0 : 1;  // development switch
+    cfg.numAttrs = getenv("KQ_GEMV_NOPDL") ? 0 : 1;  // development switch
     GemvArgs b = a;
     b.dyn = dyn;
     b.ksplit = ksplit;
