@@ -60,9 +60,10 @@ template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 
 template <int C> constexpr int KB_OF = NCOL * GCfg<C>::BPW;
 template <int C> constexpr int XSTR_OF = KB_OF<C> * QK * 2 + 64;  // staged activation row stride (bytes)
 constexpr int SMEM_BUDGET = 112 * 1024;  // per CTA: two CTAs per SM
-// 9-32 activation rows: one CTA per SM (registers for the MMA fragments of up
-// to 4 n-tiles without spills) with the ring twice as deep
-template <int NT> constexpr int CTAS_PER_SM = NT >= 2 ? 1 : 2;
+// 17-32 activation rows of Q4_K/Q6_K: one CTA per SM (registers for the MMA
+// fragments of 3-4 n-tiles without spills) with the ring twice as deep;
+// measured slower for 9-16 rows and for IQ2_XXS
+template <int C, int NT> constexpr int CTAS_PER_SM = (NT >= 3 && C != IQ2_XXS) ? 1 : 2;
 constexpr int S_MAX = 2048;              // Q4_K one-row sub-block sums table: K <= 65536
 
 template <int C, bool DPL = false> __host__ __device__ constexpr int spitch_of() {
@@ -90,7 +91,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
     static constexpr int REDB = NCOL * 8 * NT * RED_TS * 4;  // one reduction buffer (two, alternating)
     static constexpr int FIXED = 512 + (C == IQ2_XXS ? 4096 : 0) + TABS + SBYTES + 2 * REDB + DPB;
-    static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<NT> - FIXED) / STAGE;
+    static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<C, NT> - FIXED) / STAGE;
     static constexpr int NS = NS_FIT > 8 ? 8 : (NS_FIT < 2 ? 2 : NS_FIT);  // ring depth (<= 8: rowoff table)
     static constexpr int OFF_BAR = 0;                              // 2*NS mbarriers
     static constexpr int OFF_ROWOFF = 128;                         // NS x 32 bytes
@@ -739,7 +740,7 @@ __device__ __forceinline__ float dp_iq2_dot(const IQ2Regs &r, const uint32_t *xq
 // -------------------------------------------------------------------------
 
 template <int C, int NT, bool F16, bool GLU, int XR>
-__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<NT>) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(const GemvArgs a) {
     using L = GLayout<C, NT, XR>;
     constexpr bool XS = L::XS;
     constexpr int bpb = Fmt<C>::bpb, NS = L::NS, KB = L::KB, XSTR = L::XSTR, BPW = GCfg<C>::BPW;
