@@ -203,7 +203,7 @@ bool use_grouped(int codec, int64_t slots, int64_t etotal, int64_t n, int64_t ki
 }
 
 struct GroupedPlan {
-    size_t perm_off, scr_off, misc_off, tiles_off, xs_off, g_off, b_off, total;
+    size_t perm_off, scr_off, misc_off, tiles_off, mix_off, xs_off, g_off, b_off, total;
     int max_tiles, chunk_e, mt;
 };
 
@@ -224,6 +224,8 @@ GroupedPlan grouped_plan(int codec, int64_t slots, int64_t e, int64_t etotal, in
     o = align256(o + 2 * sizeof(int));
     g.tiles_off = o;
     o = align256(o + (size_t)g.max_tiles * 3 * sizeof(int));
+    g.mix_off = o;  // fused score mix: token and score of each sorted row
+    if (f32_out) o = align256(o + (size_t)slots * 2 * sizeof(int));
     g.xs_off = o;
     o = align256(o + (size_t)slots * kin * 2);
     g.g_off = o;
@@ -251,9 +253,14 @@ int run_grouped(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, 
     int *te = (int *)(base + p.tiles_off), *tr0 = te + p.max_tiles, *tre = tr0 + p.max_tiles;
     void *xsorted = base + p.xs_off;
     cudaStream_t st = (cudaStream_t)stream;
+    // score mix fused into the GEMM epilogue (atomic f32 adds into y) when y is
+    // a contiguous f32 [tokens, n]; otherwise per-slot rows and the mix kernel
+    const bool fused_mix = scores && y_dtype == KQ_F32 && yrs == n;
+    int *tok_of = (int *)(base + p.mix_off);
+    float *scale_of = (float *)(tok_of + slots);
     cudaError_t ce = launch_moe_sort(idx, (int)slots, kslot, (int)ebase, (int)e, (int)etotal, mode == 1, xidx, x, xs,
                                      (int)kin, xsorted, 128 * p.mt, cnt, scr, perm, count, ntiles, te, tr0, tre,
-                                     p.max_tiles, err, st);
+                                     p.max_tiles, err, fused_mix ? scores : nullptr, tok_of, scale_of, st);
     if (ce != cudaSuccess) return cuda_status(ce, what);
     GemmArgs g{};
     g.codec = codec;
@@ -276,6 +283,13 @@ int run_grouped(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, 
     g.y = scores ? (void *)(base + p.g_off) : y;
     g.y_dtype = scores ? KQ_F32 : y_dtype;
     g.y_row_stride = scores ? n : yrs;
+    if (fused_mix) {
+        if ((ce = cudaMemsetAsync(y, 0, (size_t)tokens * n * sizeof(float), st)) != cudaSuccess)
+            return cuda_status(ce, what);
+        g.y = y;
+        g.out_row = tok_of;
+        g.row_scale = scale_of;
+    }
     for (int64_t c0 = 0; c0 < e; c0 += p.chunk_e) {
         const int64_t c1 = std::min<int64_t>(e, c0 + p.chunk_e);
         g.ex_lo = (int)c0;
@@ -301,7 +315,7 @@ int run_grouped(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, 
         }
         if ((ce = launch_gemm_grouped(g, p.mt, p.max_tiles, bd, st)) != cudaSuccess) return cuda_status(ce, what);
     }
-    if (scores)
+    if (scores && !fused_mix)
         ce = launch_moe_mix((const float *)(base + p.g_off), scores, idx, (int)ebase, (int)e, (int)tokens, kslot, (int)n,
                             y, y_dtype, st);
     return cuda_status(ce, what);

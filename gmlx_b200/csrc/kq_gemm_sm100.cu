@@ -310,7 +310,21 @@ __global__ void __launch_bounds__(GT, 1)
             if (tok >= mend || *s_abort) continue;
             const int64_t orow = a.out_row ? (int64_t)a.out_row[tok] : (int64_t)tok;
             const int nb = n0 + col;
-            if (a.y_dtype == F32) {
+            if (a.row_scale) {  // y[out_row] += scale * row (f32; several rows add into one output row)
+                const float sc = a.row_scale[tok];
+                float *yp = reinterpret_cast<float *>(a.y) + orow * a.y_row_stride + nb;
+                if (nb + 32 <= a.N && ((uintptr_t)yp & 15) == 0) {
+#pragma unroll
+                    for (int v = 0; v < 8; v++)
+                        atomicAdd(reinterpret_cast<float4 *>(yp) + v,
+                                  make_float4(sc * __uint_as_float(r[4 * v]), sc * __uint_as_float(r[4 * v + 1]),
+                                              sc * __uint_as_float(r[4 * v + 2]), sc * __uint_as_float(r[4 * v + 3])));
+                } else {
+#pragma unroll
+                    for (int v = 0; v < 32; v++)
+                        if (nb + v < a.N) atomicAdd(yp + v, sc * __uint_as_float(r[v]));
+                }
+            } else if (a.y_dtype == F32) {
                 float *yp = reinterpret_cast<float *>(a.y) + orow * a.y_row_stride + nb;
                 if (nb + 32 <= a.N && ((uintptr_t)yp & 15) == 0) {
 #pragma unroll
@@ -517,12 +531,20 @@ __global__ void table_kernel(int ecount, int tile_rows, int *__restrict__ cnt, i
 __global__ void scatter_rows_kernel(const int32_t *__restrict__ idx, const int *__restrict__ rank,
                                     const int *__restrict__ off, int ebase, int k, int xrow_is_slot,
                                     const int32_t *__restrict__ xidx, const uint16_t *__restrict__ x, int64_t xs_stride,
-                                    int K, int *__restrict__ perm, uint16_t *__restrict__ out) {
+                                    int K, int *__restrict__ perm, uint16_t *__restrict__ out,
+                                    const float *__restrict__ scores, int *__restrict__ tok_of,
+                                    float *__restrict__ scale_of) {
     const int s = blockIdx.x;
     const int r = rank[s];
     if (r < 0) return;
     const int p = off[idx[s] - ebase] + r;
-    if (threadIdx.x == 0) perm[p] = s;
+    if (threadIdx.x == 0) {
+        perm[p] = s;
+        if (scores) {  // mixed output: sorted row p adds score * row into token s / k
+            tok_of[p] = s / k;
+            scale_of[p] = scores[s];
+        }
+    }
     const int xr = xidx ? xidx[s] : xrow_is_slot ? s : s / k;
     const uint4 *src = reinterpret_cast<const uint4 *>(x + (int64_t)xr * xs_stride);
     uint4 *dst = reinterpret_cast<uint4 *>(out + (int64_t)p * K);
@@ -543,7 +565,8 @@ cudaError_t launch_gemm_grouped(const GemmArgs &a, int mt, int max_tiles, const 
 cudaError_t launch_moe_sort(const int32_t *idx, int S, int k, int ebase, int ecount, int etotal, int xrow_is_slot,
                             const int32_t *xidx, const void *x, int64_t x_row_stride, int K, void *xs, int tile_rows,
                             int *cnt, int *scratch, int *perm, int *counts, int *n_tiles, int *tile_e, int *tile_row0,
-                            int *tile_rowend, int max_tiles, int *err, cudaStream_t st) {
+                            int *tile_rowend, int max_tiles, int *err, const float *scores, int *tok_of,
+                            float *scale_of, cudaStream_t st) {
     if (ecount > 1024) return cudaErrorInvalidValue;
     int *rank = scratch, *off = scratch + S;
     rank_kernel<<<(S + 255) / 256, 256, 0, st>>>(idx, S, ebase, ecount, etotal, cnt, rank, err);
@@ -554,7 +577,7 @@ cudaError_t launch_moe_sort(const int32_t *idx, int S, int k, int ebase, int eco
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     scatter_rows_kernel<<<S, 128, 0, st>>>(idx, rank, off, ebase, k, xrow_is_slot, xidx,
                                            reinterpret_cast<const uint16_t *>(x), x_row_stride, K, perm,
-                                           reinterpret_cast<uint16_t *>(xs));
+                                           reinterpret_cast<uint16_t *>(xs), scores, tok_of, scale_of);
     return cudaGetLastError();
 }
 

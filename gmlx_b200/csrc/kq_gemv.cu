@@ -35,6 +35,8 @@
 #include <cuda_fp16.h>
 #include <stdlib.h>
 
+#include <algorithm>
+
 #include "kq_internal.cuh"
 #include "kq_ptx.cuh"
 
@@ -1407,6 +1409,8 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
             d = 1;
         }
     }
+    if (d && L::DP && !a.ar_world)
+        if (const char *f = getenv("KQ_GEMV_FORCE_S")) S = (int)std::min<long>(nst, std::max(1, atoi(f)));  // development
     if (dyn) *dyn = d;
     if (ksplit) *ksplit = S;
     return (int)(iters < cap ? iters : cap);

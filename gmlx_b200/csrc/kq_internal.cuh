@@ -99,6 +99,9 @@ struct GemmArgs {
     // fused), or for dense B the up rows follow the gate rows of the scratch
     const uint8_t *w2;
     int act;
+    // mixed output (grouped MoE down projection): y is f32 and sorted row r
+    // adds row_scale[r] * (its output row) into y row out_row[r] atomically
+    const float *row_scale;
 };
 bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride);
 size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k, bool glu);
@@ -116,7 +119,8 @@ cudaError_t launch_gemm_grouped(const GemmArgs &a, int mt, int max_tiles, const 
 cudaError_t launch_moe_sort(const int32_t *idx, int S, int k, int ebase, int ecount, int etotal, int xrow_is_slot,
                             const int32_t *xidx, const void *x, int64_t x_row_stride, int K, void *xs, int tile_rows,
                             int *cnt, int *scratch, int *perm, int *counts, int *n_tiles, int *tile_e, int *tile_row0,
-                            int *tile_rowend, int max_tiles, int *err, cudaStream_t st);
+                            int *tile_rowend, int max_tiles, int *err, const float *scores, int *tok_of,
+                            float *scale_of, cudaStream_t st);
 
 // MoE slot grouping: idx[S] (S = T*k slots) -> groups of <= gsize slots per
 // local expert (experts [ebase, ebase+ecount); ascending slot order inside a
