@@ -8,7 +8,10 @@
 //
 // Memory-bound: each warp owns one super-block, each lane 8 consecutive
 // weights (one 32-byte f32 store or one 16-byte f16/bf16 store).
+#include <algorithm>
+
 #include "kq_internal.cuh"
+#include "kq_ptx.cuh"
 
 namespace kq {
 
@@ -86,10 +89,133 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict_
     }
 }
 
+// Contiguous rows (row stride == row bytes): the raw blocks form one byte range.
+// A persistent CTA bulk-copies chunks of DQ_CHUNK blocks into a two-slot shared
+// ring (one 1-D cp.async.bulk per chunk, mbarrier completion) and its 8 warps
+// decode them from shared memory, so ~2 chunks per CTA are in flight instead of
+// one block per warp.  Waits are bounded (~2 s; on expiry the CTA stops).
+constexpr int DQ_CHUNK = 128;
+
+__device__ __forceinline__ uint64_t dq_timer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+template <int C, int OUT>
+__device__ __forceinline__ void store8(void *out, int64_t e0, const float o[8]) {
+    if constexpr (OUT == F32) {
+        float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + e0);
+        p[0] = make_float4(o[0], o[1], o[2], o[3]);
+        p[1] = make_float4(o[4], o[5], o[6], o[7]);
+    } else {
+        uint4 v;
+        uint32_t *u = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if constexpr (OUT == BF16) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+                u[i] = *reinterpret_cast<uint32_t *>(&h);
+            } else {
+                __half2 h = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
+                u[i] = *reinterpret_cast<uint32_t *>(&h);
+            }
+        }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(out) + e0) = v;
+    }
+}
+
+template <int C, int OUT>
+__global__ void __launch_bounds__(256) dequant_bulk_kernel(const uint8_t *__restrict__ w, int64_t nblk,
+                                                           void *__restrict__ out) {
+    constexpr int bpb = Fmt<C>::bpb, CB = DQ_CHUNK * bpb + 16;
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm);
+    uint8_t *buf = sm + 128;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t nchunks = (nblk + DQ_CHUNK - 1) / DQ_CHUNK;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int64_t c, int slot) {  // thread 0: chunk c -> slot
+        const int64_t b0 = c * DQ_CHUNK, nb = min((int64_t)DQ_CHUNK, nblk - b0);
+        const uintptr_t src = (uintptr_t)(w + b0 * bpb);
+        const uint32_t off = (uint32_t)(src & 15);
+        const uint32_t bytes = (off + (uint32_t)nb * bpb + 15) & ~15u;
+        mbar_arrive_expect_tx(&bar[slot], bytes);
+        bulk_g2s(buf + slot * CB, (const void *)(src - off), bytes, &bar[slot], policy_evict_first());
+    };
+    int64_t c = blockIdx.x;
+    int iss[2] = {0, 0};  // copies issued into each slot (thread 0)
+    if (threadIdx.x == 0 && c < nchunks) {
+        issue(c, 0);
+        iss[0]++;
+    }
+    for (uint32_t it = 0; c < nchunks; c += gridDim.x, it++) {
+        const int slot = it & 1;
+        const int64_t cn = c + gridDim.x;
+        if (threadIdx.x == 0 && cn < nchunks) {  // the other slot was freed by the last barrier
+            issue(cn, slot ^ 1);
+            iss[slot ^ 1]++;
+        }
+        // bounded wait for this chunk; the decision to go on is CTA-uniform
+        bool ok = true;
+        const uint64_t t0 = dq_timer();
+        for (uint32_t i = 0; !mbar_try_wait(&bar[slot], (it >> 1) & 1); i++)
+            if ((i & 1023) == 1023 && dq_timer() - t0 > 2000000000ull) {
+                ok = false;
+                break;
+            }
+        if (__syncthreads_or(!ok)) break;
+        const int64_t b0 = c * DQ_CHUNK, nb = min((int64_t)DQ_CHUNK, nblk - b0);
+        const uint8_t *base = buf + slot * CB + ((uintptr_t)(w + b0 * bpb) & 15);
+        for (int b = warp; b < nb; b += 8) {
+            float o[8];
+            deq8<C>(base + b * bpb, lane, o);
+            store8<C, OUT>(out, (b0 + b) * QK + 8 * lane, o);
+        }
+        __syncthreads();  // slot free before it is refilled
+    }
+    // after an early exit a copy may still be in flight: wait (bounded) for the
+    // last one issued into each slot before the CTA's shared memory is released
+    if (threadIdx.x == 0) {
+        for (int sl = 0; sl < 2; sl++) {
+            if (!iss[sl]) continue;
+            const uint64_t t0 = dq_timer();
+            while (!mbar_try_wait(&bar[sl], (uint32_t)(iss[sl] - 1) & 1u) && dq_timer() - t0 < 2000000000ull) {
+            }
+        }
+    }
+}
+
 template <int C>
 static cudaError_t launch_deq(const uint8_t *w, int64_t rows, int64_t nb, int64_t stride, void *out, int dtype,
                               cudaStream_t st) {
     const int64_t nblk = rows * nb;
+    if (stride == nb * Fmt<C>::bpb && nblk >= 8 * DQ_CHUNK) {
+        constexpr int smem = 128 + 2 * (DQ_CHUNK * Fmt<C>::bpb + 16);
+        const int nsm = num_sms();
+        const int64_t nchunks = (nblk + DQ_CHUNK - 1) / DQ_CHUNK;
+        const unsigned g = (unsigned)std::min<int64_t>(nchunks, (int64_t)nsm * 3);
+        cudaError_t e;
+        if (dtype == F32) {
+            if ((e = cudaFuncSetAttribute(dequant_bulk_kernel<C, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
+                return e;
+            dequant_bulk_kernel<C, F32><<<g, 256, smem, st>>>(w, nblk, out);
+        } else if (dtype == BF16) {
+            if ((e = cudaFuncSetAttribute(dequant_bulk_kernel<C, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
+                return e;
+            dequant_bulk_kernel<C, BF16><<<g, 256, smem, st>>>(w, nblk, out);
+        } else {
+            if ((e = cudaFuncSetAttribute(dequant_bulk_kernel<C, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)))
+                return e;
+            dequant_bulk_kernel<C, F16><<<g, 256, smem, st>>>(w, nblk, out);
+        }
+        return cudaGetLastError();
+    }
     const unsigned grid = (unsigned)((nblk + 7) / 8);
     if (dtype == F32) dequant_kernel<C, F32><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);
     else if (dtype == BF16) dequant_kernel<C, BF16><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);

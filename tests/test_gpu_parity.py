@@ -42,6 +42,19 @@ def test_dequantize_bitexact(cuda, codec, dtype):
         assert np.array_equal(got, torch.from_numpy(ref).to(dtype).float().numpy())
 
 
+@pytest.mark.parametrize("codec,rows,k", [("q4_k", 600, 4096), ("q6_k", 4000, 768), ("iq2_xxs", 1500, 1792)])
+def test_dequantize_large_contiguous_bitexact(cuda, codec, rows, k):
+    """Large contiguous weights take the chunked bulk-copy dequantizer
+    (unaligned chunk starts for Q6_K 630-byte and IQ2_XXS 462-byte rows)."""
+    w = synth.random_weight(codec, rows, k, seed=130)
+    ref = O.dequantize(w, codec)
+    wd = torch.from_numpy(w).to(cuda)
+    out = kq.dequantize(wd, None, codec).cpu().numpy()
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+    bf = kq.dequantize(wd, None, codec, dtype=torch.bfloat16).float().cpu().numpy()
+    assert np.array_equal(bf, torch.from_numpy(ref).to(torch.bfloat16).float().numpy())
+
+
 @pytest.mark.parametrize("codec", CODECS)
 @pytest.mark.parametrize("m", [1, 3, 8, 17, 32, 40])
 @pytest.mark.parametrize("n,k", [(256, 1024), (200, 2048)])
