@@ -170,6 +170,8 @@ __global__ void __launch_bounds__(GT, 1)
         m0 = a.tile_row0[blockIdx.x];
         mend = a.tile_rowend[blockIdx.x];
     }
+    // row tiles with rows to compute (a grouped tile's second half may be empty)
+    const int mt_live = (MT == 1 || m0 + BM < mend) ? MT : 1;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSTAGE; i++) {
@@ -193,7 +195,7 @@ __global__ void __launch_bounds__(GT, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t tx = MT * A_BYTES + (BMODE == B_TMA ? B_BYTES : 0);
+            const uint32_t tx = mt_live * A_BYTES + (BMODE == B_TMA ? B_BYTES : 0);
             for (int s = 0; s < nk; s++) {
                 const int slot = s % NSTAGE;
                 wait_b(&empty[slot], ((s / NSTAGE) & 1) ^ 1, s_abort, a.err, 11);
@@ -201,7 +203,9 @@ __global__ void __launch_bounds__(GT, 1)
                 if (*s_abort) continue;
 #pragma unroll
                 for (int t = 0; t < MT; t++)
-                    tma_load_2d(smem + OFF_A + slot * L::STAGE_A + t * A_BYTES, &tmA, s * BK, m0 + t * BM, &fullA[slot]);
+                    if (t < mt_live)
+                        tma_load_2d(smem + OFF_A + slot * L::STAGE_A + t * A_BYTES, &tmA, s * BK, m0 + t * BM,
+                                    &fullA[slot]);
                 if (BMODE == B_TMA) {
                     const int rb = (ex - a.ex_lo) * a.n_per_expert + n0;
                     tma_load_2d(smem + OFF_B + slot * B_BYTES, &tmB, s * BK, rb, &fullA[slot]);
@@ -225,7 +229,7 @@ __global__ void __launch_bounds__(GT, 1)
                 for (int t = 0; t < MT; t++)
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++)
-                        if (!*s_abort)
+                        if (t < mt_live && !*s_abort)
                             umma(tmem + t * BN, umma_desc(sa + t * A_BYTES + kk * 32), umma_desc(sb + kk * 32), id,
                                  (s | kk) ? 1u : 0u);
                 umma_commit(&empty[slot]);
@@ -294,7 +298,7 @@ __global__ void __launch_bounds__(GT, 1)
         tc_fence_after();
         const int quarter = warp & 3, chalf = (warp - 2) >> 2;
 #pragma unroll 1
-        for (int q32 = 0; q32 < MT * (NOUT / 2); q32 += 32) {
+        for (int q32 = 0; q32 < mt_live * (NOUT / 2); q32 += 32) {
             const int t = q32 / (NOUT / 2), cc = q32 % (NOUT / 2);
             const int tok = m0 + t * BM + quarter * 32 + lane;
             const int col = chalf * (NOUT / 2) + cc;
