@@ -77,12 +77,13 @@ def _cid(codec) -> int:
     return c
 
 
-def _stream(dev: torch.device):
-    return _ct.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+def _stream(dev: torch.device) -> int:
+    # plain ints: the ctypes signatures declare c_void_p and convert them
+    return torch.cuda.current_stream(dev).cuda_stream
 
 
-def _p(t: torch.Tensor | None):
-    return _ct.c_void_p(t.data_ptr() if t is not None else 0)
+def _p(t: torch.Tensor | None) -> int:
+    return t.data_ptr() if t is not None else 0
 
 
 def _need_cuda(*ts):
@@ -113,6 +114,19 @@ def _rows2d(w: torch.Tensor) -> tuple[torch.Tensor, int]:
 # per-(device, stream) workspaces, zero-filled once and kept zero by the library
 
 _WS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+_WS_SIZE: dict[tuple, int] = {}
+
+
+def _ws_size(fn_name: str, *args) -> int:
+    """Workspace size query, memoized (a pure function of its arguments)."""
+    key = (fn_name,) + args
+    v = _WS_SIZE.get(key)
+    if v is None:
+        v = getattr(_lib.load(), fn_name)(*args)
+        _WS_SIZE[key] = v
+    return v
 
 
 def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
@@ -184,7 +198,7 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, 
     y = torch.empty(m, n, dtype=od, device=x.device)
     if m:
         L = _lib.load()
-        ws = _workspace(x.device, L.kq_quantized_matmul_workspace_size(c, m, n, k))
+        ws = _workspace(x.device, _ws_size("kq_quantized_matmul_workspace_size", c, m, n, k))
         _lib.check(L.kq_quantized_matmul(c, _p(x2), _DT[x2.dtype], m, k, x2.stride(0), _p(w), n, wstride, _p(y),
                                          _DT[od], n, _p(ws), ws.numel(), _stream(x.device)), "quantized_matmul")
     return y.reshape(*x.shape[:-1], n)
@@ -210,7 +224,7 @@ def quantized_matmul_allreduce(x: torch.Tensor, w: torch.Tensor, codec, comm,
     od = out_dtype or x.dtype
     y = torch.empty(1, n, dtype=od, device=x.device)
     L = _lib.load()
-    ws = _workspace(x.device, L.kq_quantized_matmul_workspace_size(c, 1, n, k))
+    ws = _workspace(x.device, _ws_size("kq_quantized_matmul_workspace_size", c, 1, n, k))
     _lib.check(L.kq_quantized_matmul_allreduce(c, _p(x2), _DT[x2.dtype], k, _p(w), n, wstride, _p(y), _DT[od],
                                                comm.world, comm.rank, _p(comm.table), _p(ws), ws.numel(),
                                                _stream(x.device)), "quantized_matmul_allreduce")
@@ -238,7 +252,7 @@ def quantized_glu(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, cod
     y = torch.empty(m, n, dtype=od, device=x.device)
     if m:
         L = _lib.load()
-        ws = _workspace(x.device, L.kq_quantized_glu_workspace_size(c, m, n, k))
+        ws = _workspace(x.device, _ws_size("kq_quantized_glu_workspace_size", c, m, n, k))
         _lib.check(L.kq_quantized_glu(c, _p(x2), _DT[x2.dtype], m, k, x2.stride(0), _p(gate_w), _p(up_w), n, ws_,
                                       _lib.ACTS[act], _p(y), _DT[od], n, _p(ws), ws.numel(), _stream(x.device)),
                    "quantized_glu")
@@ -299,7 +313,7 @@ def moe_glu_gather_kq(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor,
     h = torch.empty(t, k, f, dtype=od, device=x.device)
     if t:
         L = _lib.load()
-        ws = _workspace(x.device, L.kq_moe_workspace_size(c, t * k, e, f, d))
+        ws = _workspace(x.device, _ws_size("kq_moe_workspace_size", c, t * k, e, f, d))
         _lib.check(L.kq_moe_glu_gather(c, _p(x2), _DT[x2.dtype], t, d, _p(i2), k, _p(gate_w), _p(up_w), e, f, wrs,
                                        wes, _lib.ACTS[act], _p(h), _DT[od], _p(ws), ws.numel(), _stream(x.device)),
                    "moe_glu_gather_kq")
@@ -322,7 +336,7 @@ def gather_qmv_kq(h: torch.Tensor, w: torch.Tensor, codec, idx: torch.Tensor, bi
     y = torch.empty(t, k, n, dtype=od, device=h.device)
     if t:
         L = _lib.load()
-        ws = _workspace(h.device, L.kq_moe_workspace_size(c, t * k, e, n, f))
+        ws = _workspace(h.device, _ws_size("kq_moe_workspace_size", c, t * k, e, n, f))
         _lib.check(L.kq_gather_qmv(c, _p(h2), _DT[h2.dtype], t, k, f, _p(i2), _p(w), e, n, wrs, wes, _p(y), _DT[od],
                                    _p(ws), ws.numel(), _stream(h.device)), "gather_qmv_kq")
     if bias is not None:
@@ -347,7 +361,7 @@ def gather_qmv_mix_ns_kq(h: torch.Tensor, w: torch.Tensor, codec, idx: torch.Ten
     y = torch.empty(t, n, dtype=od, device=h.device)
     if t:
         L = _lib.load()
-        ws = _workspace(h.device, L.kq_moe_workspace_size(c, t * k, e, n, f))
+        ws = _workspace(h.device, _ws_size("kq_moe_workspace_size", c, t * k, e, n, f))
         _lib.check(L.kq_gather_qmv_mix(c, _p(h2), _DT[h2.dtype], t, k, f, _p(i2), _p(s2), _p(w), e, n, wrs, wes,
                                        _p(y), _DT[od], _p(ws), ws.numel(), _stream(h.device)), "gather_qmv_mix_ns_kq")
     return y
@@ -387,7 +401,7 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, lhs_in
     y = torch.empty(rows, n, dtype=od, device=x.device)
     if rows:
         L = _lib.load()
-        ws = _workspace(x.device, L.kq_moe_workspace_size(c, rows, e, n, kin))
+        ws = _workspace(x.device, _ws_size("kq_moe_workspace_size", c, rows, e, n, kin))
         _lib.check(L.kq_gather_qmm(c, _p(x2), _DT[x2.dtype], kin, x2.stride(0), rows, _p(xrow), _p(expert), _p(w),
                                    e, n, wrs, wes, _p(y), _DT[od], _p(ws), ws.numel(), _stream(x.device)),
                    "gather_qmm")
@@ -422,7 +436,7 @@ def moe_expert_layer_local(x: torch.Tensor, idx: torch.Tensor, scores: torch.Ten
     y = torch.empty(t, down_w.shape[1], dtype=od, device=x.device)
     if t:
         L = _lib.load()
-        ws = _workspace(x.device, L.kq_moe_expert_layer_workspace_size(cg, cd, t, k, e_local, d, f, _DT[x2.dtype]))
+        ws = _workspace(x.device, _ws_size("kq_moe_expert_layer_workspace_size", cg, cd, t, k, e_local, d, f, _DT[x2.dtype]))
         _lib.check(L.kq_moe_expert_layer_local(cg, cd, _p(x2), _DT[x2.dtype], t, d, _p(i2), k, _p(s2), _p(gate_w),
                                                _p(up_w), grs, ges, _p(down_w), drs, des, e_local, f, expert_base,
                                                e_total, _lib.ACTS[act], _p(y), _DT[od], _p(ws), ws.numel(),
