@@ -1413,6 +1413,16 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
         if (const char *f = getenv("KQ_GEMV_FORCE_S")) S = (int)std::min<long>(nst, std::max(1, atoi(f)));  // development
     if (dyn) *dyn = d;
     if (ksplit) *ksplit = S;
+    if (!d && iters > cap && !getenv("KQ_GEMV_GRID")) {
+        // stream-K: prefer a grid that gives every CTA the same whole number of
+        // stages of one tile (tiles x a divisor of the stages per tile), so no
+        // CTA carries an extra stage or two partial tiles; keep >= 70 % of the slots
+        for (long sd = nst; sd >= 1; sd--)
+            if (nst % sd == 0 && units * sd <= cap) {
+                if (units * sd * 10 >= cap * 7) cap = units * sd;
+                break;
+            }
+    }
     return (int)(iters < cap ? iters : cap);
 }
 
