@@ -21,6 +21,8 @@ SOURCES = ["kq_dequant.cu", "kq_gemv.cu", "kq_moe.cu", "kq_capi.cu", "kq_noalloc
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills"]
+if os.environ.get("KQ_DEVELOPMENT"):  # development switches (GEMV debug word, timestamps)
+    FLAGS.append("-DKQ_DEVELOPMENT")
 
 
 def _deps():

@@ -117,8 +117,12 @@ GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k,
     a.y_row_stride = ys;
     a.act = act;
     a.max_tokens = (int)(m < 32 ? m : 32);
+#ifdef KQ_DEVELOPMENT
+    // development builds only: skip parts of the GEMV / write per-CTA timestamps
+    // into a second output row (the caller must provide it)
     const char *dbg = getenv("KQ_GEMV_DEBUG");
     a.debug = dbg ? atoi(dbg) : 0;
+#endif
     return a;
 }
 
