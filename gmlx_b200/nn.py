@@ -3,6 +3,8 @@
 
 * ``KQuantLinear(in_dims, out_dims, bias, codec)`` (gmlx/modules.py:1539)
 * ``KQuantSwitchLinear(num_experts, out_dims, in_dims, bias, codec)`` (:1552)
+* ``KQuantEmbedding(num_embeddings, dims, codec, out_dtype)`` (:1545) and
+  ``KQuantMultiLinear(in_dims, out_dims, num_heads, codec)`` (:1530, :1556)
 * ``KQuantSwitchGLU`` -- SwitchGLU over three KQuantSwitchLinear stacks with
   the fused decode path of ``_FusedKQuantSwitchGLU`` (gmlx/modules.py:540-605):
   ``moe_glu_gather_kq`` + ``gather_qmv_mix_ns_kq`` when fewer than 64 routed
@@ -64,6 +66,61 @@ class KQuantSwitchLinear(nn.Module):
         if self.bias is not None:
             y = y + self.bias[indices.long()].unsqueeze(-2).to(y.dtype)
         return y
+
+
+class KQuantEmbedding(nn.Module):
+    """``KQuantEmbedding(num_embeddings, dims, codec, out_dtype=...)``
+    (gmlx/modules.py:1545-1547): token rows are dequantized on lookup;
+    ``as_linear`` is the tied output head, ``x @ dequant(W).T`` (used as
+    ``embed_tokens.as_linear`` by gmlx/hy_v3_model.py:341)."""
+
+    def __init__(self, num_embeddings: int, dims: int, codec: str = "q4_k", out_dtype=torch.bfloat16, device=None):
+        super().__init__()
+        if not kq.codec_has_matmul(codec):
+            raise NotImplementedError(f"no K-quant kernels for codec {codec!r}")
+        self.num_embeddings, self.dims, self.kquant_type, self.out_dtype = num_embeddings, dims, codec, out_dtype
+        self.register_buffer("weight", torch.zeros(num_embeddings, _wire_bytes(codec, dims), dtype=torch.uint8,
+                                                   device=device))
+        self.register_buffer("scales", torch.zeros(1, dtype=torch.uint8, device=device))
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        rows = self.weight[ids.reshape(-1).long()]
+        out = kq.dequantize(rows, self.scales, self.kquant_type, dtype=self.out_dtype)
+        return out.reshape(*ids.shape, self.dims)
+
+    def as_linear(self, x: torch.Tensor) -> torch.Tensor:
+        return kq.quantized_matmul(x, self.weight, self.scales, self.kquant_type)
+
+
+class KQuantMultiLinear(nn.Module):
+    """``KQuantMultiLinear(in_dims, out_dims, num_heads, codec)`` (gmlx/modules.py:1530,
+    1556): one wire matrix per head, ``weight [num_heads, out, nb*bpb]``, with
+    mlx-lm MultiLinear semantics over ``x [..., num_heads, L, K]``:
+    ``transpose=True`` -> ``x @ W[h].T`` through ``gather_qmm`` (the reference
+    dispatches these tensors to ``kq.gather_qmm`` too); ``transpose=False`` ->
+    ``x @ W[h]`` (the absorbed-MLA un-embedding) on the dequantized heads."""
+
+    def __init__(self, in_dims: int, out_dims: int, num_heads: int, codec: str = "q4_k", device=None):
+        super().__init__()
+        if not kq.codec_has_matmul(codec):
+            raise NotImplementedError(f"no K-quant kernels for codec {codec!r}")
+        self.in_dims, self.out_dims, self.num_heads, self.kquant_type = in_dims, out_dims, num_heads, codec
+        self.register_buffer("weight", torch.zeros(num_heads, out_dims, _wire_bytes(codec, in_dims),
+                                                   dtype=torch.uint8, device=device))
+        self.register_buffer("scales", torch.zeros(1, dtype=torch.uint8, device=device))
+
+    def forward(self, x: torch.Tensor, transpose: bool = True) -> torch.Tensor:
+        h = self.num_heads
+        if transpose:
+            if x.shape[-3] != h or x.shape[-1] != self.in_dims:
+                raise ValueError(f"MultiLinear expects [..., {h}, L, {self.in_dims}], got {tuple(x.shape)}")
+            # batch element (..., head) of x takes expert `head` of the stack
+            heads = torch.arange(h, device=x.device, dtype=torch.int32).expand(*x.shape[:-2])
+            return kq.gather_qmm(x, self.weight, self.scales, self.kquant_type, rhs_indices=heads)
+        if x.shape[-3] != h or x.shape[-1] != self.out_dims:
+            raise ValueError(f"MultiLinear expects [..., {h}, L, {self.out_dims}], got {tuple(x.shape)}")
+        w = kq.dequantize(self.weight, self.scales, self.kquant_type, dtype=x.dtype)  # [H, out, in]
+        return torch.matmul(x, w)
 
 
 class KQuantSwitchGLU(nn.Module):

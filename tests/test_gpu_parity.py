@@ -432,3 +432,36 @@ def test_fused_allreduce_single_rank(cuda, codec, n, k):
     finally:
         torch.cuda.synchronize()
         comm.close()
+
+
+def test_embedding_and_multilinear_modules(cuda):
+    """KQuantEmbedding (row lookup, tied head) and KQuantMultiLinear (per-head
+    stacks, both orientations) against the oracle's dequantized weights."""
+    from gmlx_b200 import nn as knn
+    vocab, dims = 300, 512
+    we = synth.random_weight("q6_k", vocab, dims, seed=140)
+    emb = knn.KQuantEmbedding(vocab, dims, "q6_k", out_dtype=torch.float32, device=cuda)
+    emb.weight.copy_(torch.from_numpy(we))
+    ids = torch.tensor([[3, 299, 0], [17, 3, 150]], device=cuda)
+    deq = O.dequantize(we, "q6_k")
+    assert np.array_equal(emb(ids).cpu().numpy(), deq[ids.cpu().numpy()])
+    x = synth.random_activations(2, dims, seed=141)
+    assert rel_err(emb.as_linear(to_dev_x(x, cuda)).float().cpu().numpy(), O.matmul(x, we, "q6_k")) <= TOL
+    h, n, k, L = 4, 128, 512, 3
+    wm = synth.random_weight("q4_k", n, k, seed=142, experts=h)
+    ml = knn.KQuantMultiLinear(k, n, h, "q4_k", device=cuda)
+    ml.weight.copy_(torch.from_numpy(wm))
+    xm = synth.random_activations(2 * h * L, k, seed=143)
+    xd = to_dev_x(xm, cuda).reshape(2, h, L, k)
+    y = ml(xd).float().cpu().numpy()
+    assert y.shape == (2, h, L, n)
+    for b in range(2):
+        for hh in range(h):
+            rows = xm.reshape(2, h, L, k)[b, hh]
+            assert rel_err(y[b, hh], O.matmul(np.ascontiguousarray(rows), wm[hh], "q4_k")) <= TOL
+    # transpose=False: x [..., h, L, n] @ W[h] -> [..., h, L, k]
+    xt = torch.randn(2, h, L, n, device=cuda).to(torch.bfloat16)
+    yt = ml(xt, transpose=False).float().cpu().numpy()
+    wd = np.stack([O.dequantize(wm[hh], "q4_k") for hh in range(h)])  # [h, n, k]
+    ref = np.einsum("bhln,hnk->bhlk", xt.float().cpu().numpy(), wd.astype(np.float32))
+    assert rel_err(yt, ref) <= TOL
