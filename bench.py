@@ -216,7 +216,7 @@ def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
             logits = x.float() @ router_w.t()
 
             def layer():
-                idx, sc = kq.moe_router_topk(logits, K, True)
+                idx, sc = kq.moe_router_topk(logits, K, True, shared_gate=False)
                 y = kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, cgu, cd, base, E, out_dtype=torch.float32)
                 if world > 1:
                     dist.all_reduce(y)

@@ -32,6 +32,7 @@ SIGNATURES = {
                                 _sz, _vp]),
     "kq_quantized_glu_workspace_size": (_sz, [_i32, _i64, _i64, _i64]),
     "kq_moe_router_topk": (_i32, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
+    "kq_moe_router_topk_ex": (_i32, [_vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
     "kq_moe_glu_gather": (_i32, [_i32, _vp, _i32, _i64, _i64, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp,
                                  _i32, _vp, _sz, _vp]),
     "kq_gather_qmv": (_i32, [_i32, _vp, _i32, _i64, _i32, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _sz,

@@ -559,8 +559,19 @@ int kq_moe_router_topk(const float *logits, int64_t t, int64_t e, int k, int nor
     if (e <= 0 || e > 1024) return fail(KQ_ERR_SHAPE, "moe_router_topk: expert count %lld outside 1..1024", (long long)e);
     if (k <= 0 || k > 16 || k > e) return fail(KQ_ERR_SHAPE, "moe_router_topk: k=%d outside 1..min(16, E)", k);
     if (t < 0) return fail(KQ_ERR_SHAPE, "moe_router_topk: t < 0");
-    return cuda_status(launch_router_topk(logits, (int)t, (int)e, k, norm_topk_prob, idx, scores, nullptr,
+    return cuda_status(launch_router_topk(logits, (int)t, (int)e, k, norm_topk_prob, idx, scores, 0, nullptr,
                                           (cudaStream_t)stream),
+                       "moe_router_topk");
+}
+
+int kq_moe_router_topk_ex(const float *logits, int64_t t, int64_t e, int k, int norm_topk_prob, int shared_gate,
+                          const float *per_expert_scale, int32_t *idx, float *scores, void *stream) {
+    g_msg[0] = 0;
+    if (e <= 0 || e > 1024) return fail(KQ_ERR_SHAPE, "moe_router_topk: expert count %lld outside 1..1024", (long long)e);
+    if (k <= 0 || k > 16 || k > e) return fail(KQ_ERR_SHAPE, "moe_router_topk: k=%d outside 1..min(16, E)", k);
+    if (t < 0) return fail(KQ_ERR_SHAPE, "moe_router_topk: t < 0");
+    return cuda_status(launch_router_topk(logits, (int)t, (int)e, k, norm_topk_prob, idx, scores, shared_gate ? 1 : 0,
+                                          per_expert_scale, (cudaStream_t)stream),
                        "moe_router_topk");
 }
 

@@ -133,7 +133,7 @@ cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int ebase, int e
 cudaError_t launch_moe_mix(const float *ys, const float *scores, const int32_t *idx, int ebase, int ecount, int T,
                            int k, int N, void *y, int y_dtype, cudaStream_t st);
 cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int norm, int32_t *idx, float *scores,
-                               int *err, cudaStream_t st);
+                               int shared_gate, const float *per_expert_scale, cudaStream_t st);
 
 int num_sms();
 // Sets the calling thread's kq_last_error() message.

@@ -19,11 +19,15 @@ namespace {
 
 constexpr int RT_MAXE = 1024, RT_MAXK = 16;
 
+// shared_gate: each logits row has E + 1 columns, the last one the shared
+// expert's gate; its sigmoid becomes score column k (scores rows of k + 1).
+// pes: optional per-expert scale applied to each picked score last.
 __global__ void router_kernel(const float *__restrict__ logits, int T, int E, int k, int norm, int32_t *__restrict__ idx,
-                              float *__restrict__ scores) {
+                              float *__restrict__ scores, int shared_gate, const float *__restrict__ pes) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
-    const float *l = logits + (int64_t)warp * E;
+    const int ld = E + (shared_gate ? 1 : 0), sk = k + (shared_gate ? 1 : 0);
+    const float *l = logits + (int64_t)warp * ld;
     constexpr int PER = RT_MAXE / 32;
     float p[PER];
     float mx = -INFINITY;
@@ -74,8 +78,10 @@ __global__ void router_kernel(const float *__restrict__ logits, int T, int E, in
     if (lane == 0) {
         for (int c = 0; c < k; c++) {
             idx[(int64_t)warp * k + c] = seli[c];
-            scores[(int64_t)warp * k + c] = norm ? sel[c] / tot : sel[c];
+            const float v = norm ? sel[c] / tot : sel[c];
+            scores[(int64_t)warp * sk + c] = pes ? v * pes[seli[c]] : v;
         }
+        if (shared_gate) scores[(int64_t)warp * sk + k] = 1.0f / (1.0f + expf(-l[E]));
     }
 }
 
@@ -150,11 +156,11 @@ __global__ void mix_kernel(const float *__restrict__ ys, const float *__restrict
 }  // namespace
 
 cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int norm, int32_t *idx, float *scores,
-                               int *err, cudaStream_t st) {
-    (void)err;
+                               int shared_gate, const float *per_expert_scale, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     const int threads = 256, per = threads / 32;
-    router_kernel<<<(T + per - 1) / per, threads, 0, st>>>(logits, T, E, k, norm, idx, scores);
+    router_kernel<<<(T + per - 1) / per, threads, 0, st>>>(logits, T, E, k, norm, idx, scores, shared_gate,
+                                                           per_expert_scale);
     return cudaGetLastError();
 }
 

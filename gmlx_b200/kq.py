@@ -39,7 +39,7 @@ from .synth import BLOCK_BYTES, CODECS, QK, codec_id
 __all__ = [
     "codecs", "codec_has_matmul", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
     "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
-    "moe_expert_layer_local", "quantized_matmul_allreduce",
+    "moe_expert_layer_local", "quantized_matmul_allreduce", "moe_glu_gather_shexp_kq", "gather_qmv_mix_kq",
 ]
 
 _DT = {torch.float32: _lib.KQ_F32, torch.float16: _lib.KQ_F16, torch.bfloat16: _lib.KQ_BF16}
@@ -268,21 +268,34 @@ def _stack(w: torch.Tensor) -> tuple[torch.Tensor, int, int]:
     return w, w.stride(1), w.stride(0)
 
 
-def moe_router_topk(logits: torch.Tensor, k: int, norm_topk_prob: bool = True, shared_gate=None,
-                    per_expert_scale=None):
-    """``kq.moe_router_topk``: softmax -> top-k -> optional renorm (f32)."""
-    if shared_gate is not None or per_expert_scale is not None:
-        raise NotImplementedError("moe_router_topk: shared_gate / per_expert_scale are not supported")
+def moe_router_topk(logits: torch.Tensor, k: int, norm_topk_prob: bool = True, shared_gate: bool = True,
+                    per_expert_scale: torch.Tensor | None = None):
+    """``kq.moe_router_topk(logits, k, norm_topk_prob, shared_gate=True, per_expert_scale=None)``:
+    softmax over the routed experts -> top-k (descending, ties to the lower id)
+    -> optional renormalisation, in f32, one launch.
+
+    shared_gate (the reference default): the last logits column is the shared
+    expert's gate (gmlx/modules.py:294-313 appends it); scores gain a last
+    column sigmoid(gate), idx stays [..., k].  shared_gate=False: every column
+    is a routed expert (gmlx/modules.py:446-447).  per_expert_scale [E]
+    multiplies each picked score (gmlx/modules.py:1043-1046)."""
     _need_cuda(logits)
     lg = logits.reshape(-1, logits.shape[-1]).float().contiguous()
-    t, e = lg.shape
+    t, cols = lg.shape
+    e = cols - 1 if shared_gate else cols
+    pes = None
+    if per_expert_scale is not None:
+        pes = per_expert_scale.reshape(-1).float().contiguous()
+        if pes.numel() != e:
+            raise ValueError(f"moe_router_topk: per_expert_scale has {pes.numel()} entries for {e} experts")
     idx = torch.empty(t, k, dtype=torch.int32, device=lg.device)
-    sc = torch.empty(t, k, dtype=torch.float32, device=lg.device)
+    sk = k + 1 if shared_gate else k
+    sc = torch.empty(t, sk, dtype=torch.float32, device=lg.device)
     if t:
-        _lib.check(_lib.load().kq_moe_router_topk(_p(lg), t, e, k, int(bool(norm_topk_prob)), _p(idx), _p(sc),
-                                                  _stream(lg.device)), "moe_router_topk")
-    shape = (*logits.shape[:-1], k)
-    return idx.reshape(shape), sc.reshape(shape)
+        _lib.check(_lib.load().kq_moe_router_topk_ex(_p(lg), t, e, k, int(bool(norm_topk_prob)), int(bool(shared_gate)),
+                                                     _p(pes), _p(idx), _p(sc), _stream(lg.device)),
+                   "moe_router_topk")
+    return idx.reshape(*logits.shape[:-1], k), sc.reshape(*logits.shape[:-1], sk)
 
 
 def _idx2d(idx: torch.Tensor, t: int) -> torch.Tensor:
@@ -318,6 +331,45 @@ def moe_glu_gather_kq(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor,
                                        wes, _lib.ACTS[act], _p(h), _DT[od], _p(ws), ws.numel(), _stream(x.device)),
                    "moe_glu_gather_kq")
     return h
+
+
+def moe_glu_gather_shexp_kq(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, shexp_gate_w: torch.Tensor,
+                            shexp_up_w: torch.Tensor, codec, idx: torch.Tensor, act: str = "silu",
+                            shexp_kquant_type=None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``kq.moe_glu_gather_shexp_kq`` (gmlx/modules.py:764-770): the routed GLU
+    gather with the shared expert riding along as slot ``k``:
+    ``h[t, :k] = moe_glu_gather_kq(...)``, ``h[t, k] = act(x Sg^T) * (x Su^T)``.
+    The shared expert's codec may differ (``shexp_kquant_type``); its
+    intermediate width must equal the routed experts'."""
+    t = x.reshape(-1, x.shape[-1]).shape[0]
+    k = idx.shape[-1]
+    sc = shexp_kquant_type or codec
+    f = gate_w.shape[-2]
+    if shexp_gate_w.shape[-2] != f:
+        raise ValueError(f"shared expert width {shexp_gate_w.shape[-2]} != routed width {f}")
+    od = out_dtype or x.dtype
+    h = torch.empty(t, k + 1, f, dtype=od, device=x.device)
+    h[:, :k] = moe_glu_gather_kq(x, gate_w, up_w, codec, idx, act=act, out_dtype=od).reshape(t, k, f)
+    h[:, k] = quantized_glu(x.reshape(t, -1), shexp_gate_w, shexp_up_w, sc, act=act, out_dtype=od)
+    return h
+
+
+def gather_qmv_mix_kq(h: torch.Tensor, w: torch.Tensor, shexp_w: torch.Tensor, codec, idx: torch.Tensor,
+                      scores: torch.Tensor, shexp_kquant_type=None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``kq.gather_qmv_mix_kq`` (gmlx/modules.py:775-779): the down projection of
+    the routed slots and the shared-expert slot with the routing mix in f32:
+    ``y[t] = sum_{j<k} scores[t,j] (h[t,j] W[idx[t,j]]^T) + scores[t,k] (h[t,k] S^T)``
+    (``scores[:, k]`` is the sigmoid shared gate from ``moe_router_topk``)."""
+    t, kp1 = h.shape[0], h.shape[1]
+    k = kp1 - 1
+    if idx.shape[-1] != k or scores.shape[-1] != kp1:
+        raise ValueError("gather_qmv_mix_kq: h [T, k+1, F], idx [T, k], scores [T, k+1]")
+    sc = shexp_kquant_type or codec
+    y = gather_qmv_mix_ns_kq(h[:, :k].contiguous(), w, codec, idx, scores[:, :k].contiguous(),
+                             out_dtype=torch.float32)
+    ys = quantized_matmul(h[:, k].contiguous(), shexp_w, None, sc, out_dtype=torch.float32)
+    y = y.reshape(t, -1) + scores[:, k:kp1].float() * ys
+    return y.to(out_dtype or h.dtype)
 
 
 def gather_qmv_kq(h: torch.Tensor, w: torch.Tensor, codec, idx: torch.Tensor, bias=None,

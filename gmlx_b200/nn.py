@@ -173,5 +173,5 @@ def qwen3_moe_forward(gate: nn.Module, switch_mlp: KQuantSwitchGLU, x: torch.Ten
     """Qwen3-MoE block forward (gmlx/moe_experts.py:226-240) on the fused ops:
     router logits -> kq.moe_router_topk (softmax, top-k, renorm) -> experts."""
     logits = gate(x).float()
-    idx, scores = kq.moe_router_topk(logits, top_k, norm_topk_prob)
+    idx, scores = kq.moe_router_topk(logits, top_k, norm_topk_prob, shared_gate=False)
     return switch_mlp(x, idx, scores)

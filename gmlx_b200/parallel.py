@@ -159,7 +159,7 @@ def ep_moe_forward(x, logits, top_k, gate_w, up_w, down_w, codec_gu, codec_d, ex
     """Expert-parallel MoE layer (decode): route all tokens, run the slots whose
     expert lies in [expert_base, expert_base + local experts), sum over ranks."""
     from . import kq
-    idx, scores = kq.moe_router_topk(logits, top_k, norm_topk_prob)
+    idx, scores = kq.moe_router_topk(logits, top_k, norm_topk_prob, shared_gate=False)
     y = kq.moe_expert_layer_local(x, idx, scores, gate_w, up_w, down_w, codec_gu, codec_d, expert_base)
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(y, group=group)

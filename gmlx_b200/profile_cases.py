@@ -47,7 +47,7 @@ def build(case):
         wg, wu, wd = _w("q4_k", f, d, 11, e), _w("q4_k", f, d, 12, e), _w("q6_k", d, f, 13, e)
         x = _x(t, d)
         logits = torch.randn(t, e, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
-        idx, sc = kq.moe_router_topk(logits, k, True)
+        idx, sc = kq.moe_router_topk(logits, k, True, shared_gate=False)
         return lambda: kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, "q4_k", "q6_k", 0, e)
     raise SystemExit(f"unknown case {case!r}; see the module docstring")
 

@@ -114,6 +114,16 @@ size_t kq_quantized_glu_workspace_size(int codec, int64_t m, int64_t n, int64_t 
 int kq_moe_router_topk(const float *logits, int64_t t, int64_t e, int k, int norm_topk_prob, int32_t *idx,
                        float *scores, void *stream);
 
+/* The full router surface kq.moe_router_topk(logits, k, norm_topk_prob,
+ * shared_gate=True, per_expert_scale=None) (gmlx/modules.py:751-752 with the
+ * shared-gate row appended by _build_router_cat, :294-313; shared_gate=False
+ * at :446-447; per_expert_scale at :1043-1046).  e = routed experts.
+ * shared_gate != 0: logits rows have e + 1 columns, the last the shared
+ * expert's gate; scores rows have k + 1 columns, the last sigmoid(gate).
+ * per_expert_scale [e] f32 (nullable) multiplies each picked score. */
+int kq_moe_router_topk_ex(const float *logits, int64_t t, int64_t e, int k, int norm_topk_prob, int shared_gate,
+                          const float *per_expert_scale, int32_t *idx, float *scores, void *stream);
+
 /* kq.moe_glu_gather_kq(x, gate_w, up_w, codec, idx, act):
  *   h[t][j][f] = act(x[t] . Wg[idx[t][j]][f]) * (x[t] . Wu[idx[t][j]][f])
  * x [t][d] f16/bf16; idx [t][k] int32 device; gate/up stacks [e][f] rows of

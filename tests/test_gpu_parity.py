@@ -148,9 +148,28 @@ def test_quantized_glu(cuda, codec):
 def test_router_topk(cuda):
     lg = synth.random_logits(64, 128, seed=3)
     idx_ref, sc_ref = O.router_topk(lg, 8, True)
-    idx, sc = kq.moe_router_topk(torch.from_numpy(lg).to(cuda), 8, True)
+    idx, sc = kq.moe_router_topk(torch.from_numpy(lg).to(cuda), 8, True, shared_gate=False)
     assert np.array_equal(idx.cpu().numpy(), idx_ref)
     assert np.allclose(sc.cpu().numpy(), sc_ref, rtol=1e-5, atol=1e-7)
+
+
+def test_router_topk_shared_gate_and_expert_scale(cuda):
+    """The reference defaults: shared_gate=True reads the last logits column
+    as the shared expert's gate (its sigmoid becomes score column k);
+    per_expert_scale multiplies each picked score."""
+    lg = synth.random_logits(64, 129, seed=4)
+    idx_ref, sc_ref = O.router_topk(np.ascontiguousarray(lg[:, :128]), 8, True)
+    idx, sc = kq.moe_router_topk(torch.from_numpy(lg).to(cuda), 8, True)
+    assert tuple(idx.shape) == (64, 8) and tuple(sc.shape) == (64, 9)
+    assert np.array_equal(idx.cpu().numpy(), idx_ref)
+    sc = sc.cpu().numpy()
+    assert np.allclose(sc[:, :8], sc_ref, rtol=1e-5, atol=1e-7)
+    assert np.allclose(sc[:, 8], 1 / (1 + np.exp(-lg[:, 128].astype(np.float64))), rtol=1e-5, atol=1e-7)
+    pes = np.random.default_rng(5).random(128).astype(np.float32) + 0.5
+    idx2, sc2 = kq.moe_router_topk(torch.from_numpy(np.ascontiguousarray(lg[:, :128])).to(cuda), 8, True,
+                                   shared_gate=False, per_expert_scale=torch.from_numpy(pes).to(cuda))
+    assert np.array_equal(idx2.cpu().numpy(), idx_ref)
+    assert np.allclose(sc2.cpu().numpy(), sc_ref * pes[idx_ref], rtol=1e-5, atol=1e-7)
 
 
 def _moe_case(codec_gu, codec_d, e, d, f, t, k, seed):
@@ -241,7 +260,7 @@ def test_nn_modules_fused_and_stock_paths_agree(cuda):
     m.down_proj.weight.copy_(torch.from_numpy(wd))
     xb = synth.random_activations(t, d, seed=4)
     x = to_dev_x(xb, cuda)
-    idx, sc = kq.moe_router_topk(torch.from_numpy(synth.random_logits(t, e, seed=5)).to(cuda), k, True)
+    idx, sc = kq.moe_router_topk(torch.from_numpy(synth.random_logits(t, e, seed=5)).to(cuda), k, True, shared_gate=False)
     y_fused = m(x, idx, sc).float().cpu().numpy()
     y_stock = m(x.repeat(32, 1), idx.repeat(32, 1), sc.repeat(32, 1))[:t].float().cpu().numpy()  # >= 64 slots
     ii, ss = idx.cpu().numpy(), sc.cpu().numpy()
@@ -306,7 +325,7 @@ def test_expert_parallel_partials_sum_to_full_layer(cuda, codec_gu, codec_d):
     e, d, f, k, t = 16, 512, 256, 4, 3
     wg, wu, wd, x, lg = _moe_case(codec_gu, codec_d, e, d, f, t, k, seed=80)
     xd = to_dev_x(x, cuda)
-    idx, sc = kq.moe_router_topk(torch.from_numpy(lg).to(cuda), k, True)
+    idx, sc = kq.moe_router_topk(torch.from_numpy(lg).to(cuda), k, True, shared_gate=False)
     tw = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
     full = kq.moe_expert_layer_local(xd, idx, sc, tw(wg), tw(wu), tw(wd), codec_gu, codec_d, 0, e,
                                      out_dtype=torch.float32)
@@ -465,3 +484,36 @@ def test_embedding_and_multilinear_modules(cuda):
     wd = np.stack([O.dequantize(wm[hh], "q4_k") for hh in range(h)])  # [h, n, k]
     ref = np.einsum("bhln,hnk->bhlk", xt.float().cpu().numpy(), wd.astype(np.float32))
     assert rel_err(yt, ref) <= TOL
+
+
+def test_shared_expert_slot_ops(cuda):
+    """moe_glu_gather_shexp_kq / gather_qmv_mix_kq (the shared expert as slot k,
+    sigmoid-gated in the mix) against the oracle, shared expert in another codec."""
+    e, d, f, k, t = 8, 512, 256, 2, 3
+    wg, wu, wd, x, _ = _moe_case("q4_k", "q6_k", e, d, f, t, k, seed=150)
+    sg = synth.random_weight("q6_k", f, d, seed=151)
+    su = synth.random_weight("q6_k", f, d, seed=152)
+    sd = synth.random_weight("q4_k", d, f, seed=153)
+    lg = synth.random_logits(t, e + 1, seed=154)
+    tw = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    idx, sc = kq.moe_router_topk(tw(lg), k, True)
+    h = kq.moe_glu_gather_shexp_kq(to_dev_x(x, cuda), tw(wg), tw(wu), tw(sg), tw(su), "q4_k", idx,
+                                   shexp_kquant_type="q6_k")
+    assert tuple(h.shape) == (t, k + 1, f)
+    ii, ss = idx.cpu().numpy(), sc.cpu().numpy()
+    silu = lambda g: g / (1 + np.exp(-g))  # noqa: E731
+    for ti in range(t):
+        xr = x[ti:ti + 1]
+        for j in range(k + 1):
+            gw, uw, c = (wg[ii[ti, j]], wu[ii[ti, j]], "q4_k") if j < k else (sg, su, "q6_k")
+            g = O.matmul(xr, gw, c)[0].astype(np.float64)
+            u = O.matmul(xr, uw, c)[0].astype(np.float64)
+            assert rel_err(h[ti, j].float().cpu().numpy(), silu(g) * u) <= TOL
+    y = kq.gather_qmv_mix_kq(h, tw(wd), tw(sd), "q6_k", idx, sc, shexp_kquant_type="q4_k", out_dtype=torch.float32)
+    hb = synth.f32_to_bf16_bits(h.float().cpu().numpy())
+    ref = np.zeros((t, d))
+    for ti in range(t):
+        for j in range(k):
+            ref[ti] += ss[ti, j] * O.matmul(hb[ti, j][None], wd[ii[ti, j]], "q6_k")[0]
+        ref[ti] += ss[ti, k] * O.matmul(hb[ti, k][None], sd, "q4_k")[0]
+    assert rel_err(y.cpu().numpy(), ref) <= TOL
