@@ -517,3 +517,23 @@ def test_shared_expert_slot_ops(cuda):
             ref[ti] += ss[ti, j] * O.matmul(hb[ti, j][None], wd[ii[ti, j]], "q6_k")[0]
         ref[ti] += ss[ti, k] * O.matmul(hb[ti, k][None], sd, "q4_k")[0]
     assert rel_err(y.cpu().numpy(), ref) <= TOL
+
+
+def test_gguf_loaded_weights_drive_the_kernels(cuda, tmp_path):
+    """A GGUF file written with gguf-py, loaded by gmlx_b200.gguf_io straight
+    into HBM, feeds quantized_matmul (checked against the oracle)."""
+    gguf = pytest.importorskip("gguf")
+    from gmlx_b200 import gguf_io
+    w = synth.random_weight("q6_k", 256, 768, seed=160)
+    wr = gguf.GGUFWriter(str(tmp_path / "w.gguf"), "llama")
+    wr.add_tensor("blk.0.ffn_down.weight", w, raw_dtype=gguf.GGMLQuantizationType.Q6_K)
+    wr.write_header_to_file()
+    wr.write_kv_data_to_file()
+    wr.write_tensors_to_file()
+    wr.close()
+    arrays, codecs, _, shapes = gguf_io.load_gguf(str(tmp_path / "w.gguf"), device=cuda)
+    wd = arrays["blk.0.ffn_down.weight"]
+    assert wd.is_cuda and codecs["blk.0.ffn_down.weight"] == "q6_k" and shapes["blk.0.ffn_down.weight"] == (768, 256)
+    x = synth.random_activations(2, 768, seed=161)
+    y = kq.quantized_matmul(to_dev_x(x, cuda), wd, arrays["blk.0.ffn_down.scales"], "q6_k", out_dtype=torch.float32)
+    assert rel_err(y.cpu().numpy(), O.matmul(x, w, "q6_k")) <= TOL
