@@ -147,7 +147,8 @@ size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
 
 int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t xs, const void *w, const void *w2,
               int64_t n, int64_t wstride, int act, void *y, int y_dtype, int64_t ys, void *ws, size_t ws_bytes,
-              void *stream, const char *what) {
+              void *stream, const char *what, const void *bias = nullptr, int bias_dtype = 0) {
+    if (bias && (w2 || !out_dtype_ok(bias_dtype))) return fail(KQ_ERR_DTYPE, "%s: bad bias", what);
     int rc;
     if ((rc = check_weights(codec, w, k, wstride, what))) return rc;
     if (w2 && (rc = check_weights(codec, w2, k, wstride, what))) return rc;
@@ -176,7 +177,10 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
         g.y_dtype = y_dtype;
         g.y_row_stride = ys;
         g.err = (int *)ws;
-        return cuda_status(launch_gemm(g, (char *)ws + p.ys_off, (cudaStream_t)stream), what);
+        cudaError_t ce = launch_gemm(g, (char *)ws + p.ys_off, (cudaStream_t)stream);
+        if (ce == cudaSuccess && bias)
+            ce = launch_add_bias(y, y_dtype, ys, m, n, bias, bias_dtype, (cudaStream_t)stream);
+        return cuda_status(ce, what);
     }
     GemvArgs a = dense_args(codec, x, x_dtype, m, k, xs, w, w2, n, wstride, y, y_dtype, ys, act);
     size_t pb, cb;
@@ -188,6 +192,8 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
     a.err = (int *)ws;
     a.counters = (int *)((char *)ws + p.cnt_off);
     a.partial = (float *)((char *)ws + p.part_off);
+    a.bias = bias;
+    a.bias_dtype = bias_dtype;
     return cuda_status(launch_gemv(a, (cudaStream_t)stream), what);
 }
 
@@ -477,6 +483,15 @@ int kq_quantized_matmul(int codec, const void *x, int x_dtype, int64_t m, int64_
     g_msg[0] = 0;
     return run_dense(codec, x, x_dtype, m, k, x_row_stride, w, nullptr, n, w_row_stride, ACT_NONE, y, y_dtype,
                      y_row_stride, workspace, workspace_bytes, stream, "quantized_matmul");
+}
+
+int kq_quantized_matmul_bias(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
+                             const void *w, int64_t n, int64_t w_row_stride, const void *bias, int bias_dtype, void *y,
+                             int y_dtype, int64_t y_row_stride, void *workspace, size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    if (!bias) return fail(KQ_ERR_SHAPE, "quantized_matmul_bias: bias required");
+    return run_dense(codec, x, x_dtype, m, k, x_row_stride, w, nullptr, n, w_row_stride, ACT_NONE, y, y_dtype,
+                     y_row_stride, workspace, workspace_bytes, stream, "quantized_matmul_bias", bias, bias_dtype);
 }
 
 size_t kq_allreduce_buffer_bytes(int world, int64_t n) {

@@ -187,6 +187,14 @@ template <bool XS> __device__ __forceinline__ uint2 ldx8(const uint16_t *p) {
     }
 }
 
+// optional per-output bias (dense, non-GLU): added once to each final value
+__device__ __forceinline__ float bias_of(const GemvArgs &a, int n) {
+    if (!a.bias) return 0.f;
+    if (a.bias_dtype == F32) return reinterpret_cast<const float *>(a.bias)[n];
+    if (a.bias_dtype == BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(a.bias)[n]);
+    return __half2float(reinterpret_cast<const __half *>(a.bias)[n]);
+}
+
 struct Tile {
     int g, tile, m, e;
 };
@@ -1007,7 +1015,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     const int ar_par = (int)(ar_epoch & 1u);
     auto emit = [&](const Tile &T, int n, float v) {
         if (a.ar_world == 0) {
-            store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v);
+            store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v + bias_of(a, n));
             return;
         }
         const int64_t off = ((int64_t)(ar_par * a.ar_world + a.ar_rank)) * a.N + n;
@@ -1181,7 +1189,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                 for (int n = ctid; n < a.N; n += CW * 32) {
                     float v = 0.f;
                     for (int r = 0; r < a.ar_world; r++) v += __ldcv(slots + (int64_t)r * a.N + n);
-                    store_out(a.y, a.y_dtype, n, v);
+                    store_out(a.y, a.y_dtype, n, v + bias_of(a, n));
                 }
             }
             return;
@@ -1305,7 +1313,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                     if (GLU) v2 += red[w * RCS + tok * RED_TS + row + 16];
                 }
                 if (GLU) v = apply_act(a.act, v) * v2;
-                store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, tok) * a.y_row_stride + n, v);
+                store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, tok) * a.y_row_stride + n, v + bias_of(a, n));
             }
         } else {
             // partial tile: slot 2c for the CTA's first tile, 2c+1 for its last
@@ -1343,7 +1351,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                         if (GLU) v2 += __ldcg(pp + 16);
                     }
                     if (GLU) v = apply_act(a.act, v) * v2;
-                    store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, tok) * a.y_row_stride + n, v);
+                    store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, tok) * a.y_row_stride + n, v + bias_of(a, n));
                 }
                 if (ctid == 0) a.counters[gt] = 0;
             }

@@ -58,6 +58,8 @@ struct GemvArgs {
     // stores its f32 partial rows into each peer's communication buffer, then
     // sums all ranks' partials into y.  ar_bufs: device array [ar_world] of the
     // buffers (this rank's own at [ar_rank]); ar_world == 0: plain output.
+    const void *bias;  // optional [N] per-output bias (dense plain GEMV), bias_dtype F32/F16/BF16
+    int bias_dtype;
     unsigned char *const *ar_bufs;
     int ar_world, ar_rank;
     int dyn;         // set by the launcher: lane-per-row tiles handed out dynamically
@@ -130,6 +132,9 @@ cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int ebase, int e
                               const int32_t *xidx, int gsize, int *n_groups, int *grp_expert, int *grp_count,
                               int *grp_xrow, int *grp_orow, int max_groups, int *err, cudaStream_t st);
 // y[t][n] = sum over local slots j of scores[t][j] * ys[t*k+j][n]  (fixed j order).
+// y[r][n] += bias[n] for rows r < m (the prefill path of the bias op)
+cudaError_t launch_add_bias(void *y, int y_dtype, int64_t y_row_stride, int64_t m, int64_t n, const void *bias,
+                            int bias_dtype, cudaStream_t st);
 cudaError_t launch_moe_mix(const float *ys, const float *scores, const int32_t *idx, int ebase, int ecount, int T,
                            int k, int N, void *y, int y_dtype, cudaStream_t st);
 cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int norm, int32_t *idx, float *scores,

@@ -153,7 +153,32 @@ __global__ void mix_kernel(const float *__restrict__ ys, const float *__restrict
     else reinterpret_cast<__half *>(y)[i] = __float2half_rn(v);
 }
 
+__global__ void add_bias_kernel(void *y, int y_dtype, int64_t ys, int64_t m, int64_t n, const void *bias, int bd) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m * n) return;
+    const int64_t r = i / n, c = i - r * n;
+    const float b = bd == F32 ? reinterpret_cast<const float *>(bias)[c]
+                  : bd == BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(bias)[c])
+                               : __half2float(reinterpret_cast<const __half *>(bias)[c]);
+    const int64_t o = r * ys + c;
+    if (y_dtype == F32) reinterpret_cast<float *>(y)[o] += b;
+    else if (y_dtype == BF16) {
+        __nv_bfloat16 *p = reinterpret_cast<__nv_bfloat16 *>(y) + o;
+        *p = __float2bfloat16_rn(__bfloat162float(*p) + b);
+    } else {
+        __half *p = reinterpret_cast<__half *>(y) + o;
+        *p = __float2half_rn(__half2float(*p) + b);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_add_bias(void *y, int y_dtype, int64_t y_row_stride, int64_t m, int64_t n, const void *bias,
+                            int bias_dtype, cudaStream_t st) {
+    if (m * n == 0) return cudaSuccess;
+    add_bias_kernel<<<(unsigned)((m * n + 255) / 256), 256, 0, st>>>(y, y_dtype, y_row_stride, m, n, bias, bias_dtype);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int norm, int32_t *idx, float *scores,
                                int shared_gate, const float *per_expert_scale, cudaStream_t st) {

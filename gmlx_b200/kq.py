@@ -39,7 +39,7 @@ from .synth import BLOCK_BYTES, CODECS, QK, codec_id
 __all__ = [
     "codecs", "codec_has_matmul", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
     "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
-    "moe_expert_layer_local", "quantized_matmul_allreduce", "moe_glu_gather_shexp_kq", "gather_qmv_mix_kq",
+    "moe_expert_layer_local", "quantized_matmul_allreduce", "quantized_matmul_qmv_bias", "moe_glu_gather_shexp_kq", "gather_qmv_mix_kq",
 ]
 
 _DT = {torch.float32: _lib.KQ_F32, torch.float16: _lib.KQ_F16, torch.bfloat16: _lib.KQ_BF16}
@@ -201,6 +201,31 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, 
         ws = _workspace(x.device, _ws_size("kq_quantized_matmul_workspace_size", c, m, n, k))
         _lib.check(L.kq_quantized_matmul(c, _p(x2), _DT[x2.dtype], m, k, x2.stride(0), _p(w), n, wstride, _p(y),
                                          _DT[od], n, _p(ws), ws.numel(), _stream(x.device)), "quantized_matmul")
+    return y.reshape(*x.shape[:-1], n)
+
+
+def quantized_matmul_qmv_bias(x: torch.Tensor, w: torch.Tensor, scales, bias: torch.Tensor, codec=None,
+                              out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``kq.quantized_matmul_qmv_bias(x, w, scales, bias, codec)``: ``x @ dequant(w).T + bias``
+    in one dispatch (gmlx/qkv_fuse.py:80)."""
+    c = _cid(codec)
+    _need_cuda(x, w, bias)
+    k = _wire_k(w, c)
+    w, wstride = _rows2d(w)
+    n = w.shape[-2] if w.dim() >= 2 else 1
+    b = bias.reshape(-1).contiguous()
+    if b.numel() != n or b.dtype not in _DT:
+        raise ValueError(f"bias must have {n} f32/f16/bf16 entries")
+    x2 = _act_2d(x, k)
+    m = x2.shape[0]
+    od = out_dtype or x.dtype
+    y = torch.empty(m, n, dtype=od, device=x.device)
+    if m:
+        L = _lib.load()
+        ws = _workspace(x.device, _ws_size("kq_quantized_matmul_workspace_size", c, m, n, k))
+        _lib.check(L.kq_quantized_matmul_bias(c, _p(x2), _DT[x2.dtype], m, k, x2.stride(0), _p(w), n, wstride, _p(b),
+                                              _DT[b.dtype], _p(y), _DT[od], n, _p(ws), ws.numel(), _stream(x.device)),
+                   "quantized_matmul_qmv_bias")
     return y.reshape(*x.shape[:-1], n)
 
 

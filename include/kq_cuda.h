@@ -182,6 +182,15 @@ size_t kq_moe_expert_layer_workspace_size(int codec_gu, int codec_d, int64_t t, 
                                           int64_t f, int h_dtype);
 
 /* Size of the fixed scratch array behind kq_quantized_matmul_noalloc. */
+/* kq.quantized_matmul_qmv_bias(x, w, scales, bias, codec): y = x . dequant(w)^T
+ * + bias in one dispatch (gmlx/qkv_fuse.py:80, the row-concatenated q|k|v
+ * projection with its biases).  bias [n] in KQ_F32 / KQ_F16 / KQ_BF16; the
+ * workspace is kq_quantized_matmul_workspace_size's.  Decode shapes add the
+ * bias in the GEMV's store; prefill shapes add it after the GEMM. */
+int kq_quantized_matmul_bias(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
+                             const void *w, int64_t n, int64_t w_row_stride, const void *bias, int bias_dtype, void *y,
+                             int y_dtype, int64_t y_row_stride, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- Row-parallel decode with the all-reduce fused in (tensor parallelism)
  *
  * Replaces the pair "quantized_matmul on this rank's K shard, then sum over

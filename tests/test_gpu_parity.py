@@ -537,3 +537,18 @@ def test_gguf_loaded_weights_drive_the_kernels(cuda, tmp_path):
     x = synth.random_activations(2, 768, seed=161)
     y = kq.quantized_matmul(to_dev_x(x, cuda), wd, arrays["blk.0.ffn_down.scales"], "q6_k", out_dtype=torch.float32)
     assert rel_err(y.cpu().numpy(), O.matmul(x, w, "q6_k")) <= TOL
+
+
+@pytest.mark.parametrize("codec,m", [("q4_k", 1), ("q6_k", 1), ("iq2_xxs", 3), ("q4_k", 64)])
+def test_quantized_matmul_qmv_bias(cuda, codec, m):
+    """x @ W^T + bias in one dispatch (decode: in the GEMV store; prefill: after the GEMM)."""
+    n, k = 320, 1024
+    w = synth.random_weight(codec, n, k, seed=170)
+    x = synth.random_activations(m, k, seed=171)
+    b = np.random.default_rng(172).standard_normal(n).astype(np.float32)
+    ref = O.matmul(x, w, codec) + b
+    y = kq.quantized_matmul_qmv_bias(to_dev_x(x, cuda), torch.from_numpy(w).to(cuda), None,
+                                     torch.from_numpy(b).to(cuda).to(torch.bfloat16), codec, out_dtype=torch.float32)
+    bb = torch.from_numpy(b).to(torch.bfloat16).float().numpy()
+    assert rel_err(y.cpu().numpy(), O.matmul(x, w, codec) + bb) <= TOL
+    assert rel_err(y.cpu().numpy(), ref) <= 2 * TOL
