@@ -355,7 +355,10 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     // groups of <= 8 slots: one MMA n-tile; an expert with more routed rows
     // streams its weights once per 8 rows (decode routes few rows per expert)
     const int64_t per_expert = mode == 2 ? slots : tokens;  // distinct experts per token bound group sizes
-    const int gsize = (int)(per_expert < 8 ? per_expert : 8);
+    // IQ2_XXS decode is ALU-bound: with sparse routing (on average well under one
+    // slot per expert) one-slot groups take the one-row integer path, faster
+    // than 8-row MMA groups even counting the few experts streamed twice
+    const int gsize = (codec == KQ_IQ2_XXS && slots * 4 <= etotal) ? 1 : (int)(per_expert < 8 ? per_expert : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;
@@ -417,7 +420,8 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
 
 size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_t n, int64_t kin, int act,
                  bool mix) {
-    const int gsize = (int)(per_expert < 8 ? (per_expert > 0 ? per_expert : 1) : 8);
+    // IQ2_XXS may run with one-slot groups (see run_routed): size for those too
+    const int gsize = codec == KQ_IQ2_XXS ? 1 : (int)(per_expert < 8 ? (per_expert > 0 ? per_expert : 1) : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;

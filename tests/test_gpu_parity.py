@@ -552,3 +552,25 @@ def test_quantized_matmul_qmv_bias(cuda, codec, m):
     bb = torch.from_numpy(b).to(torch.bfloat16).float().numpy()
     assert rel_err(y.cpu().numpy(), O.matmul(x, w, codec) + bb) <= TOL
     assert rel_err(y.cpu().numpy(), ref) <= 2 * TOL
+
+
+def test_iq2_sparse_routing_single_slot_groups(cuda):
+    """IQ2_XXS with sparse routing (slots * 4 <= experts) runs one-slot groups on
+    the one-row path; experts routed by two tokens are streamed twice."""
+    e, d, f, k, t = 64, 512, 256, 8, 2
+    wg, wu, wd, x, _ = _moe_case("iq2_xxs", "iq2_xxs", e, d, f, t, k, seed=180)
+    idx = np.array([[3, 7, 9, 11, 20, 33, 40, 63], [7, 3, 1, 2, 9, 50, 60, 61]], np.int32)  # 3, 7, 9 twice
+    sc = np.random.default_rng(181).random((t, k)).astype(np.float32)
+    tw = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    y = kq.moe_expert_layer_local(to_dev_x(x, cuda), tw(idx), tw(sc), tw(wg), tw(wu), tw(wd), "iq2_xxs", "iq2_xxs",
+                                  0, e, out_dtype=torch.float32).cpu().numpy()
+    ref = np.zeros((t, d))
+    for ti in range(t):
+        for j in range(k):
+            ex = idx[ti, j]
+            g = O.matmul(x[ti:ti + 1], wg[ex], "iq2_xxs")[0].astype(np.float64)
+            u = O.matmul(x[ti:ti + 1], wu[ex], "iq2_xxs")[0].astype(np.float64)
+            hb = synth.f32_to_bf16_bits((g / (1 + np.exp(-g)) * u).astype(np.float32))[None]
+            ref[ti] += sc[ti, j] * O.matmul(hb, wd[ex], "iq2_xxs")[0]
+    assert rel_err(y, ref) <= TOL
+    assert kq.workspace_error() == 0
