@@ -51,17 +51,17 @@ int cuda_status(cudaError_t e, const char *what) {
     return fail(KQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-bool codec_ok(int c) { return c == KQ_Q4_K || c == KQ_Q6_K || c == KQ_IQ2_XXS; }
+bool codec_ok(int c) { return c == KQ_Q4_K || c == KQ_Q5_K || c == KQ_Q6_K || c == KQ_IQ2_XXS; }
 bool act_dtype_ok(int d) { return d == KQ_F16 || d == KQ_BF16; }
 bool out_dtype_ok(int d) { return d == KQ_F32 || d == KQ_F16 || d == KQ_BF16; }
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 int check_weights(int codec, const void *w, int64_t k, int64_t row_stride, const char *what) {
-    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q4_k=12, q6_k=14, iq2_xxs=16)", what, codec);
+    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16)", what, codec);
     if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a positive multiple of %d", what, (long long)k, QK);
     const int64_t rb = k / QK * block_bytes(codec);
     if (row_stride < rb) return fail(KQ_ERR_SHAPE, "%s: row stride %lld < row bytes %lld", what, (long long)row_stride, (long long)rb);
-    const int64_t need = codec == KQ_Q4_K ? 16 : 2;
+    const int64_t need = (codec == KQ_Q4_K || codec == KQ_Q5_K) ? 16 : 2;
     if (((uintptr_t)w | (uintptr_t)row_stride) % need)
         return fail(KQ_ERR_ALIGN, "%s: weight base/row stride must be %lld-byte aligned for codec %d", what, (long long)need, codec);
     return KQ_OK;
@@ -135,10 +135,11 @@ int gemm_min_m() {
     return v;
 }
 
-bool use_gemm(int64_t m) { return m >= gemm_min_m(); }
+// Q5_K has a one-row GEMV only: every other batch goes to the tcgen05 GEMM
+bool use_gemm(int64_t m, int codec = 0) { return m >= gemm_min_m() || (codec == KQ_Q5_K && m >= 2); }
 
 size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
-    if (use_gemm(m)) return plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0).total;
+    if (use_gemm(m, codec)) return plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0).total;
     GemvArgs a = dense_args(codec, nullptr, KQ_BF16, m, k, k, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
@@ -157,7 +158,7 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
     if (m < 0 || n <= 0 || xs < k || ys < n) return fail(KQ_ERR_SHAPE, "%s: bad sizes m=%lld n=%lld", what, (long long)m, (long long)n);
     if (m == 0) return KQ_OK;
     if (n > 0x7fffffff || k > 0x7fffffff) return fail(KQ_ERR_SHAPE, "%s: n/k too large", what);
-    if (use_gemm(m) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
+    if (use_gemm(m, codec) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
         const WsPlan p = plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0);
         if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
             return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
@@ -358,7 +359,9 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     // IQ2_XXS decode is ALU-bound: with sparse routing (on average well under one
     // slot per expert) one-slot groups take the one-row integer path, faster
     // than 8-row MMA groups even counting the few experts streamed twice
-    const int gsize = (codec == KQ_IQ2_XXS && slots * 4 <= etotal) ? 1 : (int)(per_expert < 8 ? per_expert : 8);
+    const int gsize = ((codec == KQ_IQ2_XXS && slots * 4 <= etotal) || codec == KQ_Q5_K)
+                          ? 1  // Q5_K: the one-row path is its only GEMV
+                          : (int)(per_expert < 8 ? per_expert : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;
@@ -421,7 +424,8 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
 size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_t n, int64_t kin, int act,
                  bool mix) {
     // IQ2_XXS may run with one-slot groups (see run_routed): size for those too
-    const int gsize = codec == KQ_IQ2_XXS ? 1 : (int)(per_expert < 8 ? (per_expert > 0 ? per_expert : 1) : 8);
+    const int gsize = (codec == KQ_IQ2_XXS || codec == KQ_Q5_K) ? 1
+                                                                 : (int)(per_expert < 8 ? (per_expert > 0 ? per_expert : 1) : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;
@@ -453,9 +457,9 @@ int kq_version(void) { return 100; }
 const char *kq_last_error(void) { return g_msg; }
 
 int kq_codecs(int *out, int cap) {
-    static const int ids[3] = {KQ_Q4_K, KQ_Q6_K, KQ_IQ2_XXS};
-    for (int i = 0; i < 3 && i < cap; i++) out[i] = ids[i];
-    return 3;
+    static const int ids[4] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS};
+    for (int i = 0; i < 4 && i < cap; i++) out[i] = ids[i];
+    return 4;
 }
 
 int kq_codec_has_matmul(int codec) { return codec_ok(codec) ? 1 : 0; }

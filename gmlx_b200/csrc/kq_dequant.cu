@@ -29,6 +29,19 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
         const uint8_t *q = b + 16 + 32 * c + i0;
 #pragma unroll
         for (int i = 0; i < 8; i++) o[i] = dl * (float)((q[i] >> (4 * h)) & 15) - ml;
+    } else if constexpr (C == Q5_K) {  // Q4_K layout + 32 bytes of fifth bits (bit j of qh[l]: sub-block j)
+        const int j = lane >> 2, i0 = 8 * (lane & 3), c = j >> 1, h = j & 1;
+        const float d = half_bits_to_float(ld_u16(b));
+        const float dmin = half_bits_to_float(ld_u16(b + 2));
+        const uint32_t s0 = ld_u32_unaligned(b + 4), s1 = ld_u32_unaligned(b + 8), s2 = ld_u32_unaligned(b + 12);
+        uint32_t sc03, sc47, m03, m47;
+        q4k_unpack_scales(s0, s1, s2, sc03, sc47, m03, m47);
+        const uint32_t scw = j < 4 ? sc03 : sc47, mw = j < 4 ? m03 : m47;
+        const float dl = d * byte_f(scw, j & 3), ml = dmin * byte_f(mw, j & 3);
+        const uint8_t *q = b + 48 + 32 * c + i0, *qh = b + 16 + i0;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            o[i] = dl * (float)(((q[i] >> (4 * h)) & 15) | (((qh[i] >> j) & 1) << 4)) - ml;
     } else if constexpr (C == Q6_K) {
         const int i0 = 8 * lane, hf = i0 >> 7, s = (i0 & 127) >> 5, lo = i0 & 31;
         const float d = half_bits_to_float(ld_u16(b + 208));
@@ -229,6 +242,7 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     if (rows * nb == 0) return cudaSuccess;
     switch (codec) {
     case Q4_K: return launch_deq<Q4_K>(w, rows, nb, row_stride, out, dtype, st);
+    case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st);
     default: return launch_deq<IQ2_XXS>(w, rows, nb, row_stride, out, dtype, st);
     }

@@ -57,6 +57,7 @@ constexpr int RED_TS = 36;        // token stride (floats) of the reduction buff
 // request-rate bound on the TMA engine).
 template <int C> struct GCfg;
 template <> struct GCfg<Q4_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // (dsc, -mt) x 2 rows
+template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1; };    // dsc x 2 rows
 template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 2; };  // db x 2 rows
 template <int C> constexpr int KB_OF = NCOL * GCfg<C>::BPW;
@@ -591,6 +592,63 @@ __device__ __forceinline__ float dp_q4k_dot(const Q4Regs &r, const uint32_t *xq,
     return acc;
 }
 
+// Lane-per-row Q5_K: the Q4_K dot with the fifth bit of every weight OR-ed in
+// from the 32 qh bytes (bit j of qh[l] is weight l of sub-block j).
+struct Q5Regs {
+    uint4 h, qh[2], w[8];
+};
+
+__device__ __forceinline__ void dp_q5k_load(const uint8_t *row, Q5Regs &r) {
+    r.h = *reinterpret_cast<const uint4 *>(row);
+    r.qh[0] = *reinterpret_cast<const uint4 *>(row + 16);
+    r.qh[1] = *reinterpret_cast<const uint4 *>(row + 32);
+#pragma unroll
+    for (int i = 0; i < 8; i++) r.w[i] = *reinterpret_cast<const uint4 *>(row + 48 + 16 * i);
+}
+
+__device__ __forceinline__ float dp_q5k_dot(const Q5Regs &r, const uint32_t *xq, const float *xsc) {
+    const float d = half_bits_to_float(r.h.x & 0xffffu), dmin = half_bits_to_float(r.h.x >> 16);
+    uint32_t sc03, sc47, m03, m47;
+    q4k_unpack_scales(r.h.y, r.h.z, r.h.w, sc03, sc47, m03, m47);
+    const uint32_t qh8[8] = {r.qh[0].x, r.qh[0].y, r.qh[0].z, r.qh[0].w, r.qh[1].x, r.qh[1].y, r.qh[1].z, r.qh[1].w};
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint4 wa = r.w[2 * c], wb = r.w[2 * c + 1];
+        const uint32_t w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        int sl = 0, sh = 0;
+#pragma unroll
+        for (int h4 = 0; h4 < 2; h4++) {
+            const uint4 xl0 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 8 * h4);
+            const uint4 xl1 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 8 * h4 + 4);
+            const uint4 xh0 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 16 + 8 * h4);
+            const uint4 xh1 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 16 + 8 * h4 + 4);
+            const uint32_t xl[8] = {xl0.x, xl0.y, xl0.z, xl0.w, xl1.x, xl1.y, xl1.z, xl1.w};
+            const uint32_t xh[8] = {xh0.x, xh0.y, xh0.z, xh0.w, xh1.x, xh1.y, xh1.z, xh1.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t w = w8[4 * h4 + i], q5 = qh8[4 * h4 + i];
+                const int lo = (int)((w & 0x0f0f0f0fu) | (((q5 >> (2 * c)) & 0x01010101u) << 4));
+                const int hi = (int)(((w >> 4) & 0x0f0f0f0fu) | (((q5 >> (2 * c + 1)) & 0x01010101u) << 4));
+                sl = __dp2a_lo((int)xl[2 * i], lo, sl);
+                sl = __dp2a_hi((int)xl[2 * i + 1], lo, sl);
+                sh = __dp2a_lo((int)xh[2 * i], hi, sh);
+                sh = __dp2a_hi((int)xh[2 * i + 1], hi, sh);
+            }
+        }
+        const int j0 = 2 * c, j1 = 2 * c + 1;
+        const uint32_t scw = j0 < 4 ? sc03 : sc47, mw = j0 < 4 ? m03 : m47;
+        const float sc0 = (float)((scw >> (8 * (j0 & 3))) & 63u), sc1 = (float)((scw >> (8 * (j1 & 3))) & 63u);
+        const float m0 = (float)((mw >> (8 * (j0 & 3))) & 63u), m1 = (float)((mw >> (8 * (j1 & 3))) & 63u);
+        acc = fmaf(d * sc0 * xsc[j0], (float)sl, acc);
+        acc = fmaf(d * sc1 * xsc[j1], (float)sh, acc);
+        acc = fmaf(-dmin * m0, xsc[8 + j0], acc);
+        acc = fmaf(-dmin * m1, xsc[8 + j1], acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 // Lane-per-row Q6_K: lanes 0-15 / 16-31 of a warp take the two 128-weight
 // halves of rows row0..row0+15 of one block.  q6 = ql nibble | qh pair << 4 is
 // dotted unsigned with dp2a; the -32 offset is applied as -32 * sum(x) per
@@ -987,6 +1045,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q4k_dot(r, xq, xsc);
+        } else if constexpr (C == Q5_K) {
+            Q5Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_q5k_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_q5k_dot(r, xq, xsc);
         } else if constexpr (C == Q6_K) {
             // lane = row, warp = (block column warp&3, block half warp>>2)
             const int hf = warp >> 2;
@@ -1489,7 +1556,20 @@ cudaError_t launch_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     return glu ? launch_nt<C, false, true>(a, st, grid_out) : launch_nt<C, false, false>(a, st, grid_out);
 }
 
+// Q5_K has the lane-per-row path only (one activation row per group); the
+// callers route every other shape to the tcgen05 GEMM
+template <bool F16, bool GLU>
+cudaError_t launch_q5k(const GemvArgs &a, cudaStream_t st, int *grid_out) {
+    if (a.max_tokens != 1) return cudaErrorNotSupported;
+    return launch_t<Q5_K, 1, F16, GLU, 1>(a, st, grid_out);
+}
+
 cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
+    if (a.codec == Q5_K) {
+        const bool f16 = a.x_dtype == F16, glu = a.act != ACT_NONE;
+        if (f16) return glu ? launch_q5k<true, true>(a, st, grid_out) : launch_q5k<true, false>(a, st, grid_out);
+        return glu ? launch_q5k<false, true>(a, st, grid_out) : launch_q5k<false, false>(a, st, grid_out);
+    }
     switch (a.codec) {
     case Q4_K: return launch_c<Q4_K>(a, st, grid_out);
     case Q6_K: return launch_c<Q6_K>(a, st, grid_out);

@@ -19,10 +19,10 @@ from __future__ import annotations
 
 import numpy as np
 
-Q4_K, Q6_K, IQ2_XXS = 12, 14, 16
-CODECS = {"q4_k": Q4_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
+Q4_K, Q5_K, Q6_K, IQ2_XXS = 12, 13, 14, 16
+CODECS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
 CODEC_NAMES = {v: k for k, v in CODECS.items()}
-BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, IQ2_XXS: 66}
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66}
 QK = 256
 D_LO, D_HI = 1e-4, 2e-3
 
@@ -54,7 +54,7 @@ def random_blocks(codec, n_blocks: int, seed: int = 0) -> np.ndarray:
     rng = np.random.default_rng(seed)
     bpb = BLOCK_BYTES[c]
     b = rng.integers(0, 256, size=(n_blocks, bpb), dtype=np.uint8)
-    if c == Q4_K:
+    if c in (Q4_K, Q5_K):
         b[:, 0:2] = _fp16_bytes(rng, n_blocks)
         b[:, 2:4] = _fp16_bytes(rng, n_blocks)
     elif c == Q6_K:

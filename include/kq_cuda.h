@@ -35,6 +35,7 @@ extern "C" {
 #endif
 
 #define KQ_Q4_K 12
+#define KQ_Q5_K 13
 #define KQ_Q6_K 14
 #define KQ_IQ2_XXS 16
 

@@ -14,6 +14,7 @@
  *
  * Arithmetic order matches gguf-py exactly (all f32):
  *   Q4_K   (quants.py:504-522): dl = d*sc, ml = dmin*m, w = dl*q - ml
+ *   Q5_K   (quants.py:525-549): as Q4_K with q = nibble | (qh bit j) << 4
  *   Q6_K   (quants.py:554-572): dl = d*sc, w = dl*(q-32)
  *   IQ2_XXS(quants.py:802-829): db = d*(0.5+ls)*0.25, w = db*grid*sign
  * Every product above is exact in f32 (see the kernels' header), so results
@@ -31,7 +32,7 @@
 #include "kq_tables.h"
 
 #define QK 256
-enum { KQO_Q4_K = 12, KQO_Q6_K = 14, KQO_IQ2_XXS = 16 };
+enum { KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 
@@ -56,7 +57,7 @@ static float kqo_half(uint16_t h) {
 static float kqo_bf16(uint16_t b) { uint32_t u = (uint32_t)b << 16; float f; memcpy(&f, &u, 4); return f; }
 
 int kqo_block_bytes(int codec) {
-    switch (codec) { case KQO_Q4_K: return 144; case KQO_Q6_K: return 210; case KQO_IQ2_XXS: return 66; }
+    switch (codec) { case KQO_Q4_K: return 144; case KQO_Q5_K: return 176; case KQO_Q6_K: return 210; case KQO_IQ2_XXS: return 66; }
     return -1;
 }
 
@@ -85,6 +86,25 @@ static void deq_q4k(const uint8_t *b, float *o) {
                 float qv = (float)((q[32 * c + l] >> (4 * h)) & 0x0f);
                 o[32 * j + l] = dl * qv - ml;
             }
+        }
+    }
+}
+
+/* gguf-py Q5_K.dequantize_blocks (quants.py:525-549): d, dmin, the Q4_K
+ * scale/min packing, 32 bytes of fifth bits (bit j of qh[l] belongs to weight
+ * l of sub-block j) and 128 bytes of low nibbles (Q4_K order). */
+static void deq_q5k(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    float dmin = kqo_half((uint16_t)(b[2] | b[3] << 8));
+    uint8_t sc[8], mn[8];
+    q4k_scale_min(b + 4, sc, mn);
+    const uint8_t *qh = b + 16, *qs = b + 48;
+    for (int j = 0; j < 8; j++) {
+        float dl = d * (float)sc[j], ml = dmin * (float)mn[j];
+        for (int l = 0; l < 32; l++) {
+            int lo = (qs[32 * (j >> 1) + l] >> (4 * (j & 1))) & 0x0f;
+            int hi = (qh[l] >> j) & 1;
+            o[32 * j + l] = dl * (float)(lo | (hi << 4)) - ml;
         }
     }
 }
@@ -138,6 +158,7 @@ static void deq_iq2xxs(const uint8_t *b, float *o) {
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
+    case KQO_Q5_K: deq_q5k(b, o); return 0;
     case KQO_Q6_K: deq_q6k(b, o); return 0;
     case KQO_IQ2_XXS: deq_iq2xxs(b, o); return 0;
     }

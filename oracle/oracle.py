@@ -31,9 +31,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
-Q4_K, Q6_K, IQ2_XXS = 12, 14, 16
-CODEC_IDS = {"q4_k": Q4_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
-BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, IQ2_XXS: 66}
+Q4_K, Q5_K, Q6_K, IQ2_XXS = 12, 13, 14, 16
+CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66}
 QK = 256
 
 _lib = None
@@ -129,7 +129,7 @@ def _half(b2: np.ndarray) -> np.ndarray:
 
 
 def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
-    """numpy statement of the three decoders (follows gguf/quants.py)."""
+    """numpy statement of the decoders (follows gguf/quants.py)."""
     c = codec_id(codec)
     bpb = BLOCK_BYTES[c]
     blocks = np.ascontiguousarray(w, np.uint8).reshape(-1, bpb)
@@ -142,6 +142,18 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         mn = np.concatenate([s[:, 4:8] & 63, (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 2) & 48)], 1)
         q = blocks[:, 16:].reshape(n, 4, 1, 32) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
         q = (q & 15).reshape(n, 8, 32).astype(np.float32)
+        dl = (d * sc.astype(np.float32)).reshape(n, 8, 1)
+        ml = (dmin * mn.astype(np.float32)).reshape(n, 8, 1)
+        out = dl * q - ml
+    elif c == Q5_K:  # quants.py:525-549
+        d = _half(blocks[:, 0:2]).reshape(n, 1)
+        dmin = _half(blocks[:, 2:4]).reshape(n, 1)
+        s = blocks[:, 4:16].astype(np.uint8)
+        sc = np.concatenate([s[:, 0:4] & 63, (s[:, 8:12] & 15) | ((s[:, 0:4] >> 2) & 48)], 1)
+        mn = np.concatenate([s[:, 4:8] & 63, (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 2) & 48)], 1)
+        qh = blocks[:, 16:48].reshape(n, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 8, 1)
+        ql = blocks[:, 48:].reshape(n, 4, 1, 32) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
+        q = ((ql & 15).reshape(n, 8, 32) | ((qh & 1) << 4)).astype(np.float32)
         dl = (d * sc.astype(np.float32)).reshape(n, 8, 1)
         ml = (dmin * mn.astype(np.float32)).reshape(n, 8, 1)
         out = dl * q - ml

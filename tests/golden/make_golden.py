@@ -1,4 +1,4 @@
-"""Generate the committed golden vectors for the three block formats.
+"""Generate the committed golden vectors for the block formats.
 
 Source of truth: gguf-py 0.19.0 (``gguf.quants.dequantize``), the restatement
 of ggml's block formats that gmlx depends on (gmlx pyproject.toml:62).  The
@@ -11,6 +11,8 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
 (b) known-answer / edge blocks:
   Q4_K   all-zero quants (w = -dmin*m), scale/min = 0 and 63 on every
          sub-block, one-hot sub-block scales;
+  Q5_K   the same scale/min edges, fifth bits all 0 / all 1 / one sub-block
+         at a time;
   Q6_K   int8 scales at -128, -64, 0, 63, 127; quants all 0 / all 63;
   IQ2_XXS every grid index and every 7-bit sign index, ls = 0 and 15.
 Matmul references are x @ dequant(W).T in float64 for bf16 x (N(0,1)) plus
@@ -29,7 +31,7 @@ from gguf.quants import dequantize  # noqa: E402
 
 from gmlx_b200 import synth  # noqa: E402
 
-QT = {"q4_k": T.Q4_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}
+QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}
 
 
 def fp16(v):
@@ -58,6 +60,26 @@ def edge_blocks(codec):
             else:
                 b[12 + one - 4] = 1
             b[16:] = rng.integers(0, 256, 128, dtype=np.uint8)
+            blocks.append(b)
+    elif codec == "q5_k":
+        for sc_val, m_val, qh_fill in [(0, 0, 0), (63, 63, 255), (63, 0, 0), (0, 63, 255), (17, 42, None)]:
+            b = np.zeros(176, np.uint8)
+            b[0:2], b[2:4] = fp16(1e-3), fp16(5e-4)
+            for j in range(4):
+                b[4 + j] = (sc_val & 63) | ((sc_val >> 4) << 6)
+                b[8 + j] = (m_val & 63) | ((m_val >> 4) << 6)
+                b[12 + j] = (sc_val & 15) | ((m_val & 15) << 4)
+            b[16:48] = rng.integers(0, 256, 32, dtype=np.uint8) if qh_fill is None else qh_fill
+            b[48:] = 0 if (sc_val, m_val) == (0, 0) else rng.integers(0, 256, 128, dtype=np.uint8)
+            blocks.append(b)
+        for one in range(8):  # fifth bit set for one sub-block only, one-hot scale
+            b = np.zeros(176, np.uint8)
+            b[0:2], b[2:4] = fp16(1e-3), fp16(1e-3)
+            b[4 + (one % 4)] = 1 if one < 4 else 0
+            if one >= 4:
+                b[12 + one - 4] = 1
+            b[16:48] = 1 << one
+            b[48:] = rng.integers(0, 256, 128, dtype=np.uint8)
             blocks.append(b)
     elif codec == "q6_k":
         for scv, qfill in [(-128, None), (-64, 0), (0, None), (63, 255), (127, None)]:

@@ -15,7 +15,7 @@ from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
-CODECS = ["q4_k", "q6_k", "iq2_xxs"]
+CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs"]
 
 
 def rel_err(y, ref):
@@ -68,6 +68,8 @@ def test_quantized_matmul(cuda, codec, m, n, k):
 
 
 @pytest.mark.parametrize("codec,n,k", [
+    ("q5_k", 19200, 512),
+    ("q5_k", 256, 8192),
     ("q4_k", 19200, 512),   # >= 2 tiles per CTA: whole tiles handed out dynamically
     ("q4_k", 4096, 4096),   # one whole tile per CTA (stages fit the ring)
     ("q4_k", 256, 8192),    # few tiles, long K: K split into dynamic chunks
@@ -122,8 +124,8 @@ def test_quantized_matmul_split_k(cuda, codec):
 @pytest.mark.parametrize("codec", CODECS)
 def test_unaligned_row_pitch(cuda, codec):
     # K=768 (3 blocks): Q6_K rows of 630 B and IQ2_XXS rows of 198 B are not 16-byte aligned
-    if codec == "q4_k":
-        pytest.skip("Q4_K rows are always 16-byte multiples")
+    if codec in ("q4_k", "q5_k"):
+        pytest.skip("Q4_K / Q5_K rows are always 16-byte multiples")
     w = synth.random_weight(codec, 96, 768, seed=12)
     x = synth.random_activations(5, 768, seed=13)
     ref = O.matmul(x, w, codec)
@@ -181,7 +183,7 @@ def _moe_case(codec_gu, codec_d, e, d, f, t, k, seed):
     return wg, wu, wd, x, lg
 
 
-@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs")])
+@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs"), ("q5_k", "q5_k")])
 @pytest.mark.parametrize("t", [1, 5])
 def test_moe_decode_ops(cuda, codec_gu, codec_d, t):
     e, d, f, k = 16, 512, 256, 4
@@ -395,7 +397,7 @@ def test_grouped_gather_qmm(cuda, codec):
     assert kq.workspace_error() == 0
 
 
-@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs")])
+@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs"), ("q5_k", "q6_k")])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 def test_grouped_moe_layer_prefill(cuda, codec_gu, codec_d, out_dtype):
     """MoE prefill (T*k >= 33 * experts) through the grouped GEMM: gate/up GEMMs,

@@ -9,7 +9,7 @@ from gmlx_b200 import synth
 from oracle import oracle as O
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
-CODECS = ["q4_k", "q6_k", "iq2_xxs"]
+CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs"]
 
 
 @pytest.fixture(scope="module")
@@ -44,7 +44,7 @@ def test_oracle_matmul_matches_golden(gold, codec):
 def test_oracle_matches_gguf_py_random(codec, seed):
     gq = pytest.importorskip("gguf.quants")
     from gguf.constants import GGMLQuantizationType as T
-    qt = {"q4_k": T.Q4_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}[codec]
+    qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}[codec]
     w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
 
@@ -55,7 +55,8 @@ def test_raw_random_bytes_match_where_finite():
     gq = pytest.importorskip("gguf.quants")
     from gguf.constants import GGMLQuantizationType as T
     rng = np.random.default_rng(5)
-    for codec, qt, bpb in [("q4_k", T.Q4_K, 144), ("q6_k", T.Q6_K, 210), ("iq2_xxs", T.IQ2_XXS, 66)]:
+    for codec, qt, bpb in [("q4_k", T.Q4_K, 144), ("q5_k", T.Q5_K, 176), ("q6_k", T.Q6_K, 210),
+                           ("iq2_xxs", T.IQ2_XXS, 66)]:
         w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
         a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
         fin = np.isfinite(b)
@@ -103,7 +104,7 @@ def test_router_topk_semantics():
 def test_synthetic_block_statistics():
     for codec in CODECS:
         w = synth.random_blocks(codec, 4096, seed=1)
-        if codec == "q4_k":
+        if codec in ("q4_k", "q5_k"):
             d = w[:, 0:2].copy().view(np.float16).astype(np.float32)
             dm = w[:, 2:4].copy().view(np.float16).astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3 and dm.min() >= 9e-5
