@@ -51,13 +51,13 @@ int cuda_status(cudaError_t e, const char *what) {
     return fail(KQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-bool codec_ok(int c) { return c == KQ_Q4_K || c == KQ_Q5_K || c == KQ_Q6_K || c == KQ_IQ2_XXS; }
+bool codec_ok(int c) { return c == KQ_Q4_K || c == KQ_Q5_K || c == KQ_Q6_K || c == KQ_IQ2_XXS || c == KQ_Q8_0; }
 bool act_dtype_ok(int d) { return d == KQ_F16 || d == KQ_BF16; }
 bool out_dtype_ok(int d) { return d == KQ_F32 || d == KQ_F16 || d == KQ_BF16; }
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 int check_weights(int codec, const void *w, int64_t k, int64_t row_stride, const char *what) {
-    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16)", what, codec);
+    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q8_0=8, q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16)", what, codec);
     if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a positive multiple of %d", what, (long long)k, QK);
     const int64_t rb = k / QK * block_bytes(codec);
     if (row_stride < rb) return fail(KQ_ERR_SHAPE, "%s: row stride %lld < row bytes %lld", what, (long long)row_stride, (long long)rb);
@@ -135,8 +135,10 @@ int gemm_min_m() {
     return v;
 }
 
-// Q5_K has a one-row GEMV only: every other batch goes to the tcgen05 GEMM
-bool use_gemm(int64_t m, int codec = 0) { return m >= gemm_min_m() || (codec == KQ_Q5_K && m >= 2); }
+// Q5_K and Q8_0 have a one-row GEMV only: every other batch goes to the tcgen05 GEMM
+bool use_gemm(int64_t m, int codec = 0) {
+    return m >= gemm_min_m() || ((codec == KQ_Q5_K || codec == KQ_Q8_0) && m >= 2);
+}
 
 size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
     if (use_gemm(m, codec)) return plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0).total;
@@ -359,8 +361,8 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     // IQ2_XXS decode is ALU-bound: with sparse routing (on average well under one
     // slot per expert) one-slot groups take the one-row integer path, faster
     // than 8-row MMA groups even counting the few experts streamed twice
-    const int gsize = ((codec == KQ_IQ2_XXS && slots * 4 <= etotal) || codec == KQ_Q5_K)
-                          ? 1  // Q5_K: the one-row path is its only GEMV
+    const int gsize = ((codec == KQ_IQ2_XXS && slots * 4 <= etotal) || codec == KQ_Q5_K || codec == KQ_Q8_0)
+                          ? 1  // Q5_K / Q8_0: the one-row path is their only GEMV
                           : (int)(per_expert < 8 ? per_expert : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
@@ -424,7 +426,7 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
 size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_t n, int64_t kin, int act,
                  bool mix) {
     // IQ2_XXS may run with one-slot groups (see run_routed): size for those too
-    const int gsize = (codec == KQ_IQ2_XXS || codec == KQ_Q5_K) ? 1
+    const int gsize = (codec == KQ_IQ2_XXS || codec == KQ_Q5_K || codec == KQ_Q8_0) ? 1
                                                                  : (int)(per_expert < 8 ? (per_expert > 0 ? per_expert : 1) : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
@@ -457,9 +459,9 @@ int kq_version(void) { return 100; }
 const char *kq_last_error(void) { return g_msg; }
 
 int kq_codecs(int *out, int cap) {
-    static const int ids[4] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS};
-    for (int i = 0; i < 4 && i < cap; i++) out[i] = ids[i];
-    return 4;
+    static const int ids[5] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS, KQ_Q8_0};
+    for (int i = 0; i < 5 && i < cap; i++) out[i] = ids[i];
+    return 5;
 }
 
 int kq_codec_has_matmul(int codec) { return codec_ok(codec) ? 1 : 0; }

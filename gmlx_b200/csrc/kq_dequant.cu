@@ -42,6 +42,12 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
 #pragma unroll
         for (int i = 0; i < 8; i++)
             o[i] = dl * (float)(((q[i] >> (4 * h)) & 15) | (((qh[i] >> j) & 1) << 4)) - ml;
+    } else if constexpr (C == Q8_0) {  // lane: 8 weights of ggml block lane / 4
+        const uint8_t *blk = b + 34 * (lane >> 2);
+        const float d = half_bits_to_float(ld_u16(blk));
+        const uint8_t *q = blk + 2 + 8 * (lane & 3);
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = (float)(int8_t)q[i] * d;
     } else if constexpr (C == Q6_K) {
         const int i0 = 8 * lane, hf = i0 >> 7, s = (i0 & 127) >> 5, lo = i0 & 31;
         const float d = half_bits_to_float(ld_u16(b + 208));
@@ -243,6 +249,7 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     switch (codec) {
     case Q4_K: return launch_deq<Q4_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st);
+    case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st);
     default: return launch_deq<IQ2_XXS>(w, rows, nb, row_stride, out, dtype, st);
     }

@@ -26,7 +26,7 @@
 
 namespace kq {
 
-enum Codec : int { Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16 };
+enum Codec : int { Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
 constexpr int QK = 256;
@@ -34,11 +34,15 @@ constexpr int QK = 256;
 template <int C> struct Fmt;
 template <> struct Fmt<Q4_K> { static constexpr int bpb = 144; static constexpr int sub = 32; };
 template <> struct Fmt<Q5_K> { static constexpr int bpb = 176; static constexpr int sub = 32; };
+// Q8_0: ggml blocks of 32 weights (fp16 d + 32 int8); eight of them (272 bytes)
+// are handled as one 256-weight group
+template <> struct Fmt<Q8_0> { static constexpr int bpb = 272; static constexpr int sub = 32; };
 template <> struct Fmt<Q6_K> { static constexpr int bpb = 210; static constexpr int sub = 16; };
 template <> struct Fmt<IQ2_XXS> { static constexpr int bpb = 66; static constexpr int sub = 32; };
 
 __host__ __device__ inline int block_bytes(int codec) {
-    return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66 : -1;
+    return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
+         : codec == Q8_0 ? 272 : -1;
 }
 
 // 256-entry IQ2_XXS grid, byte i of entry e = |w_i| in {8, 25, 43}.

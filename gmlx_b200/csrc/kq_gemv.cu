@@ -58,6 +58,7 @@ constexpr int RED_TS = 36;        // token stride (floats) of the reduction buff
 template <int C> struct GCfg;
 template <> struct GCfg<Q4_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // (dsc, -mt) x 2 rows
 template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
 template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1; };    // dsc x 2 rows
 template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 2; };  // db x 2 rows
 template <int C> constexpr int KB_OF = NCOL * GCfg<C>::BPW;
@@ -649,14 +650,53 @@ __device__ __forceinline__ float dp_q5k_dot(const Q5Regs &r, const uint32_t *xq,
     return acc;
 }
 
+// Lane-per-row Q8_0: a lane takes four consecutive 34-byte ggml blocks (half a
+// 272-byte group); int8 quants dot the int16 activations with dp2a and each
+// block's fp16 d scales its 32-weight sum.  Blocks are only 2-byte aligned.
+__device__ __forceinline__ uint32_t lds_w2(const uint32_t *base, int i, uint32_t sh) {
+    return __funnelshift_r(base[i], base[i + 1], sh);
+}
+
+struct Q8Regs {
+    uint32_t q[4][8];
+    float d[4];
+};
+
+__device__ __forceinline__ void dp_q80_load(const uint8_t *half_blk, Q8Regs &r) {
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const uint8_t *blk = half_blk + 34 * s;
+        r.d[s] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk));
+        const uintptr_t qb = (uintptr_t)(blk + 2);
+        const uint32_t *aw = reinterpret_cast<const uint32_t *>(qb & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(qb & 3) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; i++) r.q[s][i] = lds_w2(aw, i, sh);
+    }
+}
+
+__device__ __forceinline__ float dp_q80_dot(const Q8Regs &r, int hf, const uint32_t *xq, const float *xsc) {
+    float acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 64 * hf + 16 * s + 2 * i);
+            sum = __dp2a_lo((int)xv.x, (int)r.q[s][i], sum);
+            sum = __dp2a_hi((int)xv.y, (int)r.q[s][i], sum);
+        }
+        acc = fmaf(r.d[s] * xsc[4 * hf + s], (float)sum, acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 // Lane-per-row Q6_K: lanes 0-15 / 16-31 of a warp take the two 128-weight
 // halves of rows row0..row0+15 of one block.  q6 = ql nibble | qh pair << 4 is
 // dotted unsigned with dp2a; the -32 offset is applied as -32 * sum(x) per
 // 16-weight sub-block.  Rows are only 2-byte aligned (210-byte blocks), so
 // words are assembled from aligned loads with funnel shifts.
-__device__ __forceinline__ uint32_t lds_w2(const uint32_t *base, int i, uint32_t sh) {
-    return __funnelshift_r(base[i], base[i + 1], sh);
-}
 
 struct Q6Regs {
     uint32_t ql[16], qh[8], scw0, scw1;
@@ -1016,7 +1056,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     constexpr int RCS = DP ? RED_TS : 8 * NT * RED_TS;       // their stride in the reduction buffer
     // Q4_K lane-per-row: warp = block column, lane = row.  Q6_K: warp =
     // (block column warp&3, 16-row half warp>>2), half-warp = block half.
-    const int mt = (DP && C != Q6_K) ? 0 : (warp & 1), col = (DP && C != Q6_K) ? warp : (DP ? (warp & 3) : (warp >> 1));
+    // lane-per-row codecs with 4 block columns per stage (Q6_K, Q8_0): warp =
+    // (block column, block half); the others: warp = block column
+    constexpr bool HALVES = C == Q6_K || C == Q8_0;
+    const int mt = (DP && !HALVES) ? 0 : (warp & 1), col = (DP && !HALVES) ? warp : (DP ? (warp & 3) : (warp >> 1));
     // per-warp table: scales (MMA path) or quantized activations + their
     // scales (lane-per-row path: 128 words + 32 floats = 640 bytes, as TABS)
     float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * (DP ? 160 : GCfg<C>::TABW * BPW);
@@ -1054,6 +1097,17 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q5k_dot(r, xq, xsc);
+        } else if constexpr (C == Q8_0) {
+            // lane = row, warp = (group column warp&3, half warp>>2 = four 34-byte blocks)
+            const int hf = warp >> 2;
+            Q8Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_q80_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb + 136 * hf, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_q80_dot(r, hf, xq, xsc);
         } else if constexpr (C == Q6_K) {
             // lane = row, warp = (block column warp&3, block half warp>>2)
             const int hf = warp >> 2;
@@ -1556,20 +1610,24 @@ cudaError_t launch_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     return glu ? launch_nt<C, false, true>(a, st, grid_out) : launch_nt<C, false, false>(a, st, grid_out);
 }
 
-// Q5_K has the lane-per-row path only (one activation row per group); the
-// callers route every other shape to the tcgen05 GEMM
-template <bool F16, bool GLU>
-cudaError_t launch_q5k(const GemvArgs &a, cudaStream_t st, int *grid_out) {
+// Q5_K and Q8_0 have the lane-per-row path only (one activation row per
+// group); the callers route every other shape to the tcgen05 GEMM
+template <int C, bool F16, bool GLU>
+cudaError_t launch_onerow(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.max_tokens != 1) return cudaErrorNotSupported;
-    return launch_t<Q5_K, 1, F16, GLU, 1>(a, st, grid_out);
+    return launch_t<C, 1, F16, GLU, 1>(a, st, grid_out);
+}
+
+template <int C>
+cudaError_t launch_onerow_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
+    const bool f16 = a.x_dtype == F16, glu = a.act != ACT_NONE;
+    if (f16) return glu ? launch_onerow<C, true, true>(a, st, grid_out) : launch_onerow<C, true, false>(a, st, grid_out);
+    return glu ? launch_onerow<C, false, true>(a, st, grid_out) : launch_onerow<C, false, false>(a, st, grid_out);
 }
 
 cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
-    if (a.codec == Q5_K) {
-        const bool f16 = a.x_dtype == F16, glu = a.act != ACT_NONE;
-        if (f16) return glu ? launch_q5k<true, true>(a, st, grid_out) : launch_q5k<true, false>(a, st, grid_out);
-        return glu ? launch_q5k<false, true>(a, st, grid_out) : launch_q5k<false, false>(a, st, grid_out);
-    }
+    if (a.codec == Q5_K) return launch_onerow_c<Q5_K>(a, st, grid_out);
+    if (a.codec == Q8_0) return launch_onerow_c<Q8_0>(a, st, grid_out);
     switch (a.codec) {
     case Q4_K: return launch_c<Q4_K>(a, st, grid_out);
     case Q6_K: return launch_c<Q6_K>(a, st, grid_out);

@@ -11,6 +11,9 @@ prescribe:
   [-64, 63], ``d`` (the last two bytes) fp16(U[1e-4, 2e-3]).
 * IQ2_XXS (66 B): random ``qs`` words (grid indices, sign indices and 4-bit
   sub-scales all uniform), ``d`` fp16(U[1e-4, 2e-3]).
+* Q5_K (176 B): as Q4_K (``d``, ``dmin`` fp16(U[1e-4, 2e-3]), the rest random).
+* Q8_0 (34 B per 32 weights, counted here as 272 B per 256): random int8
+  quants, ``d`` fp16(U[1e-4, 2e-3]).
 
 Activations are bf16 N(0, 1); router logits are f32 N(0, 1).  All draws use
 ``numpy.random.default_rng(seed)``.
@@ -19,10 +22,11 @@ from __future__ import annotations
 
 import numpy as np
 
-Q4_K, Q5_K, Q6_K, IQ2_XXS = 12, 13, 14, 16
-CODECS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
+Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS = 8, 12, 13, 14, 16
+CODECS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0}
 CODEC_NAMES = {v: k for k, v in CODECS.items()}
-BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66}
+# bytes per 256 weights (Q8_0: eight 34-byte ggml blocks of 32 weights)
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272}
 QK = 256
 D_LO, D_HI = 1e-4, 2e-3
 
@@ -62,6 +66,9 @@ def random_blocks(codec, n_blocks: int, seed: int = 0) -> np.ndarray:
         b[:, 208:210] = _fp16_bytes(rng, n_blocks)
     elif c == IQ2_XXS:
         b[:, 0:2] = _fp16_bytes(rng, n_blocks)
+    elif c == Q8_0:  # eight (fp16 d, 32 x int8) blocks per 256 weights
+        sub = b.reshape(n_blocks * 8, 34)
+        sub[:, 0:2] = _fp16_bytes(rng, n_blocks * 8)
     else:
         raise ValueError(codec)
     return b

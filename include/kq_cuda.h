@@ -34,6 +34,7 @@
 extern "C" {
 #endif
 
+#define KQ_Q8_0 8   /* handled in groups of eight 34-byte blocks (272 bytes per 256 weights) */
 #define KQ_Q4_K 12
 #define KQ_Q5_K 13
 #define KQ_Q6_K 14

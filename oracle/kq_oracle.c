@@ -15,6 +15,7 @@
  * Arithmetic order matches gguf-py exactly (all f32):
  *   Q4_K   (quants.py:504-522): dl = d*sc, ml = dmin*m, w = dl*q - ml
  *   Q5_K   (quants.py:525-549): as Q4_K with q = nibble | (qh bit j) << 4
+ *   Q8_0   (Q8_0.dequantize_blocks): w = q * d per 32-weight block
  *   Q6_K   (quants.py:554-572): dl = d*sc, w = dl*(q-32)
  *   IQ2_XXS(quants.py:802-829): db = d*(0.5+ls)*0.25, w = db*grid*sign
  * Every product above is exact in f32 (see the kernels' header), so results
@@ -32,7 +33,7 @@
 #include "kq_tables.h"
 
 #define QK 256
-enum { KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16 };
+enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 
@@ -57,7 +58,10 @@ static float kqo_half(uint16_t h) {
 static float kqo_bf16(uint16_t b) { uint32_t u = (uint32_t)b << 16; float f; memcpy(&f, &u, 4); return f; }
 
 int kqo_block_bytes(int codec) {
-    switch (codec) { case KQO_Q4_K: return 144; case KQO_Q5_K: return 176; case KQO_Q6_K: return 210; case KQO_IQ2_XXS: return 66; }
+    switch (codec) {
+    case KQO_Q4_K: return 144; case KQO_Q5_K: return 176; case KQO_Q6_K: return 210; case KQO_IQ2_XXS: return 66;
+    case KQO_Q8_0: return 272; /* eight 34-byte blocks per 256 weights */
+    }
     return -1;
 }
 
@@ -106,6 +110,15 @@ static void deq_q5k(const uint8_t *b, float *o) {
             int hi = (qh[l] >> j) & 1;
             o[32 * j + l] = dl * (float)(lo | (hi << 4)) - ml;
         }
+    }
+}
+
+/* gguf-py Q8_0.dequantize_blocks: eight (fp16 d, 32 x int8 q) blocks, w = q * d. */
+static void deq_q80(const uint8_t *b, float *o) {
+    for (int j = 0; j < 8; j++) {
+        const uint8_t *blk = b + 34 * j;
+        float d = kqo_half((uint16_t)(blk[0] | blk[1] << 8));
+        for (int l = 0; l < 32; l++) o[32 * j + l] = (float)(int8_t)blk[2 + l] * d;
     }
 }
 
@@ -159,6 +172,7 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
     case KQO_Q5_K: deq_q5k(b, o); return 0;
+    case KQO_Q8_0: deq_q80(b, o); return 0;
     case KQO_Q6_K: deq_q6k(b, o); return 0;
     case KQO_IQ2_XXS: deq_iq2xxs(b, o); return 0;
     }

@@ -31,9 +31,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
-Q4_K, Q5_K, Q6_K, IQ2_XXS = 12, 13, 14, 16
-CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS}
-BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66}
+Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS = 8, 12, 13, 14, 16
+CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0}
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -166,6 +166,10 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         hi = (qh.reshape(n, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
         q = (lo.reshape(n, 8, 32) | (hi.reshape(n, 8, 32) << 4)).astype(np.int8) - np.int8(32)
         out = dl * q.reshape(n, 16, 16).astype(np.float32)
+    elif c == Q8_0:  # Q8_0.dequantize_blocks: eight (fp16 d, 32 x int8) blocks per 256 weights
+        sub = blocks.reshape(n * 8, 34)
+        d = _half(sub[:, 0:2]).reshape(n * 8, 1)
+        out = sub[:, 2:].copy().view(np.int8).astype(np.float32) * d
     elif c == IQ2_XXS:  # quants.py:802-829
         from_grid = iq2xxs_grid()
         d = _half(blocks[:, 0:2]).reshape(n, 1)

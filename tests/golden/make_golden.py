@@ -13,6 +13,7 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
          sub-block, one-hot sub-block scales;
   Q5_K   the same scale/min edges, fifth bits all 0 / all 1 / one sub-block
          at a time;
+  Q8_0   quants -128, -127, 0, 127 and d = 0, negative d, the largest fp16;
   Q6_K   int8 scales at -128, -64, 0, 63, 127; quants all 0 / all 63;
   IQ2_XXS every grid index and every 7-bit sign index, ls = 0 and 15.
 Matmul references are x @ dequant(W).T in float64 for bf16 x (N(0,1)) plus
@@ -31,7 +32,7 @@ from gguf.quants import dequantize  # noqa: E402
 
 from gmlx_b200 import synth  # noqa: E402
 
-QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}
+QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0}
 
 
 def fp16(v):
@@ -81,6 +82,12 @@ def edge_blocks(codec):
             b[16:48] = 1 << one
             b[48:] = rng.integers(0, 256, 128, dtype=np.uint8)
             blocks.append(b)
+    elif codec == "q8_0":  # 272-byte groups of eight 34-byte blocks
+        for dv, qv in [(1e-3, -128), (1e-3, 127), (0.0, 55), (-2e-3, -127), (65504.0, 1), (5e-4, None)]:
+            b = np.zeros((8, 34), np.uint8)
+            b[:, 0:2] = fp16(dv)
+            b[:, 2:] = (rng.integers(-128, 128, (8, 32)) if qv is None else np.full((8, 32), qv)).astype(np.int8).view(np.uint8)
+            blocks.append(b.reshape(272))
     elif codec == "q6_k":
         for scv, qfill in [(-128, None), (-64, 0), (0, None), (63, 255), (127, None)]:
             b = rng.integers(0, 256, 210, dtype=np.uint8)

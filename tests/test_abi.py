@@ -28,10 +28,10 @@ def test_header_symbols_exported():
 def test_codecs_and_block_bytes():
     L = _lib.load()
     buf = (ctypes.c_int * 8)()
-    assert L.kq_codecs(buf, 8) == 4
-    assert list(buf[:4]) == [12, 13, 14, 16]
-    assert [L.kq_block_bytes(c) for c in (12, 13, 14, 16, 2)] == [144, 176, 210, 66, -1]
-    assert L.kq_codec_has_matmul(12) == 1 and L.kq_codec_has_matmul(8) == 0
+    assert L.kq_codecs(buf, 8) == 5
+    assert list(buf[:5]) == [12, 13, 14, 16, 8]
+    assert [L.kq_block_bytes(c) for c in (12, 13, 14, 16, 8, 2)] == [144, 176, 210, 66, 272, -1]
+    assert L.kq_codec_has_matmul(12) == 1 and L.kq_codec_has_matmul(8) == 1 and L.kq_codec_has_matmul(2) == 0
     assert L.kq_version() >= 100
 
 

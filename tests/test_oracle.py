@@ -9,7 +9,7 @@ from gmlx_b200 import synth
 from oracle import oracle as O
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
-CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs"]
+CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0"]
 
 
 @pytest.fixture(scope="module")
@@ -44,7 +44,7 @@ def test_oracle_matmul_matches_golden(gold, codec):
 def test_oracle_matches_gguf_py_random(codec, seed):
     gq = pytest.importorskip("gguf.quants")
     from gguf.constants import GGMLQuantizationType as T
-    qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}[codec]
+    qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0}[codec]
     w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
 
@@ -56,7 +56,7 @@ def test_raw_random_bytes_match_where_finite():
     from gguf.constants import GGMLQuantizationType as T
     rng = np.random.default_rng(5)
     for codec, qt, bpb in [("q4_k", T.Q4_K, 144), ("q5_k", T.Q5_K, 176), ("q6_k", T.Q6_K, 210),
-                           ("iq2_xxs", T.IQ2_XXS, 66)]:
+                           ("iq2_xxs", T.IQ2_XXS, 66), ("q8_0", T.Q8_0, 272)]:
         w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
         a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
         fin = np.isfinite(b)
@@ -108,6 +108,9 @@ def test_synthetic_block_statistics():
             d = w[:, 0:2].copy().view(np.float16).astype(np.float32)
             dm = w[:, 2:4].copy().view(np.float16).astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3 and dm.min() >= 9e-5
+        elif codec == "q8_0":
+            d = w.reshape(-1, 34)[:, 0:2].copy().view(np.float16).astype(np.float32)
+            assert d.min() >= 9e-5 and d.max() <= 2.01e-3
         elif codec == "q6_k":
             sc = w[:, 192:208].view(np.int8)
             assert sc.min() == -64 and sc.max() == 63
@@ -116,3 +119,16 @@ def test_synthetic_block_statistics():
         else:
             d = w[:, 0:2].copy().view(np.float16).astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3
+
+
+def test_q8_0_round_trip_through_gguf_quantizer():
+    """Q8_0 is the one codec here gguf-py can quantize: real weights ->
+    gguf-py quantize -> our dequantize equals gguf-py's dequantize bit for bit."""
+    from gguf import quants as gq
+    from gguf.constants import GGMLQuantizationType as T
+    rng = np.random.default_rng(9)
+    wf = (rng.standard_normal((64, 512)) * 0.02).astype(np.float32)
+    w = gq.quantize(wf, T.Q8_0)
+    assert w.shape == (64, 512 // 32 * 34)
+    assert np.array_equal(bits(O.dequantize(w, "q8_0")), bits(gq.dequantize(w, T.Q8_0).astype(np.float32)))
+    assert np.abs(O.dequantize(w, "q8_0") - wf).max() <= np.abs(wf).max() / 127
