@@ -93,7 +93,9 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int DPB = DP ? 4 * CW * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 <= 4), one row per warp
     static constexpr bool SX = false;  // Q4_K one-row sums table (off: its per-launch prologue costs more than it saves)
     static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
-    static constexpr int REDB = NCOL * 8 * NT * RED_TS * 4;  // one reduction buffer (two, alternating)
+    // one reduction buffer (two, alternating): [column][token][row]; the
+    // lane-per-row path keeps one token per warp
+    static constexpr int REDB = DP ? CW * RED_TS * 4 : NCOL * 8 * NT * RED_TS * 4;
     static constexpr int FIXED = 512 + (C == IQ2_XXS ? 4096 : 0) + TABS + SBYTES + 2 * REDB + DPB;
     static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<C, NT> - FIXED) / STAGE;
     static constexpr int NS = NS_FIT > 8 ? 8 : (NS_FIT < 2 ? 2 : NS_FIT);  // ring depth (<= 8: rowoff table)
@@ -109,6 +111,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int OFF_DPB = OFF_RED + 2 * REDB;
     static constexpr int BYTES = OFF_DPB + DPB;
     static_assert(!DP || NS <= 3, "lane-per-row path sizes its partial buffers for NS <= 3");
+    static_assert(!DP || CTAS_PER_SM<C, NT> != 2 || BYTES <= 113 * 1024, "two CTAs per SM must fit");
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
