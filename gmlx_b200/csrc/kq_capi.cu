@@ -129,7 +129,7 @@ GemvArgs dense_args(int codec, const void *x, int x_dtype, int64_t m, int64_t k,
 int gemm_min_m() {
     static int v = -1;
     if (v < 0) {
-        const char *e = getenv("KQ_GEMM_MIN_M");  // development override of the GEMV/GEMM crossover
+        const char *e = dev_env("KQ_GEMM_MIN_M");  // development override of the GEMV/GEMM crossover
         v = e ? atoi(e) : GEMM_MIN_M;
     }
     return v;
@@ -225,7 +225,7 @@ GroupedPlan grouped_plan(int codec, int64_t slots, int64_t e, int64_t etotal, in
     GroupedPlan g;
     // 256-row tiles (two accumulators per CTA) once experts average >= 192 rows
     g.mt = slots >= 192 * etotal ? 2 : 1;
-    if (const char *e = getenv("KQ_GROUPED_MT")) g.mt = atoi(e) == 2 ? 2 : 1;  // development override
+    if (const char *e = dev_env("KQ_GROUPED_MT")) g.mt = atoi(e) == 2 ? 2 : 1;  // development override
     g.max_tiles = (int)(slots / (128 * g.mt) + (slots < e ? slots : e) + 1);
     const size_t per_e = (size_t)n * kin * 2 * (glu ? 2 : 1);
     g.chunk_e = codec == KQ_Q4_K ? (int)e : (int)std::max<int64_t>(1, std::min<int64_t>(e, GROUPED_B_CHUNK / per_e));

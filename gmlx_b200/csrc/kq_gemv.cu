@@ -1523,9 +1523,9 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
     const long nst = (a.K / QK + L::KB - 1) / L::KB;
     const long iters = groups * tiles * nst, units = groups * tiles;
     long cap = (long)num_sms() * per_sm;
-    if (const char *g = getenv("KQ_GEMV_GRID")) cap = atol(g);  // development override
+    if (const char *g = dev_env("KQ_GEMV_GRID")) cap = atol(g);  // development override
     int d = 0, S = 1;
-    if (L::DP && !getenv("KQ_GEMV_STATIC")) {
+    if (L::DP && !dev_env("KQ_GEMV_STATIC")) {
         if (units >= 2 * cap) {
             d = 1;
         } else if (units <= cap && nst <= L::NS) {
@@ -1542,10 +1542,10 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
         }
     }
     if (d && L::DP && !a.ar_world)
-        if (const char *f = getenv("KQ_GEMV_FORCE_S")) S = (int)std::min<long>(nst, std::max(1, atoi(f)));  // development
+        if (const char *f = dev_env("KQ_GEMV_FORCE_S")) S = (int)std::min<long>(nst, std::max(1, atoi(f)));  // development
     if (dyn) *dyn = d;
     if (ksplit) *ksplit = S;
-    if (!d && iters > cap && !getenv("KQ_GEMV_GRID")) {
+    if (!d && iters > cap && !dev_env("KQ_GEMV_GRID")) {
         // stream-K: prefer a grid that gives every CTA the same whole number of
         // stages of one tile (tiles x a divisor of the stages per tile), so no
         // CTA carries an extra stage or two partial tiles; keep >= 70 % of the slots
@@ -1585,7 +1585,7 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = getenv("KQ_GEMV_NOPDL") ? 0 : 1;  // development switch
+    cfg.numAttrs = dev_env("KQ_GEMV_NOPDL") ? 0 : 1;  // development switch
     GemvArgs b = a;
     b.dyn = dyn;
     b.ksplit = ksplit;

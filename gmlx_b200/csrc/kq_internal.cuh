@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "kq_formats.cuh"
 
@@ -141,6 +142,16 @@ cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int nor
                                int shared_gate, const float *per_expert_scale, cudaStream_t st);
 
 int num_sms();
+// Development-only environment switches (grid / schedule overrides used while
+// tuning): read only in builds with KQ_DEVELOPMENT, nullptr otherwise.
+inline const char *dev_env(const char *name) {
+#ifdef KQ_DEVELOPMENT
+    return getenv(name);
+#else
+    (void)name;
+    return nullptr;
+#endif
+}
 // Sets the calling thread's kq_last_error() message.
 void set_last_error(const char *msg);
 
