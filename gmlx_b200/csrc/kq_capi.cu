@@ -141,7 +141,7 @@ bool use_gemm(int64_t m, int codec = 0) {
 }
 
 size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
-    if (use_gemm(m, codec)) return plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0).total;
+    if (use_gemm(m, codec)) return plan(0, gemm_scratch_bytes(codec, m, n, k, act != ACT_NONE), 0, 0).total;
     GemvArgs a = dense_args(codec, nullptr, KQ_BF16, m, k, k, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
@@ -161,7 +161,7 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
     if (m == 0) return KQ_OK;
     if (n > 0x7fffffff || k > 0x7fffffff) return fail(KQ_ERR_SHAPE, "%s: n/k too large", what);
     if (use_gemm(m, codec) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
-        const WsPlan p = plan(0, gemm_scratch_bytes(codec, n, k, act != ACT_NONE), 0, 0);
+        const WsPlan p = plan(0, gemm_scratch_bytes(codec, m, n, k, act != ACT_NONE), 0, 0);
         if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
             return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
         GemmArgs g{};

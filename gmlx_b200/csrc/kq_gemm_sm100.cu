@@ -592,8 +592,19 @@ bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int
            encode_fn() != nullptr;
 }
 
-size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k, bool glu) {
-    return codec == Q4_K ? 0 : (size_t)n * k * 2 * (glu ? 2 : 1);  // dequantized copy for the B-by-TMA path
+// Q4_K is dequantized inside the GEMM up to this many activation rows; above
+// it, one dequantized copy plus B by TMA is faster (the copy costs ~N*K*2
+// bytes of traffic once, while the in-kernel dequantization is repeated for
+// every 256-row tile and caps the tensor pipe near 64 % of peak)
+constexpr int64_t Q4K_FUSED_MAX_M = 4096;
+
+static bool fused_q4k(int codec, int64_t m) {
+    const char *e = dev_env("KQ_Q4K_FUSED_MAX_M");
+    return codec == Q4_K && m <= (e ? atol(e) : Q4K_FUSED_MAX_M);
+}
+
+size_t gemm_scratch_bytes(int codec, int64_t m, int64_t n, int64_t k, bool glu) {
+    return fused_q4k(codec, m) ? 0 : (size_t)n * k * 2 * (glu ? 2 : 1);  // dequantized copy for the B-by-TMA path
 }
 
 cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
@@ -603,7 +614,7 @@ cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
         a.ex_lo = 0;
         a.ex_hi = 1;
         a.n_per_expert = a.N;
-        if (a.codec == Q4_K)
+        if (fused_q4k(a.codec, a.M))
             return f16 ? launch_gemm_mt<true, B_Q4K, true>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K, true>(a, nullptr, st);
         cudaError_t e = launch_dequantize(a.codec, a.w, a.N, a.K, a.w_row_stride, scratch, a.x_dtype, st);
         if (e == cudaSuccess)
@@ -613,8 +624,9 @@ cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
         return f16 ? launch_gemm_mt<true, B_TMA, true>(a, scratch, st) : launch_gemm_mt<false, B_TMA, true>(a, scratch, st);
     }
     const GemmArgs &a = a0;
-    if (a.codec == Q4_K) return f16 ? launch_gemm_mt<true, B_Q4K>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K>(a, nullptr, st);
-    // other codecs: dequantize once into scratch (activation dtype), then B by TMA
+    if (fused_q4k(a.codec, a.M))
+        return f16 ? launch_gemm_mt<true, B_Q4K>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K>(a, nullptr, st);
+    // other codecs and large batches: dequantize once into scratch (activation dtype), then B by TMA
     cudaError_t e = launch_dequantize(a.codec, a.w, a.N, a.K, a.w_row_stride, scratch, a.x_dtype, st);
     if (e != cudaSuccess) return e;
     return f16 ? launch_gemm_mt<true, B_TMA>(a, scratch, st) : launch_gemm_mt<false, B_TMA>(a, scratch, st);

@@ -107,7 +107,7 @@ struct GemmArgs {
     const float *row_scale;
 };
 bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride);
-size_t gemm_scratch_bytes(int codec, int64_t n, int64_t k, bool glu);
+size_t gemm_scratch_bytes(int codec, int64_t m, int64_t n, int64_t k, bool glu);
 cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st);
 constexpr int GEMM_MIN_M = 33;  // activation rows from which the tensor-core GEMM takes over
 // Grouped GEMM over expert-sorted rows (see kq_gemm_sm100.cu); the caller

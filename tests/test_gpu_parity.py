@@ -289,7 +289,7 @@ def test_nn_modules_fused_and_stock_paths_agree(cuda):
 
 
 @pytest.mark.parametrize("codec", CODECS)
-@pytest.mark.parametrize("m,n,k", [(64, 256, 512), (200, 320, 1024), (1000, 512, 2048)])
+@pytest.mark.parametrize("m,n,k", [(64, 256, 512), (200, 320, 1024), (1000, 512, 2048), (4200, 128, 512)])
 def test_prefill_gemm_tcgen05(cuda, codec, m, n, k):
     """Prefill-sized M runs the tcgen05 GEMM (weights rounded to bf16 before the MMA)."""
     w = synth.random_weight(codec, n, k, seed=31)
@@ -304,11 +304,13 @@ def test_prefill_gemm_tcgen05(cuda, codec, m, n, k):
 
 @pytest.mark.parametrize("codec", CODECS)
 @pytest.mark.parametrize("act", ["silu", "gelu"])
-def test_prefill_glu_tcgen05(cuda, codec, act):
+@pytest.mark.parametrize("m", [200, 4200])
+def test_prefill_glu_tcgen05(cuda, codec, act, m):
     """Prefill-sized fused GLU: one tcgen05 GEMM with gate and up accumulators
-    side by side (128 output columns per tile; N=320 leaves a ragged tile)."""
+    side by side (128 output columns per tile; N=320 leaves a ragged tile).
+    M=4200: Q4_K switches from in-kernel dequantization to the dequantized copy."""
     from math import erf
-    n, k, m = 320, 1024, 200
+    n, k = 320, 1024
     wg = synth.random_weight(codec, n, k, seed=24)
     wu = synth.random_weight(codec, n, k, seed=25)
     x = synth.random_activations(m, k, seed=26)
