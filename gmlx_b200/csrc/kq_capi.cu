@@ -335,6 +335,159 @@ int run_grouped(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, 
     return cuda_status(ce, what);
 }
 
+// Whole expert layer on the grouped path: one sort of the routed slots, the
+// gate/up GEMM writes h in expert-sorted row order, and the down GEMM reads it
+// in place with the same tile table (no second sort, gather or h scatter);
+// the score mix is fused into the down epilogue when y is a contiguous f32.
+struct LayerPlan {
+    size_t perm_off, scr_off, misc_off, tiles_off, mix_off, xs_off, hs_off, ys_off, b_off, total;
+    int max_tiles, mt, chunk_gu, chunk_d;
+};
+
+LayerPlan layer_plan(int cgu, int cd, int64_t slots, int64_t e, int64_t etotal, int64_t d, int64_t f, bool need_ys) {
+    LayerPlan g;
+    g.mt = slots >= 192 * etotal ? 2 : 1;
+    g.max_tiles = (int)(slots / (128 * g.mt) + (slots < e ? slots : e) + 1);
+    const size_t per_gu = (size_t)f * d * 2 * 2, per_d = (size_t)d * f * 2;
+    g.chunk_gu = cgu == KQ_Q4_K ? (int)e : (int)std::max<int64_t>(1, std::min<int64_t>(e, GROUPED_B_CHUNK / per_gu));
+    g.chunk_d = cd == KQ_Q4_K ? (int)e : (int)std::max<int64_t>(1, std::min<int64_t>(e, GROUPED_B_CHUNK / per_d));
+    size_t o = 256 + CNT_RESERVE;
+    g.perm_off = o;
+    o = align256(o + (size_t)slots * sizeof(int));
+    g.scr_off = o;
+    o = align256(o + (size_t)(slots + e) * sizeof(int));
+    g.misc_off = o;
+    o = align256(o + 2 * sizeof(int));
+    g.tiles_off = o;
+    o = align256(o + (size_t)g.max_tiles * 3 * sizeof(int));
+    g.mix_off = o;
+    o = align256(o + (size_t)slots * 2 * sizeof(int));
+    g.xs_off = o;
+    o = align256(o + (size_t)slots * d * 2);
+    g.hs_off = o;
+    o = align256(o + (size_t)slots * f * 2);
+    g.ys_off = o;
+    if (need_ys) o = align256(o + (size_t)slots * d * sizeof(float));
+    g.b_off = o;
+    const size_t bgu = cgu == KQ_Q4_K ? 0 : (size_t)g.chunk_gu * per_gu;
+    const size_t bd = cd == KQ_Q4_K ? 0 : (size_t)g.chunk_d * per_d;
+    g.total = align256(o + std::max(bgu, bd));
+    return g;
+}
+
+// grouped GEMM over [c0, c1) expert chunks of one stack (dequantizing non-Q4_K chunks first)
+int grouped_pass(GemmArgs g, int codec, const uint8_t *w, const uint8_t *w2, int64_t e, int chunk, int64_t n,
+                 int64_t kin, int64_t wrs, int64_t wes, int x_dtype, char *bscratch, int mt, int max_tiles,
+                 cudaStream_t st, const char *what) {
+    const bool glu = w2 != nullptr;
+    for (int64_t c0 = 0; c0 < e; c0 += chunk) {
+        const int64_t c1 = std::min<int64_t>(e, c0 + chunk);
+        g.ex_lo = (int)c0;
+        g.ex_hi = (int)c1;
+        void *bd = nullptr;
+        cudaError_t ce = cudaSuccess;
+        if (codec == KQ_Q4_K) {
+            g.w = w;
+            g.w2 = w2;
+        } else {
+            bd = bscratch;
+            for (int half = 0; half < (glu ? 2 : 1) && ce == cudaSuccess; half++) {
+                const uint8_t *wp = half ? w2 : w;
+                char *dst = bscratch + (size_t)half * (c1 - c0) * n * kin * 2;
+                if (wes == n * wrs) {
+                    ce = launch_dequantize(codec, wp + c0 * wes, (c1 - c0) * n, kin, wrs, dst, x_dtype, st);
+                } else {
+                    for (int64_t ex = c0; ex < c1 && ce == cudaSuccess; ex++)
+                        ce = launch_dequantize(codec, wp + ex * wes, n, kin, wrs, dst + (ex - c0) * n * kin * 2, x_dtype,
+                                               st);
+                }
+            }
+            if (ce != cudaSuccess) return cuda_status(ce, what);
+        }
+        if ((ce = launch_gemm_grouped(g, mt, max_tiles, bd, st)) != cudaSuccess) return cuda_status(ce, what);
+    }
+    return KQ_OK;
+}
+
+int run_grouped_layer(int cgu, int cd, const void *x, int x_dtype, int64_t t, int64_t d, const int32_t *idx, int k,
+                      const float *scores, const void *gate_w, const void *up_w, int64_t gu_rs, int64_t gu_es,
+                      const void *down_w, int64_t d_rs, int64_t d_es, int64_t e, int64_t f, int64_t ebase,
+                      int64_t etotal, int act, void *y, int y_dtype, void *ws, size_t ws_bytes, void *stream) {
+    const char *what = "moe_expert_layer_local";
+    const int64_t slots = t * k;
+    const bool fused_mix = y_dtype == KQ_F32;
+    const LayerPlan p = layer_plan(cgu, cd, slots, e, etotal, d, f, !fused_mix);
+    if (ws_bytes < p.total) return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes required, got %zu", what, p.total, ws_bytes);
+    char *base = (char *)ws;
+    int *err = (int *)base, *cnt = (int *)(base + 256);
+    int *perm = (int *)(base + p.perm_off), *scr = (int *)(base + p.scr_off);
+    int *count = (int *)(base + p.misc_off), *ntiles = count + 1;
+    int *te = (int *)(base + p.tiles_off), *tr0 = te + p.max_tiles, *tre = tr0 + p.max_tiles;
+    int *tok_of = (int *)(base + p.mix_off);
+    float *scale_of = (float *)(tok_of + slots);
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t ce = launch_moe_sort(idx, (int)slots, k, (int)ebase, (int)e, (int)etotal, 0, nullptr, x, d, (int)d,
+                                     base + p.xs_off, 128 * p.mt, cnt, scr, perm, count, ntiles, te, tr0, tre,
+                                     p.max_tiles, err, fused_mix ? scores : nullptr, tok_of, scale_of, st);
+    if (ce != cudaSuccess) return cuda_status(ce, what);
+    GemmArgs g{};
+    g.M = (int)slots;
+    g.x_dtype = x_dtype;
+    g.err = err;
+    g.n_tiles = ntiles;
+    g.tile_e = te;
+    g.tile_row0 = tr0;
+    g.tile_rowend = tre;
+    // gate/up: sorted x -> sorted h (row p of h is sorted row p)
+    g.codec = cgu;
+    g.N = (int)f;
+    g.K = (int)d;
+    g.x = base + p.xs_off;
+    g.x_row_stride = d;
+    g.w_row_stride = gu_rs;
+    g.w_expert_stride = gu_es;
+    g.n_per_expert = (int)f;
+    g.act = act;
+    g.y = base + p.hs_off;
+    g.y_dtype = x_dtype;
+    g.y_row_stride = f;
+    int rc = grouped_pass(g, cgu, (const uint8_t *)gate_w, (const uint8_t *)up_w, e, p.chunk_gu, f, d, gu_rs, gu_es,
+                          x_dtype, base + p.b_off, p.mt, p.max_tiles, st, what);
+    if (rc) return rc;
+    // down: sorted h -> token rows (fused score mix) or per-slot f32 rows + mix kernel
+    g.codec = cd;
+    g.N = (int)d;
+    g.K = (int)f;
+    g.x = base + p.hs_off;
+    g.x_row_stride = f;
+    g.w_row_stride = d_rs;
+    g.w_expert_stride = d_es;
+    g.n_per_expert = (int)d;
+    g.act = ACT_NONE;
+    g.w2 = nullptr;
+    if (fused_mix) {
+        if ((ce = cudaMemsetAsync(y, 0, (size_t)t * d * sizeof(float), st)) != cudaSuccess) return cuda_status(ce, what);
+        g.y = y;
+        g.y_dtype = KQ_F32;
+        g.y_row_stride = d;
+        g.out_row = tok_of;
+        g.row_scale = scale_of;
+    } else {
+        g.y = base + p.ys_off;
+        g.y_dtype = KQ_F32;
+        g.y_row_stride = d;
+        g.out_row = perm;
+    }
+    rc = grouped_pass(g, cd, (const uint8_t *)down_w, nullptr, e, p.chunk_d, d, f, d_rs, d_es, x_dtype, base + p.b_off,
+                      p.mt, p.max_tiles, st, what);
+    if (rc) return rc;
+    if (!fused_mix)
+        return cuda_status(launch_moe_mix((const float *)(base + p.ys_off), scores, idx, (int)ebase, (int)e, (int)t, k,
+                                          (int)d, y, y_dtype, st),
+                           what);
+    return KQ_OK;
+}
+
 // Routed (MoE) GEMV over expert stacks.  mode: 0 glu (x row = slot/k),
 // 1 per-slot rows (x row = slot), 2 explicit x_index.
 int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, int64_t slots, int kslot,
@@ -665,7 +818,13 @@ size_t kq_moe_expert_layer_workspace_size(int codec_gu, int codec_d, int64_t t, 
     const size_t a = routed_ws(codec_gu, slots, t, e_local, f, d, ACT_SILU, false);
     const size_t b = routed_ws(codec_d, slots, t, e_local, d, f, ACT_NONE, true);
     const size_t esz = h_dtype == KQ_F32 ? 4 : 2;
-    return align256(a > b ? a : b) + align256((size_t)slots * f * esz);
+    size_t need = align256(a > b ? a : b) + align256((size_t)slots * f * esz);
+    if (slots >= (int64_t)GEMM_MIN_M * e_local)  // the grouped layer path may be taken (see the entry point)
+        for (int mt_total = 0; mt_total < 2; mt_total++) {
+            const LayerPlan lp = layer_plan(codec_gu, codec_d, slots, e_local, mt_total ? e_local : slots, d, f, true);
+            need = std::max(need, lp.total);
+        }
+    return need;
 }
 
 int kq_moe_expert_layer_local(int codec_gu, int codec_d, const void *x, int x_dtype, int64_t t, int64_t d,
@@ -689,6 +848,20 @@ int kq_moe_expert_layer_local(int codec_gu, int codec_d, const void *x, int x_dt
     if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255))
         return fail(KQ_ERR_WORKSPACE, "moe_expert_layer_local: workspace of %zu bytes required, got %zu", need,
                     workspace_bytes);
+    if (use_grouped(codec_gu, slots, e_total, f, d, act, true, x_dtype, d) &&
+        use_grouped(codec_d, slots, e_total, d, f, ACT_NONE, false, x_dtype, f) &&
+        workspace_bytes >= layer_plan(codec_gu, codec_d, slots, e_local, e_total, d, f, y_dtype != KQ_F32).total) {
+        const char *what = "moe_expert_layer_local";
+        int rc;
+        if ((rc = check_weights(codec_gu, gate_w, d, gu_row_stride, what)) ||
+            (rc = check_weights(codec_gu, up_w, d, gu_row_stride, what)) ||
+            (rc = check_weights(codec_d, down_w, f, d_row_stride, what)) || (rc = check_x(x, x_dtype, d, what)))
+            return rc;
+        if (!out_dtype_ok(y_dtype)) return fail(KQ_ERR_DTYPE, "%s: bad output dtype %d", what, y_dtype);
+        return run_grouped_layer(codec_gu, codec_d, x, x_dtype, t, d, idx, k, scores, gate_w, up_w, gu_row_stride,
+                                 gu_expert_stride, down_w, d_row_stride, d_expert_stride, e_local, f, expert_base,
+                                 e_total, act, y, y_dtype, workspace, workspace_bytes, stream);
+    }
     void *h = (char *)workspace + routed;
     int rc = run_routed(codec_gu, x, x_dtype, d, d, slots, k, t, idx, nullptr, 0, gate_w, up_w, e_local, f,
                         gu_row_stride, gu_expert_stride, act, h, x_dtype, f, nullptr, workspace, routed, stream,

@@ -581,3 +581,30 @@ def test_iq2_sparse_routing_single_slot_groups(cuda):
             ref[ti] += sc[ti, j] * O.matmul(hb, wd[ex], "iq2_xxs")[0]
     assert rel_err(y, ref) <= TOL
     assert kq.workspace_error() == 0
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_grouped_moe_layer_two_row_tiles(cuda, out_dtype):
+    """Experts averaging >= 192 routed rows take 256-row tiles (two accumulators
+    per CTA); the layer sorts once and the down GEMM reads h in sorted order."""
+    e, d, f, k, t = 4, 512, 256, 2, 600
+    wg, wu, wd, x, _ = _moe_case("q4_k", "q6_k", e, d, f, t, k, seed=120)
+    rng = np.random.default_rng(121)
+    idx = np.stack([_skewed_ids(rng, (t,), e), rng.integers(0, e, size=t).astype(np.int32)], 1)
+    sc = rng.random((t, k)).astype(np.float32)
+    tw = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    y = kq.moe_expert_layer_local(to_dev_x(x, cuda), tw(idx), tw(sc), tw(wg), tw(wu), tw(wd), "q4_k", "q6_k", 0, e,
+                                  out_dtype=out_dtype).float()
+    ref = np.zeros((t, d))
+    for j in range(k):
+        for ex in range(e):
+            sel = np.nonzero(idx[:, j] == ex)[0]
+            if not len(sel):
+                continue
+            xs = np.ascontiguousarray(x[sel])
+            g = O.matmul(xs, wg[ex], "q4_k").astype(np.float64)
+            u = O.matmul(xs, wu[ex], "q4_k").astype(np.float64)
+            hb = synth.f32_to_bf16_bits((g / (1 + np.exp(-g)) * u).astype(np.float32))
+            ref[sel] += sc[sel, j, None] * O.matmul(hb, wd[ex], "q6_k")
+    assert rel_err(y.cpu().numpy(), ref) <= TOL
+    assert kq.workspace_error() == 0
