@@ -51,17 +51,22 @@ int cuda_status(cudaError_t e, const char *what) {
     return fail(KQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-bool codec_ok(int c) { return c == KQ_Q4_K || c == KQ_Q5_K || c == KQ_Q6_K || c == KQ_IQ2_XXS || c == KQ_Q8_0; }
+bool codec_ok(int c) {
+    return c == KQ_Q4_K || c == KQ_Q5_K || c == KQ_Q6_K || c == KQ_IQ2_XXS || c == KQ_Q8_0 || c == KQ_IQ3_XXS ||
+           c == KQ_IQ4_XS;
+}
+// codecs whose only GEMV is the one-row (lane-per-row) path
+bool onerow_only(int c) { return c == KQ_Q5_K || c == KQ_Q8_0 || c == KQ_IQ3_XXS || c == KQ_IQ4_XS; }
 bool act_dtype_ok(int d) { return d == KQ_F16 || d == KQ_BF16; }
 bool out_dtype_ok(int d) { return d == KQ_F32 || d == KQ_F16 || d == KQ_BF16; }
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 int check_weights(int codec, const void *w, int64_t k, int64_t row_stride, const char *what) {
-    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q8_0=8, q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16)", what, codec);
+    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q8_0=8, q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16, iq3_xxs=18, iq4_xs=23)", what, codec);
     if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a positive multiple of %d", what, (long long)k, QK);
     const int64_t rb = k / QK * block_bytes(codec);
     if (row_stride < rb) return fail(KQ_ERR_SHAPE, "%s: row stride %lld < row bytes %lld", what, (long long)row_stride, (long long)rb);
-    const int64_t need = (codec == KQ_Q4_K || codec == KQ_Q5_K) ? 16 : 2;
+    const int64_t need = (codec == KQ_Q4_K || codec == KQ_Q5_K) ? 16 : codec == KQ_IQ4_XS ? 8 : 2;
     if (((uintptr_t)w | (uintptr_t)row_stride) % need)
         return fail(KQ_ERR_ALIGN, "%s: weight base/row stride must be %lld-byte aligned for codec %d", what, (long long)need, codec);
     return KQ_OK;
@@ -135,9 +140,10 @@ int gemm_min_m() {
     return v;
 }
 
-// Q5_K and Q8_0 have a one-row GEMV only: every other batch goes to the tcgen05 GEMM
+// Q5_K, Q8_0, IQ3_XXS and IQ4_XS have a one-row GEMV only: every other batch
+// goes to the tcgen05 GEMM
 bool use_gemm(int64_t m, int codec = 0) {
-    return m >= gemm_min_m() || ((codec == KQ_Q5_K || codec == KQ_Q8_0) && m >= 2);
+    return m >= gemm_min_m() || (onerow_only(codec) && m >= 2);
 }
 
 size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
@@ -514,8 +520,8 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     // IQ2_XXS decode is ALU-bound: with sparse routing (on average well under one
     // slot per expert) one-slot groups take the one-row integer path, faster
     // than 8-row MMA groups even counting the few experts streamed twice
-    const int gsize = ((codec == KQ_IQ2_XXS && slots * 4 <= etotal) || codec == KQ_Q5_K || codec == KQ_Q8_0)
-                          ? 1  // Q5_K / Q8_0: the one-row path is their only GEMV
+    const int gsize = ((codec == KQ_IQ2_XXS && slots * 4 <= etotal) || onerow_only(codec))
+                          ? 1  // one-row-only codecs: the one-row path is their only GEMV
                           : (int)(per_expert < 8 ? per_expert : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
@@ -579,7 +585,7 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
 size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_t n, int64_t kin, int act,
                  bool mix) {
     // IQ2_XXS may run with one-slot groups (see run_routed): size for those too
-    const int gsize = (codec == KQ_IQ2_XXS || codec == KQ_Q5_K || codec == KQ_Q8_0) ? 1
+    const int gsize = (codec == KQ_IQ2_XXS || onerow_only(codec)) ? 1
                                                                  : (int)(per_expert < 8 ? (per_expert > 0 ? per_expert : 1) : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
@@ -612,9 +618,9 @@ int kq_version(void) { return 100; }
 const char *kq_last_error(void) { return g_msg; }
 
 int kq_codecs(int *out, int cap) {
-    static const int ids[5] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS, KQ_Q8_0};
-    for (int i = 0; i < 5 && i < cap; i++) out[i] = ids[i];
-    return 5;
+    static const int ids[7] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS, KQ_Q8_0, KQ_IQ3_XXS, KQ_IQ4_XS};
+    for (int i = 0; i < 7 && i < cap; i++) out[i] = ids[i];
+    return 7;
 }
 
 int kq_codec_has_matmul(int codec) { return codec_ok(codec) ? 1 : 0; }

@@ -58,6 +58,26 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
             const int q = (((ql[i] >> (4 * (s >> 1))) & 15) | (((qh[i] >> (2 * s)) & 3) << 4)) - 32;
             o[i] = dl * (float)q;
         }
+    } else if constexpr (C == IQ3_XXS) {  // lane: sign group lane & 3 of sub-block lane >> 2
+        const int j = lane >> 2, l = lane & 3;
+        const float d = half_bits_to_float(ld_u16(b));
+        const uint32_t aux = ld_u32_unaligned(b + 66 + 4 * j);
+        const float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
+        const uint32_t sg = ksigns((aux >> (7 * l)) & 127u);
+        const uint32_t e0 = c_iq3xxs_grid[b[2 + 8 * j + 2 * l]], e1 = c_iq3xxs_grid[b[3 + 8 * j + 2 * l]];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float gv = (float)(((i < 4 ? e0 : e1) >> (8 * (i & 3))) & 255u);
+            o[i] = db * gv * (((sg >> i) & 1u) ? -1.0f : 1.0f);
+        }
+    } else if constexpr (C == IQ4_XS) {  // lane: weights 8 (lane & 3) .. +7 of sub-block lane >> 2
+        const int j = lane >> 2, i0 = 8 * (lane & 3), h = i0 >> 4;
+        const float d = half_bits_to_float(ld_u16(b));
+        const int ls = ((b[4 + (j >> 1)] >> (4 * (j & 1))) & 15) | (((ld_u16(b + 2) >> (2 * j)) & 3) << 4);
+        const float dl = d * (float)(ls - 32);
+        const uint8_t *q = b + 8 + 16 * j + (i0 & 15);
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = dl * (float)c_iq4nl_values[(q[i] >> (4 * h)) & 15];
     } else {
         const int g = lane >> 2, s = lane & 3;
         const float d = half_bits_to_float(ld_u16(b));
@@ -251,6 +271,8 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ3_XXS: return launch_deq<IQ3_XXS>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ4_XS: return launch_deq<IQ4_XS>(w, rows, nb, row_stride, out, dtype, st);
     default: return launch_deq<IQ2_XXS>(w, rows, nb, row_stride, out, dtype, st);
     }
 }

@@ -11,10 +11,18 @@
 //                w = (d*sc_j)*(q - 32)                    quants.py:552-572
 //   IQ2_XXS 66 B d f16 | 8 x (u32 grid indices, u32 signs+scale)
 //                w = d*(0.5+ls)*0.25 * grid * sign        quants.py:766-829
+//   Q5_K  176 B  d f16 | dmin f16 | 12 B scales | 32 B qh | 128 B nibbles
+//                w = (d*sc_j)*(q | qh_bit << 4) - (dmin*m_j)  quants.py:525-549
+//   Q8_0  8 x 34 B  (d f16 | 32 x int8), w = q*d       quants.py:378-402
+//   IQ3_XXS 98 B d f16 | 64 B grid indices | 8 x u32 (4 x 7-bit signs, ls)
+//                w = d*(0.5+ls)*0.5 * grid * sign         quants.py:1005-1054
+//   IQ4_XS 136 B d f16 | u16 scales_h | 4 B scales_l | 128 B nibbles
+//                w = (d*(ls-32)) * kvalues[q]             quants.py:1351-1377
 //
 // Exactness: every product above is exact in f32 (fp16 d has 11 significant
 // bits; d*sc <= 17 bits, d*sc*q <= 21 bits; Q6_K d*sc*(q-32) <= 24 bits;
-// IQ2_XXS d*(0.5+ls)*0.25*grid <= 22 bits), so a dequantized weight is
+// IQ2_XXS d*(0.5+ls)*0.25*grid <= 22 bits; IQ3_XXS d*(0.5+ls)*0.5*grid <= 22
+// bits; IQ4_XS d*(ls-32)*kvalue <= 24 bits), so a dequantized weight is
 // bit-identical to gguf-py whether or not the compiler contracts to FMA: only
 // the final Q4_K subtraction rounds, once, in either form.
 #pragma once
@@ -26,7 +34,7 @@
 
 namespace kq {
 
-enum Codec : int { Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16 };
+enum Codec : int { Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_XS = 23 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
 constexpr int QK = 256;
@@ -39,14 +47,20 @@ template <> struct Fmt<Q5_K> { static constexpr int bpb = 176; static constexpr 
 template <> struct Fmt<Q8_0> { static constexpr int bpb = 272; static constexpr int sub = 32; };
 template <> struct Fmt<Q6_K> { static constexpr int bpb = 210; static constexpr int sub = 16; };
 template <> struct Fmt<IQ2_XXS> { static constexpr int bpb = 66; static constexpr int sub = 32; };
+template <> struct Fmt<IQ3_XXS> { static constexpr int bpb = 98; static constexpr int sub = 32; };
+template <> struct Fmt<IQ4_XS> { static constexpr int bpb = 136; static constexpr int sub = 32; };
 
 __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
-         : codec == Q8_0 ? 272 : -1;
+         : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : -1;
 }
 
 // 256-entry IQ2_XXS grid, byte i of entry e = |w_i| in {8, 25, 43}.
 static __device__ __constant__ uint64_t c_iq2xxs_grid[256] = KQ_IQ2XXS_GRID_INIT;
+// 256-entry IQ3_XXS grid, byte i of entry e = |w_i| in {4, 12, ..., 62}.
+static __device__ __constant__ uint32_t c_iq3xxs_grid[256] = KQ_IQ3XXS_GRID_INIT;
+// The sixteen IQ4_NL values an IQ4_XS nibble selects, as bytes of four words.
+static __device__ __constant__ __align__(16) int8_t c_iq4nl_values[16] = KQ_IQ4NL_VALUES_INIT;
 
 // ggml's 7-bit -> 8-bit sign expansion: bit 7 restores even parity.
 __device__ __forceinline__ uint32_t ksigns(uint32_t i7) {

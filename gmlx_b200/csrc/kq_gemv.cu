@@ -61,6 +61,10 @@ template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; 
 template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
 template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1; };    // dsc x 2 rows
 template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 2; };  // db x 2 rows
+template <> struct GCfg<IQ3_XXS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };  // lane-per-row path only
+template <> struct GCfg<IQ4_XS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
+// shared-memory lattice table: IQ2_XXS 256 x 16 B (MMA path) or 8 B; IQ3_XXS 256 x 4 B
+template <int C> constexpr int GRIDB = C == IQ2_XXS ? 4096 : C == IQ3_XXS ? 1024 : 0;
 template <int C> constexpr int KB_OF = NCOL * GCfg<C>::BPW;
 template <int C> constexpr int XSTR_OF = KB_OF<C> * QK * 2 + 64;  // staged activation row stride (bytes)
 constexpr int SMEM_BUDGET = 112 * 1024;  // per CTA: two CTAs per SM
@@ -96,15 +100,15 @@ template <int C, int NT, int XR> struct GLayout {
     // one reduction buffer (two, alternating): [column][token][row]; the
     // lane-per-row path keeps one token per warp
     static constexpr int REDB = DP ? CW * RED_TS * 4 : NCOL * 8 * NT * RED_TS * 4;
-    static constexpr int FIXED = 512 + (C == IQ2_XXS ? 4096 : 0) + TABS + SBYTES + 2 * REDB + DPB;
+    static constexpr int FIXED = 512 + GRIDB<C> + TABS + SBYTES + 2 * REDB + DPB;
     static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<C, NT> - FIXED) / STAGE;
     static constexpr int NS = NS_FIT > 8 ? 8 : (NS_FIT < 2 ? 2 : NS_FIT);  // ring depth (<= 8: rowoff table)
     static constexpr int OFF_BAR = 0;                              // 2*NS mbarriers
     static constexpr int OFF_ROWOFF = 128;                         // NS x 32 bytes
     static constexpr int OFF_MISC = OFF_ROWOFF + 32 * 8;           // flags
     static constexpr int OFF_UNIT = 512;                           // dynamic mode: tile id per ring slot
-    static constexpr int OFF_GRID = 640;                           // IQ2 grid: 256 x 16 B
-    static constexpr int OFF_RING = OFF_GRID + (C == IQ2_XXS ? 4096 : 0);
+    static constexpr int OFF_GRID = 640;                           // lattice table (GRIDB bytes)
+    static constexpr int OFF_RING = OFF_GRID + GRIDB<C>;
     static constexpr int OFF_SCALE = OFF_RING + NS * STAGE;        // CW x TABW floats
     static constexpr int OFF_S = OFF_SCALE + TABS;
     static constexpr int OFF_RED = OFF_S + SBYTES;
@@ -848,6 +852,111 @@ __device__ __forceinline__ float dp_iq2_dot(const IQ2Regs &r, const uint32_t *xq
     return acc;
 }
 
+// Lane-per-row IQ3_XXS: as IQ2_XXS with one grid byte index per 4 weights.
+// The 98-byte block (2-byte aligned) is read as 25 words: 16 words of grid
+// indices then 8 words of (four 7-bit sign indices, ls << 28), one per
+// 32-weight sub-block.  Per sub-block:
+//     acc += d (0.5 + ls) / 2 * dx_j * sum_j(signed grid * x_q).
+struct IQ3Regs {
+    uint32_t q[24];
+    float d;
+};
+
+__device__ __forceinline__ void dp_iq3_load(const uint8_t *blk, IQ3Regs &r) {
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    uint32_t w[25];
+#pragma unroll
+    for (int i = 0; i < 25; i++) w[i] = aw[i];  // up to 2 bytes past the block: the ring row has slack
+    r.d = half_bits_to_float(__funnelshift_r(w[0], w[1], sh) & 0xffffu);
+#pragma unroll
+    for (int j = 0; j < 24; j++) r.q[j] = sh ? w[j + 1] : __funnelshift_r(w[j], w[j + 1], 16);
+}
+
+__device__ __forceinline__ float dp_iq3_dot(const IQ3Regs &r, const uint32_t *xq, const float *xsc,
+                                           const uint32_t *grid) {
+    float acc = 0.f;
+#pragma unroll
+    for (int sb = 0; sb < 8; sb++) {
+        const uint32_t aux = r.q[16 + sb];
+        int sum = 0;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint32_t gw = r.q[2 * sb + (l >> 1)] >> (16 * (l & 1));
+            const uint32_t g0 = grid[gw & 255u], g1 = grid[(gw >> 8) & 255u];
+            const uint32_t sg = ksigns((aux >> (7 * l)) & 127u);
+            const uint32_t f0 = ((sg & 15u) * 0x00204081u) & 0x01010101u, f1 = ((sg >> 4) * 0x00204081u) & 0x01010101u;
+            const int s0 = (int)((g0 ^ (f0 * 0xffu)) + f0), s1 = (int)((g1 ^ (f1 * 0xffu)) + f1);
+            const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 16 * sb + 4 * l);
+            sum = __dp2a_lo((int)xv.x, s0, sum);
+            sum = __dp2a_hi((int)xv.y, s0, sum);
+            sum = __dp2a_lo((int)xv.z, s1, sum);
+            sum = __dp2a_hi((int)xv.w, s1, sum);
+        }
+        acc = fmaf(r.d * (0.5f + (float)(aux >> 28)) * 0.5f * xsc[sb], (float)sum, acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
+// Lane-per-row IQ4_XS: every nibble selects one of sixteen signed bytes (the
+// IQ4_NL values, held in four registers) by two byte permutes (low three bits)
+// and a per-byte select on bit 3; the signed bytes dot the int16 activations
+// with dp2a.  Blocks are 136 bytes, so rows at 8-byte aligned addresses keep
+// every block 8-byte aligned (the entry points require it).  Per sub-block:
+//     acc += d (ls - 32) * dx_j * sum_j(value[q] * x_q).
+struct IQ4Regs {
+    uint2 h;
+    uint32_t q[32];
+};
+
+__device__ __forceinline__ void dp_iq4xs_load(const uint8_t *blk, IQ4Regs &r) {
+    r.h = *reinterpret_cast<const uint2 *>(blk);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(blk + 8 + 8 * i);
+        r.q[2 * i] = v.x;
+        r.q[2 * i + 1] = v.y;
+    }
+}
+
+// four nibbles (one per byte, bits 0-3) -> four signed table bytes
+__device__ __forceinline__ int iq4_lookup4(uint32_t n, const uint32_t (&tv)[4]) {
+    const uint32_t t = n & 0x07070707u;
+    const uint32_t sel = prmt(t | (t >> 4), 0, 0x0020);  // nibble k = low 3 bits of byte k
+    const uint32_t lo = prmt(tv[0], tv[1], sel), hi = prmt(tv[2], tv[3], sel);
+    const uint32_t m = ((n >> 3) & 0x01010101u) * 0xffu;
+    return (int)((lo & ~m) | (hi & m));
+}
+
+__device__ __forceinline__ float dp_iq4xs_dot(const IQ4Regs &r, const uint32_t *xq, const float *xsc) {
+    const uint32_t *tw = reinterpret_cast<const uint32_t *>(c_iq4nl_values);
+    const uint32_t tv[4] = {tw[0], tw[1], tw[2], tw[3]};
+    const float d = half_bits_to_float(r.h.x & 0xffffu);
+    const uint32_t sh = r.h.x >> 16, sl = r.h.y;
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t w = r.q[4 * j + i];
+            const int vlo = iq4_lookup4(w & 0x0f0f0f0fu, tv), vhi = iq4_lookup4((w >> 4) & 0x0f0f0f0fu, tv);
+            const uint2 xl = *reinterpret_cast<const uint2 *>(xq + 16 * j + 2 * i);
+            const uint2 xh = *reinterpret_cast<const uint2 *>(xq + 16 * j + 8 + 2 * i);
+            sum = __dp2a_lo((int)xl.x, vlo, sum);
+            sum = __dp2a_hi((int)xl.y, vlo, sum);
+            sum = __dp2a_lo((int)xh.x, vhi, sum);
+            sum = __dp2a_hi((int)xh.y, vhi, sum);
+        }
+        const int ls = (int)(((sl >> (4 * j)) & 15u) | (((sh >> (2 * j)) & 3u) << 4));
+        acc = fmaf(d * (float)(ls - 32) * xsc[j], (float)sum, acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 // -------------------------------------------------------------------------
 
 template <int C, int NT, bool F16, bool GLU, int XR>
@@ -890,6 +999,9 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
         *s_npub = 0;
         for (int b = 0; b <= NS; b++) reinterpret_cast<int *>(smem + L::OFF_MISC + 16)[b] = 0;
         fence_mbar_init();
+    }
+    if constexpr (C == IQ3_XXS) {
+        for (int e = threadIdx.x; e < 256; e += NTHREADS) reinterpret_cast<uint32_t *>(gridtab)[e] = c_iq3xxs_grid[e];
     }
     if constexpr (C == IQ2_XXS && L::DP) {
         // lane-per-row path: the raw magnitude bytes (256 x 8 B)
@@ -1122,6 +1234,24 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q6k_dot(r, hf, xq, xsc);
+        } else if constexpr (C == IQ3_XXS) {
+            IQ3Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_iq3_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_iq3_dot(r, xq, xsc, reinterpret_cast<const uint32_t *>(gridtab));
+        } else if constexpr (C == IQ4_XS) {
+            IQ4Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_iq4xs_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_iq4xs_dot(r, xq, xsc);
         } else {
             IQ2Regs r;
             if (run) {
@@ -1613,7 +1743,7 @@ cudaError_t launch_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     return glu ? launch_nt<C, false, true>(a, st, grid_out) : launch_nt<C, false, false>(a, st, grid_out);
 }
 
-// Q5_K and Q8_0 have the lane-per-row path only (one activation row per
+// Q5_K, Q8_0, IQ3_XXS and IQ4_XS have the lane-per-row path only (one activation row per
 // group); the callers route every other shape to the tcgen05 GEMM
 template <int C, bool F16, bool GLU>
 cudaError_t launch_onerow(const GemvArgs &a, cudaStream_t st, int *grid_out) {
@@ -1631,6 +1761,8 @@ cudaError_t launch_onerow_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
 cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == Q5_K) return launch_onerow_c<Q5_K>(a, st, grid_out);
     if (a.codec == Q8_0) return launch_onerow_c<Q8_0>(a, st, grid_out);
+    if (a.codec == IQ3_XXS) return launch_onerow_c<IQ3_XXS>(a, st, grid_out);
+    if (a.codec == IQ4_XS) return launch_onerow_c<IQ4_XS>(a, st, grid_out);
     switch (a.codec) {
     case Q4_K: return launch_c<Q4_K>(a, st, grid_out);
     case Q6_K: return launch_c<Q6_K>(a, st, grid_out);

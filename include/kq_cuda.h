@@ -21,7 +21,8 @@
  *    on one stream; calls that overlap in time must use different workspaces.
  *    The first int of a workspace is a sticky device error word set by a
  *    kernel whose bounded wait ran out (read it with kq_workspace_error).
- *  - Codec ids are ggml's: Q4_K = 12, Q6_K = 14, IQ2_XXS = 16.
+ *  - Codec ids are ggml's: Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16,
+ *    IQ3_XXS = 18, IQ4_XS = 23.
  *    Activation / output dtypes: KQ_F32 = 0, KQ_F16 = 1, KQ_BF16 = 2.
  */
 #ifndef KQ_CUDA_H
@@ -39,6 +40,8 @@ extern "C" {
 #define KQ_Q5_K 13
 #define KQ_Q6_K 14
 #define KQ_IQ2_XXS 16
+#define KQ_IQ3_XXS 18 /* 98-byte blocks */
+#define KQ_IQ4_XS 23  /* 136-byte blocks; weights 8-byte aligned */
 
 #define KQ_F32 0
 #define KQ_F16 1

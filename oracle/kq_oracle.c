@@ -18,6 +18,8 @@
  *   Q8_0   (Q8_0.dequantize_blocks): w = q * d per 32-weight block
  *   Q6_K   (quants.py:554-572): dl = d*sc, w = dl*(q-32)
  *   IQ2_XXS(quants.py:802-829): db = d*(0.5+ls)*0.25, w = db*grid*sign
+ *   IQ3_XXS(quants.py:1027-1054): db = d*(0.5+ls)*0.5, w = db*grid*sign
+ *   IQ4_XS (quants.py:1351-1377): dl = d*(ls-32), w = dl*kvalues[q]
  * Every product above is exact in f32 (see the kernels' header), so results
  * are independent of FMA contraction; the file is still built with
  * -ffp-contract=off to keep the statement literal.
@@ -33,9 +35,11 @@
 #include "kq_tables.h"
 
 #define QK 256
-enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16 };
+enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
+static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
+static const int8_t kqo_iq4nl[16] = KQ_IQ4NL_VALUES_INIT;
 
 /* IEEE binary16 -> f32, exact (gguf-py: view(np.float16).astype(np.float32)). */
 static float kqo_half(uint16_t h) {
@@ -61,6 +65,7 @@ int kqo_block_bytes(int codec) {
     switch (codec) {
     case KQO_Q4_K: return 144; case KQO_Q5_K: return 176; case KQO_Q6_K: return 210; case KQO_IQ2_XXS: return 66;
     case KQO_Q8_0: return 272; /* eight 34-byte blocks per 256 weights */
+    case KQO_IQ3_XXS: return 98; case KQO_IQ4_XS: return 136;
     }
     return -1;
 }
@@ -168,6 +173,45 @@ static void deq_iq2xxs(const uint8_t *b, float *o) {
     }
 }
 
+/* gguf-py IQ3_XXS.dequantize_blocks (quants.py:1027-1054): d, 64 grid-index
+ * bytes (one per 4 weights), then 8 words of (4 x 7-bit sign indices, ls << 28),
+ * one word per 32-weight sub-block. */
+static void deq_iq3xxs(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    const uint8_t *qs = b + 2, *ss = b + 66;
+    for (int j = 0; j < 8; j++) {
+        uint32_t aux;
+        memcpy(&aux, ss + 4 * j, 4);
+        float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
+        for (int l = 0; l < 4; l++) {
+            uint8_t sg = kqo_ksigns((aux >> (7 * l)) & 0x7f);
+            for (int i = 0; i < 8; i++) {
+                uint32_t e = kqo_grid3[qs[8 * j + 2 * l + (i >> 2)]];
+                float gv = (float)((e >> (8 * (i & 3))) & 0xff);
+                float sv = ((sg >> i) & 1) ? -1.0f : 1.0f;
+                o[32 * j + 8 * l + i] = db * gv * sv;
+            }
+        }
+    }
+}
+
+/* gguf-py IQ4_XS.dequantize_blocks (quants.py:1351-1377): d, 16 bits of
+ * high scale pairs, 4 bytes of low scale nibbles, then 16 bytes per sub-block
+ * (low nibbles: weights 0-15, high nibbles: 16-31) indexing IQ4_NL.kvalues. */
+static void deq_iq4xs(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    unsigned sh = (unsigned)(b[2] | b[3] << 8);
+    const uint8_t *sl = b + 4, *qs = b + 8;
+    for (int j = 0; j < 8; j++) {
+        int ls = ((sl[j >> 1] >> (4 * (j & 1))) & 0x0f) | (((sh >> (2 * j)) & 3) << 4);
+        float dl = d * (float)(ls - 32);
+        for (int l = 0; l < 16; l++) {
+            o[32 * j + l] = dl * (float)kqo_iq4nl[qs[16 * j + l] & 0x0f];
+            o[32 * j + 16 + l] = dl * (float)kqo_iq4nl[qs[16 * j + l] >> 4];
+        }
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -175,6 +219,8 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_Q8_0: deq_q80(b, o); return 0;
     case KQO_Q6_K: deq_q6k(b, o); return 0;
     case KQO_IQ2_XXS: deq_iq2xxs(b, o); return 0;
+    case KQO_IQ3_XXS: deq_iq3xxs(b, o); return 0;
+    case KQO_IQ4_XS: deq_iq4xs(b, o); return 0;
     }
     return -1;
 }

@@ -31,9 +31,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
-Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS = 8, 12, 13, 14, 16
-CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0}
-BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272}  # per 256 weights
+Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_XS = 8, 12, 13, 14, 16, 18, 23
+CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
+             "iq4_xs": IQ4_XS}
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -182,6 +183,25 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         gidx = qs[..., 0].copy().view(np.uint8).reshape(n, 8, 4)
         g = from_grid[gidx].astype(np.float32)
         out = db * g * sgn
+    elif c == IQ3_XXS:  # quants.py:1027-1054
+        d = _half(blocks[:, 0:2]).reshape(n, 1)
+        gidx = blocks[:, 2:66].reshape(n, 8, 4, 2)
+        aux = blocks[:, 66:98].copy().view(np.uint32).reshape(n, 8)
+        db = (d * (np.float32(0.5) + (aux >> 28).astype(np.float32)) * np.float32(0.5)).reshape(n, 8, 1, 1)
+        sidx = (aux.reshape(n, 8, 1) >> np.array([0, 7, 14, 21], np.uint32)) & 127
+        ks = ksigns_table()[sidx].reshape(n, 8, 4, 1)
+        sgn = np.where((ks >> np.arange(8, dtype=np.uint8)) & 1, np.float32(-1), np.float32(1))
+        g = iq3xxs_grid()[gidx].reshape(n, 8, 4, 8).astype(np.float32)
+        out = db * g * sgn
+    elif c == IQ4_XS:  # quants.py:1351-1377
+        d = _half(blocks[:, 0:2]).reshape(n, 1)
+        sh = blocks[:, 2:4].copy().view(np.uint16).reshape(n, 1)
+        sl = blocks[:, 4:8].reshape(n, 4, 1) >> np.array([0, 4], np.uint8).reshape(1, 1, 2)
+        ls = (sl.reshape(n, 8) & 15).astype(np.int32) | (((sh >> (2 * np.arange(8, dtype=np.uint16))) & 3) << 4)
+        dl = (d * (ls - 32).astype(np.float32)).reshape(n, 8, 1)
+        q = blocks[:, 8:].reshape(n, 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
+        kv = np.array(_table_values("KQ_IQ4NL_VALUES_INIT"), np.float32)
+        out = dl * kv[(q & 15).reshape(n, 8, 32)]
     else:
         raise ValueError(codec)
     return out.reshape(*np.asarray(w).shape[:-1], -1).astype(np.float32)
@@ -196,19 +216,31 @@ def ksigns_table() -> np.ndarray:
     return (i | (p << 7)).astype(np.uint8)
 
 
-_GRID = None
+_GRIDS = {}
+
+
+def _table_values(macro: str) -> list:
+    """Integer entries of one ``#define <macro> { ... }`` of the generated header."""
+    hdr = os.path.join(HERE, "..", "gmlx_b200", "csrc", "_gen", "kq_tables.h")
+    if not os.path.exists(hdr):
+        build(force=True)
+    body = open(hdr).read().split("#define " + macro, 1)[1].split("{", 1)[1].split("}")[0]
+    return [int(t.rstrip("ul"), 0) for t in body.replace("\\", " ").replace(",", " ").split()]
+
+
+def _grid(macro: str, width: int) -> np.ndarray:
+    if macro not in _GRIDS:
+        vals = _table_values(macro)
+        assert len(vals) == 256
+        _GRIDS[macro] = np.array([[(v >> (8 * i)) & 0xFF for i in range(width)] for v in vals], np.uint8)
+    return _GRIDS[macro]
 
 
 def iq2xxs_grid() -> np.ndarray:
     """``[256, 8]`` uint8 magnitudes, parsed from the generated kernel header."""
-    global _GRID
-    if _GRID is None:
-        hdr = os.path.join(HERE, "..", "gmlx_b200", "csrc", "_gen", "kq_tables.h")
-        if not os.path.exists(hdr):
-            build(force=True)
-        vals = [int(t.strip().rstrip(",").rstrip("ull").rstrip("u"), 16)
-                for t in open(hdr).read().split("{", 1)[1].split("}")[0].replace("\\", "").split()
-                if t.startswith("0x")]
-        assert len(vals) == 256
-        _GRID = np.array([[(v >> (8 * i)) & 0xFF for i in range(8)] for v in vals], np.uint8)
-    return _GRID
+    return _grid("KQ_IQ2XXS_GRID_INIT", 8)
+
+
+def iq3xxs_grid() -> np.ndarray:
+    """``[256, 4]`` uint8 magnitudes, parsed from the generated kernel header."""
+    return _grid("KQ_IQ3XXS_GRID_INIT", 4)

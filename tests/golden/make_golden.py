@@ -15,7 +15,9 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
          at a time;
   Q8_0   quants -128, -127, 0, 127 and d = 0, negative d, the largest fp16;
   Q6_K   int8 scales at -128, -64, 0, 63, 127; quants all 0 / all 63;
-  IQ2_XXS every grid index and every 7-bit sign index, ls = 0 and 15.
+  IQ2_XXS every grid index and every 7-bit sign index, ls = 0 and 15;
+  IQ3_XXS the same sweep over its 256-entry grid;
+  IQ4_XS  every nibble value, 6-bit scales 0 / 31 / 32 / 63, negative d.
 Matmul references are x @ dequant(W).T in float64 for bf16 x (N(0,1)) plus
 one-hot x rows, which must reproduce single dequantized columns exactly.
 """
@@ -32,7 +34,8 @@ from gguf.quants import dequantize  # noqa: E402
 
 from gmlx_b200 import synth  # noqa: E402
 
-QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0}
+QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
+      "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS}
 
 
 def fp16(v):
@@ -95,6 +98,36 @@ def edge_blocks(codec):
                 b[:192] = qfill
             b[192:208] = np.array([scv] * 16, np.int8).view(np.uint8)
             b[208:210] = fp16(2e-3)
+            blocks.append(b)
+    elif codec == "iq3_xxs":
+        # every grid index (64 per block -> 4 blocks), sign indices sweeping
+        # 0..127, ls alternating 0 / 15 over the sub-blocks
+        k = 0
+        for blk in range(4):
+            b = np.zeros(98, np.uint8)
+            b[0:2] = fp16(1.5e-3 if blk % 2 else -7e-4)
+            b[2:66] = np.arange(64 * blk, 64 * blk + 64, dtype=np.uint32).astype(np.uint8)
+            for j in range(8):
+                aux = 0
+                for s in range(4):
+                    aux |= ((k + s) % 128) << (7 * s)
+                k += 4
+                aux |= (15 if (j + blk) % 2 else 0) << 28
+                b[66 + 4 * j:70 + 4 * j] = np.array([aux], np.uint32).view(np.uint8)
+            blocks.append(b)
+    elif codec == "iq4_xs":
+        # every nibble value on every sub-block; 6-bit scales 0, 31, 32, 63
+        for blk, (dv, ls) in enumerate([(1e-3, 0), (1e-3, 63), (-2e-3, 32), (5e-4, 31), (1e-3, None)]):
+            b = np.zeros(136, np.uint8)
+            b[0:2] = fp16(dv)
+            lsv = rng.integers(0, 64, 8) if ls is None else np.full(8, ls)
+            sh = 0
+            for j in range(8):
+                sh |= int(lsv[j] >> 4) << (2 * j)
+                b[4 + j // 2] |= int(lsv[j] & 15) << (4 * (j % 2))
+            b[2:4] = np.array([sh], np.uint16).view(np.uint8)
+            q = (np.arange(128) + blk) % 16
+            b[8:] = (q | (((q + 7) % 16) << 4)).astype(np.uint8)
             blocks.append(b)
     else:
         # every grid index (4 per 8-byte group, 8 groups per block -> 8 blocks)

@@ -15,7 +15,7 @@ from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
-CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0"]
+CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs"]
 
 
 def rel_err(y, ref):
@@ -72,6 +72,10 @@ def test_quantized_matmul(cuda, codec, m, n, k):
     ("q5_k", 256, 8192),
     ("q8_0", 19200, 512),
     ("q8_0", 512, 14336),
+    ("iq3_xxs", 19200, 512),
+    ("iq3_xxs", 512, 14336),
+    ("iq4_xs", 4096, 4096),
+    ("iq4_xs", 256, 8192),
     ("q4_k", 19200, 512),   # >= 2 tiles per CTA: whole tiles handed out dynamically
     ("q4_k", 4096, 4096),   # one whole tile per CTA (stages fit the ring)
     ("q4_k", 256, 8192),    # few tiles, long K: K split into dynamic chunks
@@ -125,14 +129,16 @@ def test_quantized_matmul_split_k(cuda, codec):
 
 @pytest.mark.parametrize("codec", CODECS)
 def test_unaligned_row_pitch(cuda, codec):
-    # K=768 (3 blocks): Q6_K rows of 630 B and IQ2_XXS rows of 198 B are not 16-byte aligned
+    # K=768 (3 blocks): Q6_K rows of 630 B, IQ2_XXS rows of 198 B and IQ3_XXS rows of
+    # 294 B are not 16-byte aligned
     if codec in ("q4_k", "q5_k"):
         pytest.skip("Q4_K / Q5_K rows are always 16-byte multiples")
     w = synth.random_weight(codec, 96, 768, seed=12)
-    x = synth.random_activations(5, 768, seed=13)
-    ref = O.matmul(x, w, codec)
-    y = kq.quantized_matmul(to_dev_x(x, cuda), torch.from_numpy(w).to(cuda), None, codec)
-    assert rel_err(y.float().cpu().numpy(), ref) <= TOL
+    for m in (1, 5):  # the one-row path and the batched one
+        x = synth.random_activations(m, 768, seed=13)
+        ref = O.matmul(x, w, codec)
+        y = kq.quantized_matmul(to_dev_x(x, cuda), torch.from_numpy(w).to(cuda), None, codec)
+        assert rel_err(y.float().cpu().numpy(), ref) <= TOL
 
 
 @pytest.mark.parametrize("codec", CODECS)
@@ -186,7 +192,7 @@ def _moe_case(codec_gu, codec_d, e, d, f, t, k, seed):
 
 
 @pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs"), ("q5_k", "q5_k"),
-                                             ("q8_0", "q8_0")])
+                                             ("q8_0", "q8_0"), ("iq3_xxs", "iq3_xxs"), ("iq4_xs", "iq4_xs")])
 @pytest.mark.parametrize("t", [1, 5])
 def test_moe_decode_ops(cuda, codec_gu, codec_d, t):
     e, d, f, k = 16, 512, 256, 4
@@ -402,7 +408,8 @@ def test_grouped_gather_qmm(cuda, codec):
     assert kq.workspace_error() == 0
 
 
-@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs"), ("q5_k", "q6_k")])
+@pytest.mark.parametrize("codec_gu,codec_d", [("q4_k", "q6_k"), ("iq2_xxs", "iq2_xxs"), ("q5_k", "q6_k"),
+                                              ("iq3_xxs", "iq4_xs")])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 def test_grouped_moe_layer_prefill(cuda, codec_gu, codec_d, out_dtype):
     """MoE prefill (T*k >= 33 * experts) through the grouped GEMM: gate/up GEMMs,

@@ -9,7 +9,7 @@ from gmlx_b200 import synth
 from oracle import oracle as O
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
-CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0"]
+CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs"]
 
 
 @pytest.fixture(scope="module")
@@ -44,7 +44,8 @@ def test_oracle_matmul_matches_golden(gold, codec):
 def test_oracle_matches_gguf_py_random(codec, seed):
     gq = pytest.importorskip("gguf.quants")
     from gguf.constants import GGMLQuantizationType as T
-    qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0}[codec]
+    qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
+          "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS}[codec]
     w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
 
@@ -56,7 +57,8 @@ def test_raw_random_bytes_match_where_finite():
     from gguf.constants import GGMLQuantizationType as T
     rng = np.random.default_rng(5)
     for codec, qt, bpb in [("q4_k", T.Q4_K, 144), ("q5_k", T.Q5_K, 176), ("q6_k", T.Q6_K, 210),
-                           ("iq2_xxs", T.IQ2_XXS, 66), ("q8_0", T.Q8_0, 272)]:
+                           ("iq2_xxs", T.IQ2_XXS, 66), ("q8_0", T.Q8_0, 272), ("iq3_xxs", T.IQ3_XXS, 98),
+                           ("iq4_xs", T.IQ4_XS, 136)]:
         w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
         a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
         fin = np.isfinite(b)
@@ -86,6 +88,13 @@ def test_iq2xxs_grid_matches_gguf():
     gq = pytest.importorskip("gguf.quants")
     gq.IQ2_XXS.init_grid()
     assert np.array_equal(O.iq2xxs_grid().astype(np.float32), np.asarray(gq.IQ2_XXS.grid).reshape(256, 8))
+
+
+def test_iq3xxs_grid_and_iq4nl_values_match_gguf():
+    gq = pytest.importorskip("gguf.quants")
+    gq.IQ3_XXS.init_grid()
+    assert np.array_equal(O.iq3xxs_grid().astype(np.float32), np.asarray(gq.IQ3_XXS.grid).reshape(256, 4))
+    assert O._table_values("KQ_IQ4NL_VALUES_INIT") == list(gq.IQ4_NL.kvalues)
 
 
 def test_router_topk_semantics():
