@@ -3,7 +3,9 @@
 The library is a plain C-ABI shared object (``include/kq_cuda.h``); Python
 loads it with ctypes (``gmlx_b200/_lib.py``).  The IQ2_XXS grid header is
 generated first from the installed gguf-py package (``csrc/gen_tables.py``).
-Objects are compiled in parallel and relinked only when a source changed.
+Objects are compiled in parallel and relinked only when a source changed;
+each flag set (normal / ``KQ_DEVELOPMENT``) keeps its own object directory, and
+the library is relinked whenever it was last linked from the other set.
 """
 from __future__ import annotations
 
@@ -14,14 +16,16 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
-BUILD = os.path.join(HERE, "_build")
+DEV = bool(os.environ.get("KQ_DEVELOPMENT"))
+BUILD = os.path.join(HERE, "_build", "dev" if DEV else "release")
+STAMP = os.path.join(HERE, "_build", "linked_config")
 LIB = os.path.join(HERE, "libkq_cuda.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 SOURCES = ["kq_dequant.cu", "kq_gemv.cu", "kq_moe.cu", "kq_capi.cu", "kq_noalloc.cu", "kq_gemm_sm100.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills"]
-if os.environ.get("KQ_DEVELOPMENT"):  # development switches (GEMV debug word, timestamps)
+if DEV:  # development switches (GEMV debug word, timestamps)
     FLAGS.append("-DKQ_DEVELOPMENT")
 
 
@@ -58,11 +62,16 @@ def build(verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), SOURCES))
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
+    config = " ".join(FLAGS)
+    linked = open(STAMP).read() if os.path.exists(STAMP) else None
+    if (not os.path.exists(LIB) or linked != config
+            or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs)):
         cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        with open(STAMP, "w") as f:
+            f.write(config)
     return LIB
 
 
