@@ -186,6 +186,9 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
         g.y_dtype = y_dtype;
         g.y_row_stride = ys;
         g.err = (int *)ws;
+#ifdef KQ_DEVELOPMENT
+        if (const char *gd = getenv("KQ_GEMM_DEBUG")) g.debug = atoi(gd);
+#endif
         cudaError_t ce = launch_gemm(g, (char *)ws + p.ys_off, (cudaStream_t)stream);
         if (ce == cudaSuccess && bias)
             ce = launch_add_bias(y, y_dtype, ys, m, n, bias, bias_dtype, (cudaStream_t)stream);

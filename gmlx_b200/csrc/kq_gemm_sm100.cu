@@ -11,11 +11,15 @@
 //               into a 4-stage ring, SWIZZLE_128B, no cluster multicast;
 //   warp 1      allocates 256 TMEM columns; one elected lane issues
 //               tcgen05.mma (kind::f16, f32 accumulate) and tcgen05.commit;
-//   warps 2-9   Q4_K: each thread owns one weight row, reads its raw 144-byte
+//   warps 2-9   Q4_K: each thread owns one weight row, takes its raw 144-byte
 //               blocks (16-byte header once per block, 32 bytes per stage) and
 //               writes the dequantized bf16/f16 row of the stage straight into
 //               the UMMA K-major SWIZZLE_128B layout; then the epilogue
-//               (tcgen05.ld 32x32b, convert, 16-byte stores).
+//               (tcgen05.ld 32x32b, convert, 16-byte stores);
+//   warp 10     Q4_K with contiguous weight rows: TMA of the raw bytes (the
+//               stage's 32-byte quant chunk of 256 rows, the 16-byte block
+//               headers once per block) into shared rings several stages
+//               ahead, so the dequantizing warps never wait on global loads.
 // Weights are rounded to the activation type before the MMA (the tolerance of
 // the matmul outputs covers it; the exact dequantization is kq_dequantize).
 #include <cuda.h>
@@ -30,20 +34,29 @@ namespace kq {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int GT = 320;  // threads
+constexpr int GT = 352;  // threads (11 warps)
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+
+// raw Q4_K rings of the TMA-fed mode: RS stages of 32-byte quant chunks and
+// HS blocks of 16-byte headers, 256 rows each
+constexpr int RS = 3, HS = 2, QS_BYTES = BN * 32, HDR_BYTES = BN * 16;
 
 // MT activation-row tiles of 128 per CTA (MT accumulators of 256 TMEM columns
 // each): with MT = 2 every dequantized weight tile feeds twice the MMA work.
-template <int MT> struct GL {
+template <int MT, bool RAW = false> struct GL {
     static constexpr int NSTAGE = MT == 1 ? 4 : 3;
     static constexpr int STAGE_A = MT * A_BYTES;
-    static constexpr int OFF_A = 0, OFF_B = NSTAGE * STAGE_A, OFF_BAR = OFF_B + NSTAGE * B_BYTES;
+    static constexpr int OFF_A = 0, OFF_B = NSTAGE * STAGE_A, OFF_RAW = OFF_B + NSTAGE * B_BYTES;
+    static constexpr int OFF_HDR = OFF_RAW + RS * QS_BYTES;
+    static constexpr int OFF_BAR = OFF_RAW + (RAW ? RS * QS_BYTES + HS * HDR_BYTES : 0);
     static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + 1 KB for base alignment
     static constexpr int TMEM_COLS = MT * BN;
+    static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-enum BMode : int { B_Q4K = 0, B_TMA = 1 };
+// B_Q4K: Q4_K dequantized from global loads; B_TMA: dequantized copy by TMA;
+// B_Q4KT: Q4_K dequantized from raw bytes brought in by TMA
+enum BMode : int { B_Q4K = 0, B_TMA = 1, B_Q4KT = 2 };
 
 __device__ __forceinline__ uint64_t gtimer() {
     uint64_t t;
@@ -146,8 +159,10 @@ template <bool F16> __device__ __forceinline__ uint32_t q4_pair(uint32_t nib2, u
 // epilogue writes act(g) * u for 128 output columns.
 template <bool F16, int BMODE, int MT, bool GLU>
 __global__ void __launch_bounds__(GT, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
-    using L = GL<MT>;
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmH,
+                const __grid_constant__ CUtensorMap tmQ2, const __grid_constant__ CUtensorMap tmH2, const GemmArgs a) {
+    using L = GL<MT, BMODE == B_Q4KT>;
     constexpr int NSTAGE = L::NSTAGE, OFF_A = L::OFF_A, OFF_B = L::OFF_B, OFF_BAR = L::OFF_BAR;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -155,7 +170,8 @@ __global__ void __launch_bounds__(GT, 1)
     uint64_t *fullB = fullA + NSTAGE;
     uint64_t *empty = fullB + NSTAGE;
     uint64_t *accbar = empty + NSTAGE;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accbar + 1);
+    uint64_t *rawFull = accbar + 1, *rawEmpty = rawFull + RS, *hdrFull = rawEmpty + RS, *hdrEmpty = hdrFull + HS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(hdrEmpty + HS);
     volatile int *s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -180,6 +196,14 @@ __global__ void __launch_bounds__(GT, 1)
             mbar_init(&empty[i], 1);
         }
         mbar_init(accbar, 1);
+        for (int i = 0; i < RS; i++) {
+            mbar_init(&rawFull[i], 1);
+            mbar_init(&rawEmpty[i], 8);
+        }
+        for (int i = 0; i < HS; i++) {
+            mbar_init(&hdrFull[i], 1);
+            mbar_init(&hdrEmpty[i], 8);
+        }
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -221,7 +245,7 @@ __global__ void __launch_bounds__(GT, 1)
             for (int s = 0; s < nk; s++) {
                 const int slot = s % NSTAGE, par = (s / NSTAGE) & 1;
                 wait_b(&fullA[slot], par, s_abort, a.err, 12);
-                if (BMODE == B_Q4K) wait_b(&fullB[slot], par, s_abort, a.err, 13);
+                if (BMODE != B_TMA) wait_b(&fullB[slot], par, s_abort, a.err, 13);
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + OFF_A + slot * L::STAGE_A);
                 const uint32_t sb = smem_u32(smem + OFF_B + slot * B_BYTES);
@@ -236,8 +260,95 @@ __global__ void __launch_bounds__(GT, 1)
             }
             umma_commit(accbar);
         }
+    } else if (warp == 10) {
+        if constexpr (BMODE == B_Q4KT) {
+            if (lane == 0) {  // raw Q4_K bytes: rows [rb, rb + 256) (GLU: 128 gate rows over 128 up rows)
+                const int rb = ex * a.n_per_expert + n0;
+                for (int s = 0; s < nk; s++) {
+                    const int r = s % RS, b = s >> 2, q = s & 3;
+                    if (q == 0) {
+                        const int h = b % HS;
+                        wait_b(&hdrEmpty[h], ((b / HS) & 1) ^ 1, s_abort, a.err, 16);
+                        mbar_arrive_expect_tx(&hdrFull[h], HDR_BYTES);
+                        if (!*s_abort) {
+                            uint8_t *dst = smem + L::OFF_HDR + h * HDR_BYTES;
+                            tma_load_2d(dst, &tmH, b * 144, rb, &hdrFull[h]);
+                            tma_load_2d(dst + HDR_BYTES / 2, GLU ? &tmH2 : &tmH, b * 144, GLU ? rb : rb + 128,
+                                        &hdrFull[h]);
+                        }
+                    }
+                    wait_b(&rawEmpty[r], ((s / RS) & 1) ^ 1, s_abort, a.err, 17);
+                    mbar_arrive_expect_tx(&rawFull[r], QS_BYTES);
+                    if (!*s_abort) {
+                        uint8_t *dst = smem + L::OFF_RAW + r * QS_BYTES;
+                        tma_load_2d(dst, &tmQ, b * 144 + 16 + 32 * q, rb, &rawFull[r]);
+                        tma_load_2d(dst + QS_BYTES / 2, GLU ? &tmQ2 : &tmQ, b * 144 + 16 + 32 * q, GLU ? rb : rb + 128,
+                                    &rawFull[r]);
+                    }
+                }
+            }
+        }
     } else {
         const int i = threadIdx.x - 64;  // 0..255: weight row of the tile
+        if constexpr (BMODE == B_Q4KT) {
+            uint32_t dsc2[8], ndm2[8];
+            for (int s0 = 0; s0 < nk; s0 += 4)  // nk is a multiple of 4 (K % 256 == 0)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {  // static q: dsc2[] / ndm2[] stay in registers
+                const int s = s0 + q, slot = s % NSTAGE, r = s % RS;
+                if (q == 0) {  // new super-block: 8 x (d*sc, -dmin*m) as packed 16-bit pairs
+                    const int b = s >> 2, h = b % HS;
+                    wait_b(&hdrFull[h], (b / HS) & 1, s_abort, a.err, 18);
+                    const uint4 hv = *reinterpret_cast<const uint4 *>(smem + L::OFF_HDR + h * HDR_BYTES + i * 16);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&hdrEmpty[h]);
+                    const float d = half_bits_to_float(hv.x & 0xffffu), dmin = half_bits_to_float(hv.x >> 16);
+                    uint32_t sc03, sc47, m03, m47;
+                    q4k_unpack_scales(hv.y, hv.z, hv.w, sc03, sc47, m03, m47);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float ds = d * (float)((((j < 4) ? sc03 : sc47) >> (8 * (j & 3))) & 63u);
+                        const float dm = dmin * (float)((((j < 4) ? m03 : m47) >> (8 * (j & 3))) & 63u);
+                        dsc2[j] = pack2<F16>(ds, ds);
+                        ndm2[j] = pack2<F16>(-dm, -dm);
+                    }
+                }
+                wait_b(&rawFull[r], (s / RS) & 1, s_abort, a.err, 19);
+                const uint8_t *src = smem + L::OFF_RAW + r * QS_BYTES + i * 32;
+                const uint4 c0 = *reinterpret_cast<const uint4 *>(src), c1 = *reinterpret_cast<const uint4 *>(src + 16);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rawEmpty[r]);
+                const uint32_t wds[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                wait_b(&empty[slot], ((s / NSTAGE) & 1) ^ 1, s_abort, a.err, 14);
+                uint8_t *dst = smem + OFF_B + slot * B_BYTES + (i >> 3) * 1024 + (i & 7) * 128;
+                const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
+#ifdef KQ_DEVELOPMENT
+                if (a.debug & 4) {  // development: no stores
+                } else if (a.debug & 1) {  // development: store without decoding
+#pragma unroll
+                    for (int c = 0; c < 8; c++)
+                        *reinterpret_cast<uint4 *>(dst + ((c ^ (i & 7)) << 4)) = make_uint4(wds[c], wds[c], 0, 0);
+                } else
+#endif
+#pragma unroll
+                for (int c = 0; c < 8; c++) {  // 16-byte chunk c = k 8c..8c+7 of the stage
+                    const int hh = c >> 2, j = 2 * q + hh;
+                    const uint32_t w0 = wds[2 * (c & 3)] >> (4 * hh), w1 = wds[2 * (c & 3) + 1] >> (4 * hh);
+                    uint4 o;
+                    o.x = q4_pair<F16>(lop_and_or(prmt(w0, 0, 0x4140), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    o.y = q4_pair<F16>(lop_and_or(prmt(w0, 0, 0x4342), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    o.z = q4_pair<F16>(lop_and_or(prmt(w1, 0, 0x4140), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    o.w = q4_pair<F16>(lop_and_or(prmt(w1, 0, 0x4342), 0x000f000fu, magic), dsc2[j], ndm2[j]);
+                    *reinterpret_cast<uint4 *>(dst + ((c ^ (i & 7)) << 4)) = o;
+                }
+#ifdef KQ_DEVELOPMENT
+                if (!(a.debug & 2))  // development: no proxy fence
+#endif
+                    fence_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&fullB[slot]);
+            }
+        }
         if constexpr (BMODE == B_Q4K) {
             const int n = n0 + (GLU ? (i & 127) : i);
             const bool valid = n < a.N;
@@ -402,16 +513,52 @@ bool make_map(CUtensorMap *m, const void *base, bool f16, int64_t rows, int64_t 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Raw Q4_K weight bytes as 2-D uint8 tensors [rows, row bytes] (row stride a
+// multiple of 16, base 16-byte aligned): boxes of 32 (quant chunk) and 16
+// (block header) bytes x 128 rows; rows past the end read as zeros.
+bool make_raw_map(CUtensorMap *m, const void *base, int64_t rows, int64_t row_bytes, int64_t row_stride, int box_bytes) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || ((uintptr_t)base & 15) || (row_stride & 15)) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_stride};
+    const cuuint32_t box[2] = {(cuuint32_t)box_bytes, 128u};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// the four raw maps (gate/plain quant + header, up quant + header) over `rows` weight rows
+bool make_raw_maps(const GemmArgs &a, int64_t rows, CUtensorMap *q, CUtensorMap *h, CUtensorMap *q2, CUtensorMap *h2) {
+    const int64_t rb = (int64_t)a.K / QK * 144;
+    if (!make_raw_map(q, a.w, rows, rb, a.w_row_stride, 32) || !make_raw_map(h, a.w, rows, rb, a.w_row_stride, 16))
+        return false;
+    if (!a.w2) {
+        *q2 = *q;
+        *h2 = *h;
+        return true;
+    }
+    return make_raw_map(q2, a.w2, rows, rb, a.w_row_stride, 32) && make_raw_map(h2, a.w2, rows, rb, a.w_row_stride, 16);
+}
+
+// TMA-fed Q4_K needs 16-byte aligned weight bases and row strides (Q4_K rows
+// are 144-byte multiples, so every contiguous Q4_K tensor qualifies) and, for
+// expert stacks, rows of all experts equally spaced
+static bool raw_tma_ok(const GemmArgs &a, bool contiguous_experts) {
+    if (dev_env("KQ_GEMM_NO_RAW_TMA")) return false;  // development switch
+    return contiguous_experts && !(((uintptr_t)a.w | (uintptr_t)(a.w2 ? a.w2 : a.w) | (uintptr_t)a.w_row_stride) & 15);
+}
+
 template <bool F16, int BMODE, int MT, bool GLU = false>
 cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st) {
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT, GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             GL<MT>::SMEM);
+                                             GL<MT, BMODE == B_Q4KT>::SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tq, th, tq2, th2;
     if (!make_map(&ta, a.x, F16, a.M, a.K, a.x_row_stride, BM)) return cudaErrorInvalidValue;
     if (BMODE == B_TMA) {
         if (!make_map(&tb, bdense, F16, (int64_t)a.N * (GLU ? 2 : 1), a.K, a.K, GLU ? BN / 2 : BN))
@@ -419,9 +566,14 @@ cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st
     } else {
         tb = ta;
     }
+    if (BMODE == B_Q4KT) {
+        if (!make_raw_maps(a, a.N, &tq, &th, &tq2, &th2)) return cudaErrorInvalidValue;
+    } else {
+        tq = th = tq2 = th2 = ta;
+    }
     constexpr int NOUT = GLU ? BN / 2 : BN;
     dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + NOUT - 1) / NOUT);
-    gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT>::SMEM, st>>>(ta, tb, a);
+    gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT, BMODE == B_Q4KT>::SMEM, st>>>(ta, tb, tq, th, tq2, th2, a);
     return cudaGetLastError();
 }
 
@@ -439,11 +591,11 @@ cudaError_t launch_grouped_t(const GemmArgs &a, int max_tiles, const void *bdens
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT, GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             GL<MT>::SMEM);
+                                             GL<MT, BMODE == B_Q4KT>::SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tq, th, tq2, th2;
     if (!make_map(&ta, a.x, F16, a.M, a.K, a.x_row_stride, BM)) return cudaErrorInvalidValue;
     if (BMODE == B_TMA) {
         const int64_t brows = (int64_t)(a.ex_hi - a.ex_lo) * a.n_per_expert * (GLU ? 2 : 1);
@@ -451,10 +603,15 @@ cudaError_t launch_grouped_t(const GemmArgs &a, int max_tiles, const void *bdens
     } else {
         tb = ta;
     }
+    if (BMODE == B_Q4KT) {  // expert stacks of contiguous rows: one [experts * N, row bytes] tensor
+        if (!make_raw_maps(a, (int64_t)a.ex_hi * a.n_per_expert, &tq, &th, &tq2, &th2)) return cudaErrorInvalidValue;
+    } else {
+        tq = th = tq2 = th2 = ta;
+    }
     if (max_tiles <= 0) return cudaSuccess;
     const int nout = GLU ? BN / 2 : BN;
     dim3 grid(max_tiles, (a.N + nout - 1) / nout);
-    gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT>::SMEM, st>>>(ta, tb, a);
+    gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT, BMODE == B_Q4KT>::SMEM, st>>>(ta, tb, tq, th, tq2, th2, a);
     return cudaGetLastError();
 }
 
@@ -559,6 +716,9 @@ __global__ void scatter_rows_kernel(const int32_t *__restrict__ idx, const int *
 
 cudaError_t launch_gemm_grouped(const GemmArgs &a, int mt, int max_tiles, const void *b_dense, cudaStream_t st) {
     const bool f16 = a.x_dtype == F16;
+    if (!b_dense && raw_tma_ok(a, a.w_expert_stride == (int64_t)a.n_per_expert * a.w_row_stride))
+        return f16 ? launch_grouped_glu<true, B_Q4KT>(a, mt, max_tiles, nullptr, st)
+                   : launch_grouped_glu<false, B_Q4KT>(a, mt, max_tiles, nullptr, st);
     if (!b_dense)
         return f16 ? launch_grouped_glu<true, B_Q4K>(a, mt, max_tiles, nullptr, st)
                    : launch_grouped_glu<false, B_Q4K>(a, mt, max_tiles, nullptr, st);
@@ -593,10 +753,12 @@ bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int
 }
 
 // Q4_K is dequantized inside the GEMM up to this many activation rows; above
-// it, one dequantized copy plus B by TMA is faster (the copy costs ~N*K*2
-// bytes of traffic once, while the in-kernel dequantization is repeated for
-// every 256-row tile and caps the tensor pipe near 64 % of peak)
-constexpr int64_t Q4K_FUSED_MAX_M = 4096;
+// it, one dequantized copy plus B by TMA is faster.  The copy costs ~N*K*2.6
+// bytes of traffic once; the in-kernel path repeats the dequantization for
+// every row tile and holds the tensor pipe near 45 % busy.  Measured on the
+// Llama-3-8B layer shapes: fused wins at M = 512, the copy from M = 1024 on
+// (layer 593 vs 646 us at M = 1024, 950 vs 1094 us at M = 2048).
+constexpr int64_t Q4K_FUSED_MAX_M = 768;
 
 static bool fused_q4k(int codec, int64_t m) {
     const char *e = dev_env("KQ_Q4K_FUSED_MAX_M");
@@ -614,6 +776,9 @@ cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
         a.ex_lo = 0;
         a.ex_hi = 1;
         a.n_per_expert = a.N;
+        if (fused_q4k(a.codec, a.M) && raw_tma_ok(a, true))
+            return f16 ? launch_gemm_mt<true, B_Q4KT, true>(a, nullptr, st)
+                       : launch_gemm_mt<false, B_Q4KT, true>(a, nullptr, st);
         if (fused_q4k(a.codec, a.M))
             return f16 ? launch_gemm_mt<true, B_Q4K, true>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K, true>(a, nullptr, st);
         cudaError_t e = launch_dequantize(a.codec, a.w, a.N, a.K, a.w_row_stride, scratch, a.x_dtype, st);
@@ -624,6 +789,8 @@ cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
         return f16 ? launch_gemm_mt<true, B_TMA, true>(a, scratch, st) : launch_gemm_mt<false, B_TMA, true>(a, scratch, st);
     }
     const GemmArgs &a = a0;
+    if (fused_q4k(a.codec, a.M) && raw_tma_ok(a, true))
+        return f16 ? launch_gemm_mt<true, B_Q4KT>(a, nullptr, st) : launch_gemm_mt<false, B_Q4KT>(a, nullptr, st);
     if (fused_q4k(a.codec, a.M))
         return f16 ? launch_gemm_mt<true, B_Q4K>(a, nullptr, st) : launch_gemm_mt<false, B_Q4K>(a, nullptr, st);
     // other codecs and large batches: dequantize once into scratch (activation dtype), then B by TMA

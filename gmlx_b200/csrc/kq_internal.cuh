@@ -105,6 +105,7 @@ struct GemmArgs {
     // mixed output (grouped MoE down projection): y is f32 and sorted row r
     // adds row_scale[r] * (its output row) into y row out_row[r] atomically
     const float *row_scale;
+    int debug;  // development builds only (KQ_GEMM_DEBUG); 0 otherwise
 };
 bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride);
 size_t gemm_scratch_bytes(int codec, int64_t m, int64_t n, int64_t k, bool glu);

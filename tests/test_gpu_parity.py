@@ -314,7 +314,7 @@ def test_prefill_gemm_tcgen05(cuda, codec, m, n, k):
 def test_prefill_glu_tcgen05(cuda, codec, act, m):
     """Prefill-sized fused GLU: one tcgen05 GEMM with gate and up accumulators
     side by side (128 output columns per tile; N=320 leaves a ragged tile).
-    M=4200: Q4_K switches from in-kernel dequantization to the dequantized copy."""
+    M=4200: Q4_K above 768 rows goes through the dequantized copy."""
     from math import erf
     n, k = 320, 1024
     wg = synth.random_weight(codec, n, k, seed=24)
