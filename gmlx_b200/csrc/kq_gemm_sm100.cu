@@ -173,11 +173,15 @@ __global__ void __launch_bounds__(GT, 1)
     uint64_t *rawFull = accbar + 1, *rawEmpty = rawFull + RS, *hdrFull = rawEmpty + RS, *hdrEmpty = hdrFull + HS;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(hdrEmpty + HS);
     volatile int *s_abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile int *s_last = reinterpret_cast<volatile int *>(tmem_slot + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int NOUT = GLU ? BN / 2 : BN;  // output columns per CTA
     const int n0 = blockIdx.y * NOUT;
     const int nk = a.K / BK;
+    // split-K (dense plain GEMM only): this CTA covers stages [ks0, ks0 + nkl)
+    const int nsplit = (a.ksplit > 1 && !a.n_tiles && !GLU) ? a.ksplit : 1;
+    const int nkl = nk / nsplit, ks0 = (int)blockIdx.z * nkl;
     int m0 = blockIdx.x * BM * MT, mend = a.M, ex = 0;
     if (a.n_tiles) {  // grouped: this CTA's (expert, row range) from the device tile table
         if ((int)blockIdx.x >= *a.n_tiles) return;
@@ -220,21 +224,21 @@ __global__ void __launch_bounds__(GT, 1)
     if (warp == 0) {
         if (lane == 0) {
             const uint32_t tx = mt_live * A_BYTES + (BMODE == B_TMA ? B_BYTES : 0);
-            for (int s = 0; s < nk; s++) {
-                const int slot = s % NSTAGE;
+            for (int s = 0; s < nkl; s++) {
+                const int slot = s % NSTAGE, kx = (ks0 + s) * BK;
                 wait_b(&empty[slot], ((s / NSTAGE) & 1) ^ 1, s_abort, a.err, 11);
                 mbar_arrive_expect_tx(&fullA[slot], tx);
                 if (*s_abort) continue;
 #pragma unroll
                 for (int t = 0; t < MT; t++)
                     if (t < mt_live)
-                        tma_load_2d(smem + OFF_A + slot * L::STAGE_A + t * A_BYTES, &tmA, s * BK, m0 + t * BM,
+                        tma_load_2d(smem + OFF_A + slot * L::STAGE_A + t * A_BYTES, &tmA, kx, m0 + t * BM,
                                     &fullA[slot]);
                 if (BMODE == B_TMA) {
                     const int rb = (ex - a.ex_lo) * a.n_per_expert + n0;
-                    tma_load_2d(smem + OFF_B + slot * B_BYTES, &tmB, s * BK, rb, &fullA[slot]);
+                    tma_load_2d(smem + OFF_B + slot * B_BYTES, &tmB, kx, rb, &fullA[slot]);
                     if (GLU)  // up rows: second half of the dequantized scratch
-                        tma_load_2d(smem + OFF_B + slot * B_BYTES + B_BYTES / 2, &tmB, s * BK,
+                        tma_load_2d(smem + OFF_B + slot * B_BYTES + B_BYTES / 2, &tmB, kx,
                                     rb + (a.ex_hi - a.ex_lo) * a.n_per_expert, &fullA[slot]);
                 }
             }
@@ -242,7 +246,7 @@ __global__ void __launch_bounds__(GT, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t id = idesc<F16>();
-            for (int s = 0; s < nk; s++) {
+            for (int s = 0; s < nkl; s++) {
                 const int slot = s % NSTAGE, par = (s / NSTAGE) & 1;
                 wait_b(&fullA[slot], par, s_abort, a.err, 12);
                 if (BMODE != B_TMA) wait_b(&fullB[slot], par, s_abort, a.err, 13);
@@ -264,11 +268,11 @@ __global__ void __launch_bounds__(GT, 1)
         if constexpr (BMODE == B_Q4KT) {
             if (lane == 0) {  // raw Q4_K bytes: rows [rb, rb + 256) (GLU: 128 gate rows over 128 up rows)
                 const int rb = ex * a.n_per_expert + n0;
-                for (int s = 0; s < nk; s++) {
-                    const int r = s % RS, b = s >> 2, q = s & 3;
+                for (int s = 0; s < nkl; s++) {
+                    const int r = s % RS, b = (ks0 + s) >> 2, q = s & 3, bl = s >> 2;  // ks0 % 4 == 0
                     if (q == 0) {
-                        const int h = b % HS;
-                        wait_b(&hdrEmpty[h], ((b / HS) & 1) ^ 1, s_abort, a.err, 16);
+                        const int h = bl % HS;
+                        wait_b(&hdrEmpty[h], ((bl / HS) & 1) ^ 1, s_abort, a.err, 16);
                         mbar_arrive_expect_tx(&hdrFull[h], HDR_BYTES);
                         if (!*s_abort) {
                             uint8_t *dst = smem + L::OFF_HDR + h * HDR_BYTES;
@@ -292,7 +296,7 @@ __global__ void __launch_bounds__(GT, 1)
         const int i = threadIdx.x - 64;  // 0..255: weight row of the tile
         if constexpr (BMODE == B_Q4KT) {
             uint32_t dsc2[8], ndm2[8];
-            for (int s0 = 0; s0 < nk; s0 += 4)  // nk is a multiple of 4 (K % 256 == 0)
+            for (int s0 = 0; s0 < nkl; s0 += 4)  // nkl is a multiple of 4 (K % 256 == 0)
 #pragma unroll
             for (int q = 0; q < 4; q++) {  // static q: dsc2[] / ndm2[] stay in registers
                 const int s = s0 + q, slot = s % NSTAGE, r = s % RS;
@@ -353,18 +357,19 @@ __global__ void __launch_bounds__(GT, 1)
             const int n = n0 + (GLU ? (i & 127) : i);
             const bool valid = n < a.N;
             const uint8_t *wb = (GLU && i >= 128) ? a.w2 : a.w;
-            const uint8_t *row = wb + (int64_t)ex * a.w_expert_stride + (int64_t)(valid ? n : 0) * a.w_row_stride;
+            const uint8_t *row = wb + (int64_t)ex * a.w_expert_stride + (int64_t)(valid ? n : 0) * a.w_row_stride +
+                                 (int64_t)(ks0 >> 2) * 144;
             uint32_t dsc2[8], ndm2[8];
             // loads run one stage ahead of the decode (header of the next block, next chunk)
             uint4 nh = __ldg(reinterpret_cast<const uint4 *>(row));
             uint4 n0c = __ldg(reinterpret_cast<const uint4 *>(row + 16));
             uint4 n1c = __ldg(reinterpret_cast<const uint4 *>(row + 32));
-            for (int s0 = 0; s0 < nk; s0 += 4)  // nk is a multiple of 4 (K % 256 == 0)
+            for (int s0 = 0; s0 < nkl; s0 += 4)  // nkl is a multiple of 4 (K % 256 == 0)
 #pragma unroll
             for (int q = 0; q < 4; q++) {  // static q: dsc2[] / ndm2[] stay in registers
                 const int s = s0 + q, slot = s % NSTAGE;
                 const uint4 hcur = nh, c0 = n0c, c1 = n1c;
-                if (s + 1 < nk) {
+                if (s + 1 < nkl) {
                     const int b1 = (s + 1) >> 2, q1 = (s + 1) & 3;
                     if (q1 == 0) nh = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b1 * 144));
                     n0c = __ldg(reinterpret_cast<const uint4 *>(row + (int64_t)b1 * 144 + 16 + 32 * q1));
@@ -408,8 +413,46 @@ __global__ void __launch_bounds__(GT, 1)
         wait_b(accbar, 0, s_abort, a.err, 15);
         tc_fence_after();
         const int quarter = warp & 3, chalf = (warp - 2) >> 2;
+        if (nsplit > 1) {
+            // split-K: post this split's f32 partial tile; the last split of the
+            // tile to finish adds the other one (a + b == b + a: deterministic)
+            float *mine = a.part + (int64_t)blockIdx.z * a.M * a.N;
 #pragma unroll 1
-        for (int q32 = 0; q32 < mt_live * (NOUT / 2); q32 += 32) {
+            for (int q32 = 0; q32 < mt_live * (NOUT / 2); q32 += 32) {
+                const int t = q32 / (NOUT / 2), cc = q32 % (NOUT / 2);
+                const int tok = m0 + t * BM + quarter * 32 + lane;
+                const int col = chalf * (NOUT / 2) + cc;
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * BN + col), r);
+                if (tok >= mend || *s_abort) continue;
+                const int nb = n0 + col;
+                float *pp = mine + (int64_t)tok * a.N + nb;
+                if (nb + 32 <= a.N && ((uintptr_t)pp & 15) == 0) {
+#pragma unroll
+                    for (int v = 0; v < 8; v++)
+                        reinterpret_cast<float4 *>(pp)[v] =
+                            make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                        __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                } else {
+#pragma unroll
+                    for (int v = 0; v < 32; v++)
+                        if (nb + v < a.N) pp[v] = __uint_as_float(r[v]);
+                }
+            }
+            named_bar_sync(1, 256);
+            if (threadIdx.x == 64) {
+                __threadfence();
+                int *cnt = a.tile_cnt + blockIdx.y * gridDim.x + blockIdx.x;
+                const int last = atomicAdd(cnt, 1) == nsplit - 1;
+                if (last) *cnt = 0;  // counters are left zero
+                *s_last = last;
+            }
+            named_bar_sync(1, 256);
+            __threadfence();
+        }
+        const float *other = nsplit > 1 ? a.part + (int64_t)(1 - (int)blockIdx.z) * a.M * a.N : nullptr;
+#pragma unroll 1
+        for (int q32 = 0; q32 < ((nsplit == 1 || *s_last) ? mt_live * (NOUT / 2) : 0); q32 += 32) {
             const int t = q32 / (NOUT / 2), cc = q32 % (NOUT / 2);
             const int tok = m0 + t * BM + quarter * 32 + lane;
             const int col = chalf * (NOUT / 2) + cc;
@@ -425,6 +468,12 @@ __global__ void __launch_bounds__(GT, 1)
             if (tok >= mend || *s_abort) continue;
             const int64_t orow = a.out_row ? (int64_t)a.out_row[tok] : (int64_t)tok;
             const int nb = n0 + col;
+            if (other) {  // split-K: add the other split's partial
+                const float *op = other + (int64_t)tok * a.N + nb;
+#pragma unroll
+                for (int v = 0; v < 32; v++)
+                    if (nb + v < a.N) r[v] = __float_as_uint(__uint_as_float(r[v]) + __ldcg(op + v));
+            }
             if (a.row_scale) {  // y[out_row] += scale * row (f32; several rows add into one output row)
                 const float sc = a.row_scale[tok];
                 float *yp = reinterpret_cast<float *>(a.y) + orow * a.y_row_stride + nb;
@@ -572,7 +621,7 @@ cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st
         tq = th = tq2 = th2 = ta;
     }
     constexpr int NOUT = GLU ? BN / 2 : BN;
-    dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + NOUT - 1) / NOUT);
+    dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + NOUT - 1) / NOUT, (!GLU && a.ksplit > 1) ? a.ksplit : 1);
     gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT, BMODE == B_Q4KT>::SMEM, st>>>(ta, tb, tq, th, tq2, th2, a);
     return cudaGetLastError();
 }
@@ -582,7 +631,7 @@ cudaError_t launch_gemm_mt(const GemmArgs &a, const void *bdense, cudaStream_t s
     // two activation-row tiles per CTA once there are enough CTAs to fill the GPU
     constexpr int NOUT = GLU ? BN / 2 : BN;
     const long ctas2 = (long)((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + NOUT - 1) / NOUT);
-    if (ctas2 >= num_sms()) return launch_gemm_t<F16, BMODE, 2, GLU>(a, bdense, st);
+    if (ctas2 >= num_sms() && (GLU || a.ksplit <= 1)) return launch_gemm_t<F16, BMODE, 2, GLU>(a, bdense, st);
     return launch_gemm_t<F16, BMODE, 1, GLU>(a, bdense, st);
 }
 
@@ -765,8 +814,26 @@ static bool fused_q4k(int codec, int64_t m) {
     return codec == Q4_K && m <= (e ? atol(e) : Q4K_FUSED_MAX_M);
 }
 
+// Plain dense GEMMs on the dequantized-copy path that would fill at most half
+// of the SMs with 128-row tiles split K in two (K % 512 == 0 keeps each half a
+// whole number of super-blocks).  The in-kernel Q4_K path does not split: with
+// half of K per CTA its per-tile dequantization overheads cost more than the
+// idle SMs (M = 512 o projection: 43 -> 52 us).
+int gemm_ksplit(int codec, int64_t m, int64_t n, int64_t k, bool glu) {
+    if (glu || k % 512 || fused_q4k(codec, m) || dev_env("KQ_GEMM_NO_SPLIT")) return 1;
+    const int64_t nt = (n + BN - 1) / BN;
+    if (((m + 2 * BM - 1) / (2 * BM)) * nt >= num_sms()) return 1;  // two row tiles per CTA fill the GPU
+    return ((m + BM - 1) / BM) * nt * 2 <= num_sms() ? 2 : 1;
+}
+
+static size_t deq_scratch_bytes(int codec, int64_t m, int64_t n, int64_t k, bool glu) {
+    return fused_q4k(codec, m) ? 0 : ((size_t)n * k * 2 * (glu ? 2 : 1) + 255) & ~(size_t)255;
+}
+
 size_t gemm_scratch_bytes(int codec, int64_t m, int64_t n, int64_t k, bool glu) {
-    return fused_q4k(codec, m) ? 0 : (size_t)n * k * 2 * (glu ? 2 : 1);  // dequantized copy for the B-by-TMA path
+    // dequantized copy for the B-by-TMA path, then the split-K partial tiles
+    const int ks = gemm_ksplit(codec, m, n, k, glu);
+    return deq_scratch_bytes(codec, m, n, k, glu) + (ks > 1 ? (size_t)ks * m * n * sizeof(float) : 0);
 }
 
 cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
@@ -788,7 +855,10 @@ cudaError_t launch_gemm(const GemmArgs &a0, void *scratch, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         return f16 ? launch_gemm_mt<true, B_TMA, true>(a, scratch, st) : launch_gemm_mt<false, B_TMA, true>(a, scratch, st);
     }
-    const GemmArgs &a = a0;
+    GemmArgs a = a0;
+    a.ksplit = gemm_ksplit(a.codec, a.M, a.N, a.K, false);
+    a.part = reinterpret_cast<float *>((char *)scratch + deq_scratch_bytes(a.codec, a.M, a.N, a.K, false));
+    a.tile_cnt = reinterpret_cast<int *>(reinterpret_cast<char *>(a.err) + 256);  // workspace counter region
     if (fused_q4k(a.codec, a.M) && raw_tma_ok(a, true))
         return f16 ? launch_gemm_mt<true, B_Q4KT>(a, nullptr, st) : launch_gemm_mt<false, B_Q4KT>(a, nullptr, st);
     if (fused_q4k(a.codec, a.M))

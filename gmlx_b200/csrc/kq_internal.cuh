@@ -105,8 +105,16 @@ struct GemmArgs {
     // mixed output (grouped MoE down projection): y is f32 and sorted row r
     // adds row_scale[r] * (its output row) into y row out_row[r] atomically
     const float *row_scale;
+    // dense, non-GLU split-K (gridDim.z = ksplit = 2): each split writes its f32
+    // partial tile to part[z][M][N]; the last of a tile's splits (counter in
+    // tile_cnt, zero on entry and left zero) adds the other one and stores y
+    int ksplit;
+    float *part;
+    int *tile_cnt;
     int debug;  // development builds only (KQ_GEMM_DEBUG); 0 otherwise
 };
+// split-K factor the dense GEMM uses for this shape (1 or 2)
+int gemm_ksplit(int codec, int64_t m, int64_t n, int64_t k, bool glu);
 bool gemm_supported(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride);
 size_t gemm_scratch_bytes(int codec, int64_t m, int64_t n, int64_t k, bool glu);
 cudaError_t launch_gemm(const GemmArgs &a, void *scratch, cudaStream_t st);

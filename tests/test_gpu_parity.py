@@ -615,3 +615,22 @@ def test_grouped_moe_layer_two_row_tiles(cuda, out_dtype):
             ref[sel] += sc[sel, j, None] * O.matmul(hb, wd[ex], "q6_k")
     assert rel_err(y.cpu().numpy(), ref) <= TOL
     assert kq.workspace_error() == 0
+
+
+@pytest.mark.parametrize("codec", CODECS)
+@pytest.mark.parametrize("m", [300, 1000])
+def test_gemm_split_k_deterministic(cuda, codec, m):
+    """Plain GEMMs on the dequantized-copy path (every codec but Q4_K at this M)
+    that fill at most half of the SMs split K in two: each half
+    posts an f32 partial tile and the last one adds the other.  Ragged M and N,
+    bit-identical across calls, and every tile counter is left zero (the
+    workspace is reused)."""
+    n, k = 320, 2048
+    w = synth.random_weight(codec, n, k, seed=130)
+    x = synth.random_activations(m, k, seed=131)
+    ref = O.matmul(x, w, codec)
+    wd, xd = torch.from_numpy(w).to(cuda), to_dev_x(x, cuda)
+    ys = [kq.quantized_matmul(xd, wd, None, codec, out_dtype=torch.float32) for _ in range(3)]
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+    assert rel_err(ys[0].cpu().numpy(), ref) <= TOL
+    assert kq.workspace_error() == 0
