@@ -157,7 +157,7 @@ template <bool F16> __device__ __forceinline__ uint32_t q4_pair(uint32_t nib2, u
 // GLU: the 256-row weight tile is 128 gate rows over 128 up rows of the same
 // output columns; accumulator columns [0,128) hold x.Wg, [128,256) x.Wu and the
 // epilogue writes act(g) * u for 128 output columns.
-template <bool F16, int BMODE, int MT, bool GLU>
+template <bool F16, int BMODE, int MT, bool GLU, bool SPLIT = false>
 __global__ void __launch_bounds__(GT, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmH,
@@ -179,9 +179,11 @@ __global__ void __launch_bounds__(GT, 1)
     constexpr int NOUT = GLU ? BN / 2 : BN;  // output columns per CTA
     const int n0 = blockIdx.y * NOUT;
     const int nk = a.K / BK;
-    // split-K (dense plain GEMM only): this CTA covers stages [ks0, ks0 + nkl)
-    const int nsplit = (a.ksplit > 1 && !a.n_tiles && !GLU) ? a.ksplit : 1;
-    const int nkl = nk / nsplit, ks0 = (int)blockIdx.z * nkl;
+    // split-K (dense plain GEMM only, its own instantiation so the other
+    // kernels compile without it): this CTA covers stages [ks0, ks0 + nkl)
+    static_assert(!SPLIT || !GLU, "split-K is for plain GEMMs");
+    const int nsplit = SPLIT ? 2 : 1;
+    const int nkl = SPLIT ? nk / 2 : nk, ks0 = SPLIT ? (int)blockIdx.z * nkl : 0;
     int m0 = blockIdx.x * BM * MT, mend = a.M, ex = 0;
     if (a.n_tiles) {  // grouped: this CTA's (expert, row range) from the device tile table
         if ((int)blockIdx.x >= *a.n_tiles) return;
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(GT, 1)
         wait_b(accbar, 0, s_abort, a.err, 15);
         tc_fence_after();
         const int quarter = warp & 3, chalf = (warp - 2) >> 2;
-        if (nsplit > 1) {
+        if constexpr (SPLIT) {
             // split-K: post this split's f32 partial tile; the last split of the
             // tile to finish adds the other one (a + b == b + a: deterministic)
             float *mine = a.part + (int64_t)blockIdx.z * a.M * a.N;
@@ -449,10 +451,45 @@ __global__ void __launch_bounds__(GT, 1)
             }
             named_bar_sync(1, 256);
             __threadfence();
-        }
-        const float *other = nsplit > 1 ? a.part + (int64_t)(1 - (int)blockIdx.z) * a.M * a.N : nullptr;
+            const float *other = a.part + (int64_t)(1 - (int)blockIdx.z) * a.M * a.N;
 #pragma unroll 1
-        for (int q32 = 0; q32 < ((nsplit == 1 || *s_last) ? mt_live * (NOUT / 2) : 0); q32 += 32) {
+            for (int q32 = 0; q32 < (*s_last ? mt_live * (NOUT / 2) : 0); q32 += 32) {
+                const int t = q32 / (NOUT / 2), cc = q32 % (NOUT / 2);
+                const int tok = m0 + t * BM + quarter * 32 + lane;
+                const int col = chalf * (NOUT / 2) + cc;
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * BN + col), r);
+                if (tok >= mend || *s_abort) continue;
+                const int nb = n0 + col;
+                const float *op = other + (int64_t)tok * a.N + nb;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) + (nb + j < a.N ? __ldcg(op + j) : 0.f);
+                if (a.y_dtype == F32) {
+                    float *yp = reinterpret_cast<float *>(a.y) + (int64_t)tok * a.y_row_stride + nb;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (nb + j < a.N) yp[j] = v[j];
+                } else {
+                    const bool of16 = a.y_dtype == F16;
+                    uint16_t *yp = reinterpret_cast<uint16_t *>(a.y) + (int64_t)tok * a.y_row_stride + nb;
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) pk[j] = of16 ? pack2<true>(v[2 * j], v[2 * j + 1]) : pack2<false>(v[2 * j], v[2 * j + 1]);
+                    if (nb + 32 <= a.N && ((uintptr_t)yp & 15) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            reinterpret_cast<uint4 *>(yp)[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (nb + j < a.N) yp[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
+                    }
+                }
+            }
+        }
+#pragma unroll 1
+        for (int q32 = 0; q32 < (SPLIT ? 0 : mt_live * (NOUT / 2)); q32 += 32) {
             const int t = q32 / (NOUT / 2), cc = q32 % (NOUT / 2);
             const int tok = m0 + t * BM + quarter * 32 + lane;
             const int col = chalf * (NOUT / 2) + cc;
@@ -468,12 +505,6 @@ __global__ void __launch_bounds__(GT, 1)
             if (tok >= mend || *s_abort) continue;
             const int64_t orow = a.out_row ? (int64_t)a.out_row[tok] : (int64_t)tok;
             const int nb = n0 + col;
-            if (other) {  // split-K: add the other split's partial
-                const float *op = other + (int64_t)tok * a.N + nb;
-#pragma unroll
-                for (int v = 0; v < 32; v++)
-                    if (nb + v < a.N) r[v] = __float_as_uint(__uint_as_float(r[v]) + __ldcg(op + v));
-            }
             if (a.row_scale) {  // y[out_row] += scale * row (f32; several rows add into one output row)
                 const float sc = a.row_scale[tok];
                 float *yp = reinterpret_cast<float *>(a.y) + orow * a.y_row_stride + nb;
@@ -598,11 +629,11 @@ static bool raw_tma_ok(const GemmArgs &a, bool contiguous_experts) {
     return contiguous_experts && !(((uintptr_t)a.w | (uintptr_t)(a.w2 ? a.w2 : a.w) | (uintptr_t)a.w_row_stride) & 15);
 }
 
-template <bool F16, int BMODE, int MT, bool GLU = false>
+template <bool F16, int BMODE, int MT, bool GLU = false, bool SPLIT = false>
 cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT, GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, BMODE, MT, GLU, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              GL<MT, BMODE == B_Q4KT>::SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
@@ -621,8 +652,8 @@ cudaError_t launch_gemm_t(const GemmArgs &a, const void *bdense, cudaStream_t st
         tq = th = tq2 = th2 = ta;
     }
     constexpr int NOUT = GLU ? BN / 2 : BN;
-    dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + NOUT - 1) / NOUT, (!GLU && a.ksplit > 1) ? a.ksplit : 1);
-    gemm_kernel<F16, BMODE, MT, GLU><<<grid, GT, GL<MT, BMODE == B_Q4KT>::SMEM, st>>>(ta, tb, tq, th, tq2, th2, a);
+    dim3 grid((a.M + BM * MT - 1) / (BM * MT), (a.N + NOUT - 1) / NOUT, SPLIT ? 2 : 1);
+    gemm_kernel<F16, BMODE, MT, GLU, SPLIT><<<grid, GT, GL<MT, BMODE == B_Q4KT>::SMEM, st>>>(ta, tb, tq, th, tq2, th2, a);
     return cudaGetLastError();
 }
 
@@ -631,7 +662,9 @@ cudaError_t launch_gemm_mt(const GemmArgs &a, const void *bdense, cudaStream_t s
     // two activation-row tiles per CTA once there are enough CTAs to fill the GPU
     constexpr int NOUT = GLU ? BN / 2 : BN;
     const long ctas2 = (long)((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + NOUT - 1) / NOUT);
-    if (ctas2 >= num_sms() && (GLU || a.ksplit <= 1)) return launch_gemm_t<F16, BMODE, 2, GLU>(a, bdense, st);
+    if constexpr (!GLU && BMODE == B_TMA)  // split-K: the dequantized-copy path only
+        if (a.ksplit == 2) return launch_gemm_t<F16, BMODE, 1, false, true>(a, bdense, st);
+    if (ctas2 >= num_sms()) return launch_gemm_t<F16, BMODE, 2, GLU>(a, bdense, st);
     return launch_gemm_t<F16, BMODE, 1, GLU>(a, bdense, st);
 }
 
