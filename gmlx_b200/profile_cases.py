@@ -8,6 +8,9 @@ Each case builds seeded synthetic weights (the bench's shapes), runs the op
   down_m1       Q6_K 4096x14336 GEMV, one row
   iq2_m1        IQ2_XXS 2048x7168 GEMV, one row (DeepSeek-like expert)
   prefill_glu   fused gate/up tcgen05 GEMM, Q4_K 14336x4096 (x2), M=2048
+                (dequantized copy + B by TMA)
+  prefill_glu_m512  the same at M=512 (Q4_K dequantized inside the GEMM
+                from raw bytes brought in by TMA)
   prefill_down  Q6_K 4096x14336 GEMM, M=2048
   moe_prefill   Qwen3-like expert layer, T=512 (grouped GEMM path)
 """
@@ -36,6 +39,9 @@ def build(case):
     if case == "iq2_m1":
         w, x = _w("iq2_xxs", 2048, 7168, 4), _x(1, 7168)
         return lambda: kq.quantized_matmul(x, w, None, "iq2_xxs")
+    if case == "prefill_glu_m512":
+        g, u, x = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _x(512, 4096)
+        return lambda: kq.quantized_glu(x, g, u, "q4_k", act="silu")
     if case == "prefill_glu":
         g, u, x = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _x(2048, 4096)
         return lambda: kq.quantized_glu(x, g, u, "q4_k", act="silu")
