@@ -42,6 +42,16 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
 #pragma unroll
         for (int i = 0; i < 8; i++)
             o[i] = dl * (float)(((q[i] >> (4 * h)) & 15) | (((qh[i] >> j) & 1) << 4)) - ml;
+    } else if constexpr (C == Q4_0 || C == IQ4_NL) {  // lane: 8 weights of ggml block lane / 4
+        const uint8_t *blk = b + 18 * (lane >> 2);
+        const float d = half_bits_to_float(ld_u16(blk));
+        const int i0 = 8 * (lane & 3), h = i0 >> 4;
+        const uint8_t *q = blk + 2 + (i0 & 15);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int v = (q[i] >> (4 * h)) & 15;
+            o[i] = C == Q4_0 ? d * (float)(v - 8) : d * (float)c_iq4nl_values[v];
+        }
     } else if constexpr (C == Q8_0) {  // lane: 8 weights of ggml block lane / 4
         const uint8_t *blk = b + 34 * (lane >> 2);
         const float d = half_bits_to_float(ld_u16(blk));
@@ -270,6 +280,8 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case Q4_K: return launch_deq<Q4_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st);
+    case Q4_0: return launch_deq<Q4_0>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ4_NL: return launch_deq<IQ4_NL>(w, rows, nb, row_stride, out, dtype, st);
     case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st);
     case IQ3_XXS: return launch_deq<IQ3_XXS>(w, rows, nb, row_stride, out, dtype, st);
     case IQ4_XS: return launch_deq<IQ4_XS>(w, rows, nb, row_stride, out, dtype, st);

@@ -18,6 +18,9 @@
 //                w = d*(0.5+ls)*0.5 * grid * sign         quants.py:1005-1054
 //   IQ4_XS 136 B d f16 | u16 scales_h | 4 B scales_l | 128 B nibbles
 //                w = (d*(ls-32)) * kvalues[q]             quants.py:1351-1377
+//   Q4_0  8 x 18 B  (d f16 | 16 B nibbles), w = d*(q-8)  quants.py:241-251
+//   IQ4_NL 8 x 18 B (d f16 | 16 B nibbles), w = d*kvalues[q]  quants.py:1333-1348
+//         (32-weight blocks: nibble j < 16 low of byte j, else high of byte j-16)
 //
 // Exactness: every product above is exact in f32 (fp16 d has 11 significant
 // bits; d*sc <= 17 bits, d*sc*q <= 21 bits; Q6_K d*sc*(q-32) <= 24 bits;
@@ -34,7 +37,9 @@
 
 namespace kq {
 
-enum Codec : int { Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_XS = 23 };
+enum Codec : int {
+    Q4_0 = 2, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
+};
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
 constexpr int QK = 256;
@@ -45,6 +50,10 @@ template <> struct Fmt<Q5_K> { static constexpr int bpb = 176; static constexpr 
 // Q8_0: ggml blocks of 32 weights (fp16 d + 32 int8); eight of them (272 bytes)
 // are handled as one 256-weight group
 template <> struct Fmt<Q8_0> { static constexpr int bpb = 272; static constexpr int sub = 32; };
+// Q4_0 / IQ4_NL: ggml blocks of 32 weights (fp16 d + 16 nibble bytes); eight
+// of them (144 bytes) are handled as one 256-weight group
+template <> struct Fmt<Q4_0> { static constexpr int bpb = 144; static constexpr int sub = 32; };
+template <> struct Fmt<IQ4_NL> { static constexpr int bpb = 144; static constexpr int sub = 32; };
 template <> struct Fmt<Q6_K> { static constexpr int bpb = 210; static constexpr int sub = 16; };
 template <> struct Fmt<IQ2_XXS> { static constexpr int bpb = 66; static constexpr int sub = 32; };
 template <> struct Fmt<IQ3_XXS> { static constexpr int bpb = 98; static constexpr int sub = 32; };
@@ -52,7 +61,8 @@ template <> struct Fmt<IQ4_XS> { static constexpr int bpb = 136; static constexp
 
 __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
-         : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : -1;
+         : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
+         : -1;
 }
 
 // 256-entry IQ2_XXS grid, byte i of entry e = |w_i| in {8, 25, 43}.

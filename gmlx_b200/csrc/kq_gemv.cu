@@ -59,6 +59,8 @@ template <int C> struct GCfg;
 template <> struct GCfg<Q4_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // (dsc, -mt) x 2 rows
 template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
+template <> struct GCfg<Q4_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<IQ4_NL> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
 template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1; };    // dsc x 2 rows
 template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 2; };  // db x 2 rows
 template <> struct GCfg<IQ3_XXS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };  // lane-per-row path only
@@ -102,7 +104,10 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int REDB = DP ? CW * RED_TS * 4 : NCOL * 8 * NT * RED_TS * 4;
     static constexpr int FIXED = 512 + GRIDB<C> + TABS + SBYTES + 2 * REDB + DPB;
     static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<C, NT> - FIXED) / STAGE;
-    static constexpr int NS = NS_FIT > 8 ? 8 : (NS_FIT < 2 ? 2 : NS_FIT);  // ring depth (<= 8: rowoff table)
+    // ring depth (<= 8: rowoff table; <= 3 on the lane-per-row path, whose
+    // partial buffers rotate over NS + 1 <= 4 tiles)
+    static constexpr int NS_MAX = DP ? 3 : 8;
+    static constexpr int NS = NS_FIT > NS_MAX ? NS_MAX : (NS_FIT < 2 ? 2 : NS_FIT);
     static constexpr int OFF_BAR = 0;                              // 2*NS mbarriers
     static constexpr int OFF_ROWOFF = 128;                         // NS x 32 bytes
     static constexpr int OFF_MISC = OFF_ROWOFF + 32 * 8;           // flags
@@ -957,6 +962,66 @@ __device__ __forceinline__ float dp_iq4xs_dot(const IQ4Regs &r, const uint32_t *
     return acc;
 }
 
+// Lane-per-row Q4_0 / IQ4_NL: a lane takes a whole 144-byte group of eight
+// 18-byte ggml blocks (2-byte aligned), as Q4_K takes its 144-byte block, so
+// stage rows are 8 groups (1152 bytes) long.  Nibble j < 16 of a
+// block is the low half of byte j, j >= 16 the high half of byte j - 16.
+// Q4_0 dots the unsigned nibbles and applies its -8 as -8 * dx * sum(x_q);
+// IQ4_NL maps nibbles to the sixteen signed values first.
+struct Q40Regs {
+    uint32_t q[8][4];
+    float d[8];
+};
+
+__device__ __forceinline__ void dp_q40_load(const uint8_t *grp, Q40Regs &r) {
+#pragma unroll
+    for (int s = 0; s < 8; s++) {
+        const uint8_t *blk = grp + 18 * s;
+        r.d[s] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk));
+        const uintptr_t qb = (uintptr_t)(blk + 2);
+        const uint32_t *aw = reinterpret_cast<const uint32_t *>(qb & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(qb & 3) * 8;
+#pragma unroll
+        for (int i = 0; i < 4; i++) r.q[s][i] = lds_w2(aw, i, sh);
+    }
+}
+
+template <bool NL>
+__device__ __forceinline__ float dp_q40_dot(const Q40Regs &r, const uint32_t *xq, const float *xsc) {
+    uint32_t tv[4] = {0u, 0u, 0u, 0u};
+    if constexpr (NL) {
+        const uint32_t *tw = reinterpret_cast<const uint32_t *>(c_iq4nl_values);
+        tv[0] = tw[0], tv[1] = tw[1], tv[2] = tw[2], tv[3] = tw[3];
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < 8; s++) {
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t w = r.q[s][i];
+            int lo = (int)(w & 0x0f0f0f0fu), hi = (int)((w >> 4) & 0x0f0f0f0fu);
+            if constexpr (NL) {
+                lo = iq4_lookup4((uint32_t)lo, tv);
+                hi = iq4_lookup4((uint32_t)hi, tv);
+            }
+            const uint2 xl = *reinterpret_cast<const uint2 *>(xq + 16 * s + 2 * i);
+            const uint2 xh = *reinterpret_cast<const uint2 *>(xq + 16 * s + 8 + 2 * i);
+            sum = __dp2a_lo((int)xl.x, lo, sum);
+            sum = __dp2a_hi((int)xl.y, lo, sum);
+            sum = __dp2a_lo((int)xh.x, hi, sum);
+            sum = __dp2a_hi((int)xh.y, hi, sum);
+        }
+        const int g = s;  // 32-weight group of the 256
+        if constexpr (NL)
+            acc = fmaf(r.d[s] * xsc[g], (float)sum, acc);
+        else
+            acc = fmaf(r.d[s], fmaf(xsc[g], (float)sum, -8.f * xsc[8 + g]), acc);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 // -------------------------------------------------------------------------
 
 template <int C, int NT, bool F16, bool GLU, int XR>
@@ -1223,6 +1288,16 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q80_dot(r, hf, xq, xsc);
+        } else if constexpr (C == Q4_0 || C == IQ4_NL) {
+            // warp = group column, lane = row (a whole 144-byte group)
+            Q40Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_q40_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_q40_dot<C == IQ4_NL>(r, xq, xsc);
         } else if constexpr (C == Q6_K) {
             // lane = row, warp = (block column warp&3, block half warp>>2)
             const int hf = warp >> 2;
@@ -1743,7 +1818,7 @@ cudaError_t launch_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     return glu ? launch_nt<C, false, true>(a, st, grid_out) : launch_nt<C, false, false>(a, st, grid_out);
 }
 
-// Q5_K, Q8_0, IQ3_XXS and IQ4_XS have the lane-per-row path only (one activation row per
+// Q5_K, Q8_0, IQ3_XXS, IQ4_XS, Q4_0 and IQ4_NL have the lane-per-row path only (one activation row per
 // group); the callers route every other shape to the tcgen05 GEMM
 template <int C, bool F16, bool GLU>
 cudaError_t launch_onerow(const GemvArgs &a, cudaStream_t st, int *grid_out) {
@@ -1761,6 +1836,8 @@ cudaError_t launch_onerow_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
 cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == Q5_K) return launch_onerow_c<Q5_K>(a, st, grid_out);
     if (a.codec == Q8_0) return launch_onerow_c<Q8_0>(a, st, grid_out);
+    if (a.codec == Q4_0) return launch_onerow_c<Q4_0>(a, st, grid_out);
+    if (a.codec == IQ4_NL) return launch_onerow_c<IQ4_NL>(a, st, grid_out);
     if (a.codec == IQ3_XXS) return launch_onerow_c<IQ3_XXS>(a, st, grid_out);
     if (a.codec == IQ4_XS) return launch_onerow_c<IQ4_XS>(a, st, grid_out);
     switch (a.codec) {

@@ -20,6 +20,8 @@
  *   IQ2_XXS(quants.py:802-829): db = d*(0.5+ls)*0.25, w = db*grid*sign
  *   IQ3_XXS(quants.py:1027-1054): db = d*(0.5+ls)*0.5, w = db*grid*sign
  *   IQ4_XS (quants.py:1351-1377): dl = d*(ls-32), w = dl*kvalues[q]
+ *   Q4_0   (quants.py:241-251): w = d*(q-8) per 32-weight block
+ *   IQ4_NL (quants.py:1333-1348): w = d*kvalues[q] per 32-weight block
  * Every product above is exact in f32 (see the kernels' header), so results
  * are independent of FMA contraction; the file is still built with
  * -ffp-contract=off to keep the statement literal.
@@ -35,7 +37,8 @@
 #include "kq_tables.h"
 
 #define QK 256
-enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23 };
+enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
+       KQO_Q4_0 = 2, KQO_IQ4_NL = 20 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
@@ -66,6 +69,7 @@ int kqo_block_bytes(int codec) {
     case KQO_Q4_K: return 144; case KQO_Q5_K: return 176; case KQO_Q6_K: return 210; case KQO_IQ2_XXS: return 66;
     case KQO_Q8_0: return 272; /* eight 34-byte blocks per 256 weights */
     case KQO_IQ3_XXS: return 98; case KQO_IQ4_XS: return 136;
+    case KQO_Q4_0: case KQO_IQ4_NL: return 144; /* eight 18-byte blocks per 256 weights */
     }
     return -1;
 }
@@ -212,6 +216,21 @@ static void deq_iq4xs(const uint8_t *b, float *o) {
     }
 }
 
+/* gguf-py Q4_0.dequantize_blocks (quants.py:241-251) and IQ4_NL's
+ * (quants.py:1333-1348) over eight 18-byte blocks: d, then 16 bytes whose low
+ * nibbles are weights 0-15 and high nibbles 16-31. */
+static void deq_q40_nl(const uint8_t *b, float *o, int nl) {
+    for (int j = 0; j < 8; j++) {
+        const uint8_t *blk = b + 18 * j;
+        float d = kqo_half((uint16_t)(blk[0] | blk[1] << 8));
+        for (int l = 0; l < 16; l++) {
+            int lo = blk[2 + l] & 0x0f, hi = blk[2 + l] >> 4;
+            o[32 * j + l] = nl ? d * (float)kqo_iq4nl[lo] : d * (float)(lo - 8);
+            o[32 * j + 16 + l] = nl ? d * (float)kqo_iq4nl[hi] : d * (float)(hi - 8);
+        }
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -221,6 +240,8 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_IQ2_XXS: deq_iq2xxs(b, o); return 0;
     case KQO_IQ3_XXS: deq_iq3xxs(b, o); return 0;
     case KQO_IQ4_XS: deq_iq4xs(b, o); return 0;
+    case KQO_Q4_0: deq_q40_nl(b, o, 0); return 0;
+    case KQO_IQ4_NL: deq_q40_nl(b, o, 1); return 0;
     }
     return -1;
 }

@@ -31,10 +31,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
-Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_XS = 8, 12, 13, 14, 16, 18, 23
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 2, 8, 12, 13, 14, 16, 18, 20, 23
 CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
-             "iq4_xs": IQ4_XS}
-BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136}  # per 256 weights
+             "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL}
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
+               Q4_0: 144, IQ4_NL: 144}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -202,6 +203,16 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         q = blocks[:, 8:].reshape(n, 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
         kv = np.array(_table_values("KQ_IQ4NL_VALUES_INIT"), np.float32)
         out = dl * kv[(q & 15).reshape(n, 8, 32)]
+    elif c in (Q4_0, IQ4_NL):  # quants.py:241-251 / 1333-1348: eight (fp16 d, 16 nibble bytes) blocks
+        sub = blocks.reshape(n * 8, 18)
+        d = _half(sub[:, 0:2]).reshape(n * 8, 1)
+        q = (sub[:, 2:].reshape(n * 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 2, 1)) & 15
+        q = q.reshape(n * 8, 32)
+        if c == Q4_0:
+            out = d * (q.astype(np.float32) - np.float32(8))
+        else:
+            kv = np.array(_table_values("KQ_IQ4NL_VALUES_INIT"), np.float32)
+            out = d * kv[q]
     else:
         raise ValueError(codec)
     return out.reshape(*np.asarray(w).shape[:-1], -1).astype(np.float32)

@@ -17,7 +17,9 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
   Q6_K   int8 scales at -128, -64, 0, 63, 127; quants all 0 / all 63;
   IQ2_XXS every grid index and every 7-bit sign index, ls = 0 and 15;
   IQ3_XXS the same sweep over its 256-entry grid;
-  IQ4_XS  every nibble value, 6-bit scales 0 / 31 / 32 / 63, negative d.
+  IQ4_XS  every nibble value, 6-bit scales 0 / 31 / 32 / 63, negative d;
+  Q4_0    quants all 0 / all 15 / every value, d = 0, negative, 65504;
+  IQ4_NL  every nibble value on every block, negative d.
 Matmul references are x @ dequant(W).T in float64 for bf16 x (N(0,1)) plus
 one-hot x rows, which must reproduce single dequantized columns exactly.
 """
@@ -35,7 +37,7 @@ from gguf.quants import dequantize  # noqa: E402
 from gmlx_b200 import synth  # noqa: E402
 
 QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
-      "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS}
+      "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL}
 
 
 def fp16(v):
@@ -115,6 +117,15 @@ def edge_blocks(codec):
                 aux |= (15 if (j + blk) % 2 else 0) << 28
                 b[66 + 4 * j:70 + 4 * j] = np.array([aux], np.uint32).view(np.uint8)
             blocks.append(b)
+    elif codec in ("q4_0", "iq4_nl"):  # 144-byte groups of eight 18-byte blocks
+        for dv, qv in [(1e-3, 0x00), (1e-3, 0xff), (0.0, None), (-2e-3, None), (65504.0, 0x88), (5e-4, None)]:
+            b = np.zeros((8, 18), np.uint8)
+            b[:, 0:2] = fp16(dv)
+            if qv is None:  # every nibble value in both halves
+                b[:, 2:] = (np.arange(16) | (((np.arange(16) + 5) % 16) << 4)).astype(np.uint8)
+            else:
+                b[:, 2:] = qv
+            blocks.append(b.reshape(144))
     elif codec == "iq4_xs":
         # every nibble value on every sub-block; 6-bit scales 0, 31, 32, 63
         for blk, (dv, ls) in enumerate([(1e-3, 0), (1e-3, 63), (-2e-3, 32), (5e-4, 31), (1e-3, None)]):
