@@ -42,6 +42,24 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
 #pragma unroll
         for (int i = 0; i < 8; i++)
             o[i] = dl * (float)(((q[i] >> (4 * h)) & 15) | (((qh[i] >> j) & 1) << 4)) - ml;
+    } else if constexpr (C == Q2_K || C == Q3_K) {  // lane: weights 8 lane .. +7 (one 16-weight sub-block)
+        const int w0 = 8 * lane, h = w0 >> 7, k = (w0 >> 5) & 3, l0 = w0 & 31, j = w0 >> 4;
+        float dl, ml = 0.f;
+        const uint8_t *qs = b + (C == Q2_K ? 16 : 32) + 32 * h + l0;
+        if constexpr (C == Q2_K) {
+            dl = half_bits_to_float(ld_u16(b + 80)) * (float)(b[j] & 15);
+            ml = half_bits_to_float(ld_u16(b + 82)) * (float)(b[j] >> 4);
+        } else {
+            const int lo = j < 8 ? (b[96 + j] & 15) : (b[88 + j] >> 4);
+            const int hi = (b[104 + (j & 3)] >> (2 * (j >> 2))) & 3;
+            dl = half_bits_to_float(ld_u16(b + 108)) * (float)((lo | (hi << 4)) - 32);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int q = (qs[i] >> (2 * k)) & 3;
+            if constexpr (C == Q3_K) q -= ((b[l0 + i] >> (4 * h + k)) & 1) ? 0 : 4;
+            o[i] = C == Q2_K ? dl * (float)q - ml : dl * (float)q;
+        }
     } else if constexpr (C == Q4_0 || C == IQ4_NL) {  // lane: 8 weights of ggml block lane / 4
         const uint8_t *blk = b + 18 * (lane >> 2);
         const float d = half_bits_to_float(ld_u16(blk));
@@ -281,6 +299,8 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q4_0: return launch_deq<Q4_0>(w, rows, nb, row_stride, out, dtype, st);
+    case Q2_K: return launch_deq<Q2_K>(w, rows, nb, row_stride, out, dtype, st);
+    case Q3_K: return launch_deq<Q3_K>(w, rows, nb, row_stride, out, dtype, st);
     case IQ4_NL: return launch_deq<IQ4_NL>(w, rows, nb, row_stride, out, dtype, st);
     case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st);
     case IQ3_XXS: return launch_deq<IQ3_XXS>(w, rows, nb, row_stride, out, dtype, st);

@@ -21,6 +21,11 @@
 //   Q4_0  8 x 18 B  (d f16 | 16 B nibbles), w = d*(q-8)  quants.py:241-251
 //   IQ4_NL 8 x 18 B (d f16 | 16 B nibbles), w = d*kvalues[q]  quants.py:1333-1348
 //         (32-weight blocks: nibble j < 16 low of byte j, else high of byte j-16)
+//   Q2_K  84 B   16 x (sc | m << 4) | 64 B 2-bit q | d f16 | dmin f16
+//                w = (d*sc_j)*q - (dmin*m_j), 16-weight j   quants.py:404-428
+//   Q3_K  110 B  32 B high bits | 64 B 2-bit q | 12 B 6-bit scales | d f16
+//                w = (d*(s_j-32))*(q - 4*(1-hbit))          quants.py:431-472
+//         (both: weight 128h + 32k + l = bits 2k of quant byte 32h + l)
 //
 // Exactness: every product above is exact in f32 (fp16 d has 11 significant
 // bits; d*sc <= 17 bits, d*sc*q <= 21 bits; Q6_K d*sc*(q-32) <= 24 bits;
@@ -38,7 +43,7 @@
 namespace kq {
 
 enum Codec : int {
-    Q4_0 = 2, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
+    Q4_0 = 2, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
@@ -54,6 +59,8 @@ template <> struct Fmt<Q8_0> { static constexpr int bpb = 272; static constexpr 
 // of them (144 bytes) are handled as one 256-weight group
 template <> struct Fmt<Q4_0> { static constexpr int bpb = 144; static constexpr int sub = 32; };
 template <> struct Fmt<IQ4_NL> { static constexpr int bpb = 144; static constexpr int sub = 32; };
+template <> struct Fmt<Q2_K> { static constexpr int bpb = 84; static constexpr int sub = 16; };
+template <> struct Fmt<Q3_K> { static constexpr int bpb = 110; static constexpr int sub = 16; };
 template <> struct Fmt<Q6_K> { static constexpr int bpb = 210; static constexpr int sub = 16; };
 template <> struct Fmt<IQ2_XXS> { static constexpr int bpb = 66; static constexpr int sub = 32; };
 template <> struct Fmt<IQ3_XXS> { static constexpr int bpb = 98; static constexpr int sub = 32; };
@@ -62,7 +69,7 @@ template <> struct Fmt<IQ4_XS> { static constexpr int bpb = 136; static constexp
 __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
-         : -1;
+         : codec == Q2_K ? 84 : codec == Q3_K ? 110 : -1;
 }
 
 // 256-entry IQ2_XXS grid, byte i of entry e = |w_i| in {8, 25, 43}.

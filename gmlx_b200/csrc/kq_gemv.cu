@@ -59,6 +59,8 @@ template <int C> struct GCfg;
 template <> struct GCfg<Q4_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // (dsc, -mt) x 2 rows
 template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
+template <> struct GCfg<Q2_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<Q3_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q4_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<IQ4_NL> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
 template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1; };    // dsc x 2 rows
@@ -1022,6 +1024,106 @@ __device__ __forceinline__ float dp_q40_dot(const Q40Regs &r, const uint32_t *xq
     return acc;
 }
 
+// Lane-per-row Q2_K / Q3_K: a lane takes a whole super-block.  Weight
+// 128h + 32k + l is bits 2k of quant byte 32h + l, so quant word 8h + i
+// shifted by 2k gives weights 128h + 32k + 4i .. +3 (sub-block 8h + 2k + i/4).
+// The unsigned values (Q2_K: q in 0..3; Q3_K: q + 4 * hbit in 0..7) are dotted
+// against the int16 activations; per 16-weight sub-block j:
+//     Q2_K: acc += d sc_j dx S_j - dmin m_j dx sum16_j(x_q)
+//     Q3_K: acc += d (s_j - 32) (dx S_j - 4 dx sum16_j(x_q)).
+struct Q2Regs {
+    uint32_t sc[4], q[16];
+    float d, dmin;
+};
+
+__device__ __forceinline__ void dp_q2k_load(const uint8_t *blk, Q2Regs &r) {  // 4-byte aligned
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(blk);
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.sc[i] = w[i];
+#pragma unroll
+    for (int i = 0; i < 16; i++) r.q[i] = w[4 + i];
+    r.d = half_bits_to_float(w[20] & 0xffffu);
+    r.dmin = half_bits_to_float(w[20] >> 16);
+}
+
+__device__ __forceinline__ float dp_q2k_dot(const Q2Regs &r, const uint32_t *xq, const float *xsc) {
+    float acc = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            int s0 = 0, s1 = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int q = (int)((r.q[8 * h + i] >> (2 * k)) & 0x03030303u);
+                const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 64 * h + 16 * k + 2 * i);
+                int &sm = i < 4 ? s0 : s1;
+                sm = __dp2a_lo((int)xv.x, q, sm);
+                sm = __dp2a_hi((int)xv.y, q, sm);
+            }
+            const int g = 4 * h + k, j = 2 * g;  // 32-weight group, first 16-weight sub-block
+            const uint32_t scw = r.sc[j >> 2];
+            const float sc0 = (float)((scw >> (8 * (j & 3))) & 15u), m0 = (float)((scw >> (8 * (j & 3) + 4)) & 15u);
+            const float sc1 = (float)((scw >> (8 * (j & 3) + 8)) & 15u), m1 = (float)((scw >> (8 * (j & 3) + 12)) & 15u);
+            acc = fmaf(r.d * xsc[g], sc0 * (float)s0 + sc1 * (float)s1, acc);
+            acc = fmaf(-r.dmin, fmaf(m0, xsc[16 + j], m1 * xsc[17 + j]), acc);
+        }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
+struct Q3Regs {
+    uint32_t hm[8], q[16], s[3];
+    float d;
+};
+
+__device__ __forceinline__ void dp_q3k_load(const uint8_t *blk, Q3Regs &r) {  // 2-byte aligned
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    uint32_t w[29];
+#pragma unroll
+    for (int i = 0; i < 29; i++) w[i] = aw[i];  // up to 6 bytes past the block: the ring row has slack
+#pragma unroll
+    for (int i = 0; i < 8; i++) r.hm[i] = __funnelshift_r(w[i], w[i + 1], sh);
+#pragma unroll
+    for (int i = 0; i < 16; i++) r.q[i] = __funnelshift_r(w[8 + i], w[9 + i], sh);
+#pragma unroll
+    for (int i = 0; i < 3; i++) r.s[i] = __funnelshift_r(w[24 + i], w[25 + i], sh);
+    r.d = half_bits_to_float(__funnelshift_r(w[27], w[28], sh) & 0xffffu);
+}
+
+__device__ __forceinline__ float dp_q3k_dot(const Q3Regs &r, const uint32_t *xq, const float *xsc) {
+    float acc = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            int s0 = 0, s1 = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t hb = (r.hm[i] >> (4 * h + k)) & 0x01010101u;
+                const int q = (int)(((r.q[8 * h + i] >> (2 * k)) & 0x03030303u) | (hb << 2));
+                const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 64 * h + 16 * k + 2 * i);
+                int &sm = i < 4 ? s0 : s1;
+                sm = __dp2a_lo((int)xv.x, q, sm);
+                sm = __dp2a_hi((int)xv.y, q, sm);
+            }
+            const int g = 4 * h + k;
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int j = 2 * g + u;  // 16-weight sub-block
+                const uint32_t lw = r.s[(j & 7) >> 2];
+                const int lo = (int)((lw >> (8 * (j & 3) + 4 * (j >> 3))) & 15u);
+                const int hi = (int)((r.s[2] >> (8 * (j & 3) + 2 * (j >> 2))) & 3u);
+                const float sc = (float)((lo | (hi << 4)) - 32);
+                acc = fmaf(r.d * sc, fmaf(xsc[g], (float)(u ? s1 : s0), -4.f * xsc[16 + j]), acc);
+            }
+        }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 // -------------------------------------------------------------------------
 
 template <int C, int NT, bool F16, bool GLU, int XR>
@@ -1288,6 +1390,24 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q80_dot(r, hf, xq, xsc);
+        } else if constexpr (C == Q2_K) {
+            Q2Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_q2k_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_q2k_dot(r, xq, xsc);
+        } else if constexpr (C == Q3_K) {
+            Q3Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_q3k_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_q3k_dot(r, xq, xsc);
         } else if constexpr (C == Q4_0 || C == IQ4_NL) {
             // warp = group column, lane = row (a whole 144-byte group)
             Q40Regs r;
@@ -1818,7 +1938,7 @@ cudaError_t launch_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     return glu ? launch_nt<C, false, true>(a, st, grid_out) : launch_nt<C, false, false>(a, st, grid_out);
 }
 
-// Q5_K, Q8_0, IQ3_XXS, IQ4_XS, Q4_0 and IQ4_NL have the lane-per-row path only (one activation row per
+// Q5_K, Q8_0, IQ3_XXS, IQ4_XS, Q4_0, IQ4_NL, Q2_K and Q3_K have the lane-per-row path only (one activation row per
 // group); the callers route every other shape to the tcgen05 GEMM
 template <int C, bool F16, bool GLU>
 cudaError_t launch_onerow(const GemvArgs &a, cudaStream_t st, int *grid_out) {
@@ -1837,6 +1957,8 @@ cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == Q5_K) return launch_onerow_c<Q5_K>(a, st, grid_out);
     if (a.codec == Q8_0) return launch_onerow_c<Q8_0>(a, st, grid_out);
     if (a.codec == Q4_0) return launch_onerow_c<Q4_0>(a, st, grid_out);
+    if (a.codec == Q2_K) return launch_onerow_c<Q2_K>(a, st, grid_out);
+    if (a.codec == Q3_K) return launch_onerow_c<Q3_K>(a, st, grid_out);
     if (a.codec == IQ4_NL) return launch_onerow_c<IQ4_NL>(a, st, grid_out);
     if (a.codec == IQ3_XXS) return launch_onerow_c<IQ3_XXS>(a, st, grid_out);
     if (a.codec == IQ4_XS) return launch_onerow_c<IQ4_XS>(a, st, grid_out);

@@ -16,6 +16,9 @@ prescribe:
   quants, ``d`` fp16(U[1e-4, 2e-3]).
 * IQ3_XXS (98 B), IQ4_XS (136 B): random bytes, ``d`` (the first two bytes)
   fp16(U[1e-4, 2e-3]).
+* Q2_K (84 B): random scale and quant bytes, ``d``, ``dmin`` (the last four
+  bytes) fp16(U[1e-4, 2e-3]).  Q3_K (110 B): random, ``d`` (the last two
+  bytes) fp16(U[1e-4, 2e-3]).
 * Q4_0, IQ4_NL (18 B per 32 weights, counted as 144 B per 256): random
   nibbles, ``d`` fp16(U[1e-4, 2e-3]) per 32-weight block.
 
@@ -26,13 +29,13 @@ from __future__ import annotations
 
 import numpy as np
 
-Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 2, 8, 12, 13, 14, 16, 18, 20, 23
+Q4_0, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 2, 8, 10, 11, 12, 13, 14, 16, 18, 20, 23
 CODECS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
-          "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL}
+          "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K}
 CODEC_NAMES = {v: k for k, v in CODECS.items()}
 # bytes per 256 weights (Q8_0: eight 34-byte ggml blocks of 32 weights)
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
-               Q4_0: 144, IQ4_NL: 144}
+               Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110}
 QK = 256
 D_LO, D_HI = 1e-4, 2e-3
 
@@ -75,6 +78,11 @@ def random_blocks(codec, n_blocks: int, seed: int = 0) -> np.ndarray:
     elif c == Q8_0:  # eight (fp16 d, 32 x int8) blocks per 256 weights
         sub = b.reshape(n_blocks * 8, 34)
         sub[:, 0:2] = _fp16_bytes(rng, n_blocks * 8)
+    elif c == Q2_K:
+        b[:, 80:82] = _fp16_bytes(rng, n_blocks)
+        b[:, 82:84] = _fp16_bytes(rng, n_blocks)
+    elif c == Q3_K:
+        b[:, 108:110] = _fp16_bytes(rng, n_blocks)
     elif c in (Q4_0, IQ4_NL):  # eight (fp16 d, 16 nibble bytes) blocks per 256 weights
         sub = b.reshape(n_blocks * 8, 18)
         sub[:, 0:2] = _fp16_bytes(rng, n_blocks * 8)

@@ -21,6 +21,8 @@
  *   IQ3_XXS(quants.py:1027-1054): db = d*(0.5+ls)*0.5, w = db*grid*sign
  *   IQ4_XS (quants.py:1351-1377): dl = d*(ls-32), w = dl*kvalues[q]
  *   Q4_0   (quants.py:241-251): w = d*(q-8) per 32-weight block
+ *   Q2_K   (quants.py:404-428): dl = d*sc, ml = dmin*m, w = dl*q - ml (16-weight sub-blocks)
+ *   Q3_K   (quants.py:431-472): dl = d*(s-32), w = dl*(q2 - 4*(1-hbit))
  *   IQ4_NL (quants.py:1333-1348): w = d*kvalues[q] per 32-weight block
  * Every product above is exact in f32 (see the kernels' header), so results
  * are independent of FMA contraction; the file is still built with
@@ -38,7 +40,7 @@
 
 #define QK 256
 enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
-       KQO_Q4_0 = 2, KQO_IQ4_NL = 20 };
+       KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
@@ -70,6 +72,7 @@ int kqo_block_bytes(int codec) {
     case KQO_Q8_0: return 272; /* eight 34-byte blocks per 256 weights */
     case KQO_IQ3_XXS: return 98; case KQO_IQ4_XS: return 136;
     case KQO_Q4_0: case KQO_IQ4_NL: return 144; /* eight 18-byte blocks per 256 weights */
+    case KQO_Q2_K: return 84; case KQO_Q3_K: return 110;
     }
     return -1;
 }
@@ -231,6 +234,36 @@ static void deq_q40_nl(const uint8_t *b, float *o, int nl) {
     }
 }
 
+/* gguf-py Q2_K.dequantize_blocks (quants.py:404-428): 16 scale bytes (low
+ * nibble sc, high nibble m, one per 16 weights), 64 bytes of 2-bit quants
+ * (weight 128h + 32k + l = bits 2k of byte 32h + l), d, dmin. */
+static void deq_q2k(const uint8_t *b, float *o) {
+    const uint8_t *sc = b, *qs = b + 16;
+    float d = kqo_half((uint16_t)(b[80] | b[81] << 8)), dmin = kqo_half((uint16_t)(b[82] | b[83] << 8));
+    for (int w = 0; w < 256; w++) {
+        int h = w >> 7, k = (w >> 5) & 3, l = w & 31, j = w >> 4;
+        float dl = d * (float)(sc[j] & 0x0f), ml = dmin * (float)(sc[j] >> 4);
+        o[w] = dl * (float)((qs[32 * h + l] >> (2 * k)) & 3) - ml;
+    }
+}
+
+/* gguf-py Q3_K.dequantize_blocks (quants.py:431-472): 32 bytes of high bits
+ * (bit 4h + k of byte l, set meaning "no -4"), 64 bytes of 2-bit quants laid
+ * out as Q2_K's, 12 bytes of sixteen 6-bit scales (low nibbles in bytes 0-7,
+ * high pairs in bytes 8-11), d. */
+static void deq_q3k(const uint8_t *b, float *o) {
+    const uint8_t *hm = b, *qs = b + 32, *s = b + 96;
+    float d = kqo_half((uint16_t)(b[108] | b[109] << 8));
+    for (int w = 0; w < 256; w++) {
+        int h = w >> 7, k = (w >> 5) & 3, l = w & 31, j = w >> 4;
+        int lo = j < 8 ? (s[j] & 0x0f) : (s[j - 8] >> 4);
+        int hi = (s[8 + (j & 3)] >> (2 * (j >> 2))) & 3;
+        float dl = d * (float)((lo | (hi << 4)) - 32);
+        int q = ((qs[32 * h + l] >> (2 * k)) & 3) - (((hm[l] >> (4 * h + k)) & 1) ? 0 : 4);
+        o[w] = dl * (float)q;
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -241,6 +274,8 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_IQ3_XXS: deq_iq3xxs(b, o); return 0;
     case KQO_IQ4_XS: deq_iq4xs(b, o); return 0;
     case KQO_Q4_0: deq_q40_nl(b, o, 0); return 0;
+    case KQO_Q2_K: deq_q2k(b, o); return 0;
+    case KQO_Q3_K: deq_q3k(b, o); return 0;
     case KQO_IQ4_NL: deq_q40_nl(b, o, 1); return 0;
     }
     return -1;

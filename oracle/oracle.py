@@ -31,11 +31,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
-Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 2, 8, 12, 13, 14, 16, 18, 20, 23
+Q4_0, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 2, 8, 10, 11, 12, 13, 14, 16, 18, 20, 23
 CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
-             "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL}
+             "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K}
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
-               Q4_0: 144, IQ4_NL: 144}  # per 256 weights
+               Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -203,6 +203,23 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         q = blocks[:, 8:].reshape(n, 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
         kv = np.array(_table_values("KQ_IQ4NL_VALUES_INIT"), np.float32)
         out = dl * kv[(q & 15).reshape(n, 8, 32)]
+    elif c == Q2_K:  # quants.py:404-428
+        sc = blocks[:, 0:16]
+        d = _half(blocks[:, 80:82]).reshape(n, 1, 1)
+        dmin = _half(blocks[:, 82:84]).reshape(n, 1, 1)
+        q = (blocks[:, 16:80].reshape(n, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
+        q = q.reshape(n, 16, 16).astype(np.float32)
+        out = (d * (sc & 15).astype(np.float32).reshape(n, 16, 1)) * q - dmin * (sc >> 4).astype(np.float32).reshape(n, 16, 1)
+    elif c == Q3_K:  # quants.py:431-472
+        hm, qs, s = blocks[:, 0:32], blocks[:, 32:96], blocks[:, 96:108]
+        d = _half(blocks[:, 108:110]).reshape(n, 1, 1)
+        lo = np.concatenate([s[:, 0:8] & 15, s[:, 0:8] >> 4], 1)
+        hi = (s[:, 8:12].reshape(n, 1, 4) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 4, 1)).reshape(n, 16) & 3
+        sc = ((lo | (hi << 4)).astype(np.int16) - 32).astype(np.float32)
+        q2 = (qs.reshape(n, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
+        hb = (hm.reshape(n, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 8, 1)) & 1
+        q = q2.reshape(n, 8, 32).astype(np.int16) - 4 * (1 - hb.astype(np.int16))
+        out = (d * sc.reshape(n, 16, 1)) * q.reshape(n, 16, 16).astype(np.float32)
     elif c in (Q4_0, IQ4_NL):  # quants.py:241-251 / 1333-1348: eight (fp16 d, 16 nibble bytes) blocks
         sub = blocks.reshape(n * 8, 18)
         d = _half(sub[:, 0:2]).reshape(n * 8, 1)

@@ -19,7 +19,11 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
   IQ3_XXS the same sweep over its 256-entry grid;
   IQ4_XS  every nibble value, 6-bit scales 0 / 31 / 32 / 63, negative d;
   Q4_0    quants all 0 / all 15 / every value, d = 0, negative, 65504;
-  IQ4_NL  every nibble value on every block, negative d.
+  IQ4_NL  every nibble value on every block, negative d;
+  Q2_K    scale / min nibbles 0 and 15, quants all 0 / all 3, one-hot
+          sub-block scales;
+  Q3_K    6-bit scales 0 / 31 / 32 / 63 (-32 .. 31), high bits all set /
+          all clear / one plane at a time.
 Matmul references are x @ dequant(W).T in float64 for bf16 x (N(0,1)) plus
 one-hot x rows, which must reproduce single dequantized columns exactly.
 """
@@ -37,7 +41,8 @@ from gguf.quants import dequantize  # noqa: E402
 from gmlx_b200 import synth  # noqa: E402
 
 QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
-      "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL}
+      "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
+      "q3_k": T.Q3_K}
 
 
 def fp16(v):
@@ -116,6 +121,35 @@ def edge_blocks(codec):
                 k += 4
                 aux |= (15 if (j + blk) % 2 else 0) << 28
                 b[66 + 4 * j:70 + 4 * j] = np.array([aux], np.uint32).view(np.uint8)
+            blocks.append(b)
+    elif codec == "q2_k":
+        for scv, qv in [(0x00, 0x00), (0xff, 0xff), (0x0f, 0x55), (0xf0, None), (None, None)]:
+            b = np.zeros(84, np.uint8)
+            b[0:16] = rng.integers(0, 256, 16, dtype=np.uint8) if scv is None else scv
+            b[16:80] = rng.integers(0, 256, 64, dtype=np.uint8) if qv is None else qv
+            b[80:82], b[82:84] = fp16(1e-3), fp16(5e-4)
+            blocks.append(b)
+        for one in range(16):  # one-hot sub-block scale (min 0)
+            b = np.zeros(84, np.uint8)
+            b[one] = 1
+            b[16:80] = rng.integers(0, 256, 64, dtype=np.uint8)
+            b[80:82], b[82:84] = fp16(1e-3), fp16(1e-3)
+            blocks.append(b)
+    elif codec == "q3_k":
+        for sv, hfill in [(0, 0x00), (63, 0xff), (32, None), (31, 0x55), (None, None)]:
+            b = np.zeros(110, np.uint8)
+            sc = rng.integers(0, 64, 16) if sv is None else np.full(16, sv)
+            for j in range(16):
+                b[96 + (j % 8)] |= (int(sc[j]) & 15) << (4 * (j // 8))
+                b[104 + (j & 3)] |= ((int(sc[j]) >> 4) & 3) << (2 * (j >> 2))
+            b[0:32] = rng.integers(0, 256, 32, dtype=np.uint8) if hfill is None else hfill
+            b[32:96] = rng.integers(0, 256, 64, dtype=np.uint8)
+            b[108:110] = fp16(1.5e-3)
+            blocks.append(b)
+        for plane in range(8):  # high bits set on one plane only
+            b = rng.integers(0, 256, 110, dtype=np.uint8)
+            b[0:32] = 1 << plane
+            b[108:110] = fp16(-1e-3)
             blocks.append(b)
     elif codec in ("q4_0", "iq4_nl"):  # 144-byte groups of eight 18-byte blocks
         for dv, qv in [(1e-3, 0x00), (1e-3, 0xff), (0.0, None), (-2e-3, None), (65504.0, 0x88), (5e-4, None)]:

@@ -9,7 +9,7 @@ from gmlx_b200 import synth
 from oracle import oracle as O
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
-CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs", "q4_0", "iq4_nl"]
+CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs", "q4_0", "iq4_nl", "q2_k", "q3_k"]
 
 
 @pytest.fixture(scope="module")
@@ -45,7 +45,8 @@ def test_oracle_matches_gguf_py_random(codec, seed):
     gq = pytest.importorskip("gguf.quants")
     from gguf.constants import GGMLQuantizationType as T
     qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
-          "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL}[codec]
+          "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
+          "q3_k": T.Q3_K}[codec]
     w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
 
@@ -58,7 +59,8 @@ def test_raw_random_bytes_match_where_finite():
     rng = np.random.default_rng(5)
     for codec, qt, bpb in [("q4_k", T.Q4_K, 144), ("q5_k", T.Q5_K, 176), ("q6_k", T.Q6_K, 210),
                            ("iq2_xxs", T.IQ2_XXS, 66), ("q8_0", T.Q8_0, 272), ("iq3_xxs", T.IQ3_XXS, 98),
-                           ("iq4_xs", T.IQ4_XS, 136), ("q4_0", T.Q4_0, 144), ("iq4_nl", T.IQ4_NL, 144)]:
+                           ("iq4_xs", T.IQ4_XS, 136), ("q4_0", T.Q4_0, 144), ("iq4_nl", T.IQ4_NL, 144),
+                           ("q2_k", T.Q2_K, 84), ("q3_k", T.Q3_K, 110)]:
         w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
         a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
         fin = np.isfinite(b)
@@ -119,6 +121,10 @@ def test_synthetic_block_statistics():
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3 and dm.min() >= 9e-5
         elif codec in ("q8_0", "q4_0", "iq4_nl"):
             d = w.reshape(-1, 34 if codec == "q8_0" else 18)[:, 0:2].copy().view(np.float16).astype(np.float32)
+            assert d.min() >= 9e-5 and d.max() <= 2.01e-3
+        elif codec in ("q2_k", "q3_k"):
+            off = 80 if codec == "q2_k" else 108
+            d = w[:, off:off + 2].copy().view(np.float16).astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3
         elif codec == "q6_k":
             sc = w[:, 192:208].view(np.int8)
