@@ -60,15 +60,21 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
             if constexpr (C == Q3_K) q -= ((b[l0 + i] >> (4 * h + k)) & 1) ? 0 : 4;
             o[i] = C == Q2_K ? dl * (float)q - ml : dl * (float)q;
         }
-    } else if constexpr (C == Q4_0 || C == IQ4_NL) {  // lane: 8 weights of ggml block lane / 4
-        const uint8_t *blk = b + 18 * (lane >> 2);
+    } else if constexpr (Legacy<C>::IS) {  // lane: 8 weights of ggml block lane / 4
+        using LG = Legacy<C>;
+        const uint8_t *blk = b + LG::BB * (lane >> 2);
         const float d = half_bits_to_float(ld_u16(blk));
+        const float m = LG::HASM ? half_bits_to_float(ld_u16(blk + 2)) : 0.f;
+        const uint32_t qh = LG::HASH ? ld_u32_unaligned(blk + (LG::HASM ? 4 : 2)) : 0u;
         const int i0 = 8 * (lane & 3), h = i0 >> 4;
-        const uint8_t *q = blk + 2 + (i0 & 15);
+        const uint8_t *q = blk + LG::BB - 16 + (i0 & 15);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const int v = (q[i] >> (4 * h)) & 15;
-            o[i] = C == Q4_0 ? d * (float)(v - 8) : d * (float)c_iq4nl_values[v];
+            int v = (q[i] >> (4 * h)) & 15;
+            if constexpr (LG::HASH) v |= (int)((qh >> (i0 + i)) & 1u) << 4;
+            if constexpr (LG::NL) o[i] = d * (float)c_iq4nl_values[v];
+            else if constexpr (LG::HASM) o[i] = __fadd_rn(__fmul_rn(d, (float)v), m);  // gguf order: d*q + m
+            else o[i] = d * (float)(v - LG::OFF);
         }
     } else if constexpr (C == Q8_0) {  // lane: 8 weights of ggml block lane / 4
         const uint8_t *blk = b + 34 * (lane >> 2);
@@ -299,6 +305,9 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q4_0: return launch_deq<Q4_0>(w, rows, nb, row_stride, out, dtype, st);
+    case Q4_1: return launch_deq<Q4_1>(w, rows, nb, row_stride, out, dtype, st);
+    case Q5_0: return launch_deq<Q5_0>(w, rows, nb, row_stride, out, dtype, st);
+    case Q5_1: return launch_deq<Q5_1>(w, rows, nb, row_stride, out, dtype, st);
     case Q2_K: return launch_deq<Q2_K>(w, rows, nb, row_stride, out, dtype, st);
     case Q3_K: return launch_deq<Q3_K>(w, rows, nb, row_stride, out, dtype, st);
     case IQ4_NL: return launch_deq<IQ4_NL>(w, rows, nb, row_stride, out, dtype, st);

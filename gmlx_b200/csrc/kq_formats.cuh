@@ -21,6 +21,10 @@
 //   Q4_0  8 x 18 B  (d f16 | 16 B nibbles), w = d*(q-8)  quants.py:241-251
 //   IQ4_NL 8 x 18 B (d f16 | 16 B nibbles), w = d*kvalues[q]  quants.py:1333-1348
 //         (32-weight blocks: nibble j < 16 low of byte j, else high of byte j-16)
+//   Q4_1  8 x 20 B  (d | m | 16 B nibbles), w = d*q + m   quants.py:254-276
+//   Q5_0  8 x 22 B  (d | u32 qh | 16 B), w = d*(q-16)     quants.py:279-305
+//   Q5_1  8 x 24 B  (d | m | u32 qh | 16 B), w = d*q + m  quants.py:308-336
+//         (Q5: q = nibble | (qh bit j) << 4 for weight j)
 //   Q2_K  84 B   16 x (sc | m << 4) | 64 B 2-bit q | d f16 | dmin f16
 //                w = (d*sc_j)*q - (dmin*m_j), 16-weight j   quants.py:404-428
 //   Q3_K  110 B  32 B high bits | 64 B 2-bit q | 12 B 6-bit scales | d f16
@@ -43,7 +47,7 @@
 namespace kq {
 
 enum Codec : int {
-    Q4_0 = 2, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
+    Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
@@ -59,6 +63,18 @@ template <> struct Fmt<Q8_0> { static constexpr int bpb = 272; static constexpr 
 // of them (144 bytes) are handled as one 256-weight group
 template <> struct Fmt<Q4_0> { static constexpr int bpb = 144; static constexpr int sub = 32; };
 template <> struct Fmt<IQ4_NL> { static constexpr int bpb = 144; static constexpr int sub = 32; };
+template <> struct Fmt<Q4_1> { static constexpr int bpb = 160; static constexpr int sub = 32; };
+template <> struct Fmt<Q5_0> { static constexpr int bpb = 176; static constexpr int sub = 32; };
+template <> struct Fmt<Q5_1> { static constexpr int bpb = 192; static constexpr int sub = 32; };
+
+// The 32-weight legacy blocks: d (fp16), m (fp16; HASM), a u32 of fifth bits
+// (HASH), then 16 nibble bytes; BB bytes per block, OFF subtracted from q.
+template <int C> struct Legacy {
+    static constexpr bool IS = C == Q4_0 || C == Q4_1 || C == Q5_0 || C == Q5_1 || C == IQ4_NL;
+    static constexpr bool HASM = C == Q4_1 || C == Q5_1, HASH = C == Q5_0 || C == Q5_1, NL = C == IQ4_NL;
+    static constexpr int BB = 18 + (HASM ? 2 : 0) + (HASH ? 4 : 0);
+    static constexpr int OFF = C == Q4_0 ? 8 : C == Q5_0 ? 16 : 0;
+};
 template <> struct Fmt<Q2_K> { static constexpr int bpb = 84; static constexpr int sub = 16; };
 template <> struct Fmt<Q3_K> { static constexpr int bpb = 110; static constexpr int sub = 16; };
 template <> struct Fmt<Q6_K> { static constexpr int bpb = 210; static constexpr int sub = 16; };
@@ -69,6 +85,7 @@ template <> struct Fmt<IQ4_XS> { static constexpr int bpb = 136; static constexp
 __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
+         : codec == Q4_1 ? 160 : codec == Q5_0 ? 176 : codec == Q5_1 ? 192
          : codec == Q2_K ? 84 : codec == Q3_K ? 110 : -1;
 }
 

@@ -61,6 +61,9 @@ template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; 
 template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
 template <> struct GCfg<Q2_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q3_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<Q4_1> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<Q5_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<Q5_1> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
 template <> struct GCfg<Q4_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<IQ4_NL> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
 template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1; };    // dsc x 2 rows
@@ -964,61 +967,88 @@ __device__ __forceinline__ float dp_iq4xs_dot(const IQ4Regs &r, const uint32_t *
     return acc;
 }
 
-// Lane-per-row Q4_0 / IQ4_NL: a lane takes a whole 144-byte group of eight
-// 18-byte ggml blocks (2-byte aligned), as Q4_K takes its 144-byte block, so
-// stage rows are 8 groups (1152 bytes) long.  Nibble j < 16 of a
-// block is the low half of byte j, j >= 16 the high half of byte j - 16.
-// Q4_0 dots the unsigned nibbles and applies its -8 as -8 * dx * sum(x_q);
-// IQ4_NL maps nibbles to the sixteen signed values first.
-struct Q40Regs {
-    uint32_t q[8][4];
-    float d[8];
+// Lane-per-row legacy 32-weight codecs (Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL): a
+// lane takes a whole group of eight blocks (144-176 bytes, 2-byte aligned),
+// as Q4_K takes its 144-byte block, so stage rows are 8 groups long; Q5_1's
+// 192-byte groups would not fit two CTAs per SM that way, so a Q5_1 lane takes
+// half a group (NB = 4 blocks, warp = (group column, half)) as Q8_0 does.  Nibble
+// j < 16 of a block is the low half of byte j, j >= 16 the high half of byte
+// j - 16; Q5 fifth bits are OR-ed in from the block's u32.  Unsigned values
+// are dotted against the int16 activations, per block g of 32 weights:
+//     Q4_0 / Q5_0: acc += d (dx S_g - OFF dx sum_g(x_q))
+//     Q4_1 / Q5_1: acc += d dx S_g + m dx sum_g(x_q)
+//     IQ4_NL: values mapped to the sixteen signed bytes first, acc += d dx S_g.
+template <int C> constexpr int LEG_NB = C == Q5_1 ? 4 : 8;  // blocks per lane
+template <int C> struct LegRegs {
+    static constexpr int NB = LEG_NB<C>;
+    uint32_t q[NB][4];
+    uint32_t qh[Legacy<C>::HASH ? NB : 1];
+    float d[NB], m[Legacy<C>::HASM ? NB : 1];
 };
 
-__device__ __forceinline__ void dp_q40_load(const uint8_t *grp, Q40Regs &r) {
+template <int C> __device__ __forceinline__ void dp_leg_load(const uint8_t *grp, LegRegs<C> &r) {
+    using LG = Legacy<C>;
 #pragma unroll
-    for (int s = 0; s < 8; s++) {
-        const uint8_t *blk = grp + 18 * s;
+    for (int s = 0; s < LEG_NB<C>; s++) {
+        const uint8_t *blk = grp + LG::BB * s;
         r.d[s] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk));
-        const uintptr_t qb = (uintptr_t)(blk + 2);
-        const uint32_t *aw = reinterpret_cast<const uint32_t *>(qb & ~(uintptr_t)3);
-        const uint32_t sh = (uint32_t)(qb & 3) * 8;
+        if constexpr (LG::HASM) r.m[s] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk + 2));
+        const uintptr_t hb = (uintptr_t)(blk + (LG::HASM ? 4 : 2));
+        const uint32_t *aw = reinterpret_cast<const uint32_t *>(hb & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(hb & 3) * 8;
+        if constexpr (LG::HASH) {
+            r.qh[s] = lds_w2(aw, 0, sh);
 #pragma unroll
-        for (int i = 0; i < 4; i++) r.q[s][i] = lds_w2(aw, i, sh);
+            for (int i = 0; i < 4; i++) r.q[s][i] = lds_w2(aw, 1 + i, sh);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) r.q[s][i] = lds_w2(aw, i, sh);
+        }
     }
 }
 
-template <bool NL>
-__device__ __forceinline__ float dp_q40_dot(const Q40Regs &r, const uint32_t *xq, const float *xsc) {
+// four bits (bits 0-3 of v) -> bit 4 of each byte
+__device__ __forceinline__ uint32_t bits_to_b4(uint32_t v) { return ((v & 15u) * 0x00204081u & 0x01010101u) << 4; }
+
+// g0: 32-weight group index of the lane's first block (0, or 4 for the second half)
+template <int C>
+__device__ __forceinline__ float dp_leg_dot(const LegRegs<C> &r, const uint32_t *xq, const float *xsc, int g0) {
+    using LG = Legacy<C>;
     uint32_t tv[4] = {0u, 0u, 0u, 0u};
-    if constexpr (NL) {
+    if constexpr (LG::NL) {
         const uint32_t *tw = reinterpret_cast<const uint32_t *>(c_iq4nl_values);
         tv[0] = tw[0], tv[1] = tw[1], tv[2] = tw[2], tv[3] = tw[3];
     }
     float acc = 0.f;
 #pragma unroll
-    for (int s = 0; s < 8; s++) {
+    for (int s = 0; s < LEG_NB<C>; s++) {
+        const int g = g0 + s;
         int sum = 0;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const uint32_t w = r.q[s][i];
-            int lo = (int)(w & 0x0f0f0f0fu), hi = (int)((w >> 4) & 0x0f0f0f0fu);
-            if constexpr (NL) {
-                lo = iq4_lookup4((uint32_t)lo, tv);
-                hi = iq4_lookup4((uint32_t)hi, tv);
+            uint32_t lo = w & 0x0f0f0f0fu, hi = (w >> 4) & 0x0f0f0f0fu;
+            if constexpr (LG::HASH) {
+                lo |= bits_to_b4(r.qh[s] >> (4 * i));
+                hi |= bits_to_b4(r.qh[s] >> (16 + 4 * i));
             }
-            const uint2 xl = *reinterpret_cast<const uint2 *>(xq + 16 * s + 2 * i);
-            const uint2 xh = *reinterpret_cast<const uint2 *>(xq + 16 * s + 8 + 2 * i);
-            sum = __dp2a_lo((int)xl.x, lo, sum);
-            sum = __dp2a_hi((int)xl.y, lo, sum);
-            sum = __dp2a_lo((int)xh.x, hi, sum);
-            sum = __dp2a_hi((int)xh.y, hi, sum);
+            if constexpr (LG::NL) {
+                lo = (uint32_t)iq4_lookup4(lo, tv);
+                hi = (uint32_t)iq4_lookup4(hi, tv);
+            }
+            const uint2 xl = *reinterpret_cast<const uint2 *>(xq + 16 * g + 2 * i);
+            const uint2 xh = *reinterpret_cast<const uint2 *>(xq + 16 * g + 8 + 2 * i);
+            sum = __dp2a_lo((int)xl.x, (int)lo, sum);
+            sum = __dp2a_hi((int)xl.y, (int)lo, sum);
+            sum = __dp2a_lo((int)xh.x, (int)hi, sum);
+            sum = __dp2a_hi((int)xh.y, (int)hi, sum);
         }
-        const int g = s;  // 32-weight group of the 256
-        if constexpr (NL)
+        if constexpr (LG::NL)
             acc = fmaf(r.d[s] * xsc[g], (float)sum, acc);
+        else if constexpr (LG::HASM)
+            acc = fmaf(r.d[s] * xsc[g], (float)sum, fmaf(r.m[s], xsc[8 + g], acc));
         else
-            acc = fmaf(r.d[s], fmaf(xsc[g], (float)sum, -8.f * xsc[8 + g]), acc);
+            acc = fmaf(r.d[s], fmaf(xsc[g], (float)sum, -(float)LG::OFF * xsc[8 + g]), acc);
     }
     __syncwarp();  // xq is rewritten for the next block
     return acc;
@@ -1340,7 +1370,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     // (block column warp&3, 16-row half warp>>2), half-warp = block half.
     // lane-per-row codecs with 4 block columns per stage (Q6_K, Q8_0): warp =
     // (block column, block half); the others: warp = block column
-    constexpr bool HALVES = C == Q6_K || C == Q8_0;
+    constexpr bool HALVES = C == Q6_K || C == Q8_0 || C == Q5_1;
     const int mt = (DP && !HALVES) ? 0 : (warp & 1), col = (DP && !HALVES) ? warp : (DP ? (warp & 3) : (warp >> 1));
     // per-warp table: scales (MMA path) or quantized activations + their
     // scales (lane-per-row path: 128 words + 32 floats = 640 bytes, as TABS)
@@ -1408,16 +1438,18 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q3k_dot(r, xq, xsc);
-        } else if constexpr (C == Q4_0 || C == IQ4_NL) {
-            // warp = group column, lane = row (a whole 144-byte group)
-            Q40Regs r;
+        } else if constexpr (Legacy<C>::IS) {
+            // warp = group column, lane = row (a whole group of eight blocks;
+            // Q5_1: warp = (group column, half), four blocks)
+            const int hf = LEG_NB<C> == 8 ? 0 : warp >> 2;
+            LegRegs<C> r;
             if (run) {
                 dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
-                dp_q40_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+                dp_leg_load<C>(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb + hf * 4 * Legacy<C>::BB, r);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q40_dot<C == IQ4_NL>(r, xq, xsc);
+            if (run) acc += dp_leg_dot<C>(r, xq, xsc, 4 * hf);
         } else if constexpr (C == Q6_K) {
             // lane = row, warp = (block column warp&3, block half warp>>2)
             const int hf = warp >> 2;
@@ -1938,7 +1970,7 @@ cudaError_t launch_c(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     return glu ? launch_nt<C, false, true>(a, st, grid_out) : launch_nt<C, false, false>(a, st, grid_out);
 }
 
-// Q5_K, Q8_0, IQ3_XXS, IQ4_XS, Q4_0, IQ4_NL, Q2_K and Q3_K have the lane-per-row path only (one activation row per
+// Q5_K, Q8_0, IQ3_XXS, IQ4_XS, Q2_K, Q3_K and the legacy 32-weight codecs have the lane-per-row path only (one activation row per
 // group); the callers route every other shape to the tcgen05 GEMM
 template <int C, bool F16, bool GLU>
 cudaError_t launch_onerow(const GemvArgs &a, cudaStream_t st, int *grid_out) {
@@ -1957,6 +1989,9 @@ cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == Q5_K) return launch_onerow_c<Q5_K>(a, st, grid_out);
     if (a.codec == Q8_0) return launch_onerow_c<Q8_0>(a, st, grid_out);
     if (a.codec == Q4_0) return launch_onerow_c<Q4_0>(a, st, grid_out);
+    if (a.codec == Q4_1) return launch_onerow_c<Q4_1>(a, st, grid_out);
+    if (a.codec == Q5_0) return launch_onerow_c<Q5_0>(a, st, grid_out);
+    if (a.codec == Q5_1) return launch_onerow_c<Q5_1>(a, st, grid_out);
     if (a.codec == Q2_K) return launch_onerow_c<Q2_K>(a, st, grid_out);
     if (a.codec == Q3_K) return launch_onerow_c<Q3_K>(a, st, grid_out);
     if (a.codec == IQ4_NL) return launch_onerow_c<IQ4_NL>(a, st, grid_out);

@@ -24,6 +24,8 @@
  *   Q2_K   (quants.py:404-428): dl = d*sc, ml = dmin*m, w = dl*q - ml (16-weight sub-blocks)
  *   Q3_K   (quants.py:431-472): dl = d*(s-32), w = dl*(q2 - 4*(1-hbit))
  *   IQ4_NL (quants.py:1333-1348): w = d*kvalues[q] per 32-weight block
+ *   Q4_1   (quants.py:254-276): w = d*q + m;  Q5_0 (:279-305): w = d*(q-16);
+ *   Q5_1   (:308-336): w = d*q + m  (Q5: q = nibble | qh bit << 4)
  * Every product above is exact in f32 (see the kernels' header), so results
  * are independent of FMA contraction; the file is still built with
  * -ffp-contract=off to keep the statement literal.
@@ -40,7 +42,8 @@
 
 #define QK 256
 enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
-       KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11 };
+       KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11,
+       KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
@@ -73,6 +76,7 @@ int kqo_block_bytes(int codec) {
     case KQO_IQ3_XXS: return 98; case KQO_IQ4_XS: return 136;
     case KQO_Q4_0: case KQO_IQ4_NL: return 144; /* eight 18-byte blocks per 256 weights */
     case KQO_Q2_K: return 84; case KQO_Q3_K: return 110;
+    case KQO_Q4_1: return 160; case KQO_Q5_0: return 176; case KQO_Q5_1: return 192; /* eight blocks */
     }
     return -1;
 }
@@ -219,17 +223,33 @@ static void deq_iq4xs(const uint8_t *b, float *o) {
     }
 }
 
-/* gguf-py Q4_0.dequantize_blocks (quants.py:241-251) and IQ4_NL's
- * (quants.py:1333-1348) over eight 18-byte blocks: d, then 16 bytes whose low
- * nibbles are weights 0-15 and high nibbles 16-31. */
-static void deq_q40_nl(const uint8_t *b, float *o, int nl) {
+/* The 32-weight legacy blocks over eight blocks (one 256-weight group):
+ * gguf-py Q4_0 (quants.py:241-251), Q4_1 (:254-276), Q5_0 (:279-305), Q5_1
+ * (:308-336) and IQ4_NL (:1333-1348).  A block is d (fp16), then m (fp16;
+ * Q4_1 / Q5_1), then a little-endian u32 of fifth bits (Q5_0 / Q5_1; bit j
+ * belongs to weight j), then 16 bytes whose low nibbles are weights 0-15 and
+ * high nibbles 16-31. */
+static void deq_legacy(int codec, const uint8_t *b, float *o) {
+    const int has_m = codec == KQO_Q4_1 || codec == KQO_Q5_1, has_h = codec == KQO_Q5_0 || codec == KQO_Q5_1;
+    const int bb = 18 + 2 * has_m + 4 * has_h;
     for (int j = 0; j < 8; j++) {
-        const uint8_t *blk = b + 18 * j;
+        const uint8_t *blk = b + bb * j;
         float d = kqo_half((uint16_t)(blk[0] | blk[1] << 8));
-        for (int l = 0; l < 16; l++) {
-            int lo = blk[2 + l] & 0x0f, hi = blk[2 + l] >> 4;
-            o[32 * j + l] = nl ? d * (float)kqo_iq4nl[lo] : d * (float)(lo - 8);
-            o[32 * j + 16 + l] = nl ? d * (float)kqo_iq4nl[hi] : d * (float)(hi - 8);
+        float m = has_m ? kqo_half((uint16_t)(blk[2] | blk[3] << 8)) : 0.0f;
+        uint32_t qh = 0;
+        if (has_h) memcpy(&qh, blk + 2 + 2 * has_m, 4);
+        const uint8_t *qs = blk + bb - 16;
+        for (int l = 0; l < 32; l++) {
+            int v = (qs[l & 15] >> (4 * (l >> 4))) & 0x0f;
+            if (has_h) v |= (int)((qh >> l) & 1) << 4;
+            float w;
+            switch (codec) {
+            case KQO_IQ4_NL: w = d * (float)kqo_iq4nl[v]; break;
+            case KQO_Q4_0: w = d * (float)(v - 8); break;
+            case KQO_Q5_0: w = d * (float)(v - 16); break;
+            default: w = d * (float)v + m; break; /* Q4_1, Q5_1 */
+            }
+            o[32 * j + l] = w;
         }
     }
 }
@@ -273,10 +293,9 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_IQ2_XXS: deq_iq2xxs(b, o); return 0;
     case KQO_IQ3_XXS: deq_iq3xxs(b, o); return 0;
     case KQO_IQ4_XS: deq_iq4xs(b, o); return 0;
-    case KQO_Q4_0: deq_q40_nl(b, o, 0); return 0;
+    case KQO_Q4_0: case KQO_Q4_1: case KQO_Q5_0: case KQO_Q5_1: case KQO_IQ4_NL: deq_legacy(codec, b, o); return 0;
     case KQO_Q2_K: deq_q2k(b, o); return 0;
     case KQO_Q3_K: deq_q3k(b, o); return 0;
-    case KQO_IQ4_NL: deq_q40_nl(b, o, 1); return 0;
     }
     return -1;
 }

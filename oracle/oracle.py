@@ -31,11 +31,13 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
-Q4_0, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 2, 8, 10, 11, 12, 13, 14, 16, 18, 20, 23
+Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K = 2, 3, 6, 7, 8, 10, 11
+Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 12, 13, 14, 16, 18, 20, 23
 CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
-             "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K}
+             "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K, "q4_1": Q4_1,
+             "q5_0": Q5_0, "q5_1": Q5_1}
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
-               Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110}  # per 256 weights
+               Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -220,16 +222,23 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         hb = (hm.reshape(n, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 8, 1)) & 1
         q = q2.reshape(n, 8, 32).astype(np.int16) - 4 * (1 - hb.astype(np.int16))
         out = (d * sc.reshape(n, 16, 1)) * q.reshape(n, 16, 16).astype(np.float32)
-    elif c in (Q4_0, IQ4_NL):  # quants.py:241-251 / 1333-1348: eight (fp16 d, 16 nibble bytes) blocks
-        sub = blocks.reshape(n * 8, 18)
+    elif c in (Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL):  # quants.py:241-336 / 1333-1348: eight 32-weight blocks
+        has_m, has_h = c in (Q4_1, Q5_1), c in (Q5_0, Q5_1)
+        bb = 18 + 2 * has_m + 4 * has_h
+        sub = blocks.reshape(n * 8, bb)
         d = _half(sub[:, 0:2]).reshape(n * 8, 1)
-        q = (sub[:, 2:].reshape(n * 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 2, 1)) & 15
-        q = q.reshape(n * 8, 32)
-        if c == Q4_0:
-            out = d * (q.astype(np.float32) - np.float32(8))
-        else:
+        q = (sub[:, bb - 16:].reshape(n * 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 2, 1)) & 15
+        q = q.reshape(n * 8, 32).astype(np.int32)
+        if has_h:
+            qh = sub[:, 2 + 2 * has_m:6 + 2 * has_m].copy().view(np.uint32).reshape(n * 8, 1)
+            q |= (((qh >> np.arange(32, dtype=np.uint32)) & 1) << 4).astype(np.int32)
+        if c == IQ4_NL:
             kv = np.array(_table_values("KQ_IQ4NL_VALUES_INIT"), np.float32)
             out = d * kv[q]
+        elif has_m:
+            out = d * q.astype(np.float32) + _half(sub[:, 2:4]).reshape(n * 8, 1)
+        else:
+            out = d * (q - (8 if c == Q4_0 else 16)).astype(np.float32)
     else:
         raise ValueError(codec)
     return out.reshape(*np.asarray(w).shape[:-1], -1).astype(np.float32)

@@ -19,6 +19,8 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
   IQ3_XXS the same sweep over its 256-entry grid;
   IQ4_XS  every nibble value, 6-bit scales 0 / 31 / 32 / 63, negative d;
   Q4_0    quants all 0 / all 15 / every value, d = 0, negative, 65504;
+  Q4_1, Q5_0, Q5_1  the same with m = 0 / negative / positive and the fifth
+          bits all clear / all set / alternating;
   IQ4_NL  every nibble value on every block, negative d;
   Q2_K    scale / min nibbles 0 and 15, quants all 0 / all 3, one-hot
           sub-block scales;
@@ -42,7 +44,7 @@ from gmlx_b200 import synth  # noqa: E402
 
 QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
       "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
-      "q3_k": T.Q3_K}
+      "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1}
 
 
 def fp16(v):
@@ -151,15 +153,24 @@ def edge_blocks(codec):
             b[0:32] = 1 << plane
             b[108:110] = fp16(-1e-3)
             blocks.append(b)
-    elif codec in ("q4_0", "iq4_nl"):  # 144-byte groups of eight 18-byte blocks
-        for dv, qv in [(1e-3, 0x00), (1e-3, 0xff), (0.0, None), (-2e-3, None), (65504.0, 0x88), (5e-4, None)]:
-            b = np.zeros((8, 18), np.uint8)
+    elif codec in ("q4_0", "iq4_nl", "q4_1", "q5_0", "q5_1"):  # groups of eight 32-weight blocks
+        has_m, has_h = codec in ("q4_1", "q5_1"), codec in ("q5_0", "q5_1")
+        bb = 18 + 2 * has_m + 4 * has_h
+        cases = [(1e-3, 0x00, 0.0, 0x00), (1e-3, 0xff, -0.02, 0xff), (0.0, None, 0.01, 0x55),
+                 (-2e-3, None, -1e-3, None), (65504.0, 0x88, 0.0, 0xaa), (5e-4, None, -0.5, None)]
+        for dv, qv, mv, hv in cases:
+            b = np.zeros((8, bb), np.uint8)
             b[:, 0:2] = fp16(dv)
+            if has_m:
+                b[:, 2:4] = fp16(mv)
+            if has_h:
+                o = 2 + 2 * has_m
+                b[:, o:o + 4] = rng.integers(0, 256, (8, 4), dtype=np.uint8) if hv is None else hv
             if qv is None:  # every nibble value in both halves
-                b[:, 2:] = (np.arange(16) | (((np.arange(16) + 5) % 16) << 4)).astype(np.uint8)
+                b[:, bb - 16:] = (np.arange(16) | (((np.arange(16) + 5) % 16) << 4)).astype(np.uint8)
             else:
-                b[:, 2:] = qv
-            blocks.append(b.reshape(144))
+                b[:, bb - 16:] = qv
+            blocks.append(b.reshape(8 * bb))
     elif codec == "iq4_xs":
         # every nibble value on every sub-block; 6-bit scales 0, 31, 32, 63
         for blk, (dv, ls) in enumerate([(1e-3, 0), (1e-3, 63), (-2e-3, 32), (5e-4, 31), (1e-3, None)]):

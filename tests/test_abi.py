@@ -29,18 +29,19 @@ def test_codecs_and_block_bytes():
     L = _lib.load()
     buf = (ctypes.c_int * 8)()
     buf = (ctypes.c_int * 12)()
-    assert L.kq_codecs(buf, 12) == 11
-    assert list(buf[:11]) == [12, 13, 14, 16, 8, 18, 23, 2, 20, 10, 11]
-    assert [L.kq_block_bytes(c) for c in (12, 13, 14, 16, 8, 18, 23, 2, 20, 10, 11, 3)] == [
-        144, 176, 210, 66, 272, 98, 136, 144, 144, 84, 110, -1]
-    assert L.kq_codec_has_matmul(12) == 1 and L.kq_codec_has_matmul(8) == 1 and L.kq_codec_has_matmul(3) == 0
+    buf = (ctypes.c_int * 16)()
+    assert L.kq_codecs(buf, 16) == 14
+    assert list(buf[:14]) == [12, 13, 14, 16, 8, 18, 23, 2, 20, 10, 11, 3, 6, 7]
+    assert [L.kq_block_bytes(c) for c in (12, 13, 14, 16, 8, 18, 23, 2, 20, 10, 11, 3, 6, 7, 1)] == [
+        144, 176, 210, 66, 272, 98, 136, 144, 144, 84, 110, 160, 176, 192, -1]
+    assert L.kq_codec_has_matmul(12) == 1 and L.kq_codec_has_matmul(8) == 1 and L.kq_codec_has_matmul(1) == 0
     assert L.kq_version() >= 100
 
 
 def test_validation_without_gpu():
     L = _lib.load()
     # unknown codec -> KQ_ERR_CODEC, message names the op (validated before any launch)
-    rc = L.kq_dequantize(3, None, 1, 256, 144, None, 0, None)
+    rc = L.kq_dequantize(1, None, 1, 256, 144, None, 0, None)
     assert rc == _lib.KQ_ERR_CODEC
     assert b"dequantize" in L.kq_last_error()
     rc = L.kq_dequantize(12, None, 1, 300, 144, None, 0, None)
@@ -56,4 +57,4 @@ def test_python_ops_fail_loudly_without_cuda():
     with pytest.raises(ValueError, match="CUDA"):
         kq.dequantize(w, None, "q4_k")
     with pytest.raises(NotImplementedError):
-        kq.dequantize(w, None, "q5_0")
+        kq.dequantize(w, None, "iq1_s")

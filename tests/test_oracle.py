@@ -9,7 +9,8 @@ from gmlx_b200 import synth
 from oracle import oracle as O
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
-CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs", "q4_0", "iq4_nl", "q2_k", "q3_k"]
+CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs", "q4_0", "iq4_nl", "q2_k", "q3_k", "q4_1",
+          "q5_0", "q5_1"]
 
 
 @pytest.fixture(scope="module")
@@ -46,7 +47,7 @@ def test_oracle_matches_gguf_py_random(codec, seed):
     from gguf.constants import GGMLQuantizationType as T
     qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
           "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
-          "q3_k": T.Q3_K}[codec]
+          "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1}[codec]
     w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
 
@@ -60,7 +61,8 @@ def test_raw_random_bytes_match_where_finite():
     for codec, qt, bpb in [("q4_k", T.Q4_K, 144), ("q5_k", T.Q5_K, 176), ("q6_k", T.Q6_K, 210),
                            ("iq2_xxs", T.IQ2_XXS, 66), ("q8_0", T.Q8_0, 272), ("iq3_xxs", T.IQ3_XXS, 98),
                            ("iq4_xs", T.IQ4_XS, 136), ("q4_0", T.Q4_0, 144), ("iq4_nl", T.IQ4_NL, 144),
-                           ("q2_k", T.Q2_K, 84), ("q3_k", T.Q3_K, 110)]:
+                           ("q2_k", T.Q2_K, 84), ("q3_k", T.Q3_K, 110), ("q4_1", T.Q4_1, 160),
+                           ("q5_0", T.Q5_0, 176), ("q5_1", T.Q5_1, 192)]:
         w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
         a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
         fin = np.isfinite(b)
@@ -119,8 +121,9 @@ def test_synthetic_block_statistics():
             d = w[:, 0:2].copy().view(np.float16).astype(np.float32)
             dm = w[:, 2:4].copy().view(np.float16).astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3 and dm.min() >= 9e-5
-        elif codec in ("q8_0", "q4_0", "iq4_nl"):
-            d = w.reshape(-1, 34 if codec == "q8_0" else 18)[:, 0:2].copy().view(np.float16).astype(np.float32)
+        elif codec in ("q8_0", "q4_0", "iq4_nl", "q4_1", "q5_0", "q5_1"):
+            d = w.reshape(-1, synth.BLOCK_BYTES[synth.codec_id(codec)] // 8)[:, 0:2].copy().view(np.float16)
+            d = d.astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3
         elif codec in ("q2_k", "q3_k"):
             off = 80 if codec == "q2_k" else 108
@@ -149,12 +152,15 @@ def test_q8_0_round_trip_through_gguf_quantizer():
     assert np.abs(O.dequantize(w, "q8_0") - wf).max() <= np.abs(wf).max() / 127
 
 
-def test_q4_0_round_trip_through_gguf_quantizer():
-    """gguf-py quantizes Q4_0 too: its blocks dequantize bit-identically here."""
+@pytest.mark.parametrize("codec,bb", [("q4_0", 18), ("q4_1", 20), ("q5_0", 22), ("q5_1", 24)])
+def test_legacy_round_trip_through_gguf_quantizer(codec, bb):
+    """gguf-py quantizes the legacy 32-weight codecs too: its blocks
+    dequantize bit-identically here."""
     from gguf import quants as gq
     from gguf.constants import GGMLQuantizationType as T
+    qt = {"q4_0": T.Q4_0, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1}[codec]
     rng = np.random.default_rng(10)
     wf = (rng.standard_normal((32, 1024)) * 0.02).astype(np.float32)
-    w = gq.quantize(wf, T.Q4_0)
-    assert w.shape == (32, 1024 // 32 * 18)
-    assert np.array_equal(bits(O.dequantize(w, "q4_0")), bits(gq.dequantize(w, T.Q4_0).astype(np.float32)))
+    w = gq.quantize(wf, qt)
+    assert w.shape == (32, 1024 // 32 * bb)
+    assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt).astype(np.float32)))
