@@ -400,21 +400,29 @@ def main():
     prefill = {}
     if not args.no_sweep:
         L0 = layers[0]
-        mats = [(L0["qkv"], "q4_k", 4096), (L0["o"], "q4_k", 4096), (L0["gate"], "q4_k", 4096),
-                (L0["up"], "q4_k", 4096), (L0["down"], "q6_k", 14336)]
-        flops_per_tok = sum(2 * w.shape[0] * k for w, _, k in mats)
+        # this rank's shards (tensor parallel: o and down split along K, the
+        # others along N); K from the wire row length
+        kof = {"q4_k": 144, "q6_k": 210}
+        mats = [(L0[n], c, L0[n].shape[1] // kof[c] * 256) for n, c in
+                (("qkv", "q4_k"), ("o", "q4_k"), ("gate", "q4_k"), ("up", "q4_k"), ("down", "q6_k"))]
+        flops_per_tok = sum(2 * w.shape[0] * k for w, _, k in mats)  # this rank's share
+        k_in, k_o, k_down = mats[0][2], mats[1][2], mats[4][2]
         for m in (512, 2048, 8192):
-            xs = {k: torch.randn(m, k, device=dev).to(torch.bfloat16) for k in (4096, 14336)}
+            xs = {k: torch.randn(m, k, device=dev).to(torch.bfloat16) for k in {k_in, k_o, k_down}}
 
             def pf():  # gate/up/SiLU*up fused in one tcgen05 GEMM (two accumulators per tile)
-                kq.quantized_matmul(xs[4096], L0["qkv"], None, "q4_k")
-                kq.quantized_matmul(xs[4096], L0["o"], None, "q4_k")
-                kq.quantized_glu(xs[4096], L0["gate"], L0["up"], "q4_k", act="silu")
-                kq.quantized_matmul(xs[14336], L0["down"], None, "q6_k")
+                kq.quantized_matmul(xs[k_in], L0["qkv"], None, "q4_k")
+                kq.quantized_matmul(xs[k_o], L0["o"], None, "q4_k")
+                kq.quantized_glu(xs[k_in], L0["gate"], L0["up"], "q4_k", act="silu")
+                kq.quantized_matmul(xs[k_down], L0["down"], None, "q6_k")
             reps = 3 if m == 8192 else 6
             t = time_graph(torch, pf, reps, 1, stream) / reps
-            prefill[f"m{m}"] = {"ms": t * 1e3, "TFLOP/s": flops_per_tok * m / t / 1e12,
-                                "frac_tensor": flops_per_tok * m / t / 1e12 / tc_peak}
+            if dd is not None:  # slowest rank; every rank computes its own shard
+                tt = torch.tensor([t], device=dev)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                t = float(tt.item())
+            tflops = flops_per_tok * world * m / t / 1e12  # whole job
+            prefill[f"m{m}"] = {"ms": t * 1e3, "TFLOP/s": tflops, "frac_tensor": tflops / world / tc_peak}
 
     moe = {} if args.no_moe else run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak)
 
