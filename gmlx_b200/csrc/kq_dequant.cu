@@ -42,6 +42,11 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
 #pragma unroll
         for (int i = 0; i < 8; i++)
             o[i] = dl * (float)(((q[i] >> (4 * h)) & 15) | (((qh[i] >> j) & 1) << 4)) - ml;
+    } else if constexpr (C == TQ2_0) {  // lane: weights 8 lane .. +7
+        const int w0 = 8 * lane, h = w0 >> 7, k = (w0 >> 5) & 3, l0 = w0 & 31;
+        const float d = half_bits_to_float(ld_u16(b + 64));
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = d * (float)(((b[32 * h + l0 + i] >> (2 * k)) & 3) - 1);
     } else if constexpr (C == Q2_K || C == Q3_K) {  // lane: weights 8 lane .. +7 (one 16-weight sub-block)
         const int w0 = 8 * lane, h = w0 >> 7, k = (w0 >> 5) & 3, l0 = w0 & 31, j = w0 >> 4;
         float dl, ml = 0.f;
@@ -63,16 +68,17 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
     } else if constexpr (Legacy<C>::IS) {  // lane: 8 weights of ggml block lane / 4
         using LG = Legacy<C>;
         const uint8_t *blk = b + LG::BB * (lane >> 2);
-        const float d = half_bits_to_float(ld_u16(blk));
+        const float d = LG::MX ? e8m0_half(blk[0]) : half_bits_to_float(ld_u16(blk));
         const float m = LG::HASM ? half_bits_to_float(ld_u16(blk + 2)) : 0.f;
-        const uint32_t qh = LG::HASH ? ld_u32_unaligned(blk + (LG::HASM ? 4 : 2)) : 0u;
+        const uint32_t qh = LG::HASH ? ld_u32_unaligned(blk + LG::HOFF) : 0u;
         const int i0 = 8 * (lane & 3), h = i0 >> 4;
-        const uint8_t *q = blk + LG::BB - 16 + (i0 & 15);
+        const uint8_t *q = blk + LG::QOFF + (i0 & 15);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             int v = (q[i] >> (4 * h)) & 15;
             if constexpr (LG::HASH) v |= (int)((qh >> (i0 + i)) & 1u) << 4;
-            if constexpr (LG::NL) o[i] = d * (float)c_iq4nl_values[v];
+            if constexpr (LG::MX) o[i] = d * (float)c_mxfp4_values[v];
+            else if constexpr (LG::NL) o[i] = d * (float)c_iq4nl_values[v];
             else if constexpr (LG::HASM) o[i] = __fadd_rn(__fmul_rn(d, (float)v), m);  // gguf order: d*q + m
             else o[i] = d * (float)(v - LG::OFF);
         }
@@ -306,6 +312,8 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q4_0: return launch_deq<Q4_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q4_1: return launch_deq<Q4_1>(w, rows, nb, row_stride, out, dtype, st);
+    case MXFP4: return launch_deq<MXFP4>(w, rows, nb, row_stride, out, dtype, st);
+    case TQ2_0: return launch_deq<TQ2_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_0: return launch_deq<Q5_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_1: return launch_deq<Q5_1>(w, rows, nb, row_stride, out, dtype, st);
     case Q2_K: return launch_deq<Q2_K>(w, rows, nb, row_stride, out, dtype, st);

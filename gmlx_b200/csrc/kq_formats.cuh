@@ -25,6 +25,9 @@
 //   Q5_0  8 x 22 B  (d | u32 qh | 16 B), w = d*(q-16)     quants.py:279-305
 //   Q5_1  8 x 24 B  (d | m | u32 qh | 16 B), w = d*q + m  quants.py:308-336
 //         (Q5: q = nibble | (qh bit j) << 4 for weight j)
+//   MXFP4 8 x 17 B  (e8m0 e | 16 B nibbles), w = 2^(e-128) * kvalues[q]
+//                (kvalues: doubled e2m1; MXFP4.dequantize_blocks)
+//   TQ2_0 66 B   64 B 2-bit q (Q2_K's layout) | d f16, w = d*(q-1)
 //   Q2_K  84 B   16 x (sc | m << 4) | 64 B 2-bit q | d f16 | dmin f16
 //                w = (d*sc_j)*q - (dmin*m_j), 16-weight j   quants.py:404-428
 //   Q3_K  110 B  32 B high bits | 64 B 2-bit q | 12 B 6-bit scales | d f16
@@ -47,7 +50,7 @@
 namespace kq {
 
 enum Codec : int {
-    Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
+    Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, TQ2_0 = 35, MXFP4 = 39, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
@@ -66,15 +69,26 @@ template <> struct Fmt<IQ4_NL> { static constexpr int bpb = 144; static constexp
 template <> struct Fmt<Q4_1> { static constexpr int bpb = 160; static constexpr int sub = 32; };
 template <> struct Fmt<Q5_0> { static constexpr int bpb = 176; static constexpr int sub = 32; };
 template <> struct Fmt<Q5_1> { static constexpr int bpb = 192; static constexpr int sub = 32; };
+template <> struct Fmt<MXFP4> { static constexpr int bpb = 136; static constexpr int sub = 32; };
+template <> struct Fmt<TQ2_0> { static constexpr int bpb = 66; static constexpr int sub = 32; };
 
-// The 32-weight legacy blocks: d (fp16), m (fp16; HASM), a u32 of fifth bits
-// (HASH), then 16 nibble bytes; BB bytes per block, OFF subtracted from q.
+// The 32-weight legacy blocks: d (fp16; MXFP4: one e8m0 byte), m (fp16;
+// HASM), a u32 of fifth bits (HASH), then 16 nibble bytes; BB bytes per
+// block, OFF subtracted from q; NL / MX: nibbles index a value table.
 template <int C> struct Legacy {
-    static constexpr bool IS = C == Q4_0 || C == Q4_1 || C == Q5_0 || C == Q5_1 || C == IQ4_NL;
-    static constexpr bool HASM = C == Q4_1 || C == Q5_1, HASH = C == Q5_0 || C == Q5_1, NL = C == IQ4_NL;
-    static constexpr int BB = 18 + (HASM ? 2 : 0) + (HASH ? 4 : 0);
+    static constexpr bool IS = C == Q4_0 || C == Q4_1 || C == Q5_0 || C == Q5_1 || C == IQ4_NL || C == MXFP4;
+    static constexpr bool HASM = C == Q4_1 || C == Q5_1, HASH = C == Q5_0 || C == Q5_1;
+    static constexpr bool MX = C == MXFP4, NL = C == IQ4_NL || C == MXFP4;
+    static constexpr int BB = (MX ? 17 : 18) + (HASM ? 2 : 0) + (HASH ? 4 : 0);
+    static constexpr int HOFF = HASM ? 4 : 2;  // fifth bits
+    static constexpr int QOFF = BB - 16;       // nibble bytes
     static constexpr int OFF = C == Q4_0 ? 8 : C == Q5_0 ? 16 : 0;
 };
+
+// ggml's e8m0 "half" scale: 2^(e-128) as f32 bits (e < 2: subnormal)
+__device__ __forceinline__ float e8m0_half(uint32_t e) {
+    return __uint_as_float(e < 2 ? (0x00200000u << e) : ((e - 1) << 23));
+}
 template <> struct Fmt<Q2_K> { static constexpr int bpb = 84; static constexpr int sub = 16; };
 template <> struct Fmt<Q3_K> { static constexpr int bpb = 110; static constexpr int sub = 16; };
 template <> struct Fmt<Q6_K> { static constexpr int bpb = 210; static constexpr int sub = 16; };
@@ -85,7 +99,7 @@ template <> struct Fmt<IQ4_XS> { static constexpr int bpb = 136; static constexp
 __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
-         : codec == Q4_1 ? 160 : codec == Q5_0 ? 176 : codec == Q5_1 ? 192
+         : codec == Q4_1 ? 160 : codec == Q5_0 ? 176 : codec == Q5_1 ? 192 : codec == MXFP4 ? 136 : codec == TQ2_0 ? 66
          : codec == Q2_K ? 84 : codec == Q3_K ? 110 : -1;
 }
 
@@ -95,6 +109,8 @@ static __device__ __constant__ uint64_t c_iq2xxs_grid[256] = KQ_IQ2XXS_GRID_INIT
 static __device__ __constant__ uint32_t c_iq3xxs_grid[256] = KQ_IQ3XXS_GRID_INIT;
 // The sixteen IQ4_NL values an IQ4_XS nibble selects, as bytes of four words.
 static __device__ __constant__ __align__(16) int8_t c_iq4nl_values[16] = KQ_IQ4NL_VALUES_INIT;
+// MXFP4's doubled e2m1 values, as bytes of four words.
+static __device__ __constant__ __align__(16) int8_t c_mxfp4_values[16] = KQ_MXFP4_VALUES_INIT;
 
 // ggml's 7-bit -> 8-bit sign expansion: bit 7 restores even parity.
 __device__ __forceinline__ uint32_t ksigns(uint32_t i7) {

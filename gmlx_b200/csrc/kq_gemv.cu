@@ -61,6 +61,8 @@ template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; 
 template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
 template <> struct GCfg<Q2_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q3_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<MXFP4> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
+template <> struct GCfg<TQ2_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<Q4_1> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q5_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q5_1> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
@@ -991,9 +993,12 @@ template <int C> __device__ __forceinline__ void dp_leg_load(const uint8_t *grp,
 #pragma unroll
     for (int s = 0; s < LEG_NB<C>; s++) {
         const uint8_t *blk = grp + LG::BB * s;
-        r.d[s] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk));
+        if constexpr (LG::MX)
+            r.d[s] = e8m0_half(blk[0]);
+        else
+            r.d[s] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk));
         if constexpr (LG::HASM) r.m[s] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk + 2));
-        const uintptr_t hb = (uintptr_t)(blk + (LG::HASM ? 4 : 2));
+        const uintptr_t hb = (uintptr_t)(blk + (LG::HASH ? LG::HOFF : LG::QOFF));
         const uint32_t *aw = reinterpret_cast<const uint32_t *>(hb & ~(uintptr_t)3);
         const uint32_t sh = (uint32_t)(hb & 3) * 8;
         if constexpr (LG::HASH) {
@@ -1016,7 +1021,7 @@ __device__ __forceinline__ float dp_leg_dot(const LegRegs<C> &r, const uint32_t 
     using LG = Legacy<C>;
     uint32_t tv[4] = {0u, 0u, 0u, 0u};
     if constexpr (LG::NL) {
-        const uint32_t *tw = reinterpret_cast<const uint32_t *>(c_iq4nl_values);
+        const uint32_t *tw = reinterpret_cast<const uint32_t *>(LG::MX ? c_mxfp4_values : c_iq4nl_values);
         tv[0] = tw[0], tv[1] = tw[1], tv[2] = tw[2], tv[3] = tw[3];
     }
     float acc = 0.f;
@@ -1100,6 +1105,46 @@ __device__ __forceinline__ float dp_q2k_dot(const Q2Regs &r, const uint32_t *xq,
         }
     __syncwarp();  // xq is rewritten for the next block
     return acc;
+}
+
+// Lane-per-row TQ2_0: Q2_K's quant layout with one fp16 d per block (66 bytes,
+// 2-byte aligned); per 32-weight group g: acc += d (dx S_g - dx sum_g(x_q)).
+struct TQ2Regs {
+    uint32_t q[16];
+    float d;
+};
+
+__device__ __forceinline__ void dp_tq2_load(const uint8_t *blk, TQ2Regs &r) {
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    uint32_t w[18];
+#pragma unroll
+    for (int i = 0; i < 18; i++) w[i] = aw[i];  // up to 6 bytes past the block: the ring row has slack
+#pragma unroll
+    for (int i = 0; i < 16; i++) r.q[i] = __funnelshift_r(w[i], w[i + 1], sh);
+    r.d = half_bits_to_float(__funnelshift_r(w[16], w[17], sh) & 0xffffu);
+}
+
+__device__ __forceinline__ float dp_tq2_dot(const TQ2Regs &r, const uint32_t *xq, const float *xsc) {
+    float acc = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            int sum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int q = (int)((r.q[8 * h + i] >> (2 * k)) & 0x03030303u);
+                const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 64 * h + 16 * k + 2 * i);
+                sum = __dp2a_lo((int)xv.x, q, sum);
+                sum = __dp2a_hi((int)xv.y, q, sum);
+            }
+            const int g = 4 * h + k;
+            acc = fmaf(xsc[g], (float)sum, acc - xsc[8 + g]);
+        }
+    __syncwarp();  // xq is rewritten for the next block
+    return r.d * acc;
 }
 
 struct Q3Regs {
@@ -1429,6 +1474,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q2k_dot(r, xq, xsc);
+        } else if constexpr (C == TQ2_0) {
+            TQ2Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_tq2_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_tq2_dot(r, xq, xsc);
         } else if constexpr (C == Q3_K) {
             Q3Regs r;
             if (run) {
@@ -1990,6 +2044,8 @@ cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == Q8_0) return launch_onerow_c<Q8_0>(a, st, grid_out);
     if (a.codec == Q4_0) return launch_onerow_c<Q4_0>(a, st, grid_out);
     if (a.codec == Q4_1) return launch_onerow_c<Q4_1>(a, st, grid_out);
+    if (a.codec == MXFP4) return launch_onerow_c<MXFP4>(a, st, grid_out);
+    if (a.codec == TQ2_0) return launch_onerow_c<TQ2_0>(a, st, grid_out);
     if (a.codec == Q5_0) return launch_onerow_c<Q5_0>(a, st, grid_out);
     if (a.codec == Q5_1) return launch_onerow_c<Q5_1>(a, st, grid_out);
     if (a.codec == Q2_K) return launch_onerow_c<Q2_K>(a, st, grid_out);

@@ -26,6 +26,8 @@
  *   IQ4_NL (quants.py:1333-1348): w = d*kvalues[q] per 32-weight block
  *   Q4_1   (quants.py:254-276): w = d*q + m;  Q5_0 (:279-305): w = d*(q-16);
  *   Q5_1   (:308-336): w = d*q + m  (Q5: q = nibble | qh bit << 4)
+ *   MXFP4  (MXFP4.dequantize_blocks): w = e8m0_half(e) * kvalues[q] per 32 weights
+ *   TQ2_0  (TQ2_0.dequantize_blocks): w = d*(q-1), q 2-bit, Q2_K's quant layout
  * Every product above is exact in f32 (see the kernels' header), so results
  * are independent of FMA contraction; the file is still built with
  * -ffp-contract=off to keep the statement literal.
@@ -43,11 +45,12 @@
 #define QK 256
 enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
        KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11,
-       KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7 };
+       KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7, KQO_TQ2_0 = 35, KQO_MXFP4 = 39 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
 static const int8_t kqo_iq4nl[16] = KQ_IQ4NL_VALUES_INIT;
+static const int8_t kqo_mxfp4[16] = KQ_MXFP4_VALUES_INIT;
 
 /* IEEE binary16 -> f32, exact (gguf-py: view(np.float16).astype(np.float32)). */
 static float kqo_half(uint16_t h) {
@@ -77,6 +80,8 @@ int kqo_block_bytes(int codec) {
     case KQO_Q4_0: case KQO_IQ4_NL: return 144; /* eight 18-byte blocks per 256 weights */
     case KQO_Q2_K: return 84; case KQO_Q3_K: return 110;
     case KQO_Q4_1: return 160; case KQO_Q5_0: return 176; case KQO_Q5_1: return 192; /* eight blocks */
+    case KQO_MXFP4: return 136; /* eight 17-byte blocks */
+    case KQO_TQ2_0: return 66;
     }
     return -1;
 }
@@ -284,6 +289,33 @@ static void deq_q3k(const uint8_t *b, float *o) {
     }
 }
 
+/* ggml's e8m0 -> f32 "half" scale (gguf-py MXFP4.e8m0_to_fp32_half): 2^(e-128)
+ * as bits, with e < 2 as subnormals. */
+static float kqo_e8m0_half(uint8_t e) {
+    uint32_t u = e < 2 ? (0x00200000u << e) : ((uint32_t)(e - 1) << 23);
+    float f; memcpy(&f, &u, 4); return f;
+}
+
+/* gguf-py MXFP4.dequantize_blocks over eight 17-byte blocks: e, then 16 bytes
+ * (low nibbles weights 0-15, high 16-31) indexing the doubled e2m1 values. */
+static void deq_mxfp4(const uint8_t *b, float *o) {
+    for (int j = 0; j < 8; j++) {
+        const uint8_t *blk = b + 17 * j;
+        float d = kqo_e8m0_half(blk[0]);
+        for (int l = 0; l < 32; l++) o[32 * j + l] = d * (float)kqo_mxfp4[(blk[1 + (l & 15)] >> (4 * (l >> 4))) & 15];
+    }
+}
+
+/* gguf-py TQ2_0.dequantize_blocks: 64 bytes of 2-bit values laid out as
+ * Q2_K's quants, then d; w = d * (q - 1). */
+static void deq_tq20(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[64] | b[65] << 8));
+    for (int w = 0; w < 256; w++) {
+        int h = w >> 7, k = (w >> 5) & 3, l = w & 31;
+        o[w] = d * (float)(((b[32 * h + l] >> (2 * k)) & 3) - 1);
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -295,6 +327,8 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_IQ4_XS: deq_iq4xs(b, o); return 0;
     case KQO_Q4_0: case KQO_Q4_1: case KQO_Q5_0: case KQO_Q5_1: case KQO_IQ4_NL: deq_legacy(codec, b, o); return 0;
     case KQO_Q2_K: deq_q2k(b, o); return 0;
+    case KQO_MXFP4: deq_mxfp4(b, o); return 0;
+    case KQO_TQ2_0: deq_tq20(b, o); return 0;
     case KQO_Q3_K: deq_q3k(b, o); return 0;
     }
     return -1;

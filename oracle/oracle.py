@@ -31,13 +31,14 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
-Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K = 2, 3, 6, 7, 8, 10, 11
+Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, TQ2_0, MXFP4 = 2, 3, 6, 7, 8, 10, 11, 35, 39
 Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 12, 13, 14, 16, 18, 20, 23
 CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
              "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K, "q4_1": Q4_1,
-             "q5_0": Q5_0, "q5_1": Q5_1}
+             "q5_0": Q5_0, "q5_1": Q5_1, "tq2_0": TQ2_0, "mxfp4": MXFP4}
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
-               Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192}  # per 256 weights
+               Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192,
+               TQ2_0: 66, MXFP4: 136}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -222,6 +223,17 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         hb = (hm.reshape(n, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 8, 1)) & 1
         q = q2.reshape(n, 8, 32).astype(np.int16) - 4 * (1 - hb.astype(np.int16))
         out = (d * sc.reshape(n, 16, 1)) * q.reshape(n, 16, 16).astype(np.float32)
+    elif c == MXFP4:  # MXFP4.dequantize_blocks: eight (e8m0 e, 16 nibble bytes) blocks
+        sub = blocks.reshape(n * 8, 17)
+        e = sub[:, 0].astype(np.uint32)
+        bits_ = np.where(e < 2, np.uint32(0x00200000) << e, (e - 1) << np.uint32(23)).astype(np.uint32)
+        d = bits_.view(np.float32).reshape(n * 8, 1)
+        q = ((sub[:, 1:].reshape(n * 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 2, 1)) & 15).reshape(n * 8, 32)
+        out = d * np.array(_table_values("KQ_MXFP4_VALUES_INIT"), np.float32)[q]
+    elif c == TQ2_0:  # TQ2_0.dequantize_blocks
+        d = _half(blocks[:, 64:66]).reshape(n, 1)
+        q = (blocks[:, 0:64].reshape(n, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
+        out = d * (q.reshape(n, 256).astype(np.float32) - np.float32(1))
     elif c in (Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL):  # quants.py:241-336 / 1333-1348: eight 32-weight blocks
         has_m, has_h = c in (Q4_1, Q5_1), c in (Q5_0, Q5_1)
         bb = 18 + 2 * has_m + 4 * has_h

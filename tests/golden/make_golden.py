@@ -21,6 +21,8 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
   Q4_0    quants all 0 / all 15 / every value, d = 0, negative, 65504;
   Q4_1, Q5_0, Q5_1  the same with m = 0 / negative / positive and the fifth
           bits all clear / all set / alternating;
+  MXFP4   every nibble value, exponents 0, 1 (subnormal scales), 2, 127, 140;
+  TQ2_0   values all 0 / 1 / 2 / 3 (3 is outside the ternary set but decodes), d < 0;
   IQ4_NL  every nibble value on every block, negative d;
   Q2_K    scale / min nibbles 0 and 15, quants all 0 / all 3, one-hot
           sub-block scales;
@@ -44,7 +46,8 @@ from gmlx_b200 import synth  # noqa: E402
 
 QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
       "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
-      "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1}
+      "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1, "tq2_0": T.TQ2_0,
+      "mxfp4": T.MXFP4}
 
 
 def fp16(v):
@@ -152,6 +155,18 @@ def edge_blocks(codec):
             b = rng.integers(0, 256, 110, dtype=np.uint8)
             b[0:32] = 1 << plane
             b[108:110] = fp16(-1e-3)
+            blocks.append(b)
+    elif codec == "mxfp4":
+        for ev in (0, 1, 2, 127, 140, None):
+            b = np.zeros((8, 17), np.uint8)
+            b[:, 0] = rng.integers(110, 130, 8) if ev is None else ev
+            b[:, 1:] = (np.arange(16) | (((np.arange(16) + 3) % 16) << 4)).astype(np.uint8)
+            blocks.append(b.reshape(136))
+    elif codec == "tq2_0":
+        for qv, dv in [(0x00, 1e-3), (0x55, 1e-3), (0xaa, -2e-3), (0xff, 5e-4), (None, 1.5e-3)]:
+            b = np.zeros(66, np.uint8)
+            b[0:64] = rng.integers(0, 256, 64, dtype=np.uint8) if qv is None else qv
+            b[64:66] = fp16(dv)
             blocks.append(b)
     elif codec in ("q4_0", "iq4_nl", "q4_1", "q5_0", "q5_1"):  # groups of eight 32-weight blocks
         has_m, has_h = codec in ("q4_1", "q5_1"), codec in ("q5_0", "q5_1")
