@@ -42,6 +42,39 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
 #pragma unroll
         for (int i = 0; i < 8; i++)
             o[i] = dl * (float)(((q[i] >> (4 * h)) & 15) | (((qh[i] >> j) & 1) << 4)) - ml;
+    } else if constexpr (C == IQ2_XS || C == IQ2_S) {  // lane: grid entry lane (8 weights)
+        const int e = lane;
+        const float d = half_bits_to_float(ld_u16(b));
+        uint32_t sg;
+        uint64_t g;
+        int s;
+        if constexpr (C == IQ2_XS) {
+            const uint32_t v = ld_u16(b + 2 + 2 * e);
+            sg = ksigns(v >> 9);
+            g = c_iq2xs_grid[v & 511];
+            s = (b[66 + (e >> 2)] >> (4 * ((e >> 1) & 1))) & 15;
+        } else {
+            const uint32_t idx = b[2 + e] | (((b[66 + (e >> 2)] >> (2 * (e & 3))) & 3u) << 8);
+            sg = b[34 + e];
+            g = c_iq2s_grid[idx];
+            s = (b[74 + (e >> 2)] >> (4 * ((e >> 1) & 1))) & 15;
+        }
+        const float db = d * (0.5f + (float)s) * 0.25f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = db * (float)((g >> (8 * i)) & 255u) * (((sg >> i) & 1u) ? -1.0f : 1.0f);
+    } else if constexpr (C == IQ3_S) {  // lane: grid entries 2 lane, 2 lane + 1 (8 weights)
+        const float d = half_bits_to_float(ld_u16(b));
+        const int s = (b[106 + (lane >> 3)] >> (4 * ((lane >> 2) & 1))) & 15;
+        const float db = d * (float)(1 + 2 * s);
+        const uint32_t sg = b[74 + lane];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int e = 2 * lane + h;
+            const uint32_t g = c_iq3s_grid[b[2 + e] | (((b[66 + (e >> 3)] >> (e & 7)) & 1u) << 8)];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                o[4 * h + i] = db * (float)((g >> (8 * i)) & 255u) * (((sg >> (4 * h + i)) & 1u) ? -1.0f : 1.0f);
+        }
     } else if constexpr (C == TQ2_0) {  // lane: weights 8 lane .. +7
         const int w0 = 8 * lane, h = w0 >> 7, k = (w0 >> 5) & 3, l0 = w0 & 31;
         const float d = half_bits_to_float(ld_u16(b + 64));
@@ -314,6 +347,9 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case Q4_1: return launch_deq<Q4_1>(w, rows, nb, row_stride, out, dtype, st);
     case MXFP4: return launch_deq<MXFP4>(w, rows, nb, row_stride, out, dtype, st);
     case TQ2_0: return launch_deq<TQ2_0>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ2_XS: return launch_deq<IQ2_XS>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ2_S: return launch_deq<IQ2_S>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ3_S: return launch_deq<IQ3_S>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_0: return launch_deq<Q5_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_1: return launch_deq<Q5_1>(w, rows, nb, row_stride, out, dtype, st);
     case Q2_K: return launch_deq<Q2_K>(w, rows, nb, row_stride, out, dtype, st);

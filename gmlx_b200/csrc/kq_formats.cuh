@@ -28,6 +28,11 @@
 //   MXFP4 8 x 17 B  (e8m0 e | 16 B nibbles), w = 2^(e-128) * kvalues[q]
 //                (kvalues: doubled e2m1; MXFP4.dequantize_blocks)
 //   TQ2_0 66 B   64 B 2-bit q (Q2_K's layout) | d f16, w = d*(q-1)
+//   IQ2_XS 74 B  d | 32 x u16 (9-bit grid index, 7-bit sign index) | 8 B scales
+//                w = d*(0.5+s)*0.25 * grid * sign (s per 16 weights)
+//   IQ2_S 82 B   d | 32 B index lo | 32 B signs | 8 B index hi (2 bits) | 8 B scales
+//   IQ3_S 110 B  d | 64 B index lo | 8 B index hi (1 bit) | 32 B signs | 4 B scales
+//                w = d*(1+2s) * grid * sign (s per 32 weights)
 //   Q2_K  84 B   16 x (sc | m << 4) | 64 B 2-bit q | d f16 | dmin f16
 //                w = (d*sc_j)*q - (dmin*m_j), 16-weight j   quants.py:404-428
 //   Q3_K  110 B  32 B high bits | 64 B 2-bit q | 12 B 6-bit scales | d f16
@@ -50,7 +55,8 @@
 namespace kq {
 
 enum Codec : int {
-    Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, TQ2_0 = 35, MXFP4 = 39, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ3_XXS = 18, IQ4_NL = 20, IQ4_XS = 23
+    Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, TQ2_0 = 35, MXFP4 = 39, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ2_XS = 17, IQ3_XXS = 18, IQ4_NL = 20,
+    IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23
 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
@@ -71,6 +77,9 @@ template <> struct Fmt<Q5_0> { static constexpr int bpb = 176; static constexpr 
 template <> struct Fmt<Q5_1> { static constexpr int bpb = 192; static constexpr int sub = 32; };
 template <> struct Fmt<MXFP4> { static constexpr int bpb = 136; static constexpr int sub = 32; };
 template <> struct Fmt<TQ2_0> { static constexpr int bpb = 66; static constexpr int sub = 32; };
+template <> struct Fmt<IQ2_XS> { static constexpr int bpb = 74; static constexpr int sub = 16; };
+template <> struct Fmt<IQ2_S> { static constexpr int bpb = 82; static constexpr int sub = 16; };
+template <> struct Fmt<IQ3_S> { static constexpr int bpb = 110; static constexpr int sub = 32; };
 
 // The 32-weight legacy blocks: d (fp16; MXFP4: one e8m0 byte), m (fp16;
 // HASM), a u32 of fifth bits (HASH), then 16 nibble bytes; BB bytes per
@@ -100,6 +109,7 @@ __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
          : codec == Q4_1 ? 160 : codec == Q5_0 ? 176 : codec == Q5_1 ? 192 : codec == MXFP4 ? 136 : codec == TQ2_0 ? 66
+         : codec == IQ2_XS ? 74 : codec == IQ2_S ? 82 : codec == IQ3_S ? 110
          : codec == Q2_K ? 84 : codec == Q3_K ? 110 : -1;
 }
 
@@ -109,6 +119,10 @@ static __device__ __constant__ uint64_t c_iq2xxs_grid[256] = KQ_IQ2XXS_GRID_INIT
 static __device__ __constant__ uint32_t c_iq3xxs_grid[256] = KQ_IQ3XXS_GRID_INIT;
 // The sixteen IQ4_NL values an IQ4_XS nibble selects, as bytes of four words.
 static __device__ __constant__ __align__(16) int8_t c_iq4nl_values[16] = KQ_IQ4NL_VALUES_INIT;
+// IQ2_XS (512 x 8), IQ2_S (1024 x 8) and IQ3_S (512 x 4) grids, byte i = |w_i|.
+static __device__ __constant__ uint64_t c_iq2xs_grid[512] = KQ_IQ2XS_GRID_INIT;
+static __device__ __constant__ uint64_t c_iq2s_grid[1024] = KQ_IQ2S_GRID_INIT;
+static __device__ __constant__ uint32_t c_iq3s_grid[512] = KQ_IQ3S_GRID_INIT;
 // MXFP4's doubled e2m1 values, as bytes of four words.
 static __device__ __constant__ __align__(16) int8_t c_mxfp4_values[16] = KQ_MXFP4_VALUES_INIT;
 

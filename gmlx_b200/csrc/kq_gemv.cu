@@ -61,6 +61,9 @@ template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; 
 template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
 template <> struct GCfg<Q2_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q3_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<IQ2_XS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
+template <> struct GCfg<IQ2_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
+template <> struct GCfg<IQ3_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<MXFP4> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<TQ2_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<Q4_1> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
@@ -72,8 +75,10 @@ template <> struct GCfg<Q6_K> { static constexpr int TABW = 16 * 8 * 2, BPW = 1;
 template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 2; };  // db x 2 rows
 template <> struct GCfg<IQ3_XXS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };  // lane-per-row path only
 template <> struct GCfg<IQ4_XS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
-// shared-memory lattice table: IQ2_XXS 256 x 16 B (MMA path) or 8 B; IQ3_XXS 256 x 4 B
-template <int C> constexpr int GRIDB = C == IQ2_XXS ? 4096 : C == IQ3_XXS ? 1024 : 0;
+// shared-memory lattice table: IQ2_XXS 256 x 16 B (MMA path) or 8 B; IQ3_XXS 256 x 4 B;
+// IQ2_XS 512 x 8 B; IQ2_S 1024 x 8 B; IQ3_S 512 x 4 B
+template <int C> constexpr int GRIDB = C == IQ2_XXS ? 4096 : C == IQ3_XXS ? 1024 : C == IQ2_XS ? 4096 : C == IQ2_S ? 8192
+                                     : C == IQ3_S ? 2048 : 0;
 template <int C> constexpr int KB_OF = NCOL * GCfg<C>::BPW;
 template <int C> constexpr int XSTR_OF = KB_OF<C> * QK * 2 + 64;  // staged activation row stride (bytes)
 constexpr int SMEM_BUDGET = 112 * 1024;  // per CTA: two CTAs per SM
@@ -1107,6 +1112,93 @@ __device__ __forceinline__ float dp_q2k_dot(const Q2Regs &r, const uint32_t *xq,
     return acc;
 }
 
+// Lane-per-row IQ2_XS / IQ2_S / IQ3_S: as IQ2_XXS, the lane's block (2-byte
+// aligned) is realigned into IQS_NW words of block bytes 2 + 4j; each group of
+// 8 weights becomes two words of signed grid bytes dotted against the int16
+// activations, and each scale is applied once per 16 (IQ2_XS / IQ2_S) or 32
+// (IQ3_S) weights.  Word map (block byte 2 + 4j):
+//   IQ2_XS: j 0-15 u16 entries, 16-17 scales
+//   IQ2_S:  j 0-7 index low bytes, 8-15 sign bytes, 16-17 index high bits, 18-19 scales
+//   IQ3_S:  j 0-15 index low bytes, 16-17 index high bits, 18-25 sign bytes, 26 scales
+template <int C> constexpr int IQS_NW = C == IQ3_S ? 27 : C == IQ2_S ? 20 : 18;
+template <int C> struct IQSRegs {
+    uint32_t q[IQS_NW<C>];
+    float d;
+};
+
+template <int C> __device__ __forceinline__ void dp_iqs_load(const uint8_t *blk, IQSRegs<C> &r) {
+    constexpr int NW = IQS_NW<C>;
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    uint32_t w[NW + 1];
+#pragma unroll
+    for (int i = 0; i < NW + 1; i++) w[i] = aw[i];  // up to 2 bytes past the block: the ring row has slack
+    r.d = half_bits_to_float(__funnelshift_r(w[0], w[1], sh) & 0xffffu);
+#pragma unroll
+    for (int j = 0; j < NW; j++) r.q[j] = sh ? w[j + 1] : __funnelshift_r(w[j], w[j + 1], 16);
+}
+
+// signed grid bytes of 4 weights: magnitudes g (each < 128), sign bits sb (bits 0-3)
+__device__ __forceinline__ int signed4(uint32_t g, uint32_t sb) {
+    const uint32_t f = ((sb & 15u) * 0x00204081u) & 0x01010101u;
+    return (int)((g ^ (f * 0xffu)) + f);
+}
+
+template <int C>
+__device__ __forceinline__ float dp_iqs_dot(const IQSRegs<C> &r, const uint32_t *xq, const float *xsc,
+                                           const uint2 *grid8, const uint32_t *grid4) {
+    float acc = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; g++) {  // 32-weight group
+        int sm[2] = {0, 0};
+#pragma unroll
+        for (int l = 0; l < 4; l++) {  // 8 weights
+            int s0, s1;
+            if constexpr (C == IQ3_S) {
+                const int e0 = 8 * g + 2 * l;  // two 4-weight entries
+                const uint32_t lo = r.q[e0 >> 2] >> (8 * (e0 & 3));
+                const uint32_t hb = r.q[16 + (g >> 2)] >> (8 * (g & 3) + 2 * l);
+                const uint32_t g0 = grid4[(lo & 255u) | ((hb & 1u) << 8)];
+                const uint32_t g1 = grid4[((lo >> 8) & 255u) | ((hb & 2u) << 7)];
+                const uint32_t sbyte = (r.q[18 + g] >> (8 * l)) & 255u;
+                s0 = signed4(g0, sbyte);
+                s1 = signed4(g1, sbyte >> 4);
+            } else {
+                const int e = 4 * g + l;  // 8-weight entry
+                uint32_t idx, sbyte;
+                if constexpr (C == IQ2_XS) {
+                    const uint32_t v = (r.q[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+                    idx = v & 511u;
+                    sbyte = ksigns(v >> 9);
+                } else {
+                    idx = ((r.q[e >> 2] >> (8 * (e & 3))) & 255u) | (((r.q[16 + (e >> 4)] >> (2 * (e & 15))) & 3u) << 8);
+                    sbyte = (r.q[8 + (e >> 2)] >> (8 * (e & 3))) & 255u;
+                }
+                const uint2 gv = grid8[idx];
+                s0 = signed4(gv.x, sbyte);
+                s1 = signed4(gv.y, sbyte >> 4);
+            }
+            const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 16 * g + 4 * l);
+            int &sum = sm[C == IQ3_S ? 0 : (l >> 1)];
+            sum = __dp2a_lo((int)xv.x, s0, sum);
+            sum = __dp2a_hi((int)xv.y, s0, sum);
+            sum = __dp2a_lo((int)xv.z, s1, sum);
+            sum = __dp2a_hi((int)xv.w, s1, sum);
+        }
+        if constexpr (C == IQ3_S) {
+            const int s = (int)((r.q[26] >> (4 * g)) & 15u);
+            acc = fmaf(r.d * (float)(1 + 2 * s) * xsc[g], (float)sm[0], acc);
+        } else {
+            const uint32_t scw = r.q[(C == IQ2_XS ? 16 : 18) + (g >> 2)];  // byte g: two 4-bit scales
+            const float s0 = (float)((scw >> (8 * (g & 3))) & 15u), s1 = (float)((scw >> (8 * (g & 3) + 4)) & 15u);
+            acc = fmaf(r.d * 0.25f * xsc[g], (0.5f + s0) * (float)sm[0] + (0.5f + s1) * (float)sm[1], acc);
+        }
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 // Lane-per-row TQ2_0: Q2_K's quant layout with one fp16 d per block (66 bytes,
 // 2-byte aligned); per 32-weight group g: acc += d (dx S_g - dx sum_g(x_q)).
 struct TQ2Regs {
@@ -1244,6 +1336,13 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     }
     if constexpr (C == IQ3_XXS) {
         for (int e = threadIdx.x; e < 256; e += NTHREADS) reinterpret_cast<uint32_t *>(gridtab)[e] = c_iq3xxs_grid[e];
+    } else if constexpr (C == IQ3_S) {
+        for (int e = threadIdx.x; e < 512; e += NTHREADS) reinterpret_cast<uint32_t *>(gridtab)[e] = c_iq3s_grid[e];
+    } else if constexpr (C == IQ2_XS || C == IQ2_S) {
+        for (int e = threadIdx.x; e < (C == IQ2_XS ? 512 : 1024); e += NTHREADS) {
+            const uint64_t v = C == IQ2_XS ? c_iq2xs_grid[e] : c_iq2s_grid[e];
+            reinterpret_cast<uint2 *>(gridtab)[e] = make_uint2((uint32_t)v, (uint32_t)(v >> 32));
+        }
     }
     if constexpr (C == IQ2_XXS && L::DP) {
         // lane-per-row path: the raw magnitude bytes (256 x 8 B)
@@ -1474,6 +1573,17 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q2k_dot(r, xq, xsc);
+        } else if constexpr (C == IQ2_XS || C == IQ2_S || C == IQ3_S) {
+            IQSRegs<C> r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_iqs_load<C>(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run)
+                acc += dp_iqs_dot<C>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab),
+                                     reinterpret_cast<const uint32_t *>(gridtab));
         } else if constexpr (C == TQ2_0) {
             TQ2Regs r;
             if (run) {
@@ -2045,6 +2155,9 @@ cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == Q4_0) return launch_onerow_c<Q4_0>(a, st, grid_out);
     if (a.codec == Q4_1) return launch_onerow_c<Q4_1>(a, st, grid_out);
     if (a.codec == MXFP4) return launch_onerow_c<MXFP4>(a, st, grid_out);
+    if (a.codec == IQ2_XS) return launch_onerow_c<IQ2_XS>(a, st, grid_out);
+    if (a.codec == IQ2_S) return launch_onerow_c<IQ2_S>(a, st, grid_out);
+    if (a.codec == IQ3_S) return launch_onerow_c<IQ3_S>(a, st, grid_out);
     if (a.codec == TQ2_0) return launch_onerow_c<TQ2_0>(a, st, grid_out);
     if (a.codec == Q5_0) return launch_onerow_c<Q5_0>(a, st, grid_out);
     if (a.codec == Q5_1) return launch_onerow_c<Q5_1>(a, st, grid_out);

@@ -28,6 +28,8 @@
  *   Q5_1   (:308-336): w = d*q + m  (Q5: q = nibble | qh bit << 4)
  *   MXFP4  (MXFP4.dequantize_blocks): w = e8m0_half(e) * kvalues[q] per 32 weights
  *   TQ2_0  (TQ2_0.dequantize_blocks): w = d*(q-1), q 2-bit, Q2_K's quant layout
+ *   IQ2_XS (quants.py:872-898), IQ2_S (:974-1002): db = d*(0.5+s)*0.25 per 16
+ *          weights, w = db*grid*sign;  IQ3_S (:1096-1125): db = d*(1+2s) per 32
  * Every product above is exact in f32 (see the kernels' header), so results
  * are independent of FMA contraction; the file is still built with
  * -ffp-contract=off to keep the statement literal.
@@ -45,12 +47,16 @@
 #define QK 256
 enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
        KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11,
-       KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7, KQO_TQ2_0 = 35, KQO_MXFP4 = 39 };
+       KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7, KQO_TQ2_0 = 35, KQO_MXFP4 = 39,
+       KQO_IQ2_XS = 17, KQO_IQ3_S = 21, KQO_IQ2_S = 22 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
 static const int8_t kqo_iq4nl[16] = KQ_IQ4NL_VALUES_INIT;
 static const int8_t kqo_mxfp4[16] = KQ_MXFP4_VALUES_INIT;
+static const uint64_t kqo_grid2xs[512] = KQ_IQ2XS_GRID_INIT;
+static const uint64_t kqo_grid2s[1024] = KQ_IQ2S_GRID_INIT;
+static const uint32_t kqo_grid3s[512] = KQ_IQ3S_GRID_INIT;
 
 /* IEEE binary16 -> f32, exact (gguf-py: view(np.float16).astype(np.float32)). */
 static float kqo_half(uint16_t h) {
@@ -82,6 +88,7 @@ int kqo_block_bytes(int codec) {
     case KQO_Q4_1: return 160; case KQO_Q5_0: return 176; case KQO_Q5_1: return 192; /* eight blocks */
     case KQO_MXFP4: return 136; /* eight 17-byte blocks */
     case KQO_TQ2_0: return 66;
+    case KQO_IQ2_XS: return 74; case KQO_IQ2_S: return 82; case KQO_IQ3_S: return 110;
     }
     return -1;
 }
@@ -316,6 +323,54 @@ static void deq_tq20(const uint8_t *b, float *o) {
     }
 }
 
+/* gguf-py IQ2_XS.dequantize_blocks: d, 32 u16 entries (9-bit grid index,
+ * 7-bit sign index) of 8 weights, 8 bytes of 4-bit scales (one per 16
+ * weights, low nibble first). */
+static void deq_iq2xs(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    for (int e = 0; e < 32; e++) {
+        unsigned v = b[2 + 2 * e] | (b[3 + 2 * e] << 8);
+        int s = (b[66 + (e >> 2)] >> (4 * ((e >> 1) & 1))) & 15;
+        float db = d * (0.5f + (float)s) * 0.25f;
+        uint8_t sg = kqo_ksigns(v >> 9);
+        uint64_t g = kqo_grid2xs[v & 511];
+        for (int i = 0; i < 8; i++)
+            o[8 * e + i] = db * (float)((g >> (8 * i)) & 0xff) * (((sg >> i) & 1) ? -1.0f : 1.0f);
+    }
+}
+
+/* gguf-py IQ2_S.dequantize_blocks: d, 32 low index bytes, 32 sign bytes,
+ * 8 bytes of 2-bit high index parts (entry 4b + k: bits 2k of byte b), 8
+ * bytes of 4-bit scales (one per 16 weights). */
+static void deq_iq2s(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    for (int e = 0; e < 32; e++) {
+        unsigned idx = b[2 + e] | (((b[66 + (e >> 2)] >> (2 * (e & 3))) & 3u) << 8);
+        int s = (b[74 + (e >> 2)] >> (4 * ((e >> 1) & 1))) & 15;
+        float db = d * (0.5f + (float)s) * 0.25f;
+        uint8_t sg = b[34 + e];
+        uint64_t g = kqo_grid2s[idx];
+        for (int i = 0; i < 8; i++)
+            o[8 * e + i] = db * (float)((g >> (8 * i)) & 0xff) * (((sg >> i) & 1) ? -1.0f : 1.0f);
+    }
+}
+
+/* gguf-py IQ3_S.dequantize_blocks: d, 64 low index bytes (4 weights each),
+ * 8 bytes of high index bits (entry 8b + i: bit i of byte b), 32 sign bytes
+ * (8 weights each), 4 bytes of 4-bit scales (one per 32 weights). */
+static void deq_iq3s(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    for (int e = 0; e < 64; e++) {
+        unsigned idx = b[2 + e] | (((b[66 + (e >> 3)] >> (e & 7)) & 1u) << 8);
+        int s = (b[106 + (e >> 4)] >> (4 * ((e >> 3) & 1))) & 15;
+        float db = d * (float)(1 + 2 * s);
+        uint8_t sg = b[74 + (e >> 1)];
+        uint32_t g = kqo_grid3s[idx];
+        for (int i = 0; i < 4; i++)
+            o[4 * e + i] = db * (float)((g >> (8 * i)) & 0xff) * (((sg >> (4 * (e & 1) + i)) & 1) ? -1.0f : 1.0f);
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -329,6 +384,9 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_Q2_K: deq_q2k(b, o); return 0;
     case KQO_MXFP4: deq_mxfp4(b, o); return 0;
     case KQO_TQ2_0: deq_tq20(b, o); return 0;
+    case KQO_IQ2_XS: deq_iq2xs(b, o); return 0;
+    case KQO_IQ2_S: deq_iq2s(b, o); return 0;
+    case KQO_IQ3_S: deq_iq3s(b, o); return 0;
     case KQO_Q3_K: deq_q3k(b, o); return 0;
     }
     return -1;

@@ -32,13 +32,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
 Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, TQ2_0, MXFP4 = 2, 3, 6, 7, 8, 10, 11, 35, 39
-Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ3_XXS, IQ4_NL, IQ4_XS = 12, 13, 14, 16, 18, 20, 23
+Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ2_S, IQ4_XS = 12, 13, 14, 16, 17, 18, 20, 21, 22, 23
 CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
              "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K, "q4_1": Q4_1,
-             "q5_0": Q5_0, "q5_1": Q5_1, "tq2_0": TQ2_0, "mxfp4": MXFP4}
+             "q5_0": Q5_0, "q5_1": Q5_1, "tq2_0": TQ2_0, "mxfp4": MXFP4, "iq2_xs": IQ2_XS, "iq2_s": IQ2_S,
+             "iq3_s": IQ3_S}
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
                Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192,
-               TQ2_0: 66, MXFP4: 136}  # per 256 weights
+               TQ2_0: 66, MXFP4: 136, IQ2_XS: 74, IQ2_S: 82, IQ3_S: 110}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -230,6 +231,33 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
         d = bits_.view(np.float32).reshape(n * 8, 1)
         q = ((sub[:, 1:].reshape(n * 8, 1, 16) >> np.array([0, 4], np.uint8).reshape(1, 2, 1)) & 15).reshape(n * 8, 32)
         out = d * np.array(_table_values("KQ_MXFP4_VALUES_INIT"), np.float32)[q]
+    elif c in (IQ2_XS, IQ2_S):  # IQ2_XS / IQ2_S.dequantize_blocks: 32 entries of 8 weights
+        d = _half(blocks[:, 0:2]).reshape(n, 1, 1)
+        if c == IQ2_XS:
+            v = blocks[:, 2:66].copy().view(np.uint16).reshape(n, 32).astype(np.int64)
+            idx, sg = v & 511, ksigns_table()[v >> 9]
+            sc = blocks[:, 66:74]
+            grid = _grid("KQ_IQ2XS_GRID_INIT", 8, 512)
+        else:
+            qh = (blocks[:, 66:74].reshape(n, 8, 1) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4)) & 3
+            idx = blocks[:, 2:34].astype(np.int64) | (qh.reshape(n, 32).astype(np.int64) << 8)
+            sg = blocks[:, 34:66]
+            sc = blocks[:, 74:82]
+            grid = _grid("KQ_IQ2S_GRID_INIT", 8, 1024)
+        s = ((sc.reshape(n, 8, 1) >> np.array([0, 4], np.uint8).reshape(1, 1, 2)) & 15).reshape(n, 16)
+        db = (d * (np.float32(0.5) + s.astype(np.float32).reshape(n, 16, 1)) * np.float32(0.25)).reshape(n, 16, 1, 1)
+        sgn = np.where((sg.reshape(n, 32, 1) >> np.arange(8, dtype=np.uint8)) & 1, np.float32(-1), np.float32(1))
+        out = db * grid[idx].astype(np.float32).reshape(n, 16, 2, 8) * sgn.reshape(n, 16, 2, 8)
+    elif c == IQ3_S:  # IQ3_S.dequantize_blocks: 64 entries of 4 weights
+        d = _half(blocks[:, 0:2]).reshape(n, 1)
+        qh = (blocks[:, 66:74].reshape(n, 8, 1) >> np.arange(8, dtype=np.uint8).reshape(1, 1, 8)) & 1
+        idx = blocks[:, 2:66].astype(np.int64) | (qh.reshape(n, 64).astype(np.int64) << 8)
+        s = ((blocks[:, 106:110].reshape(n, 4, 1) >> np.array([0, 4], np.uint8).reshape(1, 1, 2)) & 15).reshape(n, 8)
+        db = (d * (1 + 2 * s).astype(np.float32)).reshape(n, 8, 1, 1)
+        sgn = np.where((blocks[:, 74:106].reshape(n, 32, 1) >> np.arange(8, dtype=np.uint8)) & 1, np.float32(-1),
+                       np.float32(1))
+        out = db * _grid("KQ_IQ3S_GRID_INIT", 4, 512)[idx].astype(np.float32).reshape(n, 8, 4, 8) * \
+            sgn.reshape(n, 8, 4, 8)
     elif c == TQ2_0:  # TQ2_0.dequantize_blocks
         d = _half(blocks[:, 64:66]).reshape(n, 1)
         q = (blocks[:, 0:64].reshape(n, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
@@ -277,10 +305,10 @@ def _table_values(macro: str) -> list:
     return [int(t.rstrip("ul"), 0) for t in body.replace("\\", " ").replace(",", " ").split()]
 
 
-def _grid(macro: str, width: int) -> np.ndarray:
+def _grid(macro: str, width: int, entries: int = 256) -> np.ndarray:
     if macro not in _GRIDS:
         vals = _table_values(macro)
-        assert len(vals) == 256
+        assert len(vals) == entries
         _GRIDS[macro] = np.array([[(v >> (8 * i)) & 0xFF for i in range(width)] for v in vals], np.uint8)
     return _GRIDS[macro]
 

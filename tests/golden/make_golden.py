@@ -22,6 +22,8 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
   Q4_1, Q5_0, Q5_1  the same with m = 0 / negative / positive and the fifth
           bits all clear / all set / alternating;
   MXFP4   every nibble value, exponents 0, 1 (subnormal scales), 2, 127, 140;
+  IQ2_XS, IQ2_S, IQ3_S  every grid index, every sign pattern index / byte
+          sweep, 4-bit scales 0 and 15;
   TQ2_0   values all 0 / 1 / 2 / 3 (3 is outside the ternary set but decodes), d < 0;
   IQ4_NL  every nibble value on every block, negative d;
   Q2_K    scale / min nibbles 0 and 15, quants all 0 / all 3, one-hot
@@ -47,7 +49,7 @@ from gmlx_b200 import synth  # noqa: E402
 QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
       "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
       "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1, "tq2_0": T.TQ2_0,
-      "mxfp4": T.MXFP4}
+      "mxfp4": T.MXFP4, "iq2_xs": T.IQ2_XS, "iq2_s": T.IQ2_S, "iq3_s": T.IQ3_S}
 
 
 def fp16(v):
@@ -155,6 +157,30 @@ def edge_blocks(codec):
             b = rng.integers(0, 256, 110, dtype=np.uint8)
             b[0:32] = 1 << plane
             b[108:110] = fp16(-1e-3)
+            blocks.append(b)
+    elif codec in ("iq2_xs", "iq2_s", "iq3_s"):
+        entries = {"iq2_xs": 512, "iq2_s": 1024, "iq3_s": 512}[codec]
+        per = 64 if codec == "iq3_s" else 32  # index entries per block
+        for blk in range(entries // per):
+            b = rng.integers(0, 256, {"iq2_xs": 74, "iq2_s": 82, "iq3_s": 110}[codec], dtype=np.uint8)
+            b[0:2] = fp16(1.5e-3 if blk % 2 else -7e-4)
+            idx = np.arange(per * blk, per * blk + per)
+            if codec == "iq2_xs":
+                v = idx | ((idx % 128) << 9)
+                b[2:66] = v.astype(np.uint16).view(np.uint8)
+                b[66:74] = 0x00 if blk % 2 else 0xff
+            elif codec == "iq2_s":
+                b[2:34] = (idx & 255).astype(np.uint8)
+                hi = (idx >> 8) & 3
+                b[66:74] = (hi.reshape(8, 4) << np.array([0, 2, 4, 6])).sum(1).astype(np.uint8)
+                b[34:66] = ((idx * 37) & 255).astype(np.uint8)
+                b[74:82] = 0x00 if blk % 2 else 0xff
+            else:
+                b[2:66] = (idx & 255).astype(np.uint8)
+                hi = (idx >> 8) & 1
+                b[66:74] = (hi.reshape(8, 8) << np.arange(8)).sum(1).astype(np.uint8)
+                b[74:106] = ((np.arange(32) * 53 + blk) & 255).astype(np.uint8)
+                b[106:110] = 0x00 if blk % 2 else 0xff
             blocks.append(b)
     elif codec == "mxfp4":
         for ev in (0, 1, 2, 127, 140, None):
