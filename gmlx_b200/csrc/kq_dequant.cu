@@ -62,6 +62,28 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
         const float db = d * (0.5f + (float)s) * 0.25f;
 #pragma unroll
         for (int i = 0; i < 8; i++) o[i] = db * (float)((g >> (8 * i)) & 255u) * (((sg >> i) & 1u) ? -1.0f : 1.0f);
+    } else if constexpr (C == IQ1_S || C == IQ1_M) {  // lane: grid entry lane (8 weights)
+        const int e = lane;
+        float dl, delta;
+        uint32_t idx;
+        if constexpr (C == IQ1_S) {
+            const uint32_t qh = ld_u16(b + 34 + 2 * (e >> 2));
+            dl = half_bits_to_float(ld_u16(b)) * (float)(2 * ((qh >> 12) & 7) + 1);
+            delta = (qh & 0x8000u) ? -0.125f : 0.125f;
+            idx = b[2 + e] | (((qh >> (3 * (e & 3))) & 7u) << 8);
+        } else {
+            const uint32_t s0 = ld_u16(b + 48), s1 = ld_u16(b + 50), s2 = ld_u16(b + 52), s3 = ld_u16(b + 54);
+            const float d = half_bits_to_float((s0 >> 12) | ((s1 >> 8) & 0xf0u) | ((s2 >> 4) & 0xf00u) | (s3 & 0xf000u));
+            const int k = e >> 1;
+            const uint32_t sk = ld_u16(b + 48 + 2 * (k >> 2));
+            dl = d * (float)(2 * ((sk >> (3 * (k & 3))) & 7) + 1);
+            const uint32_t nib = (b[32 + (e >> 1)] >> (4 * (e & 1))) & 15u;
+            delta = (nib & 8u) ? -0.125f : 0.125f;
+            idx = b[e] | ((nib & 7u) << 8);
+        }
+        const uint64_t g = c_iq1s_grid[idx];
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = dl * ((float)(int8_t)((g >> (8 * i)) & 255u) + delta);
     } else if constexpr (C == IQ3_S) {  // lane: grid entries 2 lane, 2 lane + 1 (8 weights)
         const float d = half_bits_to_float(ld_u16(b));
         const int s = (b[106 + (lane >> 3)] >> (4 * ((lane >> 2) & 1))) & 15;
@@ -350,6 +372,8 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case IQ2_XS: return launch_deq<IQ2_XS>(w, rows, nb, row_stride, out, dtype, st);
     case IQ2_S: return launch_deq<IQ2_S>(w, rows, nb, row_stride, out, dtype, st);
     case IQ3_S: return launch_deq<IQ3_S>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ1_S: return launch_deq<IQ1_S>(w, rows, nb, row_stride, out, dtype, st);
+    case IQ1_M: return launch_deq<IQ1_M>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_0: return launch_deq<Q5_0>(w, rows, nb, row_stride, out, dtype, st);
     case Q5_1: return launch_deq<Q5_1>(w, rows, nb, row_stride, out, dtype, st);
     case Q2_K: return launch_deq<Q2_K>(w, rows, nb, row_stride, out, dtype, st);

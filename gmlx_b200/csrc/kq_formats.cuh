@@ -33,6 +33,10 @@
 //   IQ2_S 82 B   d | 32 B index lo | 32 B signs | 8 B index hi (2 bits) | 8 B scales
 //   IQ3_S 110 B  d | 64 B index lo | 8 B index hi (1 bit) | 32 B signs | 4 B scales
 //                w = d*(1+2s) * grid * sign (s per 32 weights)
+//   IQ1_S 50 B   d | 32 B index lo | 8 x u16 (3 index bits x 4, s in 12-14, delta sign 15)
+//                w = d*(2s+1) * (grid + delta), grid in {-1,0,1}, delta = +-1/8 (per 32)
+//   IQ1_M 56 B   32 B index lo | 16 B nibbles (3 index bits, delta sign) | 4 x u16
+//                (3-bit s per 16 weights; top nibbles = fp16 d); delta per 8 weights
 //   Q2_K  84 B   16 x (sc | m << 4) | 64 B 2-bit q | d f16 | dmin f16
 //                w = (d*sc_j)*q - (dmin*m_j), 16-weight j   quants.py:404-428
 //   Q3_K  110 B  32 B high bits | 64 B 2-bit q | 12 B 6-bit scales | d f16
@@ -56,7 +60,7 @@ namespace kq {
 
 enum Codec : int {
     Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, TQ2_0 = 35, MXFP4 = 39, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ2_XS = 17, IQ3_XXS = 18, IQ4_NL = 20,
-    IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23
+    IQ1_S = 19, IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23, IQ1_M = 29
 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
@@ -80,6 +84,8 @@ template <> struct Fmt<TQ2_0> { static constexpr int bpb = 66; static constexpr 
 template <> struct Fmt<IQ2_XS> { static constexpr int bpb = 74; static constexpr int sub = 16; };
 template <> struct Fmt<IQ2_S> { static constexpr int bpb = 82; static constexpr int sub = 16; };
 template <> struct Fmt<IQ3_S> { static constexpr int bpb = 110; static constexpr int sub = 32; };
+template <> struct Fmt<IQ1_S> { static constexpr int bpb = 50; static constexpr int sub = 32; };
+template <> struct Fmt<IQ1_M> { static constexpr int bpb = 56; static constexpr int sub = 16; };
 
 // The 32-weight legacy blocks: d (fp16; MXFP4: one e8m0 byte), m (fp16;
 // HASM), a u32 of fifth bits (HASH), then 16 nibble bytes; BB bytes per
@@ -109,7 +115,7 @@ __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
          : codec == Q4_1 ? 160 : codec == Q5_0 ? 176 : codec == Q5_1 ? 192 : codec == MXFP4 ? 136 : codec == TQ2_0 ? 66
-         : codec == IQ2_XS ? 74 : codec == IQ2_S ? 82 : codec == IQ3_S ? 110
+         : codec == IQ2_XS ? 74 : codec == IQ2_S ? 82 : codec == IQ3_S ? 110 : codec == IQ1_S ? 50 : codec == IQ1_M ? 56
          : codec == Q2_K ? 84 : codec == Q3_K ? 110 : -1;
 }
 
@@ -123,6 +129,8 @@ static __device__ __constant__ __align__(16) int8_t c_iq4nl_values[16] = KQ_IQ4N
 static __device__ __constant__ uint64_t c_iq2xs_grid[512] = KQ_IQ2XS_GRID_INIT;
 static __device__ __constant__ uint64_t c_iq2s_grid[1024] = KQ_IQ2S_GRID_INIT;
 static __device__ __constant__ uint32_t c_iq3s_grid[512] = KQ_IQ3S_GRID_INIT;
+// IQ1_S / IQ1_M grid: 2048 x 8 values in {-1, 0, 1} as two's-complement bytes.
+static __device__ __constant__ uint64_t c_iq1s_grid[2048] = KQ_IQ1S_GRID_INIT;
 // MXFP4's doubled e2m1 values, as bytes of four words.
 static __device__ __constant__ __align__(16) int8_t c_mxfp4_values[16] = KQ_MXFP4_VALUES_INIT;
 

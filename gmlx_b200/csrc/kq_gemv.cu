@@ -61,6 +61,8 @@ template <> struct GCfg<Q5_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; 
 template <> struct GCfg<Q8_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 1; };     // lane-per-row path only
 template <> struct GCfg<Q2_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q3_K> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
+template <> struct GCfg<IQ1_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
+template <> struct GCfg<IQ1_M> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<IQ2_XS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
 template <> struct GCfg<IQ2_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<IQ3_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
@@ -76,9 +78,9 @@ template <> struct GCfg<IQ2_XXS> { static constexpr int TABW = 8 * 8 * 2, BPW = 
 template <> struct GCfg<IQ3_XXS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };  // lane-per-row path only
 template <> struct GCfg<IQ4_XS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };   // lane-per-row path only
 // shared-memory lattice table: IQ2_XXS 256 x 16 B (MMA path) or 8 B; IQ3_XXS 256 x 4 B;
-// IQ2_XS 512 x 8 B; IQ2_S 1024 x 8 B; IQ3_S 512 x 4 B
+// IQ2_XS 512 x 8 B; IQ2_S 1024 x 8 B; IQ3_S 512 x 4 B; IQ1_S / IQ1_M 2048 x 8 B
 template <int C> constexpr int GRIDB = C == IQ2_XXS ? 4096 : C == IQ3_XXS ? 1024 : C == IQ2_XS ? 4096 : C == IQ2_S ? 8192
-                                     : C == IQ3_S ? 2048 : 0;
+                                     : C == IQ3_S ? 2048 : (C == IQ1_S || C == IQ1_M) ? 16384 : 0;
 template <int C> constexpr int KB_OF = NCOL * GCfg<C>::BPW;
 template <int C> constexpr int XSTR_OF = KB_OF<C> * QK * 2 + 64;  // staged activation row stride (bytes)
 constexpr int SMEM_BUDGET = 112 * 1024;  // per CTA: two CTAs per SM
@@ -1120,7 +1122,7 @@ __device__ __forceinline__ float dp_q2k_dot(const Q2Regs &r, const uint32_t *xq,
 //   IQ2_XS: j 0-15 u16 entries, 16-17 scales
 //   IQ2_S:  j 0-7 index low bytes, 8-15 sign bytes, 16-17 index high bits, 18-19 scales
 //   IQ3_S:  j 0-15 index low bytes, 16-17 index high bits, 18-25 sign bytes, 26 scales
-template <int C> constexpr int IQS_NW = C == IQ3_S ? 27 : C == IQ2_S ? 20 : 18;
+template <int C> constexpr int IQS_NW = C == IQ3_S ? 27 : C == IQ2_S ? 20 : C == IQ1_S ? 12 : 18;
 template <int C> struct IQSRegs {
     uint32_t q[IQS_NW<C>];
     float d;
@@ -1193,6 +1195,80 @@ __device__ __forceinline__ float dp_iqs_dot(const IQSRegs<C> &r, const uint32_t 
             const uint32_t scw = r.q[(C == IQ2_XS ? 16 : 18) + (g >> 2)];  // byte g: two 4-bit scales
             const float s0 = (float)((scw >> (8 * (g & 3))) & 15u), s1 = (float)((scw >> (8 * (g & 3) + 4)) & 15u);
             acc = fmaf(r.d * 0.25f * xsc[g], (0.5f + s0) * (float)sm[0] + (0.5f + s1) * (float)sm[1], acc);
+        }
+    }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
+// Lane-per-row IQ1_S / IQ1_M: grid values g in {-1, 0, 1} plus a delta of
+// +-1/8 become the integers 8g +- 1 (per byte: (g << 3) masked, then a
+// carry-free byte add of +-1), dotted against the int16 activations; the 1/8
+// rides on the scale d (2s + 1) / 8.  IQ1_S is realigned at block byte 2
+// (IQS_NW = 12 words: index bytes, then the 8 u16), IQ1_M at byte 0 (14 words:
+// index bytes, nibbles, scales).
+struct IQ1MRegs {
+    uint32_t q[14];
+};
+
+__device__ __forceinline__ void dp_iq1m_load(const uint8_t *blk, IQ1MRegs &r) {
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;
+    uint32_t w[15];
+#pragma unroll
+    for (int i = 0; i < 15; i++) w[i] = aw[i];  // up to 4 bytes past the block: the ring row has slack
+#pragma unroll
+    for (int j = 0; j < 14; j++) r.q[j] = __funnelshift_r(w[j], w[j + 1], sh);
+}
+
+__device__ __forceinline__ int iq1_vals(uint32_t g, bool neg) {
+    return (int)__vadd4((g << 3) & 0xf8f8f8f8u, neg ? 0xffffffffu : 0x01010101u);
+}
+
+template <int C>
+__device__ __forceinline__ float dp_iq1_dot(const uint32_t *q, float d_iq1s, const uint32_t *xq, const float *xsc,
+                                           const uint2 *grid8) {
+    float acc = 0.f, d = d_iq1s;
+    if constexpr (C == IQ1_M)
+        d = half_bits_to_float((q[12] >> 12 & 0xfu) | ((q[12] >> 24) & 0xf0u) | ((q[13] >> 4) & 0xf00u) |
+                               ((q[13] >> 16) & 0xf000u));
+#pragma unroll
+    for (int g = 0; g < 8; g++) {  // 32-weight group
+        int sm[2] = {0, 0};
+        uint32_t qh = 0;
+        if constexpr (C == IQ1_S) qh = (q[8 + (g >> 1)] >> (16 * (g & 1))) & 0xffffu;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const int e = 4 * g + l;
+            uint32_t idx;
+            bool neg;
+            if constexpr (C == IQ1_S) {
+                idx = ((q[e >> 2] >> (8 * (e & 3))) & 255u) | (((qh >> (3 * l)) & 7u) << 8);
+                neg = (qh & 0x8000u) != 0;
+            } else {
+                const uint32_t nib = (q[8 + (e >> 3)] >> (4 * (e & 7))) & 15u;
+                idx = ((q[e >> 2] >> (8 * (e & 3))) & 255u) | ((nib & 7u) << 8);
+                neg = (nib & 8u) != 0;
+            }
+            const uint2 gv = grid8[idx];
+            const int s0 = iq1_vals(gv.x, neg), s1 = iq1_vals(gv.y, neg);
+            const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 16 * g + 4 * l);
+            int &sum = sm[C == IQ1_S ? 0 : (l >> 1)];
+            sum = __dp2a_lo((int)xv.x, s0, sum);
+            sum = __dp2a_hi((int)xv.y, s0, sum);
+            sum = __dp2a_lo((int)xv.z, s1, sum);
+            sum = __dp2a_hi((int)xv.w, s1, sum);
+        }
+        if constexpr (C == IQ1_S) {
+            acc = fmaf(d * 0.125f * (float)(2 * ((qh >> 12) & 7) + 1) * xsc[g], (float)sm[0], acc);
+        } else {
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int k = 2 * g + u;  // 16-weight sub-block: u16 k >> 2 of the scales
+                const uint32_t sk = (q[12 + (k >> 3)] >> (16 * ((k >> 2) & 1))) & 0xffffu;
+                acc = fmaf(d * 0.125f * (float)(2 * ((sk >> (3 * (k & 3))) & 7) + 1) * xsc[g], (float)sm[u], acc);
+            }
         }
     }
     __syncwarp();  // xq is rewritten for the next block
@@ -1338,6 +1414,11 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
         for (int e = threadIdx.x; e < 256; e += NTHREADS) reinterpret_cast<uint32_t *>(gridtab)[e] = c_iq3xxs_grid[e];
     } else if constexpr (C == IQ3_S) {
         for (int e = threadIdx.x; e < 512; e += NTHREADS) reinterpret_cast<uint32_t *>(gridtab)[e] = c_iq3s_grid[e];
+    } else if constexpr (C == IQ1_S || C == IQ1_M) {
+        for (int e = threadIdx.x; e < 2048; e += NTHREADS) {
+            const uint64_t v = c_iq1s_grid[e];
+            reinterpret_cast<uint2 *>(gridtab)[e] = make_uint2((uint32_t)v, (uint32_t)(v >> 32));
+        }
     } else if constexpr (C == IQ2_XS || C == IQ2_S) {
         for (int e = threadIdx.x; e < (C == IQ2_XS ? 512 : 1024); e += NTHREADS) {
             const uint64_t v = C == IQ2_XS ? c_iq2xs_grid[e] : c_iq2s_grid[e];
@@ -1573,6 +1654,24 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc += dp_q2k_dot(r, xq, xsc);
+        } else if constexpr (C == IQ1_S) {
+            IQSRegs<C> r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_iqs_load<C>(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_iq1_dot<C>(r.q, r.d, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
+        } else if constexpr (C == IQ1_M) {
+            IQ1MRegs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_iq1m_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_iq1_dot<C>(r.q, 0.f, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
         } else if constexpr (C == IQ2_XS || C == IQ2_S || C == IQ3_S) {
             IQSRegs<C> r;
             if (run) {
@@ -2158,6 +2257,8 @@ cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == IQ2_XS) return launch_onerow_c<IQ2_XS>(a, st, grid_out);
     if (a.codec == IQ2_S) return launch_onerow_c<IQ2_S>(a, st, grid_out);
     if (a.codec == IQ3_S) return launch_onerow_c<IQ3_S>(a, st, grid_out);
+    if (a.codec == IQ1_S) return launch_onerow_c<IQ1_S>(a, st, grid_out);
+    if (a.codec == IQ1_M) return launch_onerow_c<IQ1_M>(a, st, grid_out);
     if (a.codec == TQ2_0) return launch_onerow_c<TQ2_0>(a, st, grid_out);
     if (a.codec == Q5_0) return launch_onerow_c<Q5_0>(a, st, grid_out);
     if (a.codec == Q5_1) return launch_onerow_c<Q5_1>(a, st, grid_out);

@@ -22,8 +22,9 @@ prescribe:
 * MXFP4 (17 B per 32 weights, 136 B per 256): random nibbles, the e8m0
   exponent byte uniform in [115, 125] (scales 2^-13 .. 2^-3).  TQ2_0 (66 B):
   random 2-bit values, ``d`` fp16(U[1e-4, 2e-3]).
-* IQ2_XS (74 B), IQ2_S (82 B), IQ3_S (110 B): random, ``d`` (the first two
-  bytes) fp16(U[1e-4, 2e-3]).
+* IQ2_XS (74 B), IQ2_S (82 B), IQ3_S (110 B), IQ1_S (50 B): random, ``d``
+  (the first two bytes) fp16(U[1e-4, 2e-3]).  IQ1_M (56 B): random, its fp16
+  ``d`` (the top nibbles of the last four u16) fp16(U[1e-4, 2e-3]).
 * Q4_0, IQ4_NL (18 B per 32 weights, counted as 144 B per 256), Q4_1 (20 B),
   Q5_0 (22 B), Q5_1 (24 B): random quant bytes, ``d`` fp16(U[1e-4, 2e-3]) per
   32-weight block, ``m`` (Q4_1 / Q5_1) fp16(-U[1e-3, 2e-2]).
@@ -37,15 +38,17 @@ import numpy as np
 
 Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, TQ2_0, MXFP4 = 2, 3, 6, 7, 8, 10, 11, 35, 39
 Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ2_S, IQ4_XS = 12, 13, 14, 16, 17, 18, 20, 21, 22, 23
+IQ1_S, IQ1_M = 19, 29
 CODECS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
           "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K, "q4_1": Q4_1,
           "q5_0": Q5_0, "q5_1": Q5_1, "tq2_0": TQ2_0, "mxfp4": MXFP4, "iq2_xs": IQ2_XS, "iq2_s": IQ2_S,
-          "iq3_s": IQ3_S}
+          "iq3_s": IQ3_S, "iq1_s": IQ1_S, "iq1_m": IQ1_M}
 CODEC_NAMES = {v: k for k, v in CODECS.items()}
 # bytes per 256 weights (Q8_0: eight 34-byte ggml blocks of 32 weights)
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
                Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192,
-               TQ2_0: 66, MXFP4: 136, IQ2_XS: 74, IQ2_S: 82, IQ3_S: 110}
+               TQ2_0: 66, MXFP4: 136, IQ2_XS: 74, IQ2_S: 82, IQ3_S: 110,
+               IQ1_S: 50, IQ1_M: 56}
 QK = 256
 D_LO, D_HI = 1e-4, 2e-3
 
@@ -83,7 +86,13 @@ def random_blocks(codec, n_blocks: int, seed: int = 0) -> np.ndarray:
     elif c == Q6_K:
         b[:, 192:208] = rng.integers(-64, 64, size=(n_blocks, 16), dtype=np.int8).view(np.uint8)
         b[:, 208:210] = _fp16_bytes(rng, n_blocks)
-    elif c in (IQ2_XXS, IQ3_XXS, IQ4_XS, IQ2_XS, IQ2_S, IQ3_S):
+    elif c == IQ1_M:  # d's four nibbles sit in the top nibbles of the last four u16
+        dbits = _fp16_bytes(rng, n_blocks).copy().view(np.uint16).reshape(n_blocks).astype(np.uint16)
+        s = b[:, 48:56].copy().view(np.uint16).reshape(n_blocks, 4)
+        for t in range(4):
+            s[:, t] = (s[:, t] & np.uint16(0x0FFF)) | (((dbits >> np.uint16(4 * t)) & np.uint16(15)) << np.uint16(12))
+        b[:, 48:56] = s.view(np.uint8).reshape(n_blocks, 8)
+    elif c in (IQ2_XXS, IQ3_XXS, IQ4_XS, IQ2_XS, IQ2_S, IQ3_S, IQ1_S):
         b[:, 0:2] = _fp16_bytes(rng, n_blocks)
     elif c == Q8_0:  # eight (fp16 d, 32 x int8) blocks per 256 weights
         sub = b.reshape(n_blocks * 8, 34)

@@ -28,6 +28,8 @@
  *   Q5_1   (:308-336): w = d*q + m  (Q5: q = nibble | qh bit << 4)
  *   MXFP4  (MXFP4.dequantize_blocks): w = e8m0_half(e) * kvalues[q] per 32 weights
  *   TQ2_0  (TQ2_0.dequantize_blocks): w = d*(q-1), q 2-bit, Q2_K's quant layout
+ *   IQ1_S  (quants.py:1267-1288): dl = d*(2s+1) per 32, w = dl*(grid + delta), delta = +-0.125
+ *   IQ1_M  (quants.py:1300-1327): the same with s per 16, delta per 8, d packed in the scales
  *   IQ2_XS (quants.py:872-898), IQ2_S (:974-1002): db = d*(0.5+s)*0.25 per 16
  *          weights, w = db*grid*sign;  IQ3_S (:1096-1125): db = d*(1+2s) per 32
  * Every product above is exact in f32 (see the kernels' header), so results
@@ -48,7 +50,7 @@
 enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
        KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11,
        KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7, KQO_TQ2_0 = 35, KQO_MXFP4 = 39,
-       KQO_IQ2_XS = 17, KQO_IQ3_S = 21, KQO_IQ2_S = 22 };
+       KQO_IQ2_XS = 17, KQO_IQ3_S = 21, KQO_IQ2_S = 22, KQO_IQ1_S = 19, KQO_IQ1_M = 29 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
@@ -57,6 +59,7 @@ static const int8_t kqo_mxfp4[16] = KQ_MXFP4_VALUES_INIT;
 static const uint64_t kqo_grid2xs[512] = KQ_IQ2XS_GRID_INIT;
 static const uint64_t kqo_grid2s[1024] = KQ_IQ2S_GRID_INIT;
 static const uint32_t kqo_grid3s[512] = KQ_IQ3S_GRID_INIT;
+static const uint64_t kqo_grid1s[2048] = KQ_IQ1S_GRID_INIT;
 
 /* IEEE binary16 -> f32, exact (gguf-py: view(np.float16).astype(np.float32)). */
 static float kqo_half(uint16_t h) {
@@ -89,6 +92,7 @@ int kqo_block_bytes(int codec) {
     case KQO_MXFP4: return 136; /* eight 17-byte blocks */
     case KQO_TQ2_0: return 66;
     case KQO_IQ2_XS: return 74; case KQO_IQ2_S: return 82; case KQO_IQ3_S: return 110;
+    case KQO_IQ1_S: return 50; case KQO_IQ1_M: return 56;
     }
     return -1;
 }
@@ -371,6 +375,40 @@ static void deq_iq3s(const uint8_t *b, float *o) {
     }
 }
 
+static float kqo_grid1(unsigned idx, int i) { return (float)(int8_t)((kqo_grid1s[idx] >> (8 * i)) & 0xff); }
+
+/* gguf-py IQ1_S.dequantize_blocks: d, 32 low index bytes (8 weights each),
+ * 8 u16 (one per 32 weights: 3 high index bits per entry, scale in bits
+ * 12-14, delta sign in bit 15). */
+static void deq_iq1s(const uint8_t *b, float *o) {
+    float d = kqo_half((uint16_t)(b[0] | b[1] << 8));
+    for (int e = 0; e < 32; e++) {
+        int g = e >> 2;
+        unsigned qh = b[34 + 2 * g] | (b[35 + 2 * g] << 8);
+        float dl = d * (float)(2 * ((qh >> 12) & 7) + 1);
+        float delta = (qh & 0x8000) ? -0.125f : 0.125f;
+        unsigned idx = b[2 + e] | (((qh >> (3 * (e & 3))) & 7) << 8);
+        for (int i = 0; i < 8; i++) o[8 * e + i] = dl * (kqo_grid1(idx, i) + delta);
+    }
+}
+
+/* gguf-py IQ1_M.dequantize_blocks: 32 low index bytes, 16 bytes of one nibble
+ * per entry (3 high index bits, delta sign in bit 3), 4 u16 of 3-bit scales
+ * (one per 16 weights) whose top nibbles together hold the fp16 d. */
+static void deq_iq1m(const uint8_t *b, float *o) {
+    unsigned s[4];
+    for (int t = 0; t < 4; t++) s[t] = b[48 + 2 * t] | (b[49 + 2 * t] << 8);
+    float d = kqo_half((uint16_t)((s[0] >> 12) | ((s[1] >> 8) & 0xf0) | ((s[2] >> 4) & 0xf00) | (s[3] & 0xf000)));
+    for (int e = 0; e < 32; e++) {
+        int k = e >> 1;
+        float dl = d * (float)(2 * ((s[k >> 2] >> (3 * (k & 3))) & 7) + 1);
+        unsigned nib = (b[32 + (e >> 1)] >> (4 * (e & 1))) & 15;
+        float delta = (nib & 8) ? -0.125f : 0.125f;
+        unsigned idx = b[e] | ((nib & 7) << 8);
+        for (int i = 0; i < 8; i++) o[8 * e + i] = dl * (kqo_grid1(idx, i) + delta);
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -387,6 +425,8 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_IQ2_XS: deq_iq2xs(b, o); return 0;
     case KQO_IQ2_S: deq_iq2s(b, o); return 0;
     case KQO_IQ3_S: deq_iq3s(b, o); return 0;
+    case KQO_IQ1_S: deq_iq1s(b, o); return 0;
+    case KQO_IQ1_M: deq_iq1m(b, o); return 0;
     case KQO_Q3_K: deq_q3k(b, o); return 0;
     }
     return -1;

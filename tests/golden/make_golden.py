@@ -24,6 +24,7 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
   MXFP4   every nibble value, exponents 0, 1 (subnormal scales), 2, 127, 140;
   IQ2_XS, IQ2_S, IQ3_S  every grid index, every sign pattern index / byte
           sweep, 4-bit scales 0 and 15;
+  IQ1_S, IQ1_M  every grid index, both delta signs, 3-bit scales 0 and 7;
   TQ2_0   values all 0 / 1 / 2 / 3 (3 is outside the ternary set but decodes), d < 0;
   IQ4_NL  every nibble value on every block, negative d;
   Q2_K    scale / min nibbles 0 and 15, quants all 0 / all 3, one-hot
@@ -49,7 +50,8 @@ from gmlx_b200 import synth  # noqa: E402
 QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
       "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
       "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1, "tq2_0": T.TQ2_0,
-      "mxfp4": T.MXFP4, "iq2_xs": T.IQ2_XS, "iq2_s": T.IQ2_S, "iq3_s": T.IQ3_S}
+      "mxfp4": T.MXFP4, "iq2_xs": T.IQ2_XS, "iq2_s": T.IQ2_S, "iq3_s": T.IQ3_S,
+      "iq1_s": T.IQ1_S, "iq1_m": T.IQ1_M}
 
 
 def fp16(v):
@@ -181,6 +183,26 @@ def edge_blocks(codec):
                 b[66:74] = (hi.reshape(8, 8) << np.arange(8)).sum(1).astype(np.uint8)
                 b[74:106] = ((np.arange(32) * 53 + blk) & 255).astype(np.uint8)
                 b[106:110] = 0x00 if blk % 2 else 0xff
+            blocks.append(b)
+    elif codec in ("iq1_s", "iq1_m"):
+        for blk in range(64):
+            idx = np.arange(32 * blk, 32 * blk + 32)
+            if codec == "iq1_s":
+                b = np.zeros(50, np.uint8)
+                b[0:2] = fp16(1.5e-3 if blk % 2 else -7e-4)
+                b[2:34] = (idx & 255).astype(np.uint8)
+                hi = ((idx >> 8) & 7).reshape(8, 4)
+                qh = (hi << np.array([0, 3, 6, 9])).sum(1) | ((7 if blk % 3 else 0) << 12) | ((blk % 2) << 15)
+                b[34:50] = qh.astype(np.uint16).view(np.uint8)
+            else:
+                b = np.zeros(56, np.uint8)
+                b[0:32] = (idx & 255).astype(np.uint8)
+                nib = ((idx >> 8) & 7) | ((np.arange(32) + blk) % 2 << 3)
+                b[32:48] = (nib[0::2] | (nib[1::2] << 4)).astype(np.uint8)
+                dbits = int(np.array([1.5e-3 if blk % 2 else -7e-4], np.float16).view(np.uint16)[0])
+                sv = 7 if blk % 3 else 0
+                s = [(sv | sv << 3 | sv << 6 | sv << 9) | (((dbits >> (4 * t)) & 15) << 12) for t in range(4)]
+                b[48:56] = np.array(s, np.uint16).view(np.uint8)
             blocks.append(b)
     elif codec == "mxfp4":
         for ev in (0, 1, 2, 127, 140, None):

@@ -10,7 +10,7 @@ from oracle import oracle as O
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
 CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs", "q4_0", "iq4_nl", "q2_k", "q3_k", "q4_1",
-          "q5_0", "q5_1", "tq2_0", "mxfp4", "iq2_xs", "iq2_s", "iq3_s"]
+          "q5_0", "q5_1", "tq2_0", "mxfp4", "iq2_xs", "iq2_s", "iq3_s", "iq1_s", "iq1_m"]
 
 
 @pytest.fixture(scope="module")
@@ -48,7 +48,8 @@ def test_oracle_matches_gguf_py_random(codec, seed):
     qt = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_0": T.Q8_0,
           "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
           "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1, "tq2_0": T.TQ2_0,
-          "mxfp4": T.MXFP4, "iq2_xs": T.IQ2_XS, "iq2_s": T.IQ2_S, "iq3_s": T.IQ3_S}[codec]
+          "mxfp4": T.MXFP4, "iq2_xs": T.IQ2_XS, "iq2_s": T.IQ2_S, "iq3_s": T.IQ3_S,
+          "iq1_s": T.IQ1_S, "iq1_m": T.IQ1_M}[codec]
     w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
 
@@ -65,7 +66,7 @@ def test_raw_random_bytes_match_where_finite():
                            ("q2_k", T.Q2_K, 84), ("q3_k", T.Q3_K, 110), ("q4_1", T.Q4_1, 160),
                            ("q5_0", T.Q5_0, 176), ("q5_1", T.Q5_1, 192), ("tq2_0", T.TQ2_0, 66),
                            ("mxfp4", T.MXFP4, 136), ("iq2_xs", T.IQ2_XS, 74), ("iq2_s", T.IQ2_S, 82),
-                           ("iq3_s", T.IQ3_S, 110)]:
+                           ("iq3_s", T.IQ3_S, 110), ("iq1_s", T.IQ1_S, 50), ("iq1_m", T.IQ1_M, 56)]:
         w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
         a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
         fin = np.isfinite(b)
@@ -99,12 +100,14 @@ def test_iq2xxs_grid_matches_gguf():
 
 @pytest.mark.parametrize("name,macro,entries,width", [("IQ2_XS", "KQ_IQ2XS_GRID_INIT", 512, 8),
                                                      ("IQ2_S", "KQ_IQ2S_GRID_INIT", 1024, 8),
-                                                     ("IQ3_S", "KQ_IQ3S_GRID_INIT", 512, 4)])
+                                                     ("IQ3_S", "KQ_IQ3S_GRID_INIT", 512, 4),
+                                                     ("IQ1_S", "KQ_IQ1S_GRID_INIT", 2048, 8)])
 def test_generated_grids_match_gguf(name, macro, entries, width):
     gq = pytest.importorskip("gguf.quants")
     cls = getattr(gq, name)
     cls.init_grid()
-    assert np.array_equal(O._grid(macro, width, entries).astype(np.float32), np.asarray(cls.grid).reshape(entries, width))
+    assert np.array_equal(O._grid(macro, width, entries).view(np.int8).astype(np.float32),
+                          np.asarray(cls.grid).reshape(entries, width))
 
 
 def test_iq3xxs_grid_and_iq4nl_values_match_gguf():
@@ -137,6 +140,11 @@ def test_synthetic_block_statistics():
         elif codec in ("q8_0", "q4_0", "iq4_nl", "q4_1", "q5_0", "q5_1"):
             d = w.reshape(-1, synth.BLOCK_BYTES[synth.codec_id(codec)] // 8)[:, 0:2].copy().view(np.float16)
             d = d.astype(np.float32)
+            assert d.min() >= 9e-5 and d.max() <= 2.01e-3
+        elif codec == "iq1_m":  # d's nibbles are the top nibbles of the last four u16
+            sc = w[:, 48:56].copy().view(np.uint16).astype(np.int64)
+            db = (sc[:, 0] >> 12) | ((sc[:, 1] >> 8) & 0xF0) | ((sc[:, 2] >> 4) & 0xF00) | (sc[:, 3] & 0xF000)
+            d = db.astype(np.uint16).view(np.float16).astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3
         elif codec == "mxfp4":
             e = w.reshape(-1, 17)[:, 0]
