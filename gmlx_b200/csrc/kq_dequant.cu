@@ -97,6 +97,38 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
             for (int i = 0; i < 4; i++)
                 o[4 * h + i] = db * (float)((g >> (8 * i)) & 255u) * (((sg >> (4 * h + i)) & 1u) ? -1.0f : 1.0f);
         }
+    } else if constexpr (C == TQ1_0) {  // lane: weights 8 lane .. +7 (one digit position of 8 bytes)
+        const int w0 = 8 * lane;
+        const uint8_t *src;
+        uint32_t pw;
+        if (w0 < 160) {
+            src = b + (w0 & 31);
+            pw = 1u;
+            for (int k = 0; k < (w0 >> 5); k++) pw *= 3u;
+        } else if (w0 < 240) {
+            src = b + 32 + ((w0 - 160) & 15);
+            pw = 1u;
+            for (int k = 0; k < ((w0 - 160) >> 4); k++) pw *= 3u;
+        } else {  // weights 240 + 4k + l: two digit positions of the last 4 bytes
+            src = nullptr;
+            pw = 0u;
+        }
+        const float d = half_bits_to_float(ld_u16(b + 52));
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            uint32_t v, p;
+            if (src) {
+                v = src[i];
+                p = pw;
+            } else {
+                const int w = w0 + i - 240;
+                v = b[48 + (w & 3)];
+                p = 1u;
+                for (int k = 0; k < (w >> 2); k++) p *= 3u;
+            }
+            const int t = (int)((((v * p) & 255u) * 3u) >> 8);
+            o[i] = d * (float)(t - 1);
+        }
     } else if constexpr (C == TQ2_0) {  // lane: weights 8 lane .. +7
         const int w0 = 8 * lane, h = w0 >> 7, k = (w0 >> 5) & 3, l0 = w0 & 31;
         const float d = half_bits_to_float(ld_u16(b + 64));
@@ -369,6 +401,7 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case Q4_1: return launch_deq<Q4_1>(w, rows, nb, row_stride, out, dtype, st);
     case MXFP4: return launch_deq<MXFP4>(w, rows, nb, row_stride, out, dtype, st);
     case TQ2_0: return launch_deq<TQ2_0>(w, rows, nb, row_stride, out, dtype, st);
+    case TQ1_0: return launch_deq<TQ1_0>(w, rows, nb, row_stride, out, dtype, st);
     case IQ2_XS: return launch_deq<IQ2_XS>(w, rows, nb, row_stride, out, dtype, st);
     case IQ2_S: return launch_deq<IQ2_S>(w, rows, nb, row_stride, out, dtype, st);
     case IQ3_S: return launch_deq<IQ3_S>(w, rows, nb, row_stride, out, dtype, st);

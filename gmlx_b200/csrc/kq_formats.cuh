@@ -28,6 +28,8 @@
 //   MXFP4 8 x 17 B  (e8m0 e | 16 B nibbles), w = 2^(e-128) * kvalues[q]
 //                (kvalues: doubled e2m1; MXFP4.dequantize_blocks)
 //   TQ2_0 66 B   64 B 2-bit q (Q2_K's layout) | d f16, w = d*(q-1)
+//   TQ1_0 54 B   48 B of five base-3 digits | 4 B of four | d f16, w = d*(t-1);
+//                digit k of byte v = ((v*3^k mod 256)*3) >> 8   quants.py:602-620
 //   IQ2_XS 74 B  d | 32 x u16 (9-bit grid index, 7-bit sign index) | 8 B scales
 //                w = d*(0.5+s)*0.25 * grid * sign (s per 16 weights)
 //   IQ2_S 82 B   d | 32 B index lo | 32 B signs | 8 B index hi (2 bits) | 8 B scales
@@ -60,7 +62,7 @@ namespace kq {
 
 enum Codec : int {
     Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, TQ2_0 = 35, MXFP4 = 39, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ2_XS = 17, IQ3_XXS = 18, IQ4_NL = 20,
-    IQ1_S = 19, IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23, IQ1_M = 29
+    IQ1_S = 19, IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23, IQ1_M = 29, TQ1_0 = 34
 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
@@ -86,6 +88,7 @@ template <> struct Fmt<IQ2_S> { static constexpr int bpb = 82; static constexpr 
 template <> struct Fmt<IQ3_S> { static constexpr int bpb = 110; static constexpr int sub = 32; };
 template <> struct Fmt<IQ1_S> { static constexpr int bpb = 50; static constexpr int sub = 32; };
 template <> struct Fmt<IQ1_M> { static constexpr int bpb = 56; static constexpr int sub = 16; };
+template <> struct Fmt<TQ1_0> { static constexpr int bpb = 54; static constexpr int sub = 32; };
 
 // The 32-weight legacy blocks: d (fp16; MXFP4: one e8m0 byte), m (fp16;
 // HASM), a u32 of fifth bits (HASH), then 16 nibble bytes; BB bytes per
@@ -116,6 +119,7 @@ __host__ __device__ inline int block_bytes(int codec) {
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
          : codec == Q4_1 ? 160 : codec == Q5_0 ? 176 : codec == Q5_1 ? 192 : codec == MXFP4 ? 136 : codec == TQ2_0 ? 66
          : codec == IQ2_XS ? 74 : codec == IQ2_S ? 82 : codec == IQ3_S ? 110 : codec == IQ1_S ? 50 : codec == IQ1_M ? 56
+         : codec == TQ1_0 ? 54
          : codec == Q2_K ? 84 : codec == Q3_K ? 110 : -1;
 }
 

@@ -67,6 +67,7 @@ template <> struct GCfg<IQ2_XS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2
 template <> struct GCfg<IQ2_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<IQ3_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<MXFP4> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
+template <> struct GCfg<TQ1_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<TQ2_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<Q4_1> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
 template <> struct GCfg<Q5_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
@@ -1315,6 +1316,69 @@ __device__ __forceinline__ float dp_tq2_dot(const TQ2Regs &r, const uint32_t *xq
     return r.d * acc;
 }
 
+// Lane-per-row TQ1_0: four base-3 digits at a time.  For a word of four
+// bytes and a power m = 3^k, the even and odd bytes sit in 16-bit lanes, so
+// (v * m) mod 256 and then ((.) * 3) >> 8 run per lane without carries; the
+// digits t in {0, 1, 2} are dotted against the int16 activations and the -1
+// rides on the per-32 activation sums.  Digit position k of bytes 0-31 is the
+// 32-weight group k; of bytes 32-47 half of group 5 + k/2; bytes 48-51 the
+// second half of group 7.
+struct TQ1Regs {
+    uint32_t q[13];
+    float d;
+};
+
+__device__ __forceinline__ void dp_tq1_load(const uint8_t *blk, TQ1Regs &r) {
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    uint32_t w[15];
+#pragma unroll
+    for (int i = 0; i < 15; i++) w[i] = aw[i];  // up to 6 bytes past the block: the ring row has slack
+#pragma unroll
+    for (int i = 0; i < 13; i++) r.q[i] = __funnelshift_r(w[i], w[i + 1], sh);
+    r.d = half_bits_to_float(__funnelshift_r(w[13], w[14], sh) & 0xffffu);
+}
+
+__device__ __forceinline__ int tq1_digits(uint32_t w, uint32_t m) {
+    const uint32_t lo = ((w & 0x00ff00ffu) * m) & 0x00ff00ffu, hi = (((w >> 8) & 0x00ff00ffu) * m) & 0x00ff00ffu;
+    return (int)((((lo * 3u) >> 8) & 0x00030003u) | ((((hi * 3u) >> 8) & 0x00030003u) << 8));
+}
+
+__device__ __forceinline__ float dp_tq1_dot(const TQ1Regs &r, const uint32_t *xq, const float *xsc) {
+    int S[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 5; k++) {
+        const uint32_t m = k == 0 ? 1u : k == 1 ? 3u : k == 2 ? 9u : k == 3 ? 27u : 81u;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {  // bytes 4i .. 4i + 3: weights 32k + 4i .. +3
+            const int t = tq1_digits(r.q[i], m);
+            const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 16 * k + 2 * i);
+            S[k] = __dp2a_lo((int)xv.x, t, S[k]);
+            S[k] = __dp2a_hi((int)xv.y, t, S[k]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {  // bytes 32 + 4i .. : weights 160 + 16k + 4i .. +3
+            const int t = tq1_digits(r.q[8 + i], m);
+            const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 80 + 8 * k + 2 * i);
+            int &s = S[5 + (k >> 1)];
+            s = __dp2a_lo((int)xv.x, t, s);
+            s = __dp2a_hi((int)xv.y, t, s);
+        }
+        if (k < 4) {  // bytes 48 .. 51: weights 240 + 4k .. +3
+            const int t = tq1_digits(r.q[12], m);
+            const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 120 + 2 * k);
+            S[7] = __dp2a_lo((int)xv.x, t, S[7]);
+            S[7] = __dp2a_hi((int)xv.y, t, S[7]);
+        }
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; g++) acc = fmaf(xsc[g], (float)S[g], acc - xsc[8 + g]);
+    __syncwarp();  // xq is rewritten for the next block
+    return r.d * acc;
+}
+
 struct Q3Regs {
     uint32_t hm[8], q[16], s[3];
     float d;
@@ -1683,6 +1747,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             if (run)
                 acc += dp_iqs_dot<C>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab),
                                      reinterpret_cast<const uint32_t *>(gridtab));
+        } else if constexpr (C == TQ1_0) {
+            TQ1Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_tq1_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_tq1_dot(r, xq, xsc);
         } else if constexpr (C == TQ2_0) {
             TQ2Regs r;
             if (run) {
@@ -2260,6 +2333,7 @@ cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == IQ1_S) return launch_onerow_c<IQ1_S>(a, st, grid_out);
     if (a.codec == IQ1_M) return launch_onerow_c<IQ1_M>(a, st, grid_out);
     if (a.codec == TQ2_0) return launch_onerow_c<TQ2_0>(a, st, grid_out);
+    if (a.codec == TQ1_0) return launch_onerow_c<TQ1_0>(a, st, grid_out);
     if (a.codec == Q5_0) return launch_onerow_c<Q5_0>(a, st, grid_out);
     if (a.codec == Q5_1) return launch_onerow_c<Q5_1>(a, st, grid_out);
     if (a.codec == Q2_K) return launch_onerow_c<Q2_K>(a, st, grid_out);

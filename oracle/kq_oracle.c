@@ -28,6 +28,7 @@
  *   Q5_1   (:308-336): w = d*q + m  (Q5: q = nibble | qh bit << 4)
  *   MXFP4  (MXFP4.dequantize_blocks): w = e8m0_half(e) * kvalues[q] per 32 weights
  *   TQ2_0  (TQ2_0.dequantize_blocks): w = d*(q-1), q 2-bit, Q2_K's quant layout
+ *   TQ1_0  (quants.py:602-620): trit k of byte b = ((b*3^k mod 256)*3) >> 8, w = d*(t-1)
  *   IQ1_S  (quants.py:1267-1288): dl = d*(2s+1) per 32, w = dl*(grid + delta), delta = +-0.125
  *   IQ1_M  (quants.py:1300-1327): the same with s per 16, delta per 8, d packed in the scales
  *   IQ2_XS (quants.py:872-898), IQ2_S (:974-1002): db = d*(0.5+s)*0.25 per 16
@@ -50,7 +51,7 @@
 enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
        KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11,
        KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7, KQO_TQ2_0 = 35, KQO_MXFP4 = 39,
-       KQO_IQ2_XS = 17, KQO_IQ3_S = 21, KQO_IQ2_S = 22, KQO_IQ1_S = 19, KQO_IQ1_M = 29 };
+       KQO_IQ2_XS = 17, KQO_IQ3_S = 21, KQO_IQ2_S = 22, KQO_IQ1_S = 19, KQO_IQ1_M = 29, KQO_TQ1_0 = 34 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
@@ -92,7 +93,7 @@ int kqo_block_bytes(int codec) {
     case KQO_MXFP4: return 136; /* eight 17-byte blocks */
     case KQO_TQ2_0: return 66;
     case KQO_IQ2_XS: return 74; case KQO_IQ2_S: return 82; case KQO_IQ3_S: return 110;
-    case KQO_IQ1_S: return 50; case KQO_IQ1_M: return 56;
+    case KQO_IQ1_S: return 50; case KQO_IQ1_M: return 56; case KQO_TQ1_0: return 54;
     }
     return -1;
 }
@@ -409,6 +410,23 @@ static void deq_iq1m(const uint8_t *b, float *o) {
     }
 }
 
+/* gguf-py TQ1_0.dequantize_blocks: 48 bytes of five base-3 digits each
+ * (bytes 0-31: weight 32k + l; bytes 32-47: weight 160 + 16k + l), 4 bytes of
+ * four digits (weight 240 + 4k + l), d.  Digit k of byte v is
+ * ((v * 3^k mod 256) * 3) >> 8. */
+static void deq_tq10(const uint8_t *b, float *o) {
+    static const unsigned pw[5] = {1, 3, 9, 27, 81};
+    float d = kqo_half((uint16_t)(b[52] | b[53] << 8));
+    for (int w = 0; w < 256; w++) {
+        unsigned v, k;
+        if (w < 160) { v = b[w & 31]; k = w >> 5; }
+        else if (w < 240) { v = b[32 + ((w - 160) & 15)]; k = (w - 160) >> 4; }
+        else { v = b[48 + ((w - 240) & 3)]; k = (w - 240) >> 2; }
+        int t = (int)((((v * pw[k]) & 255u) * 3u) >> 8);
+        o[w] = d * (float)(t - 1);
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -426,6 +444,7 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_IQ2_S: deq_iq2s(b, o); return 0;
     case KQO_IQ3_S: deq_iq3s(b, o); return 0;
     case KQO_IQ1_S: deq_iq1s(b, o); return 0;
+    case KQO_TQ1_0: deq_tq10(b, o); return 0;
     case KQO_IQ1_M: deq_iq1m(b, o); return 0;
     case KQO_Q3_K: deq_q3k(b, o); return 0;
     }

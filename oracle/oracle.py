@@ -33,15 +33,15 @@ LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
 Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, TQ2_0, MXFP4 = 2, 3, 6, 7, 8, 10, 11, 35, 39
 Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ2_S, IQ4_XS = 12, 13, 14, 16, 17, 18, 20, 21, 22, 23
-IQ1_S, IQ1_M = 19, 29
+IQ1_S, IQ1_M, TQ1_0 = 19, 29, 34
 CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
              "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K, "q4_1": Q4_1,
              "q5_0": Q5_0, "q5_1": Q5_1, "tq2_0": TQ2_0, "mxfp4": MXFP4, "iq2_xs": IQ2_XS, "iq2_s": IQ2_S,
-             "iq3_s": IQ3_S, "iq1_s": IQ1_S, "iq1_m": IQ1_M}
+             "iq3_s": IQ3_S, "iq1_s": IQ1_S, "iq1_m": IQ1_M, "tq1_0": TQ1_0}
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
                Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192,
                TQ2_0: 66, MXFP4: 136, IQ2_XS: 74, IQ2_S: 82, IQ3_S: 110,
-               IQ1_S: 50, IQ1_M: 56}  # per 256 weights
+               IQ1_S: 50, IQ1_M: 56, TQ1_0: 54}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -279,6 +279,13 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
             delta = np.where(nib & 8, np.float32(-0.125), np.float32(0.125))
             idx = blocks[:, 0:32].astype(np.int64) | ((nib & 7).astype(np.int64) << 8)
         out = dl.reshape(n, 32, 1) * (grid[idx] + delta.reshape(n, 32, 1))
+    elif c == TQ1_0:  # TQ1_0.dequantize_blocks (quants.py:602-620)
+        p5 = np.array([1, 3, 9, 27, 81], np.uint16)
+        t0 = (blocks[:, 0:32].reshape(n, 1, 32).astype(np.uint16) * p5.reshape(1, 5, 1)) & 255
+        t1 = (blocks[:, 32:48].reshape(n, 1, 16).astype(np.uint16) * p5.reshape(1, 5, 1)) & 255
+        t2 = (blocks[:, 48:52].reshape(n, 1, 4).astype(np.uint16) * p5[:4].reshape(1, 4, 1)) & 255
+        t = np.concatenate([t0.reshape(n, 160), t1.reshape(n, 80), t2.reshape(n, 16)], 1)
+        out = _half(blocks[:, 52:54]).reshape(n, 1) * (((t * 3) >> 8).astype(np.float32) - np.float32(1))
     elif c == TQ2_0:  # TQ2_0.dequantize_blocks
         d = _half(blocks[:, 64:66]).reshape(n, 1)
         q = (blocks[:, 0:64].reshape(n, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
