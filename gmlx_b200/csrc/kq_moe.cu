@@ -87,52 +87,73 @@ __global__ void router_kernel(const float *__restrict__ logits, int T, int E, in
 
 // Groups over the local expert range [ebase, ebase + ecount): slots routed
 // elsewhere are skipped (expert-parallel ranks); ids outside [0, etotal) are
-// an error.
+// an error.  Slots of an expert keep their slot order (group g of expert e
+// holds its slots gsize*g .. gsize*g + gsize - 1).  Three passes in one CTA:
+// per-expert counts (shared-memory atomics), group offsets (one warp's scan),
+// then one warp places the slots 32 at a time, ranking equal experts within
+// the chunk with __match_any_sync, so the work is O(slots + experts).
 __global__ void groups_kernel(const int32_t *__restrict__ idx, int S, int k, int ebase, int ecount, int etotal,
                               int xrow_is_slot, const int32_t *__restrict__ xidx, int gsize,
                               int *__restrict__ n_groups, int *__restrict__ grp_expert, int *__restrict__ grp_count,
                               int *__restrict__ grp_xrow, int *__restrict__ grp_orow, int max_groups,
                               int *__restrict__ err) {
-    __shared__ int s_first[RT_MAXE + 1];
+    constexpr int SIDX = 4096;  // routing ids staged in shared memory for the placement pass
+    __shared__ int s_cnt[RT_MAXE], s_first[RT_MAXE + 1], s_base[RT_MAXE], s_idx[SIDX];
     __shared__ int s_bad;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) s_bad = 0;
+    for (int e = threadIdx.x; e < ecount; e += blockDim.x) s_cnt[e] = 0, s_base[e] = 0;
     __syncthreads();
     for (int s = threadIdx.x; s < S; s += blockDim.x) {
         const int v = idx[s];
+        if (s < SIDX) s_idx[s] = v;
         if (v < 0 || v >= etotal) s_bad = 1;
-    }
-    for (int e = threadIdx.x; e < ecount; e += blockDim.x) {
-        int c = 0;
-        for (int s = 0; s < S; s++) c += idx[s] == ebase + e;
-        s_first[e + 1] = (c + gsize - 1) / gsize;
+        else if (v >= ebase && v < ebase + ecount) atomicAdd(&s_cnt[v - ebase], 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        s_first[0] = 0;
-        for (int e = 0; e < ecount; e++) s_first[e + 1] += s_first[e];
-        *n_groups = s_bad ? 0 : min(s_first[ecount], max_groups);
-        if (s_bad) atomicCAS(err, 0, 3);
-        else if (s_first[ecount] > max_groups) atomicCAS(err, 0, 4);
-    }
-    __syncthreads();
-    if (s_bad) return;
-    for (int e = threadIdx.x; e < ecount; e += blockDim.x) {
-        int gi = s_first[e], n = 0;
-        for (int s = 0; s < S; s++) {
-            if (idx[s] != ebase + e) continue;
-            if (gi >= max_groups) break;
-            grp_xrow[gi * 32 + n] = xidx ? xidx[s] : xrow_is_slot ? s : s / k;
-            grp_orow[gi * 32 + n] = s;
-            if (++n == gsize) {
-                grp_expert[gi] = e;
-                grp_count[gi] = gsize;
-                gi++;
-                n = 0;
-            }
+    if (warp == 0) {  // s_first[e] = groups of experts < e (lane-chunked exclusive scan)
+        const int per = (ecount + 31) / 32, e0 = lane * per, e1 = min(ecount, e0 + per);
+        int t = 0;
+        for (int e = e0; e < e1; e++) t += (s_cnt[e] + gsize - 1) / gsize;
+        int incl = t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += u;
         }
-        if (n && gi < max_groups) {
+        int run = incl - t;
+        for (int e = e0; e < e1; e++) {
+            s_first[e] = run;
+            run += (s_cnt[e] + gsize - 1) / gsize;
+        }
+        if (lane == 31) {
+            s_first[ecount] = incl;
+            *n_groups = s_bad ? 0 : min(incl, max_groups);
+            if (s_bad) atomicCAS(err, 0, 3);
+            else if (incl > max_groups) atomicCAS(err, 0, 4);
+        }
+    }
+    __syncthreads();
+    if (s_bad || warp != 0) return;
+    for (int c = 0; c < S; c += 32) {  // stable placement, 32 slots at a time
+        const int s = c + lane;
+        const int v = s < S ? (s < SIDX ? s_idx[s] : idx[s]) : -1;
+        const bool local = v >= ebase && v < ebase + ecount;
+        const int e = v - ebase;
+        const unsigned peers = __match_any_sync(0xffffffffu, local ? e : -1 - lane);
+        int p = 0;
+        if (local) p = s_base[e] + __popc(peers & ((1u << lane) - 1u));
+        __syncwarp();
+        if (local && lane == 31 - __clz(peers)) s_base[e] += __popc(peers);
+        __syncwarp();
+        if (!local) continue;
+        const int gi = s_first[e] + p / gsize, n = p % gsize;
+        if (gi >= max_groups) continue;
+        grp_xrow[gi * 32 + n] = xidx ? xidx[s] : xrow_is_slot ? s : s / k;
+        grp_orow[gi * 32 + n] = s;
+        if (n == 0) {
             grp_expert[gi] = e;
-            grp_count[gi] = n;
+            grp_count[gi] = min(gsize, s_cnt[e] - p);
         }
     }
 }
@@ -192,6 +213,7 @@ cudaError_t launch_router_topk(const float *logits, int T, int E, int k, int nor
 cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int ebase, int ecount, int etotal, int xrow_is_slot,
                               const int32_t *xidx, int gsize, int *n_groups, int *grp_expert, int *grp_count,
                               int *grp_xrow, int *grp_orow, int max_groups, int *err, cudaStream_t st) {
+    if (ecount > RT_MAXE) return cudaErrorInvalidValue;  // per-expert tables live in shared memory
     groups_kernel<<<1, 1024, 0, st>>>(idx, S, k, ebase, ecount, etotal, xrow_is_slot, xidx, gsize, n_groups,
                                       grp_expert, grp_count, grp_xrow, grp_orow, max_groups, err);
     return cudaGetLastError();
