@@ -89,3 +89,26 @@ def test_not_gguf(tmp_path):
     p.write_bytes(b"NOTGGUF" + b"\0" * 64)
     with pytest.raises(ValueError):
         gguf_io.load_gguf(str(p))
+
+
+def test_every_kernel_codec_survives_a_gguf_file(tmp_path):
+    """Each codec with kernels here, written by gguf-py into one GGUF file, comes
+    back from our loader under the codec name the ops take, with the wire row
+    length the ops expect (the 32-weight ggml codecs: whole 256-weight groups)
+    and bytes that dequantize (oracle) exactly as gguf-py's own dequantizer."""
+    from gguf import quants as gq
+    from oracle import oracle as O
+    tensors = []
+    for i, name in enumerate(sorted(synth.CODECS)):
+        w = synth.random_weight(name, 3, 512, seed=40 + i)
+        tensors.append((f"t.{name}.weight", w, Q[name.upper()]))
+    path = tmp_path / "codecs.gguf"
+    _write(path, tensors)
+    arrays, codecs, _, _ = gguf_io.load_gguf(str(path), zero_copy=False)
+    for name, w, qt in tensors:
+        codec = codecs[name]
+        assert synth.codec_id(codec) == synth.CODECS[codec]
+        got = arrays[name].numpy()
+        assert got.shape == (3, synth.row_bytes(codec, 512)) and np.array_equal(got, w)
+        ref = gq.dequantize(got, qt).astype(np.float32)
+        assert np.array_equal(O.dequantize(got, codec).view(np.uint32), ref.view(np.uint32))
