@@ -1,7 +1,7 @@
 """Build libkq_cuda.so (sm_100a) in-tree with nvcc.
 
 The library is a plain C-ABI shared object (``include/kq_cuda.h``); Python
-loads it with ctypes (``gmlx_b200/_lib.py``).  The IQ2_XXS grid header is
+loads it with ctypes (``gmlx_b200/_lib.py``).  The grid and value-table header is
 generated first from the installed gguf-py package (``csrc/gen_tables.py``).
 Objects are compiled in parallel and relinked only when a source changed;
 each flag set (normal / ``KQ_DEVELOPMENT``) keeps its own object directory, and
