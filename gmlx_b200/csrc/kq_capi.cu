@@ -55,21 +55,21 @@ bool codec_ok(int c) {
     return c == KQ_Q4_K || c == KQ_Q5_K || c == KQ_Q6_K || c == KQ_IQ2_XXS || c == KQ_Q8_0 || c == KQ_IQ3_XXS ||
            c == KQ_IQ4_XS || c == KQ_Q4_0 || c == KQ_IQ4_NL || c == KQ_Q2_K || c == KQ_Q3_K || c == KQ_Q4_1 ||
            c == KQ_Q5_0 || c == KQ_Q5_1 || c == KQ_TQ2_0 || c == KQ_MXFP4 || c == KQ_IQ2_XS || c == KQ_IQ2_S ||
-           c == KQ_IQ3_S || c == KQ_IQ1_S || c == KQ_IQ1_M || c == KQ_TQ1_0;
+           c == KQ_IQ3_S || c == KQ_IQ1_S || c == KQ_IQ1_M || c == KQ_TQ1_0 || c == KQ_NVFP4;
 }
 // codecs whose only GEMV is the one-row (lane-per-row) path
 bool onerow_only(int c) {
     return c == KQ_Q5_K || c == KQ_Q8_0 || c == KQ_IQ3_XXS || c == KQ_IQ4_XS || c == KQ_Q4_0 || c == KQ_IQ4_NL ||
            c == KQ_Q2_K || c == KQ_Q3_K || c == KQ_Q4_1 || c == KQ_Q5_0 || c == KQ_Q5_1 || c == KQ_TQ2_0 || c == KQ_MXFP4 ||
            c == KQ_IQ2_XS || c == KQ_IQ2_S || c == KQ_IQ3_S || c == KQ_IQ1_S || c == KQ_IQ1_M ||
-           c == KQ_TQ1_0;
+           c == KQ_TQ1_0 || c == KQ_NVFP4;
 }
 bool act_dtype_ok(int d) { return d == KQ_F16 || d == KQ_BF16; }
 bool out_dtype_ok(int d) { return d == KQ_F32 || d == KQ_F16 || d == KQ_BF16; }
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 int check_weights(int codec, const void *w, int64_t k, int64_t row_stride, const char *what) {
-    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q8_0=8, q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16, iq3_xxs=18, iq4_xs=23, q4_0=2, iq4_nl=20, q2_k=10, q3_k=11, q4_1=3, q5_0=6, q5_1=7, tq2_0=35, mxfp4=39, iq2_xs=17, iq2_s=22, iq3_s=21, iq1_s=19, iq1_m=29, tq1_0=34)", what, codec);
+    if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q8_0=8, q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16, iq3_xxs=18, iq4_xs=23, q4_0=2, iq4_nl=20, q2_k=10, q3_k=11, q4_1=3, q5_0=6, q5_1=7, tq2_0=35, mxfp4=39, iq2_xs=17, iq2_s=22, iq3_s=21, iq1_s=19, iq1_m=29, tq1_0=34, nvfp4=40)", what, codec);
     if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a positive multiple of %d", what, (long long)k, QK);
     const int64_t rb = k / QK * block_bytes(codec);
     if (row_stride < rb) return fail(KQ_ERR_SHAPE, "%s: row stride %lld < row bytes %lld", what, (long long)row_stride, (long long)rb);
@@ -628,11 +628,11 @@ int kq_version(void) { return 100; }
 const char *kq_last_error(void) { return g_msg; }
 
 int kq_codecs(int *out, int cap) {
-    static const int ids[22] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS, KQ_Q8_0, KQ_IQ3_XXS, KQ_IQ4_XS, KQ_Q4_0,
+    static const int ids[23] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS, KQ_Q8_0, KQ_IQ3_XXS, KQ_IQ4_XS, KQ_Q4_0,
                                 KQ_IQ4_NL, KQ_Q2_K, KQ_Q3_K, KQ_Q4_1, KQ_Q5_0, KQ_Q5_1, KQ_TQ2_0, KQ_MXFP4,
-                                KQ_IQ2_XS, KQ_IQ2_S, KQ_IQ3_S, KQ_IQ1_S, KQ_IQ1_M, KQ_TQ1_0};
-    for (int i = 0; i < 22 && i < cap; i++) out[i] = ids[i];
-    return 22;
+                                KQ_IQ2_XS, KQ_IQ2_S, KQ_IQ3_S, KQ_IQ1_S, KQ_IQ1_M, KQ_TQ1_0, KQ_NVFP4};
+    for (int i = 0; i < 23 && i < cap; i++) out[i] = ids[i];
+    return 23;
 }
 
 int kq_codec_has_matmul(int codec) { return codec_ok(codec) ? 1 : 0; }

@@ -97,6 +97,13 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
             for (int i = 0; i < 4; i++)
                 o[4 * h + i] = db * (float)((g >> (8 * i)) & 255u) * (((sg >> (4 * h + i)) & 1u) ? -1.0f : 1.0f);
         }
+    } else if constexpr (C == NVFP4) {  // lane: weights 8 lane .. +7 (one nibble half of 8 bytes)
+        const uint8_t *blk = b + 36 * (lane >> 3);
+        const int j = (lane >> 1) & 3, h = lane & 1;
+        const float d = ue4m3_half(blk[j]);
+        const uint8_t *q = blk + 4 + 8 * j;
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = d * (float)c_mxfp4_values[(q[i] >> (4 * h)) & 15];
     } else if constexpr (C == TQ1_0) {  // lane: weights 8 lane .. +7 (one digit position of 8 bytes)
         const int w0 = 8 * lane;
         const uint8_t *src;
@@ -402,6 +409,7 @@ cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t
     case MXFP4: return launch_deq<MXFP4>(w, rows, nb, row_stride, out, dtype, st);
     case TQ2_0: return launch_deq<TQ2_0>(w, rows, nb, row_stride, out, dtype, st);
     case TQ1_0: return launch_deq<TQ1_0>(w, rows, nb, row_stride, out, dtype, st);
+    case NVFP4: return launch_deq<NVFP4>(w, rows, nb, row_stride, out, dtype, st);
     case IQ2_XS: return launch_deq<IQ2_XS>(w, rows, nb, row_stride, out, dtype, st);
     case IQ2_S: return launch_deq<IQ2_S>(w, rows, nb, row_stride, out, dtype, st);
     case IQ3_S: return launch_deq<IQ3_S>(w, rows, nb, row_stride, out, dtype, st);

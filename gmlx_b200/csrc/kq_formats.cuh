@@ -28,6 +28,9 @@
 //   MXFP4 8 x 17 B  (e8m0 e | 16 B nibbles), w = 2^(e-128) * kvalues[q]
 //                (kvalues: doubled e2m1; MXFP4.dequantize_blocks)
 //   TQ2_0 66 B   64 B 2-bit q (Q2_K's layout) | d f16, w = d*(q-1)
+//   NVFP4 4 x 36 B (4 UE4M3 scales, one per 16 | 4 x 8 B nibbles: low = weights
+//                0-7, high = 8-15 of each 16), w = ue4m3(s)/2 * kvalues[q]
+//                (MXFP4's doubled e2m1 values)   quants.py:707-763
 //   TQ1_0 54 B   48 B of five base-3 digits | 4 B of four | d f16, w = d*(t-1);
 //                digit k of byte v = ((v*3^k mod 256)*3) >> 8   quants.py:602-620
 //   IQ2_XS 74 B  d | 32 x u16 (9-bit grid index, 7-bit sign index) | 8 B scales
@@ -62,7 +65,7 @@ namespace kq {
 
 enum Codec : int {
     Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, TQ2_0 = 35, MXFP4 = 39, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ2_XS = 17, IQ3_XXS = 18, IQ4_NL = 20,
-    IQ1_S = 19, IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23, IQ1_M = 29, TQ1_0 = 34
+    IQ1_S = 19, IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23, IQ1_M = 29, TQ1_0 = 34, NVFP4 = 40
 };
 enum DType : int { F32 = 0, F16 = 1, BF16 = 2 };
 
@@ -89,6 +92,7 @@ template <> struct Fmt<IQ3_S> { static constexpr int bpb = 110; static constexpr
 template <> struct Fmt<IQ1_S> { static constexpr int bpb = 50; static constexpr int sub = 32; };
 template <> struct Fmt<IQ1_M> { static constexpr int bpb = 56; static constexpr int sub = 16; };
 template <> struct Fmt<TQ1_0> { static constexpr int bpb = 54; static constexpr int sub = 32; };
+template <> struct Fmt<NVFP4> { static constexpr int bpb = 144; static constexpr int sub = 16; };
 
 // The 32-weight legacy blocks: d (fp16; MXFP4: one e8m0 byte), m (fp16;
 // HASM), a u32 of fifth bits (HASH), then 16 nibble bytes; BB bytes per
@@ -102,6 +106,15 @@ template <int C> struct Legacy {
     static constexpr int QOFF = BB - 16;       // nibble bytes
     static constexpr int OFF = C == Q4_0 ? 8 : C == Q5_0 ? 16 : 0;
 };
+
+// NVFP4's scale: unsigned E4M3 (bias 7) times 0.5, 0 and 0x7F decoding to 0;
+// normal values are placed straight into f32 bits ((1 + m/8) 2^(e-8))
+__device__ __forceinline__ float ue4m3_half(uint32_t x) {
+    const uint32_t e = (x >> 3) & 15u, m = x & 7u;
+    if (x == 0u || x == 0x7Fu) return 0.f;
+    if (e == 0u) return (float)m * 0.0009765625f;  // m 2^-9 / 2
+    return __uint_as_float(((e + 119u) << 23) | (m << 20));
+}
 
 // ggml's e8m0 "half" scale: 2^(e-128) as f32 bits (e < 2: subnormal)
 __device__ __forceinline__ float e8m0_half(uint32_t e) {
@@ -119,7 +132,7 @@ __host__ __device__ inline int block_bytes(int codec) {
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144
          : codec == Q4_1 ? 160 : codec == Q5_0 ? 176 : codec == Q5_1 ? 192 : codec == MXFP4 ? 136 : codec == TQ2_0 ? 66
          : codec == IQ2_XS ? 74 : codec == IQ2_S ? 82 : codec == IQ3_S ? 110 : codec == IQ1_S ? 50 : codec == IQ1_M ? 56
-         : codec == TQ1_0 ? 54
+         : codec == TQ1_0 ? 54 : codec == NVFP4 ? 144
          : codec == Q2_K ? 84 : codec == Q3_K ? 110 : -1;
 }
 

@@ -67,6 +67,7 @@ template <> struct GCfg<IQ2_XS> { static constexpr int TABW = 8 * 8 * 4, BPW = 2
 template <> struct GCfg<IQ2_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<IQ3_S> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<MXFP4> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
+template <> struct GCfg<NVFP4> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<TQ1_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<TQ2_0> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };    // lane-per-row path only
 template <> struct GCfg<Q4_1> { static constexpr int TABW = 8 * 8 * 4, BPW = 2; };     // lane-per-row path only
@@ -1379,6 +1380,54 @@ __device__ __forceinline__ float dp_tq1_dot(const TQ1Regs &r, const uint32_t *xq
     return r.d * acc;
 }
 
+// Lane-per-row NVFP4: a lane takes a whole 144-byte group (four 36-byte
+// blocks, realigned into 36 words: block s = word 9s of scales, then 8 words
+// of nibbles); nibbles map to the doubled e2m1 bytes by two byte permutes and
+// a select (as IQ4_NL), each 16-weight sub-block J is one dot and one scale:
+//     acc += ue4m3(s_J)/2 * dx_(J/2) * S_J.
+struct NVRegs {
+    uint32_t q[36];
+};
+
+__device__ __forceinline__ void dp_nv_load(const uint8_t *grp, NVRegs &r) {
+    const uintptr_t ab = (uintptr_t)grp;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;
+    uint32_t w[37];
+#pragma unroll
+    for (int i = 0; i < 37; i++) w[i] = aw[i];  // up to 4 bytes past the group: the ring row has slack
+#pragma unroll
+    for (int j = 0; j < 36; j++) r.q[j] = __funnelshift_r(w[j], w[j + 1], sh);
+}
+
+__device__ __forceinline__ float dp_nv_dot(const NVRegs &r, const uint32_t *xq, const float *xsc) {
+    const uint32_t *tw = reinterpret_cast<const uint32_t *>(c_mxfp4_values);
+    const uint32_t tv[4] = {tw[0], tw[1], tw[2], tw[3]};
+    float acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < 4; s++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int J = 4 * s + j;  // 16-weight sub-block of the 256
+            int sum = 0;
+#pragma unroll
+            for (int u = 0; u < 2; u++) {  // bytes 4u .. 4u + 3 of the sub-block's 8
+                const uint32_t w = r.q[9 * s + 1 + 2 * j + u];
+                const int lo = iq4_lookup4(w & 0x0f0f0f0fu, tv), hi = iq4_lookup4((w >> 4) & 0x0f0f0f0fu, tv);
+                const uint2 xl = *reinterpret_cast<const uint2 *>(xq + 8 * J + 2 * u);
+                const uint2 xh = *reinterpret_cast<const uint2 *>(xq + 8 * J + 4 + 2 * u);
+                sum = __dp2a_lo((int)xl.x, lo, sum);
+                sum = __dp2a_hi((int)xl.y, lo, sum);
+                sum = __dp2a_lo((int)xh.x, hi, sum);
+                sum = __dp2a_hi((int)xh.y, hi, sum);
+            }
+            const float d = ue4m3_half((r.q[9 * s] >> (8 * j)) & 255u);
+            acc = fmaf(d * xsc[J >> 1], (float)sum, acc);
+        }
+    __syncwarp();  // xq is rewritten for the next block
+    return acc;
+}
+
 struct Q3Regs {
     uint32_t hm[8], q[16], s[3];
     float d;
@@ -1747,6 +1796,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             if (run)
                 acc += dp_iqs_dot<C>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab),
                                      reinterpret_cast<const uint32_t *>(gridtab));
+        } else if constexpr (C == NVFP4) {
+            NVRegs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+                dp_nv_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (run) acc += dp_nv_dot(r, xq, xsc);
         } else if constexpr (C == TQ1_0) {
             TQ1Regs r;
             if (run) {
@@ -2334,6 +2392,7 @@ cudaError_t dispatch(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     if (a.codec == IQ1_M) return launch_onerow_c<IQ1_M>(a, st, grid_out);
     if (a.codec == TQ2_0) return launch_onerow_c<TQ2_0>(a, st, grid_out);
     if (a.codec == TQ1_0) return launch_onerow_c<TQ1_0>(a, st, grid_out);
+    if (a.codec == NVFP4) return launch_onerow_c<NVFP4>(a, st, grid_out);
     if (a.codec == Q5_0) return launch_onerow_c<Q5_0>(a, st, grid_out);
     if (a.codec == Q5_1) return launch_onerow_c<Q5_1>(a, st, grid_out);
     if (a.codec == Q2_K) return launch_onerow_c<Q2_K>(a, st, grid_out);

@@ -33,7 +33,7 @@ GGML_TYPES = {
     20: ("iq4_nl", 32, 18), 21: ("iq3_s", 256, 110), 22: ("iq2_s", 256, 82), 23: ("iq4_xs", 256, 136),
     24: ("i8", 1, 1), 25: ("i16", 1, 2), 26: ("i32", 1, 4), 27: ("i64", 1, 8), 28: ("f64", 1, 8),
     29: ("iq1_m", 256, 56), 30: ("bf16", 1, 2), 34: ("tq1_0", 256, 54), 35: ("tq2_0", 256, 66),
-    39: ("mxfp4", 32, 17),
+    39: ("mxfp4", 32, 17), 40: ("nvfp4", 64, 36),
 }
 _NATIVE = {0: np.float32, 1: np.float16, 24: np.int8, 25: np.int16, 26: np.int32, 27: np.int64, 28: np.float64,
            30: np.uint16}  # bf16 is read as uint16 bits, viewed as torch.bfloat16

@@ -19,6 +19,8 @@ prescribe:
 * Q2_K (84 B): random scale and quant bytes, ``d``, ``dmin`` (the last four
   bytes) fp16(U[1e-4, 2e-3]).  Q3_K (110 B): random, ``d`` (the last two
   bytes) fp16(U[1e-4, 2e-3]).
+* NVFP4 (36 B per 64 weights, 144 B per 256): random nibbles, the four UE4M3
+  scale bytes of a block with exponent field 1..6 and any mantissa.
 * TQ1_0 (54 B): random digit bytes, ``d`` (the last two bytes)
   fp16(U[1e-4, 2e-3]).
 * MXFP4 (17 B per 32 weights, 136 B per 256): random nibbles, the e8m0
@@ -40,17 +42,17 @@ import numpy as np
 
 Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, TQ2_0, MXFP4 = 2, 3, 6, 7, 8, 10, 11, 35, 39
 Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ2_S, IQ4_XS = 12, 13, 14, 16, 17, 18, 20, 21, 22, 23
-IQ1_S, IQ1_M, TQ1_0 = 19, 29, 34
+IQ1_S, IQ1_M, TQ1_0, NVFP4 = 19, 29, 34, 40
 CODECS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
           "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K, "q4_1": Q4_1,
           "q5_0": Q5_0, "q5_1": Q5_1, "tq2_0": TQ2_0, "mxfp4": MXFP4, "iq2_xs": IQ2_XS, "iq2_s": IQ2_S,
-          "iq3_s": IQ3_S, "iq1_s": IQ1_S, "iq1_m": IQ1_M, "tq1_0": TQ1_0}
+          "iq3_s": IQ3_S, "iq1_s": IQ1_S, "iq1_m": IQ1_M, "tq1_0": TQ1_0, "nvfp4": NVFP4}
 CODEC_NAMES = {v: k for k, v in CODECS.items()}
 # bytes per 256 weights (Q8_0: eight 34-byte ggml blocks of 32 weights)
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
                Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192,
                TQ2_0: 66, MXFP4: 136, IQ2_XS: 74, IQ2_S: 82, IQ3_S: 110,
-               IQ1_S: 50, IQ1_M: 56, TQ1_0: 54}
+               IQ1_S: 50, IQ1_M: 56, TQ1_0: 54, NVFP4: 144}
 QK = 256
 D_LO, D_HI = 1e-4, 2e-3
 
@@ -108,6 +110,9 @@ def random_blocks(codec, n_blocks: int, seed: int = 0) -> np.ndarray:
         b[:, 64:66] = _fp16_bytes(rng, n_blocks)
     elif c == TQ1_0:
         b[:, 52:54] = _fp16_bytes(rng, n_blocks)
+    elif c == NVFP4:  # four 36-byte blocks per 256 weights
+        sub = b.reshape(n_blocks * 4, 36)
+        sub[:, 0:4] = (rng.integers(1, 7, size=(n_blocks * 4, 4)) << 3 | rng.integers(0, 8, size=(n_blocks * 4, 4)))
     elif c == MXFP4:
         b.reshape(n_blocks * 8, 17)[:, 0] = rng.integers(115, 126, size=n_blocks * 8, dtype=np.uint8)
     elif c in (Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL):  # eight 32-weight blocks per 256 weights

@@ -24,7 +24,7 @@
  *  - Codec ids are ggml's: Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16,
  *    IQ3_XXS = 18, IQ4_XS = 23, Q4_0 = 2, IQ4_NL = 20, Q2_K = 10, Q3_K = 11, Q4_1 = 3,
  *    Q5_0 = 6, Q5_1 = 7, TQ2_0 = 35, MXFP4 = 39, IQ2_XS = 17, IQ2_S = 22, IQ3_S = 21,
- *    IQ1_S = 19, IQ1_M = 29, TQ1_0 = 34.
+ *    IQ1_S = 19, IQ1_M = 29, TQ1_0 = 34, NVFP4 = 40.
  *    Activation / output dtypes: KQ_F32 = 0, KQ_F16 = 1, KQ_BF16 = 2.
  */
 #ifndef KQ_CUDA_H
@@ -47,6 +47,7 @@ extern "C" {
 #define KQ_IQ2_XS 17 /* 74-byte blocks */
 #define KQ_IQ3_S 21  /* 110-byte blocks */
 #define KQ_IQ2_S 22  /* 82-byte blocks */
+#define KQ_NVFP4 40 /* groups of four 36-byte blocks of 64 weights (144 bytes per 256) */
 #define KQ_TQ1_0 34 /* 54-byte blocks */
 #define KQ_TQ2_0 35 /* 66-byte blocks */
 #define KQ_MXFP4 39 /* groups of eight 17-byte blocks (136 bytes per 256 weights) */

@@ -28,6 +28,7 @@
  *   Q5_1   (:308-336): w = d*q + m  (Q5: q = nibble | qh bit << 4)
  *   MXFP4  (MXFP4.dequantize_blocks): w = e8m0_half(e) * kvalues[q] per 32 weights
  *   TQ2_0  (TQ2_0.dequantize_blocks): w = d*(q-1), q 2-bit, Q2_K's quant layout
+ *   NVFP4  (quants.py:707-763): w = ue4m3_half(s_j) * kvalues[q], s_j per 16 weights
  *   TQ1_0  (quants.py:602-620): trit k of byte b = ((b*3^k mod 256)*3) >> 8, w = d*(t-1)
  *   IQ1_S  (quants.py:1267-1288): dl = d*(2s+1) per 32, w = dl*(grid + delta), delta = +-0.125
  *   IQ1_M  (quants.py:1300-1327): the same with s per 16, delta per 8, d packed in the scales
@@ -51,7 +52,7 @@
 enum { KQO_Q8_0 = 8, KQO_Q4_K = 12, KQO_Q5_K = 13, KQO_Q6_K = 14, KQO_IQ2_XXS = 16, KQO_IQ3_XXS = 18, KQO_IQ4_XS = 23,
        KQO_Q4_0 = 2, KQO_IQ4_NL = 20, KQO_Q2_K = 10, KQO_Q3_K = 11,
        KQO_Q4_1 = 3, KQO_Q5_0 = 6, KQO_Q5_1 = 7, KQO_TQ2_0 = 35, KQO_MXFP4 = 39,
-       KQO_IQ2_XS = 17, KQO_IQ3_S = 21, KQO_IQ2_S = 22, KQO_IQ1_S = 19, KQO_IQ1_M = 29, KQO_TQ1_0 = 34 };
+       KQO_IQ2_XS = 17, KQO_IQ3_S = 21, KQO_IQ2_S = 22, KQO_IQ1_S = 19, KQO_IQ1_M = 29, KQO_TQ1_0 = 34, KQO_NVFP4 = 40 };
 
 static const uint64_t kqo_grid[256] = KQ_IQ2XXS_GRID_INIT;
 static const uint32_t kqo_grid3[256] = KQ_IQ3XXS_GRID_INIT;
@@ -94,6 +95,7 @@ int kqo_block_bytes(int codec) {
     case KQO_TQ2_0: return 66;
     case KQO_IQ2_XS: return 74; case KQO_IQ2_S: return 82; case KQO_IQ3_S: return 110;
     case KQO_IQ1_S: return 50; case KQO_IQ1_M: return 56; case KQO_TQ1_0: return 54;
+    case KQO_NVFP4: return 144; /* four 36-byte blocks of 64 weights */
     }
     return -1;
 }
@@ -427,6 +429,29 @@ static void deq_tq10(const uint8_t *b, float *o) {
     }
 }
 
+/* gguf-py NVFP4.ue4m3_to_fp32: unsigned E4M3 (bias 7) times 0.5; 0 and 0x7F
+ * decode to 0. */
+static float kqo_ue4m3_half(uint8_t x) {
+    int e = (x >> 3) & 15, m = x & 7;
+    if (x == 0 || x == 0x7F) return 0.0f;
+    float raw = e == 0 ? (float)m * 0.001953125f : (1.0f + (float)m / 8.0f) * ldexpf(1.0f, e - 7);
+    return raw * 0.5f;
+}
+
+/* gguf-py NVFP4.dequantize_blocks over four 36-byte blocks: four scale bytes
+ * (one per 16 weights), then 4 x 8 bytes (low nibbles weights 0-7, high
+ * nibbles 8-15 of each 16) indexing the doubled e2m1 values. */
+static void deq_nvfp4(const uint8_t *b, float *o) {
+    for (int s = 0; s < 4; s++) {
+        const uint8_t *blk = b + 36 * s;
+        for (int j = 0; j < 4; j++) {
+            float d = kqo_ue4m3_half(blk[j]);
+            for (int l = 0; l < 16; l++)
+                o[64 * s + 16 * j + l] = d * (float)kqo_mxfp4[(blk[4 + 8 * j + (l & 7)] >> (4 * (l >> 3))) & 15];
+        }
+    }
+}
+
 static int deq_block(int codec, const uint8_t *b, float *o) {
     switch (codec) {
     case KQO_Q4_K: deq_q4k(b, o); return 0;
@@ -445,6 +470,7 @@ static int deq_block(int codec, const uint8_t *b, float *o) {
     case KQO_IQ3_S: deq_iq3s(b, o); return 0;
     case KQO_IQ1_S: deq_iq1s(b, o); return 0;
     case KQO_TQ1_0: deq_tq10(b, o); return 0;
+    case KQO_NVFP4: deq_nvfp4(b, o); return 0;
     case KQO_IQ1_M: deq_iq1m(b, o); return 0;
     case KQO_Q3_K: deq_q3k(b, o); return 0;
     }

@@ -33,15 +33,15 @@ LIB_PATH = os.path.join(HERE, "_build", "libkq_oracle.so")
 
 Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, TQ2_0, MXFP4 = 2, 3, 6, 7, 8, 10, 11, 35, 39
 Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ2_S, IQ4_XS = 12, 13, 14, 16, 17, 18, 20, 21, 22, 23
-IQ1_S, IQ1_M, TQ1_0 = 19, 29, 34
+IQ1_S, IQ1_M, TQ1_0, NVFP4 = 19, 29, 34, 40
 CODEC_IDS = {"q4_k": Q4_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq2_xxs": IQ2_XXS, "q8_0": Q8_0, "iq3_xxs": IQ3_XXS,
              "iq4_xs": IQ4_XS, "q4_0": Q4_0, "iq4_nl": IQ4_NL, "q2_k": Q2_K, "q3_k": Q3_K, "q4_1": Q4_1,
              "q5_0": Q5_0, "q5_1": Q5_1, "tq2_0": TQ2_0, "mxfp4": MXFP4, "iq2_xs": IQ2_XS, "iq2_s": IQ2_S,
-             "iq3_s": IQ3_S, "iq1_s": IQ1_S, "iq1_m": IQ1_M, "tq1_0": TQ1_0}
+             "iq3_s": IQ3_S, "iq1_s": IQ1_S, "iq1_m": IQ1_M, "tq1_0": TQ1_0, "nvfp4": NVFP4}
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS: 98, IQ4_XS: 136,
                Q4_0: 144, IQ4_NL: 144, Q2_K: 84, Q3_K: 110, Q4_1: 160, Q5_0: 176, Q5_1: 192,
                TQ2_0: 66, MXFP4: 136, IQ2_XS: 74, IQ2_S: 82, IQ3_S: 110,
-               IQ1_S: 50, IQ1_M: 56, TQ1_0: 54}  # per 256 weights
+               IQ1_S: 50, IQ1_M: 56, TQ1_0: 54, NVFP4: 144}  # per 256 weights
 QK = 256
 
 _lib = None
@@ -279,6 +279,16 @@ def np_dequantize(w: np.ndarray, codec) -> np.ndarray:
             delta = np.where(nib & 8, np.float32(-0.125), np.float32(0.125))
             idx = blocks[:, 0:32].astype(np.int64) | ((nib & 7).astype(np.int64) << 8)
         out = dl.reshape(n, 32, 1) * (grid[idx] + delta.reshape(n, 32, 1))
+    elif c == NVFP4:  # NVFP4.dequantize_blocks (quants.py:707-763): four 36-byte blocks of 64
+        sub = blocks.reshape(n * 4, 36)
+        x = sub[:, 0:4].astype(np.int32)
+        e, m = (x >> 3) & 15, (x & 7).astype(np.float32)
+        raw = np.where(e == 0, m * np.float32(2.0 ** -9),
+                       (np.float32(1) + m / np.float32(8)) * np.exp2(e - 7).astype(np.float32))
+        d = np.where((x == 0) | (x == 0x7F), np.float32(0), raw * np.float32(0.5)).astype(np.float32)
+        q = sub[:, 4:].reshape(n * 4, 4, 1, 8) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
+        v = np.array(_table_values("KQ_MXFP4_VALUES_INIT"), np.float32)[(q & 15).reshape(n * 4, 4, 16)]
+        out = d.reshape(n * 4, 4, 1) * v
     elif c == TQ1_0:  # TQ1_0.dequantize_blocks (quants.py:602-620)
         p5 = np.array([1, 3, 9, 27, 81], np.uint16)
         t0 = (blocks[:, 0:32].reshape(n, 1, 32).astype(np.uint16) * p5.reshape(1, 5, 1)) & 255

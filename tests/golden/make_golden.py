@@ -26,6 +26,7 @@ Each codec gets (a) seeded random blocks per the benchmark statistics and
           sweep, 4-bit scales 0 and 15;
   IQ1_S, IQ1_M  every grid index, both delta signs, 3-bit scales 0 and 7;
   TQ1_0   every byte value in every digit position, d < 0;
+  NVFP4   every UE4M3 scale byte (0, subnormals, 0x7F, normals), every nibble;
   TQ2_0   values all 0 / 1 / 2 / 3 (3 is outside the ternary set but decodes), d < 0;
   IQ4_NL  every nibble value on every block, negative d;
   Q2_K    scale / min nibbles 0 and 15, quants all 0 / all 3, one-hot
@@ -52,7 +53,7 @@ QT = {"q4_k": T.Q4_K, "q5_k": T.Q5_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS, "q8_
       "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
       "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1, "tq2_0": T.TQ2_0,
       "mxfp4": T.MXFP4, "iq2_xs": T.IQ2_XS, "iq2_s": T.IQ2_S, "iq3_s": T.IQ3_S,
-      "iq1_s": T.IQ1_S, "iq1_m": T.IQ1_M, "tq1_0": T.TQ1_0}
+      "iq1_s": T.IQ1_S, "iq1_m": T.IQ1_M, "tq1_0": T.TQ1_0, "nvfp4": T.NVFP4}
 
 
 def fp16(v):
@@ -211,6 +212,12 @@ def edge_blocks(codec):
             b[:, 0] = rng.integers(110, 130, 8) if ev is None else ev
             b[:, 1:] = (np.arange(16) | (((np.arange(16) + 3) % 16) << 4)).astype(np.uint8)
             blocks.append(b.reshape(136))
+    elif codec == "nvfp4":  # 144-byte groups of four 36-byte blocks
+        for grp in range(16):
+            b = np.zeros((4, 36), np.uint8)
+            b[:, 0:4] = (np.arange(16) + 16 * grp).reshape(4, 4).astype(np.uint8)
+            b[:, 4:] = ((np.arange(32) * 7 + grp) % 256).astype(np.uint8)
+            blocks.append(b.reshape(144))
     elif codec == "tq1_0":
         for blk in range(6):
             b = np.zeros(54, np.uint8)

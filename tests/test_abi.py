@@ -31,11 +31,11 @@ def test_codecs_and_block_bytes():
     buf = (ctypes.c_int * 12)()
     buf = (ctypes.c_int * 16)()
     buf = (ctypes.c_int * 24)()
-    assert L.kq_codecs(buf, 24) == 22
-    ids = [12, 13, 14, 16, 8, 18, 23, 2, 20, 10, 11, 3, 6, 7, 35, 39, 17, 22, 21, 19, 29, 34]
-    assert list(buf[:22]) == ids
+    assert L.kq_codecs(buf, 24) == 23
+    ids = [12, 13, 14, 16, 8, 18, 23, 2, 20, 10, 11, 3, 6, 7, 35, 39, 17, 22, 21, 19, 29, 34, 40]
+    assert list(buf[:23]) == ids
     assert [L.kq_block_bytes(c) for c in ids + [1]] == [
-        144, 176, 210, 66, 272, 98, 136, 144, 144, 84, 110, 160, 176, 192, 66, 136, 74, 82, 110, 50, 56, 54, -1]
+        144, 176, 210, 66, 272, 98, 136, 144, 144, 84, 110, 160, 176, 192, 66, 136, 74, 82, 110, 50, 56, 54, 144, -1]
     assert L.kq_codec_has_matmul(12) == 1 and L.kq_codec_has_matmul(8) == 1 and L.kq_codec_has_matmul(1) == 0
     assert L.kq_version() >= 100
 

@@ -16,7 +16,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
 CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs", "q4_0", "iq4_nl", "q2_k", "q3_k", "q4_1",
-          "q5_0", "q5_1", "tq2_0", "mxfp4", "iq2_xs", "iq2_s", "iq3_s", "iq1_s", "iq1_m", "tq1_0"]
+          "q5_0", "q5_1", "tq2_0", "mxfp4", "iq2_xs", "iq2_s", "iq3_s", "iq1_s", "iq1_m", "tq1_0", "nvfp4"]
 
 
 def rel_err(y, ref):
@@ -89,6 +89,7 @@ def test_quantized_matmul(cuda, codec, m, n, k):
     ("iq1_s", 4096, 4096),
     ("iq1_m", 512, 14336),
     ("tq1_0", 19200, 512),
+    ("nvfp4", 4096, 4096),
     ("mxfp4", 512, 14336),
     ("q5_0", 512, 14336),
     ("q5_1", 4096, 4096),
@@ -214,7 +215,7 @@ def _moe_case(codec_gu, codec_d, e, d, f, t, k, seed):
                                              ("q4_0", "iq4_nl"), ("q2_k", "q3_k"), ("q4_1", "q5_1"),
                                              ("q5_0", "q5_0"), ("mxfp4", "tq2_0"), ("iq2_xs", "iq2_s"),
                                              ("iq3_s", "iq3_s"), ("iq1_s", "iq1_m"),
-                                             ("tq1_0", "tq1_0")])
+                                             ("tq1_0", "tq1_0"), ("nvfp4", "nvfp4")])
 @pytest.mark.parametrize("t", [1, 5])
 def test_moe_decode_ops(cuda, codec_gu, codec_d, t):
     e, d, f, k = 16, 512, 256, 4

@@ -10,7 +10,7 @@ from oracle import oracle as O
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_blocks.npz")
 CODECS = ["q4_k", "q5_k", "q6_k", "iq2_xxs", "q8_0", "iq3_xxs", "iq4_xs", "q4_0", "iq4_nl", "q2_k", "q3_k", "q4_1",
-          "q5_0", "q5_1", "tq2_0", "mxfp4", "iq2_xs", "iq2_s", "iq3_s", "iq1_s", "iq1_m", "tq1_0"]
+          "q5_0", "q5_1", "tq2_0", "mxfp4", "iq2_xs", "iq2_s", "iq3_s", "iq1_s", "iq1_m", "tq1_0", "nvfp4"]
 
 
 @pytest.fixture(scope="module")
@@ -49,7 +49,7 @@ def test_oracle_matches_gguf_py_random(codec, seed):
           "iq3_xxs": T.IQ3_XXS, "iq4_xs": T.IQ4_XS, "q4_0": T.Q4_0, "iq4_nl": T.IQ4_NL, "q2_k": T.Q2_K,
           "q3_k": T.Q3_K, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1, "tq2_0": T.TQ2_0,
           "mxfp4": T.MXFP4, "iq2_xs": T.IQ2_XS, "iq2_s": T.IQ2_S, "iq3_s": T.IQ3_S,
-          "iq1_s": T.IQ1_S, "iq1_m": T.IQ1_M, "tq1_0": T.TQ1_0}[codec]
+          "iq1_s": T.IQ1_S, "iq1_m": T.IQ1_M, "tq1_0": T.TQ1_0, "nvfp4": T.NVFP4}[codec]
     w = synth.random_weight(codec, 256, 2048, seed=seed)  # 2048 blocks per seed
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt)))
 
@@ -67,7 +67,7 @@ def test_raw_random_bytes_match_where_finite():
                            ("q5_0", T.Q5_0, 176), ("q5_1", T.Q5_1, 192), ("tq2_0", T.TQ2_0, 66),
                            ("mxfp4", T.MXFP4, 136), ("iq2_xs", T.IQ2_XS, 74), ("iq2_s", T.IQ2_S, 82),
                            ("iq3_s", T.IQ3_S, 110), ("iq1_s", T.IQ1_S, 50), ("iq1_m", T.IQ1_M, 56),
-                           ("tq1_0", T.TQ1_0, 54)]:
+                           ("tq1_0", T.TQ1_0, 54), ("nvfp4", T.NVFP4, 144)]:
         w = rng.integers(0, 256, size=(64, 4 * bpb), dtype=np.uint8)
         a, b = O.dequantize(w, codec), gq.dequantize(w, qt).astype(np.float32)
         fin = np.isfinite(b)
@@ -147,6 +147,9 @@ def test_synthetic_block_statistics():
             db = (sc[:, 0] >> 12) | ((sc[:, 1] >> 8) & 0xF0) | ((sc[:, 2] >> 4) & 0xF00) | (sc[:, 3] & 0xF000)
             d = db.astype(np.uint16).view(np.float16).astype(np.float32)
             assert d.min() >= 9e-5 and d.max() <= 2.01e-3
+        elif codec == "nvfp4":
+            e = (w.reshape(-1, 36)[:, 0:4] >> 3) & 15
+            assert e.min() >= 1 and e.max() <= 6
         elif codec == "mxfp4":
             e = w.reshape(-1, 17)[:, 0]
             assert e.min() >= 115 and e.max() <= 125
@@ -185,9 +188,9 @@ def test_legacy_round_trip_through_gguf_quantizer(codec, bb):
     from gguf import quants as gq
     from gguf.constants import GGMLQuantizationType as T
     qt = {"q4_0": T.Q4_0, "q4_1": T.Q4_1, "q5_0": T.Q5_0, "q5_1": T.Q5_1, "tq2_0": T.TQ2_0, "mxfp4": T.MXFP4,
-          "tq1_0": T.TQ1_0}[codec]
+          "tq1_0": T.TQ1_0, "nvfp4": T.NVFP4}[codec]
     rng = np.random.default_rng(10)
     wf = (rng.standard_normal((32, 1024)) * 0.02).astype(np.float32)
     w = gq.quantize(wf, qt)
-    assert w.shape == (32, 1024 // (256 if codec in ("tq2_0", "tq1_0") else 32) * bb)
+    assert w.shape == (32, 1024 // {"tq2_0": 256, "tq1_0": 256, "nvfp4": 64}.get(codec, 32) * bb)
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt).astype(np.float32)))
