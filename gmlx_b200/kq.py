@@ -37,7 +37,7 @@ from . import _lib
 from .synth import BLOCK_BYTES, CODECS, QK, codec_id
 
 __all__ = [
-    "codecs", "codec_has_matmul", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
+    "codecs", "codec_has_matmul", "codec_has_moe_glu", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
     "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
     "moe_expert_layer_local", "quantized_matmul_allreduce", "quantized_matmul_qmv_bias", "moe_glu_gather_shexp_kq", "gather_qmv_mix_kq",
 ]
@@ -61,6 +61,14 @@ def codec_has_matmul(codec) -> bool:
     except ValueError:
         return False
     return bool(_lib.load().kq_codec_has_matmul(c))
+
+
+def codec_has_moe_glu(codec) -> bool:
+    """Whether the fused MoE ops (``moe_glu_gather_kq`` and the down/mix
+    gathers) take ``codec``: gmlx's fused-MoE capability probe asks this for
+    the native-fp codecs (modules.py:177-181).  Every codec with kernels here
+    qualifies (decode groups of one slot or the grouped tensor-core GEMM)."""
+    return codec_has_matmul(codec)
 
 
 def block_bytes(codec) -> int:

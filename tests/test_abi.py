@@ -60,3 +60,14 @@ def test_python_ops_fail_loudly_without_cuda():
         kq.dequantize(w, None, "q4_k")
     with pytest.raises(NotImplementedError):
         kq.dequantize(w, None, "iq4_ks")
+
+
+def test_capability_queries_for_the_fused_moe_probe():
+    """gmlx's fused-MoE probe asks codec_has_moe_glu for mxfp4 / nvfp4 and reads
+    the kq ops' docstrings for the kwargs they take (modules.py:161-234)."""
+    from gmlx_b200 import kq
+    assert kq.codec_has_moe_glu("mxfp4") and kq.codec_has_moe_glu("nvfp4") and kq.codec_has_moe_glu("q4_k")
+    assert not kq.codec_has_moe_glu("iq4_ks")
+    assert "per_expert_scale" in kq.moe_router_topk.__doc__
+    assert all(hasattr(kq, n) for n in ("moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_kq",
+                                        "gather_qmv_mix_ns_kq", "moe_router_topk", "codecs"))
