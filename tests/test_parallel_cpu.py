@@ -107,3 +107,24 @@ def test_split_helpers():
     w = synth.random_weight("q6_k", 4, 2048, seed=1)
     s = par.shard_k(w, "q6_k", 4, 1)
     assert s.shape == (4, 2 * 210) and np.array_equal(s, w[:, 420:840])
+
+
+def test_k_shards_of_every_codec_sum_to_the_full_product():
+    """Row-parallel K shards cut at whole 256-weight groups for every codec
+    (the 32/64-weight codecs' groups of blocks included): the shards
+    reassemble the wire rows and their oracle products sum to the full one."""
+    from gmlx_b200 import parallel as par, synth
+    from oracle import oracle as O
+    for codec in sorted(synth.CODECS):
+        w = synth.random_weight(codec, 16, 2048, seed=5)
+        x = synth.random_activations(2, 2048, seed=6)
+        full = O.matmul(x, w, codec).astype(np.float64)
+        parts, acc, k0 = [], np.zeros_like(full), 0
+        for r in range(4):
+            ws = np.ascontiguousarray(par.shard_k(w, codec, 4, r))
+            kk = ws.shape[1] // synth.BLOCK_BYTES[synth.codec_id(codec)] * 256
+            acc += O.matmul(np.ascontiguousarray(x[:, k0:k0 + kk]), ws, codec)
+            parts.append(ws)
+            k0 += kk
+        assert k0 == 2048 and np.array_equal(np.concatenate(parts, 1), w), codec
+        assert np.abs(acc - full).max() <= 1e-4 * np.abs(full).max(), codec
