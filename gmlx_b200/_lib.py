@@ -47,6 +47,7 @@ SIGNATURES = {
                                          _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _i32, _vp, _sz, _vp]),
     "kq_moe_expert_layer_workspace_size": (_sz, [_i32, _i32, _i64, _i32, _i64, _i64, _i64, _i32]),
     "kq_quantized_matmul_noalloc": (_i32, [_i32, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _vp]),
+    "kq_noalloc_error": (_i32, [_i32, _vp]),
     "kq_quantized_matmul_bias": (_i32, [_i32, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _i32, _i64,
                                         _vp, _sz, _vp]),
     "kq_allreduce_buffer_bytes": (_sz, [_i32, _i64]),

@@ -153,12 +153,19 @@ bool use_gemm(int64_t m, int codec = 0) {
     return m >= gemm_min_m() || (onerow_only(codec) && m >= 2);
 }
 
-size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
-    if (use_gemm(m, codec)) return plan(0, gemm_scratch_bytes(codec, m, n, k, act != ACT_NONE), 0, 0).total;
-    GemvArgs a = dense_args(codec, nullptr, KQ_BF16, m, k, k, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
+// workspace bytes of the path run_dense takes for these activations (the
+// GEMM when the batch is prefill-sized and the GEMM takes this layout)
+size_t dense_ws_x(int codec, int64_t m, int64_t n, int64_t k, int act, int x_dtype, int64_t xs) {
+    if (use_gemm(m, codec) && gemm_supported(codec, m, n, k, x_dtype, xs))
+        return plan(0, gemm_scratch_bytes(codec, m, n, k, act != ACT_NONE), 0, 0).total;
+    GemvArgs a = dense_args(codec, nullptr, x_dtype, m, k, xs, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
     size_t pb, cb;
     gemv_scratch_need(a, &pb, &cb);
     return plan(0, 0, cb, pb).total;
+}
+
+size_t dense_ws(int codec, int64_t m, int64_t n, int64_t k, int act) {
+    return dense_ws_x(codec, m, n, k, act, KQ_BF16, k);
 }
 
 int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t xs, const void *w, const void *w2,
@@ -619,6 +626,12 @@ size_t routed_ws(int codec, int64_t slots, int64_t per_expert, int64_t e, int64_
 
 }  // namespace
 
+namespace kq {
+size_t dense_matmul_workspace_bytes(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride) {
+    return dense_ws_x(codec, m, n, k, ACT_NONE, x_dtype, x_row_stride);
+}
+}  // namespace kq
+
 void kq::set_last_error(const char *msg) { snprintf(g_msg, sizeof(g_msg), "%s", msg); }
 
 extern "C" {
@@ -631,7 +644,7 @@ int kq_codecs(int *out, int cap) {
     static const int ids[23] = {KQ_Q4_K, KQ_Q5_K, KQ_Q6_K, KQ_IQ2_XXS, KQ_Q8_0, KQ_IQ3_XXS, KQ_IQ4_XS, KQ_Q4_0,
                                 KQ_IQ4_NL, KQ_Q2_K, KQ_Q3_K, KQ_Q4_1, KQ_Q5_0, KQ_Q5_1, KQ_TQ2_0, KQ_MXFP4,
                                 KQ_IQ2_XS, KQ_IQ2_S, KQ_IQ3_S, KQ_IQ1_S, KQ_IQ1_M, KQ_TQ1_0, KQ_NVFP4};
-    for (int i = 0; i < 23 && i < cap; i++) out[i] = ids[i];
+    for (int i = 0; out && i < 23 && i < cap; i++) out[i] = ids[i];
     return 23;
 }
 

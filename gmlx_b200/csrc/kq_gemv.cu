@@ -2282,7 +2282,7 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
         } else if (units <= cap && nst <= L::NS) {
             d = 1;
             cap = units;
-        } else if (getenv("KQ_GEMV_KSPLIT") || a.ar_world) {
+        } else if (dev_env("KQ_GEMV_KSPLIT") || a.ar_world) {
             // split K into chunks so there are >= 2 units per CTA (off by default:
             // each chunk's partial publish stalls its CTA on a gpu-scope fence,
             // slower than stream-K's at most two partial tiles per CTA)

@@ -163,5 +163,8 @@ inline const char *dev_env(const char *name) {
 }
 // Sets the calling thread's kq_last_error() message.
 void set_last_error(const char *msg);
+// workspace bytes kq_quantized_matmul needs for exactly these activations
+// (the same GEMV / GEMM choice the call makes)
+size_t dense_matmul_workspace_bytes(int codec, int64_t m, int64_t n, int64_t k, int x_dtype, int64_t x_row_stride);
 
 }  // namespace kq

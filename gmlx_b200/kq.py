@@ -37,7 +37,7 @@ from . import _lib
 from .synth import BLOCK_BYTES, CODECS, QK, codec_id
 
 __all__ = [
-    "codecs", "codec_has_matmul", "codec_has_moe_glu", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
+    "codecs", "all_codecs", "codec_has_matmul", "codec_has_moe_glu", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
     "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
     "moe_expert_layer_local", "quantized_matmul_allreduce", "quantized_matmul_qmv_bias", "moe_glu_gather_shexp_kq", "gather_qmv_mix_kq",
 ]
@@ -46,13 +46,31 @@ _DT = {torch.float32: _lib.KQ_F32, torch.float16: _lib.KQ_F16, torch.bfloat16: _
 _TORCH_DT = {v: k for k, v in _DT.items()}
 
 
-def codecs() -> list[str]:
-    """Codec names with kernels here (the loader whitelists against this)."""
+# The codec names gmlx's loader whitelists (gmlx/preflight.py:23-30); the
+# reference's own check compares kq.codecs() with this set for EQUALITY
+# (tests/test_preflight.py:96-99), so the ternary TQ1_0 / TQ2_0 codecs, which
+# have kernels here but are not on gmlx's list, are reported by all_codecs().
+GMLX_CODECS = ("q2_k", "q3_k", "q4_k", "q5_k", "q6_k", "q4_0", "q4_1", "q5_0", "q5_1", "q8_0", "iq4_nl",
+               "iq4_xs", "iq3_s", "iq3_xxs", "iq2_xxs", "iq2_xs", "iq2_s", "iq1_s", "iq1_m", "mxfp4", "nvfp4")
+
+
+def all_codecs() -> list[str]:
+    """Every codec name with kernels in libkq_cuda.so (the C ABI's
+    kq_codecs list, sized from its own count)."""
     L = _lib.load()
-    buf = (_ct.c_int * 8)()
-    n = L.kq_codecs(buf, 8)
+    n = L.kq_codecs(None, 0)
+    buf = (_ct.c_int * max(n, 1))()
+    n = L.kq_codecs(buf, n)
     names = {v: k for k, v in CODECS.items()}
-    return [names[buf[i]] for i in range(min(n, 8))]
+    return [names[buf[i]] for i in range(n)]
+
+
+def codecs() -> list[str]:
+    """Codec names the loader may serve (gmlx gates loading on
+    ``set(kq.codecs())``, modules.py:1442, :1524, loader.py:2798-2801): the
+    21 codecs of gmlx's list, every one backed by kernels here."""
+    have = set(all_codecs())
+    return [c for c in GMLX_CODECS if c in have]
 
 
 def codec_has_matmul(codec) -> bool:

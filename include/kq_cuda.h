@@ -204,7 +204,6 @@ int kq_moe_expert_layer_local(int codec_gu, int codec_d, const void *x, int x_dt
 size_t kq_moe_expert_layer_workspace_size(int codec_gu, int codec_d, int64_t t, int k, int64_t e_local, int64_t d,
                                           int64_t f, int h_dtype);
 
-/* Size of the fixed scratch array behind kq_quantized_matmul_noalloc. */
 /* kq.quantized_matmul_qmv_bias(x, w, scales, bias, codec): y = x . dequant(w)^T
  * + bias in one dispatch (gmlx/qkv_fuse.py:80, the row-concatenated q|k|v
  * projection with its biases).  bias [n] in KQ_F32 / KQ_F16 / KQ_BF16; the
@@ -242,6 +241,7 @@ int kq_ipc_handle(const void *ptr, void *handle64);
 int kq_ipc_open(const void *handle64, void **ptr);
 int kq_ipc_close(void *ptr);
 
+/* Size of the fixed scratch array behind kq_quantized_matmul_noalloc. */
 #define KQ_NOALLOC_SCRATCH_BYTES (4 << 20)
 
 /* kq_quantized_matmul for callers that cannot allocate device memory (a host
@@ -254,10 +254,20 @@ int kq_ipc_close(void *ptr);
  * device looks up that array's device address (make it before any stream
  * capture); each call clears the scratch it uses on `stream`; calls whose GPU
  * work overlaps race on the shared array.  Shapes needing more scratch than
- * the array holds return KQ_ERR_WORKSPACE. */
+ * the array holds return KQ_ERR_WORKSPACE.  The cached address is not valid
+ * across cudaDeviceReset: do not use this entry point after resetting a
+ * device it has run on. */
 int kq_quantized_matmul_noalloc(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64_t x_row_stride,
                                 const void *w, int64_t n, int64_t w_row_stride, void *y, int y_dtype,
                                 int64_t y_row_stride, void *stream);
+
+/* The device error word of kq_quantized_matmul_noalloc's scratch on the
+ * current device (no counterpart in the reference; the accessor of the
+ * allocation-free entry point): 0, or the code that a kernel of the last call
+ * recorded when a bounded wait ran out.  Read it before the next call, which
+ * clears it.  Synchronises `stream`; clear != 0 resets the word; < 0 on a
+ * CUDA failure. */
+int kq_noalloc_error(int clear, void *stream);
 
 /* Reads (and with clear != 0 resets) the workspace's device error word;
  * synchronises `stream`.  Returns the word (0 = no device-side error). */

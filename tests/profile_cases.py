@@ -1,6 +1,6 @@
-"""Small, fixed invocations of single kq ops for profiler captures.
+"""Profiler-capture harness (not collected by pytest): small, fixed invocations of single kq ops for profiler captures.
 
-    python -m gmlx_b200.profile_cases <case> [launches]
+    python tests/profile_cases.py <case> [launches]
 
 Each case builds seeded synthetic weights (the bench's shapes), runs the op
 `launches` times (default 3) on cuda:0 and synchronizes.  Cases:
@@ -14,11 +14,13 @@ Each case builds seeded synthetic weights (the bench's shapes), runs the op
   prefill_down  Q6_K 4096x14336 GEMM, M=2048
   moe_prefill   Qwen3-like expert layer, T=512 (grouped GEMM path)
 """
+import os
 import sys
 
 import torch
 
-from . import kq, synth
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from gmlx_b200 import kq, synth  # noqa: E402
 
 
 def _w(codec, n, k, seed, experts=None):

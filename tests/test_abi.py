@@ -27,10 +27,8 @@ def test_header_symbols_exported():
 
 def test_codecs_and_block_bytes():
     L = _lib.load()
-    buf = (ctypes.c_int * 8)()
-    buf = (ctypes.c_int * 12)()
-    buf = (ctypes.c_int * 16)()
     buf = (ctypes.c_int * 24)()
+    assert L.kq_codecs(None, 0) == 23
     assert L.kq_codecs(buf, 24) == 23
     ids = [12, 13, 14, 16, 8, 18, 23, 2, 20, 10, 11, 3, 6, 7, 35, 39, 17, 22, 21, 19, 29, 34, 40]
     assert list(buf[:23]) == ids
@@ -71,3 +69,20 @@ def test_capability_queries_for_the_fused_moe_probe():
     assert "per_expert_scale" in kq.moe_router_topk.__doc__
     assert all(hasattr(kq, n) for n in ("moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_kq",
                                         "gather_qmv_mix_ns_kq", "moe_router_topk", "codecs"))
+
+
+# gmlx's loader whitelist (gmlx/preflight.py:23-30, SUPPORTED_QUANT_TYPES)
+GMLX_SUPPORTED_QUANT_TYPES = {"Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0",
+                              "IQ4_NL", "IQ4_XS", "IQ3_S", "IQ3_XXS", "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ1_S",
+                              "IQ1_M", "MXFP4", "NVFP4"}
+
+
+def test_codecs_match_the_loader_whitelist():
+    """gmlx gates loading on set(kq.codecs()) (modules.py:1442, :1524,
+    loader.py:2798-2801), and its own preflight test asks for equality with
+    SUPPORTED_QUANT_TYPES (tests/test_preflight.py:96-99)."""
+    from gmlx_b200 import kq
+    assert {c.lower() for c in GMLX_SUPPORTED_QUANT_TYPES} == set(kq.codecs())
+    assert len(kq.codecs()) == 21
+    assert set(kq.all_codecs()) == set(kq.codecs()) | {"tq1_0", "tq2_0"}
+    assert all(kq.codec_has_matmul(c) for c in kq.all_codecs())

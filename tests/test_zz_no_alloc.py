@@ -26,13 +26,19 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-@pytest.mark.parametrize("codec,n,k,m", [("q4_k", 4096, 4096, 1), ("q6_k", 1024, 14336, 3), ("iq2_xxs", 2048, 2048, 12)])
-def test_noalloc_matches_workspace_entry(cuda, codec, n, k, m):
+@pytest.mark.parametrize("codec,n,k,m,xpad", [("q4_k", 4096, 4096, 1, 0), ("q6_k", 1024, 14336, 3, 0),
+                                               ("iq2_xxs", 2048, 2048, 12, 0), ("q4_k", 512, 2048, 64, 24)])
+def test_noalloc_matches_workspace_entry(cuda, codec, n, k, m, xpad):
     L = _lib.load()
     c = synth.codec_id(codec)
     w = torch.from_numpy(synth.random_weight(codec, n, k, seed=71)).to(cuda)
     xb = synth.random_activations(m, k, seed=72)
-    x = torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).to(cuda)
+    # xpad > 0: activation rows at a padded stride (the scratch must be sized
+    # for the path these activations take, not for a dense layout)
+    xs = k + xpad
+    xfull = torch.zeros(m, xs, dtype=torch.bfloat16, device=cuda)
+    xfull[:, :k] = torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).to(cuda)
+    x = xfull
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
     # existing entry point with a caller-allocated (zeroed) workspace
@@ -40,15 +46,17 @@ def test_noalloc_matches_workspace_entry(cuda, codec, n, k, m):
     assert 0 < wsb <= (4 << 20)
     ws = torch.zeros(wsb, dtype=torch.uint8, device=cuda)
     y_ref = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
-    _lib.check(L.kq_quantized_matmul(c, _p(x), KQ_BF16, m, k, k, _p(w), n, w.shape[1], _p(y_ref), KQ_BF16, n,
+    _lib.check(L.kq_quantized_matmul(c, _p(x), KQ_BF16, m, k, xs, _p(w), n, w.shape[1], _p(y_ref), KQ_BF16, n,
                                      _p(ws), wsb, stream))
     # the no-allocation entry point, twice in a row (the shared scratch keeps
     # the previous call's contents; the second result must not change)
     outs = []
     for _ in range(2):
         y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda)
-        _lib.check(L.kq_quantized_matmul_noalloc(c, _p(x), KQ_BF16, m, k, k, _p(w), n, w.shape[1], _p(y), KQ_BF16,
-                                                 n, stream))
+        _lib.check(L.kq_quantized_matmul_noalloc(c, _p(x), KQ_BF16, m, k, xs, _p(w), n, w.shape[1], _p(y),
+                                                 KQ_BF16, n, stream))
+        # no bounded device wait ran out (the word is cleared by the next call)
+        assert L.kq_noalloc_error(0, stream) == 0
         outs.append(y)
     torch.cuda.synchronize()
     ref = O.matmul(xb, synth.random_weight(codec, n, k, seed=71), codec)
