@@ -194,3 +194,19 @@ def test_legacy_round_trip_through_gguf_quantizer(codec, bb):
     w = gq.quantize(wf, qt)
     assert w.shape == (32, 1024 // {"tq2_0": 256, "tq1_0": 256, "nvfp4": 64}.get(codec, 32) * bb)
     assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt).astype(np.float32)))
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("codec", ["q4_k", "q6_k", "iq2_xxs"])
+def test_oracle_matches_gguf_py_million_blocks(codec):
+    """The north-star codecs: 2^20 seeded random super-blocks each (16 chunks
+    of 65536), the C oracle bit-identical to gguf-py's dequantize."""
+    gq = pytest.importorskip("gguf.quants")
+    from gguf.constants import GGMLQuantizationType as T
+    qt = {"q4_k": T.Q4_K, "q6_k": T.Q6_K, "iq2_xxs": T.IQ2_XXS}[codec]
+    n = 0
+    for chunk in range(16):
+        w = synth.random_weight(codec, 256, 65536, seed=10_000 + chunk)
+        assert np.array_equal(bits(O.dequantize(w, codec)), bits(gq.dequantize(w, qt))), chunk
+        n += w.shape[0] * (w.shape[1] // synth.BLOCK_BYTES[synth.codec_id(codec)])
+    assert n == 1 << 20
