@@ -1,22 +1,27 @@
-"""Benchmark: K-quant decode GEMV over a Llama-3-8B Q4_K_M decoder layer on B200.
+"""Benchmark: K-quant decode over Llama-3-8B Q4_K_M decoder layers on B200.
 
-Workload: the seven projections of one Llama-3-8B
+Workload: the seven projections of a Llama-3-8B
 layer -- q/k/v/o/gate/up in Q4_K, down in Q6_K (137,822,208 wire bytes) --
 applied to M bf16 activation rows (M=1 headline; M in {4, 16, 32} reported
-under ``sweep``).  One step = one layer forward through the kq ops:
+under ``sweep``).  One step = one token through all 32 layers of the model
+(32 distinct layers, 4.41 GB of weights, far larger than the 126 MB L2); per
+layer, through the kq ops:
 
-    qkv   = quantized_matmul(x, Wqkv)            (row-concatenated q|k|v wire,
-                                                  as gmlx/occupancy_fuse.py does)
-    o     = quantized_matmul(x, Wo)
-    h     = quantized_glu(x, Wgate, Wup, silu)    (gate+up+SiLU*up in one launch)
-    y     = quantized_matmul(h, Wdown)            (Q6_K)
+    qkv, o, h, y = quantized_matmul_chain([        (M = 1: ONE launch per layer)
+        q|k|v (x),                 row-concatenated wire, as gmlx/occupancy_fuse.py does
+        o     (a),                 a = this rank's slice of the attention output stand-in
+        gate+up+SiLU (x),          fused gate/up
+        down  (h = output 2)])     Q6_K, reads the gate/up output in the same launch
 
-Eight distinct layers (1.10 GB) are cycled so every step streams weights that
-are not resident in the 126 MB L2.  Weights and activations are seeded
-synthetic data with the configuration's block statistics (no GGUF files on the
-box).  ``value`` is device-timed (CUDA graph replay, CUDA events, max over
-ranks); ``e2e`` goes through the public Python op API with the step input
-copied from pinned host memory and the output read back every step.
+(``--ops`` / M > 1: quantized_matmul / quantized_glu, one launch per group.)
+Weights and activations are seeded synthetic data with the configuration's
+block statistics (no GGUF files on the box).  ``value`` is device-timed over
+exactly ``--steps`` replays of the step's CUDA graph (CUDA events on the
+launching stream, max over ranks); ``e2e`` runs the same steps through the
+public Python op API with the step input copied from pinned host memory and
+the output read back every step.  Every cell (decode, prefill, MoE) checks
+one untimed step against f32 dequantization + an f32 torch matmul and
+reports the max relative error.
 
 ``--impl reference`` times the CPU dequantize-then-matmul path (the C oracle
 restating the ggml block formats; the reference's own kernels are Apple Metal
@@ -40,7 +45,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "K/IQ-quant qmatmul: decode GB/s as % HBM peak, prefill TFLOP/s, at 1/2/4/8 GPU"
 UNIT = "GB/s"
-N_LAYERS = 8
+N_LAYERS = 32  # Llama-3-8B: one decode step = one token through its 32 layers
 LAYER_WEIGHT_BYTES = 137_822_208
 
 
@@ -131,15 +136,41 @@ def build_layers(dev, n_layers, world=1, rank=0, seed0=100):
     return layers
 
 
-def layer_step(kq, L, x, a=None, dist=None, comm=None):
-    """One decoder-layer pass of the seven quantized projections (4 launches).
-    Under tensor parallelism the row-parallel o and down outputs are summed
-    over ranks: at M=1 inside their GEMV kernels (peer stores over NVLink,
-    `comm`), otherwise with NCCL all-reduces.  `a` stands in for this rank's
-    slice of the attention output."""
+def layer_step(kq, L, x, a=None, dist=None, comm=None, mode="chain"):
+    """One decoder-layer pass of the seven quantized projections.
+
+    mode "chain" (M = 1): q|k|v, o, gate+up and down in ONE persistent launch
+    (kq.quantized_matmul_chain), down reading the gate/up output through the
+    kernel's completion counters.  mode "chain_dep" (M = 1, one GPU): the same
+    launch with every projection reading the previous one's output (q rows ->
+    o -> gate/up -> down), the dependency shape of a real layer minus
+    attention and norms.  mode "ops": one kq op per projection group (4
+    launches).  Under tensor parallelism the row-parallel o and down outputs
+    are summed over ranks: at M=1 optionally inside their GEMV kernels (peer
+    stores over NVLink, `comm`), otherwise with NCCL all-reduces.  `a` stands
+    in for this rank's slice of the attention output."""
+    xa = x if a is None else a
+    if x.shape[0] == 1 and comm is None and mode == "chain":
+        qkv, o, h, y = kq.quantized_matmul_chain([
+            {"x": x, "w": L["qkv"], "codec": "q4_k"},
+            {"x": xa, "w": L["o"], "codec": "q4_k"},
+            {"x": x, "w": L["gate"], "w2": L["up"], "act": "silu", "codec": "q4_k"},
+            {"x": 2, "w": L["down"], "codec": "q6_k"}])
+        if dist is not None:
+            dist.all_reduce(o)
+            dist.all_reduce(y)
+        return qkv, o, y
+    if x.shape[0] == 1 and mode == "chain_dep":
+        nq = L["o"].shape[1] // 144 * 256
+        q, kv, o, h, y = kq.quantized_matmul_chain([
+            {"x": x, "w": L["qkv"][:nq], "codec": "q4_k"},
+            {"x": x, "w": L["qkv"][nq:], "codec": "q4_k"},
+            {"x": 0, "w": L["o"], "codec": "q4_k"},
+            {"x": 2, "w": L["gate"], "w2": L["up"], "act": "silu", "codec": "q4_k"},
+            {"x": 3, "w": L["down"], "codec": "q6_k"}])
+        return q, o, y
     qkv = kq.quantized_matmul(x, L["qkv"], None, "q4_k")
     h = kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
-    xa = x if a is None else a
     if comm is not None and x.shape[0] == 1:
         o = kq.quantized_matmul_allreduce(xa, L["o"], "q4_k", comm)
         y = kq.quantized_matmul_allreduce(h, L["down"], "q6_k", comm)
@@ -187,12 +218,73 @@ def time_graph(torch, fn, steps, warmup, stream, min_warm_s=0.0):
 
 
 GLU_LAUNCH_DRAM_BYTES = 66_643_712  # ncu: fused gate/up GEMV, Q4_K 2 x 14336 x 4096, M = 1
+CHAIN_LAUNCH_DRAM_BYTES = None      # ncu: one chain launch (a whole layer), from the capture in profiles/
+
+
+def _rel(y, ref):
+    return float((y.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+
+
+def _deq(kq, w, codec):
+    return kq.dequantize(w, None, codec)  # f32, bit-exact with the ggml block formats
+
+
+def verify_layer(torch, kq, L, m, dev, mode, ka):
+    """Max relative error of one layer step's outputs at the bench's own shapes
+    (this rank's shards), each against f32 dequantization then an f32 torch
+    matmul (TF32 off).  Outside every timed region."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x = torch.randn(m, 4096, generator=g).to(torch.bfloat16).to(dev)
+    a = x[:, :ka].contiguous()
+    if mode == "chain":
+        qkv, o, h, y = kq.quantized_matmul_chain([
+            {"x": x, "w": L["qkv"], "codec": "q4_k"}, {"x": a, "w": L["o"], "codec": "q4_k"},
+            {"x": x, "w": L["gate"], "w2": L["up"], "act": "silu", "codec": "q4_k"},
+            {"x": 2, "w": L["down"], "codec": "q6_k"}], out_dtype=torch.float32)
+    else:
+        qkv = kq.quantized_matmul(x, L["qkv"], None, "q4_k", out_dtype=torch.float32)
+        o = kq.quantized_matmul(a, L["o"], None, "q4_k", out_dtype=torch.float32)
+        h = kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
+        y = kq.quantized_matmul(h, L["down"], None, "q6_k", out_dtype=torch.float32)
+    xf, af = x.float(), a.float()
+    gt = xf @ _deq(kq, L["gate"], "q4_k").t()
+    ut = xf @ _deq(kq, L["up"], "q4_k").t()
+    errs = {"qkv": _rel(qkv, xf @ _deq(kq, L["qkv"], "q4_k").t()),
+            "o": _rel(o, af @ _deq(kq, L["o"], "q4_k").t()),
+            "gate_up": _rel(h, torch.nn.functional.silu(gt) * ut),
+            "down": _rel(y, h.float() @ _deq(kq, L["down"], "q6_k").t())}
+    torch.cuda.empty_cache()
+    return {"max_rel_err": max(errs.values()), "per_projection": errs, "tolerance": 1e-2,
+            "reference": "kq.dequantize (f32) then torch f32 matmul, TF32 off"}
 
 MOE_CONFIGS = (
     # (name, experts, top_k, hidden, ffn, gate/up codec, down codec, token counts)
     ("qwen3-30b-a3b-like", 128, 8, 2048, 768, "q4_k", "q6_k", (1, 64, 4096)),
     ("deepseek-v3-like-iq2", 256, 8, 7168, 2048, "iq2_xxs", "iq2_xxs", (1, 8, 64)),
 )
+
+
+def moe_check(torch, kq, x, idx, sc, y, wg, wu, wd, cgu, cd, base, toks):
+    """Max relative error of an expert layer's output rows `toks` (this rank's
+    experts [base, base + len(wg))) against f32 dequantization + f32 torch
+    matmuls, with the gate/up product rounded to the activation dtype as the
+    layer keeps it."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    el = wg.shape[0]
+    ref = torch.zeros(len(toks), wd.shape[1], device=x.device)
+    ic, scc = idx.cpu(), sc.cpu()
+    for r, t in enumerate(toks):
+        xt = x[t].float()
+        for j in range(ic.shape[1]):
+            e = int(ic[t, j]) - base
+            if not 0 <= e < el:
+                continue
+            g = _deq(kq, wg[e], cgu) @ xt
+            u = _deq(kq, wu[e], cgu) @ xt
+            h = (torch.nn.functional.silu(g) * u).to(x.dtype).float()
+            ref[r] += float(scc[t, j]) * (_deq(kq, wd[e], cd) @ h)
+    return _rel(y[toks], ref) if ref.abs().max() > 0 else 0.0
 
 
 def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
@@ -230,38 +322,98 @@ def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
                 dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             secs = float(tt.item())
             gbs = uniq * ebytes / secs / 1e9
+            # parity of this cell, outside the timed region: this rank's share of
+            # the layer for up to 8 sampled tokens against f32 dequantization
+            idx, sc = kq.moe_router_topk(logits, K, True, shared_gate=False)
+            yl = kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, cgu, cd, base, E, out_dtype=torch.float32)
+            toks = torch.randperm(t, generator=torch.Generator().manual_seed(t))[:8].tolist()
+            err = moe_check(torch, kq, x, idx, sc, yl, wg, wu, wd, cgu, cd, base, toks)
             cell[f"t{t}"] = {"ms": secs * 1e3, "unique_experts": uniq, "GB/s": gbs,
                              "frac_hbm_per_gpu": gbs / world / hbm_peak,
-                             "TFLOP/s": 2.0 * t * K * 3 * D * F / secs / 1e12}
+                             "TFLOP/s": 2.0 * t * K * 3 * D * F / secs / 1e12,
+                             "rel_err": err, "rel_err_tokens_checked": len(toks)}
         out[name] = cell
         del wg, wu, wd
         torch.cuda.empty_cache()
     return out
 
 
+_CPU_LAYER = None
+
+
+def _cpu_layer():
+    """One Llama-3-8B Q4_K_M layer (the seven projections) and its inputs, host side."""
+    global _CPU_LAYER
+    if _CPU_LAYER is None:
+        from gmlx_b200 import synth
+        w = {name: (codec, synth.random_weight(codec, n, k, seed=500 + i))
+             for i, (name, codec, n, k) in enumerate(synth.LLAMA3_8B_LAYER)}
+        x = synth.random_activations(1, 4096, seed=3)
+        h = synth.random_activations(1, 14336, seed=4)
+        _CPU_LAYER = (w, x, h)
+    return _CPU_LAYER
+
+
 def cpu_baseline_run(seconds=12.0, threads=None):
-    """C oracle dequantize-then-matmul (all host threads) on a bounded sample:
-    repeated q_proj-sized Q4_K layers (4096x4096) and the Q6_K down_proj at M=1."""
-    from gmlx_b200 import synth
+    """C oracle dequantize-then-matmul (OpenMP, all host threads) on the GPU
+    arm's per-layer workload: the seven projections of one layer at M = 1,
+    repeated for `seconds`; the median layer time gives the rate."""
     from oracle import oracle as O
     O.build()
     thr = threads or os.cpu_count() or 1
-    wq = synth.random_weight("q4_k", 4096, 4096, seed=1)
-    wd = synth.random_weight("q6_k", 4096, 14336, seed=2)
-    x1 = synth.random_activations(1, 4096, seed=3)
-    x2 = synth.random_activations(1, 14336, seed=4)
-    O.matmul(x1, wq, "q4_k", threads=thr)
-    done, t0 = 0, time.perf_counter()
-    nbytes = 0
-    while time.perf_counter() - t0 < seconds:
-        O.matmul(x1, wq, "q4_k", threads=thr)
-        O.matmul(x2, wd, "q6_k", threads=thr)
-        nbytes += wq.nbytes + wd.nbytes
-        done += 1
-    dt = time.perf_counter() - t0
-    return {"value": nbytes / dt / 1e9, "unit": UNIT, "cores": thr, "kind": "port",
-            "sample": f"{done} x (Q4_K 4096x4096 + Q6_K 4096x14336) GEMV at M=1, {dt:.1f} s, "
-                      "C oracle dequantize-then-matmul (OpenMP)"}
+    w, x, h = _cpu_layer()
+
+    def layer():
+        for name, (codec, wb) in w.items():
+            O.matmul(h if name == "down_proj" else x, wb, codec, threads=thr)
+    layer()
+    times, t0 = [], time.perf_counter()
+    while time.perf_counter() - t0 < seconds or len(times) < 3:
+        t1 = time.perf_counter()
+        layer()
+        times.append(time.perf_counter() - t1)
+    med = statistics.median(times)
+    return {"value": LAYER_WEIGHT_BYTES / med / 1e9, "unit": UNIT, "cores": thr, "kind": "port",
+            "os_cpu_count": os.cpu_count(),
+            "sample": f"{len(times)} x one Llama-3-8B Q4_K_M layer (7 projections, 137.8 MB of weights) at M=1, "
+                      f"median {med * 1e3:.1f} ms, C oracle dequantize-then-matmul (OpenMP, {thr} threads)"}
+
+
+def cpu_gguf_arm(reps=3):
+    """gguf-py arm: gguf.quants.dequantize (the ggml formats' Python reference,
+    a declared gmlx dependency) to f32 W, then x @ W.T in torch on the CPU;
+    dequantize and matmul timed separately over one full layer, median of
+    `reps` warm repetitions."""
+    import torch
+    try:
+        import gguf.quants as gq
+        from gguf.constants import GGMLQuantizationType as T
+    except ImportError as e:
+        return {"unavailable": f"gguf-py not importable: {e}"}
+    qt = {"q4_k": T.Q4_K, "q6_k": T.Q6_K}
+    w, x, h = _cpu_layer()
+    xt = torch.from_numpy(x.view(np.int16).copy()).view(torch.bfloat16).float()
+    ht = torch.from_numpy(h.view(np.int16).copy()).view(torch.bfloat16).float()
+    deq_t, mm_t = [], []
+    for r in range(reps + 1):
+        td = tm = 0.0
+        for name, (codec, wb) in w.items():
+            t0 = time.perf_counter()
+            W = torch.from_numpy(gq.dequantize(wb, qt[codec]))
+            t1 = time.perf_counter()
+            _ = (ht if name == "down_proj" else xt) @ W.t()
+            t2 = time.perf_counter()
+            td += t1 - t0
+            tm += t2 - t1
+        if r:  # the first pass warms up
+            deq_t.append(td)
+            mm_t.append(tm)
+    d, m = statistics.median(deq_t), statistics.median(mm_t)
+    return {"value": LAYER_WEIGHT_BYTES / (d + m) / 1e9, "unit": UNIT, "dequant_s": d, "matmul_s": m,
+            "total_s": d + m, "dequant_GB/s": LAYER_WEIGHT_BYTES / d / 1e9,
+            "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(),
+            "sample": f"median of {reps} x one Llama-3-8B Q4_K_M layer at M=1 (gguf-py dequantize, numpy; "
+                      "torch CPU matmul)"}
 
 
 def run_reference(args, rank, world):
@@ -271,14 +423,14 @@ def run_reference(args, rank, world):
     for _ in range(args.warmup):
         cpu_baseline_run(seconds=1.0)
     for _ in range(args.steps):
-        res.append(cpu_baseline_run(seconds=max(2.0, 30.0 / max(1, args.steps))))
+        res.append(cpu_baseline_run(seconds=max(1.0, 30.0 / max(1, args.steps))))
     v = statistics.median(r["value"] for r in res)
     cb = dict(res[0])
     cb["value"] = v
     line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama3-8b Q4_K_M decoder layer decode GEMV (CPU sample)", "m": 1},
+            "config": {"workload": "llama3-8b Q4_K_M decode step (32 layers; CPU sample: whole layers)", "m": 1},
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -287,7 +439,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--m", type=int, default=1)
@@ -295,6 +447,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--fused-allreduce", action="store_true")
+    ap.add_argument("--ops", action="store_true", help="one kq op per projection group instead of the chain launch")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -323,77 +476,113 @@ def main():
     ka = 4096 // world  # this rank's slice of the attention output (o_proj K)
     from gmlx_b200 import parallel as par
     # --fused-allreduce: row-parallel o/down with the cross-rank sum inside their
-    # GEMV kernels (peer stores over NVLink); default: GEMV + NCCL all-reduce,
-    # which measured faster at tp2 (2460 vs 1929 GB/s aggregate)
+    # GEMV kernels (peer stores over NVLink); default: NCCL all-reduce
     comm = par.PeerComm(4096, dev) if (world > 1 and args.fused_allreduce) else None
+    head_mode = "chain" if (args.m == 1 and comm is None and not args.ops) else "ops"
 
-    def measure(m, steps, warmup, min_warm_s=0.0):
+    def measure(m, steps, warmup, mode, min_warm_s=0.0):
+        """Seconds per decode step (one token through all N_LAYERS layers),
+        timed over exactly `steps` replays of the step's CUDA graph."""
         g = torch.Generator(device="cpu").manual_seed(0)
         xs = [torch.randn(m, 4096, generator=g).to(torch.bfloat16).to(dev) for _ in range(N_LAYERS)]
         att = [x[:, :ka].contiguous() for x in xs]
 
-        def one_pass():
+        def one_step():
             for li, L in enumerate(layers):
-                layer_step(kq, L, xs[li], att[li], dd, comm)
-        reps = max(1, steps // N_LAYERS)
-        secs = time_graph(torch, one_pass, reps, max(1, warmup // N_LAYERS), stream, min_warm_s)
-        return secs / (reps * N_LAYERS)
+                layer_step(kq, L, xs[li], att[li], dd, comm, mode)
+        return time_graph(torch, one_step, steps, warmup, stream, min_warm_s) / steps
 
     # timed region (headline), with clock sampling and barrier + max over ranks
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        t_step = measure(args.m, args.steps, args.warmup, min_warm_s=1.0)
+        t_step = measure(args.m, args.steps, args.warmup, head_mode, min_warm_s=1.0)
     tt = torch.tensor([t_step], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     t_step = float(tt.item())
-    nbytes = step_bytes(args.m)
-    value = nbytes / t_step / 1e9  # the whole layer's bytes (strong scaling: the layer is split over ranks)
+    nbytes = N_LAYERS * step_bytes(args.m)
+    value = nbytes / t_step / 1e9  # all layers' bytes (strong scaling: each layer is split over ranks)
 
-    # dominant kernel: the fused gate/up GLU GEMV (66 MB of the 138 MB step),
-    # timed alone on its launch stream with CUDA events over many launches
-    x = torch.randn(args.m, 4096, device=dev).to(torch.bfloat16)
+    # parity of one step's outputs at these full shapes, outside the timed region
+    check = verify_layer(torch, kq, layers[0], args.m, dev, head_mode, ka)
 
-    def glu_pass():
-        for L in layers:
-            kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
-    reps = 6
-    glu_t = time_graph(torch, glu_pass, reps, 2, stream) / (reps * N_LAYERS)
-    glu_bytes = 2 * (14336 // world) * 2304 + args.m * 4096 * 2 + args.m * (14336 // world) * 2
-    achieved = glu_bytes / glu_t / 1e9
+    # dominant kernel: the chain launch (one layer) or, per op, the fused
+    # gate/up GEMV; its average launch duration over many launches
+    if head_mode == "chain":
+        per_launch = t_step / N_LAYERS
+        dom_bytes = nbytes // N_LAYERS // world
+        kernel_name = "chain_kernel<Q4_K,Q6_K> (one layer: q|k|v, o, gate+up, down in one launch)"
+        traffic = CHAIN_LAUNCH_DRAM_BYTES if world == 1 else None
+    else:
+        x = torch.randn(args.m, 4096, device=dev).to(torch.bfloat16)
 
-    # e2e through the public op API: pinned host input -> device, layer, output -> host
+        def glu_pass():
+            for L in layers:
+                kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
+        reps = 4
+        per_launch = time_graph(torch, glu_pass, reps, 2, stream) / (reps * N_LAYERS)
+        dom_bytes = 2 * (14336 // world) * 2304 + args.m * 4096 * 2 + args.m * (14336 // world) * 2
+        kernel_name = "gemv_kernel<Q4_K, GLU> (gate+up 14336x4096)"
+        traffic = GLU_LAUNCH_DRAM_BYTES if (world == 1 and args.m == 1) else None
+    achieved = dom_bytes / per_launch / 1e9
+
+    # e2e through the public op API: pinned host input -> device, one token
+    # through every layer, output -> host, all inside the timed region
     hx = torch.randn(args.m, 4096).to(torch.bfloat16).pin_memory()
     hy = torch.empty(args.m, 4096, dtype=torch.bfloat16).pin_memory()
-    e2e_steps = max(args.steps, 16)
-    torch.cuda.synchronize()
-    for i in range(args.warmup):
+
+    def e2e_step():
         dx = hx.to(dev, non_blocking=True)
-        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka], dd, comm)
+        y = dx
+        for L in layers:
+            _, _, y = layer_step(kq, L, dx, dx[:, :ka].contiguous(), dd, comm, head_mode)
         hy.copy_(y, non_blocking=True)
+    for _ in range(args.warmup):
+        e2e_step()
     torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for i in range(e2e_steps):
-        dx = hx.to(dev, non_blocking=True)
-        _, _, y = layer_step(kq, layers[i % N_LAYERS], dx, dx[:, :ka].contiguous(), dd, comm)
-        hy.copy_(y, non_blocking=True)
-    b.record()
+    if world > 1:
+        dist.barrier()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(args.steps):
+        e2e_step()
+    eb.record()
     torch.cuda.synchronize()
-    e2e_t = a.elapsed_time(b) / 1e3 / e2e_steps
+    e2e_t = ea.elapsed_time(eb) / 1e3 / args.steps
     te = torch.tensor([e2e_t], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_t = float(te.item())
 
+    # the other decode launch structures at M = 1 (same work per step)
+    modes = {}
+    if not args.no_sweep and args.m == 1:
+        for mode in ("ops", "chain", "chain_dep"):
+            if (mode == "chain_dep" and world > 1) or (comm is not None and mode != "ops"):
+                continue
+            tm = measure(1, 10, 3, mode)
+            if world > 1:
+                tt = torch.tensor([tm], device=dev, dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                tm = float(tt.item())
+            modes[mode] = {"ms_per_step": tm * 1e3, "us_per_layer": tm / N_LAYERS * 1e6,
+                           "GB/s": N_LAYERS * step_bytes(1) / tm / 1e9,
+                           "frac_hbm": N_LAYERS * step_bytes(1) / tm / 1e9 / world / hbm_peak}
+
     sweep = {}
     if not args.no_sweep:
         for m in (1, 4, 16, 32):
-            ts = measure(m, 16, 8)
-            sweep[f"m{m}"] = {"ms_per_step": ts * 1e3, "GB/s": step_bytes(m) / ts / 1e9,
-                              "frac_hbm": step_bytes(m) / ts / 1e9 / hbm_peak}
+            mode = head_mode if m == 1 else "ops"
+            ts = measure(m, 10, 3, mode)
+            if world > 1:
+                tt = torch.tensor([ts], device=dev, dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                ts = float(tt.item())
+            gbs = N_LAYERS * step_bytes(m) / ts / 1e9
+            sweep[f"m{m}"] = {"ms_per_step": ts * 1e3, "us_per_layer": ts / N_LAYERS * 1e6, "GB/s": gbs,
+                              "frac_hbm": gbs / world / hbm_peak, "launch": mode}
 
     # prefill: the layer's matmuls (qkv | o | gate+up concatenated | down) at
     # M = 512 / 2048 / 8192 tokens on the tcgen05 GEMM, TFLOP/s over 2*M*N*K
@@ -412,9 +601,12 @@ def main():
 
             def pf():  # gate/up/SiLU*up fused in one tcgen05 GEMM (two accumulators per tile)
                 kq.quantized_matmul(xs[k_in], L0["qkv"], None, "q4_k")
-                kq.quantized_matmul(xs[k_o], L0["o"], None, "q4_k")
+                o = kq.quantized_matmul(xs[k_o], L0["o"], None, "q4_k")
                 kq.quantized_glu(xs[k_in], L0["gate"], L0["up"], "q4_k", act="silu")
-                kq.quantized_matmul(xs[k_down], L0["down"], None, "q6_k")
+                y = kq.quantized_matmul(xs[k_down], L0["down"], None, "q6_k")
+                if dd is not None:  # row-parallel partial sums over ranks (bf16, NCCL)
+                    dist.all_reduce(o)
+                    dist.all_reduce(y)
             reps = 3 if m == 8192 else 6
             t = time_graph(torch, pf, reps, 1, stream) / reps
             if dd is not None:  # slowest rank; every rank computes its own shard
@@ -422,36 +614,59 @@ def main():
                 dist.all_reduce(tt, op=dist.ReduceOp.MAX)
                 t = float(tt.item())
             tflops = flops_per_tok * world * m / t / 1e12  # whole job
-            prefill[f"m{m}"] = {"ms": t * 1e3, "TFLOP/s": tflops, "frac_tensor": tflops / world / tc_peak}
+            # parity of this cell (outside the timed region): 64 sampled rows of
+            # every product against f32 dequantization + f32 torch matmul
+            rows = torch.randperm(m, generator=torch.Generator().manual_seed(m))[:64].to(dev)
+            errs = {}
+            for name, w, c, xin in (("qkv", L0["qkv"], "q4_k", xs[k_in]), ("o", L0["o"], "q4_k", xs[k_o]),
+                                    ("down", L0["down"], "q6_k", xs[k_down])):
+                yv = kq.quantized_matmul(xin, w, None, c, out_dtype=torch.float32)[rows]
+                errs[name] = _rel(yv, xin[rows].float() @ _deq(kq, w, c).t())
+            hv = kq.quantized_glu(xs[k_in], L0["gate"], L0["up"], "q4_k", act="silu", out_dtype=torch.float32)[rows]
+            xr = xs[k_in][rows].float()
+            errs["gate_up"] = _rel(hv, torch.nn.functional.silu(xr @ _deq(kq, L0["gate"], "q4_k").t())
+                                   * (xr @ _deq(kq, L0["up"], "q4_k").t()))
+            torch.cuda.empty_cache()
+            prefill[f"m{m}"] = {"ms": t * 1e3, "TFLOP/s": tflops, "frac_tensor": tflops / world / tc_peak,
+                                "rel_err": max(errs.values()), "rel_err_rows_checked": 64}
 
     moe = {} if args.no_moe else run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak)
 
     if rank == 0:
         cpu = None if args.no_cpu or world > 1 else cpu_baseline_run()
+        cpu_arms = None if args.no_cpu or world > 1 else {"c_oracle_openmp": cpu, "gguf_py_torch_cpu": cpu_gguf_arm()}
+        launches_per_layer = 1 if head_mode == "chain" else 4
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama3-8b Q4_K_M decoder layer decode GEMV (q/k/v/o/gate/up Q4_K, down Q6_K)",
-                       "m": args.m, "layers_cycled": N_LAYERS, "weight_bytes_per_step": LAYER_WEIGHT_BYTES,
-                       "l2": "inputs larger than L2 (8 distinct layers, 1.10 GB, cycled)",
+            "config": {"workload": "llama3-8b Q4_K_M decode step: one token through 32 decoder layers "
+                                   "(q/k/v/o/gate/up Q4_K, down Q6_K)",
+                       "m": args.m, "layers": N_LAYERS, "weight_bytes_per_layer": LAYER_WEIGHT_BYTES,
+                       "weight_bytes_per_step": N_LAYERS * LAYER_WEIGHT_BYTES,
+                       "launch": ("one chain launch per layer (q|k|v, o, gate+up, down)" if head_mode == "chain"
+                                  else "one launch per projection group (q|k|v, o, gate+up, down)"),
+                       "l2": "inputs larger than L2 (32 distinct layers, 4.41 GB per step)",
                        "parallelism": (f"tp{world} (column-parallel qkv/gate/up, row-parallel o/down, "
                                        + ("cross-rank sum fused into their GEMV kernels over NVLink peer stores)"
                                           if comm is not None else "NCCL all-reduce)")) if world > 1 else "single"},
             "frac_hbm": value / world / hbm_peak,
+            "us_per_layer": t_step / N_LAYERS * 1e6,
+            "rel_err": check["max_rel_err"], "parity": check,
+            "decode_launch_modes": modes,
             "moe": moe,
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K, GLU> (gate+up 14336x4096)",
+            "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / hbm_peak,
+                         "algorithmic_bytes_per_launch": dom_bytes,
                          # dram__bytes_read.sum + dram__bytes_write.sum of this launch at this
-                         # shape from an ncu capture (66.14 MB read + 0.51 MB written); the
-                         # algorithmic bytes are 66.07 MB
-                         "traffic": GLU_LAUNCH_DRAM_BYTES if (world == 1 and args.m == 1) else None,
-                         "traffic_unit": "bytes per launch"},
+                         # shape from an ncu capture (profiles/)
+                         "traffic": traffic, "traffic_unit": "bytes per launch"},
             "cpu_baseline": cpu,
+            "cpu_baseline_arms": cpu_arms,
             "e2e": {"value": nbytes / e2e_t / 1e9, "unit": UNIT,
                     "h2d_bytes_per_step": int(hx.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2)},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": launches_per_layer * N_LAYERS * args.steps,
             "clocks": clk.summary(),
             "sweep": sweep,
             "prefill": prefill,

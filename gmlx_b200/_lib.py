@@ -17,6 +17,16 @@ KQ_OK, KQ_ERR_CODEC, KQ_ERR_SHAPE, KQ_ERR_ALIGN, KQ_ERR_DTYPE, KQ_ERR_CUDA, KQ_E
 KQ_F32, KQ_F16, KQ_BF16 = 0, 1, 2
 ACTS = {"none": 0, "silu": 1, "gelu": 2, "gelu_approx": 3, "gelu_tanh": 3}
 
+class ChainProblem(ctypes.Structure):
+    """struct kq_chain_problem (include/kq_cuda.h)."""
+    _fields_ = [("codec", ctypes.c_int), ("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("w2", ctypes.c_void_p),
+                ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("w_row_stride", ctypes.c_int64), ("act", ctypes.c_int),
+                ("y", ctypes.c_void_p), ("y_dtype", ctypes.c_int), ("bias", ctypes.c_void_p),
+                ("bias_dtype", ctypes.c_int), ("depends_on", ctypes.c_int)]
+
+
+KQ_CHAIN_MAX = 8
+
 # Every symbol include/kq_cuda.h declares, with its ctypes signature.
 _vp, _i32, _i64, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
 SIGNATURES = {
@@ -48,6 +58,8 @@ SIGNATURES = {
     "kq_moe_expert_layer_workspace_size": (_sz, [_i32, _i32, _i64, _i32, _i64, _i64, _i64, _i32]),
     "kq_quantized_matmul_noalloc": (_i32, [_i32, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _vp]),
     "kq_noalloc_error": (_i32, [_i32, _vp]),
+    "kq_quantized_matmul_chain_workspace_size": (_sz, [_vp, _i32]),
+    "kq_quantized_matmul_chain": (_i32, [_vp, _i32, _i32, _vp, _sz, _vp]),
     "kq_quantized_matmul_bias": (_i32, [_i32, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _i32, _i64,
                                         _vp, _sz, _vp]),
     "kq_allreduce_buffer_bytes": (_sz, [_i32, _i64]),

@@ -903,6 +903,104 @@ int kq_moe_expert_layer_local(int codec_gu, int codec_d, const void *x, int x_dt
                       "moe_expert_layer_local", expert_base, e_total);
 }
 
+// ---- chain of one-row projections (kq_chain.cu) ----
+
+static int chain_descs(const kq_chain_problem *pr, int count, int x_dtype, kq::ChainProblemDesc *d, bool check) {
+    const char *what = "quantized_matmul_chain";
+    if (count < 1 || count > KQ_CHAIN_MAX || !pr)
+        return fail(KQ_ERR_SHAPE, "%s: count %d outside 1..%d", what, count, KQ_CHAIN_MAX);
+    if (check && !act_dtype_ok(x_dtype)) return fail(KQ_ERR_DTYPE, "%s: activations must be f16 or bf16", what);
+    for (int q = 0; q < count; q++) {
+        const kq_chain_problem &p = pr[q];
+        if (check) {
+            int rc;
+            if ((rc = check_weights(p.codec, p.w, p.k, p.w_row_stride, what))) return rc;
+            if (p.act != ACT_NONE && (rc = check_weights(p.codec, p.w2, p.k, p.w_row_stride, what))) return rc;
+            if ((rc = check_x(p.x, x_dtype, p.k, what))) return rc;
+            if (!out_dtype_ok(p.y_dtype)) return fail(KQ_ERR_DTYPE, "%s: problem %d: bad output dtype", what, q);
+            if (p.bias && (p.act != ACT_NONE || !out_dtype_ok(p.bias_dtype)))
+                return fail(KQ_ERR_DTYPE, "%s: problem %d: bias only on plain projections", what, q);
+            if (p.act < ACT_NONE || p.act > ACT_GELU_TANH) return fail(KQ_ERR_SHAPE, "%s: problem %d: bad act", what, q);
+            if (p.n <= 0 || p.n > 0x7fffffff || p.k > 0x7fffffff)
+                return fail(KQ_ERR_SHAPE, "%s: problem %d: bad n / k", what, q);
+            if (p.depends_on >= q || p.depends_on < -1)
+                return fail(KQ_ERR_SHAPE, "%s: problem %d depends on %d (must be an earlier problem or -1)", what, q,
+                            p.depends_on);
+        } else if (p.k <= 0 || p.k % QK || p.n <= 0) {
+            return 1;
+        }
+        kq::ChainProblemDesc &e = d[q];
+        e.codec = p.codec;
+        e.x = p.x;
+        e.w = p.w;
+        e.w2 = p.w2;
+        e.n = p.n;
+        e.k = p.k;
+        e.w_row_stride = p.w_row_stride;
+        e.act = p.act;
+        e.y = p.y;
+        e.y_dtype = p.y_dtype;
+        e.bias = p.bias;
+        e.bias_dtype = p.bias_dtype;
+        e.dep = p.depends_on;
+    }
+    return KQ_OK;
+}
+
+// chain workspace: [0, 256) error word; [256, 512) work / exit / completion
+// counters; then the K-split tile counters and partial rows
+struct ChainWs {
+    size_t ctl_off = 256, tcnt_off = 512, part_off = 512, total = 512;
+};
+static ChainWs chain_ws(const kq::ChainPlan &pl) {
+    ChainWs w;
+    w.part_off = align256(w.tcnt_off + (size_t)pl.split_tiles * sizeof(int));
+    w.total = align256(w.part_off + (size_t)pl.partial_floats * sizeof(float));
+    return w;
+}
+
+size_t kq_quantized_matmul_chain_workspace_size(const kq_chain_problem *problems, int count) {
+    kq::ChainProblemDesc d[KQ_CHAIN_MAX];
+    if (chain_descs(problems, count, KQ_BF16, d, false)) return 0;
+    size_t need = 256;
+    kq::ChainPlan pl;
+    if (kq::chain_plan(d, count, &pl)) need = chain_ws(pl).total;
+    // the per-problem path's workspace, should the fused kernel not take the chain
+    for (int q = 0; q < count; q++)
+        need = std::max(need, dense_ws(d[q].codec, 1, d[q].n, d[q].k, d[q].act));
+    return need;
+}
+
+int kq_quantized_matmul_chain(const kq_chain_problem *problems, int count, int x_dtype, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+    g_msg[0] = 0;
+    const char *what = "quantized_matmul_chain";
+    kq::ChainProblemDesc d[KQ_CHAIN_MAX];
+    int rc = chain_descs(problems, count, x_dtype, d, true);
+    if (rc) return rc;
+    if (!workspace || ((uintptr_t)workspace & 255))
+        return fail(KQ_ERR_WORKSPACE, "%s: a 256-byte aligned workspace is required", what);
+    kq::ChainPlan pl;
+    if (!dev_env("KQ_CHAIN_UNFUSED") && kq::chain_plan(d, count, &pl)) {
+        const ChainWs w = chain_ws(pl);
+        if (workspace_bytes < w.total)
+            return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes required, got %zu", what, w.total, workspace_bytes);
+        char *ws = (char *)workspace;
+        return cuda_status(kq::launch_chain(d, count, pl, x_dtype, (int *)ws, (int *)(ws + w.ctl_off),
+                                            (int *)(ws + w.tcnt_off), (float *)(ws + w.part_off), (cudaStream_t)stream),
+                           what);
+    }
+    // no fused kernel for this chain: one launch per problem, in order
+    for (int q = 0; q < count; q++) {
+        const kq::ChainProblemDesc &e = d[q];
+        rc = run_dense(e.codec, e.x, x_dtype, 1, e.k, e.k, e.w, e.act != ACT_NONE ? e.w2 : nullptr, e.n,
+                       e.w_row_stride, e.act, e.y, e.y_dtype, e.n, workspace, workspace_bytes, stream, what, e.bias,
+                       e.bias_dtype);
+        if (rc) return rc;
+    }
+    return KQ_OK;
+}
+
 int kq_workspace_error(void *workspace, int clear, void *stream) {
     if (!workspace) return 0;
     int v = 0;

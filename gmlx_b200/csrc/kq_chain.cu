@@ -1,0 +1,535 @@
+// kq_chain.cu -- a chain of one-row decode GEMVs in ONE persistent launch.
+//
+// A decoder layer at decode time is a short sequence of quantized matmuls on
+// one activation row (q|k|v, o, gate+up, down).  gmlx shrinks the launch
+// count by row-concatenating projections that share an input
+// (gmlx/occupancy_fuse.py:141-200 q|k|v, :272-330 gate+up and split-K down);
+// this kernel streams every projection of a list in one launch:
+//
+//  * Work units (32-row tile x K chunk) of all problems form one ordered list;
+//    CTAs claim them in order (the first by CTA index, then from a counter),
+//    so the GPU flows from one projection into the next with no drain.
+//  * A problem may read an earlier problem's output (depends_on).  Its tile
+//    stores raise that problem's completion counter; the consumers of a CTA
+//    reaching a dependent problem wait for the counter while the producer
+//    keeps streaming the problem's weights into the ring (weights never
+//    depend on anything), so HBM keeps streaming through the hand-off.
+//    Deadlock-free: units are claimed in list order and a problem only waits
+//    on earlier ones, whose units are all held by running CTAs that wait on
+//    nothing later.  Every wait is bounded (~2 s, then an error code in the
+//    workspace's first word and the kernel winds down).
+//  * One CTA per SM: a producer warp streams raw weight rows (1-D bulk
+//    copies, >= ~1 KB per row) into a ring of stages of 32 rows; 16 consumer
+//    warps (2 row halves x 8 block columns) run the integer tensor-core dot
+//    of kq_imma.cuh on each stage.
+//  * Each problem's activation row is quantized ONCE per CTA (int16 split
+//    into two exact bytes, one f32 scale per 32 values, plus the sums the
+//    codecs' offset terms need) into shared memory, when the CTA reaches the
+//    problem's first unit -- after its dependency is complete.
+//  * K-split units (long rows such as Q6_K down, 14336 inputs) post f32
+//    partial rows; the last chunk of a tile to arrive sums them in chunk
+//    order (deterministic) and stores.
+//  * The last CTA to finish resets the work and completion counters, so the
+//    workspace is left zeroed for the next call (as every kq workspace).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "../../include/kq_cuda.h"
+#include "kq_gemv_dev.cuh"
+#include "kq_imma.cuh"
+
+namespace kq {
+namespace {
+
+constexpr int CH_MAX = KQ_CHAIN_MAX;
+constexpr int CH_CW = 16;                     // consumer warps: 2 row halves x 8 block columns
+constexpr int CH_THREADS = 32 * (CH_CW + 1);  // + one producer warp
+constexpr int CH_KMAX = 16384;                // activation row length held quantized in shared memory
+constexpr int CH_XQB = CH_KMAX / QK * IMMA_XB;
+constexpr int CH_SMEM = 232448;               // one CTA per SM
+
+struct ChainProb {
+    const uint8_t *w, *w2;
+    int64_t w_row_stride;
+    const uint8_t *x;  // one activation row (f16 / bf16)
+    void *y;
+    const void *bias;
+    int y_dtype, bias_dtype;
+    int N, K, codec, act, dep;
+    int counted;       // a later problem depends on this one: count finished tiles
+    int tiles, nst, S, chunk;
+    int unit_base, split_base;
+};
+
+struct ChainArgs {
+    ChainProb p[CH_MAX];
+    int count, total_units;
+    int *err;
+    int *ctl;         // [0] work counter, [1] finished CTAs, [2 + p] finished tiles of problem p
+    int *tcnt;        // K-split tile counters
+    float *partial;   // K-split partial rows [split tile][S][32]
+};
+
+template <int C> constexpr int ch_kb() { return KB_OF<C>; }
+template <int C> constexpr int ch_sp() { return spitch_of<C, true>(); }
+template <int C> constexpr int ch_wbytes() { return 32 * ch_sp<C>(); }
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+template <int CA, int CB> struct ChainLayout {
+    static constexpr int SLOT = cmax(ch_wbytes<CA>(), ch_wbytes<CB>());  // one stage: 32 weight rows
+    static constexpr int OFF_BAR = 0;       // full[NS], empty[NS]
+    static constexpr int OFF_UNIT = 128;    // s_unit[8]
+    static constexpr int OFF_ROWOFF = 256;  // NS x 32 bytes
+    static constexpr int OFF_MISC = 512;    // abort flag, sync counter, partial-buffer counters
+    static constexpr int OFF_XQ = 640;      // the current problem's quantized activations
+    static constexpr int RB_ONE = 8 * 32 * 4;  // [block column][tile row] partials
+    static constexpr int OFF_RB = OFF_XQ + CH_XQB;
+    static constexpr int NS_FIT = (CH_SMEM - OFF_RB - RB_ONE - 128) / (SLOT + RB_ONE);  // NS + 1 partial buffers
+    static constexpr int NS = NS_FIT > 6 ? 6 : NS_FIT;
+    static constexpr int OFF_RING = (OFF_RB + (NS + 1) * RB_ONE + 127) / 128 * 128;
+    static constexpr int BYTES = OFF_RING + NS * SLOT;
+    static_assert(NS >= 3, "ring must hold three stages");
+    static_assert(NS * 32 <= 256, "row offsets");
+    static_assert(BYTES <= CH_SMEM, "shared memory");
+};
+
+__device__ __forceinline__ int ld_acquire(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int prob_of(const ChainArgs &a, int unit) {
+    int p = 0;
+#pragma unroll 1
+    while (p + 1 < a.count && unit >= a.p[p + 1].unit_base) p++;
+    return p;
+}
+
+// the stages [s0, s1) of a unit's tile
+__device__ __forceinline__ void unit_stages(const ChainProb &P, int unit, int &tile, int &chunk, int &s0, int &s1) {
+    const int lu = unit - P.unit_base;
+    tile = lu / P.S;
+    chunk = lu - tile * P.S;
+    s0 = chunk * P.chunk;
+    s1 = min(P.nst, s0 + P.chunk);
+}
+
+// Bounded barrier of the consumer warps (a monotonic shared counter): false
+// when the kernel is aborting or ~2 s passed.
+__device__ __forceinline__ bool consumers_sync(int *ctr, int target, volatile int *abort, int *err) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) {
+        __threadfence_block();
+        atomicAdd(ctr, 1);
+    }
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; i++) {
+        if (*reinterpret_cast<volatile int *>(ctr) >= target) break;
+        if (*abort) return false;
+        if ((i & 255) == 0) {
+            const uint64_t now = globaltimer();
+            if (t0 == 0) t0 = now;
+            if (now - t0 > 2000000000ull) {
+                *abort = 1;
+                atomicCAS(err, 0, 4);
+                return false;
+            }
+        }
+    }
+    __threadfence_block();
+    __syncwarp();
+    return true;
+}
+
+template <int CA, int CB, bool F16>
+__global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_constant__ ChainArgs a) {
+    using L = ChainLayout<CA, CB>;
+    constexpr int NS = L::NS;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+    uint64_t *empty = full + NS;
+    int *s_unit = reinterpret_cast<int *>(smem + L::OFF_UNIT);
+    uint8_t *rowoff = smem + L::OFF_ROWOFF;
+    volatile int *s_abort = reinterpret_cast<volatile int *>(smem + L::OFF_MISC);
+    int *s_sync = reinterpret_cast<int *>(smem + L::OFF_MISC + 4);
+    int *dcnt = reinterpret_cast<int *>(smem + L::OFF_MISC + 16);  // NS + 1 partial-buffer counters
+    uint8_t *xq8 = smem + L::OFF_XQ;
+    uint8_t *ring = smem + L::OFF_RING;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], CH_CW);
+        }
+        *s_abort = 0;
+        *s_sync = 0;
+        for (int b = 0; b <= NS; b++) dcnt[b] = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (warp == CH_CW) {
+        // ---------------- producer: lane r streams tile row r of every stage ----------------
+        const uint64_t pol = policy_evict_first();
+        uint32_t it = 0;
+        bool dep_done = false;
+        int unit = blockIdx.x, next = -1;
+        while (!*s_abort) {
+            if (unit >= a.total_units) {  // end marker: a stage with a negative unit id
+                const int slot = it % NS;
+                if (wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1) && lane == 0) {
+                    s_unit[slot] = -1;
+                    mbar_arrive(&full[slot]);
+                }
+                it++;
+                break;
+            }
+            const int p = prob_of(a, unit);
+            const ChainProb &P = a.p[p];
+            int tile, chunk, s0, s1;
+            unit_stages(P, unit, tile, chunk, s0, s1);
+            const bool glu = P.act != ACT_NONE;
+            const int orow = glu ? tile * 16 + (lane & 15) : tile * 32 + lane;
+            const bool valid = orow < P.N;
+            const uint8_t *base = ((glu && lane >= 16) ? P.w2 : P.w) + (int64_t)orow * P.w_row_stride;
+            const bool ca = P.codec == CA;
+            const int nb = P.K / QK, kb = ca ? ch_kb<CA>() : ch_kb<CB>(), bpb = ca ? Fmt<CA>::bpb : Fmt<CB>::bpb;
+            const int sp = ca ? ch_sp<CA>() : ch_sp<CB>();
+            for (int st = s0; st < s1; st++, it++) {
+                const int slot = it % NS;
+                if (!wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1)) break;
+                const int bs = st * kb, nbk = min(kb, nb - bs);
+                const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
+                const uint32_t off = (uint32_t)(src & 15);
+                const uint32_t bytes = valid ? ((off + nbk * bpb + 15) & ~15u) : 0u;
+                rowoff[slot * 32 + lane] = (uint8_t)off;
+                uint32_t total = bytes;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+                if (lane == 0) {
+                    s_unit[slot] = unit;
+                    if (total) mbar_arrive_expect_tx(&full[slot], total);
+                    else mbar_arrive(&full[slot]);
+                }
+                __syncwarp();
+                if (bytes)
+                    bulk_g2s(ring + slot * L::SLOT + lane * sp, (const void *)(src - off), bytes, &full[slot], pol);
+                if (!dep_done) {  // first weights in flight; the work counter is the previous kernel's
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    dep_done = true;
+                }
+                if (st == s0 && next < 0) {  // claim the following unit now: its latency hides behind the copies
+                    int nu = 0;
+                    if (lane == 0) nu = (int)gridDim.x + atomicAdd(a.ctl, 1);
+                    next = __shfl_sync(0xffffffffu, nu, 0);
+                }
+            }
+            unit = next;
+            next = -1;
+        }
+        if (*s_abort) {
+            // gave up: wait (bounded) until the copies this CTA issued last have
+            // landed, so none writes shared memory after the CTA is gone
+            const uint64_t t0 = globaltimer();
+            for (uint32_t i = it > (uint32_t)NS ? it - NS : 0; i < it; i++)
+                while (!mbar_try_wait(&full[i % NS], (i / NS) & 1) && globaltimer() - t0 < 500000000ull) {
+                }
+        }
+    } else {
+        // ---------------- consumers: warp = (row half, block column) ----------------
+        // thread (g, tq) of the m16n8k32 fragments holds rows g and g + 8 of
+        // its warp's 16-row half of the tile
+        const int rh = warp & 1, bc = warp >> 1, g = lane >> 2, tq = lane & 3;
+        const int r0 = 16 * rh + g, r1 = r0 + 8;
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        uint32_t it = 0;
+        int tix = 0, cur = -1, sync_target = 0;
+        for (;;) {
+            const int slot = it % NS;
+            if (!wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2)) break;
+            const int unit = s_unit[slot];
+            if (unit < 0 || *s_abort) break;
+            const int q = prob_of(a, unit);
+            const ChainProb &P = a.p[q];
+            if (q != cur) {
+                // a new problem: wait until every warp is done with the previous
+                // one and (if it reads an earlier problem's output) until that
+                // problem's every tile is stored, then quantize its activation row
+                sync_target += CH_CW;
+                if (!consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
+                if (P.dep >= 0 && warp == 0 && lane == 0) {
+                    const int need = a.p[P.dep].tiles;
+                    const uint64_t t0 = globaltimer();
+                    while (ld_acquire(a.ctl + 2 + P.dep) < need) {
+                        if (*s_abort) break;
+                        if (globaltimer() - t0 > 2000000000ull) {
+                            *s_abort = 1;
+                            atomicCAS(a.err, 0, 3);
+                            break;
+                        }
+                    }
+                }
+                sync_target += CH_CW;
+                if (!consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
+                const int nb = P.K / QK;
+                const uint16_t *xs = reinterpret_cast<const uint16_t *>(P.x);
+                for (int b0 = warp; b0 < nb; b0 += 4 * CH_CW) {
+                    uint4 v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int b = b0 + u * CH_CW;
+                        if (b < nb) v[u] = __ldcg(reinterpret_cast<const uint4 *>(xs + (int64_t)b * QK + 8 * lane));
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int b = b0 + u * CH_CW;
+                        if (b < nb) imma_quantize<F16>(v[u], xq8 + b * IMMA_XB);
+                    }
+                }
+                sync_target += CH_CW;
+                if (!consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
+                cur = q;
+            }
+            int tile, chunk, s0, s1;
+            unit_stages(P, unit, tile, chunk, s0, s1);
+            const int nb = P.K / QK;
+            const bool q6 = P.codec == Q6_K;
+            float acc0 = 0.f, acc1 = 0.f;
+            bool ok = true;
+            for (int st = s0; st < s1; st++, it++) {
+                const int sl = it % NS;
+                if (st > s0 && !wait_bounded(&full[sl], (it / NS) & 1, s_abort, a.err, 2)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *stg = ring + sl * L::SLOT;
+                const uint8_t *ro = rowoff + sl * 32;
+                if (!*s_abort) {
+                    if (!q6) {  // Q4_K: 8 blocks per stage, one per block column
+                        const int b = st * ch_kb<Q4_K>() + bc;
+                        if (b < nb)
+                            imma_q4k(stg + r0 * ch_sp<Q4_K>() + ro[r0] + bc * 144,
+                                     stg + r1 * ch_sp<Q4_K>() + ro[r1] + bc * 144, xq8 + b * IMMA_XB, g, tq, acc0,
+                                     acc1);
+                    } else {    // Q6_K: 4 blocks per stage, two 128-value halves each
+                        const int b = st * ch_kb<Q6_K>() + (bc >> 1);
+                        if (b < nb)
+                            imma_q6k(stg + r0 * ch_sp<Q6_K>() + ro[r0] + (bc >> 1) * 210,
+                                     stg + r1 * ch_sp<Q6_K>() + ro[r1] + (bc >> 1) * 210, bc & 1,
+                                     xq8 + b * IMMA_XB, g, tq, acc0, acc1);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[sl]);
+            }
+            if (!ok || *s_abort) break;
+            if (q6) {  // lanes tq = 0 / 1 hold the two 16-value sub-blocks of each MMA
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+            }
+            // tile store: each warp posts its 16 row partials (lanes tq == 0);
+            // the last of the 16 warps to arrive sums the 8 block columns of
+            // every row in column order (and K chunks in chunk order through
+            // the partial buffer) and stores
+            const int bi = tix % (NS + 1);
+            float *rb = reinterpret_cast<float *>(smem + L::OFF_RB) + bi * (8 * 32);
+            if (tq == 0) {
+                rb[bc * 32 + r0] = acc0;
+                rb[bc * 32 + r1] = acc1;
+            }
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                old = atomicAdd(dcnt + bi, 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            tix++;
+            if (old != CH_CW - 1) continue;
+            __threadfence_block();
+            const bool glu = P.act != ACT_NONE;
+            const int row = glu ? (lane & 15) : lane;
+            float u = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; c++) u += rb[c * 32 + lane];
+            bool store = true;
+            float v = 0.f, v2 = 0.f;
+            if (P.S > 1) {
+                const int stile = P.split_base + tile;
+                __stcg(a.partial + ((int64_t)stile * P.S + chunk) * 32 + lane, u);
+                __threadfence();
+                __syncwarp();
+                int prev = 0;
+                if (lane == 0) {
+                    prev = atomicAdd(a.tcnt + stile, 1);
+                    if (prev == P.S - 1) __threadfence();
+                }
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                store = prev == P.S - 1;
+                if (store) {
+                    for (int c = 0; c < P.S; c++) {
+                        const float *pp = a.partial + ((int64_t)stile * P.S + c) * 32;
+                        v += __ldcg(pp + row);
+                        if (glu) v2 += __ldcg(pp + row + 16);
+                    }
+                    if (lane == 0) a.tcnt[stile] = 0;
+                }
+            } else {
+                v = __shfl_sync(0xffffffffu, u, row);
+                v2 = __shfl_sync(0xffffffffu, u, (row + 16) & 31);
+            }
+            if (store) {
+                if (glu) v = apply_act(P.act, v) * v2;
+                const int n = tile * (glu ? 16 : 32) + row;
+                if (n < P.N && (!glu || lane < 16)) {
+                    float bv = 0.f;
+                    if (P.bias) {
+                        if (P.bias_dtype == F32) bv = reinterpret_cast<const float *>(P.bias)[n];
+                        else if (P.bias_dtype == BF16)
+                            bv = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(P.bias)[n]);
+                        else bv = __half2float(reinterpret_cast<const __half *>(P.bias)[n]);
+                    }
+                    store_out(P.y, P.y_dtype, n, v + bv);
+                }
+                if (P.counted) {  // publish the finished tile to dependent problems
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) atomicAdd(a.ctl + 2 + q, 1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) dcnt[bi] = 0;
+        }
+    }
+    // the last CTA out resets the work and completion counters
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.ctl + 1, 1) == (int)gridDim.x - 1) {
+            __threadfence();
+            a.ctl[0] = 0;
+            for (int q = 0; q < a.count; q++) a.ctl[2 + q] = 0;
+            __threadfence();
+            a.ctl[1] = 0;
+        }
+    }
+}
+
+template <int CA, int CB, bool F16>
+cudaError_t launch_chain_t(const ChainArgs &a, cudaStream_t st) {
+    using L = ChainLayout<CA, CB>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(chain_kernel<CA, CB, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             L::BYTES);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel<CA, CB, F16>, CH_THREADS, L::BYTES);
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;  // the kernel needs one whole SM
+    int grid = num_sms() * per_sm;
+    if (const char *g = dev_env("KQ_CHAIN_GRID")) grid = atoi(g);  // development override
+    grid = std::min(grid, a.total_units);
+    if (grid <= 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(CH_THREADS);
+    cfg.dynamicSmemBytes = L::BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, chain_kernel<CA, CB, F16>, a);
+}
+
+int chain_kb(int codec) { return codec == Q4_K ? ch_kb<Q4_K>() : ch_kb<Q6_K>(); }
+
+}  // namespace
+
+// Host plan: units and K chunks per problem, scratch sizes.  The fused kernel
+// takes Q4_K and Q6_K problems (the Q4_K_M mix) with K <= 16384.
+bool chain_plan(const ChainProblemDesc *pd, int count, ChainPlan *out) {
+    if (count < 1 || count > CH_MAX) return false;
+    for (int q = 0; q < count; q++) {
+        if (pd[q].codec != Q4_K && pd[q].codec != Q6_K) return false;
+        if (pd[q].k > CH_KMAX) return false;  // the activation row must fit in shared memory
+    }
+    int chunk_stages = 2;
+    if (const char *e = dev_env("KQ_CHAIN_CHUNK")) chunk_stages = std::max(1, atoi(e));  // development override
+    ChainPlan pl{};
+    pl.pair = 0;
+    long units = 0, split_tiles = 0, partial_floats = 0;
+    for (int q = 0; q < count; q++) {
+        const ChainProblemDesc &d = pd[q];
+        const int kb = chain_kb(d.codec);
+        const long rows_out = d.act != ACT_NONE ? 16 : 32;
+        const long tiles = (d.n + rows_out - 1) / rows_out;
+        const long nst = (d.k / QK + kb - 1) / kb;
+        const long chunk = std::min<long>(nst, chunk_stages);
+        const long S = (nst + chunk - 1) / chunk;
+        pl.tiles[q] = (int)tiles;
+        pl.nst[q] = (int)nst;
+        pl.S[q] = (int)S;
+        pl.chunk[q] = (int)chunk;
+        pl.unit_base[q] = (int)units;
+        pl.split_base[q] = (int)split_tiles;
+        units += tiles * S;
+        if (S > 1) {
+            split_tiles += tiles;
+            partial_floats += tiles * S * 32;
+        }
+    }
+    if (units > 0x3fffffffL) return false;
+    pl.total_units = (int)units;
+    pl.split_tiles = split_tiles;
+    pl.partial_floats = partial_floats;
+    *out = pl;
+    return true;
+}
+
+cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan &pl, int x_dtype, int *err, int *ctl,
+                         int *tcnt, float *partial, cudaStream_t st) {
+    ChainArgs a{};
+    a.count = count;
+    a.total_units = pl.total_units;
+    a.err = err;
+    a.ctl = ctl;
+    a.tcnt = tcnt;
+    a.partial = partial;
+    for (int q = 0; q < count; q++) {
+        ChainProb &P = a.p[q];
+        const ChainProblemDesc &d = pd[q];
+        P.w = (const uint8_t *)d.w;
+        P.w2 = (const uint8_t *)d.w2;
+        P.w_row_stride = d.w_row_stride;
+        P.x = (const uint8_t *)d.x;
+        P.y = d.y;
+        P.bias = d.bias;
+        P.y_dtype = d.y_dtype;
+        P.bias_dtype = d.bias_dtype;
+        P.N = (int)d.n;
+        P.K = (int)d.k;
+        P.codec = d.codec;
+        P.act = d.act;
+        P.dep = d.dep;
+        P.counted = 0;
+        for (int r = q + 1; r < count; r++) P.counted |= pd[r].dep == q;
+        P.tiles = pl.tiles[q];
+        P.nst = pl.nst[q];
+        P.S = pl.S[q];
+        P.chunk = pl.chunk[q];
+        P.unit_base = pl.unit_base[q];
+        P.split_base = pl.split_base[q];
+    }
+    return x_dtype == F16 ? launch_chain_t<Q4_K, Q6_K, true>(a, st) : launch_chain_t<Q4_K, Q6_K, false>(a, st);
+}
+
+}  // namespace kq

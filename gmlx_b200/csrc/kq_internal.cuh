@@ -68,6 +68,28 @@ struct GemvArgs {
     int debug;       // development only: 1 = skip decode, 2 = skip weight copies
 };
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st);
+// A chain of one-row GEMVs in one persistent launch (kq_chain.cu).
+struct ChainProblemDesc {
+    int codec;
+    const void *x, *w, *w2;
+    int64_t n, k, w_row_stride;
+    int act;
+    void *y;
+    int y_dtype;
+    const void *bias;
+    int bias_dtype;
+    int dep;  // index of an earlier problem whose output this one reads, or -1
+};
+struct ChainPlan {
+    int pair, total_units;
+    int tiles[8], nst[8], S[8], chunk[8], unit_base[8], split_base[8];
+    long split_tiles, partial_floats;
+};
+// false when no fused chain kernel takes these problems (codec mix, sizes)
+bool chain_plan(const ChainProblemDesc *pd, int count, ChainPlan *out);
+cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan &pl, int x_dtype, int *err, int *ctl,
+                         int *tcnt, float *partial, cudaStream_t st);
+
 // Communication buffer of the fused all-reduce: a 4 KB header (word 0: this
 // rank's call epoch; flags at 64 + 4 * (parity * world + rank)) and f32 slots
 // [parity][world][n] from byte 4096.

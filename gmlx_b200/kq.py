@@ -39,7 +39,7 @@ from .synth import BLOCK_BYTES, CODECS, QK, codec_id
 __all__ = [
     "codecs", "all_codecs", "codec_has_matmul", "codec_has_moe_glu", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
     "moe_glu_gather_kq", "gather_qmv_kq", "gather_qmv_mix_ns_kq", "moe_router_topk", "workspace_error",
-    "moe_expert_layer_local", "quantized_matmul_allreduce", "quantized_matmul_qmv_bias", "moe_glu_gather_shexp_kq", "gather_qmv_mix_kq",
+    "moe_expert_layer_local", "quantized_matmul_chain", "quantized_matmul_allreduce", "quantized_matmul_qmv_bias", "moe_glu_gather_shexp_kq", "gather_qmv_mix_kq",
 ]
 
 _DT = {torch.float32: _lib.KQ_F32, torch.float16: _lib.KQ_F16, torch.bfloat16: _lib.KQ_BF16}
@@ -545,3 +545,75 @@ def moe_expert_layer_local(x: torch.Tensor, idx: torch.Tensor, scores: torch.Ten
                                                e_total, _lib.ACTS[act], _p(y), _DT[od], _p(ws), ws.numel(),
                                                _stream(x.device)), "moe_expert_layer_local")
     return y
+
+
+def quantized_matmul_chain(problems, out_dtype: torch.dtype | None = None) -> list[torch.Tensor]:
+    """A chain of one-row decode projections in one launch (the dense decode
+    of one token: q|k|v, o, gate+up, down).  gmlx fuses projections that share
+    an input by row-concatenation (occupancy_fuse.py:141-200, 272-330); this
+    op streams every projection of the list in a single persistent kernel.
+
+    ``problems``: up to 8 dicts with keys ``x`` (one activation row ``[k]`` or
+    ``[1, k]``, or the int index of an earlier problem whose output it is),
+    ``w`` (wire weights), ``codec``, optional ``w2`` + ``act`` (fused gate/up,
+    as ``quantized_glu``) or ``bias`` (as ``quantized_matmul_qmv_bias``).
+    Returns the outputs ``[1, n]`` in order (a problem read by a later one
+    keeps the activation dtype); each equals the single-op result for that
+    row within the kernels' tolerance."""
+    L = _lib.load()
+    n = len(problems)
+    if not 1 <= n <= _lib.KQ_CHAIN_MAX:
+        raise ValueError(f"quantized_matmul_chain takes 1..{_lib.KQ_CHAIN_MAX} problems, got {n}")
+    arr = (_lib.ChainProblem * n)()
+    outs, keep = [], []
+    x_dtype, dev = None, None
+    for i, pr in enumerate(problems):
+        c = _cid(pr["codec"])
+        w, rs = _rows2d(pr["w"])
+        _need_cuda(w)
+        k = _wire_k(w, c)
+        x = pr["x"]
+        dep = -1
+        if isinstance(x, int):
+            if not 0 <= x < i:
+                raise ValueError(f"problem {i}: x index {x} is not an earlier problem")
+            dep = x
+            x = outs[x]
+        _need_cuda(x)
+        x = x.reshape(-1)
+        if x.numel() != k:
+            raise ValueError(f"problem {i}: activation row of {x.numel()} values for K={k}")
+        x = x.contiguous()
+        if x_dtype is None:
+            x_dtype, dev = x.dtype, x.device
+        if x.dtype != x_dtype or x.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("chain activations must all be f16 or all bf16")
+        w2 = None
+        act = "none"
+        if pr.get("w2") is not None:
+            w2, rs2 = _rows2d(pr["w2"])
+            if rs2 != rs or w2.shape != w.shape:
+                raise ValueError(f"problem {i}: gate and up weights must share shape and layout")
+            act = pr.get("act", "silu")
+        nout = w.shape[-2] if w.dim() >= 2 else 1
+        od = out_dtype or x_dtype
+        if any(isinstance(p.get("x"), int) and p["x"] == i for p in problems[i + 1:]):
+            od = x_dtype  # read back as a later problem's activations
+        y = torch.empty(1, nout, dtype=od, device=dev)
+        b = pr.get("bias")
+        if b is not None:
+            _need_cuda(b)
+            b = b.contiguous()
+        arr[i].codec, arr[i].x, arr[i].w = c, _p(x), _p(w)
+        arr[i].w2 = _p(w2)
+        arr[i].n, arr[i].k, arr[i].w_row_stride = nout, k, rs
+        arr[i].act = _lib.ACTS[act]
+        arr[i].y, arr[i].y_dtype = _p(y), _DT[od]
+        arr[i].bias, arr[i].bias_dtype = _p(b), (_DT[b.dtype] if b is not None else 0)
+        arr[i].depends_on = dep
+        outs.append(y)
+        keep += [x, w, w2, b]
+    ws = _workspace(dev, int(L.kq_quantized_matmul_chain_workspace_size(arr, n)))
+    _lib.check(L.kq_quantized_matmul_chain(arr, n, _DT[x_dtype], _p(ws), ws.numel(), _stream(dev)),
+               "quantized_matmul_chain")
+    return outs

@@ -269,6 +269,42 @@ int kq_quantized_matmul_noalloc(int codec, const void *x, int x_dtype, int64_t m
  * CUDA failure. */
 int kq_noalloc_error(int clear, void *stream);
 
+/* ---- A chain of one-row decode projections in one launch
+ *
+ * The dense decode of one token is a short chain of quantized matmuls on one
+ * activation row: q|k|v, o, gate+up, down (gmlx's occupancy fusions row-
+ * concatenate the ones that share an input, gmlx/occupancy_fuse.py:141-200
+ * and :272-330, to launch fewer kernels).  kq_quantized_matmul_chain runs up
+ * to KQ_CHAIN_MAX such projections in ONE persistent launch: the GPU flows
+ * from one projection's weights into the next with no per-launch ramp or
+ * tail.  A problem whose input is an earlier problem's output names it in
+ * depends_on; its weights stream in while it waits, and its activations are
+ * read only once that problem's every output tile is stored (device-side
+ * completion counters, bounded waits: on expiry the workspace error word
+ * becomes 3 or 4).  Each problem computes what kq_quantized_matmul (act ==
+ * KQ_ACT_NONE, optional bias) or kq_quantized_glu (act != KQ_ACT_NONE, w2 =
+ * up weights) computes for one activation row.  The fused kernel takes
+ * chains of Q4_K and Q6_K problems (the Q4_K_M mix) with k <= 16384; any
+ * other chain runs as one launch per problem, in order, with the same
+ * results. */
+#define KQ_CHAIN_MAX 8
+typedef struct kq_chain_problem {
+    int codec;
+    const void *x;        /* one activation row [k] of the chain's x_dtype, 16-byte aligned */
+    const void *w;        /* [n] rows of k/256 blocks at w_row_stride bytes */
+    const void *w2;       /* up weights of a fused gate/up (act != KQ_ACT_NONE), else NULL */
+    int64_t n, k, w_row_stride;
+    int act;              /* KQ_ACT_NONE, or the gate activation of a fused gate/up */
+    void *y;              /* [n] outputs in y_dtype */
+    int y_dtype;
+    const void *bias;     /* optional [n] bias (act == KQ_ACT_NONE only), NULL if none */
+    int bias_dtype;
+    int depends_on;       /* index of an earlier problem whose output x reads, or -1 */
+} kq_chain_problem;
+size_t kq_quantized_matmul_chain_workspace_size(const kq_chain_problem *problems, int count);
+int kq_quantized_matmul_chain(const kq_chain_problem *problems, int count, int x_dtype, void *workspace,
+                              size_t workspace_bytes, void *stream);
+
 /* Reads (and with clear != 0 resets) the workspace's device error word;
  * synchronises `stream`.  Returns the word (0 = no device-side error). */
 int kq_workspace_error(void *workspace, int clear, void *stream);

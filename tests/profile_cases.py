@@ -13,6 +13,8 @@ Each case builds seeded synthetic weights (the bench's shapes), runs the op
                 from raw bytes brought in by TMA)
   prefill_down  Q6_K 4096x14336 GEMM, M=2048
   moe_prefill   Qwen3-like expert layer, T=512 (grouped GEMM path)
+  chain_layer   one Llama-3-8B Q4_K_M layer at M=1 in one chain launch
+                (q|k|v, o, gate+up, down reading the gate/up output)
 """
 import os
 import sys
@@ -57,6 +59,13 @@ def build(case):
         logits = torch.randn(t, e, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
         idx, sc = kq.moe_router_topk(logits, k, True, shared_gate=False)
         return lambda: kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, "q4_k", "q6_k", 0, e)
+    if case == "chain_layer":
+        x = _x(1, 4096)
+        qkv, o = _w("q4_k", 6144, 4096, 5), _w("q4_k", 4096, 4096, 6)
+        g, u, d = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _w("q6_k", 4096, 14336, 3)
+        pr = [{"x": x, "w": qkv, "codec": "q4_k"}, {"x": x, "w": o, "codec": "q4_k"},
+              {"x": x, "w": g, "w2": u, "act": "silu", "codec": "q4_k"}, {"x": 2, "w": d, "codec": "q6_k"}]
+        return lambda: kq.quantized_matmul_chain(pr)
     raise SystemExit(f"unknown case {case!r}; see the module docstring")
 
 
