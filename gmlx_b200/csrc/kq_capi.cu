@@ -947,24 +947,30 @@ static int chain_descs(const kq_chain_problem *pr, int count, int x_dtype, kq::C
     return KQ_OK;
 }
 
-// chain workspace: [0, 256) error word; [256, 512) work / exit / completion
-// counters; then the K-split tile counters and partial rows
+// chain workspace: [0, 256) error word; the work / exit / completion counters
+// and the K-split tile counters in the last 64 KB of the counter region that
+// every kq call leaves zero (the chain leaves its counters zero too, so calls
+// sharing one workspace never see each other's counts); the partial rows,
+// scratch, after that region
+constexpr size_t CHAIN_CTL = 256 + CNT_RESERVE - 65536;
+constexpr long CHAIN_MAX_SPLIT_TILES = (65536 - 256) / 4;
 struct ChainWs {
-    size_t ctl_off = 256, tcnt_off = 512, part_off = 512, total = 512;
+    size_t ctl_off = CHAIN_CTL, tcnt_off = CHAIN_CTL + 256, part_off = 256 + CNT_RESERVE, total = 0;
 };
 static ChainWs chain_ws(const kq::ChainPlan &pl) {
     ChainWs w;
-    w.part_off = align256(w.tcnt_off + (size_t)pl.split_tiles * sizeof(int));
     w.total = align256(w.part_off + (size_t)pl.partial_floats * sizeof(float));
     return w;
 }
+
+static bool chain_fits(const kq::ChainPlan &pl) { return pl.split_tiles <= CHAIN_MAX_SPLIT_TILES; }
 
 size_t kq_quantized_matmul_chain_workspace_size(const kq_chain_problem *problems, int count) {
     kq::ChainProblemDesc d[KQ_CHAIN_MAX];
     if (chain_descs(problems, count, KQ_BF16, d, false)) return 0;
     size_t need = 256;
     kq::ChainPlan pl;
-    if (kq::chain_plan(d, count, &pl)) need = chain_ws(pl).total;
+    if (kq::chain_plan(d, count, &pl) && chain_fits(pl)) need = chain_ws(pl).total;
     // the per-problem path's workspace, should the fused kernel not take the chain
     for (int q = 0; q < count; q++)
         need = std::max(need, dense_ws(d[q].codec, 1, d[q].n, d[q].k, d[q].act));
@@ -981,7 +987,7 @@ int kq_quantized_matmul_chain(const kq_chain_problem *problems, int count, int x
     if (!workspace || ((uintptr_t)workspace & 255))
         return fail(KQ_ERR_WORKSPACE, "%s: a 256-byte aligned workspace is required", what);
     kq::ChainPlan pl;
-    if (!dev_env("KQ_CHAIN_UNFUSED") && kq::chain_plan(d, count, &pl)) {
+    if (!dev_env("KQ_CHAIN_UNFUSED") && kq::chain_plan(d, count, &pl) && chain_fits(pl)) {
         const ChainWs w = chain_ws(pl);
         if (workspace_bytes < w.total)
             return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes required, got %zu", what, w.total, workspace_bytes);

@@ -70,6 +70,7 @@ struct ChainArgs {
     int *ctl;         // [0] work counter, [1] finished CTAs, [2 + p] finished tiles of problem p
     int *tcnt;        // K-split tile counters
     float *partial;   // K-split partial rows [split tile][S][32]
+    int debug;        // development builds only: 1 = consumers skip the arithmetic, 2 = no weight copies
 };
 
 template <int C> constexpr int ch_kb() { return KB_OF<C>; }
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                 const int bs = st * kb, nbk = min(kb, nb - bs);
                 const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
                 const uint32_t off = (uint32_t)(src & 15);
-                const uint32_t bytes = valid ? ((off + nbk * bpb + 15) & ~15u) : 0u;
+                const uint32_t bytes = (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
                 rowoff[slot * 32 + lane] = (uint8_t)off;
                 uint32_t total = bytes;
 #pragma unroll
@@ -309,7 +310,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                 }
                 const uint8_t *stg = ring + sl * L::SLOT;
                 const uint8_t *ro = rowoff + sl * 32;
-                if (!*s_abort) {
+                if (!*s_abort && !(a.debug & 1)) {
                     if (!q6) {  // Q4_K: 8 blocks per stage, one per block column
                         const int b = st * ch_kb<Q4_K>() + bc;
                         if (b < nb)
@@ -504,6 +505,7 @@ cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan 
     a.ctl = ctl;
     a.tcnt = tcnt;
     a.partial = partial;
+    if (const char *e = dev_env("KQ_CHAIN_DEBUG")) a.debug = atoi(e);  // development switch
     for (int q = 0; q < count; q++) {
         ChainProb &P = a.p[q];
         const ChainProblemDesc &d = pd[q];
