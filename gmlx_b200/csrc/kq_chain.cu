@@ -18,10 +18,12 @@
 //    on earlier ones, whose units are all held by running CTAs that wait on
 //    nothing later.  Every wait is bounded (~2 s, then an error code in the
 //    workspace's first word and the kernel winds down).
-//  * One CTA per SM: a producer warp streams raw weight rows (1-D bulk
-//    copies, >= ~1 KB per row) into a ring of stages of 32 rows; 16 consumer
-//    warps (2 row halves x 8 block columns) run the integer tensor-core dot
-//    of kq_imma.cuh on each stage.
+//  * One CTA per SM: a producer warp streams each stage -- 32 weight rows x
+//    8 super-blocks of wire bytes -- into a ring with ONE 2-D TMA tensor copy
+//    (two 16-row boxes for a fused gate/up).  Per-row 1-D bulk copies of
+//    ~1 KB cap the SM's copy engine near 20 GB/s; one box per stage streams
+//    at full HBM rate.  16 consumer warps (2 row halves x 8 block columns)
+//    run the integer tensor-core dot of kq_imma.cuh on each stage.
 //  * Each problem's activation row is quantized ONCE per CTA (int16 split
 //    into two exact bytes, one f32 scale per 32 values, plus the sums the
 //    codecs' offset terms need) into shared memory, when the CTA reaches the
@@ -31,6 +33,7 @@
 //    order (deterministic) and stores.
 //  * The last CTA to finish resets the work and completion counters, so the
 //    workspace is left zeroed for the next call (as every kq workspace).
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -45,12 +48,15 @@ namespace {
 
 constexpr int CH_MAX = KQ_CHAIN_MAX;
 constexpr int CH_CW = 16;                     // consumer warps: 2 row halves x 8 block columns
-constexpr int CH_THREADS = 32 * (CH_CW + 1);  // + one producer warp
+constexpr int CH_PW = CH_CW;                  // producer warp
+constexpr int CH_THREADS = 32 * (CH_CW + 2);  // + producer + epilogue
+constexpr int CH_EQ = 8;                      // finished-tile queue entries
 constexpr int CH_KMAX = 16384;                // activation row length held quantized in shared memory
 constexpr int CH_XQB = CH_KMAX / QK * IMMA_XB;
 constexpr int CH_SMEM = 232448;               // one CTA per SM
 
-struct ChainProb {
+struct alignas(64) ChainProb {
+    CUtensorMap tmw, tmw2;  // weight rows as [rows][row bytes / 8] uint64 tensors (w2: fused gate/up's up)
     const uint8_t *w, *w2;
     int64_t w_row_stride;
     const uint8_t *x;  // one activation row (f16 / bf16)
@@ -70,11 +76,19 @@ struct ChainArgs {
     int *ctl;         // [0] work counter, [1] finished CTAs, [2 + p] finished tiles of problem p
     int *tcnt;        // K-split tile counters
     float *partial;   // K-split partial rows [split tile][S][32]
-    int debug;        // development builds only: 1 = consumers skip the arithmetic, 2 = no weight copies
+    int debug;        // development builds only: 1 = consumers skip the arithmetic, 2 = no weight copies,
+                      // 4 = no activation quantization, 8 = no consumer barriers, 16 = no dependency wait,
+                      // 32 = epilogue without fences (wrong results; timing only),
+                      // 64 = CTA 0 records stage timestamps into dbg
+    unsigned long long *dbg;  // development: [0,256) issue, [256,512) full seen, [512,768) slot free
 };
 
-template <int C> constexpr int ch_kb() { return KB_OF<C>; }
-template <int C> constexpr int ch_sp() { return spitch_of<C, true>(); }
+// a stage: 8 super-blocks of 32 rows; the box row pitch is == 16 (mod 128)
+// bytes, so the 8 rows x 4 words of an MMA fragment load hit 32 banks
+// (Q4_K: 1152 bytes + 16 bytes of the next block; Q6_K: exactly 1680)
+template <int C> constexpr int ch_kb() { return 8; }
+template <int C> constexpr int ch_boxw() { return C == Q4_K ? 146 : 210; }  // uint64 elements per box row
+template <int C> constexpr int ch_sp() { return 8 * ch_boxw<C>(); }
 template <int C> constexpr int ch_wbytes() { return 32 * ch_sp<C>(); }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
@@ -82,19 +96,30 @@ template <int CA, int CB> struct ChainLayout {
     static constexpr int SLOT = cmax(ch_wbytes<CA>(), ch_wbytes<CB>());  // one stage: 32 weight rows
     static constexpr int OFF_BAR = 0;       // full[NS], empty[NS]
     static constexpr int OFF_UNIT = 128;    // s_unit[8]
-    static constexpr int OFF_ROWOFF = 256;  // NS x 32 bytes
     static constexpr int OFF_MISC = 512;    // abort flag, sync counter, partial-buffer counters
-    static constexpr int OFF_XQ = 640;      // the current problem's quantized activations
+    static constexpr int OFF_EBAR = 576;    // tile-queue mbarriers: efull[EQ], eempty[EQ]
+    static constexpr int OFF_EQ = 768;      // tile queue: [EQ] x (q, tile, chunk, pad, 32 f32 row sums)
+    static constexpr int EQ_ENTRY = 144;
+    static constexpr int OFF_XQ = OFF_EQ + CH_EQ * EQ_ENTRY;  // the current problem's quantized activations
     static constexpr int RB_ONE = 8 * 32 * 4;  // [block column][tile row] partials
     static constexpr int OFF_RB = OFF_XQ + CH_XQB;
     static constexpr int NS_FIT = (CH_SMEM - OFF_RB - RB_ONE - 128) / (SLOT + RB_ONE);  // NS + 1 partial buffers
     static constexpr int NS = NS_FIT > 6 ? 6 : NS_FIT;
     static constexpr int OFF_RING = (OFF_RB + (NS + 1) * RB_ONE + 127) / 128 * 128;
-    static constexpr int BYTES = OFF_RING + NS * SLOT;
+    static constexpr int BYTES = OFF_RING + NS * SLOT + 16;  // + the tail the 2-byte-aligned Q6_K reads may touch
     static_assert(NS >= 3, "ring must hold three stages");
-    static_assert(NS * 32 <= 256, "row offsets");
+    static_assert(OFF_RING % 128 == 0 && SLOT % 128 == 0, "TMA destinations");
     static_assert(BYTES <= CH_SMEM, "shared memory");
 };
+
+__device__ __forceinline__ void tma_box(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                        uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
     int v;
@@ -153,18 +178,24 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
     uint64_t *empty = full + NS;
     int *s_unit = reinterpret_cast<int *>(smem + L::OFF_UNIT);
-    uint8_t *rowoff = smem + L::OFF_ROWOFF;
     volatile int *s_abort = reinterpret_cast<volatile int *>(smem + L::OFF_MISC);
     int *s_sync = reinterpret_cast<int *>(smem + L::OFF_MISC + 4);
     int *dcnt = reinterpret_cast<int *>(smem + L::OFF_MISC + 16);  // NS + 1 partial-buffer counters
     uint8_t *xq8 = smem + L::OFF_XQ;
     uint8_t *ring = smem + L::OFF_RING;
+    uint64_t *efull = reinterpret_cast<uint64_t *>(smem + L::OFF_EBAR);
+    uint64_t *eempty = efull + CH_EQ;
+    uint8_t *equeue = smem + L::OFF_EQ;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], CH_CW);
+        }
+        for (int i = 0; i < CH_EQ; i++) {
+            mbar_init(&efull[i], 1);
+            mbar_init(&eempty[i], 1);
         }
         *s_abort = 0;
         *s_sync = 0;
@@ -174,12 +205,12 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
     __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    if (warp == CH_CW) {
+    if (warp == CH_PW) {
         // ---------------- producer: lane r streams tile row r of every stage ----------------
         const uint64_t pol = policy_evict_first();
         uint32_t it = 0;
         bool dep_done = false;
-        int unit = blockIdx.x, next = -1;
+        int unit = blockIdx.x, next = -1;  // next: lane 0's claim of the following unit
         while (!*s_abort) {
             if (unit >= a.total_units) {  // end marker: a stage with a negative unit id
                 const int slot = it % NS;
@@ -195,42 +226,39 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
             int tile, chunk, s0, s1;
             unit_stages(P, unit, tile, chunk, s0, s1);
             const bool glu = P.act != ACT_NONE;
-            const int orow = glu ? tile * 16 + (lane & 15) : tile * 32 + lane;
-            const bool valid = orow < P.N;
-            const uint8_t *base = ((glu && lane >= 16) ? P.w2 : P.w) + (int64_t)orow * P.w_row_stride;
             const bool ca = P.codec == CA;
-            const int nb = P.K / QK, kb = ca ? ch_kb<CA>() : ch_kb<CB>(), bpb = ca ? Fmt<CA>::bpb : Fmt<CB>::bpb;
-            const int sp = ca ? ch_sp<CA>() : ch_sp<CB>();
+            const int boxw = ca ? ch_boxw<CA>() : ch_boxw<CB>(), xstep = ca ? Fmt<CA>::bpb : Fmt<CB>::bpb;
+            const uint32_t stage_bytes = 32u * 8u * (uint32_t)boxw;
             for (int st = s0; st < s1; st++, it++) {
                 const int slot = it % NS;
                 if (!wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1)) break;
-                const int bs = st * kb, nbk = min(kb, nb - bs);
-                const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
-                const uint32_t off = (uint32_t)(src & 15);
-                const uint32_t bytes = (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
-                rowoff[slot * 32 + lane] = (uint8_t)off;
-                uint32_t total = bytes;
-#pragma unroll
-                for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+                if ((a.debug & 64) && blockIdx.x == 0 && lane == 0 && it < 256) a.dbg[512 + it] = globaltimer();
                 if (lane == 0) {
                     s_unit[slot] = unit;
-                    if (total) mbar_arrive_expect_tx(&full[slot], total);
-                    else mbar_arrive(&full[slot]);
+                    uint8_t *dst = ring + slot * L::SLOT;
+                    const int x = st * xstep;  // 8 blocks of bpb bytes = bpb uint64 elements
+                    if (a.debug & 2) {
+                        mbar_arrive(&full[slot]);
+                    } else {
+                        mbar_arrive_expect_tx(&full[slot], stage_bytes);
+                        if (glu) {  // 16 gate rows over the same 16 up rows
+                            tma_box(dst, &P.tmw, x, tile * 16, &full[slot], pol);
+                            tma_box(dst + 16 * 8 * boxw, &P.tmw2, x, tile * 16, &full[slot], pol);
+                        } else {
+                            tma_box(dst, &P.tmw, x, tile * 32, &full[slot], pol);
+                        }
+                    }
                 }
                 __syncwarp();
-                if (bytes)
-                    bulk_g2s(ring + slot * L::SLOT + lane * sp, (const void *)(src - off), bytes, &full[slot], pol);
+                if ((a.debug & 64) && blockIdx.x == 0 && lane == 0 && it < 256) a.dbg[it] = globaltimer();
                 if (!dep_done) {  // first weights in flight; the work counter is the previous kernel's
                     asm volatile("griddepcontrol.wait;" ::: "memory");
                     dep_done = true;
                 }
-                if (st == s0 && next < 0) {  // claim the following unit now: its latency hides behind the copies
-                    int nu = 0;
-                    if (lane == 0) nu = (int)gridDim.x + atomicAdd(a.ctl, 1);
-                    next = __shfl_sync(0xffffffffu, nu, 0);
-                }
+                if (st == s0 && lane == 0)  // claim the following unit now; its result is read
+                    next = (int)gridDim.x + atomicAdd(a.ctl, 1);  // after this unit's copies are out
             }
-            unit = next;
+            unit = __shfl_sync(0xffffffffu, next, 0);
             next = -1;
         }
         if (*s_abort) {
@@ -241,7 +269,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                 while (!mbar_try_wait(&full[i % NS], (i / NS) & 1) && globaltimer() - t0 < 500000000ull) {
                 }
         }
-    } else {
+    } else if (warp < CH_CW) {
         // ---------------- consumers: warp = (row half, block column) ----------------
         // thread (g, tq) of the m16n8k32 fragments holds rows g and g + 8 of
         // its warp's 16-row half of the tile
@@ -262,8 +290,8 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                 // one and (if it reads an earlier problem's output) until that
                 // problem's every tile is stored, then quantize its activation row
                 sync_target += CH_CW;
-                if (!consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
-                if (P.dep >= 0 && warp == 0 && lane == 0) {
+                if (!(a.debug & 8) && !consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
+                if (P.dep >= 0 && warp == 0 && lane == 0 && !(a.debug & 16)) {
                     const int need = a.p[P.dep].tiles;
                     const uint64_t t0 = globaltimer();
                     while (ld_acquire(a.ctl + 2 + P.dep) < need) {
@@ -276,8 +304,8 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     }
                 }
                 sync_target += CH_CW;
-                if (!consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
-                const int nb = P.K / QK;
+                if (!(a.debug & 8) && !consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
+                const int nb = (a.debug & 4) ? 0 : P.K / QK;
                 const uint16_t *xs = reinterpret_cast<const uint16_t *>(P.x);
                 for (int b0 = warp; b0 < nb; b0 += 4 * CH_CW) {
                     uint4 v[4];
@@ -293,7 +321,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     }
                 }
                 sync_target += CH_CW;
-                if (!consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
+                if (!(a.debug & 8) && !consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
                 cur = q;
             }
             int tile, chunk, s0, s1;
@@ -308,21 +336,20 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     ok = false;
                     break;
                 }
+                if ((a.debug & 64) && blockIdx.x == 0 && warp == 0 && lane == 0 && it < 256)
+                    a.dbg[256 + it] = globaltimer();
                 const uint8_t *stg = ring + sl * L::SLOT;
-                const uint8_t *ro = rowoff + sl * 32;
                 if (!*s_abort && !(a.debug & 1)) {
-                    if (!q6) {  // Q4_K: 8 blocks per stage, one per block column
-                        const int b = st * ch_kb<Q4_K>() + bc;
-                        if (b < nb)
-                            imma_q4k(stg + r0 * ch_sp<Q4_K>() + ro[r0] + bc * 144,
-                                     stg + r1 * ch_sp<Q4_K>() + ro[r1] + bc * 144, xq8 + b * IMMA_XB, g, tq, acc0,
-                                     acc1);
-                    } else {    // Q6_K: 4 blocks per stage, two 128-value halves each
-                        const int b = st * ch_kb<Q6_K>() + (bc >> 1);
-                        if (b < nb)
-                            imma_q6k(stg + r0 * ch_sp<Q6_K>() + ro[r0] + (bc >> 1) * 210,
-                                     stg + r1 * ch_sp<Q6_K>() + ro[r1] + (bc >> 1) * 210, bc & 1,
+                    const int b = st * 8 + bc;  // 8 blocks per stage, one per block column
+                    if (b < nb) {
+                        if (!q6) {
+                            imma_q4k(stg + r0 * ch_sp<Q4_K>() + bc * 144, stg + r1 * ch_sp<Q4_K>() + bc * 144,
                                      xq8 + b * IMMA_XB, g, tq, acc0, acc1);
+                        } else {  // Q6_K: both 128-value halves of the block
+                            const uint8_t *b0 = stg + r0 * ch_sp<Q6_K>() + bc * 210, *b1 = stg + r1 * ch_sp<Q6_K>() + bc * 210;
+                            imma_q6k(b0, b1, 0, xq8 + b * IMMA_XB, g, tq, acc0, acc1);
+                            imma_q6k(b0, b1, 1, xq8 + b * IMMA_XB, g, tq, acc0, acc1);
+                        }
                     }
                 }
                 __syncwarp();
@@ -352,23 +379,61 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
             old = __shfl_sync(0xffffffffu, old, 0);
             tix++;
             if (old != CH_CW - 1) continue;
+            // the last warp of the unit hands the tile's 32 row sums to the
+            // epilogue warp through the queue (entry = the unit's sequence
+            // number, the same in every warp), so no consumer waits on a fence
             __threadfence_block();
-            const bool glu = P.act != ACT_NONE;
-            const int row = glu ? (lane & 15) : lane;
             float u = 0.f;
 #pragma unroll
             for (int c = 0; c < 8; c++) u += rb[c * 32 + lane];
+            const int e = (tix - 1) % CH_EQ;
+            if (!wait_bounded(&eempty[e], (((tix - 1) / CH_EQ) & 1) ^ 1, s_abort, a.err, 5)) break;
+            int *ent = reinterpret_cast<int *>(equeue + e * L::EQ_ENTRY);
+            reinterpret_cast<float *>(ent + 4)[lane] = u;
+            if (lane == 0) {
+                ent[0] = q;
+                ent[1] = tile;
+                ent[2] = chunk;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                dcnt[bi] = 0;
+                mbar_arrive(&efull[e]);
+            }
+        }
+        // end of work: one warp queues the end marker for the epilogue warp
+        if (warp == 0 && !*s_abort) {
+            const int e = tix % CH_EQ;
+            if (wait_bounded(&eempty[e], ((tix / CH_EQ) & 1) ^ 1, s_abort, a.err, 5) && lane == 0) {
+                reinterpret_cast<int *>(equeue + e * L::EQ_ENTRY)[0] = -1;
+                mbar_arrive(&efull[e]);
+            }
+        }
+    } else {
+        // ---------------- epilogue: finished tiles, in unit order ----------------
+        for (uint32_t n = 0;; n++) {
+            const int e = n % CH_EQ;
+            if (!wait_bounded(&efull[e], (n / CH_EQ) & 1, s_abort, a.err, 6)) break;
+            const int *ent = reinterpret_cast<const int *>(equeue + e * L::EQ_ENTRY);
+            const int q = ent[0], tile = ent[1], chunk = ent[2];
+            if (q < 0) break;
+            const float u = reinterpret_cast<const float *>(ent + 4)[lane];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&eempty[e]);
+            const ChainProb &P = a.p[q];
+            const bool glu = P.act != ACT_NONE;
+            const int row = glu ? (lane & 15) : lane;
             bool store = true;
             float v = 0.f, v2 = 0.f;
-            if (P.S > 1) {
+            if (P.S > 1) {  // K-split: the last chunk of the tile to arrive sums them in chunk order
                 const int stile = P.split_base + tile;
                 __stcg(a.partial + ((int64_t)stile * P.S + chunk) * 32 + lane, u);
-                __threadfence();
+                if (!(a.debug & 32)) __threadfence();
                 __syncwarp();
                 int prev = 0;
                 if (lane == 0) {
                     prev = atomicAdd(a.tcnt + stile, 1);
-                    if (prev == P.S - 1) __threadfence();
+                    if (prev == P.S - 1 && !(a.debug & 32)) __threadfence();
                 }
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 store = prev == P.S - 1;
@@ -386,25 +451,23 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
             }
             if (store) {
                 if (glu) v = apply_act(P.act, v) * v2;
-                const int n = tile * (glu ? 16 : 32) + row;
-                if (n < P.N && (!glu || lane < 16)) {
+                const int nn = tile * (glu ? 16 : 32) + row;
+                if (nn < P.N && (!glu || lane < 16)) {
                     float bv = 0.f;
                     if (P.bias) {
-                        if (P.bias_dtype == F32) bv = reinterpret_cast<const float *>(P.bias)[n];
+                        if (P.bias_dtype == F32) bv = reinterpret_cast<const float *>(P.bias)[nn];
                         else if (P.bias_dtype == BF16)
-                            bv = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(P.bias)[n]);
-                        else bv = __half2float(reinterpret_cast<const __half *>(P.bias)[n]);
+                            bv = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(P.bias)[nn]);
+                        else bv = __half2float(reinterpret_cast<const __half *>(P.bias)[nn]);
                     }
-                    store_out(P.y, P.y_dtype, n, v + bv);
+                    store_out(P.y, P.y_dtype, nn, v + bv);
                 }
                 if (P.counted) {  // publish the finished tile to dependent problems
-                    __threadfence();
+                    if (!(a.debug & 32)) __threadfence();
                     __syncwarp();
                     if (lane == 0) atomicAdd(a.ctl + 2 + q, 1);
                 }
             }
-            __syncwarp();
-            if (lane == 0) dcnt[bi] = 0;
         }
     }
     // the last CTA out resets the work and completion counters
@@ -453,6 +516,38 @@ cudaError_t launch_chain_t(const ChainArgs &a, cudaStream_t st) {
 
 int chain_kb(int codec) { return codec == Q4_K ? ch_kb<Q4_K>() : ch_kb<Q6_K>(); }
 
+// host: tensor maps through the driver entry point
+typedef CUresult (*ChainEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+ChainEncodeFn chain_encode() {
+    static ChainEncodeFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<ChainEncodeFn>(p);
+    }
+    return fn;
+}
+
+// A weight matrix's wire rows as a 2-D tensor of uint64 elements [n][row
+// bytes / 8]; boxes of `box_rows` rows x one stage (plus the pitch pad).  Rows
+// past n and bytes past the row read as zeros.
+bool chain_map(CUtensorMap *m, const void *w, int64_t n, int64_t row_bytes, int64_t row_stride, int boxw,
+               int box_rows) {
+    ChainEncodeFn fn = chain_encode();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_stride};
+    const cuuint32_t box[2] = {(cuuint32_t)boxw, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 // Host plan: units and K chunks per problem, scratch sizes.  The fused kernel
@@ -460,8 +555,15 @@ int chain_kb(int codec) { return codec == Q4_K ? ch_kb<Q4_K>() : ch_kb<Q6_K>(); 
 bool chain_plan(const ChainProblemDesc *pd, int count, ChainPlan *out) {
     if (count < 1 || count > CH_MAX) return false;
     for (int q = 0; q < count; q++) {
-        if (pd[q].codec != Q4_K && pd[q].codec != Q6_K) return false;
-        if (pd[q].k > CH_KMAX) return false;  // the activation row must fit in shared memory
+        const ChainProblemDesc &d = pd[q];
+        if (d.codec != Q4_K && d.codec != Q6_K) return false;
+        if (d.k > CH_KMAX) return false;  // the activation row must fit in shared memory
+        // the weights must be describable as a TMA tensor: 16-byte aligned base
+        // and row stride, rows a whole number of 8-byte elements
+        const int64_t row_bytes = d.k / QK * (d.codec == Q4_K ? 144 : 210);
+        if (row_bytes % 8 || d.w_row_stride % 16 || (uintptr_t)d.w % 16 || (d.w2 && (uintptr_t)d.w2 % 16))
+            return false;
+        if (d.n > (1 << 30)) return false;
     }
     int chunk_stages = 2;
     if (const char *e = dev_env("KQ_CHAIN_CHUNK")) chunk_stages = std::max(1, atoi(e));  // development override
@@ -506,6 +608,7 @@ cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan 
     a.tcnt = tcnt;
     a.partial = partial;
     if (const char *e = dev_env("KQ_CHAIN_DEBUG")) a.debug = atoi(e);  // development switch
+    a.dbg = reinterpret_cast<unsigned long long *>(reinterpret_cast<char *>(partial) + (1 << 20));
     for (int q = 0; q < count; q++) {
         ChainProb &P = a.p[q];
         const ChainProblemDesc &d = pd[q];
@@ -530,6 +633,12 @@ cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan 
         P.chunk = pl.chunk[q];
         P.unit_base = pl.unit_base[q];
         P.split_base = pl.split_base[q];
+        const bool q4 = d.codec == Q4_K;
+        const int64_t row_bytes = d.k / QK * (q4 ? 144 : 210);
+        const int boxw = q4 ? ch_boxw<Q4_K>() : ch_boxw<Q6_K>(), rows = d.act != ACT_NONE ? 16 : 32;
+        if (!chain_map(&P.tmw, d.w, d.n, row_bytes, d.w_row_stride, boxw, rows)) return cudaErrorInvalidValue;
+        if (d.act != ACT_NONE && !chain_map(&P.tmw2, d.w2, d.n, row_bytes, d.w_row_stride, boxw, rows))
+            return cudaErrorInvalidValue;
     }
     return x_dtype == F16 ? launch_chain_t<Q4_K, Q6_K, true>(a, st) : launch_chain_t<Q4_K, Q6_K, false>(a, st);
 }

@@ -42,8 +42,9 @@ def layer(cgu, cd, d, f, nqkv, seed):
 
 @pytest.mark.parametrize("cgu,cd,d,f,nqkv", [
     ("q4_k", "q6_k", 4096, 14336, 6144),   # Llama-3-8B Q4_K_M layer
-    ("q4_k", "q6_k", 1024, 2816, 1536),    # ragged tiles (2816 = 176 x 16), a ragged K chunk
-    ("q6_k", "q6_k", 2048, 5632, 2560),    # Q6_K everywhere (Q6_K gate/up in the fused GLU)
+    ("q4_k", "q6_k", 1024, 4096, 1000),    # ragged last tile (1000 rows), K chunks of 2 stages
+    ("q6_k", "q6_k", 2048, 4096, 2560),    # Q6_K everywhere (Q6_K gate/up in the fused GLU)
+    ("q4_k", "q6_k", 1024, 2816, 1536),    # Q6_K rows of 2310 bytes: no TMA tensor, one launch per problem
     ("q5_k", "q6_k", 2048, 5632, 2560),    # no fused kernel for this mix: one launch per problem
     ("iq4_xs", "q6_k", 2048, 2816, 2560),
 ])
@@ -107,7 +108,7 @@ def test_chain_dependency_chain_and_bias(cuda):
 
 
 @pytest.mark.parametrize("codec", ["q4_k", "q6_k"])
-@pytest.mark.parametrize("n,k", [(32, 256), (100, 768), (4096, 16384)])
+@pytest.mark.parametrize("n,k", [(32, 256), (100, 2048), (4096, 16384), (33, 6144)])
 def test_chain_single_problem_edges(cuda, codec, n, k):
     """One-problem chains at the smallest K, a ragged tile and the largest K
     the fused kernel holds; f16 activations too."""
