@@ -287,19 +287,33 @@ def moe_check(torch, kq, x, idx, sc, y, wg, wu, wd, cgu, cd, base, toks):
     return _rel(y[toks], ref) if ref.abs().max() > 0 else 0.0
 
 
-def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
-    """Expert-parallel routed expert layer (configs 4 and 5): experts split by
-    id range over ranks, all ranks route the same tokens, partial outputs are
-    all-reduced.  Reported per token count: layer ms (max over ranks) and GB/s
-    of the expert bytes the routing touched (unique experts x expert bytes)."""
+def expert_stack(torch, codec, n, k, seed, e0, e1, dev):
+    """Experts [e0, e1) of a seeded synthetic stack, each expert from its own
+    seed, so every rank builds only the experts it owns and the values do not
+    depend on the world size."""
     from gmlx_b200 import synth
+    return torch.stack([torch.from_numpy(synth.random_weight(codec, n, k, seed=seed * 100_000 + e)).to(dev)
+                        for e in range(e0, e1)])
+
+
+def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
+    """Expert-parallel routed expert layer (configs 4 and 5), experts split by
+    id range over ranks.  Reported per token count: layer ms (max over ranks)
+    and GB/s of the expert bytes the routing touched (unique experts x expert
+    bytes).  Two ways to move tokens at N > 1:
+      allreduce -- every rank routes all T tokens, runs its experts' slots,
+                   partial outputs summed with one NCCL all-reduce (graph-timed);
+      alltoall  -- each rank routes its own T / N tokens and sends the routed
+                   rows to the experts' owners and back (NCCL all-to-all with
+                   host-side split sizes, so timed eagerly with CUDA events)."""
+    from gmlx_b200 import parallel as par
     out = {}
     for name, E, K, D, F, cgu, cd, ts in MOE_CONFIGS:
         el = E // world
         base = rank * el
-        wg = torch.from_numpy(synth.random_weight(cgu, F, D, seed=11, experts=E)[base:base + el]).to(dev)
-        wu = torch.from_numpy(synth.random_weight(cgu, F, D, seed=12, experts=E)[base:base + el]).to(dev)
-        wd = torch.from_numpy(synth.random_weight(cd, D, F, seed=13, experts=E)[base:base + el]).to(dev)
+        wg = expert_stack(torch, cgu, F, D, 11, base, base + el, dev)
+        wu = expert_stack(torch, cgu, F, D, 12, base, base + el, dev)
+        wd = expert_stack(torch, cd, D, F, 13, base, base + el, dev)
         router_w = torch.randn(E, D, device=dev, generator=torch.Generator(device=dev).manual_seed(5)) / D ** 0.5
         ebytes = (wg[0].numel() + wu[0].numel() + wd[0].numel())
         cell = {}
@@ -328,14 +342,69 @@ def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
             yl = kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, cgu, cd, base, E, out_dtype=torch.float32)
             toks = torch.randperm(t, generator=torch.Generator().manual_seed(t))[:8].tolist()
             err = moe_check(torch, kq, x, idx, sc, yl, wg, wu, wd, cgu, cd, base, toks)
-            cell[f"t{t}"] = {"ms": secs * 1e3, "unique_experts": uniq, "GB/s": gbs,
-                             "frac_hbm_per_gpu": gbs / world / hbm_peak,
-                             "TFLOP/s": 2.0 * t * K * 3 * D * F / secs / 1e12,
-                             "rel_err": err, "rel_err_tokens_checked": len(toks)}
+            c = {"ms": secs * 1e3, "unique_experts": uniq, "GB/s": gbs, "frac_hbm_per_gpu": gbs / world / hbm_peak,
+                 "TFLOP/s": 2.0 * t * K * 3 * D * F / secs / 1e12, "rel_err": err, "rel_err_tokens_checked": len(toks)}
+            if world > 1:
+                c = {"allreduce": c, "alltoall": moe_alltoall_cell(torch, kq, dist, par, x, logits, K, wg, wu, wd,
+                                                                   cgu, cd, E, world, rank, dev, uniq, ebytes,
+                                                                   hbm_peak)}
+                c["alltoall"]["rel_err_vs_allreduce"] = moe_a2a_vs_allreduce(torch, kq, dist, par, x, logits, K, wg,
+                                                                             wu, wd, cgu, cd, E, world, rank, base)
+            cell[f"t{t}"] = c
         out[name] = cell
         del wg, wu, wd
         torch.cuda.empty_cache()
     return out
+
+
+def _local_tokens(t, world, rank):
+    per, extra = divmod(t, world)
+    t0 = rank * per + min(rank, extra)
+    return t0, t0 + per + (1 if rank < extra else 0)
+
+
+def moe_alltoall_cell(torch, kq, dist, par, x, logits, K, wg, wu, wd, cgu, cd, E, world, rank, dev, uniq, ebytes,
+                      hbm_peak):
+    """Time the all-to-all expert-parallel layer: this rank's share of the T
+    tokens, routed, dispatched, computed by the experts' owners, combined."""
+    t0, t1 = _local_tokens(x.shape[0], world, rank)
+    xl, ll = x[t0:t1].contiguous(), logits[t0:t1].contiguous()
+
+    def layer():
+        return par.ep_moe_alltoall(xl, ll, K, wg, wu, wd, cgu, cd, E)
+    for _ in range(3):
+        layer()
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = 20
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        layer()
+    b.record()
+    torch.cuda.synchronize()
+    tt = torch.tensor([a.elapsed_time(b) / 1e3 / reps], device=dev, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    secs = float(tt.item())
+    gbs = uniq * ebytes / secs / 1e9
+    return {"ms": secs * 1e3, "GB/s": gbs, "frac_hbm_per_gpu": gbs / world / hbm_peak,
+            "tokens_per_rank": [_local_tokens(x.shape[0], world, r)[1] - _local_tokens(x.shape[0], world, r)[0]
+                                for r in range(world)]}
+
+
+def moe_a2a_vs_allreduce(torch, kq, dist, par, x, logits, K, wg, wu, wd, cgu, cd, E, world, rank, base):
+    """Max relative difference (over ranks) between the all-to-all layer's
+    rows and the all-reduce layer's rows for the same tokens (the latter is
+    checked against f32 dequantization per rank)."""
+    idx, sc = kq.moe_router_topk(logits, K, True, shared_gate=False)
+    yf = kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, cgu, cd, base, E, out_dtype=torch.float32)
+    dist.all_reduce(yf)
+    t0, t1 = _local_tokens(x.shape[0], world, rank)
+    ya = par.ep_moe_alltoall(x[t0:t1].contiguous(), logits[t0:t1].contiguous(), K, wg, wu, wd, cgu, cd, E)
+    e = torch.tensor([float((ya - yf[t0:t1]).abs().max() / yf.abs().max().clamp_min(1e-30)) if t1 > t0 else 0.0],
+                     device=x.device, dtype=torch.float64)
+    dist.all_reduce(e, op=dist.ReduceOp.MAX)
+    return float(e.item())
 
 
 _CPU_LAYER = None

@@ -134,6 +134,23 @@ __device__ __forceinline__ int prob_of(const ChainArgs &a, int unit) {
     return p;
 }
 
+// Bounded mbarrier wait that sleeps between checks (see mbar_try_wait_sleep):
+// gives up after ~2 s or when another warp gave up, records `code` once.
+__device__ __forceinline__ bool ch_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err, int code) {
+    uint64_t t0 = 0;
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+        if (*abort) return false;
+        const uint64_t now = globaltimer();
+        if (t0 == 0) t0 = now;
+        if (now - t0 > 2000000000ull) {
+            *abort = 1;
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
 // the stages [s0, s1) of a unit's tile
 __device__ __forceinline__ void unit_stages(const ChainProb &P, int unit, int &tile, int &chunk, int &s0, int &s1) {
     const int lu = unit - P.unit_base;
@@ -155,6 +172,7 @@ __device__ __forceinline__ bool consumers_sync(int *ctr, int target, volatile in
     for (uint32_t i = 1;; i++) {
         if (*reinterpret_cast<volatile int *>(ctr) >= target) break;
         if (*abort) return false;
+        __nanosleep(64);
         if ((i & 255) == 0) {
             const uint64_t now = globaltimer();
             if (t0 == 0) t0 = now;
@@ -214,7 +232,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         while (!*s_abort) {
             if (unit >= a.total_units) {  // end marker: a stage with a negative unit id
                 const int slot = it % NS;
-                if (wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1) && lane == 0) {
+                if (ch_wait(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1) && lane == 0) {
                     s_unit[slot] = -1;
                     mbar_arrive(&full[slot]);
                 }
@@ -231,7 +249,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
             const uint32_t stage_bytes = 32u * 8u * (uint32_t)boxw;
             for (int st = s0; st < s1; st++, it++) {
                 const int slot = it % NS;
-                if (!wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1)) break;
+                if (!ch_wait(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1)) break;
                 if ((a.debug & 64) && blockIdx.x == 0 && lane == 0 && it < 256) a.dbg[512 + it] = globaltimer();
                 if (lane == 0) {
                     s_unit[slot] = unit;
@@ -280,7 +298,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         int tix = 0, cur = -1, sync_target = 0;
         for (;;) {
             const int slot = it % NS;
-            if (!wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2)) break;
+            if (!ch_wait(&full[slot], (it / NS) & 1, s_abort, a.err, 2)) break;
             const int unit = s_unit[slot];
             if (unit < 0 || *s_abort) break;
             const int q = prob_of(a, unit);
@@ -296,6 +314,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     const uint64_t t0 = globaltimer();
                     while (ld_acquire(a.ctl + 2 + P.dep) < need) {
                         if (*s_abort) break;
+                        __nanosleep(128);
                         if (globaltimer() - t0 > 2000000000ull) {
                             *s_abort = 1;
                             atomicCAS(a.err, 0, 3);
@@ -332,7 +351,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
             bool ok = true;
             for (int st = s0; st < s1; st++, it++) {
                 const int sl = it % NS;
-                if (st > s0 && !wait_bounded(&full[sl], (it / NS) & 1, s_abort, a.err, 2)) {
+                if (st > s0 && !ch_wait(&full[sl], (it / NS) & 1, s_abort, a.err, 2)) {
                     ok = false;
                     break;
                 }
@@ -356,10 +375,11 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                 if (lane == 0) mbar_arrive(&empty[sl]);
             }
             if (!ok || *s_abort) break;
-            if (q6) {  // lanes tq = 0 / 1 hold the two 16-value sub-blocks of each MMA
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-            }
+            // the four lanes of a row (tq) each hold a quarter of its sub-blocks
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
             // tile store: each warp posts its 16 row partials (lanes tq == 0);
             // the last of the 16 warps to arrive sums the 8 block columns of
             // every row in column order (and K chunks in chunk order through
@@ -387,7 +407,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
 #pragma unroll
             for (int c = 0; c < 8; c++) u += rb[c * 32 + lane];
             const int e = (tix - 1) % CH_EQ;
-            if (!wait_bounded(&eempty[e], (((tix - 1) / CH_EQ) & 1) ^ 1, s_abort, a.err, 5)) break;
+            if (!ch_wait(&eempty[e], (((tix - 1) / CH_EQ) & 1) ^ 1, s_abort, a.err, 5)) break;
             int *ent = reinterpret_cast<int *>(equeue + e * L::EQ_ENTRY);
             reinterpret_cast<float *>(ent + 4)[lane] = u;
             if (lane == 0) {
@@ -404,7 +424,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         // end of work: one warp queues the end marker for the epilogue warp
         if (warp == 0 && !*s_abort) {
             const int e = tix % CH_EQ;
-            if (wait_bounded(&eempty[e], ((tix / CH_EQ) & 1) ^ 1, s_abort, a.err, 5) && lane == 0) {
+            if (ch_wait(&eempty[e], ((tix / CH_EQ) & 1) ^ 1, s_abort, a.err, 5) && lane == 0) {
                 reinterpret_cast<int *>(equeue + e * L::EQ_ENTRY)[0] = -1;
                 mbar_arrive(&efull[e]);
             }
@@ -413,7 +433,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         // ---------------- epilogue: finished tiles, in unit order ----------------
         for (uint32_t n = 0;; n++) {
             const int e = n % CH_EQ;
-            if (!wait_bounded(&efull[e], (n / CH_EQ) & 1, s_abort, a.err, 6)) break;
+            if (!ch_wait(&efull[e], (n / CH_EQ) & 1, s_abort, a.err, 6)) break;
             const int *ent = reinterpret_cast<const int *>(equeue + e * L::EQ_ENTRY);
             const int q = ent[0], tile = ent[1], chunk = ent[2];
             if (q < 0) break;

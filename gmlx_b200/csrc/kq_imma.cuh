@@ -99,93 +99,114 @@ __device__ __forceinline__ uint32_t lds32_a2(const uint8_t *p) {
     return __funnelshift_r(q[0], q[1], (uint32_t)(a & 3) * 8);
 }
 
+// m16n8k32 MMA accumulating into c.
+__device__ __forceinline__ void imma16832_acc(int c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Column placement: the four sub-blocks of a group go to B column pairs
+// (0,1), (2,3), (4,5), (6,7) -- lo bytes in the even column, hi bytes in the
+// odd one -- and the group's MMAs chain into ONE accumulator.  A column pair
+// is zero in every other MMA of the group, so thread (g, tq) ends with the
+// lo / hi sums of sub-block tq of the group for rows g and g + 8: each lane
+// applies the scales of one sub-block instead of all four lanes repeating
+// the same work.  The caller adds the four lanes of a row (tq) at the end.
+
 // Q4_K: 16 weight rows (thread rows g and g+8: blocks bg / bg8 in shared
-// memory, 16-byte aligned) x one 256-value block.  acc0 / acc1: the two
-// rows' f32 partials (valid in lanes with tq == 0).
+// memory, 16-byte aligned) x one 256-value block; acc0 / acc1 gather this
+// lane's share of rows g / g+8.
 __device__ __forceinline__ void imma_q4k(const uint8_t *bg, const uint8_t *bg8, const uint8_t *xb, int g, int tq,
                                          float &acc0, float &acc1) {
-    const uint4 h0 = *reinterpret_cast<const uint4 *>(bg), h1 = *reinterpret_cast<const uint4 *>(bg8);
-    uint32_t sc03a, sc47a, m03a, m47a, sc03b, sc47b, m03b, m47b;
-    q4k_unpack_scales(h0.y, h0.z, h0.w, sc03a, sc47a, m03a, m47a);
-    q4k_unpack_scales(h1.y, h1.z, h1.w, sc03b, sc47b, m03b, m47b);
-    const float d0 = half_bits_to_float(h0.x & 0xffffu), dm0 = half_bits_to_float(h0.x >> 16);
-    const float d1 = half_bits_to_float(h1.x & 0xffffu), dm1 = half_bits_to_float(h1.x >> 16);
     const float *xf = reinterpret_cast<const float *>(xb + 512);
-    const bool bcol = g < 2;
-    float s0 = 0.f, s1 = 0.f, m0 = 0.f, m1 = 0.f;
+    const int pair = g >> 1, gq = g & 1;  // this thread's B column pair and lo / hi byte column
+    int d[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // group 0: sub-blocks 0-3, group 1: 4-7
 #pragma unroll
     for (int c = 0; c < 4; c++) {
         const uint32_t wa = lds32(bg + 16 + 32 * c + 4 * tq), wb = lds32(bg + 32 + 32 * c + 4 * tq);
         const uint32_t va = lds32(bg8 + 16 + 32 * c + 4 * tq), vb = lds32(bg8 + 32 + 32 * c + 4 * tq);
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++) {  // sub-block 2c (low nibbles), 2c + 1 (high nibbles)
+        for (int hh = 0; hh < 2; hh++) {  // sub-block j = 2c (low nibbles) and 2c + 1 (high nibbles)
             const int j = 2 * c + hh;
             const uint32_t a[4] = {(wa >> (4 * hh)) & 0x0f0f0f0fu, (va >> (4 * hh)) & 0x0f0f0f0fu,
                                    (wb >> (4 * hh)) & 0x0f0f0f0fu, (vb >> (4 * hh)) & 0x0f0f0f0fu};
             uint2 bb = make_uint2(0u, 0u);
-            if (bcol) bb = *reinterpret_cast<const uint2 *>(xb + 64 * j + 32 * g + 8 * tq);
-            int dd[4];
-            imma16832(dd, a, bb.x, bb.y);
-            const float dxj = xf[j], sxj = xf[8 + j];
-            const uint32_t sw0 = j < 4 ? sc03a : sc47a, mw0 = j < 4 ? m03a : m47a;
-            const uint32_t sw1 = j < 4 ? sc03b : sc47b, mw1 = j < 4 ? m03b : m47b;
-            const int sh = 8 * (j & 3);
-            s0 = fmaf((float)((sw0 >> sh) & 63u) * dxj, (float)(dd[1] * 256 + dd[0]), s0);
-            s1 = fmaf((float)((sw1 >> sh) & 63u) * dxj, (float)(dd[3] * 256 + dd[2]), s1);
-            m0 = fmaf((float)((mw0 >> sh) & 63u), sxj, m0);
-            m1 = fmaf((float)((mw1 >> sh) & 63u), sxj, m1);
+            if (pair == (j & 3)) bb = *reinterpret_cast<const uint2 *>(xb + 64 * j + 32 * gq + 8 * tq);
+            imma16832_acc(d[j >> 2], a, bb.x, bb.y);
         }
     }
+    // this lane's sub-blocks: j = tq (group 0) and 4 + tq (group 1)
+    const uint4 h0 = *reinterpret_cast<const uint4 *>(bg), h1 = *reinterpret_cast<const uint4 *>(bg8);
+    uint32_t sc03a, sc47a, m03a, m47a, sc03b, sc47b, m03b, m47b;
+    q4k_unpack_scales(h0.y, h0.z, h0.w, sc03a, sc47a, m03a, m47a);
+    q4k_unpack_scales(h1.y, h1.z, h1.w, sc03b, sc47b, m03b, m47b);
+    const int sh = 8 * tq;
+    float s0 = 0.f, s1 = 0.f, m0 = 0.f, m1 = 0.f;
+#pragma unroll
+    for (int grp = 0; grp < 2; grp++) {
+        const int j = 4 * grp + tq;
+        const float dxj = xf[j], sxj = xf[8 + j];
+        const uint32_t sw0 = grp ? sc47a : sc03a, mw0 = grp ? m47a : m03a;
+        const uint32_t sw1 = grp ? sc47b : sc03b, mw1 = grp ? m47b : m03b;
+        s0 = fmaf((float)((sw0 >> sh) & 63u) * dxj, (float)(d[grp][1] * 256 + d[grp][0]), s0);
+        s1 = fmaf((float)((sw1 >> sh) & 63u) * dxj, (float)(d[grp][3] * 256 + d[grp][2]), s1);
+        m0 = fmaf((float)((mw0 >> sh) & 63u), sxj, m0);
+        m1 = fmaf((float)((mw1 >> sh) & 63u), sxj, m1);
+    }
+    const float d0 = half_bits_to_float(h0.x & 0xffffu), dm0 = half_bits_to_float(h0.x >> 16);
+    const float d1 = half_bits_to_float(h1.x & 0xffffu), dm1 = half_bits_to_float(h1.x >> 16);
     acc0 += fmaf(d0, s0, -dm0 * m0);
     acc1 += fmaf(d1, s1, -dm1 * m1);
 }
 
 // Q6_K: 16 weight rows x one 128-value half (hf) of a 256-value block
-// (blocks bg / bg8, 2-byte aligned).  Each k32 MMA covers two 16-value
-// sub-blocks: B columns 0/1 carry the first 16 values' lo/hi bytes, columns
-// 2/3 the second 16's, so lanes tq == 0 and tq == 1 hold one sub-block each
-// (the caller adds the two lanes).
+// (blocks bg / bg8, 2-byte aligned).  Each k32 MMA spans two 16-value
+// sub-blocks (one per column pair); two MMAs (quarters qd, qd + 1) chain into
+// one accumulator holding four sub-blocks, 16-value sub-block 8 hf + 2 qd0 + tq
+// in lane tq.
 __device__ __forceinline__ void imma_q6k(const uint8_t *bg, const uint8_t *bg8, int hf, const uint8_t *xb, int g,
                                          int tq, float &acc0, float &acc1) {
     const float *xf = reinterpret_cast<const float *>(xb + 512);
-    const float d0 = half_bits_to_float(lds32_a2(bg + 208) & 0xffffu);
-    const float d1 = half_bits_to_float(lds32_a2(bg8 + 208) & 0xffffu);
-    const int gq = g & 1;             // lo / hi byte column
-    const bool first = g < 2, second = g >= 2 && g < 4;
-    const int sel = tq & 1;           // this lane's sub-block of the pair (meaningful for tq < 2)
-    float s0 = 0.f, s1 = 0.f;
+    const int mm = g >> 2, part = g & 3;  // B columns 4mm .. 4mm+3: (first 16 lo, hi), (second 16 lo, hi)
     // quarter qd of the half: values l = 0..31 of ql[64 hf + 32 (qd & 1) + l] nibble (qd >> 1)
     // and qh[32 hf + l] bits 2 qd.  Thread tq: a0/a1 = l 4tq..4tq+3 (rows g, g+8), a2/a3 = l 16+4tq..
     const uint32_t ha0 = lds32_a2(bg + 128 + 32 * hf + 4 * tq), hb0 = lds32_a2(bg + 128 + 32 * hf + 16 + 4 * tq);
     const uint32_t ha1 = lds32_a2(bg8 + 128 + 32 * hf + 4 * tq), hb1 = lds32_a2(bg8 + 128 + 32 * hf + 16 + 4 * tq);
+    float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int qd = 0; qd < 4; qd++) {
-        const int qo = 64 * hf + 32 * (qd & 1), ns = 4 * (qd >> 1), hs = 2 * qd;
-        const uint32_t la0 = lds32_a2(bg + qo + 4 * tq), lb0 = lds32_a2(bg + qo + 16 + 4 * tq);
-        const uint32_t la1 = lds32_a2(bg8 + qo + 4 * tq), lb1 = lds32_a2(bg8 + qo + 16 + 4 * tq);
-        const uint32_t a[4] = {((la0 >> ns) & 0x0f0f0f0fu) | (((ha0 >> hs) & 0x03030303u) << 4),
-                               ((la1 >> ns) & 0x0f0f0f0fu) | (((ha1 >> hs) & 0x03030303u) << 4),
-                               ((lb0 >> ns) & 0x0f0f0f0fu) | (((hb0 >> hs) & 0x03030303u) << 4),
-                               ((lb1 >> ns) & 0x0f0f0f0fu) | (((hb1 >> hs) & 0x03030303u) << 4)};
-        // activation values 128 hf + 32 qd + (0..31) = 32-value sub-block j = 4 hf + qd
-        const int j = 4 * hf + qd;
-        uint32_t b0 = 0u, b1 = 0u;
-        if (first || second) {
-            const uint2 bb = *reinterpret_cast<const uint2 *>(xb + 64 * j + 32 * gq + 8 * tq);
-            b0 = first ? bb.x : 0u;
-            b1 = second ? bb.y : 0u;
+    for (int q2 = 0; q2 < 2; q2++) {  // quarters 2 q2, 2 q2 + 1
+        int d[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            const int qd = 2 * q2 + m;
+            const int qo = 64 * hf + 32 * (qd & 1), ns = 4 * (qd >> 1), hs = 2 * qd;
+            const uint32_t la0 = lds32_a2(bg + qo + 4 * tq), lb0 = lds32_a2(bg + qo + 16 + 4 * tq);
+            const uint32_t la1 = lds32_a2(bg8 + qo + 4 * tq), lb1 = lds32_a2(bg8 + qo + 16 + 4 * tq);
+            const uint32_t a[4] = {((la0 >> ns) & 0x0f0f0f0fu) | (((ha0 >> hs) & 0x03030303u) << 4),
+                                   ((la1 >> ns) & 0x0f0f0f0fu) | (((ha1 >> hs) & 0x03030303u) << 4),
+                                   ((lb0 >> ns) & 0x0f0f0f0fu) | (((hb0 >> hs) & 0x03030303u) << 4),
+                                   ((lb1 >> ns) & 0x0f0f0f0fu) | (((hb1 >> hs) & 0x03030303u) << 4)};
+            const int j = 4 * hf + qd;  // 32-value activation sub-block
+            uint32_t b0 = 0u, b1 = 0u;
+            if (mm == m) {
+                const uint2 bb = *reinterpret_cast<const uint2 *>(xb + 64 * j + 32 * (part & 1) + 8 * tq);
+                b0 = part < 2 ? bb.x : 0u;   // columns 4m, 4m+1: the first 16 values
+                b1 = part >= 2 ? bb.y : 0u;  // columns 4m+2, 4m+3: the second 16
+            }
+            imma16832_acc(d, a, b0, b1);
         }
-        int dd[4];
-        imma16832(dd, a, b0, b1);
-        // lane tq < 2: 16-value sub-block s = 2 j + tq (columns 2tq, 2tq+1)
-        const int s = 2 * j + sel;
+        // lane tq: 16-value sub-block s = 2 (4 hf + 2 q2) + tq, of 32-value sub-block j = 4 hf + 2 q2 + (tq >> 1)
+        const int j = 4 * hf + 2 * q2 + (tq >> 1), s = 2 * j + (tq & 1);
         const float sc0 = (float)(int8_t)bg[192 + s], sc1 = (float)(int8_t)bg8[192 + s];
         const float dxj = xf[j], sx16 = xf[16 + s];
-        s0 = fmaf(sc0, fmaf(dxj, (float)(dd[1] * 256 + dd[0]), -32.f * sx16), s0);
-        s1 = fmaf(sc1, fmaf(dxj, (float)(dd[3] * 256 + dd[2]), -32.f * sx16), s1);
+        s0 = fmaf(sc0, fmaf(dxj, (float)(d[1] * 256 + d[0]), -32.f * sx16), s0);
+        s1 = fmaf(sc1, fmaf(dxj, (float)(d[3] * 256 + d[2]), -32.f * sx16), s1);
     }
-    acc0 = fmaf(d0, s0, acc0);
-    acc1 = fmaf(d1, s1, acc1);
+    acc0 = fmaf(half_bits_to_float(lds32_a2(bg + 208) & 0xffffu), s0, acc0);
+    acc1 = fmaf(half_bits_to_float(lds32_a2(bg8 + 208) & 0xffffu), s1, acc1);
 }
 
 }  // namespace

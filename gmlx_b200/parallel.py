@@ -9,10 +9,18 @@ all-reduce of the partial sums after each row-parallel projection.  This is the
 shard_linear layout gmlx uses for hy_v3 (gmlx/hy_v3_model.py:396-443) with the
 all_sum of gmlx/hy_v3_model.py:259.
 
-MoE expert layer (e2): experts split by contiguous expert-id range; every rank
-routes the same tokens, runs the routed slots whose expert it owns, and the
-per-rank partial outputs are summed -- the sharding_group all_sum of
-gmlx/moe_experts.py:250-266.
+MoE expert layer (e2), two ways, experts split by contiguous expert-id range:
+ * route-all + all-reduce (ep_moe_forward): every rank routes the same tokens,
+   runs the routed slots whose expert it owns, and the per-rank partial
+   outputs are summed -- the sharding_group all_sum of
+   gmlx/moe_experts.py:250-266;
+ * all-to-all dispatch / combine (ep_moe_alltoall, ep_dispatch_combine): each
+   rank holds its own tokens, routes them, and sends every routed slot's
+   token row, expert id and score to the expert's owner (NCCL all-to-all with
+   the per-destination counts exchanged first); the owner runs its local
+   experts on the rows it received and sends the score-weighted rows back
+   (the inverse all-to-all), where they are added per token.  Only routed
+   rows cross NVLink, instead of a [T, hidden] f32 all-reduce.
 """
 from __future__ import annotations
 
@@ -166,6 +174,71 @@ def ep_moe_forward(x, logits, top_k, gate_w, up_w, down_w, codec_gu, codec_d, ex
     return y
 
 
+def ep_dispatch_combine(x: torch.Tensor, idx: torch.Tensor, scores: torch.Tensor, n_experts: int, expert_fn,
+                        group=None) -> torch.Tensor:
+    """All-to-all expert-parallel dispatch and combine for this rank's tokens.
+
+    x [t, D] (t may be 0), idx [t, k] global expert ids, scores [t, k] routing
+    weights.  Experts are owned in contiguous ranges of n_experts / world.
+    expert_fn(rows [R, D], local_expert [R] int32, score [R] f32) -> [R, D]
+    f32, the score-weighted expert outputs of the rows this rank received.
+    Returns y [t, D] f32 = sum_j scores[t, j] * expert_{idx[t, j]}(x[t]).
+    Steps: counts per destination rank (all-to-all), rows + (expert, score)
+    to the owners (all-to-all with those splits), local expert compute,
+    weighted rows back (the inverse all-to-all), per-token add."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split over {world} ranks")
+    el = n_experts // world
+    t, k = idx.shape
+    d = x.shape[1]
+    flat = idx.reshape(-1).long()
+    dest = flat // el
+    order = torch.argsort(dest, stable=True)                     # slots grouped by owner rank
+    tok = order // k                                             # token of each sent slot
+    send_counts = torch.bincount(dest, minlength=world).to(torch.int64)
+    xs = x.index_select(0, tok)
+    meta = torch.stack([(flat - dest * el)[order].to(torch.float32),  # local expert id (exact in f32)
+                        scores.reshape(-1)[order].float()], 1)
+    if world == 1:
+        yb = expert_fn(xs, meta[:, 0].to(torch.int32), meta[:, 1].contiguous())
+    else:
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()      # the split sizes the row exchange needs
+        r = sum(rc)
+        xr = x.new_empty(r, d)
+        dist.all_to_all_single(xr, xs.contiguous(), rc, sc, group=group)
+        mr = meta.new_empty(r, 2)
+        dist.all_to_all_single(mr, meta, rc, sc, group=group)
+        yr = expert_fn(xr, mr[:, 0].to(torch.int32), mr[:, 1].contiguous()).float().contiguous()
+        yb = yr.new_empty(t * k, d)
+        dist.all_to_all_single(yb, yr, sc, rc, group=group)
+    y = torch.zeros(t, d, dtype=torch.float32, device=x.device)
+    if t * k:
+        y.index_add_(0, tok, yb.float())
+    return y
+
+
+def ep_moe_alltoall(x, logits, top_k, gate_w, up_w, down_w, codec_gu, codec_d, n_experts, group=None,
+                    norm_topk_prob=True, act="silu"):
+    """Expert-parallel MoE layer with all-to-all dispatch / combine on the kq
+    ops: route this rank's tokens (kq.moe_router_topk), exchange the routed
+    rows, run the local experts (kq.moe_expert_layer_local over one slot per
+    received row, the score applied there), send the weighted rows back and
+    add them per token.  x [t, D] this rank's tokens; the stacks hold this
+    rank's n_experts / world experts."""
+    from . import kq
+    idx, scores = kq.moe_router_topk(logits, top_k, norm_topk_prob, shared_gate=False)
+
+    def local(rows, e_local, score):
+        if rows.shape[0] == 0:
+            return torch.zeros(0, rows.shape[1], dtype=torch.float32, device=rows.device)
+        return kq.moe_expert_layer_local(rows, e_local.reshape(-1, 1), score.reshape(-1, 1), gate_w, up_w, down_w,
+                                         codec_gu, codec_d, 0, gate_w.shape[0], act=act, out_dtype=torch.float32)
+    return ep_dispatch_combine(x, idx, scores, n_experts, local, group)
+
+
 def ep_partial_reference(x_f32: np.ndarray, idx: np.ndarray, scores: np.ndarray, expert_out, expert_base: int,
                          n_local: int) -> np.ndarray:
     """Host statement of one rank's share of the expert layer (tests): sum over
@@ -181,4 +254,4 @@ def ep_partial_reference(x_f32: np.ndarray, idx: np.ndarray, scores: np.ndarray,
 
 
 __all__ = ["block_split", "row_split", "shard_rows", "shard_k", "shard_llama_layer", "TPDecoderMLP", "PeerComm",
-           "expert_range", "ep_moe_forward", "ep_partial_reference", "QK"]
+           "expert_range", "ep_moe_forward", "ep_dispatch_combine", "ep_moe_alltoall", "ep_partial_reference", "QK"]

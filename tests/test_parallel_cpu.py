@@ -72,6 +72,46 @@ def _ep_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _a2a_worker(rank, world, port, q):
+    """All-to-all dispatch / combine: each rank routes ITS tokens (an uneven
+    split, one rank may have none), experts split by id range; the combined
+    rows equal the full layer on those tokens computed in one process."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        e, d, k, t = 6 * world, 256, 3, 7
+        w = synth.random_weight("q4_k", d, d, seed=13, experts=e)
+        deq = torch.from_numpy(O.dequantize(w, "q4_k").astype(np.float64))
+        x = torch.from_numpy(O.bf16_bits_to_f32(synth.random_activations(t, d, seed=14)).astype(np.float64))
+        idx, sc = O.router_topk(synth.random_logits(t, e, seed=15), k, True)
+        idx, sc = torch.from_numpy(idx), torch.from_numpy(sc)
+        # tokens of this rank: an uneven split of the t tokens (the last rank gets none when t < world * 2)
+        bounds = [0, 4, t, t, t][:world + 1] if world <= 4 else None
+        bounds[-1] = t
+        t0, t1 = bounds[rank], bounds[rank + 1]
+        el = e // world
+        seen = []
+
+        def expert_fn(rows, e_local, score):
+            seen.append(int(rows.shape[0]))
+            assert bool(((e_local >= 0) & (e_local < el)).all())
+            out = torch.zeros(rows.shape[0], d, dtype=torch.float64)
+            for r in range(rows.shape[0]):
+                out[r] = float(score[r]) * (deq[rank * el + int(e_local[r])] @ rows[r].double())
+            return out.float()
+        y = par.ep_dispatch_combine(x[t0:t1].float(), idx[t0:t1], sc[t0:t1], e, expert_fn)
+        ref = torch.zeros(t1 - t0, d, dtype=torch.float64)
+        for ti in range(t0, t1):
+            for j in range(k):
+                ref[ti - t0] += float(sc[ti, j]) * (deq[int(idx[ti, j])] @ x[ti].float().double())
+        err = float((y.double() - ref).abs().max() / max(float(ref.abs().max()), 1e-30)) if t1 > t0 else 0.0
+        q.put((f"a2a{rank}", err))
+        q.put((f"rows{rank}", seen[0]))
+        q.put((f"shape{rank}", tuple(y.shape) == (t1 - t0, d)))
+    finally:
+        dist.destroy_process_group()
+
+
 def _run(worker, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -128,3 +168,15 @@ def test_k_shards_of_every_codec_sum_to_the_full_product():
             k0 += kk
         assert k0 == 2048 and np.array_equal(np.concatenate(parts, 1), w), codec
         assert np.abs(acc - full).max() <= 1e-4 * np.abs(full).max(), codec
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_expert_parallel_all_to_all_gloo(world):
+    """Dispatch / combine over gloo ranks: every rank's combined rows match
+    the full layer on its own tokens, and all routed slots were computed
+    exactly once (received rows over the ranks = t * k)."""
+    out = _run(_a2a_worker, world)
+    for r in range(world):
+        assert out[f"a2a{r}"] < 1e-5, out
+        assert out[f"shape{r}"]
+    assert sum(out[f"rows{r}"] for r in range(world)) == 7 * 3

@@ -61,3 +61,58 @@ def test_fused_allreduce_two_ranks():
             for y in ys:
                 assert np.abs(y - full).max() / np.abs(full).max() <= 1e-4
                 assert np.array_equal(y.view(np.uint32), got[0][codec][1][0].view(np.uint32))  # same bits everywhere
+
+
+def _ep_rank_main(rank, port, out_q):
+    import torch.distributed as dist
+    from gmlx_b200 import kq, parallel as par, synth
+    from oracle import oracle as O
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, device_id=dev)
+    try:
+        e, d, f, k, t = 16, 1024, 512, 4, 9
+        wg = synth.random_weight("q4_k", f, d, seed=31, experts=e)
+        wu = synth.random_weight("q4_k", f, d, seed=32, experts=e)
+        wd = synth.random_weight("q6_k", d, f, seed=33, experts=e)
+        el = e // WORLD
+        loc = [torch.from_numpy(a[rank * el:(rank + 1) * el]).to(dev) for a in (wg, wu, wd)]
+        x = synth.random_activations(t, d, seed=34)
+        lg = synth.random_logits(t, e, seed=35)
+        t0, t1 = (0, 5) if rank == 0 else (5, t)  # uneven token split
+        xd = torch.from_numpy(x[t0:t1].view(np.int16).copy()).view(torch.bfloat16).to(dev)
+        y = par.ep_moe_alltoall(xd, torch.from_numpy(lg[t0:t1]).to(dev), k, *loc, "q4_k", "q6_k", e)
+        idx, sc = O.router_topk(lg, k, True)
+        ref = np.zeros((t1 - t0, d))
+        for ti in range(t0, t1):
+            for j in range(k):
+                ex = idx[ti, j]
+                g = O.matmul(x[ti:ti + 1], wg[ex], "q4_k")[0].astype(np.float64)
+                u = O.matmul(x[ti:ti + 1], wu[ex], "q4_k")[0].astype(np.float64)
+                hb = synth.f32_to_bf16_bits((g / (1 + np.exp(-g)) * u).astype(np.float32))
+                ref[ti - t0] += float(sc[ti, j]) * O.matmul(hb[None], wd[ex], "q6_k")[0]
+        torch.cuda.synchronize()
+        out_q.put((rank, (float(np.abs(y.cpu().numpy() - ref).max() / np.abs(ref).max()), kq.workspace_error())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_expert_parallel_all_to_all_two_ranks():
+    """All-to-all dispatch / combine over NCCL on 2 GPUs: each rank's combined
+    rows for its own tokens against the CPU oracle's full expert layer."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29800 + os.getpid() % 200
+    procs = [ctx.Process(target=_ep_rank_main, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(WORLD):
+        err, werr = got[r]
+        assert werr == 0 and err <= 1e-2, got
