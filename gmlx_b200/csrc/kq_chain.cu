@@ -52,7 +52,7 @@ constexpr int CH_PW = CH_CW;                  // producer warp
 constexpr int CH_THREADS = 32 * (CH_CW + 2);  // + producer + epilogue
 constexpr int CH_EQ = 8;                      // finished-tile queue entries
 constexpr int CH_KMAX = 16384;                // activation row length held quantized in shared memory
-constexpr int CH_XQB = CH_KMAX / QK * IMMA_XB;
+constexpr int CH_XQB = 101 * IMMA_XB;          // quantized activation rows of a chain (deduplicated)
 constexpr int CH_SMEM = 232448;               // one CTA per SM
 
 struct alignas(64) ChainProb {
@@ -67,13 +67,22 @@ struct alignas(64) ChainProb {
     int counted;       // a later problem depends on this one: count finished tiles
     int tiles, nst, S, chunk;
     int unit_base, split_base;
+    int xreg, xoff;    // activation region (rows shared by several problems share one) and its byte offset
+    int cmajor;        // units ordered chunk-major (a K-split problem reading another's output)
+    int rows_out;      // output rows per tile (32, or 16 for a fused gate/up)
 };
+
+// Completion is counted per slab of 4096 output rows (one K chunk of two
+// 8-block stages of a problem that reads this output), so a dependent chunk
+// waits only for the tiles that produce its inputs.
+constexpr int CH_SLAB = 4096;
+constexpr int CH_SLABS = 4;  // K <= 16384
 
 struct ChainArgs {
     ChainProb p[CH_MAX];
-    int count, total_units;
+    int count, total_units, nreg;
     int *err;
-    int *ctl;         // [0] work counter, [1] finished CTAs, [2 + p] finished tiles of problem p
+    int *ctl;         // [0] work counter, [1] finished CTAs, [16 + 4 p + s] finished tiles of slab s of problem p
     int *tcnt;        // K-split tile counters
     float *partial;   // K-split partial rows [split tile][S][32]
     int debug;        // development builds only: 1 = consumers skip the arithmetic, 2 = no weight copies,
@@ -100,7 +109,7 @@ template <int CA, int CB> struct ChainLayout {
     static constexpr int OFF_EBAR = 576;    // tile-queue mbarriers: efull[EQ], eempty[EQ]
     static constexpr int OFF_EQ = 768;      // tile queue: [EQ] x (q, tile, chunk, pad, 32 f32 row sums)
     static constexpr int EQ_ENTRY = 144;
-    static constexpr int OFF_XQ = OFF_EQ + CH_EQ * EQ_ENTRY;  // the current problem's quantized activations
+    static constexpr int OFF_XQ = OFF_EQ + CH_EQ * EQ_ENTRY;  // the chain's quantized activation rows
     static constexpr int RB_ONE = 8 * 32 * 4;  // [block column][tile row] partials
     static constexpr int OFF_RB = OFF_XQ + CH_XQB;
     static constexpr int NS_FIT = (CH_SMEM - OFF_RB - RB_ONE - 128) / (SLOT + RB_ONE);  // NS + 1 partial buffers
@@ -154,8 +163,13 @@ __device__ __forceinline__ bool ch_wait(uint64_t *bar, uint32_t parity, volatile
 // the stages [s0, s1) of a unit's tile
 __device__ __forceinline__ void unit_stages(const ChainProb &P, int unit, int &tile, int &chunk, int &s0, int &s1) {
     const int lu = unit - P.unit_base;
-    tile = lu / P.S;
-    chunk = lu - tile * P.S;
+    if (P.cmajor) {  // chunk 0 of every tile first: its inputs are the first to be ready
+        chunk = lu / P.tiles;
+        tile = lu - chunk * P.tiles;
+    } else {
+        tile = lu / P.S;
+        chunk = lu - tile * P.S;
+    }
     s0 = chunk * P.chunk;
     s1 = min(P.nst, s0 + P.chunk);
 }
@@ -228,7 +242,10 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         const uint64_t pol = policy_evict_first();
         uint32_t it = 0;
         bool dep_done = false;
-        int unit = blockIdx.x, next = -1;  // next: lane 0's claim of the following unit
+        // lane 0 claims units two ahead (pend: the next unit, nn: the one after),
+        // so a claim's round trip hides behind a whole unit of copies
+        int unit = blockIdx.x, pend = -1, nn = -1;
+        bool first_unit = true;
         while (!*s_abort) {
             if (unit >= a.total_units) {  // end marker: a stage with a negative unit id
                 const int slot = it % NS;
@@ -273,11 +290,14 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     asm volatile("griddepcontrol.wait;" ::: "memory");
                     dep_done = true;
                 }
-                if (st == s0 && lane == 0)  // claim the following unit now; its result is read
-                    next = (int)gridDim.x + atomicAdd(a.ctl, 1);  // after this unit's copies are out
+                if (st == s0 && lane == 0) {
+                    if (first_unit) pend = (int)gridDim.x + atomicAdd(a.ctl, 1);
+                    nn = (int)gridDim.x + atomicAdd(a.ctl, 1);
+                }
             }
-            unit = __shfl_sync(0xffffffffu, next, 0);
-            next = -1;
+            first_unit = false;
+            unit = __shfl_sync(0xffffffffu, pend, 0);
+            pend = nn;
         }
         if (*s_abort) {
             // gave up: wait (bounded) until the copies this CTA issued last have
@@ -294,86 +314,128 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         const int rh = warp & 1, bc = warp >> 1, g = lane >> 2, tq = lane & 3;
         const int r0 = 16 * rh + g, r1 = r0 + 8;
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        // quantize one activation row into its region; warps take blocks in turn
+        auto quantize_row = [&](const ChainProb &P, int bb0, int bb1) {
+            const int nb = (a.debug & 4) ? bb0 : bb1;
+            const uint16_t *xs = reinterpret_cast<const uint16_t *>(P.x);
+            uint8_t *dst = xq8 + P.xoff;
+            for (int b0 = bb0 + warp; b0 < nb; b0 += 4 * CH_CW) {
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int b = b0 + u * CH_CW;
+                    if (b < nb) v[u] = __ldcg(reinterpret_cast<const uint4 *>(xs + (int64_t)b * QK + 8 * lane));
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int b = b0 + u * CH_CW;
+                    if (b < nb) imma_quantize<F16>(v[u], dst + b * IMMA_XB);
+                }
+            }
+        };
+        // rows that depend on nothing (the chain's inputs) are quantized up front
+        unsigned ready = 0;
+        int sync_target = 0;
+        for (int q = 0; q < a.count; q++) {
+            const ChainProb &P = a.p[q];
+            const unsigned all = ((1u << CH_SLABS) - 1) << (P.xreg * CH_SLABS);
+            if (P.dep < 0 && (ready & all) != all) {
+                quantize_row(P, 0, P.K / QK);
+                ready |= all;
+            }
+        }
+        sync_target += CH_CW;
+        consumers_sync(s_sync, sync_target, s_abort, a.err);
         uint32_t it = 0;
-        int tix = 0, cur = -1, sync_target = 0;
+        int tix = 0;
+        const bool tr = (a.debug & 64) && blockIdx.x == 0;  // development: time accounting, every consumer warp
+        uint64_t t_wait = 0, t_comp = 0, t_store = 0, t_switch = 0, tm = tr ? globaltimer() : 0;
+        auto lap = [&](uint64_t &acc) {
+            if (tr) {
+                const uint64_t n = globaltimer();
+                acc += n - tm;
+                tm = n;
+            }
+        };
         for (;;) {
             const int slot = it % NS;
+            lap(t_store);
             if (!ch_wait(&full[slot], (it / NS) & 1, s_abort, a.err, 2)) break;
+            lap(t_wait);
             const int unit = s_unit[slot];
             if (unit < 0 || *s_abort) break;
             const int q = prob_of(a, unit);
             const ChainProb &P = a.p[q];
-            if (q != cur) {
-                // a new problem: wait until every warp is done with the previous
-                // one and (if it reads an earlier problem's output) until that
-                // problem's every tile is stored, then quantize its activation row
-                sync_target += CH_CW;
-                if (!(a.debug & 8) && !consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
-                if (P.dep >= 0 && warp == 0 && lane == 0 && !(a.debug & 16)) {
-                    const int need = a.p[P.dep].tiles;
-                    const uint64_t t0 = globaltimer();
-                    while (ld_acquire(a.ctl + 2 + P.dep) < need) {
-                        if (*s_abort) break;
-                        __nanosleep(128);
-                        if (globaltimer() - t0 > 2000000000ull) {
-                            *s_abort = 1;
-                            atomicCAS(a.err, 0, 3);
-                            break;
-                        }
-                    }
-                }
-                sync_target += CH_CW;
-                if (!(a.debug & 8) && !consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
-                const int nb = (a.debug & 4) ? 0 : P.K / QK;
-                const uint16_t *xs = reinterpret_cast<const uint16_t *>(P.x);
-                for (int b0 = warp; b0 < nb; b0 += 4 * CH_CW) {
-                    uint4 v[4];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int b = b0 + u * CH_CW;
-                        if (b < nb) v[u] = __ldcg(reinterpret_cast<const uint4 *>(xs + (int64_t)b * QK + 8 * lane));
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int b = b0 + u * CH_CW;
-                        if (b < nb) imma_quantize<F16>(v[u], xq8 + b * IMMA_XB);
-                    }
-                }
-                sync_target += CH_CW;
-                if (!(a.debug & 8) && !consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
-                cur = q;
-            }
             int tile, chunk, s0, s1;
             unit_stages(P, unit, tile, chunk, s0, s1);
+            if (P.dep >= 0) {
+                // this unit's inputs: activation blocks [8 s0, 8 s1) of a row that is
+                // problem P.dep's output.  Slabs of 16 blocks (4096 values) are made
+                // ready once per CTA: each warp waits for the slab's completion count,
+                // quantizes its blocks, then all consumers meet once.
+                const int sl0 = (8 * s0 * QK) / CH_SLAB, sl1 = min(CH_SLABS, (min(8 * s1 * QK, P.K) + CH_SLAB - 1) / CH_SLAB);
+                const ChainProb &D = a.p[P.dep];
+                bool fresh = false;
+                for (int sl = sl0; sl < sl1; sl++) {
+                    const unsigned bit = 1u << (P.xreg * CH_SLABS + sl);
+                    if (ready & bit) continue;
+                    fresh = true;
+                    if (lane == 0 && !(a.debug & 16)) {
+                        const int t0s = sl * CH_SLAB / D.rows_out;
+                        const int need = min(D.tiles, (sl + 1) * CH_SLAB / D.rows_out) - t0s;
+                        const uint64_t t0 = globaltimer();
+                        while (ld_acquire(a.ctl + 16 + 4 * P.dep + sl) < need) {
+                            if (*s_abort) break;
+                            __nanosleep(128);
+                            if (globaltimer() - t0 > 2000000000ull) {
+                                *s_abort = 1;
+                                atomicCAS(a.err, 0, 3);
+                                break;
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    quantize_row(P, sl * (CH_SLAB / QK), min(P.K / QK, (sl + 1) * (CH_SLAB / QK)));
+                    ready |= bit;
+                }
+                if (fresh) {
+                    sync_target += CH_CW;
+                    if (!(a.debug & 8) && !consumers_sync(s_sync, sync_target, s_abort, a.err)) break;
+                }
+                lap(t_switch);
+            }
             const int nb = P.K / QK;
             const bool q6 = P.codec == Q6_K;
             float acc0 = 0.f, acc1 = 0.f;
             bool ok = true;
             for (int st = s0; st < s1; st++, it++) {
                 const int sl = it % NS;
+                lap(t_comp);
                 if (st > s0 && !ch_wait(&full[sl], (it / NS) & 1, s_abort, a.err, 2)) {
                     ok = false;
                     break;
                 }
+                lap(t_wait);
                 if ((a.debug & 64) && blockIdx.x == 0 && warp == 0 && lane == 0 && it < 256)
-                    a.dbg[256 + it] = globaltimer();
+                    a.dbg[256 + it] = globaltimer();  // (warp 0: when it saw the stage full)
                 const uint8_t *stg = ring + sl * L::SLOT;
                 if (!*s_abort && !(a.debug & 1)) {
                     const int b = st * 8 + bc;  // 8 blocks per stage, one per block column
                     if (b < nb) {
                         if (!q6) {
                             imma_q4k(stg + r0 * ch_sp<Q4_K>() + bc * 144, stg + r1 * ch_sp<Q4_K>() + bc * 144,
-                                     xq8 + b * IMMA_XB, g, tq, acc0, acc1);
+                                     xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
                         } else {  // Q6_K: both 128-value halves of the block
                             const uint8_t *b0 = stg + r0 * ch_sp<Q6_K>() + bc * 210, *b1 = stg + r1 * ch_sp<Q6_K>() + bc * 210;
-                            imma_q6k(b0, b1, 0, xq8 + b * IMMA_XB, g, tq, acc0, acc1);
-                            imma_q6k(b0, b1, 1, xq8 + b * IMMA_XB, g, tq, acc0, acc1);
+                            imma_q6k(b0, b1, 0, xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
+                            imma_q6k(b0, b1, 1, xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
                         }
                     }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[sl]);
             }
+            lap(t_comp);
             if (!ok || *s_abort) break;
             // the four lanes of a row (tq) each hold a quarter of its sub-blocks
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
@@ -420,6 +482,13 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                 dcnt[bi] = 0;
                 mbar_arrive(&efull[e]);
             }
+        }
+        if (tr && lane == 0) {
+            a.dbg[768 + 8 * warp] = t_wait;
+            a.dbg[769 + 8 * warp] = t_comp;
+            a.dbg[770 + 8 * warp] = t_store;
+            a.dbg[771 + 8 * warp] = t_switch;
+            a.dbg[772 + 8 * warp] = (unsigned long long)tix;
         }
         // end of work: one warp queues the end marker for the epilogue warp
         if (warp == 0 && !*s_abort) {
@@ -482,10 +551,10 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     }
                     store_out(P.y, P.y_dtype, nn, v + bv);
                 }
-                if (P.counted) {  // publish the finished tile to dependent problems
+                if (P.counted) {  // publish the finished tile to dependent problems (its slab's count)
                     if (!(a.debug & 32)) __threadfence();
                     __syncwarp();
-                    if (lane == 0) atomicAdd(a.ctl + 2 + q, 1);
+                    if (lane == 0) atomicAdd(a.ctl + 16 + 4 * q + tile * P.rows_out / CH_SLAB, 1);
                 }
             }
         }
@@ -497,7 +566,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         if (atomicAdd(a.ctl + 1, 1) == (int)gridDim.x - 1) {
             __threadfence();
             a.ctl[0] = 0;
-            for (int q = 0; q < a.count; q++) a.ctl[2 + q] = 0;
+            for (int q = 0; q < 4 * CH_MAX; q++) a.ctl[16 + q] = 0;
             __threadfence();
             a.ctl[1] = 0;
         }
@@ -610,6 +679,28 @@ bool chain_plan(const ChainProblemDesc *pd, int count, ChainPlan *out) {
             partial_floats += tiles * S * 32;
         }
     }
+    // activation regions: one per distinct row (pointer, length), packed
+    int nreg = 0;
+    long xbytes = 0;
+    for (int q = 0; q < count; q++) {
+        int r = -1;
+        for (int p = 0; p < q && r < 0; p++)
+            if (pd[p].x == pd[q].x && pd[p].k == pd[q].k) r = pl.xreg[p];
+        if (r < 0) {
+            r = nreg++;
+            pl.xoff[q] = (int)xbytes;
+            xbytes += pd[q].k / QK * IMMA_XB;
+        } else {
+            for (int p = 0; p < q; p++)
+                if (pl.xreg[p] == r) {
+                    pl.xoff[q] = pl.xoff[p];
+                    break;
+                }
+        }
+        pl.xreg[q] = r;
+    }
+    if (xbytes > CH_XQB) return false;  // the chain's activation rows must fit in shared memory
+    pl.nreg = nreg;
     if (units > 0x3fffffffL) return false;
     pl.total_units = (int)units;
     pl.split_tiles = split_tiles;
@@ -622,6 +713,7 @@ cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan 
                          int *tcnt, float *partial, cudaStream_t st) {
     ChainArgs a{};
     a.count = count;
+    a.nreg = pl.nreg;
     a.total_units = pl.total_units;
     a.err = err;
     a.ctl = ctl;
@@ -647,12 +739,16 @@ cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan 
         P.dep = d.dep;
         P.counted = 0;
         for (int r = q + 1; r < count; r++) P.counted |= pd[r].dep == q;
+        P.rows_out = d.act != ACT_NONE ? 16 : 32;
+        P.cmajor = d.dep >= 0 && P.S > 1;
         P.tiles = pl.tiles[q];
         P.nst = pl.nst[q];
         P.S = pl.S[q];
         P.chunk = pl.chunk[q];
         P.unit_base = pl.unit_base[q];
         P.split_base = pl.split_base[q];
+        P.xreg = pl.xreg[q];
+        P.xoff = pl.xoff[q];
         const bool q4 = d.codec == Q4_K;
         const int64_t row_bytes = d.k / QK * (q4 ? 144 : 210);
         const int boxw = q4 ? ch_boxw<Q4_K>() : ch_boxw<Q6_K>(), rows = d.act != ACT_NONE ? 16 : 32;

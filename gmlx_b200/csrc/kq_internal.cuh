@@ -82,7 +82,7 @@ struct ChainProblemDesc {
 };
 struct ChainPlan {
     int pair, total_units;
-    int tiles[8], nst[8], S[8], chunk[8], unit_base[8], split_base[8];
+    int tiles[8], nst[8], S[8], chunk[8], unit_base[8], split_base[8], xreg[8], xoff[8], nreg;
     long split_tiles, partial_floats;
 };
 // false when no fused chain kernel takes these problems (codec mix, sizes)
