@@ -68,10 +68,13 @@ bool act_dtype_ok(int d) { return d == KQ_F16 || d == KQ_BF16; }
 bool out_dtype_ok(int d) { return d == KQ_F32 || d == KQ_F16 || d == KQ_BF16; }
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-int check_weights(int codec, const void *w, int64_t k, int64_t row_stride, const char *what) {
+// ragged: K may end in a partial 256-weight group (a whole number of the
+// codec's 32- or 64-weight blocks); only the entry points that handle it pass true
+int check_weights(int codec, const void *w, int64_t k, int64_t row_stride, const char *what, bool ragged = false) {
     if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "%s: unsupported codec %d (have q8_0=8, q4_k=12, q5_k=13, q6_k=14, iq2_xxs=16, iq3_xxs=18, iq4_xs=23, q4_0=2, iq4_nl=20, q2_k=10, q3_k=11, q4_1=3, q5_0=6, q5_1=7, tq2_0=35, mxfp4=39, iq2_xs=17, iq2_s=22, iq3_s=21, iq1_s=19, iq1_m=29, tq1_0=34, nvfp4=40)", what, codec);
-    if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a positive multiple of %d", what, (long long)k, QK);
-    const int64_t rb = k / QK * block_bytes(codec);
+    const int gran = ragged ? sub_block_weights(codec) : QK;
+    if (k <= 0 || k % gran) return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a positive multiple of %d", what, (long long)k, gran);
+    const int64_t rb = wire_row_bytes(codec, k);
     if (row_stride < rb) return fail(KQ_ERR_SHAPE, "%s: row stride %lld < row bytes %lld", what, (long long)row_stride, (long long)rb);
     const int64_t need = (codec == KQ_Q4_K || codec == KQ_Q5_K) ? 16 : codec == KQ_IQ4_XS ? 8 : codec == KQ_Q2_K ? 4 : 2;
     if (((uintptr_t)w | (uintptr_t)row_stride) % need)
@@ -156,7 +159,7 @@ bool use_gemm(int64_t m, int codec = 0) {
 // workspace bytes of the path run_dense takes for these activations (the
 // GEMM when the batch is prefill-sized and the GEMM takes this layout)
 size_t dense_ws_x(int codec, int64_t m, int64_t n, int64_t k, int act, int x_dtype, int64_t xs) {
-    if (use_gemm(m, codec) && gemm_supported(codec, m, n, k, x_dtype, xs))
+    if ((use_gemm(m, codec) || k % QK) && gemm_supported(codec, m, n, k, x_dtype, xs))
         return plan(0, gemm_scratch_bytes(codec, m, n, k, act != ACT_NONE), 0, 0).total;
     GemvArgs a = dense_args(codec, nullptr, x_dtype, m, k, xs, nullptr, nullptr, n, 0, nullptr, KQ_BF16, n, act);
     size_t pb, cb;
@@ -173,14 +176,20 @@ int run_dense(int codec, const void *x, int x_dtype, int64_t m, int64_t k, int64
               void *stream, const char *what, const void *bias = nullptr, int bias_dtype = 0) {
     if (bias && (w2 || !out_dtype_ok(bias_dtype))) return fail(KQ_ERR_DTYPE, "%s: bad bias", what);
     int rc;
-    if ((rc = check_weights(codec, w, k, wstride, what))) return rc;
-    if (w2 && (rc = check_weights(codec, w2, k, wstride, what))) return rc;
+    if ((rc = check_weights(codec, w, k, wstride, what, true))) return rc;
+    if (w2 && (rc = check_weights(codec, w2, k, wstride, what, true))) return rc;
     if ((rc = check_x(x, x_dtype, xs, what))) return rc;
+    // K ending in a partial 256-weight group (32/64-weight codecs): every batch
+    // size runs on the GEMM over a dequantized copy, which takes K % 64 == 0
+    const bool ragged = k % QK != 0;
+    if (ragged && !gemm_supported(codec, m > 0 ? m : 1, n, k, x_dtype, xs))
+        return fail(KQ_ERR_SHAPE, "%s: K=%lld is not a multiple of 256; a partial last group needs K %% 64 == 0", what,
+                    (long long)k);
     if (!out_dtype_ok(y_dtype)) return fail(KQ_ERR_DTYPE, "%s: bad output dtype %d", what, y_dtype);
     if (m < 0 || n <= 0 || xs < k || ys < n) return fail(KQ_ERR_SHAPE, "%s: bad sizes m=%lld n=%lld", what, (long long)m, (long long)n);
     if (m == 0) return KQ_OK;
     if (n > 0x7fffffff || k > 0x7fffffff) return fail(KQ_ERR_SHAPE, "%s: n/k too large", what);
-    if (use_gemm(m, codec) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
+    if ((use_gemm(m, codec) || ragged) && gemm_supported(codec, m, n, k, x_dtype, xs)) {
         const WsPlan p = plan(0, gemm_scratch_bytes(codec, m, n, k, act != ACT_NONE), 0, 0);
         if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255))
             return fail(KQ_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-aligned) required, got %zu", what, p.total, ws_bytes);
@@ -656,18 +665,21 @@ int kq_dequantize(int codec, const void *w, int64_t rows, int64_t k, int64_t w_r
                   void *stream) {
     g_msg[0] = 0;
     if (!codec_ok(codec)) return fail(KQ_ERR_CODEC, "dequantize: unsupported codec %d", codec);
-    if (k <= 0 || k % QK) return fail(KQ_ERR_SHAPE, "dequantize: K=%lld is not a positive multiple of 256", (long long)k);
+    if (k <= 0 || k % sub_block_weights(codec))
+        return fail(KQ_ERR_SHAPE, "dequantize: K=%lld is not a positive multiple of %d", (long long)k,
+                    sub_block_weights(codec));
     if (rows < 0) return fail(KQ_ERR_SHAPE, "dequantize: rows < 0");
     if (!out_dtype_ok(out_dtype)) return fail(KQ_ERR_DTYPE, "dequantize: bad output dtype %d", out_dtype);
     if ((uintptr_t)out % 16) return fail(KQ_ERR_ALIGN, "dequantize: output must be 16-byte aligned");
-    if (w_row_stride < k / QK * block_bytes(codec)) return fail(KQ_ERR_SHAPE, "dequantize: row stride too small");
+    if (w_row_stride < wire_row_bytes(codec, k)) return fail(KQ_ERR_SHAPE, "dequantize: row stride too small");
+
     return cuda_status(launch_dequantize(codec, (const uint8_t *)w, rows, k, w_row_stride, out, out_dtype,
                                          (cudaStream_t)stream),
                        "dequantize");
 }
 
 size_t kq_quantized_matmul_workspace_size(int codec, int64_t m, int64_t n, int64_t k) {
-    if (!codec_ok(codec) || k <= 0 || k % QK || n <= 0 || m <= 0) return 256;
+    if (!codec_ok(codec) || k <= 0 || k % sub_block_weights(codec) || n <= 0 || m <= 0) return 256;
     return dense_ws(codec, m, n, k, ACT_NONE);
 }
 
@@ -749,7 +761,7 @@ int kq_ipc_open(const void *handle64, void **ptr) {
 int kq_ipc_close(void *ptr) { return cuda_status(cudaIpcCloseMemHandle(ptr), "ipc_close"); }
 
 size_t kq_quantized_glu_workspace_size(int codec, int64_t m, int64_t n, int64_t k) {
-    if (!codec_ok(codec) || k <= 0 || k % QK || n <= 0 || m <= 0) return 256;
+    if (!codec_ok(codec) || k <= 0 || k % sub_block_weights(codec) || n <= 0 || m <= 0) return 256;
     return dense_ws(codec, m, n, k, ACT_SILU);
 }
 

@@ -47,7 +47,11 @@ namespace kq {
 namespace {
 
 constexpr int CH_MAX = KQ_CHAIN_MAX;
-constexpr int CH_CW = 16;                     // consumer warps: 2 row halves x 8 block columns
+#ifndef KQ_CHAIN_CW
+#define KQ_CHAIN_CW 8
+#endif
+constexpr int CH_CW = KQ_CHAIN_CW;            // consumer warps: 2 row halves x CH_NBC block columns
+constexpr int CH_NBC = CH_CW / 2;             // block columns; each takes 8 / CH_NBC of a stage's 8 blocks
 constexpr int CH_PW = CH_CW;                  // producer warp
 constexpr int CH_THREADS = 32 * (CH_CW + 2);  // + producer + epilogue
 constexpr int CH_EQ = 8;                      // finished-tile queue entries
@@ -420,15 +424,19 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     a.dbg[256 + it] = globaltimer();  // (warp 0: when it saw the stage full)
                 const uint8_t *stg = ring + sl * L::SLOT;
                 if (!*s_abort && !(a.debug & 1)) {
-                    const int b = st * 8 + bc;  // 8 blocks per stage, one per block column
-                    if (b < nb) {
-                        if (!q6) {
-                            imma_q4k(stg + r0 * ch_sp<Q4_K>() + bc * 144, stg + r1 * ch_sp<Q4_K>() + bc * 144,
-                                     xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
-                        } else {  // Q6_K: both 128-value halves of the block
-                            const uint8_t *b0 = stg + r0 * ch_sp<Q6_K>() + bc * 210, *b1 = stg + r1 * ch_sp<Q6_K>() + bc * 210;
-                            imma_q6k(b0, b1, 0, xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
-                            imma_q6k(b0, b1, 1, xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
+#pragma unroll
+                    for (int i = 0; i < 8 / CH_NBC; i++) {  // independent blocks: their latencies overlap
+                        const int bi = bc + CH_NBC * i, b = st * 8 + bi;
+                        if (b < nb) {
+                            if (!q6) {
+                                imma_q4k(stg + r0 * ch_sp<Q4_K>() + bi * 144, stg + r1 * ch_sp<Q4_K>() + bi * 144,
+                                         xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
+                            } else {  // Q6_K: both 128-value halves of the block
+                                const uint8_t *b0 = stg + r0 * ch_sp<Q6_K>() + bi * 210,
+                                              *b1 = stg + r1 * ch_sp<Q6_K>() + bi * 210;
+                                imma_q6k(b0, b1, 0, xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
+                                imma_q6k(b0, b1, 1, xq8 + P.xoff + b * IMMA_XB, g, tq, acc0, acc1);
+                            }
                         }
                     }
                 }
@@ -467,7 +475,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
             __threadfence_block();
             float u = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; c++) u += rb[c * 32 + lane];
+            for (int c = 0; c < CH_NBC; c++) u += rb[c * 32 + lane];
             const int e = (tix - 1) % CH_EQ;
             if (!ch_wait(&eempty[e], (((tix - 1) / CH_EQ) & 1) ^ 1, s_abort, a.err, 5)) break;
             int *ent = reinterpret_cast<int *>(equeue + e * L::EQ_ENTRY);

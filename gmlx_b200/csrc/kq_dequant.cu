@@ -229,14 +229,19 @@ __device__ __forceinline__ void deq8(const uint8_t *b, int lane, float o[8]) {
 
 template <int C, int OUT>
 __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict__ w, int64_t rows, int64_t nb,
-                                                      int64_t row_stride, void *__restrict__ out) {
+                                                      int64_t row_stride, void *__restrict__ out, int64_t out_k,
+                                                      int tail) {
+    // nb groups per row, then (tail > 0) a partial last group of `tail`
+    // weights: its lanes past the tail read and write nothing
     const int lane = threadIdx.x & 31;
+    const int64_t gpr = nb + (tail > 0);
     const int64_t blk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (blk >= rows * nb) return;
-    const int64_t r = blk / nb, b = blk - r * nb;
+    if (blk >= rows * gpr) return;
+    const int64_t r = blk / gpr, b = blk - r * gpr;
+    if (b == nb && 8 * lane >= tail) return;
     float o[8];
     deq8<C>(w + r * row_stride + b * Fmt<C>::bpb, lane, o);
-    const int64_t e0 = r * nb * QK + b * QK + 8 * lane;
+    const int64_t e0 = r * out_k + b * QK + 8 * lane;
     if constexpr (OUT == F32) {
         float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + e0);
         p[0] = make_float4(o[0], o[1], o[2], o[3]);
@@ -366,9 +371,9 @@ __global__ void __launch_bounds__(256) dequant_bulk_kernel(const uint8_t *__rest
 
 template <int C>
 static cudaError_t launch_deq(const uint8_t *w, int64_t rows, int64_t nb, int64_t stride, void *out, int dtype,
-                              cudaStream_t st) {
+                              cudaStream_t st, int64_t out_k, int tail) {
     const int64_t nblk = rows * nb;
-    if (stride == nb * Fmt<C>::bpb && nblk >= 8 * DQ_CHUNK) {
+    if (tail == 0 && stride == nb * Fmt<C>::bpb && nblk >= 8 * DQ_CHUNK) {
         constexpr int smem = 128 + 2 * (DQ_CHUNK * Fmt<C>::bpb + 16);
         const int nsm = num_sms();
         const int64_t nchunks = (nblk + DQ_CHUNK - 1) / DQ_CHUNK;
@@ -389,41 +394,43 @@ static cudaError_t launch_deq(const uint8_t *w, int64_t rows, int64_t nb, int64_
         }
         return cudaGetLastError();
     }
-    const unsigned grid = (unsigned)((nblk + 7) / 8);
-    if (dtype == F32) dequant_kernel<C, F32><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);
-    else if (dtype == BF16) dequant_kernel<C, BF16><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);
-    else dequant_kernel<C, F16><<<grid, 256, 0, st>>>(w, rows, nb, stride, out);
+    const unsigned grid = (unsigned)((rows * (nb + (tail > 0)) + 7) / 8);
+    if (dtype == F32) dequant_kernel<C, F32><<<grid, 256, 0, st>>>(w, rows, nb, stride, out, out_k, tail);
+    else if (dtype == BF16) dequant_kernel<C, BF16><<<grid, 256, 0, st>>>(w, rows, nb, stride, out, out_k, tail);
+    else dequant_kernel<C, F16><<<grid, 256, 0, st>>>(w, rows, nb, stride, out, out_k, tail);
     return cudaGetLastError();
 }
 
 cudaError_t launch_dequantize(int codec, const uint8_t *w, int64_t rows, int64_t k, int64_t row_stride, void *out,
                               int dtype, cudaStream_t st) {
+    // whole 256-weight groups, then a partial last group (32/64-weight codecs)
     const int64_t nb = k / QK;
-    if (rows * nb == 0) return cudaSuccess;
+    const int tail = (int)(k % QK);
+    if (rows == 0 || k == 0) return cudaSuccess;
     switch (codec) {
-    case Q4_K: return launch_deq<Q4_K>(w, rows, nb, row_stride, out, dtype, st);
-    case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st);
-    case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st);
-    case Q4_0: return launch_deq<Q4_0>(w, rows, nb, row_stride, out, dtype, st);
-    case Q4_1: return launch_deq<Q4_1>(w, rows, nb, row_stride, out, dtype, st);
-    case MXFP4: return launch_deq<MXFP4>(w, rows, nb, row_stride, out, dtype, st);
-    case TQ2_0: return launch_deq<TQ2_0>(w, rows, nb, row_stride, out, dtype, st);
-    case TQ1_0: return launch_deq<TQ1_0>(w, rows, nb, row_stride, out, dtype, st);
-    case NVFP4: return launch_deq<NVFP4>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ2_XS: return launch_deq<IQ2_XS>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ2_S: return launch_deq<IQ2_S>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ3_S: return launch_deq<IQ3_S>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ1_S: return launch_deq<IQ1_S>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ1_M: return launch_deq<IQ1_M>(w, rows, nb, row_stride, out, dtype, st);
-    case Q5_0: return launch_deq<Q5_0>(w, rows, nb, row_stride, out, dtype, st);
-    case Q5_1: return launch_deq<Q5_1>(w, rows, nb, row_stride, out, dtype, st);
-    case Q2_K: return launch_deq<Q2_K>(w, rows, nb, row_stride, out, dtype, st);
-    case Q3_K: return launch_deq<Q3_K>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ4_NL: return launch_deq<IQ4_NL>(w, rows, nb, row_stride, out, dtype, st);
-    case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ3_XXS: return launch_deq<IQ3_XXS>(w, rows, nb, row_stride, out, dtype, st);
-    case IQ4_XS: return launch_deq<IQ4_XS>(w, rows, nb, row_stride, out, dtype, st);
-    default: return launch_deq<IQ2_XXS>(w, rows, nb, row_stride, out, dtype, st);
+    case Q4_K: return launch_deq<Q4_K>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q5_K: return launch_deq<Q5_K>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q8_0: return launch_deq<Q8_0>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q4_0: return launch_deq<Q4_0>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q4_1: return launch_deq<Q4_1>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case MXFP4: return launch_deq<MXFP4>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case TQ2_0: return launch_deq<TQ2_0>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case TQ1_0: return launch_deq<TQ1_0>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case NVFP4: return launch_deq<NVFP4>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ2_XS: return launch_deq<IQ2_XS>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ2_S: return launch_deq<IQ2_S>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ3_S: return launch_deq<IQ3_S>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ1_S: return launch_deq<IQ1_S>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ1_M: return launch_deq<IQ1_M>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q5_0: return launch_deq<Q5_0>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q5_1: return launch_deq<Q5_1>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q2_K: return launch_deq<Q2_K>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q3_K: return launch_deq<Q3_K>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ4_NL: return launch_deq<IQ4_NL>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case Q6_K: return launch_deq<Q6_K>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ3_XXS: return launch_deq<IQ3_XXS>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    case IQ4_XS: return launch_deq<IQ4_XS>(w, rows, nb, row_stride, out, dtype, st, k, tail);
+    default: return launch_deq<IQ2_XXS>(w, rows, nb, row_stride, out, dtype, st, k, tail);
     }
 }
 

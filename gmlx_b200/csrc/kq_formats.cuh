@@ -127,6 +127,24 @@ template <> struct Fmt<IQ2_XXS> { static constexpr int bpb = 66; static constexp
 template <> struct Fmt<IQ3_XXS> { static constexpr int bpb = 98; static constexpr int sub = 32; };
 template <> struct Fmt<IQ4_XS> { static constexpr int bpb = 136; static constexpr int sub = 32; };
 
+// Weights per ggml block of the codecs that are handled in 256-weight groups
+// of smaller blocks (a row may end in a partial group: K need only be a whole
+// number of these blocks); 256 for every super-block codec.
+__host__ __device__ inline int sub_block_weights(int codec) {
+    switch (codec) {
+    case Q8_0: case Q4_0: case Q4_1: case Q5_0: case Q5_1: case IQ4_NL: case MXFP4: return 32;
+    case NVFP4: return 64;
+    default: return 256;
+    }
+}
+
+__host__ __device__ inline int block_bytes(int codec);
+// Wire bytes of a row of k weights.
+__host__ __device__ inline int64_t wire_row_bytes(int codec, int64_t k) {
+    const int sw = sub_block_weights(codec);
+    return k / sw * (block_bytes(codec) / (256 / sw));
+}
+
 __host__ __device__ inline int block_bytes(int codec) {
     return codec == Q4_K ? 144 : codec == Q5_K ? 176 : codec == Q6_K ? 210 : codec == IQ2_XXS ? 66
          : codec == Q8_0 ? 272 : codec == IQ3_XXS ? 98 : codec == IQ4_XS ? 136 : (codec == Q4_0 || codec == IQ4_NL) ? 144

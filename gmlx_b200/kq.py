@@ -34,7 +34,7 @@ import ctypes as _ct
 import torch
 
 from . import _lib
-from .synth import BLOCK_BYTES, CODECS, QK, codec_id
+from .synth import BLOCK_BYTES, CODECS, QK, SUB_BLOCK, codec_id
 
 __all__ = [
     "codecs", "all_codecs", "codec_has_matmul", "codec_has_moe_glu", "block_bytes", "dequantize", "quantized_matmul", "quantized_glu", "gather_qmm",
@@ -122,9 +122,12 @@ def _wire_k(w: torch.Tensor, c: int) -> int:
     bpb = BLOCK_BYTES[c]
     if w.dtype != torch.uint8:
         raise ValueError(f"wire weights must be uint8, got {w.dtype}")
-    if w.shape[-1] % bpb:
-        raise ValueError(f"wire row of {w.shape[-1]} bytes is not a whole number of {bpb}-byte blocks")
-    return w.shape[-1] // bpb * QK
+    if w.shape[-1] % bpb == 0:
+        return w.shape[-1] // bpb * QK
+    if c in SUB_BLOCK and w.shape[-1] % SUB_BLOCK[c][1] == 0:  # a partial last 256-weight group
+        bw, bb = SUB_BLOCK[c]
+        return w.shape[-1] // bb * bw
+    raise ValueError(f"wire row of {w.shape[-1]} bytes is not a whole number of {bpb}-byte blocks")
 
 
 def _rows2d(w: torch.Tensor) -> tuple[torch.Tensor, int]:

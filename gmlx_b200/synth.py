@@ -55,6 +55,10 @@ BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, Q8_0: 272, IQ3_XXS:
                IQ1_S: 50, IQ1_M: 56, TQ1_0: 54, NVFP4: 144}
 QK = 256
 D_LO, D_HI = 1e-4, 2e-3
+# codecs handled in 256-weight groups of smaller ggml blocks: (weights, bytes)
+# per block; a row may end in a partial group
+SUB_BLOCK = {Q8_0: (32, 34), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24), IQ4_NL: (32, 18),
+             MXFP4: (32, 17), NVFP4: (64, 36)}
 
 
 def codec_id(codec) -> int:
@@ -133,6 +137,17 @@ def random_weight(codec, n: int, k: int, seed: int = 0, experts: int | None = No
     b = random_blocks(c, e * n * nb, seed)
     shape = (n, nb * BLOCK_BYTES[c]) if experts is None else (e, n, nb * BLOCK_BYTES[c])
     return b.reshape(shape)
+
+
+def random_weight_ragged(codec, n: int, k: int, seed: int = 0) -> np.ndarray:
+    """Wire bytes [n, k / bw * bb] of a 32/64-weight-block codec for any K that
+    is a whole number of its blocks (the last 256-weight group may be partial)."""
+    c = codec_id(codec)
+    bw, bb = SUB_BLOCK[c]
+    if k % bw:
+        raise ValueError(f"K={k} is not a whole number of {bw}-weight blocks")
+    full = random_weight(c, n, -(-k // QK) * QK, seed=seed)
+    return np.ascontiguousarray(full[:, : k // bw * bb])
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
