@@ -134,6 +134,12 @@ __device__ __forceinline__ void tma_box(void *dst, const CUtensorMap *map, int x
         : "memory");
 }
 
+// Bring a box into L2 ahead of its shared-memory copy (no completion to wait on).
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap *map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
+}
+
 __device__ __forceinline__ int ld_acquire(const int *p) {
     int v;
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -149,10 +155,16 @@ __device__ __forceinline__ int prob_of(const ChainArgs &a, int unit) {
 
 // Bounded mbarrier wait that sleeps between checks (see mbar_try_wait_sleep):
 // gives up after ~2 s or when another warp gave up, records `code` once.
+__device__ int g_chain_wait_mode;  // development: 0 sleeping try_wait, 1 try_wait, 2 test_wait spin
+
 __device__ __forceinline__ bool ch_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err, int code) {
     uint64_t t0 = 0;
+    const int mode = g_chain_wait_mode;
     for (;;) {
-        if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+        for (int i = 0; i < 64; i++)
+            if (mode == 0 ? mbar_try_wait_sleep(bar, parity, 20000)
+                          : mode == 1 ? mbar_try_wait(bar, parity) : mbar_test_wait(bar, parity))
+                return true;
         if (*abort) return false;
         const uint64_t now = globaltimer();
         if (t0 == 0) t0 = now;
@@ -223,6 +235,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
     uint64_t *eempty = efull + CH_EQ;
     uint8_t *equeue = smem + L::OFF_EQ;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if ((a.debug & 128) && threadIdx.x == 0 && blockIdx.x < 256) a.dbg[1024 + 4 * blockIdx.x] = globaltimer();
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; i++) {
@@ -248,7 +261,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         bool dep_done = false;
         // lane 0 claims units two ahead (pend: the next unit, nn: the one after),
         // so a claim's round trip hides behind a whole unit of copies
-        int unit = blockIdx.x, pend = -1, nn = -1;
+        int unit = blockIdx.x, pend = -1, nn = -1, n3 = -1;  // claims: next, after next, third
         bool first_unit = true;
         while (!*s_abort) {
             if (unit >= a.total_units) {  // end marker: a stage with a negative unit id
@@ -267,6 +280,24 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
             const bool glu = P.act != ACT_NONE;
             const bool ca = P.codec == CA;
             const int boxw = ca ? ch_boxw<CA>() : ch_boxw<CB>(), xstep = ca ? Fmt<CA>::bpb : Fmt<CB>::bpb;
+            // the next claimed unit's weights to L2 now: its stage copies a unit from now then
+            // come from L2, so more bytes are in flight than the ring holds
+            if (!first_unit && lane == 0 && nn >= 0 && nn < a.total_units && !(a.debug & 2) &&
+                !(a.debug & 512)) {  // the unit after next (its claim is a unit old)
+                const int pq = prob_of(a, nn);
+                const ChainProb &Q = a.p[pq];
+                int qt, qc, q0, q1;
+                unit_stages(Q, nn, qt, qc, q0, q1);
+                const int qstep = Q.codec == CA ? Fmt<CA>::bpb : Fmt<CB>::bpb;
+                for (int qs = q0; qs < q1; qs++) {
+                    if (Q.act != ACT_NONE) {
+                        tma_prefetch_l2(&Q.tmw, qs * qstep, qt * 16);
+                        tma_prefetch_l2(&Q.tmw2, qs * qstep, qt * 16);
+                    } else {
+                        tma_prefetch_l2(&Q.tmw, qs * qstep, qt * 32);
+                    }
+                }
+            }
             const uint32_t stage_bytes = 32u * 8u * (uint32_t)boxw;
             for (int st = s0; st < s1; st++, it++) {
                 const int slot = it % NS;
@@ -295,13 +326,17 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                     dep_done = true;
                 }
                 if (st == s0 && lane == 0) {
-                    if (first_unit) pend = (int)gridDim.x + atomicAdd(a.ctl, 1);
-                    nn = (int)gridDim.x + atomicAdd(a.ctl, 1);
+                    if (first_unit) {
+                        pend = (int)gridDim.x + atomicAdd(a.ctl, 1);
+                        nn = (int)gridDim.x + atomicAdd(a.ctl, 1);
+                    }
+                    n3 = (int)gridDim.x + atomicAdd(a.ctl, 1);
                 }
             }
             first_unit = false;
             unit = __shfl_sync(0xffffffffu, pend, 0);
             pend = nn;
+            nn = n3;
         }
         if (*s_abort) {
             // gave up: wait (bounded) until the copies this CTA issued last have
@@ -350,6 +385,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
         }
         sync_target += CH_CW;
         consumers_sync(s_sync, sync_target, s_abort, a.err);
+        if ((a.debug & 128) && warp == 0 && lane == 0 && blockIdx.x < 256) a.dbg[1025 + 4 * blockIdx.x] = globaltimer();
         uint32_t it = 0;
         int tix = 0;
         const bool tr = (a.debug & 64) && blockIdx.x == 0;  // development: time accounting, every consumer warp
@@ -491,6 +527,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
                 mbar_arrive(&efull[e]);
             }
         }
+        if ((a.debug & 128) && warp == 0 && lane == 0 && blockIdx.x < 256) a.dbg[1026 + 4 * blockIdx.x] = globaltimer();
         if (tr && lane == 0) {
             a.dbg[768 + 8 * warp] = t_wait;
             a.dbg[769 + 8 * warp] = t_comp;
@@ -569,6 +606,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) chain_kernel(const __grid_const
     }
     // the last CTA out resets the work and completion counters
     __syncthreads();
+    if ((a.debug & 128) && threadIdx.x == 0 && blockIdx.x < 256) a.dbg[1027 + 4 * blockIdx.x] = globaltimer();
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(a.ctl + 1, 1) == (int)gridDim.x - 1) {
@@ -728,6 +766,10 @@ cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan 
     a.tcnt = tcnt;
     a.partial = partial;
     if (const char *e = dev_env("KQ_CHAIN_DEBUG")) a.debug = atoi(e);  // development switch
+    if (const char *e = dev_env("KQ_CHAIN_WAIT")) {                    // development switch
+        const int m = atoi(e);
+        cudaMemcpyToSymbolAsync(g_chain_wait_mode, &m, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+    }
     a.dbg = reinterpret_cast<unsigned long long *>(reinterpret_cast<char *>(partial) + (1 << 20));
     for (int q = 0; q < count; q++) {
         ChainProb &P = a.p[q];
