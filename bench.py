@@ -7,13 +7,14 @@ under ``sweep``).  One step = one token through all 32 layers of the model
 (32 distinct layers, 4.41 GB of weights, far larger than the 126 MB L2); per
 layer, through the kq ops:
 
-    qkv, o, h, y = quantized_matmul_chain([        (M = 1: ONE launch per layer)
-        q|k|v (x),                 row-concatenated wire, as gmlx/occupancy_fuse.py does
-        o     (a),                 a = this rank's slice of the attention output stand-in
-        gate+up+SiLU (x),          fused gate/up
-        down  (h = output 2)])     Q6_K, reads the gate/up output in the same launch
+    qkv = quantized_matmul(x, Wqkv)           row-concatenated q|k|v wire, as gmlx/occupancy_fuse.py does
+    o   = quantized_matmul(a, Wo)             a = this rank's slice of the attention output stand-in
+    h   = quantized_glu(x, Wgate, Wup, silu)  fused gate/up
+    y   = quantized_matmul(h, Wdown)          Q6_K
 
-(``--ops`` / M > 1: quantized_matmul / quantized_glu, one launch per group.)
+(``--chain``, M = 1: the four as ONE persistent launch, quantized_matmul_chain,
+down reading h through device-side completion counters; both launch
+structures are reported under ``decode_launch_modes``.)
 Weights and activations are seeded synthetic data with the configuration's
 block statistics (no GGUF files on the box).  ``value`` is device-timed over
 exactly ``--steps`` replays of the step's CUDA graph (CUDA events on the
@@ -516,7 +517,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--fused-allreduce", action="store_true")
-    ap.add_argument("--ops", action="store_true", help="one kq op per projection group instead of the chain launch")
+    ap.add_argument("--chain", action="store_true", help="one chain launch per layer instead of one launch per op")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -547,7 +548,9 @@ def main():
     # --fused-allreduce: row-parallel o/down with the cross-rank sum inside their
     # GEMV kernels (peer stores over NVLink); default: NCCL all-reduce
     comm = par.PeerComm(4096, dev) if (world > 1 and args.fused_allreduce) else None
-    head_mode = "chain" if (args.m == 1 and comm is None and not args.ops) else "ops"
+    # headline launch structure: one kq op per projection group (measured the
+    # faster of the two on B200); --chain times the single persistent chain launch
+    head_mode = "chain" if (args.m == 1 and comm is None and args.chain) else "ops"
 
     def measure(m, steps, warmup, mode, min_warm_s=0.0):
         """Seconds per decode step (one token through all N_LAYERS layers),

@@ -31,6 +31,7 @@
 //  * Activation rows are the MMA N dimension (8 per n-tile, up to 4 n-tiles).
 //  * Fused GLU: a 32-row tile holds 16 gate rows and the same 16 up rows, so
 //    act(gate)*up is formed in the epilogue without a second pass.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdlib.h>
@@ -47,8 +48,26 @@ namespace {
 
 // -------------------------------------------------------------------------
 
+// Weight rows of a dense one-row Q4_K problem as a 2-D tensor of uint64
+// [N][row bytes / 8] (the whole-SM copy engine streams one box per stage far
+// faster than 32 row copies).  use == 0: the per-row bulk copies.
+struct GemvMaps {
+    CUtensorMap w, w2;
+    int use;
+};
+
+__device__ __forceinline__ void tma_box_g(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 template <int C, int NT, bool F16, bool GLU, int XR>
-__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(const GemvArgs a,
+                                                                             const __grid_constant__ GemvMaps mp) {
     using L = GLayout<C, NT, XR>;
     constexpr bool XS = L::XS;
     constexpr int bpb = Fmt<C>::bpb, NS = L::NS, KB = L::KB, XSTR = L::XSTR, BPW = GCfg<C>::BPW;
@@ -173,9 +192,12 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                     const int bs = st * KB, nbk = min(KB, nb - bs);
                     const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
                     const uint32_t off = (uint32_t)(src & 15);
-                    const uint32_t bytes = (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
+                    // tensor-map path (mp.use): the stage's 32 rows arrive as one 2-D box
+                    // (two 16-row boxes for the fused GLU) instead of 32 row copies
+                    const uint32_t bytes = mp.use ? (lane == 0 ? (uint32_t)(TROWS * L::SP) : 0u)
+                                                  : (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
                     const uint32_t xbytes = (lane == 0 && !(a.debug & 8)) ? (uint32_t)nbk * QK * 2 : 0u;
-                    rowoff[slot * 32 + lane] = (uint8_t)off;
+                    rowoff[slot * 32 + lane] = mp.use ? (uint8_t)0 : (uint8_t)off;
                     uint32_t total = bytes + xbytes;
 #pragma unroll
                     for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
@@ -186,7 +208,19 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                     __syncwarp();
                     if (!*s_abort) {
                         uint8_t *stg = ring + slot * L::STAGE;
-                        if (bytes) bulk_g2s(stg + lane * L::SP, (const void *)(src - off), bytes, &full[slot], pol);
+                        if (mp.use) {
+                            if (lane == 0) {
+                                const int x = bs * bpb / 8;
+                                if (GLU) {
+                                    tma_box_g(stg, &mp.w, x, T.tile * 16, &full[slot], pol);
+                                    tma_box_g(stg + 16 * L::SP, &mp.w2, x, T.tile * 16, &full[slot], pol);
+                                } else {
+                                    tma_box_g(stg, &mp.w, x, T.tile * 32, &full[slot], pol);
+                                }
+                            }
+                        } else if (bytes) {
+                            bulk_g2s(stg + lane * L::SP, (const void *)(src - off), bytes, &full[slot], pol);
+                        }
                         if (!dep_done) {
                             asm volatile("griddepcontrol.wait;" ::: "memory");
                             dep_done = true;
@@ -812,6 +846,48 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     }
 }
 
+// host: encoded tensor maps, cached by (base, rows, row bytes, stride, box rows)
+typedef CUresult (*GemvEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+bool gemv_map(CUtensorMap *m, const void *w, int64_t n, int64_t row_bytes, int64_t stride, int box_rows) {
+    static GemvEncodeFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return false;
+        fn = reinterpret_cast<GemvEncodeFn>(p);
+    }
+    if (((uintptr_t)w & 15) || (stride & 15) || (row_bytes & 7)) return false;
+    struct Entry {
+        const void *w;
+        int64_t n, rb, stride;
+        int box;
+        CUtensorMap m;
+    };
+    static thread_local Entry cache[16];
+    static thread_local int next = 0;
+    for (const Entry &e : cache)
+        if (e.w == w && e.n == n && e.rb == row_bytes && e.stride == stride && e.box == box_rows) {
+            *m = e.m;
+            return true;
+        }
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride};
+    const cuuint32_t box[2] = {146u, (cuuint32_t)box_rows};  // 8 blocks + 16 bytes: the stage row pitch
+    const cuuint32_t es[2] = {1, 1};
+    if (fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    Entry &e = cache[next];
+    next = (next + 1) % 16;
+    e = Entry{w, n, row_bytes, stride, box_rows, *m};
+    return true;
+}
+
 template <int C, int NT, bool F16, bool GLU, int XR>
 cudaError_t configure() {
     static bool done = false;  // per instantiation; the attribute set is idempotent
@@ -905,7 +981,16 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     GemvArgs b = a;
     b.dyn = dyn;
     b.ksplit = ksplit;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<C, NT, F16, GLU, XR>, b);
+    GemvMaps mp{};
+    if constexpr (C == Q4_K && XR == 1) {
+        // dense one-row Q4_K on the dynamic schedule: weights by tensor boxes
+        if (dyn && a.dense_m > 0 && !a.ar_world && !dev_env("KQ_GEMV_NO_TMAP") && L::SP == 1168 &&
+            L::STAGE % 128 == 0 && L::OFF_RING % 128 == 0 && (16 * L::SP) % 128 == 0 &&
+            gemv_map(&mp.w, a.w, a.N, (int64_t)a.K / QK * 144, a.w_row_stride, GLU ? 16 : 32) &&
+            (!GLU || gemv_map(&mp.w2, a.w2, a.N, (int64_t)a.K / QK * 144, a.w2_row_stride, 16)))
+            mp.use = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<C, NT, F16, GLU, XR>, b, mp);
 }
 
 template <int C, bool F16, bool GLU>

@@ -79,7 +79,9 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int XSTR = XSTR_OF<C>;
     static constexpr int SP = spitch_of<C, DP>();
     static constexpr int WBYTES = TROWS * SP;
-    static constexpr int STAGE = WBYTES + XR * XSTR;
+    // a stage starts on 128 bytes on the lane-per-row path: tensor copies (the
+    // Q4_K one-row weights) need a 128-byte aligned shared destination
+    static constexpr int STAGE = DP ? (WBYTES + XR * XSTR + 127) / 128 * 128 : WBYTES + XR * XSTR;
     // scale tables (MMA path) or per-warp quantized activations (lane-per-row path)
     static constexpr int TABS = DP ? CW * 640 : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;  // per warp: 160 / TABW*BPW floats
     static constexpr int DPB = DP ? 4 * CW * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 <= 4), one row per warp
