@@ -13,6 +13,9 @@ Each case builds seeded synthetic weights (the bench's shapes), runs the op
                 from raw bytes brought in by TMA)
   prefill_down  Q6_K 4096x14336 GEMM, M=2048
   moe_prefill   Qwen3-like expert layer, T=512 (grouped GEMM path)
+  moe_iq2_t64   DeepSeek-like IQ2_XXS expert layer (256 experts, top-8,
+                hidden 7168, ffn 2048), T=64 decode (grouped MMA GEMV path)
+  glu_m32       fused gate/up GEMV, Q4_K 14336x4096 (x2), 32 activation rows
   chain_layer   one Llama-3-8B Q4_K_M layer at M=1 in one chain launch
                 (q|k|v, o, gate+up, down reading the gate/up output)
 """
@@ -59,6 +62,16 @@ def build(case):
         logits = torch.randn(t, e, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
         idx, sc = kq.moe_router_topk(logits, k, True, shared_gate=False)
         return lambda: kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, "q4_k", "q6_k", 0, e)
+    if case == "moe_iq2_t64":
+        e, k, d, f, t = 256, 8, 7168, 2048, 64
+        wg, wu, wd = _w("iq2_xxs", f, d, 11, e), _w("iq2_xxs", f, d, 12, e), _w("iq2_xxs", d, f, 13, e)
+        x = _x(t, d)
+        logits = torch.randn(t, e, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+        idx, sc = kq.moe_router_topk(logits, k, True, shared_gate=False)
+        return lambda: kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, "iq2_xxs", "iq2_xxs", 0, e)
+    if case == "glu_m32":
+        g, u, x = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _x(32, 4096)
+        return lambda: kq.quantized_glu(x, g, u, "q4_k", act="silu")
     if case == "chain_layer":
         x = _x(1, 4096)
         qkv, o = _w("q4_k", 6144, 4096, 5), _w("q4_k", 4096, 4096, 6)
