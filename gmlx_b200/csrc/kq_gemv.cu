@@ -197,7 +197,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                     const uint32_t bytes = mp.use ? (lane == 0 ? (uint32_t)(TROWS * L::SP) : 0u)
                                                   : (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
                     const uint32_t xbytes = (lane == 0 && !(a.debug & 8)) ? (uint32_t)nbk * QK * 2 : 0u;
-                    rowoff[slot * 32 + lane] = mp.use ? (uint8_t)0 : (uint8_t)off;
+                    // tensor boxes start at the 16-byte granule holding the stage's first
+                    // byte (rows are 16-byte aligned, so the offset is the same in every row)
+                    const uint32_t boff = (uint32_t)(bs * bpb) & 15u;
+                    rowoff[slot * 32 + lane] = mp.use ? (uint8_t)boff : (uint8_t)off;
                     uint32_t total = bytes + xbytes;
 #pragma unroll
                     for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
@@ -210,7 +213,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                         uint8_t *stg = ring + slot * L::STAGE;
                         if (mp.use) {
                             if (lane == 0) {
-                                const int x = bs * bpb / 8;
+                                const int x = (bs * bpb >> 4) << 1;  // uint64 units, even: 16-byte aligned
                                 if (GLU) {
                                     tma_box_g(stg, &mp.w, x, T.tile * 16, &full[slot], pol);
                                     tma_box_g(stg + 16 * L::SP, &mp.w2, x, T.tile * 16, &full[slot], pol);
@@ -265,9 +268,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             const int bs = st * KB, nbk = min(KB, nb - bs);
             const uintptr_t src = (uintptr_t)(base + (int64_t)bs * bpb);
             const uint32_t off = (uint32_t)(src & 15);
-            const uint32_t bytes = (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
+            const uint32_t bytes = mp.use ? (lane == 0 ? (uint32_t)(TROWS * L::SP) : 0u)
+                                          : (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
             const uint32_t xbytes = (XS && lane < T.m && !(a.debug & 8)) ? (uint32_t)nbk * QK * 2 : 0u;
-            rowoff[slot * 32 + lane] = (uint8_t)off;
+            rowoff[slot * 32 + lane] = mp.use ? (uint8_t)((uint32_t)(bs * bpb) & 15u) : (uint8_t)off;
             uint32_t total = bytes + xbytes;
 #pragma unroll
             for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
@@ -276,7 +280,17 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             if ((a.debug & 128) && lane == 0 && it < 6) stamps[4 + it] = (unsigned)(clock64() - c_entry);
             if (!*s_abort) {
                 uint8_t *stg = ring + slot * L::STAGE;
-                if (bytes) {
+                if (mp.use) {
+                    if (lane == 0) {
+                        const int x = (bs * bpb >> 4) << 1;
+                        if (GLU) {
+                            tma_box_g(stg, &mp.w, x, T.tile * 16, &full[slot], pol);
+                            tma_box_g(stg + 16 * L::SP, &mp.w2, x, T.tile * 16, &full[slot], pol);
+                        } else {
+                            tma_box_g(stg, &mp.w, x, T.tile * 32, &full[slot], pol);
+                        }
+                    }
+                } else if (bytes) {
                     if (a.debug & 4)
                         asm volatile(
                             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -850,7 +864,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
 typedef CUresult (*GemvEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-bool gemv_map(CUtensorMap *m, const void *w, int64_t n, int64_t row_bytes, int64_t stride, int box_rows) {
+bool gemv_map(CUtensorMap *m, const void *w, int64_t n, int64_t row_bytes, int64_t stride, int box_rows, int box_w) {
     static GemvEncodeFn fn = nullptr;
     if (!fn) {
         void *p = nullptr;
@@ -860,23 +874,23 @@ bool gemv_map(CUtensorMap *m, const void *w, int64_t n, int64_t row_bytes, int64
             return false;
         fn = reinterpret_cast<GemvEncodeFn>(p);
     }
-    if (((uintptr_t)w & 15) || (stride & 15) || (row_bytes & 7)) return false;
+    if (((uintptr_t)w & 15) || (stride & 15) || (row_bytes & 15) || (box_w & 1) || box_w > 256) return false;
     struct Entry {
         const void *w;
         int64_t n, rb, stride;
-        int box;
+        int box, bw;
         CUtensorMap m;
     };
     static thread_local Entry cache[16];
     static thread_local int next = 0;
     for (const Entry &e : cache)
-        if (e.w == w && e.n == n && e.rb == row_bytes && e.stride == stride && e.box == box_rows) {
+        if (e.w == w && e.n == n && e.rb == row_bytes && e.stride == stride && e.box == box_rows && e.bw == box_w) {
             *m = e.m;
             return true;
         }
     const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)n};
     const cuuint64_t strides[1] = {(cuuint64_t)stride};
-    const cuuint32_t box[2] = {146u, (cuuint32_t)box_rows};  // 8 blocks + 16 bytes: the stage row pitch
+    const cuuint32_t box[2] = {(cuuint32_t)box_w, (cuuint32_t)box_rows};  // the stage row pitch in uint64
     const cuuint32_t es[2] = {1, 1};
     if (fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -884,7 +898,7 @@ bool gemv_map(CUtensorMap *m, const void *w, int64_t n, int64_t row_bytes, int64
         return false;
     Entry &e = cache[next];
     next = (next + 1) % 16;
-    e = Entry{w, n, row_bytes, stride, box_rows, *m};
+    e = Entry{w, n, row_bytes, stride, box_rows, box_w, *m};
     return true;
 }
 
@@ -982,12 +996,16 @@ cudaError_t launch_t(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     b.dyn = dyn;
     b.ksplit = ksplit;
     GemvMaps mp{};
-    if constexpr (C == Q4_K && XR == 1) {
-        // dense one-row Q4_K on the dynamic schedule: weights by tensor boxes
-        if (dyn && a.dense_m > 0 && !a.ar_world && !dev_env("KQ_GEMV_NO_TMAP") && L::SP == 1168 &&
+    {
+        // dense problems whose wire rows are 16-byte aligned: each stage's
+        // rows arrive as one 2-D tensor box (two 16-row boxes for the fused GLU),
+        // one copy per stage instead of one per row (per-row copies of ~1 KB
+        // leave one SM's copy engine request-bound well below its share of HBM)
+        const int64_t rb = (int64_t)a.K / QK * Fmt<C>::bpb;
+        if (a.dense_m > 0 && !a.ar_world && !dev_env("KQ_GEMV_NO_TMAP") && L::SP % 16 == 0 &&
             L::STAGE % 128 == 0 && L::OFF_RING % 128 == 0 && (16 * L::SP) % 128 == 0 &&
-            gemv_map(&mp.w, a.w, a.N, (int64_t)a.K / QK * 144, a.w_row_stride, GLU ? 16 : 32) &&
-            (!GLU || gemv_map(&mp.w2, a.w2, a.N, (int64_t)a.K / QK * 144, a.w2_row_stride, 16)))
+            gemv_map(&mp.w, a.w, a.N, rb, a.w_row_stride, GLU ? 16 : 32, L::SP / 8) &&
+            (!GLU || gemv_map(&mp.w2, a.w2, a.N, rb, a.w2_row_stride, 16, L::SP / 8)))
             mp.use = 1;
     }
     return cudaLaunchKernelEx(&cfg, gemv_kernel<C, NT, F16, GLU, XR>, b, mp);
