@@ -546,9 +546,12 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     // IQ2_XXS decode is ALU-bound: with sparse routing (on average well under one
     // slot per expert) one-slot groups take the one-row integer path, faster
     // than 8-row MMA groups even counting the few experts streamed twice
+    // with up to two routed slots per expert on average, groups of <= 4 slots
+    // take the lane-per-row path with every slot's row staged
     const int gsize = ((codec == KQ_IQ2_XXS && slots * 4 <= etotal) || onerow_only(codec))
                           ? 1  // one-row-only codecs: the one-row path is their only GEMV
-                          : (int)(per_expert < 8 ? per_expert : 8);
+                      : (codec == KQ_IQ2_XXS && slots <= 2 * etotal) ? (int)(per_expert < 4 ? per_expert : 4)
+                                                                      : (int)(per_expert < 8 ? per_expert : 8);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;

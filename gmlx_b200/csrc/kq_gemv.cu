@@ -184,8 +184,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                 const bool valid = orow < a.N;
                 const uint8_t *base = up ? a.w2 + (int64_t)T.e * a.w2_expert_stride + (int64_t)orow * a.w2_row_stride
                                          : a.w + (int64_t)T.e * a.w_expert_stride + (int64_t)orow * a.w_row_stride;
-                const uint8_t *xsrc =
-                    reinterpret_cast<const uint8_t *>(a.x) + (int64_t)xrow_of(a, T, 0) * a.x_row_stride * 2;
+                // lane t < m stages activation row t of the group (m <= XR)
+                const int xm = min(T.m, XR);
+                const uint8_t *xsrc = reinterpret_cast<const uint8_t *>(a.x) +
+                                      (int64_t)xrow_of(a, T, lane < xm ? lane : 0) * a.x_row_stride * 2;
                 for (int st = s0; st < s1; st++, it++) {
                     const int slot = it % NS;
                     wait_bounded(&empty[slot], ((it / NS) & 1) ^ 1, s_abort, a.err, 1);
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                     // (two 16-row boxes for the fused GLU) instead of 32 row copies
                     const uint32_t bytes = mp.use ? (lane == 0 ? (uint32_t)(TROWS * L::SP) : 0u)
                                                   : (valid && !(a.debug & 2)) ? ((off + nbk * bpb + 15) & ~15u) : 0u;
-                    const uint32_t xbytes = (lane == 0 && !(a.debug & 8)) ? (uint32_t)nbk * QK * 2 : 0u;
+                    const uint32_t xbytes = (lane < xm && !(a.debug & 8)) ? (uint32_t)nbk * QK * 2 : 0u;
                     // tensor boxes start at the 16-byte granule holding the stage's first
                     // byte (rows are 16-byte aligned, so the offset is the same in every row)
                     const uint32_t boff = (uint32_t)(bs * bpb) & 15u;
@@ -228,7 +230,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                             asm volatile("griddepcontrol.wait;" ::: "memory");
                             dep_done = true;
                         }
-                        if (xbytes) bulk_g2s(stg + L::WBYTES, xsrc + (int64_t)bs * QK * 2, xbytes, &full[slot], pol_x);
+                        if (xbytes)
+                            bulk_g2s(stg + L::WBYTES + lane * XSTR, xsrc + (int64_t)bs * QK * 2, xbytes, &full[slot], pol_x);
                     }
                 }
                 int nu = 0;
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     const int mt = (DP && !HALVES) ? 0 : (warp & 1), col = (DP && !HALVES) ? warp : (DP ? (warp & 3) : (warp >> 1));
     // per-warp table: scales (MMA path) or quantized activations + their
     // scales (lane-per-row path: 128 words + 32 floats = 640 bytes, as TABS)
-    float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * (DP ? 160 : GCfg<C>::TABW * BPW);
+    float *stab = reinterpret_cast<float *>(smem + L::OFF_SCALE) + warp * (DP ? 160 * XR : GCfg<C>::TABW * BPW);
     const int ctid = threadIdx.x;  // 0 .. CW*32-1
     // Consumers block here until the previous kernel on the stream has finished
     // (they need its activations anyway).  Polling the ring instead would burn
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     int *dcnt = const_cast<int *>(reinterpret_cast<volatile int *>(smem + L::OFF_MISC + 16));  // NS+1 tile counters
     // lane-per-row path: one stage of one block column (operands to registers,
     // release the stage, then the arithmetic)
-    auto dp_stage = [&](int slot, int b, float &acc) {
+    auto dp_stage = [&](int slot, int b, float *acc, int m) {
         uint32_t *xq = reinterpret_cast<uint32_t *>(stab);
         float *xsc = stab + 128;
         const bool run = b < nb && !*s_abort && !(a.debug & 1);
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q4k_dot(r, xq, xsc);
+            if (run) acc[0] += dp_q4k_dot(r, xq, xsc);
         } else if constexpr (C == Q5_K) {
             Q5Regs r;
             if (run) {
@@ -359,7 +362,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q5k_dot(r, xq, xsc);
+            if (run) acc[0] += dp_q5k_dot(r, xq, xsc);
         } else if constexpr (C == Q8_0) {
             // lane = row, warp = (group column warp&3, half warp>>2 = four 34-byte blocks)
             const int hf = warp >> 2;
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q80_dot(r, hf, xq, xsc);
+            if (run) acc[0] += dp_q80_dot(r, hf, xq, xsc);
         } else if constexpr (C == Q2_K) {
             Q2Regs r;
             if (run) {
@@ -379,7 +382,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q2k_dot(r, xq, xsc);
+            if (run) acc[0] += dp_q2k_dot(r, xq, xsc);
         } else if constexpr (C == IQ1_S) {
             IQSRegs<C> r;
             if (run) {
@@ -388,7 +391,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_iq1_dot<C>(r.q, r.d, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
+            if (run) acc[0] += dp_iq1_dot<C>(r.q, r.d, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
         } else if constexpr (C == IQ1_M) {
             IQ1MRegs r;
             if (run) {
@@ -397,7 +400,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_iq1_dot<C>(r.q, 0.f, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
+            if (run) acc[0] += dp_iq1_dot<C>(r.q, 0.f, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
         } else if constexpr (C == IQ2_XS || C == IQ2_S || C == IQ3_S) {
             IQSRegs<C> r;
             if (run) {
@@ -407,7 +410,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run)
-                acc += dp_iqs_dot<C>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab),
+                acc[0] += dp_iqs_dot<C>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab),
                                      reinterpret_cast<const uint32_t *>(gridtab));
         } else if constexpr (C == NVFP4) {
             NVRegs r;
@@ -417,7 +420,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_nv_dot(r, xq, xsc);
+            if (run) acc[0] += dp_nv_dot(r, xq, xsc);
         } else if constexpr (C == TQ1_0) {
             TQ1Regs r;
             if (run) {
@@ -426,7 +429,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_tq1_dot(r, xq, xsc);
+            if (run) acc[0] += dp_tq1_dot(r, xq, xsc);
         } else if constexpr (C == TQ2_0) {
             TQ2Regs r;
             if (run) {
@@ -435,7 +438,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_tq2_dot(r, xq, xsc);
+            if (run) acc[0] += dp_tq2_dot(r, xq, xsc);
         } else if constexpr (C == Q3_K) {
             Q3Regs r;
             if (run) {
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q3k_dot(r, xq, xsc);
+            if (run) acc[0] += dp_q3k_dot(r, xq, xsc);
         } else if constexpr (Legacy<C>::IS) {
             // warp = group column, lane = row (a whole group of eight blocks;
             // Q5_1: warp = (group column, half), four blocks)
@@ -456,7 +459,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_leg_dot<C>(r, xq, xsc, 4 * hf);
+            if (run) acc[0] += dp_leg_dot<C>(r, xq, xsc, 4 * hf);
         } else if constexpr (C == Q6_K) {
             // lane = row, warp = (block column warp&3, block half warp>>2)
             const int hf = warp >> 2;
@@ -467,7 +470,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_q6k_dot(r, hf, xq, xsc);
+            if (run) acc[0] += dp_q6k_dot(r, hf, xq, xsc);
         } else if constexpr (C == IQ3_XXS) {
             IQ3Regs r;
             if (run) {
@@ -476,7 +479,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_iq3_dot(r, xq, xsc, reinterpret_cast<const uint32_t *>(gridtab));
+            if (run) acc[0] += dp_iq3_dot(r, xq, xsc, reinterpret_cast<const uint32_t *>(gridtab));
         } else if constexpr (C == IQ4_XS) {
             IQ4Regs r;
             if (run) {
@@ -485,25 +488,34 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_iq4xs_dot(r, xq, xsc);
+            if (run) acc[0] += dp_iq4xs_dot(r, xq, xsc);
         } else {
             IQ2Regs r;
             if (run) {
-                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
+#pragma unroll
+                for (int t = 0; t < (XR > 0 ? XR : 1); t++)
+                    if (t < m)
+                        dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES + t * XSTR) + col * QK,
+                                         xq + 160 * t, xsc + 160 * t);
                 dp_iq2_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) acc += dp_iq2_dot(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
+            if (run) {
+                if constexpr (XR > 1)
+                    dp_iq2_dot_m<XR>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab), m, acc);
+                else
+                    acc[0] += dp_iq2_dot(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
+            }
         }
     };
     // final value of output n of tile T: to y, or (fused all-reduce) as this
     // rank's f32 partial into every rank's communication buffer
     const unsigned ar_epoch = a.ar_world ? *reinterpret_cast<volatile unsigned *>(a.ar_bufs[a.ar_rank]) : 0u;
     const int ar_par = (int)(ar_epoch & 1u);
-    auto emit = [&](const Tile &T, int n, float v) {
+    auto emit = [&](const Tile &T, int tok, int n, float v) {
         if (a.ar_world == 0) {
-            store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, 0) * a.y_row_stride + n, v + bias_of(a, n));
+            store_out(a.y, a.y_dtype, (int64_t)orow_of(a, T, tok) * a.y_row_stride + n, v + bias_of(a, n));
             return;
         }
         const int64_t off = ((int64_t)(ar_par * a.ar_world + a.ar_rank)) * a.N + n;
@@ -513,10 +525,11 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
     // lane-per-row path, whole tile: barrier-free store.  Each warp posts its 32
     // row partials; the last of the KB warps to arrive sums them in column order
     // and stores.  Buffers rotate over NS+1 tiles, which the ring keeps apart.
-    auto dp_store = [&](const Tile &T, float acc, int tix, int split_tile = -1, int chunk_id = 0) {
+    auto dp_store = [&](const Tile &T, const float *acc, int m, int tix, int split_tile = -1, int chunk_id = 0) {
         const int bi = tix % (NS + 1);
-        float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (CW * 32);
-        rb[warp * 32 + lane] = acc;
+        float *rb = reinterpret_cast<float *>(smem + L::OFF_DPB) + bi * (CW * 32 * XR);
+#pragma unroll
+        for (int t = 0; t < XR; t++) rb[(warp * XR + t) * 32 + lane] = acc[t];
         __syncwarp();
         int old = 0;
         if (lane == 0) {
@@ -528,6 +541,21 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             __threadfence_block();
             const int row = GLU ? (lane & 15) : lane;
             const int n = T.tile * rows_out + row;
+            if constexpr (XR > 1) {  // several rows: whole tiles only (no K split)
+                for (int t = 0; t < m; t++) {
+                    float v = 0.f, v2 = 0.f;
+#pragma unroll
+                    for (int w = 0; w < CW; w++) {
+                        v += rb[(w * XR + t) * 32 + row];
+                        if (GLU) v2 += rb[(w * XR + t) * 32 + row + 16];
+                    }
+                    if (GLU) v = apply_act(a.act, v) * v2;
+                    if (n < a.N && (!GLU || lane < 16)) emit(T, t, n, v);
+                }
+                __syncwarp();
+                if (lane == 0) dcnt[bi] = 0;
+                return;
+            }
             float v = 0.f, v2 = 0.f;
             if (split_tile < 0) {
 #pragma unroll
@@ -571,7 +599,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                 }
             }
             if (GLU) v = apply_act(a.act, v) * v2;
-            if (split_tile != -2 && n < a.N && (!GLU || lane < 16)) emit(T, n, v);
+            if (split_tile != -2 && n < a.N && (!GLU || lane < 16)) emit(T, 0, n, v);
             __syncwarp();
             if (lane == 0) dcnt[bi] = 0;
         }
@@ -589,13 +617,16 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                 const int tile = unit / S, s0 = (unit % S) * chunk, s1 = min(nst, s0 + chunk);
                 Tile T;
                 tile_of(a, tile, tiles, T);
-                float acc = 0.f;
+                float acc[XR];
+#pragma unroll
+                for (int t = 0; t < XR; t++) acc[t] = 0.f;
+                const int m = min(T.m, XR);
                 for (int st = s0; st < s1; st++, it++) {
                     slot = it % NS;
                     if (st > s0) wait_bounded(&full[slot], (it / NS) & 1, s_abort, a.err, 2, (a.debug & 256) != 0);
-                    dp_stage(slot, st * KB + col, acc);
+                    dp_stage(slot, st * KB + col, acc, m);
                 }
-                if (!(a.debug & 32)) dp_store(T, acc, tix, S > 1 ? tile : -1, unit % S);
+                if (!(a.debug & 32)) dp_store(T, acc, m, tix, S > 1 ? tile : -1, unit % S);
                 tix++;
             }
             // publish the deferred K-chunk partials: each warp fences its own
@@ -624,8 +655,16 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
                     if (GLU) v2 += __ldcg(pp + row + 16);
                 }
                 if (GLU) v = apply_act(a.act, v) * v2;
-                if (n < a.N && (!GLU || lane < 16)) emit(T, n, v);
+                if (n < a.N && (!GLU || lane < 16)) emit(T, 0, n, v);
                 if (lane == 0) a.counters[2 + t] = 0;
+            }
+            if ((a.debug & 128) && ctid == 0) {  // development timing: per-CTA entry / end / tiles
+                unsigned *o = reinterpret_cast<unsigned *>(a.y) + a.y_row_stride + 32 * blockIdx.x;
+                o[0] = g_entry;
+                o[1] = stamps[0];
+                o[4] = (unsigned)(clock64() - c_entry);
+                o[5] = (unsigned)tix;
+                o[6] = (unsigned)globaltimer();
             }
             // the last CTA out resets the work counters (zero on entry, left zero).
             // Fused all-reduce: it also raises this rank's flag on every peer, waits
@@ -736,7 +775,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
             if ((a.debug & 128) && ctid == 0 && i == lo) stamps[2] = (unsigned)(clock64() - c_entry);
             const int col0 = DP ? col : col * BPW, b = st * KB + col0;
             if constexpr (DP) {
-                dp_stage(slot, b, acc[0][0]);
+                dp_stage(slot, b, &acc[0][0], 1);
                 continue;
             } else if (b < nb && !*s_abort && !(a.debug & 1)) {
                 const uint8_t *stg = ring + slot * L::STAGE;
@@ -766,7 +805,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(cons
         const bool whole = tile_lo >= lo && tile_hi <= hi;
         if constexpr (DP) {
             if (whole) {
-                dp_store(T, acc[0][0], tix);
+                dp_store(T, &acc[0][0], 1, tix);
                 tix++;
                 continue;
             }
@@ -931,7 +970,7 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
     long cap = (long)num_sms() * per_sm;
     if (const char *g = dev_env("KQ_GEMV_GRID")) cap = atol(g);  // development override
     int d = 0, S = 1;
-    if (L::DP && !dev_env("KQ_GEMV_STATIC")) {
+    if (L::DP && XR == 1 && !dev_env("KQ_GEMV_STATIC")) {
         if (units >= 2 * cap) {
             d = 1;
         } else if (units <= cap && nst <= L::NS) {
@@ -947,7 +986,11 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
             d = 1;
         }
     }
-    if (d && L::DP && !a.ar_world)
+    if (XR > 1 && !d) {  // several staged rows: whole tiles handed out dynamically (no K split)
+        d = 1;
+        if (units < cap) cap = units;
+    }
+    if (d && L::DP && !a.ar_world && XR == 1)
         if (const char *f = dev_env("KQ_GEMV_FORCE_S")) S = (int)std::min<long>(nst, std::max(1, atoi(f)));  // development
     if (dyn) *dyn = d;
     if (ksplit) *ksplit = S;
@@ -1015,6 +1058,10 @@ template <int C, bool F16, bool GLU>
 cudaError_t launch_nt(const GemvArgs &a, cudaStream_t st, int *grid_out) {
     // one activation row: its slice is staged in the ring with the weights;
     // more rows: MMA B fragments read from global / L1
+    // IQ2_XXS groups of 2-4 rows (sparse MoE decode): the lane-per-row integer
+    // path with every row staged, each weight decoded once for all rows
+    if constexpr (C == IQ2_XXS)
+        if (a.max_tokens >= 2 && a.max_tokens <= 4 && a.K <= 32 * S_MAX) return launch_t<C, 1, F16, GLU, 4>(a, st, grid_out);
     switch ((a.max_tokens + 7) / 8) {
     case 1:
         return (a.max_tokens == 1 && a.K <= 32 * S_MAX) ? launch_t<C, 1, F16, GLU, 1>(a, st, grid_out)

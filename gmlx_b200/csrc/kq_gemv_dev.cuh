@@ -72,8 +72,9 @@ template <int C, bool DPL = false> __host__ __device__ constexpr int spitch_of()
 // XR: activation rows staged per stage with the weights (0 = read from global)
 template <int C, int NT, int XR> struct GLayout {
     static constexpr bool XS = XR > 0;
-    // lane-per-row integer dot-product path (one activation row, Q4_K)
-    static constexpr bool DP = XR == 1;  // every codec has a lane-per-row path
+    // lane-per-row integer dot-product path: XR activation rows staged with the
+    // weights (1: every codec; up to 4 rows per group: IQ2_XXS)
+    static constexpr bool DP = XR >= 1;
     static constexpr int bpb = Fmt<C>::bpb;
     static constexpr int KB = KB_OF<C>;
     static constexpr int XSTR = XSTR_OF<C>;
@@ -83,18 +84,20 @@ template <int C, int NT, int XR> struct GLayout {
     // Q4_K one-row weights) need a 128-byte aligned shared destination
     static constexpr int STAGE = DP ? (WBYTES + XR * XSTR + 127) / 128 * 128 : WBYTES + XR * XSTR;
     // scale tables (MMA path) or per-warp quantized activations (lane-per-row path)
-    static constexpr int TABS = DP ? CW * 640 : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;  // per warp: 160 / TABW*BPW floats
-    static constexpr int DPB = DP ? 4 * CW * 32 * 4 : 0;  // rotating row-partial buffers (NS + 1 <= 4), one row per warp
+    static constexpr int TABS = DP ? CW * 640 * XR : CW * GCfg<C>::TABW * GCfg<C>::BPW * 4;  // per warp: 160 / TABW*BPW floats
+    // rotating row-partial buffers (NS + 1 <= 4; NS + 1 <= 3 with several rows), one row x XR tokens per warp
+    static constexpr int DPB = DP ? (XR > 1 ? 3 : 4) * CW * 32 * 4 * XR : 0;
     static constexpr bool SX = false;  // Q4_K one-row sums table (off: its per-launch prologue costs more than it saves)
     static constexpr int SBYTES = SX ? S_MAX * 4 : 0;
     // one reduction buffer (two, alternating): [column][token][row]; the
     // lane-per-row path keeps one token per warp
-    static constexpr int REDB = DP ? CW * RED_TS * 4 : NCOL * 8 * NT * RED_TS * 4;
+    // (several staged rows run only on the dynamic schedule, which needs none)
+    static constexpr int REDB = DP ? (XR > 1 ? 0 : CW * RED_TS * 4) : NCOL * 8 * NT * RED_TS * 4;
     static constexpr int FIXED = 512 + GRIDB<C> + TABS + SBYTES + 2 * REDB + DPB;
     static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<C, NT> - FIXED) / STAGE;
     // ring depth (<= 8: rowoff table; <= 3 on the lane-per-row path, whose
     // partial buffers rotate over NS + 1 <= 4 tiles)
-    static constexpr int NS_MAX = DP ? 3 : 8;
+    static constexpr int NS_MAX = DP ? (XR > 1 ? 2 : 3) : 8;
     static constexpr int NS = NS_FIT > NS_MAX ? NS_MAX : (NS_FIT < 2 ? 2 : NS_FIT);
     static constexpr int OFF_BAR = 0;                              // 2*NS mbarriers
     static constexpr int OFF_ROWOFF = 128;                         // NS x 32 bytes
@@ -108,6 +111,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int OFF_DPB = OFF_RED + 2 * REDB;
     static constexpr int BYTES = OFF_DPB + DPB;
     static_assert(!DP || NS <= 3, "lane-per-row path sizes its partial buffers for NS <= 3");
+    static_assert(XR <= 1 || NS <= 2, "several staged rows size their partial buffers for NS <= 2");
     static_assert(!DP || CTAS_PER_SM<C, NT> != 2 || BYTES <= 113 * 1024, "two CTAs per SM must fit");
 };
 
@@ -843,6 +847,44 @@ __device__ __forceinline__ float dp_iq2_dot(const IQ2Regs &r, const uint32_t *xq
     }
     __syncwarp();  // xq is rewritten for the next block
     return acc;
+}
+
+// Lane-per-row IQ2_XXS against up to R activation rows (m of them live): each
+// group of 8 weights is turned into signed bytes once (as dp_iq2_dot), then
+// dotted with every row's int16 activations.  xq / xsc of row t sit at
+// xq + 160 t and xsc + 160 t (the per-warp layout of dp_quantize, one table per row).
+template <int R>
+__device__ __forceinline__ void dp_iq2_dot_m(const IQ2Regs &r, const uint32_t *xq, const float *xsc,
+                                             const uint2 *grid, int m, float *acc) {
+#pragma unroll
+    for (int sb = 0; sb < 8; sb++) {
+        const uint32_t a0 = r.q[2 * sb], a1 = r.q[2 * sb + 1];
+        int sum[R];
+#pragma unroll
+        for (int t = 0; t < R; t++) sum[t] = 0;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint2 g = grid[(a0 >> (8 * l)) & 255u];
+            const uint32_t sg = ksigns((a1 >> (7 * l)) & 127u);
+            const uint32_t f0 = ((sg & 15u) * 0x00204081u) & 0x01010101u, f1 = ((sg >> 4) * 0x00204081u) & 0x01010101u;
+            const int s0 = (int)((g.x ^ (f0 * 0xffu)) + f0), s1 = (int)((g.y ^ (f1 * 0xffu)) + f1);
+#pragma unroll
+            for (int t = 0; t < R; t++) {
+                if (t < m) {
+                    const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 160 * t + 16 * sb + 4 * l);
+                    sum[t] = __dp2a_lo((int)xv.x, s0, sum[t]);
+                    sum[t] = __dp2a_hi((int)xv.y, s0, sum[t]);
+                    sum[t] = __dp2a_lo((int)xv.z, s1, sum[t]);
+                    sum[t] = __dp2a_hi((int)xv.w, s1, sum[t]);
+                }
+            }
+        }
+        const float db = r.d * (0.5f + (float)(a1 >> 28)) * 0.25f;
+#pragma unroll
+        for (int t = 0; t < R; t++)
+            if (t < m) acc[t] = fmaf(db * xsc[160 * t + sb], (float)sum[t], acc[t]);
+    }
+    __syncwarp();  // xq is rewritten for the next block
 }
 
 // Lane-per-row IQ3_XXS: as IQ2_XXS with one grid byte index per 4 weights.
