@@ -16,6 +16,7 @@ Each case builds seeded synthetic weights (the bench's shapes), runs the op
   moe_iq2_t64   DeepSeek-like IQ2_XXS expert layer (256 experts, top-8,
                 hidden 7168, ffn 2048), T=64 decode (grouped MMA GEMV path)
   glu_m32       fused gate/up GEMV, Q4_K 14336x4096 (x2), 32 activation rows
+  glu_m4        the same with 4 activation rows
   chain_layer   one Llama-3-8B Q4_K_M layer at M=1 in one chain launch
                 (q|k|v, o, gate+up, down reading the gate/up output)
 """
@@ -69,8 +70,8 @@ def build(case):
         logits = torch.randn(t, e, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
         idx, sc = kq.moe_router_topk(logits, k, True, shared_gate=False)
         return lambda: kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, "iq2_xxs", "iq2_xxs", 0, e)
-    if case == "glu_m32":
-        g, u, x = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _x(32, 4096)
+    if case in ("glu_m32", "glu_m4"):
+        g, u, x = _w("q4_k", 14336, 4096, 1), _w("q4_k", 14336, 4096, 2), _x(int(case[5:]), 4096)
         return lambda: kq.quantized_glu(x, g, u, "q4_k", act="silu")
     if case == "chain_layer":
         x = _x(1, 4096)
