@@ -218,7 +218,7 @@ def time_graph(torch, fn, steps, warmup, stream, min_warm_s=0.0):
     return a.elapsed_time(b) / 1e3  # seconds for `steps` replays
 
 
-GLU_LAUNCH_DRAM_BYTES = 66_643_712  # ncu: fused gate/up GEMV, Q4_K 2 x 14336 x 4096, M = 1
+GLU_LAUNCH_DRAM_BYTES = 67_143_936  # ncu: fused gate/up GEMV, Q4_K 2 x 14336 x 4096, M = 1 (read + write)
 CHAIN_LAUNCH_DRAM_BYTES = None      # ncu: one chain launch (a whole layer), from the capture in profiles/
 
 

@@ -66,7 +66,7 @@ __device__ __forceinline__ void tma_box_g(void *dst, const CUtensorMap *map, int
 }
 
 template <int C, int NT, bool F16, bool GLU, int XR>
-__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT>) gemv_kernel(const GemvArgs a,
+__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT, XR>) gemv_kernel(const GemvArgs a,
                                                                              const __grid_constant__ GemvMaps mp) {
     using L = GLayout<C, NT, XR>;
     constexpr bool XS = L::XS;
@@ -976,7 +976,7 @@ int grid_for(const GemvArgs &a, int *dyn = nullptr, int *ksplit = nullptr) {
         } else if (units <= cap && nst <= L::NS) {
             d = 1;
             cap = units;
-        } else if (dev_env("KQ_GEMV_KSPLIT") || a.ar_world) {
+        } else if (getenv("KQ_GEMV_KSPLIT") || a.ar_world) {  // a supported run-time switch, read per launch
             // split K into chunks so there are >= 2 units per CTA (off by default:
             // each chunk's partial publish stalls its CTA on a gpu-scope fence,
             // slower than stream-K's at most two partial tiles per CTA)

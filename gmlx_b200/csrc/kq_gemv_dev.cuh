@@ -59,7 +59,7 @@ constexpr int SMEM_BUDGET = 112 * 1024;  // per CTA: two CTAs per SM
 // 17-32 activation rows of Q4_K/Q6_K: one CTA per SM (registers for the MMA
 // fragments of 3-4 n-tiles without spills) with the ring twice as deep;
 // measured slower for 9-16 rows and for IQ2_XXS
-template <int C, int NT> constexpr int CTAS_PER_SM = (NT >= 3 && C != IQ2_XXS) ? 1 : 2;
+template <int C, int NT, int XR> constexpr int CTAS_PER_SM = (XR == 0 && NT >= 3 && C != IQ2_XXS) ? 1 : 2;
 constexpr int S_MAX = 2048;              // Q4_K one-row sub-block sums table: K <= 65536
 
 template <int C, bool DPL = false> __host__ __device__ constexpr int spitch_of() {
@@ -94,7 +94,7 @@ template <int C, int NT, int XR> struct GLayout {
     // (several staged rows run only on the dynamic schedule, which needs none)
     static constexpr int REDB = DP ? (XR > 1 ? 0 : CW * RED_TS * 4) : NCOL * 8 * NT * RED_TS * 4;
     static constexpr int FIXED = 512 + GRIDB<C> + TABS + SBYTES + 2 * REDB + DPB;
-    static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<C, NT> - FIXED) / STAGE;
+    static constexpr int NS_FIT = (SMEM_BUDGET * 2 / CTAS_PER_SM<C, NT, XR> - FIXED) / STAGE;
     // ring depth (<= 8: rowoff table; <= 3 on the lane-per-row path, whose
     // partial buffers rotate over NS + 1 <= 4 tiles)
     static constexpr int NS_MAX = DP ? (XR > 1 ? 2 : 3) : 8;
@@ -112,7 +112,7 @@ template <int C, int NT, int XR> struct GLayout {
     static constexpr int BYTES = OFF_DPB + DPB;
     static_assert(!DP || NS <= 3, "lane-per-row path sizes its partial buffers for NS <= 3");
     static_assert(XR <= 1 || NS <= 2, "several staged rows size their partial buffers for NS <= 2");
-    static_assert(!DP || CTAS_PER_SM<C, NT> != 2 || BYTES <= 113 * 1024, "two CTAs per SM must fit");
+    static_assert(!DP || CTAS_PER_SM<C, NT, XR> != 2 || BYTES <= 113 * 1024, "two CTAs per SM must fit");
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -564,7 +564,8 @@ __device__ __forceinline__ float dp_q4k_dot(const Q4Regs &r, const uint32_t *xq,
     for (int c = 0; c < 4; c++) {
         const uint4 wa = r.w[2 * c], wb = r.w[2 * c + 1];
         const uint32_t w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-        int sl = 0, sh = 0;
+        // four independent dp2a chains (two per sub-block) halve the dependent depth
+        int sl = 0, sh = 0, sl2 = 0, sh2 = 0;
 #pragma unroll
         for (int h4 = 0; h4 < 2; h4++) {
             // x values of sub 2c (k = 64c + 16*h4 .. +15) and sub 2c+1 (+32)
@@ -579,11 +580,13 @@ __device__ __forceinline__ float dp_q4k_dot(const Q4Regs &r, const uint32_t *xq,
                 const uint32_t w = w8[4 * h4 + i];
                 const int lo = (int)(w & 0x0f0f0f0fu), hi = (int)((w >> 4) & 0x0f0f0f0fu);
                 sl = __dp2a_lo((int)xl[2 * i], lo, sl);
-                sl = __dp2a_hi((int)xl[2 * i + 1], lo, sl);
+                sl2 = __dp2a_hi((int)xl[2 * i + 1], lo, sl2);
                 sh = __dp2a_lo((int)xh[2 * i], hi, sh);
-                sh = __dp2a_hi((int)xh[2 * i + 1], hi, sh);
+                sh2 = __dp2a_hi((int)xh[2 * i + 1], hi, sh2);
             }
         }
+        sl += sl2;
+        sh += sh2;
         const int j0 = 2 * c, j1 = 2 * c + 1;
         const uint32_t scw = j0 < 4 ? sc03 : sc47, mw = j0 < 4 ? m03 : m47;
         const float sc0 = (float)((scw >> (8 * (j0 & 3))) & 63u), sc1 = (float)((scw >> (8 * (j1 & 3))) & 63u);
@@ -621,7 +624,8 @@ __device__ __forceinline__ float dp_q5k_dot(const Q5Regs &r, const uint32_t *xq,
     for (int c = 0; c < 4; c++) {
         const uint4 wa = r.w[2 * c], wb = r.w[2 * c + 1];
         const uint32_t w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-        int sl = 0, sh = 0;
+        // four independent dp2a chains (two per sub-block) halve the dependent depth
+        int sl = 0, sh = 0, sl2 = 0, sh2 = 0;
 #pragma unroll
         for (int h4 = 0; h4 < 2; h4++) {
             const uint4 xl0 = *reinterpret_cast<const uint4 *>(xq + 32 * c + 8 * h4);
@@ -773,7 +777,7 @@ __device__ __forceinline__ float dp_q6k_dot(const Q6Regs &r, int hf, const uint3
 #pragma unroll
     for (int s4 = 0; s4 < 4; s4++) {
         const int ns = 4 * (s4 >> 1);
-        int sm[2] = {0, 0};  // the two 16-weight sub-blocks of this 32-weight group
+        int sm[2] = {0, 0}, sm2[2] = {0, 0};  // the two 16-weight sub-blocks of this 32-weight group (2 chains each)
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const uint32_t lw = r.ql[8 * (s4 & 1) + i] >> ns;
@@ -781,10 +785,11 @@ __device__ __forceinline__ float dp_q6k_dot(const Q6Regs &r, int hf, const uint3
             const int q6 = (int)lop_and_or(hw, 0x30303030u, lw & 0x0f0f0f0fu);
             // weights 128hf + 32 s4 + 4i .. +3  <-> x words (64 s4 + 8i)/2 of the block-half
             const uint2 xv = *reinterpret_cast<const uint2 *>(xq + 64 * hf + 16 * s4 + 2 * i);
-            int &acc_i = sm[i >> 2];
-            acc_i = __dp2a_lo((int)xv.x, q6, acc_i);
-            acc_i = __dp2a_hi((int)xv.y, q6, acc_i);
+            sm[i >> 2] = __dp2a_lo((int)xv.x, q6, sm[i >> 2]);
+            sm2[i >> 2] = __dp2a_hi((int)xv.y, q6, sm2[i >> 2]);
         }
+        sm[0] += sm2[0];
+        sm[1] += sm2[1];
         const int g32 = 4 * hf + s4;  // x quantization group of these 32 weights
 #pragma unroll
         for (int u = 0; u < 2; u++) {

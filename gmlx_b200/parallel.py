@@ -1,7 +1,7 @@
 """Tensor- and expert-parallel layers over the kq ops (one process per GPU,
 torch.distributed for the collectives: NCCL on B200s, gloo in CPU tests).
 
-Dense decoder layer (SURVEY §8(e) e1): column-parallel q/k/v and gate/up
+Dense decoder layer: column-parallel q/k/v and gate/up
 (split the output rows -- wire rows are independent, so any row split is exact,
 gmlx/occupancy_fuse.py:32-34), row-parallel o and down (split K at whole
 256-weight-block granularity, i.e. a byte range of every wire row), one
@@ -9,7 +9,7 @@ all-reduce of the partial sums after each row-parallel projection.  This is the
 shard_linear layout gmlx uses for hy_v3 (gmlx/hy_v3_model.py:396-443) with the
 all_sum of gmlx/hy_v3_model.py:259.
 
-MoE expert layer (e2), two ways, experts split by contiguous expert-id range:
+MoE expert layer, two ways, experts split by contiguous expert-id range:
  * route-all + all-reduce (ep_moe_forward): every rank routes the same tokens,
    runs the routed slots whose expert it owns, and the per-rank partial
    outputs are summed -- the sharding_group all_sum of
