@@ -75,5 +75,32 @@ def build(verbose: bool = False) -> str:
     return LIB
 
 
+EXT_DIR = os.path.join(HERE, "_ext")
+EXT_SO = os.path.join(EXT_DIR, "kq_torch.so")
+
+
+def build_torch_ext(verbose: bool = False) -> str:
+    """Compile the torch C++ fast path of the decode ops (csrc/kq_torch.cpp)
+    in-tree into _ext/kq_torch.so (rebuilt only when its source changed)."""
+    import torch.utils.cpp_extension as ce
+    os.makedirs(EXT_DIR, exist_ok=True)
+    ce.load(name="kq_torch", sources=[os.path.join(CSRC, "kq_torch.cpp")], build_directory=EXT_DIR,
+            extra_cflags=["-O3"], with_cuda=True, verbose=verbose)
+    return EXT_SO
+
+
+def load_torch_ext():
+    """Import the prebuilt _ext/kq_torch.so (None when it was not built)."""
+    if not os.path.exists(EXT_SO):
+        return None
+    import importlib.util
+    import torch  # noqa: F401  (the extension links against the loaded torch libraries)
+    spec = importlib.util.spec_from_file_location("kq_torch", EXT_SO)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
+    print(build_torch_ext(verbose="-v" in sys.argv))

@@ -158,9 +158,43 @@ def _ws_size(fn_name: str, *args) -> int:
     return v
 
 
+_EXT = None  # the native fast path (gmlx_b200/_ext/kq_torch.so) once loaded; False: not built
+
+
+def _ext():
+    """The torch C++ extension of the decode ops, bound to this process's
+    libkq_cuda entry points; None if it was not built."""
+    global _EXT
+    if _EXT is None:
+        from . import build as _build
+        e = _build.load_torch_ext()
+        if e is not None:
+            L = _lib.load()
+            addr = lambda f: _ct.cast(f, _ct.c_void_p).value  # noqa: E731
+            e.set_entry_points(addr(L.kq_quantized_matmul), addr(L.kq_quantized_glu),
+                               addr(L.kq_quantized_matmul_workspace_size), addr(L.kq_quantized_glu_workspace_size))
+        _EXT = e if e is not None else False
+    return _EXT or None
+
+
+_FAST_CODEC: dict = {}  # codec argument -> (codec id, block bytes)
+
+
+def _fast_codec(codec):
+    v = _FAST_CODEC.get(codec)
+    if v is None:
+        c = _cid(codec)
+        v = (c, BLOCK_BYTES[c])
+        _FAST_CODEC[codec] = v
+    return v
+
+
 def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
     key = (dev.index if dev.index is not None else torch.cuda.current_device(),
            torch.cuda.current_stream(dev).cuda_stream)
+    e = _ext()
+    if e is not None:  # one registry for both paths
+        return e.workspace(key[0], key[1], nbytes)
     ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
@@ -172,8 +206,9 @@ def workspace_error(device=None, clear: bool = True) -> int:
     """Device-side error word of the current stream's workspace (syncs)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
-    ws = _WS.get(key)
-    if ws is None:
+    e = _ext()
+    ws = e.workspace_peek(key[0], key[1]) if e is not None else _WS.get(key)
+    if ws is None:  # (an undefined tensor from the extension arrives as None)
         return 0
     return _lib.load().kq_workspace_error(_p(ws), int(clear), _stream(dev))
 
@@ -214,6 +249,13 @@ def _act_2d(x: torch.Tensor, k: int) -> torch.Tensor:
 def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales=None, codec=None, transpose: bool = True,
                      out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """``kq.quantized_matmul(x, w, scales, codec, transpose=True)``: ``x @ dequant(w).T``."""
+    if transpose and w.dim() == 2 and (out_dtype is None or out_dtype in _DT):
+        e = _ext()
+        if e is not None:  # native fast path; None: the full path below (and its errors)
+            c, bpb = _fast_codec(codec)
+            y = e.quantized_matmul(x, w, c, bpb, -1 if out_dtype is None else _DT[out_dtype])
+            if y is not None:
+                return y
     if not transpose:
         raise NotImplementedError("kq.quantized_matmul: only transpose=True (wire rows are outputs)")
     c = _cid(codec)
@@ -288,6 +330,13 @@ def quantized_matmul_allreduce(x: torch.Tensor, w: torch.Tensor, codec, comm,
 def quantized_glu(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, codec=None, act: str = "silu",
                   out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """Fused ``act(x @ Wg.T) * (x @ Wu.T)`` for a dense gate/up pair (one launch)."""
+    if gate_w.dim() == 2 and act in _lib.ACTS and (out_dtype is None or out_dtype in _DT):
+        e = _ext()
+        if e is not None:  # native fast path; None: the full path below (and its errors)
+            c, bpb = _fast_codec(codec)
+            y = e.quantized_glu(x, gate_w, up_w, c, bpb, _lib.ACTS[act], -1 if out_dtype is None else _DT[out_dtype])
+            if y is not None:
+                return y
     c = _cid(codec)
     _need_cuda(x, gate_w, up_w)
     k = _wire_k(gate_w, c)

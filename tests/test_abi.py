@@ -86,3 +86,13 @@ def test_codecs_match_the_loader_whitelist():
     assert len(kq.codecs()) == 21
     assert set(kq.all_codecs()) == set(kq.codecs()) | {"tq1_0", "tq2_0"}
     assert all(kq.codec_has_matmul(c) for c in kq.all_codecs())
+
+
+def test_torch_extension_exports():
+    """The decode fast path extension (built by build()) loads and exports its ops."""
+    from gmlx_b200 import build
+    mod = build.load_torch_ext()
+    if mod is None:
+        pytest.skip("gmlx_b200/_ext/kq_torch.so not built")
+    for name in ("set_entry_points", "workspace", "workspace_peek", "quantized_matmul", "quantized_glu"):
+        assert hasattr(mod, name)
