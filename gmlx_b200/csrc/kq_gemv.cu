@@ -502,10 +502,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT, XR>) gemv_kernel(
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) {
-                if constexpr (XR > 1)
-                    dp_iq2_dot_m<XR>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab), m, acc);
-                else
-                    acc[0] += dp_iq2_dot(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab));
+                const uint2 *gt = reinterpret_cast<const uint2 *>(gridtab);
+                if constexpr (XR > 1) {  // exactly the group's rows (m is warp-uniform)
+                    if (m == 1) dp_iq2_dot_r<1>(r, xq, xsc, gt, acc);
+                    else if (m == 2) dp_iq2_dot_r<2>(r, xq, xsc, gt, acc);
+                    else if (m == 3) dp_iq2_dot_r<3>(r, xq, xsc, gt, acc);
+                    else dp_iq2_dot_r<4>(r, xq, xsc, gt, acc);
+                } else {
+                    dp_iq2_dot_r<1>(r, xq, xsc, gt, acc);
+                }
             }
         }
     };

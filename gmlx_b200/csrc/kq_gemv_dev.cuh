@@ -805,9 +805,9 @@ __device__ __forceinline__ float dp_q6k_dot(const Q6Regs &r, int hf, const uint3
 
 // Lane-per-row IQ2_XXS: the lane's 66-byte block (2-byte aligned) is read as
 // words with funnel shifts; each group of 8 weights becomes two words of
-// signed int8 (grid magnitude bytes, negated where the sign bit is set:
-// (g ^ 0xff) + 1 per byte, no carries as 1 <= g < 128) dotted against the
-// int16 activations with dp2a.  Per 32-weight sub-block:
+// signed int8 (grid magnitude bytes, replaced by their negation where the
+// sign bit is set) dotted against the int16 activations with dp2a.  Per
+// 32-weight sub-block:
 //     acc += d (0.5 + ls) / 4 * dx_j * sum_j(signed grid * x_q).
 struct IQ2Regs {
     uint32_t q[16];
@@ -827,40 +827,16 @@ __device__ __forceinline__ void dp_iq2_load(const uint8_t *blk, IQ2Regs &r) {
     for (int j = 0; j < 16; j++) r.q[j] = sh ? w[j + 1] : __funnelshift_r(w[j], w[j + 1], 16);
 }
 
-__device__ __forceinline__ float dp_iq2_dot(const IQ2Regs &r, const uint32_t *xq, const float *xsc,
-                                           const uint2 *grid) {
-    float acc = 0.f;
-#pragma unroll
-    for (int sb = 0; sb < 8; sb++) {
-        const uint32_t a0 = r.q[2 * sb], a1 = r.q[2 * sb + 1];
-        int sum = 0;
-#pragma unroll
-        for (int l = 0; l < 4; l++) {
-            const uint2 g = grid[(a0 >> (8 * l)) & 255u];
-            // sign bits -> byte flags (bit i at bit 8i) -> 0x00 / 0xff byte masks
-            // (arithmetic: a shared-memory table lookup per lane bank-conflicts)
-            const uint32_t sg = ksigns((a1 >> (7 * l)) & 127u);
-            const uint32_t f0 = ((sg & 15u) * 0x00204081u) & 0x01010101u, f1 = ((sg >> 4) * 0x00204081u) & 0x01010101u;
-            const int s0 = (int)((g.x ^ (f0 * 0xffu)) + f0), s1 = (int)((g.y ^ (f1 * 0xffu)) + f1);
-            const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 16 * sb + 4 * l);
-            sum = __dp2a_lo((int)xv.x, s0, sum);
-            sum = __dp2a_hi((int)xv.y, s0, sum);
-            sum = __dp2a_lo((int)xv.z, s1, sum);
-            sum = __dp2a_hi((int)xv.w, s1, sum);
-        }
-        acc = fmaf(r.d * (0.5f + (float)(a1 >> 28)) * 0.25f * xsc[sb], (float)sum, acc);
-    }
-    __syncwarp();  // xq is rewritten for the next block
-    return acc;
-}
-
-// Lane-per-row IQ2_XXS against up to R activation rows (m of them live): each
-// group of 8 weights is turned into signed bytes once (as dp_iq2_dot), then
-// dotted with every row's int16 activations.  xq / xsc of row t sit at
-// xq + 160 t and xsc + 160 t (the per-warp layout of dp_quantize, one table per row).
+// Lane-per-row IQ2_XXS against R activation rows (row t's int16 table of
+// dp_quantize at xq + 160 t, its scales at xsc + 160 t).  Each group of 8 weights is decoded
+// once for all rows: sign bit i of the group lands in bit 7 of byte i
+// (multiply by 0x10204080 spreads a nibble's bits to bytes), a byte permute
+// replicates it into a 0x00 / 0xff mask, and the mask selects between the
+// grid bytes g and their negations 0x01010100 - g (bytewise 256 - g: no
+// borrows, as 1 <= g < 128).
 template <int R>
-__device__ __forceinline__ void dp_iq2_dot_m(const IQ2Regs &r, const uint32_t *xq, const float *xsc,
-                                             const uint2 *grid, int m, float *acc) {
+__device__ __forceinline__ void dp_iq2_dot_r(const IQ2Regs &r, const uint32_t *xq, const float *xsc, const uint2 *grid,
+                                            float *acc) {
 #pragma unroll
     for (int sb = 0; sb < 8; sb++) {
         const uint32_t a0 = r.q[2 * sb], a1 = r.q[2 * sb + 1];
@@ -870,24 +846,23 @@ __device__ __forceinline__ void dp_iq2_dot_m(const IQ2Regs &r, const uint32_t *x
 #pragma unroll
         for (int l = 0; l < 4; l++) {
             const uint2 g = grid[(a0 >> (8 * l)) & 255u];
-            const uint32_t sg = ksigns((a1 >> (7 * l)) & 127u);
-            const uint32_t f0 = ((sg & 15u) * 0x00204081u) & 0x01010101u, f1 = ((sg >> 4) * 0x00204081u) & 0x01010101u;
-            const int s0 = (int)((g.x ^ (f0 * 0xffu)) + f0), s1 = (int)((g.y ^ (f1 * 0xffu)) + f1);
+            const uint32_t s7 = (a1 >> (7 * l)) & 127u;
+            const uint32_t nlo = s7 & 15u, nhi = (s7 >> 4) | ((__popc(s7) & 1u) << 3);
+            const uint32_t mlo = prmt(nlo * 0x10204080u, 0u, 0xBA98u), mhi = prmt(nhi * 0x10204080u, 0u, 0xBA98u);
+            const int s0 = (int)((g.x & ~mlo) | ((0x01010100u - g.x) & mlo));
+            const int s1 = (int)((g.y & ~mhi) | ((0x01010100u - g.y) & mhi));
 #pragma unroll
             for (int t = 0; t < R; t++) {
-                if (t < m) {
-                    const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 160 * t + 16 * sb + 4 * l);
-                    sum[t] = __dp2a_lo((int)xv.x, s0, sum[t]);
-                    sum[t] = __dp2a_hi((int)xv.y, s0, sum[t]);
-                    sum[t] = __dp2a_lo((int)xv.z, s1, sum[t]);
-                    sum[t] = __dp2a_hi((int)xv.w, s1, sum[t]);
-                }
+                const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 160 * t + 16 * sb + 4 * l);
+                sum[t] = __dp2a_lo((int)xv.x, s0, sum[t]);
+                sum[t] = __dp2a_hi((int)xv.y, s0, sum[t]);
+                sum[t] = __dp2a_lo((int)xv.z, s1, sum[t]);
+                sum[t] = __dp2a_hi((int)xv.w, s1, sum[t]);
             }
         }
         const float db = r.d * (0.5f + (float)(a1 >> 28)) * 0.25f;
 #pragma unroll
-        for (int t = 0; t < R; t++)
-            if (t < m) acc[t] = fmaf(db * xsc[160 * t + sb], (float)sum[t], acc[t]);
+        for (int t = 0; t < R; t++) acc[t] = fmaf(db * xsc[160 * t + sb], (float)sum[t], acc[t]);
     }
     __syncwarp();  // xq is rewritten for the next block
 }
