@@ -489,29 +489,32 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM<C, NT, XR>) gemv_kernel(
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (run) acc[0] += dp_iq4xs_dot(r, xq, xsc);
-        } else {
-            IQ2Regs r;
+        } else if constexpr (XR > 1) {
+            // IQ2_XXS, 1-4 staged rows: the dot reads the stage, then releases it
             if (run) {
 #pragma unroll
-                for (int t = 0; t < (XR > 0 ? XR : 1); t++)
+                for (int t = 0; t < XR; t++)
                     if (t < m)
                         dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES + t * XSTR) + col * QK,
                                          xq + 160 * t, xsc + 160 * t);
+                const uint8_t *blk = stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb;
+                const uint2 *gt = reinterpret_cast<const uint2 *>(gridtab);
+                if (m == 1) dp_iq2_dot_smem<1>(blk, xq, xsc, gt, acc);  // m is warp-uniform
+                else if (m == 2) dp_iq2_dot_smem<2>(blk, xq, xsc, gt, acc);
+                else if (m == 3) dp_iq2_dot_smem<3>(blk, xq, xsc, gt, acc);
+                else dp_iq2_dot_smem<4>(blk, xq, xsc, gt, acc);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        } else {
+            IQ2Regs r;
+            if (run) {
+                dp_quantize<F16>(reinterpret_cast<const uint16_t *>(stg + L::WBYTES) + col * QK, xq, xsc);
                 dp_iq2_load(stg + lane * L::SP + rowoff[slot * 32 + lane] + col * bpb, r);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (run) {
-                const uint2 *gt = reinterpret_cast<const uint2 *>(gridtab);
-                if constexpr (XR > 1) {  // exactly the group's rows (m is warp-uniform)
-                    if (m == 1) dp_iq2_dot_r<1>(r, xq, xsc, gt, acc);
-                    else if (m == 2) dp_iq2_dot_r<2>(r, xq, xsc, gt, acc);
-                    else if (m == 3) dp_iq2_dot_r<3>(r, xq, xsc, gt, acc);
-                    else dp_iq2_dot_r<4>(r, xq, xsc, gt, acc);
-                } else {
-                    dp_iq2_dot_r<1>(r, xq, xsc, gt, acc);
-                }
-            }
+            if (run) dp_iq2_dot_r<1>(r, xq, xsc, reinterpret_cast<const uint2 *>(gridtab), acc);
         }
     };
     // final value of output n of tile T: to y, or (fused all-reduce) as this

@@ -867,6 +867,51 @@ __device__ __forceinline__ void dp_iq2_dot_r(const IQ2Regs &r, const uint32_t *x
     __syncwarp();  // xq is rewritten for the next block
 }
 
+// The same dot read straight from the ring stage (the caller releases the
+// stage afterwards), with the sub-block loop kept rolled: a kernel that holds
+// all four row counts then stays within the instruction cache (the unrolled,
+// register-held form is used for one row).  The 66-byte block is 2-byte
+// aligned; qs word j is bytes 2 + 4j .. 5 + 4j.
+template <int R>
+__device__ __forceinline__ void dp_iq2_dot_smem(const uint8_t *blk, const uint32_t *xq, const float *xsc,
+                                                const uint2 *grid, float *acc) {
+    const uintptr_t ab = (uintptr_t)blk;
+    const uint32_t *aw = reinterpret_cast<const uint32_t *>(ab & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(ab & 3) * 8;  // 0 or 16
+    const float dq = half_bits_to_float(__funnelshift_r(aw[0], aw[1], sh) & 0xffffu) * 0.25f;
+    const uint32_t *bw = aw + (sh ? 1 : 0);
+    const uint32_t s2 = 16u - sh;
+#pragma unroll 1
+    for (int sb = 0; sb < 8; sb++) {
+        const uint32_t w0 = bw[2 * sb], w1 = bw[2 * sb + 1], w2 = bw[2 * sb + 2];
+        const uint32_t a0 = __funnelshift_r(w0, w1, s2), a1 = __funnelshift_r(w1, w2, s2);
+        int sum[R];
+#pragma unroll
+        for (int t = 0; t < R; t++) sum[t] = 0;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint2 g = grid[(a0 >> (8 * l)) & 255u];
+            const uint32_t s7 = (a1 >> (7 * l)) & 127u;
+            const uint32_t nlo = s7 & 15u, nhi = (s7 >> 4) | ((__popc(s7) & 1u) << 3);
+            const uint32_t mlo = prmt(nlo * 0x10204080u, 0u, 0xBA98u), mhi = prmt(nhi * 0x10204080u, 0u, 0xBA98u);
+            const int s0 = (int)((g.x & ~mlo) | ((0x01010100u - g.x) & mlo));
+            const int s1 = (int)((g.y & ~mhi) | ((0x01010100u - g.y) & mhi));
+#pragma unroll
+            for (int t = 0; t < R; t++) {
+                const uint4 xv = *reinterpret_cast<const uint4 *>(xq + 160 * t + 16 * sb + 4 * l);
+                sum[t] = __dp2a_lo((int)xv.x, s0, sum[t]);
+                sum[t] = __dp2a_hi((int)xv.y, s0, sum[t]);
+                sum[t] = __dp2a_lo((int)xv.z, s1, sum[t]);
+                sum[t] = __dp2a_hi((int)xv.w, s1, sum[t]);
+            }
+        }
+        const float db = dq * (0.5f + (float)(a1 >> 28));
+#pragma unroll
+        for (int t = 0; t < R; t++) acc[t] = fmaf(db * xsc[160 * t + sb], (float)sum[t], acc[t]);
+    }
+    __syncwarp();  // xq is rewritten for the next block
+}
+
 // Lane-per-row IQ3_XXS: as IQ2_XXS with one grid byte index per 4 weights.
 // The 98-byte block (2-byte aligned) is read as 25 words: 16 words of grid
 // indices then 8 words of (four 7-bit sign indices, ls << 28), one per
