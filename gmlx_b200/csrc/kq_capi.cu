@@ -522,11 +522,22 @@ int run_grouped_layer(int cgu, int cd, const void *x, int x_dtype, int64_t t, in
 
 // Routed (MoE) GEMV over expert stacks.  mode: 0 glu (x row = slot/k),
 // 1 per-slot rows (x row = slot), 2 explicit x_index.
+// Slots per group of the routed GEMV.  per_expert bounds the slots one expert
+// can receive (distinct experts per token).  IQ2_XXS decode is ALU-bound: with
+// up to two routed slots per expert on average, groups of <= 4 slots take the
+// lane-per-row path with every slot's row staged (each weight decoded once for
+// the group; a one-slot group is the one-row dot).
+int routed_gsize(int codec, int64_t slots, int64_t per_expert, int64_t etotal) {
+    if (onerow_only(codec)) return 1;  // one-row-only codecs: the one-row path is their only GEMV
+    if (codec == KQ_IQ2_XXS && slots <= 2 * etotal) return (int)(per_expert < 4 ? per_expert : 4);
+    return (int)(per_expert < 8 ? per_expert : 8);
+}
+
 int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, int64_t slots, int kslot,
                int64_t tokens, const int32_t *idx, const int32_t *xidx, int mode, const void *w, const void *w2,
                int64_t e, int64_t n, int64_t wrs, int64_t wes, int act, void *y, int y_dtype, int64_t yrs,
                const float *scores, void *ws, size_t ws_bytes, void *stream, const char *what, int64_t ebase = 0,
-               int64_t etotal = -1) {
+               int64_t etotal = -1, bool reuse_groups = false) {
     if (etotal < 0) etotal = e;
     int rc;
     if ((rc = check_weights(codec, w, kin, wrs, what))) return rc;
@@ -542,16 +553,7 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
                            y, y_dtype, yrs, scores, ws, ws_bytes, stream, what, ebase, etotal);
     // groups of <= 8 slots: one MMA n-tile; an expert with more routed rows
     // streams its weights once per 8 rows (decode routes few rows per expert)
-    const int64_t per_expert = mode == 2 ? slots : tokens;  // distinct experts per token bound group sizes
-    // IQ2_XXS decode is ALU-bound: with sparse routing (on average well under one
-    // slot per expert) one-slot groups take the one-row integer path, faster
-    // than 8-row MMA groups even counting the few experts streamed twice
-    // with up to two routed slots per expert on average, groups of <= 4 slots
-    // take the lane-per-row path with every slot's row staged
-    const int gsize = ((codec == KQ_IQ2_XXS && slots * 4 <= etotal) || onerow_only(codec))
-                          ? 1  // one-row-only codecs: the one-row path is their only GEMV
-                      : (codec == KQ_IQ2_XXS && slots <= 2 * etotal) ? (int)(per_expert < 4 ? per_expert : 4)
-                                                                      : (int)(per_expert < 8 ? per_expert : 8);
+    const int gsize = routed_gsize(codec, slots, mode == 2 ? slots : tokens, etotal);
     const int maxg = moe_max_groups(slots, e, gsize);
     GemvArgs a{};
     a.codec = codec;
@@ -581,14 +583,18 @@ int run_routed(int codec, const void *x, int x_dtype, int64_t xs, int64_t kin, i
     int *err = (int *)base, *ng = (int *)(base + 4);
     int *gexp = (int *)(base + p.groups_off), *gcnt = gexp + maxg, *gx = gcnt + maxg, *go = gx + (size_t)maxg * 32;
     cudaStream_t st = (cudaStream_t)stream;
-    cudaError_t ce = launch_moe_groups(idx, (int)slots, kslot, (int)ebase, (int)e, (int)etotal, mode == 1, xidx, gsize,
-                                       ng, gexp, gcnt, gx, go,
-                                       maxg, err, st);
+    cudaError_t ce = cudaSuccess;
+    // reuse_groups (down projection of an expert layer, mode 1): the gate/up
+    // call on this workspace grouped the same slots with the same group size,
+    // and a slot's activation row here is the slot itself, its output row
+    if (!reuse_groups)
+        ce = launch_moe_groups(idx, (int)slots, kslot, (int)ebase, (int)e, (int)etotal, mode == 1, xidx, gsize, ng, gexp,
+                               gcnt, gx, go, maxg, err, st);
     if (ce != cudaSuccess) return cuda_status(ce, what);
     a.n_groups = ng;
     a.grp_expert = gexp;
     a.grp_count = gcnt;
-    a.grp_xrow = gx;
+    a.grp_xrow = reuse_groups ? go : gx;
     a.grp_orow = go;
     a.err = err;
     a.counters = (int *)(base + p.cnt_off);
@@ -913,9 +919,14 @@ int kq_moe_expert_layer_local(int codec_gu, int codec_d, const void *x, int x_dt
                         gu_row_stride, gu_expert_stride, act, h, x_dtype, f, nullptr, workspace, routed, stream,
                         "moe_expert_layer_local", expert_base, e_total);
     if (rc) return rc;
+    // both projections on the routed GEMV with the same group size: the down
+    // projection reads the gate/up call's group tables (one grouping launch per layer)
+    const bool reuse = !use_grouped(codec_gu, slots, e_total, f, d, act, true, x_dtype, d) &&
+                       !use_grouped(codec_d, slots, e_total, d, f, ACT_NONE, false, x_dtype, f) &&
+                       routed_gsize(codec_gu, slots, t, e_total) == routed_gsize(codec_d, slots, t, e_total);
     return run_routed(codec_d, h, x_dtype, f, f, slots, k, t, idx, nullptr, 1, down_w, nullptr, e_local, d, d_row_stride,
                       d_expert_stride, ACT_NONE, y, y_dtype, d, scores, workspace, routed, stream,
-                      "moe_expert_layer_local", expert_base, e_total);
+                      "moe_expert_layer_local", expert_base, e_total, reuse);
 }
 
 // ---- chain of one-row projections (kq_chain.cu) ----
