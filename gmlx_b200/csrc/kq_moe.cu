@@ -100,6 +100,10 @@ __global__ void groups_kernel(const int32_t *__restrict__ idx, int S, int k, int
     constexpr int SIDX = 4096;  // routing ids staged in shared memory for the placement pass
     __shared__ int s_cnt[RT_MAXE], s_first[RT_MAXE + 1], s_base[RT_MAXE], s_idx[SIDX];
     __shared__ int s_bad;
+    // launched as a programmatic dependent: the routing ids may be the
+    // previous kernel's output (no early trigger here: the GEMV that follows
+    // reads the group tables before its own dependency wait)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) s_bad = 0;
     for (int e = threadIdx.x; e < ecount; e += blockDim.x) s_cnt[e] = 0, s_base[e] = 0;
@@ -161,6 +165,7 @@ __global__ void groups_kernel(const int32_t *__restrict__ idx, int S, int k, int
 __global__ void mix_kernel(const float *__restrict__ ys, const float *__restrict__ scores,
                            const int32_t *__restrict__ idx, int ebase, int ecount, int T, int k, int N,
                            void *__restrict__ y, int y_dtype) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // ys is the previous kernel's output
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * N) return;
     const int t = (int)(i / N), n = (int)(i - (int64_t)t * N);
@@ -214,17 +219,35 @@ cudaError_t launch_moe_groups(const int32_t *idx, int S, int k, int ebase, int e
                               const int32_t *xidx, int gsize, int *n_groups, int *grp_expert, int *grp_count,
                               int *grp_xrow, int *grp_orow, int max_groups, int *err, cudaStream_t st) {
     if (ecount > RT_MAXE) return cudaErrorInvalidValue;  // per-expert tables live in shared memory
-    groups_kernel<<<1, 1024, 0, st>>>(idx, S, k, ebase, ecount, etotal, xrow_is_slot, xidx, gsize, n_groups,
-                                      grp_expert, grp_count, grp_xrow, grp_orow, max_groups, err);
-    return cudaGetLastError();
+    // programmatic dependent launch: the launch overlaps the previous kernel's
+    // tail; the kernel waits for that kernel's completion before reading idx
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(1024);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, groups_kernel, idx, S, k, ebase, ecount, etotal, xrow_is_slot, xidx, gsize,
+                              n_groups, grp_expert, grp_count, grp_xrow, grp_orow, max_groups, err);
 }
 
 cudaError_t launch_moe_mix(const float *ys, const float *scores, const int32_t *idx, int ebase, int ecount, int T,
                            int k, int N, void *y, int y_dtype, cudaStream_t st) {
     const int64_t n = (int64_t)T * N;
     if (n == 0) return cudaSuccess;
-    mix_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ys, scores, idx, ebase, ecount, T, k, N, y, y_dtype);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};  // programmatic dependent of the down-projection GEMV
+    cfg.gridDim = dim3((unsigned)((n + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, mix_kernel, ys, scores, idx, ebase, ecount, T, k, N, y, y_dtype);
 }
 
 }  // namespace kq
