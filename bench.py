@@ -137,7 +137,7 @@ def build_layers(dev, n_layers, world=1, rank=0, seed0=100):
     return layers
 
 
-def layer_step(kq, L, x, a=None, dist=None, comm=None, mode="chain"):
+def layer_step(kq, L, x, a=None, dist=None, comm=None, mode="chain", ar="nccl"):
     """One decoder-layer pass of the seven quantized projections.
 
     mode "chain" (M = 1): q|k|v, o, gate+up and down in ONE persistent launch
@@ -148,8 +148,10 @@ def layer_step(kq, L, x, a=None, dist=None, comm=None, mode="chain"):
     attention and norms.  mode "ops": one kq op per projection group (4
     launches).  Under tensor parallelism the row-parallel o and down outputs
     are summed over ranks: at M=1 optionally inside their GEMV kernels (peer
-    stores over NVLink, `comm`), otherwise with NCCL all-reduces.  `a` stands
-    in for this rank's slice of the attention output."""
+    stores over NVLink, `comm`, ar "fused"), after them with the one-shot
+    peer-memory all-reduce kernel (kq.all_reduce, ar "peer"), or with NCCL
+    all-reduces (ar "nccl").  `a` stands in for this rank's slice of the
+    attention output."""
     xa = x if a is None else a
     if x.shape[0] == 1 and comm is None and mode == "chain":
         qkv, o, h, y = kq.quantized_matmul_chain([
@@ -172,13 +174,16 @@ def layer_step(kq, L, x, a=None, dist=None, comm=None, mode="chain"):
         return q, o, y
     qkv = kq.quantized_matmul(x, L["qkv"], None, "q4_k")
     h = kq.quantized_glu(x, L["gate"], L["up"], "q4_k", act="silu")
-    if comm is not None and x.shape[0] == 1:
+    if comm is not None and x.shape[0] == 1 and ar == "fused":
         o = kq.quantized_matmul_allreduce(xa, L["o"], "q4_k", comm)
         y = kq.quantized_matmul_allreduce(h, L["down"], "q6_k", comm)
         return qkv, o, y
     o = kq.quantized_matmul(xa, L["o"], None, "q4_k")
     y = kq.quantized_matmul(h, L["down"], None, "q6_k")
-    if dist is not None:
+    if dist is not None and ar == "peer" and comm is not None:
+        kq.all_reduce(o, comm)
+        kq.all_reduce(y, comm)
+    elif dist is not None:
         dist.all_reduce(o)
         dist.all_reduce(y)
     return qkv, o, y
@@ -516,7 +521,9 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
-    ap.add_argument("--fused-allreduce", action="store_true")
+    ap.add_argument("--fused-allreduce", action="store_true", help="same as --allreduce fused")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl", "fused"],
+                    help="cross-rank sum of the row-parallel decode projections (N > 1)")
     ap.add_argument("--chain", action="store_true", help="one chain launch per layer instead of one launch per op")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -545,9 +552,11 @@ def main():
     dd = dist if world > 1 else None
     ka = 4096 // world  # this rank's slice of the attention output (o_proj K)
     from gmlx_b200 import parallel as par
-    # --fused-allreduce: row-parallel o/down with the cross-rank sum inside their
-    # GEMV kernels (peer stores over NVLink); default: NCCL all-reduce
-    comm = par.PeerComm(4096, dev) if (world > 1 and args.fused_allreduce) else None
+    # cross-rank sum of the row-parallel o/down outputs: "peer" (default) the
+    # one-shot all-reduce kernel over NVLink peer memory after each GEMV;
+    # "fused" inside their GEMV kernels (M = 1); "nccl" NCCL all-reduce
+    ar = "fused" if args.fused_allreduce else args.allreduce
+    comm = par.PeerComm(32 * 4096, dev) if (world > 1 and ar != "nccl") else None
     # headline launch structure: one kq op per projection group (measured the
     # faster of the two on B200); --chain times the single persistent chain launch
     head_mode = "chain" if (args.m == 1 and comm is None and args.chain) else "ops"
@@ -561,7 +570,7 @@ def main():
 
         def one_step():
             for li, L in enumerate(layers):
-                layer_step(kq, L, xs[li], att[li], dd, comm, mode)
+                layer_step(kq, L, xs[li], att[li], dd, comm, mode, ar)
         return time_graph(torch, one_step, steps, warmup, stream, min_warm_s) / steps
 
     # timed region (headline), with clock sampling and barrier + max over ranks
@@ -609,7 +618,7 @@ def main():
         dx = hx.to(dev, non_blocking=True)
         y = dx
         for L in layers:
-            _, _, y = layer_step(kq, L, dx, dx[:, :ka].contiguous(), dd, comm, head_mode)
+            _, _, y = layer_step(kq, L, dx, dx[:, :ka].contiguous(), dd, comm, head_mode, ar)
         hy.copy_(y, non_blocking=True)
     for _ in range(args.warmup):
         e2e_step()
@@ -720,8 +729,9 @@ def main():
                                   else "one launch per projection group (q|k|v, o, gate+up, down)"),
                        "l2": "inputs larger than L2 (32 distinct layers, 4.41 GB per step)",
                        "parallelism": (f"tp{world} (column-parallel qkv/gate/up, row-parallel o/down, "
-                                       + ("cross-rank sum fused into their GEMV kernels over NVLink peer stores)"
-                                          if comm is not None else "NCCL all-reduce)")) if world > 1 else "single"},
+                                       + {"fused": "cross-rank sum fused into their GEMV kernels over NVLink peer stores)",
+                                          "peer": "one-shot all-reduce kernel over NVLink peer memory)",
+                                          "nccl": "NCCL all-reduce)"}[ar]) if world > 1 else "single"},
             "frac_hbm": value / world / hbm_peak,
             "us_per_layer": t_step / N_LAYERS * 1e6,
             "rel_err": check["max_rel_err"], "parity": check,

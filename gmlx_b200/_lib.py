@@ -65,6 +65,8 @@ SIGNATURES = {
     "kq_allreduce_buffer_bytes": (_sz, [_i32, _i64]),
     "kq_quantized_matmul_allreduce": (_i32, [_i32, _vp, _i32, _i64, _vp, _i64, _i64, _vp, _i32, _i32, _i32, _vp, _vp,
                                              _sz, _vp]),
+    "kq_allreduce": (_i32, [_vp, _i32, _vp, _i32, _i64, _i64, _i32, _i32, _vp, _vp]),
+    "kq_comm_error": (_i32, [_vp, _i32, _vp]),
     "kq_comm_alloc": (_i32, [_sz, _vp]),
     "kq_comm_free": (_i32, [_vp]),
     "kq_ipc_handle": (_i32, [_vp, _vp]),

@@ -21,7 +21,7 @@ BUILD = os.path.join(HERE, "_build", "dev" if DEV else "release")
 STAMP = os.path.join(HERE, "_build", "linked_config")
 LIB = os.path.join(HERE, "libkq_cuda.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["kq_dequant.cu", "kq_gemv.cu", "kq_moe.cu", "kq_capi.cu", "kq_noalloc.cu", "kq_gemm_sm100.cu", "kq_chain.cu"]
+SOURCES = ["kq_dequant.cu", "kq_gemv.cu", "kq_moe.cu", "kq_capi.cu", "kq_noalloc.cu", "kq_gemm_sm100.cu", "kq_chain.cu", "kq_allreduce.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills"]

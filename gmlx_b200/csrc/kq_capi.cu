@@ -742,6 +742,35 @@ int kq_quantized_matmul_allreduce(int codec, const void *x, int x_dtype, int64_t
     return cuda_status(launch_gemv(a, (cudaStream_t)stream), what);
 }
 
+int kq_allreduce(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, int64_t buf_n, int world, int rank,
+                 void *const *comm_bufs, void *stream) {
+    g_msg[0] = 0;
+    const char *what = "allreduce";
+    if (!x || !y) return fail(KQ_ERR_SHAPE, "%s: null pointer", what);
+    if (!out_dtype_ok(x_dtype) || !out_dtype_ok(y_dtype)) return fail(KQ_ERR_DTYPE, "%s: bad dtype", what);
+    if (n < 0 || n > buf_n || buf_n > 0x7fffffff)
+        return fail(KQ_ERR_SHAPE, "%s: bad size n=%lld (buffers for %lld)", what, (long long)n, (long long)buf_n);
+    if (world < 1 || world > AR_MAX_WORLD || rank < 0 || rank >= world || !comm_bufs)
+        return fail(KQ_ERR_SHAPE, "%s: bad world %d (1..%d) / rank %d / buffers", what, world, AR_MAX_WORLD, rank);
+    if (n == 0) return KQ_OK;
+    return cuda_status(launch_allreduce(x, x_dtype, y, y_dtype, n, buf_n, world, rank,
+                                        reinterpret_cast<unsigned char *const *>(comm_bufs), (cudaStream_t)stream),
+                       what);
+}
+
+int kq_comm_error(void *own_buf, int clear, void *stream) {
+    g_msg[0] = 0;
+    if (!own_buf) return fail(KQ_ERR_SHAPE, "comm_error: null buffer");
+    int v = 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    char *p = (char *)own_buf + AR_ERR;
+    cudaError_t e = cudaMemcpyAsync(&v, p, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(p, 0, sizeof(int), st);
+    if (e != cudaSuccess) return -cuda_status(e, "comm_error");
+    return v;
+}
+
 int kq_comm_alloc(size_t bytes, void **ptr) {
     g_msg[0] = 0;
     if (!ptr || !bytes) return fail(KQ_ERR_SHAPE, "comm_alloc: bad arguments");

@@ -94,7 +94,15 @@ cudaError_t launch_chain(const ChainProblemDesc *pd, int count, const ChainPlan 
 // rank's call epoch; flags at 64 + 4 * (parity * world + rank)) and f32 slots
 // [parity][world][n] from byte 4096.
 constexpr size_t AR_HDR = 4096;
-inline size_t ar_buffer_bytes(int world, int64_t n) { return AR_HDR + (size_t)2 * world * n * sizeof(float); }
+// f32 slots of the fused GEMV, then the one-shot all-reduce's (kq_allreduce.cu)
+// 8-byte {value, flag} slots [parity][world][n]; its done counter sits at
+// header byte 16 and its error word at 32.
+inline size_t ar_ll_offset(int world, int64_t n) { return AR_HDR + (size_t)2 * world * n * sizeof(float); }
+inline size_t ar_buffer_bytes(int world, int64_t n) { return ar_ll_offset(world, n) + (size_t)2 * world * n * 8; }
+constexpr int AR_CNT = 16, AR_ERR = 32, AR_CMAX = 256, AR_MAX_WORLD = 8;
+int allreduce_ctas(int world, int64_t n);
+cudaError_t launch_allreduce(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, int64_t buf_n, int world,
+                             int rank, unsigned char *const *bufs, cudaStream_t st);
 // Scratch the GEMV needs for `a` (bytes of f32 partials, bytes of counters).
 void gemv_scratch_need(const GemvArgs &a, size_t *partial_bytes, size_t *counter_bytes);
 

@@ -327,6 +327,30 @@ def quantized_matmul_allreduce(x: torch.Tensor, w: torch.Tensor, codec, comm,
     return y.reshape(*x.shape[:-1], n)
 
 
+def all_reduce(x: torch.Tensor, comm, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Sum of ``x`` over the ranks of ``comm`` (a ``gmlx_b200.parallel.PeerComm``)
+    in one launch: one-shot push of {value, flag} words over NVLink peer
+    memory, f32 rank-order sum,
+    the same bits on every rank.  For the short vectors of decode (the all_sum
+    after a row-parallel projection, gmlx/hy_v3_model.py:259).  ``out``
+    defaults to ``x`` (in place)."""
+    _need_cuda(x)
+    if not x.is_contiguous():
+        raise ValueError("all_reduce: contiguous tensor expected")
+    if x.dtype not in _DT:
+        raise TypeError(f"all_reduce: unsupported dtype {x.dtype}")
+    n = x.numel()
+    if n > comm.n:
+        raise ValueError(f"all_reduce: {n} values exceed the communication buffer ({comm.n})")
+    y = x if out is None else out
+    if y.shape != x.shape or not y.is_contiguous() or y.dtype not in _DT:
+        raise ValueError("all_reduce: out must be a contiguous tensor of x's shape")
+    L = _lib.load()
+    _lib.check(L.kq_allreduce(_p(x), _DT[x.dtype], _p(y), _DT[y.dtype], n, comm.n, comm.world, comm.rank, _p(comm.table),
+                              _stream(x.device)), "all_reduce")
+    return y
+
+
 def quantized_glu(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, codec=None, act: str = "silu",
                   out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """Fused ``act(x @ Wg.T) * (x @ Wu.T)`` for a dense gate/up pair (one launch)."""

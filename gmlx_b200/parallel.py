@@ -148,6 +148,17 @@ class PeerComm:
                 ptrs = [self._own]
             self.table = torch.tensor(ptrs, dtype=torch.int64, device=device)
 
+    def error(self, clear: bool = False) -> int:
+        """Error word of this rank's buffer (7: a one-shot all-reduce gave up
+        waiting for a peer); synchronizes the current stream."""
+        import ctypes
+        from . import _lib
+        v = self._L.kq_comm_error(ctypes.c_void_p(self._own), int(clear),
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if v < 0:
+            _lib.check(-v, "comm_error")
+        return v
+
     def close(self):
         import ctypes
         for p in self._opened:

@@ -235,6 +235,23 @@ size_t kq_allreduce_buffer_bytes(int world, int64_t n);
 int kq_quantized_matmul_allreduce(int codec, const void *x, int x_dtype, int64_t k, const void *w, int64_t n,
                                   int64_t w_row_stride, void *y, int y_dtype, int world, int rank,
                                   void *const *comm_bufs, void *workspace, size_t workspace_bytes, void *stream);
+/* One-shot all-reduce (sum) of n values over the ranks of a buffer set, for
+ * the cross-rank sum after a row-parallel decode projection: the all_sum of
+ * gmlx's tensor-parallel layers (gmlx/hy_v3_model.py:259 after shard_linear,
+ * :396-443).  Every rank stores each value, as one 8-byte word {f32 bits,
+ * call flag}, into every rank's communication buffer over NVLink, waits for
+ * all ranks' words of this call (bounded, ~2 s: on expiry the buffer's error
+ * word, read by kq_comm_error, becomes 7 and y is left incomplete) and writes
+ * the rank-order f32 sum to y in y_dtype, identical bits on every rank.  y may
+ * equal x.  x_dtype / y_dtype: KQ_F32 / KQ_F16 / KQ_BF16; buf_n: the n the
+ * buffers were sized for (kq_allreduce_buffer_bytes(world, buf_n)), n <= buf_n;
+ * world <= 8.  Shares the buffers, epoch and call-order rule of
+ * kq_quantized_matmul_allreduce. */
+int kq_allreduce(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, int64_t buf_n, int world, int rank,
+                 void *const *comm_bufs, void *stream);
+/* Error word of this rank's communication buffer (0 = no expired wait), read
+ * after synchronizing `stream`; clear != 0 resets it.  Negative: -KQ_ERR_CUDA. */
+int kq_comm_error(void *own_buf, int clear, void *stream);
 int kq_comm_alloc(size_t bytes, void **ptr);
 int kq_comm_free(void *ptr);
 int kq_ipc_handle(const void *ptr, void *handle64);

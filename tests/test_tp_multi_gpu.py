@@ -116,3 +116,60 @@ def test_expert_parallel_all_to_all_two_ranks():
     for r in range(WORLD):
         err, werr = got[r]
         assert werr == 0 and err <= 1e-2, got
+
+
+def _ar_rank_main(rank, port, out_q):
+    import torch.distributed as dist
+    from gmlx_b200 import kq, parallel as par
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, device_id=dev)
+    try:
+        comm = par.PeerComm(8192, dev)
+        res = []
+        g = torch.Generator(device="cpu").manual_seed(100 + rank)
+        # sizes off the 512-value CTA slices, both dtypes, in place and out of
+        # place, and more calls than the two buffer parities
+        for i, (n, dt, inplace) in enumerate([(4096, torch.bfloat16, True), (4095, torch.float32, False),
+                                              (1, torch.float32, True), (8192, torch.float16, False),
+                                              (1000, torch.bfloat16, False)]):
+            x = torch.randn(n, generator=g).to(dt).to(dev)
+            xin = x.clone()
+            y = kq.all_reduce(x, comm) if inplace else kq.all_reduce(x, comm, out=torch.empty_like(x))
+            parts = [torch.empty_like(xin) for _ in range(WORLD)]
+            dist.all_gather(parts, xin)
+            ref = torch.zeros(n, dtype=torch.float32, device=dev)
+            for p in parts:  # the kernel's rank-order f32 sum
+                ref = ref + p.float()
+            torch.cuda.synchronize()
+            res.append((y.float().cpu().numpy(), ref.to(dt).float().cpu().numpy()))
+        err = comm.error()
+        dist.barrier()
+        comm.close()
+        out_q.put((rank, (res, err)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_peer_allreduce_two_ranks():
+    """kq.all_reduce (one-shot over NVLink peer memory) equals the rank-order
+    f32 sum of the gathered inputs bit for bit, on every rank."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29800 + os.getpid() % 150
+    procs = [ctx.Process(target=_ar_rank_main, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(WORLD):
+        res, err = got[r]
+        assert err == 0
+        for (y, ref), (y0, _) in zip(res, got[0][0]):
+            assert np.array_equal(y, ref)
+            assert np.array_equal(y, y0)
