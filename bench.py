@@ -308,12 +308,15 @@ def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
     and GB/s of the expert bytes the routing touched (unique experts x expert
     bytes).  Two ways to move tokens at N > 1:
       allreduce -- every rank routes all T tokens, runs its experts' slots,
-                   partial outputs summed with one NCCL all-reduce (graph-timed);
+                   partial outputs summed with one all-reduce (graph-timed):
+                   the one-shot peer-memory kernel (kq.all_reduce) up to
+                   64 x 7168 values, NCCL above;
       alltoall  -- each rank routes its own T / N tokens and sends the routed
                    rows to the experts' owners and back (NCCL all-to-all with
                    host-side split sizes, so timed eagerly with CUDA events)."""
     from gmlx_b200 import parallel as par
     out = {}
+    comm = par.PeerComm(64 * 7168, dev) if world > 1 else None
     for name, E, K, D, F, cgu, cd, ts in MOE_CONFIGS:
         el = E // world
         base = rank * el
@@ -330,7 +333,9 @@ def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
             def layer():
                 idx, sc = kq.moe_router_topk(logits, K, True, shared_gate=False)
                 y = kq.moe_expert_layer_local(x, idx, sc, wg, wu, wd, cgu, cd, base, E, out_dtype=torch.float32)
-                if world > 1:
+                if world > 1 and y.numel() <= comm.n:
+                    kq.all_reduce(y, comm)
+                elif world > 1:
                     dist.all_reduce(y)
                 return idx
             idx = layer()
@@ -360,6 +365,9 @@ def run_moe(torch, kq, dist, dev, world, rank, stream, hbm_peak):
         out[name] = cell
         del wg, wu, wd
         torch.cuda.empty_cache()
+    if comm is not None:
+        dist.barrier()
+        comm.close()
     return out
 
 
